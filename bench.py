@@ -1,0 +1,397 @@
+#!/usr/bin/env python
+"""Benchmark of the VMonarch attention hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
+                    [--workload dit14b] [--scaling weak|strong]
+
+A step is one forward + backward of VMonarch attention over one synthetic layer of the workload
+(default: the video-DiT 14B-class layer B=1, H=40, m=21, b=1560, D=128, 2 iterations, 1560 recomputed
+tokens: the N~32K, H=40, D=128 configuration the metric is quoted on). The metric is effective
+algorithmic TFLOP/s of forward+backward (FLOPs counted on unpadded shapes, 2 per multiply-add).
+
+impl ours       this repository's CUDA path; `value` from inputs resident in HBM (every input and
+                activation is > 126 MB, larger than L2, so no flush is needed), `e2e` through the public
+                API with the step's inputs copied from pinned host memory and the loss read back.
+impl reference  the reference's CPU path (the fp32 oracle restating the reference's PyTorch code)
+                on the host cores, on a bounded sample (whole heads) of the same workload.
+impl triton     the reference's own Triton kernels (installed in baseline/_ref) on the same GPU;
+                reported for comparison, not part of the driver's contract.
+Multi-GPU (torchrun): (batch x head) units are sharded with no collective on the hot path;
+`--scaling weak` (default) gives every rank one full layer, `strong` splits one layer's heads.
+"""
+from __future__ import annotations
+
+import argparse
+import contextlib
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from vmonarch_b200 import shard  # noqa: E402
+from vmonarch_b200.configs import WORKLOADS, Workload, make_inputs  # noqa: E402
+
+METRIC = "VMonarch fwd+bwd effective TFLOP/s (N~32K, H=40, D=128, bf16)"
+
+
+def parse_args():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours")
+    ap.add_argument("--workload", choices=sorted(WORKLOADS), default="dit14b")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget-s", type=float, default=150.0, help="wall-clock cap of the CPU reference arm")
+    return ap.parse_args()
+
+
+# ----------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """Samples nvidia-smi clocks / throttle reasons every 200 ms while the timed region runs."""
+
+    FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: torch.device):
+        self.uuid = None
+        try:
+            self.uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
+        except Exception:
+            pass
+        self.proc = None
+        self.tmp = None
+
+    def __enter__(self):
+        try:
+            self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+            self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                                          "-lms", "200"], stdout=self.tmp, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        if self.proc is None or self.tmp is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        rows = []
+        with open(self.tmp.name) as f:
+            for line in f:
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) < 8 or (self.uuid and parts[0] != self.uuid):
+                    continue
+                rows.append(parts)
+        os.unlink(self.tmp.name)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        sm = [float(r[1]) for r in rows if r[1].replace(".", "").isdigit()]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
+                "samples": len(rows), "reasons": reasons}
+
+
+# ----------------------------------------------------------------------------------------- steps
+def unit_plan(w: Workload, info: shard.RankInfo, scaling: str):
+    """(heads of this rank, seed offset, layers per job) for weak / strong scaling."""
+    if scaling == "weak":
+        return range(w.H), info.rank, info.world
+    return shard.unit_range(w.H, info.rank, info.world), 0, 1
+
+
+def make_step(w: Workload, api):
+    """Returns step(q, k, v, do, de) -> (out, grads) running forward + backward through `api`."""
+    if w.kind == "vmonarch":
+        def step(q, k, v, do, de):
+            z = api.vmonarch_attention(q, k, v, w.m, w.b, w.iters, recompute_tokens=w.recompute)
+            return z, torch.autograd.grad(z, (q, k, v), do)
+    else:
+        def step(q, k, v, do, de):
+            o, e = api.flash_entropy_attention(q, k, v)
+            return o, torch.autograd.grad((o, e), (q, k, v), (do, de))
+    return step
+
+
+def scaled_flops(w: Workload, n_heads: int) -> float:
+    f = w.flops()
+    return (f["fwd"] + f["bwd"]) * n_heads / w.H
+
+
+def time_steps(step, args_dev, steps: int, warmup: int, device) -> float:
+    """ms per step: W warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events."""
+    for _ in range(warmup):
+        step(*args_dev)
+    torch.cuda.synchronize(device)
+    shard.barrier()
+    torch.cuda.synchronize(device)
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    start.record()
+    for _ in range(steps):
+        step(*args_dev)
+    end.record()
+    torch.cuda.synchronize(device)
+    shard.barrier()
+    return start.elapsed_time(end) / steps
+
+
+def kernel_flops(name: str, a) -> tuple[float, float]:
+    """(algorithmic FLOPs, algorithmic HBM bytes) of one C-ABI call, from its argument struct."""
+    if name == "vmb_fea_fwd":
+        f = 2.0 * a.batch * a.n_q * a.n_kv * (a.d + a.dv)
+        by = 2.0 * a.batch * (a.n_q * (a.d + a.dv) + a.n_kv * (a.d + a.dv))
+        return f, by
+    if name == "vmb_fea_bwd":
+        f = 2.0 * a.batch * a.n_q * a.n_kv * (3 * a.d + 2 * a.dv)
+        by = 2.0 * a.batch * (a.n_q * (a.d + 2 * a.dv) + 2 * a.n_kv * (a.d + a.dv))
+        return f, by
+    dv = a.dw - a.d if a.last else a.d
+    n = a.bh * a.m * a.b
+    f = 2.0 * a.bh * a.b * a.m * a.m * (a.d + dv) * (2 if name == "vmb_lstep_bwd" else 1)
+    by = n * (2 * a.d + 2 * a.dw + 4 + 2 * dv) if name == "vmb_lstep_fwd" else n * (2 * a.d + 4 * a.dw + 4 + 8 * a.d)
+    return f, by
+
+
+def profile_step(step, args_dev, device) -> dict:
+    """One step with every C-ABI call bracketed by CUDA events on the current stream."""
+    from vmonarch_b200 import ops
+    recs = []
+
+    @contextlib.contextmanager
+    def timer(name, a):
+        s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        s.record()
+        yield
+        e.record()
+        recs.append((name, kernel_flops(name, a), s, e))
+
+    ops.set_timer(timer)
+    try:
+        step(*args_dev)
+    finally:
+        ops.set_timer(None)
+    torch.cuda.synchronize(device)
+    per = {}
+    for name, (f, by), s, e in recs:
+        d = per.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+        d["launches"] += 1
+        d["ms"] += s.elapsed_time(e)
+        d["flops"] += f
+        d["bytes"] += by
+    return per
+
+
+def load_peaks() -> tuple[dict, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        return json.loads(p.read_text()), "measured"
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}, "fallback"
+
+
+def roofline(per: dict) -> dict:
+    peaks, src = load_peaks()
+    name, d = max(per.items(), key=lambda kv: kv[1]["ms"])
+    total = sum(x["ms"] for x in per.values())
+    if name.startswith("vmb_fea"):
+        achieved = d["flops"] / (d["ms"] * 1e-3) / 1e12
+        peak, unit, bound = peaks["bf16_tflops_sustained"], "TFLOP/s", "tensor"
+        per_launch = d["flops"] / d["launches"]
+    else:
+        achieved = d["bytes"] / (d["ms"] * 1e-3) / 1e9
+        peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
+        per_launch = d["bytes"] / d["launches"]
+    traffic = None
+    tp = ROOT / "profiles" / "traffic.json"
+    if tp.exists():
+        traffic = json.loads(tp.read_text()).get(name)
+    return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
+            "frac": round(achieved / peak, 4), "peak_source": f"{src} (sustained bf16)" if bound == "tensor" else src,
+            "per_launch_algorithmic": per_launch, "avg_launch_ms": round(d["ms"] / d["launches"], 4),
+            "share_of_step": round(d["ms"] / total, 4), "traffic": traffic,
+            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per.items()}}
+
+
+# ----------------------------------------------------------------------------------------- CPU
+def cpu_reference_sample(w: Workload, seed: int, budget_s: float, steps: int, warmup: int) -> dict:
+    """The reference's CPU path (fp32 oracle) on whole heads of the workload; TFLOP/s of fwd+bwd."""
+    import oracle
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    q, k, v, do, de = make_inputs(w, seed=seed, heads=range(0, 1), dtype=torch.float32)
+
+    def one():
+        leaves = [t.clone().requires_grad_() for t in (q, k, v)]
+        if w.kind == "vmonarch":
+            z = oracle.vmonarch_attention(*leaves, w.m, w.b, w.iters, recompute_tokens=w.recompute)
+            torch.autograd.grad(z, leaves, do)
+        else:
+            o, e = oracle.entropy_attention(*leaves, w.D ** -0.5)
+            torch.autograd.grad((o, e), leaves, (do, de))
+
+    t0 = time.perf_counter()
+    for _ in range(min(warmup, 1)):
+        one()
+    times = []
+    while len(times) < max(steps, 1):
+        t = time.perf_counter()
+        one()
+        times.append(time.perf_counter() - t)
+        if time.perf_counter() - t0 > budget_s:
+            break
+    sec = statistics.mean(times)
+    return {"value": round(scaled_flops(w, 1) / sec / 1e12, 5), "unit": "TFLOP/s", "cores": torch.get_num_threads(),
+            "kind": "port", "seconds_per_sample": round(sec, 3), "timed_samples": len(times),
+            "sample": f"1 of {w.H} heads of {w.name} (B=1,H=1,N={w.N}), fp32 forward+backward on the host, "
+                      f"extrapolates x{w.H} per layer"}
+
+
+# ----------------------------------------------------------------------------------------- arms
+def base_line(args, w, n_gpus, ms, value, impl=None) -> dict:
+    line = {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": n_gpus, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": args.scaling,
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) + per-frame shared mean, std 0.3)",
+            "config": {"workload": w.name, "B": w.B, "H": w.H, "num_blocks": w.m, "block_size": w.b, "N": w.N,
+                       "D": w.D, "num_iters": w.iters, "recompute_tokens": w.recompute,
+                       "layers_per_job": n_gpus if args.scaling == "weak" else 1,
+                       "parallelism": f"heads x{n_gpus}, no collective",
+                       "l2": "inputs and activations larger than L2 (no flush needed)"}}
+    if impl:
+        line["impl"] = impl
+    return line
+
+
+def run_ours(args, info, device):
+    import vmonarch_b200 as api
+    from vmonarch_b200 import ops
+    w = WORKLOADS[args.workload]
+    heads, seed_off, layers = unit_plan(w, info, args.scaling)
+    q, k, v, do, de = make_inputs(w, seed=args.seed + seed_off, heads=heads, pin=True)
+    dev = [t.to(device, non_blocking=True) for t in (q, k, v, do, de)]
+    dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(dev)]
+    step = make_step(w, api)
+    n_local = len(heads)
+    flops_local = scaled_flops(w, n_local)
+    flops_job = flops_local * (info.world if args.scaling == "weak" else 1)
+    if args.scaling == "strong":
+        flops_job = scaled_flops(w, w.H)
+
+    launches0 = ops.kernel_launches()
+    with ClockSampler(device) as clk:
+        ms = time_steps(step, dev, args.steps, args.warmup, device)
+    launches = ops.kernel_launches() - launches0
+    ms_max = shard.max_over_ranks(ms, device)
+    value = flops_job / (ms_max * 1e-3) / 1e12
+    per = profile_step(step, dev, device)
+
+    e2e = None
+    if not args.no_e2e:
+        host = (q, k, v, do, de)
+
+        def e2e_step(*_):
+            leaves = [h.to(device, non_blocking=True) for h in host]
+            leaves = [t.requires_grad_() if i < 3 else t for i, t in enumerate(leaves)]
+            out, grads = step(*leaves)
+            return (out.float() * leaves[3].float()).sum().item()  # the step's loss, read back
+
+        ms_e2e = time_steps(e2e_step, (), max(1, min(args.steps, 3)), 1, device)
+        ms_e2e = shard.max_over_ranks(ms_e2e, device)
+        h2d = sum(t.numel() * t.element_size() for t in host)
+        e2e = {"value": round(flops_job / (ms_e2e * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
+               "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4}
+
+    if info.rank != 0:
+        return None
+    line = base_line(args, w, info.world, ms_max, value)
+    f = w.flops()
+    line["dense_equivalent_tflops"] = round(3.5 * f["dense_fwd"] * n_local / w.H * layers / (ms_max * 1e-3) / 1e12, 2)
+    line["flops_per_step"] = flops_job
+    line["roofline"] = roofline(per)
+    line["e2e"] = e2e
+    line["gpu_launches"] = int(launches)
+    line["clocks"] = clk.summary()
+    line["cpu_baseline"] = None
+    if info.world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_reference_sample(w, args.seed, 60.0, 1, 0)
+    return line
+
+
+def run_reference(args, info):
+    if info.rank != 0:
+        return None
+    w = WORKLOADS[args.workload]
+    cpu = cpu_reference_sample(w, args.seed, args.cpu_budget_s, args.steps, args.warmup)
+    ms = scaled_flops(w, w.H) / (cpu["value"] * 1e12) * 1e3  # one full layer, extrapolated from the heads
+    line = base_line(args, w, info.world, ms, cpu["value"], impl="reference")
+    line["steps"] = cpu["timed_samples"]
+    line["cpu_baseline"] = cpu
+    line["e2e"] = {"value": cpu["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
+    line["gpu_launches"] = 0
+    return line
+
+
+def run_triton(args, info, device):
+    """The reference's Triton path from baseline/_ref on the same GPU (comparison only)."""
+    ref_dir = ROOT / "baseline" / "_ref"
+    sys.path.insert(0, str(ref_dir))
+    try:
+        import video_monarch_attention as ref
+    except Exception as exc:  # pragma: no cover - depends on the box
+        return {"impl": "reference-triton", "unavailable": f"cannot import the reference: {exc}"}
+    w = WORKLOADS[args.workload]
+    heads, seed_off, layers = unit_plan(w, info, args.scaling)
+    q, k, v, do, de = make_inputs(w, seed=args.seed + seed_off, heads=heads)
+    dev = [t.to(device) for t in (q, k, v, do, de)]
+    dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(dev)]
+    step = make_step(w, ref)
+    with ClockSampler(device) as clk:
+        ms = time_steps(step, dev, args.steps, args.warmup, device)
+    ms_max = shard.max_over_ranks(ms, device)
+    flops_job = scaled_flops(w, len(heads)) * (info.world if args.scaling == "weak" else 1)
+    if args.scaling == "strong":
+        flops_job = scaled_flops(w, w.H)
+    if info.rank != 0:
+        return None
+    line = base_line(args, w, info.world, ms_max, flops_job / (ms_max * 1e-3) / 1e12, impl="reference-triton")
+    line["clocks"] = clk.summary()
+    return line
+
+
+def main():
+    args = parse_args()
+    info = shard.env_rank()
+    if args.impl == "reference":
+        line = run_reference(args, info)  # rank 0 only; no process group, the other ranks exit at once
+    else:
+        device = torch.device("cuda", info.local_rank)
+        torch.cuda.set_device(device)
+        shard.init("nccl")
+        line = run_ours(args, info, device) if args.impl == "ours" else run_triton(args, info, device)
+    if line is not None:
+        print(json.dumps(line), flush=True)
+    if torch.distributed.is_initialized():
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,156 @@
+/*
+ * vmonarch_b200 — C ABI of the B200 (sm_100a) VMonarch attention hot path.
+ *
+ * The reference (EricLina/VMonarch) is a Python package whose hot path crosses from the host to
+ * the GPU only at its Triton kernel launches and at a handful of torch ops. Each entry point
+ * below replaces one of those crossings; the Python package `vmonarch_b200` binds them with
+ * ctypes and mirrors the reference's Python API on top.
+ *
+ * Conventions
+ *  - Every pointer is a device pointer; tensors are dense row-major with the batch stride given
+ *    in ELEMENTS. Rows are contiguous (row stride = number of columns). Base pointers must be
+ *    16-byte aligned and batch strides multiples of 8 elements.
+ *  - dtype selects the 16-bit element type (VMB_DTYPE_BF16 or VMB_DTYPE_F16); all arithmetic
+ *    accumulates in fp32. Statistics (lse, ent, dent) are fp32.
+ *  - `stream` is a cudaStream_t (NULL = legacy default stream). Calls only enqueue work; they
+ *    never synchronize and never allocate.
+ *  - Return value: VMB_OK or an error code; vmb_last_error() describes the last failure of the
+ *    calling thread.
+ */
+#ifndef VMONARCH_B200_H
+#define VMONARCH_B200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define VMB_ABI_VERSION 1
+
+#define VMB_DTYPE_BF16 0
+#define VMB_DTYPE_F16 1
+
+#define VMB_OK 0
+#define VMB_EINVAL 1   /* malformed argument: null pointer, bad size, misalignment */
+#define VMB_ENOTSUP 2  /* head dimensions without a kernel */
+#define VMB_ECUDA 3    /* CUDA runtime error while launching */
+
+/* ABI version (VMB_ABI_VERSION of the library that was loaded). */
+int vmb_abi_version(void);
+
+/* Human-readable description of the last error returned on the calling thread. */
+const char* vmb_last_error(void);
+
+/* Number of kernels this library has launched in the process so far (all threads, all devices).
+ * Diagnostic with no reference counterpart: the benchmark reports it as its launch count. */
+uint64_t vmb_kernel_launches(void);
+
+/*
+ * FlashEntropyAttention forward over `batch` independent sequences:
+ *   o = softmax(sm_scale q k^T) [v | v2],  ent_i = -sum_j P_ij log P_ij,
+ *   lse_i = log2 sum_j 2^(x_ij) with x = sm_scale q k^T log2(e)   (kept for the backward).
+ * Replaces the `_attn_fwd` launch and the pad-row zeroing of _FlashEntropyAttention.forward
+ * (video_monarch_attention/kernel.py:346-353) and the F.pad / slice of flash_entropy_attention
+ * (kernel.py:399-402): sequences of any length are handled without padding. The optional second
+ * value tensor replaces the torch.cat([kg, vg], -1) of the last R step (vmonarch.py:50).
+ * Shapes: d in {64, 128}; dv in {64, 128, 256} with dv a multiple of d (the reference requires
+ * Dv % D == 0 for its backward, kernel.py:260). o may be a strided view (o_bs) into a larger
+ * tensor, which is how the exact first-frame recompute writes straight into z.
+ */
+typedef struct vmb_fea_fwd_args {
+  const void* q;  int64_t q_bs;   /* [batch][n_q][d]                               */
+  const void* k;  int64_t k_bs;   /* [batch][n_kv][d]                              */
+  const void* v;  int64_t v_bs;   /* [batch][n_kv][dv1]  -> o columns [0, dv1)     */
+  const void* v2; int64_t v2_bs;  /* [batch][n_kv][dv-dv1] -> o columns [dv1, dv); NULL if dv1 == dv */
+  void* o;        int64_t o_bs;   /* [batch][n_q][dv]                              */
+  float* lse;                     /* [batch][n_q] or NULL                          */
+  float* ent;                     /* [batch][n_q] or NULL (entropy not computed)   */
+  int64_t batch, n_q, n_kv;
+  int32_t d, dv, dv1, dtype;
+  float sm_scale;
+} vmb_fea_fwd_args;
+
+int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream);
+
+/*
+ * FlashEntropyAttention backward. Replaces `_attn_bwd_preprocess` + `_attn_bwd`
+ * (video_monarch_attention/kernel.py:360-381) including the entropy-gradient term
+ * dS = P (dP - delta) + dE P (-E - log P) (kernel.py:165-167).
+ * grad_mode 0: grad_q/grad_k/grad_v/grad_v2 are written in the element dtype (standalone op).
+ * grad_mode 1: grad_* are fp32 buffers that the gradients are ADDED into (VMonarch chains
+ *              several R steps and the recompute into one set of accumulators).
+ * v_is_k = 1: the value columns [0, dv1) are the key tensor itself (dv1 == d); their gradient is
+ *              added into grad_k and grad_v must be NULL. This is the VMonarch R step
+ *              (vmonarch.py:50).
+ * dent may be NULL (dE = 0, e.g. the detached entropy of VMonarch, vmonarch.py:26); ent is then
+ * not read either.
+ * The caller provides a device workspace of vmb_fea_bwd_workspace_bytes() bytes (256-byte
+ * aligned); its contents need not be initialised.
+ */
+typedef struct vmb_fea_bwd_args {
+  const void* q;    int64_t q_bs;
+  const void* k;    int64_t k_bs;
+  const void* v;    int64_t v_bs;
+  const void* v2;   int64_t v2_bs;
+  const void* o;    int64_t o_bs;    /* forward output                         */
+  const void* dout; int64_t do_bs;   /* gradient of o, [batch][n_q][dv]        */
+  const float* lse;                  /* forward lse, [batch][n_q]              */
+  const float* ent;                  /* forward entropy (read only with dent)  */
+  const float* dent;                 /* gradient of ent or NULL                */
+  void* grad_q;  int64_t grad_q_bs;   /* [batch][n_q][d]                        */
+  void* grad_k;  int64_t grad_k_bs;   /* [batch][n_kv][d]                       */
+  void* grad_v;  int64_t grad_v_bs;   /* [batch][n_kv][dv1]  (NULL if v_is_k)   */
+  void* grad_v2; int64_t grad_v2_bs;  /* [batch][n_kv][dv-dv1] (NULL if no v2)  */
+  void* workspace; int64_t workspace_bytes;
+  int64_t batch, n_q, n_kv;
+  int32_t d, dv, dv1, dtype;
+  int32_t grad_mode, v_is_k;
+  float sm_scale;
+} vmb_fea_bwd_args;
+
+int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);
+int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream);
+
+/*
+ * Monarch L step (the b dense m x m blocks), forward and backward, for `bh` heads of
+ * N = m * b tokens. Replaces the einsum / softmax / col_mass / scaling ops of
+ * video_monarch_attention/vmonarch.py:51-63 (forward) and their autograd backward.
+ *   q    [bh][N][d]   original queries        out [bh][N][dw] R-step output
+ *   ent  [bh][N]      R-step row entropy (the reference's -neg_ent)
+ * forward, last == 0: u  [bh][N][d]    next R-step queries (already scaled)
+ * forward, last == 1: z  [bh][N][dw-d] Monarch output; tokens < skip_rows are left unwritten
+ * backward, last == 0: du [bh][N][d] fp32 gradient of u
+ * backward, last == 1: dz [bh][N][dw-d] gradient of z; tokens < skip_rows carry none
+ * backward outputs: dq [bh][N][d] fp32 (ADDED into), dout [bh][N][dw] gradient of out.
+ * m <= 64, d in {64, 128}, dw - d in {64, 128, 256} when last.
+ */
+typedef struct vmb_lstep_args {
+  const void* q;
+  const void* out;
+  const float* ent;
+  void* u;
+  void* z;
+  const float* du;
+  const void* dz;
+  float* dq;
+  void* dout;
+  int64_t bh, m, b;
+  int32_t d, dw, dtype, last;
+  int64_t skip_rows;
+  float scale, min_col_mass;
+} vmb_lstep_args;
+
+int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream);
+int vmb_lstep_bwd(const vmb_lstep_args* a, void* stream);
+
+/* dst[b][i] = (dtype) src[b][i], i < n (n and both batch strides multiples of 4).
+ * Converts the fp32 gradient accumulators of grad_mode 1 to the element dtype. */
+int vmb_cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
+                 int32_t dtype, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* VMONARCH_B200_H */

@@ -1,0 +1,97 @@
+"""FlashEntropyAttention on the B200 against the fp32 oracle and the reference's golden vectors.
+
+Tolerances, checked both ways:
+  reference convention (tests/test_vmonarch.py:22-42): max|x - ref| <= tol * max|ref|, o/e 2e-2,
+      gradients 3e-2;
+  north-star absolute bounds: o max-abs 2e-2 and mean-abs 2e-3; e within 1e-3 of max|e|;
+      gradients max-abs 5e-2 (floored at 8e-3 * max|grad|, the bf16 rounding of large gradients).
+"""
+import pytest
+import torch
+
+import oracle
+from conftest import FEA_GOLDEN, load_golden, max_rel_err
+from vmonarch_b200 import flash_entropy_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def run_cuda(q, k, v, do, de, dtype=torch.bfloat16, sm_scale=None):
+    leaves = [t.cuda().to(dtype).requires_grad_() for t in (q, k, v)]
+    o, e = flash_entropy_attention(*leaves, sm_scale=sm_scale)
+    grads = torch.autograd.grad((o.float() * do.cuda()).sum() + (e * de.cuda()).sum(), leaves)
+    torch.cuda.synchronize()
+    return [t.detach().float().cpu() for t in (o, e, *grads)]
+
+
+def run_oracle(q, k, v, do, de, sm_scale):
+    leaves = [t.float().clone().requires_grad_() for t in (q, k, v)]
+    o, e = oracle.entropy_attention(*leaves, sm_scale)
+    grads = torch.autograd.grad((o * do).sum() + (e * de).sum(), leaves)
+    return [t.detach() for t in (o, e, *grads)]
+
+
+def check(got, ref):
+    o, e, *g = got
+    o_r, e_r, *g_r = ref
+    assert max_rel_err(o, o_r) <= 2e-2 and max_rel_err(e, e_r) <= 2e-2
+    for a, b in zip(g, g_r):
+        assert max_rel_err(a, b) <= 3e-2
+    assert (o - o_r).abs().max() <= 2e-2 and (o - o_r).abs().mean() <= 2e-3
+    assert (e - e_r).abs().max() <= 1e-3 * e_r.abs().max()
+    for a, b in zip(g, g_r):
+        assert (a - b).abs().max() <= max(5e-2, 8e-3 * b.abs().max().item())
+
+
+@pytest.mark.parametrize("name", FEA_GOLDEN)
+def test_fea_against_reference_golden(name):
+    g = load_golden(name)
+    got = run_cuda(g["q"], g["k"], g["v"], g["do"], g["de"])
+    check(got, [g[x] for x in ("o", "e", "dq", "dk", "dv")])
+
+
+@pytest.mark.parametrize("N", [128, 200, 1024])
+@pytest.mark.parametrize("D, Dv", [(64, 64), (128, 128), (64, 128), (128, 256)])
+def test_flash_entropy_attention(N, D, Dv):
+    # the reference's test matrix (tests/test_vmonarch.py:27-42): B=2, H=3, random dO and dE
+    gen = torch.Generator().manual_seed(0)
+    q, k = (torch.randn(2, 3, N, D, generator=gen).bfloat16().float() for _ in range(2))
+    v = torch.randn(2, 3, N, Dv, generator=gen).bfloat16().float()
+    do, de = torch.randn(2, 3, N, Dv, generator=gen), torch.randn(2, 3, N, generator=gen)
+    check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
+
+
+@pytest.mark.parametrize("N", [1, 17, 64, 127, 129, 333])
+def test_ragged_and_tiny_sequences(N):
+    gen = torch.Generator().manual_seed(N)
+    q, k, v = (torch.randn(1, 5, N, 64, generator=gen).bfloat16().float() for _ in range(3))
+    do, de = torch.randn(1, 5, N, 64, generator=gen), torch.randn(1, 5, N, generator=gen)
+    check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, 0.125))
+
+
+def test_fp16_and_custom_scale():
+    gen = torch.Generator().manual_seed(7)
+    q, k, v = (torch.randn(1, 2, 300, 128, generator=gen).half().float() for _ in range(3))
+    do, de = torch.randn(1, 2, 300, 128, generator=gen), torch.randn(1, 2, 300, generator=gen)
+    got = run_cuda(q, k, v, do, de, dtype=torch.float16, sm_scale=0.05)
+    check(got, run_oracle(q, k, v, do, de, 0.05))
+
+
+def test_noncontiguous_inputs_and_no_mutation():
+    gen = torch.Generator().manual_seed(8)
+    base = torch.randn(1, 200, 2, 64, generator=gen).bfloat16().cuda()
+    q = base.transpose(1, 2)  # (1, 2, 200, 64) non-contiguous view
+    snapshot = base.clone()
+    o, e = flash_entropy_attention(q, q, q)
+    o2, e2 = flash_entropy_attention(q.contiguous(), q.contiguous(), q.contiguous())
+    torch.cuda.synchronize()
+    assert torch.equal(base, snapshot)
+    assert torch.equal(o, o2) and torch.equal(e, e2)
+
+
+def test_deterministic_forward():
+    gen = torch.Generator().manual_seed(9)
+    q, k, v = (torch.randn(2, 2, 500, 128, generator=gen).bfloat16().cuda() for _ in range(3))
+    a = flash_entropy_attention(q, k, v)
+    b = flash_entropy_attention(q, k, v)
+    assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])

@@ -1,0 +1,98 @@
+"""VMonarch attention on the B200 against the fp32 oracle (the reference's own fp32 graph) and the
+reference's golden vectors. Tolerances follow tests/test_vmonarch.py:45-66 (max-relative: z 3e-2,
+gradients 5e-2)."""
+import pytest
+import torch
+import torch.nn.functional as F
+
+import oracle
+from conftest import VM_GOLDEN, load_golden, max_rel_err
+from vmonarch_b200 import VMonarchAttention, vmonarch_attention
+
+pytestmark = pytest.mark.gpu
+
+
+def run_cuda(q, k, v, dz, m, b, iters, r, dtype=torch.bfloat16):
+    leaves = [t.cuda().to(dtype).requires_grad_() for t in (q, k, v)]
+    z = vmonarch_attention(*leaves, m, b, iters, recompute_tokens=r)
+    grads = torch.autograd.grad((z.float() * dz.cuda()).sum(), leaves)
+    torch.cuda.synchronize()
+    return [t.detach().float().cpu() for t in (z, *grads)]
+
+
+def run_oracle(q, k, v, dz, m, b, iters, r, device="cpu"):
+    leaves = [t.float().to(device).clone().requires_grad_() for t in (q, k, v)]
+    z = oracle.vmonarch_attention(*leaves, m, b, iters, recompute_tokens=r)
+    grads = torch.autograd.grad((z * dz.to(device)).sum(), leaves)
+    return [t.detach().cpu() for t in (z, *grads)]
+
+
+def check(got, ref):
+    assert max_rel_err(got[0], ref[0]) <= 3e-2
+    for a, b in zip(got[1:], ref[1:]):
+        assert max_rel_err(a, b) <= 5e-2
+
+
+@pytest.mark.parametrize("name", VM_GOLDEN)
+def test_vmonarch_against_reference_golden(name):
+    g = load_golden(name)
+    B, H, m, b, D, iters, r, _ = g["meta"].tolist()
+    check(run_cuda(g["q"], g["k"], g["v"], g["dz"], m, b, iters, r), [g[x] for x in ("z", "dq", "dk", "dv")])
+
+
+@pytest.mark.parametrize("m, b", [(4, 256), (8, 100)])
+@pytest.mark.parametrize("num_iters", [1, 2, 3])
+def test_vmonarch_attention(m, b, num_iters):
+    # the reference's test matrix (tests/test_vmonarch.py:45-66): B=1, H=2, D=64, recompute = b
+    gen = torch.Generator().manual_seed(0)
+    q, k, v = (torch.randn(1, 2, m * b, 64, generator=gen).bfloat16().float() for _ in range(3))
+    dz = torch.randn(1, 2, m * b, 64, generator=gen)
+    check(run_cuda(q, k, v, dz, m, b, num_iters, b), run_oracle(q, k, v, dz, m, b, num_iters, b))
+
+
+@pytest.mark.parametrize("m, b, iters, r", [(16, 256, 2, 256), (21, 200, 2, 200), (5, 130, 3, 0), (1, 64, 2, 10)])
+def test_vmonarch_head_dim_128(m, b, iters, r):
+    gen = torch.Generator().manual_seed(m * b)
+    q, k, v = (torch.randn(1, 1, m * b, 128, generator=gen).bfloat16().float() for _ in range(3))
+    dz = torch.randn(1, 1, m * b, 128, generator=gen)
+    check(run_cuda(q, k, v, dz, m, b, iters, r), run_oracle(q, k, v, dz, m, b, iters, r))
+
+
+def test_recompute_tokens_are_exact():
+    # tests/test_vmonarch.py:69-74
+    torch.manual_seed(0)
+    q, k, v = (torch.randn(1, 2, 4 * 128, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    z = vmonarch_attention(q, k, v, 4, 128, recompute_tokens=128)
+    exact = F.scaled_dot_product_attention(q, k, v)
+    torch.testing.assert_close(z[:, :, :128], exact[:, :, :128])
+
+
+def test_recompute_everything_is_full_attention():
+    torch.manual_seed(1)
+    q, k, v = (torch.randn(1, 2, 3 * 64, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3))
+    z = vmonarch_attention(q, k, v, 3, 64, recompute_tokens=10_000)
+    torch.testing.assert_close(z, F.scaled_dot_product_attention(q, k, v))
+
+
+def test_fp16_vmonarch():
+    gen = torch.Generator().manual_seed(3)
+    q, k, v = (torch.randn(1, 1, 4 * 96, 64, generator=gen).half().float() for _ in range(3))
+    dz = torch.randn(1, 1, 4 * 96, 64, generator=gen)
+    check(run_cuda(q, k, v, dz, 4, 96, 2, 96, dtype=torch.float16), run_oracle(q, k, v, dz, 4, 96, 2, 96))
+
+
+def test_module_readme_usage():
+    attn = VMonarchAttention(num_blocks=16, block_size=256, num_iters=2)
+    B, H, N, D = 2, 4, 16 * 256, 128
+    q, k, v = (torch.randn(B, H, N, D, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    o = attn(q, k, v, recompute_tokens=256)
+    assert o.shape == (B, H, N, D) and o.dtype == torch.bfloat16 and torch.isfinite(o.float()).all()
+    ref = oracle.vmonarch_attention(q[:1, :1].float(), k[:1, :1].float(), v[:1, :1].float(), 16, 256, 2, 256)
+    assert max_rel_err(o[:1, :1].float(), ref) <= 3e-2
+
+
+def test_inference_mode_saves_nothing():
+    q = torch.randn(1, 2, 4 * 64, 64, device="cuda", dtype=torch.bfloat16)
+    with torch.no_grad():
+        z = vmonarch_attention(q, q, q, 4, 64, recompute_tokens=64)
+    assert z.grad_fn is None

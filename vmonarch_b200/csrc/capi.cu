@@ -1,0 +1,207 @@
+// extern "C" entry points declared in include/vmonarch_b200.h: argument validation, workspace
+// carving and dispatch to the kernel files.
+#include <atomic>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+
+#include "../../include/vmonarch_b200.h"
+#include "launch.h"
+
+static constexpr float kLog2eHost = 1.4426950408889634f;
+
+namespace {
+
+thread_local std::string g_last_error;
+std::atomic<uint64_t> g_launches{0};
+
+void count(int n) { g_launches.fetch_add((uint64_t)n, std::memory_order_relaxed); }
+
+int fail(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+
+int cuda_status(cudaError_t e, const char* what) {
+  if (e == cudaSuccess) return VMB_OK;
+  if (e == cudaErrorNotSupported) return fail(VMB_ENOTSUP, "%s: unsupported head dimensions", what);
+  return fail(VMB_ECUDA, "%s: %s", what, cudaGetErrorString(e));
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+
+bool fea_dims_ok(int d, int dv) {
+  return (d == 64 || d == 128) && (dv == 64 || dv == 128 || dv == 256) && dv % d == 0;
+}
+
+int check_common(const char* what, int64_t batch, int64_t n_q, int64_t n_kv, int d, int dv, int dv1, int dtype,
+                 const void* v2) {
+  if (dtype != VMB_DTYPE_BF16 && dtype != VMB_DTYPE_F16) return fail(VMB_EINVAL, "%s: unknown dtype %d", what, dtype);
+  if (batch < 0 || n_q < 0 || n_kv < 1) return fail(VMB_EINVAL, "%s: bad sizes batch=%lld n_q=%lld n_kv=%lld", what,
+                                                   (long long)batch, (long long)n_q, (long long)n_kv);
+  if (n_q > 0x7fffffff || n_kv > 0x7fffffff) return fail(VMB_EINVAL, "%s: sequence longer than 2^31-1", what);
+  if (!fea_dims_ok(d, dv)) return fail(VMB_ENOTSUP, "%s: no kernel for head dims d=%d dv=%d", what, d, dv);
+  if (dv1 <= 0 || dv1 > dv || dv1 % 8) return fail(VMB_EINVAL, "%s: dv1=%d must be a multiple of 8 in (0, dv]", what, dv1);
+  if ((dv1 < dv) != (v2 != nullptr)) return fail(VMB_EINVAL, "%s: v2 must be given exactly when dv1 < dv", what);
+  return VMB_OK;
+}
+
+int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
+
+}  // namespace
+
+extern "C" {
+
+int vmb_abi_version(void) { return VMB_ABI_VERSION; }
+
+const char* vmb_last_error(void) { return g_last_error.c_str(); }
+
+uint64_t vmb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
+
+int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
+  if (!a) return fail(VMB_EINVAL, "vmb_fea_fwd: null args");
+  int rc = check_common("vmb_fea_fwd", a->batch, a->n_q, a->n_kv, a->d, a->dv, a->dv1, a->dtype, a->v2);
+  if (rc) return rc;
+  if (a->batch == 0 || a->n_q == 0) return VMB_OK;
+  if (!a->q || !a->k || !a->v || !a->o) return fail(VMB_EINVAL, "vmb_fea_fwd: null tensor pointer");
+  if (!aligned16(a->q) || !aligned16(a->k) || !aligned16(a->v) || !aligned16(a->o) || (a->v2 && !aligned16(a->v2)))
+    return fail(VMB_EINVAL, "vmb_fea_fwd: tensors must be 16-byte aligned");
+  if ((a->q_bs | a->k_bs | a->v_bs | a->o_bs | a->v2_bs) & 7)
+    return fail(VMB_EINVAL, "vmb_fea_fwd: batch strides must be multiples of 8 elements");
+  vmb::FwdParams p{};
+  p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.o = a->o; p.lse = a->lse; p.ent = a->ent;
+  p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.o_bs = a->o_bs;
+  p.n_q = (int)a->n_q; p.n_kv = (int)a->n_kv; p.dv1 = a->dv1;
+  p.scale_log2 = a->sm_scale * kLog2eHost;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  count(1);
+  return cuda_status(vmb::fea_fwd_mma(p, a->batch, a->d, a->dv, a->ent != nullptr, a->dtype == VMB_DTYPE_BF16, st),
+                     "vmb_fea_fwd");
+}
+
+int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
+  if (!a || a->batch < 0 || a->n_q < 0) return -1;
+  const int64_t rows = a->batch * a->n_q;
+  int64_t bytes = 2 * round_up(rows * 4, 256);
+  if (a->grad_mode == 0) bytes += round_up(rows * a->d * 4, 256);
+  return bytes;
+}
+
+int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
+  if (!a) return fail(VMB_EINVAL, "vmb_fea_bwd: null args");
+  int rc = check_common("vmb_fea_bwd", a->batch, a->n_q, a->n_kv, a->d, a->dv, a->dv1, a->dtype, a->v2);
+  if (rc) return rc;
+  if (a->grad_mode != 0 && a->grad_mode != 1) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_mode must be 0 or 1");
+  if (a->v_is_k && (a->dv1 != a->d || a->grad_v != nullptr))
+    return fail(VMB_EINVAL, "vmb_fea_bwd: v_is_k needs dv1 == d and grad_v == NULL");
+  if (!a->v_is_k && !a->grad_v) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_v is NULL");
+  if ((a->dv1 < a->dv) != (a->grad_v2 != nullptr))
+    return fail(VMB_EINVAL, "vmb_fea_bwd: grad_v2 must be given exactly when dv1 < dv");
+  if (!a->q || !a->k || !a->v || !a->o || !a->dout || !a->lse || !a->grad_q || !a->grad_k)
+    return fail(VMB_EINVAL, "vmb_fea_bwd: null tensor pointer");
+  if (a->dent && !a->ent) return fail(VMB_EINVAL, "vmb_fea_bwd: dent given without ent");
+  const void* ptrs[] = {a->q, a->k, a->v, a->v2, a->o, a->dout, a->grad_q, a->grad_k, a->grad_v, a->grad_v2,
+                        a->workspace};
+  for (const void* ptr : ptrs)
+    if (ptr && !aligned16(ptr)) return fail(VMB_EINVAL, "vmb_fea_bwd: tensors must be 16-byte aligned");
+  if ((a->q_bs | a->k_bs | a->v_bs | a->v2_bs | a->o_bs | a->do_bs | a->grad_q_bs | a->grad_k_bs | a->grad_v_bs |
+       a->grad_v2_bs) & 7)
+    return fail(VMB_EINVAL, "vmb_fea_bwd: batch strides must be multiples of 8 elements");
+  if (a->batch == 0) return VMB_OK;
+  const int64_t need = vmb_fea_bwd_workspace_bytes(a);
+  if (!a->workspace || a->workspace_bytes < need)
+    return fail(VMB_EINVAL, "vmb_fea_bwd: workspace of %lld bytes needed", (long long)need);
+  if (a->n_q == 0) return VMB_OK;  // no query: no gradient contribution (grad_mode 1 adds nothing)
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = a->dtype == VMB_DTYPE_BF16;
+  const int64_t rows = a->batch * a->n_q;
+  char* ws = static_cast<char*>(a->workspace);
+  float* cc = reinterpret_cast<float*>(ws);
+  float* gg = reinterpret_cast<float*>(ws + round_up(rows * 4, 256));
+  float* dq_acc = a->grad_mode == 0 ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
+
+  count(dq_acc ? 3 : 2);
+  cudaError_t e = vmb::fea_bwd_pre(a->o, a->o_bs, a->dout, a->do_bs, a->lse, a->ent, a->dent, cc, gg, a->batch,
+                                   (int)a->n_q, a->dv, bf16, st);
+  if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(pre)");
+  if (dq_acc) {
+    e = cudaMemsetAsync(dq_acc, 0, rows * a->d * 4, st);
+    if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(memset)");
+  }
+  vmb::BwdParams p{};
+  p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.dout = a->dout; p.lse = a->lse; p.cc = cc; p.gg = gg;
+  p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
+  p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
+  p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.do_bs = a->do_bs;
+  p.dq_bs = dq_acc ? a->n_q * a->d : a->grad_q_bs;
+  p.dk_bs = a->grad_k_bs; p.dv_bs = a->grad_v_bs; p.dv2_bs = a->grad_v2_bs;
+  p.n_q = (int)a->n_q; p.n_kv = (int)a->n_kv; p.dv1 = a->dv1;
+  p.acc_kv = a->grad_mode;
+  p.sm_scale = a->sm_scale;
+  p.scale_log2 = a->sm_scale * kLog2eHost;
+  e = vmb::fea_bwd_mma(p, a->batch, a->d, a->dv, a->v_is_k != 0, bf16, st);
+  if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd");
+  if (dq_acc) {
+    e = vmb::cast_f32(dq_acc, a->n_q * a->d, a->grad_q, a->grad_q_bs, a->batch, a->n_q * a->d, bf16, st);
+    if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(dq cast)");
+  }
+  return VMB_OK;
+}
+
+static int lstep_check(const char* what, const vmb_lstep_args* a, bool bwd) {
+  if (!a) return fail(VMB_EINVAL, "%s: null args", what);
+  if (a->dtype != VMB_DTYPE_BF16 && a->dtype != VMB_DTYPE_F16) return fail(VMB_EINVAL, "%s: unknown dtype", what);
+  if (a->d != 64 && a->d != 128) return fail(VMB_ENOTSUP, "%s: no kernel for d=%d", what, a->d);
+  if (a->m < 1 || a->m > 64) return fail(VMB_ENOTSUP, "%s: num_blocks m=%lld outside [1, 64]", what, (long long)a->m);
+  if (a->b < 1 || a->bh < 0) return fail(VMB_EINVAL, "%s: bad sizes", what);
+  if (a->last) {
+    const int dv = a->dw - a->d;
+    if (dv != 64 && dv != 128 && dv != 256) return fail(VMB_ENOTSUP, "%s: no kernel for value dim %d", what, dv);
+  } else if (a->dw != a->d) {
+    return fail(VMB_EINVAL, "%s: non-last step needs dw == d", what);
+  }
+  if (!a->q || !a->out || !a->ent) return fail(VMB_EINVAL, "%s: null tensor pointer", what);
+  if (!bwd && !(a->last ? a->z : a->u)) return fail(VMB_EINVAL, "%s: null output pointer", what);
+  if (bwd && (!a->dq || !a->dout || !(a->last ? (const void*)a->dz : (const void*)a->du)))
+    return fail(VMB_EINVAL, "%s: null gradient pointer", what);
+  const void* ptrs[] = {a->q, a->out, a->u, a->z, a->du, a->dz, a->dq, a->dout};
+  for (const void* p : ptrs)
+    if (p && !aligned16(p)) return fail(VMB_EINVAL, "%s: tensors must be 16-byte aligned", what);
+  return VMB_OK;
+}
+
+static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* stream) {
+  int rc = lstep_check(what, a, bwd);
+  if (rc) return rc;
+  if (a->bh == 0) return VMB_OK;
+  count(1);
+  vmb::LstepParams p{};
+  p.q = a->q; p.out = a->out; p.ent = a->ent; p.u = a->u; p.z = a->z; p.du = a->du; p.dz = a->dz;
+  p.dq = a->dq; p.dout = a->dout;
+  p.bh = a->bh; p.m = a->m; p.b = a->b; p.d = a->d; p.dw = a->dw; p.skip_rows = a->skip_rows;
+  p.scale = a->scale; p.min_col_mass = a->min_col_mass;
+  return cuda_status(vmb::lstep_launch(p, a->last != 0, bwd, a->dtype == VMB_DTYPE_BF16, static_cast<cudaStream_t>(stream)),
+                     what);
+}
+
+int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream) { return lstep_run("vmb_lstep_fwd", a, false, stream); }
+int vmb_lstep_bwd(const vmb_lstep_args* a, void* stream) { return lstep_run("vmb_lstep_bwd", a, true, stream); }
+
+int vmb_cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n, int32_t dtype,
+                 void* stream) {
+  if (dtype != VMB_DTYPE_BF16 && dtype != VMB_DTYPE_F16) return fail(VMB_EINVAL, "vmb_cast_f32: unknown dtype");
+  if (batch < 0 || n < 0 || (n | src_bs | dst_bs) & 3) return fail(VMB_EINVAL, "vmb_cast_f32: sizes must be multiples of 4");
+  if (batch == 0 || n == 0) return VMB_OK;
+  if (!src || !dst || !aligned16(src) || (reinterpret_cast<uintptr_t>(dst) & 7))
+    return fail(VMB_EINVAL, "vmb_cast_f32: bad pointer");
+  count(1);
+  return cuda_status(vmb::cast_f32(src, src_bs, dst, dst_bs, batch, n, dtype == VMB_DTYPE_BF16, static_cast<cudaStream_t>(stream)),
+                     "vmb_cast_f32");
+}
+
+}  // extern "C"

@@ -1,0 +1,41 @@
+// Kernel-side parameter blocks for the FlashEntropyAttention kernels. These are filled by the
+// C-ABI layer (capi.cu) from the public argument structs declared in include/vmonarch_b200.h.
+#pragma once
+#include <stdint.h>
+
+namespace vmb {
+
+struct FwdParams {
+  const void* q;   // [batch][n_q][D]
+  const void* k;   // [batch][n_kv][D]
+  const void* v;   // [batch][n_kv][dv1]   -> o columns [0, dv1)
+  const void* v2;  // [batch][n_kv][DV-dv1] -> o columns [dv1, DV)
+  void* o;         // [batch][n_q][DV]
+  float* lse;      // [batch][n_q]  log2-domain LSE of x = s * sm_scale * log2(e)
+  float* ent;      // [batch][n_q]  natural-log row entropy
+  int64_t q_bs, k_bs, v_bs, v2_bs, o_bs;  // batch strides in elements
+  int n_q, n_kv, dv1, n_qtiles;
+  float scale_log2;  // sm_scale * log2(e)
+};
+
+struct BwdParams {
+  const void* q;
+  const void* k;
+  const void* v;
+  const void* v2;
+  const void* dout;   // [batch][n_q][DV]
+  const float* lse;   // [batch][n_q]
+  const float* cc;    // [batch][n_q]  delta_i + dE_i * (E_i - LSE_i)
+  const float* gg;    // [batch][n_q]  dE_i * ln(2)
+  float* dq;          // fp32 accumulator [batch][n_q][D] (batch stride dq_bs)
+  void* dk;           // [batch][n_kv][D]      element type or fp32 (acc_kv)
+  void* dv;           // [batch][n_kv][dv1]    unused when v aliases k
+  void* dv2;          // [batch][n_kv][DV-dv1]
+  int64_t q_bs, k_bs, v_bs, v2_bs, do_bs, dq_bs, dk_bs, dv_bs, dv2_bs;
+  int n_q, n_kv, dv1, n_ktiles;
+  int acc_kv;         // 1: dk/dv/dv2 are fp32 buffers that are added into
+  float scale_log2;   // sm_scale * log2(e)
+  float sm_scale;
+};
+
+}  // namespace vmb

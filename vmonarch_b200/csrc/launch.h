@@ -1,0 +1,35 @@
+// Internal (C++) launch interface between the C-ABI layer (capi.cu) and the kernel files.
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include "fea_params.h"
+
+namespace vmb {
+
+struct LstepParams {
+  const void* q;      // [bh][N][D]
+  const void* out;    // [bh][N][dw]   R-step output; cols [0,D) -> kr, [D,dw) -> y (last step)
+  const float* ent;   // [bh][N]       R-step row entropy
+  void* u;            // fwd, non-last: [bh][N][D]
+  void* z;            // fwd, last:     [bh][N][dw-D]
+  const float* du;    // bwd, non-last: [bh][N][D] fp32 gradient of u
+  const void* dz;     // bwd, last:     [bh][N][dw-D]
+  float* dq;          // bwd: [bh][N][D] fp32, added into
+  void* dout;         // bwd: [bh][N][dw] gradient of `out`
+  int64_t bh, m, b;
+  int d, dw;
+  int64_t skip_rows;  // tokens [0, skip_rows) of every head are not produced / carry no gradient
+  float scale, min_col_mass;
+};
+
+cudaError_t fea_fwd_mma(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, cudaStream_t st);
+cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
+cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
+                        const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
+                        bool bf16, cudaStream_t st);
+cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
+                     bool bf16, cudaStream_t st);
+cudaError_t lstep_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
+size_t lstep_smem_bytes(int m, int d, int dw, bool last, bool bwd);
+
+}  // namespace vmb

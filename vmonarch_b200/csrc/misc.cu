@@ -1,0 +1,96 @@
+// Small HBM-bound helpers of the FlashEntropyAttention backward.
+//
+// fea_bwd_pre replaces _attn_bwd_preprocess (video_monarch_attention/kernel.py:154-162) and also
+// folds the entropy-gradient terms of kernel.py:202/241 into two per-row constants:
+//   c_i = sum_d o_id dO_id + dE_i (E_i - LSE_i)     (LSE_i natural: LSE2_i * ln 2)
+//   g_i = dE_i ln 2
+// so the main backward kernel computes dS = P (dP - c_i - g_i x_ij) with one extra FMA.
+#include "common.cuh"
+#include "launch.h"
+
+namespace vmb {
+
+// one warp per row, 16-byte loads
+template <typename T>
+__global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_bs, const T* dout, int64_t do_bs,
+                                                          const float* lse, const float* ent, const float* dent,
+                                                          float* cc, float* gg, int64_t rows, int n_q, int dv) {
+  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  const int64_t bi = row / n_q, r = row % n_q;
+  const T* orow = o + bi * o_bs + r * dv;
+  const T* drow = dout + bi * do_bs + r * dv;
+  float acc = 0.f;
+  for (int c = lane; c < dv / 8; c += 32) {
+    const uint4 a = *reinterpret_cast<const uint4*>(orow + c * 8);
+    const uint4 b = *reinterpret_cast<const uint4*>(drow + c * 8);
+    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const float2 fa = Elem<T>::unpack(wa[e]), fb = Elem<T>::unpack(wb[e]);
+      acc = fmaf(fa.x, fb.x, acc);
+      acc = fmaf(fa.y, fb.y, acc);
+    }
+  }
+#pragma unroll
+  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (lane == 0) {
+    float c = acc, g = 0.f;
+    if (dent) {
+      const float de = dent[row];
+      c = fmaf(de, ent[row] - lse[row] * kLn2, acc);
+      g = de * kLn2;
+    }
+    cc[row] = c;
+    gg[row] = g;
+  }
+}
+
+cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
+                        const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
+                        bool bf16, cudaStream_t st) {
+  const int64_t rows = batch * n_q;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if (bf16)
+    fea_bwd_pre_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
+        static_cast<const __nv_bfloat16*>(o), o_bs, static_cast<const __nv_bfloat16*>(dout), do_bs, lse, ent, dent,
+        cc, gg, rows, n_q, dv);
+  else
+    fea_bwd_pre_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __half*>(o), o_bs,
+                                                                  static_cast<const __half*>(dout), do_bs, lse, ent,
+                                                                  dent, cc, gg, rows, n_q, dv);
+  return cudaGetLastError();
+}
+
+// dst[b][i] = (T) src[b][i] for i < n, 4 elements per thread (n % 4 == 0, strides % 4 == 0)
+template <typename T>
+__global__ void cast_f32_kernel(const float* src, int64_t src_bs, T* dst, int64_t dst_bs, int64_t n4, int64_t total4) {
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total4; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t bi = idx / n4, i = (idx % n4) * 4;
+    const float4 v = *reinterpret_cast<const float4*>(src + bi * src_bs + i);
+    uint2 w;
+    w.x = Elem<T>::pack(v.x, v.y);
+    w.y = Elem<T>::pack(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst + bi * dst_bs + i) = w;
+  }
+}
+
+cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n, bool bf16,
+                     cudaStream_t st) {
+  const int64_t n4 = n / 4, total4 = batch * n4;
+  if (total4 == 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (total4 + 255) / 256;
+  const unsigned blocks = (unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  if (bf16)
+    cast_f32_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, src_bs, static_cast<__nv_bfloat16*>(dst), dst_bs, n4, total4);
+  else
+    cast_f32_kernel<__half><<<blocks, 256, 0, st>>>(src, src_bs, static_cast<__half*>(dst), dst_bs, n4, total4);
+  return cudaGetLastError();
+}
+
+}  // namespace vmb

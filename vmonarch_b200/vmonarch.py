@@ -1,0 +1,170 @@
+"""
+VMonarch attention on the B200 kernels.
+
+Drop-in for ``video_monarch_attention.vmonarch`` (reference ``video_monarch_attention/vmonarch.py``).
+The N = m * b tokens lie on an (m, b) grid, token n -> (n // b, n % b). The attention map is
+approximated by a Monarch matrix: R = m dense (b x b) blocks mixing tokens inside a grid row, and
+L = b dense (m x m) blocks mixing tokens inside a grid column, fitted by `num_iters` steps of
+alternating minimisation (reference vmonarch.py:1-11).
+
+Execution per iteration (all on the C ABI, no torch math on the hot path):
+  R step: FlashEntropyAttention over the B*H*m grid rows (vmb_fea_fwd, entropy on). The first
+          iteration folds the reference's u = q * scale (vmonarch.py:47) into sm_scale, and the last
+          iteration reads [k | v] through two value pointers instead of torch.cat (vmonarch.py:50).
+  L step: one fused kernel per iteration (vmb_lstep_fwd) for the einsum / softmax / column mass /
+          rescale of vmonarch.py:51-63.
+Recompute: the first `recompute_tokens` queries run exact attention (vmb_fea_fwd without entropy)
+          written straight into rows [0, r) of z, replacing SDPA + torch.cat (vmonarch.py:66-68).
+The backward is hand-derived (the reference relies on autograd through the same ops) and
+accumulates dq / dk / dv in fp32 across the recompute and every R and L step.
+"""
+from __future__ import annotations
+
+import torch
+import torch.nn as nn
+
+from . import ops
+from .kernel import _check_inputs
+
+
+class _VMonarchAttention(torch.autograd.Function):
+
+    @staticmethod
+    def forward(ctx, q, k, v, num_blocks, block_size, num_iters, recompute_tokens, min_col_mass):
+        B, H, N, D = q.shape
+        Dv = v.shape[-1]
+        m, b = num_blocks, block_size
+        BH = B * H
+        scale = D ** -0.5
+        qf = q.contiguous().view(BH, N, D)
+        kf = k.contiguous().view(BH, N, D)
+        vf = v.contiguous().view(BH, N, Dv)
+        dev, dt = q.device, q.dtype
+        rr = min(max(int(recompute_tokens), 0), N)
+        grid = lambda t: t.view(BH * m, b, t.size(-1))  # noqa: E731  (grid rows as FEA batches)
+
+        steps = []
+        u = qf
+        z = None
+        for it in range(num_iters):
+            last = it == num_iters - 1
+            Dw = D + Dv if last else D
+            out = torch.empty((BH, N, Dw), device=dev, dtype=dt)
+            lse = torch.empty((BH, N), device=dev, dtype=torch.float32)
+            ent = torch.empty((BH, N), device=dev, dtype=torch.float32)
+            sm = scale if it == 0 else 1.0
+            ops.fea_fwd(grid(u), grid(kf), grid(kf), grid(out), lse.view(BH * m, b), ent.view(BH * m, b), sm,
+                        v2=grid(vf) if last else None)
+            if last:
+                z = torch.empty((BH, N, Dv), device=dev, dtype=dt)
+                ops.lstep_fwd(qf, out, ent, m, b, scale, min_col_mass, z=z, skip_rows=rr)
+                nxt = None
+            else:
+                nxt = torch.empty((BH, N, D), device=dev, dtype=dt)
+                ops.lstep_fwd(qf, out, ent, m, b, scale, min_col_mass, u=nxt)
+            steps.append((u, out, lse, ent, sm))
+            u = nxt
+
+        lse_r = None
+        if rr > 0:
+            lse_r = torch.empty((BH, rr), device=dev, dtype=torch.float32)
+            ops.fea_fwd(qf[:, :rr], kf, vf, z[:, :rr], lse_r, None, scale)
+
+        ctx.meta = (B, H, N, D, Dv, m, b, rr, scale, min_col_mass)
+        if any(ctx.needs_input_grad[:3]):
+            flat = [qf, kf, vf, z] + ([lse_r] if lse_r is not None else [])
+            for s in steps:
+                flat.extend(s[:4])
+            ctx.save_for_backward(*flat)
+            ctx.sms = [s[4] for s in steps]
+        return z.view(B, H, N, Dv)
+
+    @staticmethod
+    def backward(ctx, dz):
+        B, H, N, D, Dv, m, b, rr, scale, min_col_mass = ctx.meta
+        BH = B * H
+        saved = ctx.saved_tensors
+        qf, kf, vf, z = saved[:4]
+        pos = 4
+        lse_r = None
+        if rr > 0:
+            lse_r = saved[4]
+            pos = 5
+        steps = [saved[pos + 4 * i: pos + 4 * i + 4] for i in range(len(ctx.sms))]
+        dev, dt = qf.device, qf.dtype
+        dz = dz.to(dt).contiguous().view(BH, N, Dv)
+        grid = lambda t: t.view(BH * m, b, t.size(-1))  # noqa: E731
+
+        dq_acc = torch.zeros((BH, N, D), device=dev, dtype=torch.float32)
+        dk_acc = torch.zeros((BH, N, D), device=dev, dtype=torch.float32)
+        dv_acc = torch.zeros((BH, N, Dv), device=dev, dtype=torch.float32)
+        if rr > 0:
+            ops.fea_bwd(qf[:, :rr], kf, vf, z[:, :rr], dz[:, :rr], lse_r, dq_acc[:, :rr], dk_acc, dv_acc, scale,
+                        grad_mode=1)
+
+        du = None
+        n_it = len(steps)
+        for it in reversed(range(n_it)):
+            u, out, lse, ent = steps[it]
+            sm = ctx.sms[it]
+            last = it == n_it - 1
+            dout = torch.empty_like(out)
+            if last:
+                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, dz=dz, skip_rows=rr)
+            else:
+                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, du=du)
+            gq = dq_acc if it == 0 else torch.zeros((BH, N, D), device=dev, dtype=torch.float32)
+            ops.fea_bwd(grid(u), grid(kf), grid(kf), grid(out), grid(dout), lse.view(BH * m, b), grid(gq),
+                        grid(dk_acc), None, sm, v2=grid(vf) if last else None,
+                        grad_v2=grid(dv_acc) if last else None, grad_mode=1, v_is_k=True)
+            du = gq
+
+        dq = torch.empty((B, H, N, D), device=dev, dtype=dt)
+        dk = torch.empty((B, H, N, D), device=dev, dtype=dt)
+        dv = torch.empty((B, H, N, Dv), device=dev, dtype=dt)
+        ops.cast_f32(dq_acc, dq)
+        ops.cast_f32(dk_acc, dk)
+        ops.cast_f32(dv_acc, dv)
+        return dq, dk, dv, None, None, None, None, None
+
+
+def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_tokens=0, min_col_mass=0.01):
+    """
+    Args:
+        q, k: (B, H, N, D); v: (B, H, N, Dv), with N == num_blocks * block_size.
+        num_blocks: m, number of grid rows (keep it small).
+        block_size: b, number of tokens per grid row.
+        num_iters: alternating-minimization steps.
+        recompute_tokens: the first `recompute_tokens` queries use exact attention.
+        min_col_mass: lower bound of the column mass of L, for stability.
+    Returns:
+        (B, H, N, Dv)
+    """
+    B, H, N, D = q.shape
+    assert N == num_blocks * block_size, f"N={N} != {num_blocks} * {block_size}"
+    if num_iters < 1:
+        # the reference leaves z unbound when the loop does not run (vmonarch.py:48-65)
+        raise UnboundLocalError("cannot access local variable 'z' where it is not associated with a value")
+    _check_inputs(q, k, v)
+    Dv = v.shape[-1]
+    # the last R step attends over [k | v] (vmonarch.py:50): its value width D + Dv must be a
+    # multiple of D and a width the reference kernel accepts (kernel.py:260, 324)
+    assert (D + Dv) % D == 0 and D + Dv <= 256, f"D + Dv = {D + Dv} is not a valid last-step value width"
+    return _VMonarchAttention.apply(q, k, v, int(num_blocks), int(block_size), int(num_iters), recompute_tokens,
+                                    float(min_col_mass))
+
+
+class VMonarchAttention(nn.Module):
+    def __init__(self, num_blocks, block_size, num_iters=2, min_col_mass=0.01):
+        super().__init__()
+        self.num_blocks = num_blocks
+        self.block_size = block_size
+        self.num_iters = num_iters
+        self.min_col_mass = min_col_mass
+
+    def forward(self, q, k, v, recompute_tokens=0):
+        return vmonarch_attention(q, k, v, self.num_blocks, self.block_size, self.num_iters,
+                                  recompute_tokens, self.min_col_mass)
+
+    def extra_repr(self):
+        return f"num_blocks={self.num_blocks}, block_size={self.block_size}, num_iters={self.num_iters}"
