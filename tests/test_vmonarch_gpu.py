@@ -58,20 +58,33 @@ def test_vmonarch_head_dim_128(m, b, iters, r):
     check(run_cuda(q, k, v, dz, m, b, iters, r), run_oracle(q, k, v, dz, m, b, iters, r))
 
 
+def check_exact_rows(z, q, k, v, r):
+    """Rows [0, r) are exact attention. The reference checks them with assert_close against SDPA
+    (tests/test_vmonarch.py:69-74), which is what it computes them with; here they come from this
+    library's kernel, which rounds P to bf16 at different points than SDPA's backend, so they are
+    held to the fp32 bound (max-abs 2e-2, mean-abs 2e-3), to SDPA's own error against fp32, and to
+    SDPA itself within bf16 output noise."""
+    exact32 = F.scaled_dot_product_attention(q.float(), k.float(), v.float())[:, :, :r]
+    sdpa = F.scaled_dot_product_attention(q, k, v)[:, :, :r]
+    err = (z[:, :, :r].float() - exact32).abs()
+    err_sdpa = (sdpa.float() - exact32).abs()
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3
+    assert err.max() <= 2 * err_sdpa.max() + 1e-3 and err.mean() <= 2 * err_sdpa.mean() + 1e-4
+    torch.testing.assert_close(z[:, :, :r], sdpa, rtol=1.6e-2, atol=2e-3)
+
+
 def test_recompute_tokens_are_exact():
-    # tests/test_vmonarch.py:69-74
     torch.manual_seed(0)
     q, k, v = (torch.randn(1, 2, 4 * 128, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3))
     z = vmonarch_attention(q, k, v, 4, 128, recompute_tokens=128)
-    exact = F.scaled_dot_product_attention(q, k, v)
-    torch.testing.assert_close(z[:, :, :128], exact[:, :, :128])
+    check_exact_rows(z, q, k, v, 128)
 
 
 def test_recompute_everything_is_full_attention():
     torch.manual_seed(1)
     q, k, v = (torch.randn(1, 2, 3 * 64, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3))
     z = vmonarch_attention(q, k, v, 3, 64, recompute_tokens=10_000)
-    torch.testing.assert_close(z, F.scaled_dot_product_attention(q, k, v))
+    check_exact_rows(z, q, k, v, 3 * 64)
 
 
 def test_fp16_vmonarch():
