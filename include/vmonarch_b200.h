@@ -113,6 +113,23 @@ int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);
 int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream);
 
 /*
+ * vmb_fea_bwd for callers that cannot allocate device memory. No counterpart in the reference.
+ * Same arguments and results as vmb_fea_bwd, but `workspace` / `workspace_bytes` are ignored: the
+ * scratch comes from a 32 MiB array compiled into the library (a static __device__ buffer that
+ * every GPU holding the library's module keeps until the process exits). Meant for hosts that
+ * cannot hand over a workspace: plugins whose enqueue hook must not allocate because the host
+ * framework owns all device memory, foreign-language bindings that can only pass the user's
+ * tensors, and pipelines that cannot afford cudaMalloc inside a step.
+ *  - Calls whose workspace need (vmb_fea_bwd_workspace_bytes) exceeds 32 MiB return VMB_EINVAL.
+ *  - The first call on a device looks the buffer's address up with that device current; make
+ *    that first call before any stream capture begins.
+ *  - All calls share the buffer, which keeps the previous call's contents (the backward clears
+ *    what must start at zero). Calls that overlap on the GPU race on it: serialise them.
+ *  - Calls no cudaMalloc, cudaFree or other allocating routine.
+ */
+int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream);
+
+/*
  * Monarch L step (the b dense m x m blocks), forward and backward, for `bh` heads of
  * N = m * b tokens. Replaces the einsum / softmax / col_mass / scaling ops of
  * video_monarch_attention/vmonarch.py:51-63 (forward) and their autograd backward.

@@ -81,6 +81,7 @@ SIGNATURES = {
     "vmb_fea_fwd": (ctypes.c_int, [ctypes.POINTER(FeaFwdArgs), c_vp]),
     "vmb_fea_bwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaBwdArgs)]),
     "vmb_fea_bwd": (ctypes.c_int, [ctypes.POINTER(FeaBwdArgs), c_vp]),
+    "vmb_fea_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(FeaBwdArgs), c_vp]),
     "vmb_lstep_fwd": (ctypes.c_int, [ctypes.POINTER(LstepArgs), c_vp]),
     "vmb_lstep_bwd": (ctypes.c_int, [ctypes.POINTER(LstepArgs), c_vp]),
     "vmb_cast_f32": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp]),

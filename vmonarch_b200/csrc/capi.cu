@@ -55,6 +55,18 @@ int64_t round_up(int64_t x, int64_t a) { return (x + a - 1) / a * a; }
 
 }  // namespace
 
+namespace vmb {
+int set_error(int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  g_last_error = buf;
+  return code;
+}
+}  // namespace vmb
+
 extern "C" {
 
 int vmb_abi_version(void) { return VMB_ABI_VERSION; }

@@ -32,4 +32,7 @@ cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs
 cudaError_t lstep_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
 size_t lstep_smem_bytes(int m, int d, int dw, bool last, bool bwd);
 
+// Records `code` and a printf-style message as the calling thread's last error; returns `code`.
+int set_error(int code, const char* fmt, ...);
+
 }  // namespace vmb
