@@ -52,6 +52,7 @@ def parse_args():
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="dit14b")
     ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
     ap.add_argument("--seed", type=int, default=0)
+    ap.add_argument("--heads", type=int, default=0, help="run only this many heads of the layer (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=150.0, help="wall-clock cap of the CPU reference arm")
@@ -118,6 +119,14 @@ def unit_plan(w: Workload, info: shard.RankInfo, scaling: str):
     if scaling == "weak":
         return range(w.H), info.rank, info.world
     return shard.unit_range(w.H, info.rank, info.world), 0, 1
+
+
+def restrict_heads(w: Workload, heads: int) -> Workload:
+    """The workload with only `heads` heads (profiling runs); 0 keeps it whole."""
+    if heads <= 0 or heads >= w.H:
+        return w
+    from dataclasses import replace
+    return replace(w, H=heads, name=f"{w.name}[{heads} heads]")
 
 
 def make_step(w: Workload, api):
@@ -283,7 +292,7 @@ def base_line(args, w, n_gpus, ms, value, impl=None) -> dict:
 def run_ours(args, info, device):
     import vmonarch_b200 as api
     from vmonarch_b200 import ops
-    w = WORKLOADS[args.workload]
+    w = restrict_heads(WORKLOADS[args.workload], args.heads)
     heads, seed_off, layers = unit_plan(w, info, args.scaling)
     q, k, v, do, de = make_inputs(w, seed=args.seed + seed_off, heads=heads, pin=True)
     dev = [t.to(device, non_blocking=True) for t in (q, k, v, do, de)]

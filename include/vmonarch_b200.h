@@ -42,6 +42,13 @@ int vmb_abi_version(void);
 /* Human-readable description of the last error returned on the calling thread. */
 const char* vmb_last_error(void);
 
+/* Pipeline-timeout status of the tcgen05 kernels on the current device: synchronises `stream`,
+ * stores into *out the OR of the error codes recorded since the last call (0 = none) and clears
+ * them. A kernel whose pipeline wait exceeds its time limit (~2 s) records a code, drains its
+ * in-flight copies and MMAs, frees its tensor memory and exits instead of hanging; its outputs
+ * are then invalid. No counterpart in the reference (Triton kernels have no such check). */
+int vmb_device_status(void* stream, int32_t* out);
+
 /* Number of kernels this library has launched in the process so far (all threads, all devices).
  * Diagnostic with no reference counterpart: the benchmark reports it as its launch count. */
 uint64_t vmb_kernel_launches(void);

@@ -23,6 +23,15 @@ def pytest_collection_modifyitems(config, items):
             item.add_marker(skip)
 
 
+@pytest.fixture(autouse=True)
+def _device_status_clean(request):
+    """After every GPU test: no tcgen05 pipeline wait may have timed out (vmb_device_status)."""
+    yield
+    if "gpu" in request.keywords and torch.cuda.is_available():
+        from vmonarch_b200 import _native
+        assert _native.device_status(torch.device("cuda", torch.cuda.current_device())) == 0
+
+
 def load_golden(name: str) -> dict:
     """Fixture arrays; bf16 bit patterns (uint16) are decoded to fp32 tensors."""
     data = np.load(GOLDEN / f"{name}.npz")

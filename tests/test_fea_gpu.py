@@ -95,3 +95,21 @@ def test_deterministic_forward():
     a = flash_entropy_attention(q, k, v)
     b = flash_entropy_attention(q, k, v)
     assert torch.equal(a[0], b[0]) and torch.equal(a[1], b[1])
+
+
+@pytest.mark.parametrize("D, Dv", [(128, 128), (128, 256), (64, 64)])
+def test_growing_row_max_forces_rescales(D, Dv):
+    # Later key tiles score far higher than the first ones, so the running max of many (but not
+    # all) rows jumps by more than the lazy-rescale threshold at different tiles: exercises the
+    # O / l / h rescale path with rows of one warp disagreeing.
+    gen = torch.Generator().manual_seed(21)
+    N = 640
+    q = torch.randn(1, 2, N, D, generator=gen)
+    k = torch.randn(1, 2, N, D, generator=gen)
+    boost = torch.linspace(0.0, 3.0, N).view(1, 1, N, 1)
+    c = torch.randn(1, 2, 1, D, generator=gen)
+    q = (q + 1.5 * c * (torch.rand(1, 2, N, 1, generator=gen) > 0.5)).bfloat16().float()
+    k = (k + boost * c).bfloat16().float()
+    v = torch.randn(1, 2, N, Dv, generator=gen).bfloat16().float()
+    do, de = torch.randn(1, 2, N, Dv, generator=gen), torch.randn(1, 2, N, generator=gen)
+    check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))

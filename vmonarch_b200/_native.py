@@ -78,6 +78,7 @@ SIGNATURES = {
     "vmb_abi_version": (ctypes.c_int, []),
     "vmb_last_error": (ctypes.c_char_p, []),
     "vmb_kernel_launches": (ctypes.c_uint64, []),
+    "vmb_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int32)]),
     "vmb_fea_fwd": (ctypes.c_int, [ctypes.POINTER(FeaFwdArgs), c_vp]),
     "vmb_fea_bwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaBwdArgs)]),
     "vmb_fea_bwd": (ctypes.c_int, [ctypes.POINTER(FeaBwdArgs), c_vp]),
@@ -123,6 +124,13 @@ def dtype_code(dt: torch.dtype) -> int:
 
 def ptr(t: torch.Tensor | None) -> int | None:
     return None if t is None else t.data_ptr()
+
+
+def device_status(device: torch.device) -> int:
+    """OR of the pipeline-timeout codes recorded by the kernels since the last call (0 = none)."""
+    out = ctypes.c_int32(0)
+    check(lib.vmb_device_status(stream_ptr(device), ctypes.byref(out)), "vmb_device_status")
+    return out.value
 
 
 def stream_ptr(device: torch.device) -> int:

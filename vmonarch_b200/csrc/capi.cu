@@ -75,6 +75,15 @@ const char* vmb_last_error(void) { return g_last_error.c_str(); }
 
 uint64_t vmb_kernel_launches(void) { return g_launches.load(std::memory_order_relaxed); }
 
+int vmb_device_status(void* stream, int32_t* out) {
+  if (!out) return fail(VMB_EINVAL, "vmb_device_status: null output");
+  int v = 0;
+  const cudaError_t e = vmb::fea_fwd_sm100_status(static_cast<cudaStream_t>(stream), &v);
+  if (e != cudaSuccess) return cuda_status(e, "vmb_device_status");
+  *out = v;
+  return VMB_OK;
+}
+
 int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   if (!a) return fail(VMB_EINVAL, "vmb_fea_fwd: null args");
   int rc = check_common("vmb_fea_fwd", a->batch, a->n_q, a->n_kv, a->d, a->dv, a->dv1, a->dtype, a->v2);
@@ -91,9 +100,13 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   p.n_q = (int)a->n_q; p.n_kv = (int)a->n_kv; p.dv1 = a->dv1;
   p.scale_log2 = a->sm_scale * kLog2eHost;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  const bool bf16 = a->dtype == VMB_DTYPE_BF16;
+  // V aliasing K (the VMonarch R step): the key tile in shared memory doubles as the value tile
+  const bool vk = a->v == a->k && a->v_bs == a->k_bs && a->dv1 == a->d;
   count(1);
-  return cuda_status(vmb::fea_fwd_mma(p, a->batch, a->d, a->dv, a->ent != nullptr, a->dtype == VMB_DTYPE_BF16, st),
-                     "vmb_fea_fwd");
+  if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk))
+    return cuda_status(vmb::fea_fwd_sm100(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, vk, st), "vmb_fea_fwd");
+  return cuda_status(vmb::fea_fwd_mma(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, st), "vmb_fea_fwd");
 }
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
