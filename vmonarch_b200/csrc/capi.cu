@@ -210,8 +210,11 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
   p.dq = a->dq; p.dout = a->dout;
   p.bh = a->bh; p.m = a->m; p.b = a->b; p.d = a->d; p.dw = a->dw; p.skip_rows = a->skip_rows;
   p.scale = a->scale; p.min_col_mass = a->min_col_mass;
-  return cuda_status(vmb::lstep_launch(p, a->last != 0, bwd, a->dtype == VMB_DTYPE_BF16, static_cast<cudaStream_t>(stream)),
-                     what);
+  const bool bf16 = a->dtype == VMB_DTYPE_BF16;
+  const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (vmb::lstep_mma_supported(p, a->last != 0))
+    return cuda_status(vmb::lstep_mma_launch(p, a->last != 0, bwd, bf16, st), what);
+  return cuda_status(vmb::lstep_launch(p, a->last != 0, bwd, bf16, st), what);
 }
 
 int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream) { return lstep_run("vmb_lstep_fwd", a, false, stream); }

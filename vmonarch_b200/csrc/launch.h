@@ -33,6 +33,8 @@ cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t d
                         bool bf16, cudaStream_t st);
 cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
                      bool bf16, cudaStream_t st);
+bool lstep_mma_supported(const LstepParams& p, bool last);
+cudaError_t lstep_mma_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
 cudaError_t lstep_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
 size_t lstep_smem_bytes(int m, int d, int dw, bool last, bool bwd);
 

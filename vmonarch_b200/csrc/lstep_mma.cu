@@ -1,0 +1,510 @@
+// Monarch L step on warp-level tensor-core MMA (mma.sync m16n8k16, fp32 accumulate), m <= 32.
+//
+// Same mathematics as lstep.cu (reference video_monarch_attention/vmonarch.py:51-63 and its
+// autograd backward); this is the fast path for the shapes VMonarch uses (Dv == D, m <= 32).
+// One warp owns one grid column j of one (batch, head): it gathers the m rows q_i = q[i*b + j]
+// and out_k = out[k*b + j] (16-byte cp.async, rows padded to MP = 16 or 32 with zeros), and
+// every m x m x D contraction is a handful of MMAs out of swizzled shared memory. The L step is
+// HBM-bound (~10 flop/byte), so the tensor cores only serve to keep the arithmetic off the
+// critical path; outputs are staged in shared memory and written with 16-byte stores.
+//
+// Forward: logits = scale * q out_D^T (+ ent_k), a = softmax_k (fp32 registers)
+//   non-last: c_k = scale / max(sum_i a_ik, min_col_mass);  u_k = c_k * sum_i a_ik q_i
+//   last:     z_i = sum_k a_ik y_k   (tokens < skip_rows are left to the exact recompute)
+// Backward (non-last), with G = q du^T:
+//   dc_k = sum_i a_ik G_ik,  dcm_k = [cs_k > min_col_mass] (-dc_k c_k / cm_k),
+//   dA = c_k G_ik + dcm_k,   dlog = a (dA - rowsum(a dA)),
+//   dq_i += sum_k a_ik c_k du_k + scale * sum_k dlog_ik out_k,  dout_k = scale * sum_i dlog_ik q_i
+// Backward (last): dA = dz y^T, dlog as above, dq_i += scale * sum_k dlog_ik out_k,
+//   dout_k[:D] = scale * sum_i dlog_ik q_i,  dout_k[D:] = sum_i a_ik dz_i
+#include "common.cuh"
+#include "launch.h"
+
+namespace vmb {
+namespace {
+
+constexpr int kWarps = 4;
+
+template <int MP>
+struct Tile {
+  static constexpr int MT = MP / 16;  // 16-row MMA tiles over i (or k)
+  static constexpr int NT = MP / 8;   // 8-col MMA tiles over k
+  static constexpr int SA = MP + 8;   // row stride (elements) of the m x m staging tile
+};
+
+// C[i][k] += sum_d X[i][d] * Y[k][d] over D (X, Y: MP rows, swizzled, XCH chunks per row; the
+// contraction starts at chunk xc0 / yc0).
+template <typename T, int MP, int D, int XCH, int YCH>
+__device__ __forceinline__ void mm_rows(float (&acc)[MP / 16][MP / 8][4], const T* X, int xc0, const T* Y, int yc0,
+                                        int lane) {
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t a[MP / 16][4];
+#pragma unroll
+    for (int mt = 0; mt < MP / 16; ++mt)
+      ldsm_x4(smem_u32(X + swz<XCH>(mt * 16 + (lane & 15), xc0 + kk * 2 + (lane >> 4))), a[mt][0], a[mt][1],
+              a[mt][2], a[mt][3]);
+#pragma unroll
+    for (int np = 0; np < MP / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(Y + swz<YCH>(np * 16 + (lane & 7) + ((lane >> 4) << 3), yc0 + kk * 2 + ((lane >> 3) & 1))), b0,
+              b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < MP / 16; ++mt) {
+        mma16816<T>(acc[mt][2 * np], a[mt], b0, b1);
+        mma16816<T>(acc[mt][2 * np + 1], a[mt], b2, b3);
+      }
+    }
+  }
+}
+
+// Packs rows (mt) x k-step (kk) of an accumulator-layout MP x MP fp32 matrix into an A fragment.
+template <typename T, int MP>
+__device__ __forceinline__ void frag_from_acc(const float (&v)[MP / 16][MP / 8][4], int mt, int kk, uint32_t (&a)[4]) {
+  a[0] = Elem<T>::pack(v[mt][2 * kk][0], v[mt][2 * kk][1]);
+  a[1] = Elem<T>::pack(v[mt][2 * kk][2], v[mt][2 * kk][3]);
+  a[2] = Elem<T>::pack(v[mt][2 * kk + 1][0], v[mt][2 * kk + 1][1]);
+  a[3] = Elem<T>::pack(v[mt][2 * kk + 1][2], v[mt][2 * kk + 1][3]);
+}
+
+// Writes an accumulator-layout MP x MP matrix to a row-major [MP][SA] staging tile (bf16/fp16).
+template <typename T, int MP>
+__device__ __forceinline__ void stage_mm(T* S, const float (&v)[MP / 16][MP / 8][4], int lane) {
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int r = mt * 16 + (lane >> 2) + h * 8, c = nt * 8 + (lane & 3) * 2;
+        *reinterpret_cast<uint32_t*>(S + r * Tile<MP>::SA + c) = Elem<T>::pack(v[mt][nt][2 * h], v[mt][nt][2 * h + 1]);
+      }
+}
+
+// out[r][n] (r: MP rows, n: 64 columns from chunk bc0 of B) = sum_i A[r][i] * B[i][n]
+// where A comes from the [MP][SA] staging tile TRANSPOSED (A[r][i] = S[i][r]) and B rows are i.
+template <typename T, int MP, int BCH>
+__device__ __forceinline__ void mm_tn64(float (&acc)[MP / 16][8][4], const T* S, const T* B, int bc0, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < MP / 16; ++kk) {
+    uint32_t a[MP / 16][4];
+    const int mi = lane >> 3;
+#pragma unroll
+    for (int mt = 0; mt < MP / 16; ++mt)
+      ldsm_x4_t(smem_u32(S + (kk * 16 + (lane & 7) + ((mi >> 1) << 3)) * Tile<MP>::SA + mt * 16 + ((mi & 1) << 3)),
+                a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
+    const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(smem_u32(B + swz<BCH>(r, bc0 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < MP / 16; ++mt) {
+        mma16816<T>(acc[mt][2 * np], a[mt], b0, b1);
+        mma16816<T>(acc[mt][2 * np + 1], a[mt], b2, b3);
+      }
+    }
+  }
+}
+
+// out[i][n] += sum_k A[i][k] * B[k][n] with A given in accumulator layout (registers).
+template <typename T, int MP, int BCH>
+__device__ __forceinline__ void mm_rn64(float (&acc)[MP / 16][8][4], const float (&A)[MP / 16][MP / 8][4], const T* B,
+                                        int bc0, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < MP / 16; ++kk) {
+    uint32_t a[MP / 16][4];
+#pragma unroll
+    for (int mt = 0; mt < MP / 16; ++mt) frag_from_acc<T, MP>(A, mt, kk, a[mt]);
+    const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(smem_u32(B + swz<BCH>(r, bc0 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < MP / 16; ++mt) {
+        mma16816<T>(acc[mt][2 * np], a[mt], b0, b1);
+        mma16816<T>(acc[mt][2 * np + 1], a[mt], b2, b3);
+      }
+    }
+  }
+}
+
+template <int MP>
+__device__ __forceinline__ void zero(float (&a)[MP / 16][8][4]) {
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int n = 0; n < 8; ++n) a[mt][n][0] = a[mt][n][1] = a[mt][n][2] = a[mt][n][3] = 0.f;
+}
+
+// 64 output columns (half of D = 128 or all of D = 64) of an accumulator -> swizzled staging rows.
+template <typename T, int MP, int CH>
+__device__ __forceinline__ void stage_rows64(T* S, int c0, const float (&v)[MP / 16][8][4], const float* rowscale,
+                                             int lane) {
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + (lane >> 2) + h * 8;
+      const float s = rowscale ? rowscale[r] : 1.f;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int col = c0 * 8 + nt * 8 + (lane & 3) * 2;
+        *reinterpret_cast<uint32_t*>(S + swz<CH>(r, col >> 3) + (col & 7)) =
+            Elem<T>::pack(v[mt][nt][2 * h] * s, v[mt][nt][2 * h + 1] * s);
+      }
+    }
+}
+
+// Gathers rows i < m (token i*b + j) of a [N][W] tensor, columns [c0*8, (c0+nch)*8), into a
+// swizzled [MP][CH] tile; rows >= m, and rows whose token < skip, are zero-filled.
+template <typename T, int CH>
+__device__ __forceinline__ void gather(T* dst, const T* src, int64_t W, int c0, int nch, int m, int64_t b, int j,
+                                       int64_t skip, int MP, int lane) {
+  for (int c = lane; c < MP * nch; c += 32) {
+    const int i = c / nch, ch = c % nch;
+    const int64_t tok = (int64_t)i * b + j;
+    const bool ok = i < m && tok >= skip;
+    cp_async16(smem_u32(dst + swz<CH>(i, c0 + ch)), src + (ok ? tok : 0) * W + (c0 + ch) * 8, ok ? 16 : 0);
+  }
+}
+
+// Writes rows r < m of a swizzled [MP][CH] staging tile to token r*b + j of a [N][W] tensor.
+template <typename T, int CH>
+__device__ __forceinline__ void scatter(T* dst, const T* S, int64_t W, int c0, int nch, int m, int64_t b, int j,
+                                        int64_t skip, int MP, int lane) {
+  for (int c = lane; c < MP * nch; c += 32) {
+    const int r = c / nch, ch = c % nch;
+    const int64_t tok = (int64_t)r * b + j;
+    if (r < m && tok >= skip)
+      *reinterpret_cast<uint4*>(dst + tok * W + (c0 + ch) * 8) = *reinterpret_cast<const uint4*>(S + swz<CH>(r, c0 + ch));
+  }
+}
+
+// logits -> a = softmax over valid k of (scale * logit + ent_k); padded rows / columns become 0.
+template <int MP>
+__device__ __forceinline__ void softmax_rows(float (&acc)[MP / 16][MP / 8][4], const float (&ent)[MP / 8][2],
+                                             float scale, int m, int lane) {
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float mx = -INFINITY;
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const int k = nt * 8 + (lane & 3) * 2 + e;
+          const float x = k < m ? (acc[mt][nt][2 * h + e] * scale + ent[nt][e]) * kLog2e : -INFINITY;
+          acc[mt][nt][2 * h + e] = x;
+          mx = fmaxf(mx, x);
+        }
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      float s = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          const float pv = exp2f(acc[mt][nt][2 * h + e] - mx);
+          acc[mt][nt][2 * h + e] = pv;
+          s += pv;
+        }
+      s += __shfl_xor_sync(0xffffffffu, s, 1);
+      s += __shfl_xor_sync(0xffffffffu, s, 2);
+      const bool row_ok = mt * 16 + (lane >> 2) + h * 8 < m;
+      const float inv = row_ok ? 1.f / s : 0.f;
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) acc[mt][nt][2 * h + e] *= inv;
+    }
+}
+
+// Column sums over all rows: result for this thread's columns (nt, e), replicated across lane>>2.
+template <int MP>
+__device__ __forceinline__ void col_sums(const float (&v)[MP / 16][MP / 8][4], float (&cs)[MP / 8][2]) {
+#pragma unroll
+  for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float s = 0.f;
+#pragma unroll
+      for (int mt = 0; mt < MP / 16; ++mt) s += v[mt][nt][e] + v[mt][nt][2 + e];
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 8);
+      s += __shfl_xor_sync(0xffffffffu, s, 16);
+      cs[nt][e] = s;
+    }
+}
+
+template <typename T, int MP>
+__device__ __forceinline__ void load_ent(float (&ent)[MP / 8][2], const float* e, int64_t b, int j, int m, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+    for (int x = 0; x < 2; ++x) {
+      const int k = nt * 8 + (lane & 3) * 2 + x;
+      ent[nt][x] = k < m ? e[(int64_t)k * b + j] : 0.f;
+    }
+}
+
+// ============================================================================ forward
+template <typename T, int MP, int D, bool LAST>
+__global__ void __launch_bounds__(kWarps * 32) lstep_fwd_mma_kernel(const LstepParams p) {
+  constexpr int DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr size_t PER_WARP = (size_t)(MP * D + MP * OW + MP * Tile<MP>::SA) * sizeof(T) + MP * sizeof(float);
+  T* sq = reinterpret_cast<T*>(smem_raw + warp * PER_WARP);
+  T* so = sq + MP * D;
+  T* sa = so + MP * OW;
+  float* svec = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);
+
+  const int64_t col = (int64_t)blockIdx.x * kWarps + warp;
+  if (col >= p.bh * p.b) return;  // no block-level barrier below: each warp is independent
+  const int64_t bh = col / p.b;
+  const int j = (int)(col % p.b), m = (int)p.m;
+  const int64_t N = p.m * p.b;
+  const T* gq = static_cast<const T*>(p.q) + bh * N * D;
+  const T* go = static_cast<const T*>(p.out) + bh * N * p.dw;
+  gather<T, DCH>(sq, gq, D, 0, DCH, m, p.b, j, 0, MP, lane);
+  gather<T, OCH>(so, go, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);
+  cp_async_commit();
+  float ent[MP / 8][2];
+  load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
+  cp_async_wait<0>();
+  __syncwarp();
+
+  float a[MP / 16][MP / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < MP / 8; ++nt) a[mt][nt][0] = a[mt][nt][1] = a[mt][nt][2] = a[mt][nt][3] = 0.f;
+  mm_rows<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, lane);
+  softmax_rows<MP>(a, ent, p.scale, m, lane);
+
+  if (LAST) {
+    // z_i = sum_k a_ik y_k -> staged in sq (q no longer needed)
+    __syncwarp();
+    T* gz = static_cast<T*>(p.z) + bh * N * D;
+#pragma unroll 1
+    for (int half = 0; half < D / 64; ++half) {
+      float z[MP / 16][8][4];
+      zero<MP>(z);
+      mm_rn64<T, MP, OCH>(z, a, so, DCH + half * 8, lane);
+      stage_rows64<T, MP, DCH>(sq, half * 8, z, nullptr, lane);
+    }
+    __syncwarp();
+    scatter<T, DCH>(gz, sq, D, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
+  } else {
+    float cs[MP / 8][2];
+    col_sums<MP>(a, cs);
+    if ((lane >> 2) == 0) {
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) svec[nt * 8 + lane * 2 + e] = p.scale / fmaxf(cs[nt][e], p.min_col_mass);
+    }
+    stage_mm<T, MP>(sa, a, lane);
+    __syncwarp();
+    T* gu = static_cast<T*>(p.u) + bh * N * D;
+#pragma unroll 1
+    for (int half = 0; half < D / 64; ++half) {
+      float u[MP / 16][8][4];
+      zero<MP>(u);
+      mm_tn64<T, MP, DCH>(u, sa, sq, half * 8, lane);
+      stage_rows64<T, MP, OCH>(so, half * 8, u, svec, lane);  // so (out_D) is free after the logits
+    }
+    __syncwarp();
+    scatter<T, OCH>(gu, so, D, 0, DCH, m, p.b, j, 0, MP, lane);
+  }
+}
+
+// ============================================================================ backward
+template <typename T, int MP, int D, bool LAST>
+__global__ void __launch_bounds__(kWarps * 32) lstep_bwd_mma_kernel(const LstepParams p) {
+  constexpr int DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  constexpr size_t PER_WARP = (size_t)(2 * MP * D + MP * OW + 2 * MP * Tile<MP>::SA) * sizeof(T);
+  T* sq = reinterpret_cast<T*>(smem_raw + warp * PER_WARP);
+  T* so = sq + MP * D;      // out rows (kr | y), later the dout staging
+  T* sg = so + MP * OW;     // du (non-last) or dz (last), element dtype
+  T* sa = sg + MP * D;      // m x m staging (a or a*c)
+  T* sd = sa + MP * Tile<MP>::SA;  // m x m staging (dlog)
+
+  const int64_t col = (int64_t)blockIdx.x * kWarps + warp;
+  if (col >= p.bh * p.b) return;
+  const int64_t bh = col / p.b;
+  const int j = (int)(col % p.b), m = (int)p.m;
+  const int64_t N = p.m * p.b;
+  gather<T, DCH>(sq, static_cast<const T*>(p.q) + bh * N * D, D, 0, DCH, m, p.b, j, 0, MP, lane);
+  gather<T, OCH>(so, static_cast<const T*>(p.out) + bh * N * p.dw, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);
+  if (LAST) gather<T, DCH>(sg, static_cast<const T*>(p.dz) + bh * N * D, D, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
+  cp_async_commit();
+  if (!LAST) {  // du is fp32: convert while the other rows are in flight
+    const float* du = p.du + bh * N * D;
+    for (int c = lane; c < MP * DCH; c += 32) {
+      const int k = c / DCH, ch = c % DCH;
+      uint4 w = make_uint4(0, 0, 0, 0);
+      if (k < m) {
+        const float4 v0 = *reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * D + ch * 8);
+        const float4 v1 = *reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * D + ch * 8 + 4);
+        w.x = Elem<T>::pack(v0.x, v0.y);
+        w.y = Elem<T>::pack(v0.z, v0.w);
+        w.z = Elem<T>::pack(v1.x, v1.y);
+        w.w = Elem<T>::pack(v1.z, v1.w);
+      }
+      *reinterpret_cast<uint4*>(sg + swz<DCH>(k, ch)) = w;
+    }
+  }
+  float ent[MP / 8][2];
+  load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
+  cp_async_wait<0>();
+  __syncwarp();
+
+  float a[MP / 16][MP / 8][4], g[MP / 16][MP / 8][4], ac[MP / 16][MP / 8][4];
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) a[mt][nt][e] = g[mt][nt][e] = ac[mt][nt][e] = 0.f;
+  mm_rows<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, lane);
+  softmax_rows<MP>(a, ent, p.scale, m, lane);
+
+  if (LAST) {
+    // dA = dz y^T
+    mm_rows<T, MP, D, DCH, OCH>(g, sg, 0, so, DCH, lane);
+  } else {
+    // G = q du^T ; dc_k = sum_i a_ik G_ik ; dA = c_k G_ik + dcm_k ; ac = a * c for the dq term
+    mm_rows<T, MP, D, DCH, DCH>(g, sq, 0, sg, 0, lane);
+    float cs[MP / 8][2], dc[MP / 8][2];
+    col_sums<MP>(a, cs);
+#pragma unroll
+    for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 4; ++e) ac[mt][nt][e] = a[mt][nt][e] * g[mt][nt][e];
+    col_sums<MP>(ac, dc);
+#pragma unroll
+    for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float cm = fmaxf(cs[nt][e], p.min_col_mass);
+        const float c = p.scale / cm;
+        const float dcm = cs[nt][e] > p.min_col_mass ? -dc[nt][e] * c / cm : 0.f;
+#pragma unroll
+        for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+          for (int h = 0; h < 2; ++h) {
+            g[mt][nt][2 * h + e] = c * g[mt][nt][2 * h + e] + dcm;   // dA
+            ac[mt][nt][2 * h + e] = a[mt][nt][2 * h + e] * c;        // a * c
+          }
+      }
+  }
+  // dlog = a (dA - rowsum(a dA)), computed in place in g and pre-multiplied by scale
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float rs = 0.f;
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+        rs += a[mt][nt][2 * h] * g[mt][nt][2 * h] + a[mt][nt][2 * h + 1] * g[mt][nt][2 * h + 1];
+      rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+      rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+#pragma unroll
+      for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) g[mt][nt][2 * h + e] = a[mt][nt][2 * h + e] * (g[mt][nt][2 * h + e] - rs) * p.scale;
+    }
+  stage_mm<T, MP>(sd, g, lane);
+  if (LAST) stage_mm<T, MP>(sa, a, lane);
+  __syncwarp();
+
+  // dq_i += sum_k (scale dlog_ik) out_k  [non-last: + sum_k (a_ik c_k) du_k]
+  float* gdq = p.dq + bh * N * D;
+#pragma unroll 1
+  for (int half = 0; half < D / 64; ++half) {
+    float acc[MP / 16][8][4];
+    zero<MP>(acc);
+    mm_rn64<T, MP, OCH>(acc, g, so, half * 8, lane);
+    if (!LAST) mm_rn64<T, MP, DCH>(acc, ac, sg, half * 8, lane);
+#pragma unroll
+    for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int i = mt * 16 + (lane >> 2) + h * 8;
+        if (i >= m) continue;
+        float* dst = gdq + ((int64_t)i * p.b + j) * D + half * 64 + (lane & 3) * 2;
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt) {
+          float2 v = *reinterpret_cast<float2*>(dst + nt * 8);
+          v.x += acc[mt][nt][2 * h];
+          v.y += acc[mt][nt][2 * h + 1];
+          *reinterpret_cast<float2*>(dst + nt * 8) = v;
+        }
+      }
+  }
+  __syncwarp();
+  // dout_k[:D] = sum_i (scale dlog_ik) q_i ; last: dout_k[D:] = sum_i a_ik dz_i   (staged in so)
+  T* gdo = static_cast<T*>(p.dout) + bh * N * p.dw;
+#pragma unroll 1
+  for (int half = 0; half < D / 64; ++half) {
+    float acc[MP / 16][8][4];
+    zero<MP>(acc);
+    mm_tn64<T, MP, DCH>(acc, sd, sq, half * 8, lane);
+    stage_rows64<T, MP, OCH>(so, half * 8, acc, nullptr, lane);
+  }
+  if (LAST) {
+#pragma unroll 1
+    for (int half = 0; half < D / 64; ++half) {
+      float acc[MP / 16][8][4];
+      zero<MP>(acc);
+      mm_tn64<T, MP, DCH>(acc, sa, sg, half * 8, lane);
+      stage_rows64<T, MP, OCH>(so, DCH + half * 8, acc, nullptr, lane);
+    }
+  }
+  __syncwarp();
+  scatter<T, OCH>(gdo, so, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);
+}
+
+template <typename T, int MP, int D, bool LAST>
+cudaError_t launch(const LstepParams& p, bool bwd, cudaStream_t st) {
+  constexpr int OW = LAST ? 2 * D : D;
+  const size_t per_warp = bwd ? (size_t)(2 * MP * D + MP * OW + 2 * MP * Tile<MP>::SA) * sizeof(T)
+                              : (size_t)(MP * D + MP * OW + MP * Tile<MP>::SA) * sizeof(T) + MP * sizeof(float);
+  const size_t smem = per_warp * kWarps;
+  auto kern = bwd ? lstep_bwd_mma_kernel<T, MP, D, LAST> : lstep_fwd_mma_kernel<T, MP, D, LAST>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = (p.bh * p.b + kWarps - 1) / kWarps;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T, int D>
+cudaError_t dispatch_m(const LstepParams& p, bool last, bool bwd, cudaStream_t st) {
+  if (p.m <= 16) return last ? launch<T, 16, D, true>(p, bwd, st) : launch<T, 16, D, false>(p, bwd, st);
+  return last ? launch<T, 32, D, true>(p, bwd, st) : launch<T, 32, D, false>(p, bwd, st);
+}
+
+}  // namespace
+
+bool lstep_mma_supported(const LstepParams& p, bool last) {
+  return p.m <= 32 && (p.d == 64 || p.d == 128) && p.dw == (last ? 2 * p.d : p.d);
+}
+
+cudaError_t lstep_mma_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st) {
+  if (bf16) {
+    return p.d == 64 ? dispatch_m<__nv_bfloat16, 64>(p, last, bwd, st) : dispatch_m<__nv_bfloat16, 128>(p, last, bwd, st);
+  }
+  return p.d == 64 ? dispatch_m<__half, 64>(p, last, bwd, st) : dispatch_m<__half, 128>(p, last, bwd, st);
+}
+
+}  // namespace vmb
