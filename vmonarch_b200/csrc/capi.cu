@@ -77,10 +77,11 @@ uint64_t vmb_kernel_launches(void) { return g_launches.load(std::memory_order_re
 
 int vmb_device_status(void* stream, int32_t* out) {
   if (!out) return fail(VMB_EINVAL, "vmb_device_status: null output");
-  int v = 0;
-  const cudaError_t e = vmb::fea_fwd_sm100_status(static_cast<cudaStream_t>(stream), &v);
+  int v = 0, w = 0;
+  cudaError_t e = vmb::fea_fwd_sm100_status(static_cast<cudaStream_t>(stream), &v);
+  if (e == cudaSuccess) e = vmb::fea_bwd_sm100_status(static_cast<cudaStream_t>(stream), &w);
   if (e != cudaSuccess) return cuda_status(e, "vmb_device_status");
-  *out = v;
+  *out = v | (w << 8);
   return VMB_OK;
 }
 
@@ -150,7 +151,9 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   float* gg = reinterpret_cast<float*>(ws + round_up(rows * 4, 256));
   float* dq_acc = a->grad_mode == 0 ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
 
-  count(dq_acc ? 3 : 2);
+  const bool sm100 = vmb::fea_bwd_sm100_supported(a->d, a->dv, a->dv1, a->v_is_k != 0);
+  if (sm100) dq_acc = nullptr;  // the tcgen05 dQ kernel writes grad_q directly in either mode
+  count(sm100 ? 3 : (dq_acc ? 3 : 2));
   cudaError_t e = vmb::fea_bwd_pre(a->o, a->o_bs, a->dout, a->do_bs, a->lse, a->ent, a->dent, cc, gg, a->batch,
                                    (int)a->n_q, a->dv, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(pre)");
@@ -167,8 +170,10 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.dk_bs = a->grad_k_bs; p.dv_bs = a->grad_v_bs; p.dv2_bs = a->grad_v2_bs;
   p.n_q = (int)a->n_q; p.n_kv = (int)a->n_kv; p.dv1 = a->dv1;
   p.acc_kv = a->grad_mode;
+  p.acc_q = a->grad_mode;
   p.sm_scale = a->sm_scale;
   p.scale_log2 = a->sm_scale * kLog2eHost;
+  if (sm100) return cuda_status(vmb::fea_bwd_sm100(p, a->batch, a->dv, a->v_is_k != 0, bf16, st), "vmb_fea_bwd");
   e = vmb::fea_bwd_mma(p, a->batch, a->d, a->dv, a->v_is_k != 0, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd");
   if (dq_acc) {

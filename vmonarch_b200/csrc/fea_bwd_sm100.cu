@@ -1,0 +1,626 @@
+// FlashEntropyAttention backward on tcgen05 / TMEM / TMA, D = 128 (reference semantics:
+// video_monarch_attention/kernel.py:154-313, including the entropy-gradient term folded into the
+// per-row constants c_i, g_i computed by fea_bwd_pre: dS = P (dP - c_i - g_i x_ij)).
+//
+// TMEM holds 512 fp32 columns per SM, too few for S^T, dP^T, dK, dV and dQ of one tile at once, so
+// the backward is two kernels (7 MMAs per 128x64 tile pair instead of 5, but no atomics and a
+// deterministic result):
+//
+// dkdv kernel: CTA = 128 keys of one sequence, walks the query tiles (64 rows):
+//   S^T = K Q^T, dP^T = W dO^T                  (SS MMAs, M = 128 keys, N = 64 queries)
+//   thread = key row: P^T = 2^(x - LSE2_q), dS^T = P^T (dP^T - c_q - g_q x) sm_scale
+//     -> bf16 back into TMEM (double-buffered)
+//   dK += dS^T Q;  dV += P^T dO                  (TS MMAs, A = P^T / dS^T from TMEM)
+//   With V aliasing K (the VMonarch R step, W = [K | V2]) the value gradient of the K columns is
+//   added into dK by one more TS MMA (dK += P^T dO[:, :128]) and dV holds the V2 columns.
+//   TMEM: S^T [0,64) dP^T [64,128) P^T 2x32 [128,192) dS^T 2x32 [192,256) dK [256,384) dV [384,512)
+// dq kernel: CTA = 128 queries, walks the key tiles (64 rows):
+//   S = Q K^T, dP = dO W^T (SS, double-buffered in TMEM), dS (thread = query row) -> TMEM,
+//   dQ += dS K (TS). TMEM: S 2x64 [0,128) dP 2x64 [128,256) dS 2x32 [256,320) dQ [384,512)
+// Both write their gradients directly (bf16, or added into fp32 accumulators in grad_mode 1).
+// Tails: rows past n_q / n_kv load as zeros (TMA), query statistics past n_q are (+inf, 0, 0) so
+// their P is 0; gradients are only stored for valid rows. Every wait is bounded (sm100.cuh).
+#include "common.cuh"
+#include "fea_params.h"
+#include "launch.h"
+#include "sm100.cuh"
+#include "tma_host.h"
+
+namespace vmb {
+
+__device__ int g_bwd_err;
+
+namespace {
+
+using namespace sm100;
+
+constexpr int kThreads = 192;
+constexpr int kAtom128 = 128 * 128;  // swizzle-atom column block of 128 rows x 128 B
+constexpr int kAtom64 = 64 * 128;    // ... of 64 rows x 128 B
+
+struct Sm100BwdParams {
+  CUtensorMap tm_a, tm_b, tm_c, tm_d;  // dkdv: K, X, Q, dO (box 128,128,64,64); dq: Q, dO, K, X (128,128,64,64)
+  const float* lse;
+  const float* cc;
+  const float* gg;
+  void* grad0;   // dkdv: grad_k ; dq: grad_q
+  void* grad1;   // dkdv: grad_v (or grad_v2 when v aliases k)
+  int64_t g0_bs, g1_bs;
+  int g1_cols;   // row width of grad1
+  int n_q, n_kv, n_tiles;
+  int acc;       // 1: fp32 accumulate
+  float scale_log2, sm_scale;
+};
+
+// Writes one 128-column fp32 TMEM row (this thread's lane) to a gradient row. The TMEM loads are
+// warp-collective and run on every lane; only lanes with `valid` rows store.
+template <typename T>
+__device__ __forceinline__ void store_row128(uint32_t taddr, void* base, int64_t off, bool acc, bool valid) {
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    uint32_t v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+    if (!valid) continue;
+    if (acc) {
+      float* dst = static_cast<float*>(base) + off + c * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i += 4) {
+        float4 o = *reinterpret_cast<float4*>(dst + i);
+        o.x += __uint_as_float(v[i]);
+        o.y += __uint_as_float(v[i + 1]);
+        o.z += __uint_as_float(v[i + 2]);
+        o.w += __uint_as_float(v[i + 3]);
+        *reinterpret_cast<float4*>(dst + i) = o;
+      }
+    } else {
+      T* dst = static_cast<T*>(base) + off + c * 32;
+#pragma unroll
+      for (int i = 0; i < 32; i += 8) {
+        uint4 w;
+        w.x = Elem<T>::pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
+        w.y = Elem<T>::pack(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
+        w.z = Elem<T>::pack(__uint_as_float(v[i + 4]), __uint_as_float(v[i + 5]));
+        w.w = Elem<T>::pack(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7]));
+        *reinterpret_cast<uint4*>(dst + i) = w;
+      }
+    }
+  }
+}
+
+// ================================================================================ dK / dV kernel
+// XA: resident value atoms (V when !VK, V2 when VK); DW = width of W (and of dO).
+template <int XA, bool VK, int NQS>
+struct DkdvCfg {
+  static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
+  static constexpr int RES = (2 + XA) * kAtom128;                 // resident K | X
+  static constexpr int SLOT_T = (2 + DW / 64) * kAtom64;          // Q | dO tiles of one query tile
+  static constexpr int SLOT = SLOT_T + 1024;                      // + statistics (3 x 64 floats)
+  static constexpr int SMEM = 1024 + RES + NQS * SLOT;
+  static constexpr bool HAS_DV = XA > 0;
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <typename T, int XA, bool VK, int NQS>
+__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_constant__ Sm100BwdParams p) {
+  using C = DkdvCfg<XA, VK, NQS>;
+  constexpr bool kBf16 = Elem<T>::is_bf16;
+  constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);   // S^T, dP^T
+  constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);  // dK, dV (B MN-major)
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 7];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bi = blockIdx.x / p.n_tiles;
+  const int k0 = (blockIdx.x % p.n_tiles) * 128;
+  const int nq = (p.n_q + 63) / 64;
+
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sRes = sbase;                       // K atoms, then X atoms
+  const uint32_t sW = VK ? sRes : sRes + 2 * kAtom128;
+  const uint32_t sSlots = sbase + C::RES;
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t BAR_KV = bar0;
+  auto BAR_QFULL = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto BAR_QEMPTY = [&](int s) { return bar0 + 8u * (1 + NQS + s); };
+  const uint32_t BAR_SPFULL = bar0 + 8u * (1 + 2 * NQS);
+  const uint32_t BAR_SPFREE = bar0 + 8u * (2 + 2 * NQS);
+  auto BAR_PDSFULL = [&](int b) { return bar0 + 8u * (3 + 2 * NQS + b); };
+  auto BAR_PDSFREE = [&](int b) { return bar0 + 8u * (5 + 2 * NQS + b); };
+  const uint32_t BAR_DONE = bar0 + 8u * (7 + 2 * NQS);
+  volatile int* abort = &abort_sh;
+  auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
+  auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom64; };
+  auto slot_stats = [&](int s) {
+    return reinterpret_cast<float*>(smem_raw + (sSlots - smem_u32(smem_raw)) + s * C::SLOT + C::SLOT_T);
+  };
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    mbar_init(BAR_KV, 1);
+    for (int s = 0; s < NQS; ++s) {
+      mbar_init(BAR_QFULL(s), 1 + 32);
+      mbar_init(BAR_QEMPTY(s), 1);
+    }
+    mbar_init(BAR_SPFULL, 1);
+    mbar_init(BAR_SPFREE, 128);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR_PDSFULL(b), 128);
+      mbar_init(BAR_PDSFREE(b), 1);
+    }
+    mbar_init(BAR_DONE, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_base_sh), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    int armed[NQS];
+    for (int s = 0; s < NQS; ++s) armed[s] = 0;
+    if (lane == 0) {
+      prefetch_tmap(&p.tm_a);
+      prefetch_tmap(&p.tm_c);
+      prefetch_tmap(&p.tm_d);
+      mbar_expect_tx(BAR_KV, C::RES);
+      tma_load_3d(sRes, &p.tm_a, 0, k0, bi, BAR_KV);
+      tma_load_3d(sRes + kAtom128, &p.tm_a, 64, k0, bi, BAR_KV);
+      for (int a = 0; a < XA; ++a) tma_load_3d(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bi, BAR_KV);
+    }
+    const float* lse = p.lse + (int64_t)bi * p.n_q;
+    const float* cc = p.cc + (int64_t)bi * p.n_q;
+    const float* gg = p.gg + (int64_t)bi * p.n_q;
+    for (int i = 0; i < nq; ++i) {
+      const int s = i % NQS;
+      bool ok = true;
+      if (lane == 0 && i >= NQS) ok = mbar_wait(BAR_QEMPTY(s), ((i / NQS) - 1) & 1, abort, &g_bwd_err, 1);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      if (lane == 0) {
+        mbar_expect_tx(BAR_QFULL(s), C::SLOT_T);
+        tma_load_3d(slot_q(s), &p.tm_c, 0, i * 64, bi, BAR_QFULL(s));
+        tma_load_3d(slot_q(s) + kAtom64, &p.tm_c, 64, i * 64, bi, BAR_QFULL(s));
+        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(slot_do(s) + a * kAtom64, &p.tm_d, 64 * a, i * 64, bi, BAR_QFULL(s));
+      }
+      float* st = slot_stats(s);
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int q = i * 64 + lane + 32 * h;
+        const bool okq = q < p.n_q;
+        st[lane + 32 * h] = okq ? lse[q] : __int_as_float(0x7f800000);
+        st[64 + lane + 32 * h] = okq ? cc[q] : 0.f;
+        st[128 + lane + 32 * h] = okq ? gg[q] : 0.f;
+      }
+      mbar_arrive(BAR_QFULL(s));
+      armed[s] = i / NQS + 1;
+    }
+    if (lane == 0) {
+      mbar_wait_drain(BAR_KV, 0);
+      for (int s = 0; s < NQS; ++s)
+        if (armed[s] > 0) mbar_wait_drain(BAR_QFULL(s), (armed[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(BAR_KV, 0, abort, &g_bwd_err, 2);
+      auto issue_sp = [&](int i) -> bool {
+        const int s = i % NQS;
+        if (!mbar_wait(BAR_QFULL(s), (i / NQS) & 1, abort, &g_bwd_err, 2)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
+          const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
+          mma_ss(tmem + 0, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024),
+                 IDESC_SP, kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
+          const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
+          mma_ss(tmem + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
+                 IDESC_SP, kk > 0);
+        }
+        mma_commit(BAR_SPFULL);
+        return true;
+      };
+      if (ok) ok = issue_sp(0);
+      for (int i = 0; ok && i < nq; ++i) {
+        if (i + 1 < nq) {
+          if (!mbar_wait(BAR_SPFREE, i & 1, abort, &g_bwd_err, 4)) break;
+          if (!issue_sp(i + 1)) break;
+        }
+        if (!mbar_wait(BAR_PDSFULL(i & 1), (i >> 1) & 1, abort, &g_bwd_err, 4)) break;
+        tc_fence_after();
+        const int s = i % NQS;
+        const uint32_t pt = tmem + 128 + 32 * (i & 1), dst = tmem + 192 + 32 * (i & 1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // dK += dS^T Q   (K = 64 queries)
+          mma_ts(tmem + 256, dst + kk * 8, smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
+                 (i > 0 || kk > 0) ? 1u : 0u);
+        if (VK) {
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // dK += P^T dO[:, :128]  (value gradient of the K columns)
+            mma_ts(tmem + 256, pt + kk * 8, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
+        }
+        if (C::HAS_DV) {
+          const uint32_t vo = VK ? 2 * kAtom64 : 0;
+#pragma unroll
+          for (int kk = 0; kk < 4; ++kk)  // dV += P^T dO[:, cols]
+            mma_ts(tmem + 384, pt + kk * 8, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
+                   (i > 0 || kk > 0) ? 1u : 0u);
+        }
+        mma_commit(BAR_PDSFREE(i & 1));
+        mma_commit(BAR_QEMPTY(s));
+      }
+      mma_commit(BAR_DONE);
+      mbar_wait_drain(BAR_DONE, 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- compute: thread = key row
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+      const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
+      return __all_sync(0xffffffffu, mine);
+    };
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int s = i % NQS;
+      if (!warp_wait(BAR_SPFULL, i & 1, 8)) { ok = false; break; }
+      if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
+      if (i >= 2 && !warp_wait(BAR_PDSFREE(i & 1), ((i - 2) >> 1) & 1, 8)) { ok = false; break; }
+      tc_fence_after();
+      const float* st = slot_stats(s);
+      const uint32_t pt = tmem + lane_off + 128 + 32 * (i & 1), dst = tmem + lane_off + 192 + 32 * (i & 1);
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(tmem + lane_off + c * 32, sv);
+        tmem_ld32(tmem + lane_off + 64 + c * 32, dv);
+        tmem_wait_ld();
+        if (c == 1) {
+          tc_fence_before();
+          mbar_arrive(BAR_SPFREE);
+        }
+        uint32_t pk[16], dk[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float pr[2], dr[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const int q = c * 32 + e + u;
+            const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
+            const float pv = fast_exp2(x - st[q]);
+            pr[u] = pv;
+            dr[u] = pv * (__uint_as_float(dv[e + u]) - st[64 + q] - st[128 + q] * x) * p.sm_scale;
+          }
+          pk[e >> 1] = Elem<T>::pack(pr[0], pr[1]);
+          dk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        }
+        tmem_st16(pt + c * 16, pk);
+        tmem_st16(dst + c * 16, dk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(BAR_PDSFULL(i & 1));
+    }
+    if (ok) ok = warp_wait(BAR_DONE, 0, 8);
+    tc_fence_after();
+    const int key = k0 + row;
+    const bool kok = key < p.n_kv;
+    const int64_t krow = kok ? key : 0;
+    if (ok) {
+      store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok);
+      if (C::HAS_DV)
+        store_row128<T>(tmem + lane_off + 384, p.grad1, (int64_t)bi * p.g1_bs + krow * p.g1_cols, p.acc, kok);
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ================================================================================ dQ kernel
+template <int XA, bool VK, int NSLOT>
+struct DqCfg {
+  static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
+  static constexpr int RES = (2 + DW / 64) * kAtom128;  // resident Q | dO
+  static constexpr int SLOT = (2 + XA) * kAtom64;       // K | X of one 64-key tile
+  static constexpr int SMEM = 1024 + RES + NSLOT * SLOT;
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <typename T, int XA, bool VK, int NSLOT>
+__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq_kernel(const __grid_constant__ Sm100BwdParams p) {
+  using C = DqCfg<XA, VK, NSLOT>;
+  constexpr bool kBf16 = Elem<T>::is_bf16;
+  constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);
+  constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 128, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[1 + 3 * NSLOT + 5];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bi = blockIdx.x / p.n_tiles;
+  const int q0 = (blockIdx.x % p.n_tiles) * 128;
+  const int nk = (p.n_kv + 63) / 64;
+
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sQ = sbase, sDO = sbase + 2 * kAtom128;
+  const uint32_t sRing = sbase + C::RES;
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t BAR_Q = bar0;
+  auto BAR_KFULL = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto BAR_VFULL = [&](int s) { return bar0 + 8u * (1 + NSLOT + s); };
+  auto BAR_EMPTY = [&](int s) { return bar0 + 8u * (1 + 2 * NSLOT + s); };
+  auto BAR_SPFULL = [&](int b) { return bar0 + 8u * (1 + 3 * NSLOT + b); };
+  auto BAR_DSFULL = [&](int b) { return bar0 + 8u * (3 + 3 * NSLOT + b); };
+  const uint32_t BAR_DONE = bar0 + 8u * (5 + 3 * NSLOT);
+  volatile int* abort = &abort_sh;
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    mbar_init(BAR_Q, 1);
+    for (int s = 0; s < NSLOT; ++s) {
+      mbar_init(BAR_KFULL(s), 1);
+      mbar_init(BAR_VFULL(s), 1);
+      mbar_init(BAR_EMPTY(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR_SPFULL(b), 1);
+      mbar_init(BAR_DSFULL(b), 128);
+    }
+    mbar_init(BAR_DONE, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_base_sh), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&p.tm_a);
+      prefetch_tmap(&p.tm_b);
+      prefetch_tmap(&p.tm_c);
+      mbar_expect_tx(BAR_Q, C::RES);
+      tma_load_3d(sQ, &p.tm_a, 0, q0, bi, BAR_Q);
+      tma_load_3d(sQ + kAtom128, &p.tm_a, 64, q0, bi, BAR_Q);
+      for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(sDO + a * kAtom128, &p.tm_b, 64 * a, q0, bi, BAR_Q);
+      int armed[NSLOT];
+      for (int s = 0; s < NSLOT; ++s) armed[s] = 0;
+      for (int j = 0; j < nk; ++j) {
+        const int s = j % NSLOT;
+        if (j >= NSLOT && !mbar_wait(BAR_EMPTY(s), ((j / NSLOT) - 1) & 1, abort, &g_bwd_err, 16)) break;
+        const uint32_t slot = sRing + s * C::SLOT;
+        mbar_expect_tx(BAR_KFULL(s), 2 * kAtom64);
+        tma_load_3d(slot, &p.tm_c, 0, j * 64, bi, BAR_KFULL(s));
+        tma_load_3d(slot + kAtom64, &p.tm_c, 64, j * 64, bi, BAR_KFULL(s));
+        if (XA > 0) {
+          mbar_expect_tx(BAR_VFULL(s), XA * kAtom64);
+          for (int a = 0; a < XA; ++a) tma_load_3d(slot + (2 + a) * kAtom64, &p.tm_d, 64 * a, j * 64, bi, BAR_VFULL(s));
+        }
+        armed[s] = j / NSLOT + 1;
+      }
+      mbar_wait_drain(BAR_Q, 0);
+      for (int s = 0; s < NSLOT; ++s) {
+        if (armed[s] > 0) {
+          mbar_wait_drain(BAR_KFULL(s), (armed[s] - 1) & 1);
+          if (XA > 0) mbar_wait_drain(BAR_VFULL(s), (armed[s] - 1) & 1);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (lane == 0) {
+      bool ok = mbar_wait(BAR_Q, 0, abort, &g_bwd_err, 32);
+      auto issue_sp = [&](int j) -> bool {
+        const int s = j % NSLOT;
+        const uint32_t slot = sRing + s * C::SLOT;
+        if (!mbar_wait(BAR_KFULL(s), (j / NSLOT) & 1, abort, &g_bwd_err, 32)) return false;
+        if (XA > 0 && !mbar_wait(BAR_VFULL(s), (j / NSLOT) & 1, abort, &g_bwd_err, 32)) return false;
+        tc_fence_after();
+        const uint32_t ds = tmem + 64 * (j & 1), dp = tmem + 128 + 64 * (j & 1);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // S = Q K^T
+          const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
+          mma_ss(ds, smem_desc_sw128(sQ + offa, 16, 1024), smem_desc_sw128(slot + offb, 16, 1024), IDESC_SP, kk > 0);
+        }
+        const uint32_t w = VK ? slot : slot + 2 * kAtom64;
+#pragma unroll
+        for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP = dO W^T
+          const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
+          mma_ss(dp, smem_desc_sw128(sDO + offa, 16, 1024), smem_desc_sw128(w + offb, 16, 1024), IDESC_SP, kk > 0);
+        }
+        mma_commit(BAR_SPFULL(j & 1));
+        return true;
+      };
+      if (ok) ok = issue_sp(0);
+      if (ok && nk > 1) ok = issue_sp(1);
+      for (int j = 0; ok && j < nk; ++j) {
+        if (!mbar_wait(BAR_DSFULL(j & 1), (j >> 1) & 1, abort, &g_bwd_err, 64)) break;
+        tc_fence_after();
+        const int s = j % NSLOT;
+        const uint32_t slot = sRing + s * C::SLOT;
+        const uint32_t dsb = tmem + 256 + 32 * (j & 1);
+#pragma unroll
+        for (int kk = 0; kk < 4; ++kk)  // dQ += dS K  (K = 64 keys)
+          mma_ts(tmem + 384, dsb + kk * 8, smem_desc_sw128(slot + kk * 2048, kAtom64, 1024), IDESC_DQ,
+                 (j > 0 || kk > 0) ? 1u : 0u);
+        mma_commit(BAR_EMPTY(s));
+        if (j + 2 < nk) ok = issue_sp(j + 2);
+      }
+      mma_commit(BAR_DONE);
+      mbar_wait_drain(BAR_DONE, 0);
+    }
+  } else {
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const int q = q0 + row;
+    const bool qok = q < p.n_q;
+    const int64_t ridx = (int64_t)bi * p.n_q + q;
+    const float lse = qok ? p.lse[ridx] : __int_as_float(0x7f800000);
+    const float cc = qok ? p.cc[ridx] : 0.f;
+    const float gg = qok ? p.gg[ridx] : 0.f;
+    auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+      const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
+      return __all_sync(0xffffffffu, mine);
+    };
+    bool ok = true;
+    for (int j = 0; j < nk; ++j) {
+      if (!warp_wait(BAR_SPFULL(j & 1), (j >> 1) & 1, 128)) { ok = false; break; }
+      tc_fence_after();
+      const uint32_t ts = tmem + lane_off + 64 * (j & 1), tdp = tmem + lane_off + 128 + 64 * (j & 1);
+      const uint32_t tds = tmem + lane_off + 256 + 32 * (j & 1);
+#pragma unroll 1
+      for (int c = 0; c < 2; ++c) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(ts + c * 32, sv);
+        tmem_ld32(tdp + c * 32, dv);
+        tmem_wait_ld();
+        uint32_t dk32[16];
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          float dr[2];
+#pragma unroll
+          for (int u = 0; u < 2; ++u) {
+            const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
+            const float pv = fast_exp2(x - lse);
+            dr[u] = pv * (__uint_as_float(dv[e + u]) - cc - gg * x) * p.sm_scale;
+          }
+          dk32[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        }
+        tmem_st16(tds + c * 16, dk32);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(BAR_DSFULL(j & 1));
+    }
+    if (ok) ok = warp_wait(BAR_DONE, 0, 128);
+    tc_fence_after();
+    if (ok) store_row128<T>(tmem + lane_off + 384, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc, qok);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ================================================================================ host side
+template <typename Kern>
+cudaError_t run(Kern kern, int smem, int64_t blocks, const Sm100BwdParams& p, cudaStream_t st) {
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+  if (e != cudaSuccess) return e;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  kern<<<(unsigned)blocks, kThreads, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
+template <typename T>
+cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaStream_t st) {
+  const bool bf16 = Elem<T>::is_bf16;
+  const int xa = vk ? (dv - 128) / 64 : dv / 64;  // value atoms beyond K (vk) or V atoms
+  // ---- dK / dV
+  Sm100BwdParams pa{};
+  if (!tma::make_map(&pa.tm_a, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 128)) return cudaErrorInvalidValue;
+  if (xa > 0) {
+    const void* xsrc = vk ? b.v2 : b.v;
+    const int64_t xbs = vk ? b.v2_bs : b.v_bs;
+    if (!tma::make_map(&pa.tm_b, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 128)) return cudaErrorInvalidValue;
+  } else {
+    pa.tm_b = pa.tm_a;
+  }
+  if (!tma::make_map(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.q_bs, 64)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.do_bs, 64)) return cudaErrorInvalidValue;
+  pa.lse = b.lse;
+  pa.cc = b.cc;
+  pa.gg = b.gg;
+  pa.grad0 = b.dk;
+  pa.g0_bs = b.dk_bs;
+  pa.grad1 = vk ? b.dv2 : b.dv;
+  pa.g1_bs = vk ? b.dv2_bs : b.dv_bs;
+  pa.g1_cols = 128;
+  pa.n_q = b.n_q;
+  pa.n_kv = b.n_kv;
+  pa.n_tiles = (b.n_kv + 127) / 128;
+  pa.acc = b.acc_kv;
+  pa.scale_log2 = b.scale_log2;
+  pa.sm_scale = b.sm_scale;
+  cudaError_t e;
+  const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
+  if (vk && xa == 0) {
+    e = run(fea_bwd_dkdv_kernel<T, 0, true, 4>, DkdvCfg<0, true, 4>::SMEM, blocks_a, pa, st);
+  } else if (vk) {
+    e = run(fea_bwd_dkdv_kernel<T, 2, true, 3>, DkdvCfg<2, true, 3>::SMEM, blocks_a, pa, st);
+  } else {
+    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4>, DkdvCfg<2, false, 4>::SMEM, blocks_a, pa, st);
+  }
+  if (e != cudaSuccess) return e;
+  // ---- dQ
+  Sm100BwdParams pb{};
+  if (!tma::make_map(&pb.tm_a, b.q, bf16, 128, b.n_q, batch, b.q_bs, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&pb.tm_b, b.dout, bf16, dv, b.n_q, batch, b.do_bs, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&pb.tm_c, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 64)) return cudaErrorInvalidValue;
+  if (xa > 0) {
+    const void* xsrc = vk ? b.v2 : b.v;
+    const int64_t xbs = vk ? b.v2_bs : b.v_bs;
+    if (!tma::make_map(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 64)) return cudaErrorInvalidValue;
+  } else {
+    pb.tm_d = pb.tm_c;
+  }
+  pb.lse = b.lse;
+  pb.cc = b.cc;
+  pb.gg = b.gg;
+  pb.grad0 = b.dq;
+  pb.g0_bs = b.dq_bs;
+  pb.n_q = b.n_q;
+  pb.n_kv = b.n_kv;
+  pb.n_tiles = (b.n_q + 127) / 128;
+  pb.acc = b.acc_q;
+  pb.scale_log2 = b.scale_log2;
+  pb.sm_scale = b.sm_scale;
+  const int64_t blocks_b = (int64_t)pb.n_tiles * batch;
+  if (vk && xa == 0) return run(fea_bwd_dq_kernel<T, 0, true, 6>, DqCfg<0, true, 6>::SMEM, blocks_b, pb, st);
+  if (vk) return run(fea_bwd_dq_kernel<T, 2, true, 3>, DqCfg<2, true, 3>::SMEM, blocks_b, pb, st);
+  return run(fea_bwd_dq_kernel<T, 2, false, 4>, DqCfg<2, false, 4>::SMEM, blocks_b, pb, st);
+}
+
+}  // namespace
+
+bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {
+  if (d != 128) return false;
+  if (vk) return dv1 == 128 && (dv == 128 || dv == 256);
+  return dv == 128 && dv1 == 128;
+}
+
+cudaError_t fea_bwd_sm100(const BwdParams& p, int64_t batch, int dv, bool vk, bool bf16, cudaStream_t st) {
+  return bf16 ? launch_all<__nv_bfloat16>(p, batch, dv, vk, st) : launch_all<__half>(p, batch, dv, vk, st);
+}
+
+cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out) {
+  int zero = 0;
+  cudaError_t e = cudaMemcpyFromSymbolAsync(out, g_bwd_err, sizeof(int), 0, cudaMemcpyDeviceToHost, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  if (e == cudaSuccess && *out) e = cudaMemcpyToSymbolAsync(g_bwd_err, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, st);
+  if (e == cudaSuccess) e = cudaStreamSynchronize(st);
+  return e;
+}
+
+}  // namespace vmb

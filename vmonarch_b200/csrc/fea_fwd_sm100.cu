@@ -24,12 +24,11 @@
 // Every mbarrier wait is bounded (sm100.cuh); a CTA that gives up records an error code in
 // g_fwd_err (read by vmb_device_status) and drains its in-flight copies and MMAs before freeing
 // TMEM, so a fault in the pipeline ends the kernel instead of hanging the GPU.
-#include <mutex>
-
 #include "common.cuh"
 #include "fea_params.h"
 #include "launch.h"
 #include "sm100.cuh"
+#include "tma_host.h"
 
 namespace vmb {
 
@@ -327,36 +326,6 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 }
 
 // ---------------------------------------------------------------------------------- host side
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
-
-EncodeTiledFn encode_fn() {
-  static EncodeTiledFn fn = nullptr;
-  static std::once_flag once;
-  std::call_once(once, [] {
-    void* ptr = nullptr;
-    cudaDriverEntryPointQueryResult q;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q) == cudaSuccess &&
-        q == cudaDriverEntryPointSuccess)
-      fn = reinterpret_cast<EncodeTiledFn>(ptr);
-  });
-  return fn;
-}
-
-// 3-D map over [batch][rows][cols] 16-bit elements, rows contiguous, 64 x 128 boxes, 128 B swizzle.
-bool make_map(CUtensorMap* m, const void* base, bool bf16, int64_t cols, int64_t rows, int64_t batch, int64_t bs) {
-  EncodeTiledFn enc = encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[3] = {(cuuint64_t)cols, (cuuint64_t)rows, (cuuint64_t)batch};
-  cuuint64_t strides[2] = {(cuuint64_t)cols * 2, (cuuint64_t)bs * 2};
-  cuuint32_t box[3] = {64, 128, 1};
-  cuuint32_t estr[3] = {1, 1, 1};
-  return enc(m, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 3, const_cast<void*>(base),
-             dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-             CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
-}
-
 template <typename T, int XA, bool VK, int NSLOT, bool ENT>
 cudaError_t launch(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   using C = FwdCfg<XA, VK, NSLOT>;
@@ -393,15 +362,15 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
                           cudaStream_t st) {
   Sm100FwdParams p;
   const int dv1 = fp.dv1;
-  if (!make_map(&p.tm_q, fp.q, bf16, d, fp.n_q, batch, fp.q_bs)) return cudaErrorInvalidValue;
-  if (!make_map(&p.tm_k, fp.k, bf16, d, fp.n_kv, batch, fp.k_bs)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&p.tm_q, fp.q, bf16, d, fp.n_q, batch, fp.q_bs, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&p.tm_k, fp.k, bf16, d, fp.n_kv, batch, fp.k_bs, 128)) return cudaErrorInvalidValue;
   if (vk) {
-    if (dv > dv1 && !make_map(&p.tm_x, fp.v2, bf16, dv - dv1, fp.n_kv, batch, fp.v2_bs)) return cudaErrorInvalidValue;
+    if (dv > dv1 && !tma::make_map(&p.tm_x, fp.v2, bf16, dv - dv1, fp.n_kv, batch, fp.v2_bs, 128)) return cudaErrorInvalidValue;
     if (dv == dv1) p.tm_x = p.tm_k;
   } else {
-    if (!make_map(&p.tm_x, fp.v, bf16, dv, fp.n_kv, batch, fp.v_bs)) return cudaErrorInvalidValue;
+    if (!tma::make_map(&p.tm_x, fp.v, bf16, dv, fp.n_kv, batch, fp.v_bs, 128)) return cudaErrorInvalidValue;
   }
-  if (!make_map(&p.tm_o, fp.o, bf16, dv, fp.n_q, batch, fp.o_bs)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&p.tm_o, fp.o, bf16, dv, fp.n_q, batch, fp.o_bs, 128)) return cudaErrorInvalidValue;
   p.lse = fp.lse;
   p.ent = fp.ent;
   p.n_q = fp.n_q;

@@ -34,6 +34,7 @@ struct BwdParams {
   int64_t q_bs, k_bs, v_bs, v2_bs, do_bs, dq_bs, dk_bs, dv_bs, dv2_bs;
   int n_q, n_kv, dv1, n_ktiles;
   int acc_kv;         // 1: dk/dv/dv2 are fp32 buffers that are added into
+  int acc_q;          // 1: dq is an fp32 buffer that is added into (else element dtype)
   float scale_log2;   // sm_scale * log2(e)
   float sm_scale;
 };

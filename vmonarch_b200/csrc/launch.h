@@ -27,6 +27,9 @@ bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk);
 cudaError_t fea_fwd_sm100(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, bool vk,
                           cudaStream_t st);
 cudaError_t fea_fwd_sm100_status(cudaStream_t st, int* out);
+bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk);
+cudaError_t fea_bwd_sm100(const BwdParams& p, int64_t batch, int dv, bool vk, bool bf16, cudaStream_t st);
+cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out);
 cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,

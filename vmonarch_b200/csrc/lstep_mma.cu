@@ -27,8 +27,6 @@ constexpr int kWarps = 4;
 
 template <int MP>
 struct Tile {
-  static constexpr int MT = MP / 16;  // 16-row MMA tiles over i (or k)
-  static constexpr int NT = MP / 8;   // 8-col MMA tiles over k
   static constexpr int SA = MP + 8;   // row stride (elements) of the m x m staging tile
 };
 
