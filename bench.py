@@ -181,6 +181,13 @@ def kernel_flops(name: str, a) -> tuple[float, float]:
     return f, by
 
 
+def call_key(name: str, a) -> str:
+    """Entry point + shape: calls with the same key run the same kernels on the same sizes."""
+    if name.startswith("vmb_fea"):
+        return f"{name}[batch={a.batch},n_q={a.n_q},n_kv={a.n_kv},d={a.d},dv={a.dv}]"
+    return f"{name}[bh={a.bh},m={a.m},b={a.b},d={a.d},dw={a.dw}]"
+
+
 def profile_step(step, args_dev, device) -> dict:
     """One step with every C-ABI call bracketed by CUDA events on the current stream."""
     from vmonarch_b200 import ops
@@ -192,7 +199,7 @@ def profile_step(step, args_dev, device) -> dict:
         s.record()
         yield
         e.record()
-        recs.append((name, kernel_flops(name, a), s, e))
+        recs.append((call_key(name, a), kernel_flops(name, a), s, e))
 
     ops.set_timer(timer)
     try:
@@ -201,8 +208,8 @@ def profile_step(step, args_dev, device) -> dict:
         ops.set_timer(None)
     torch.cuda.synchronize(device)
     per = {}
-    for name, (f, by), s, e in recs:
-        d = per.setdefault(name, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+    for key, (f, by), s, e in recs:
+        d = per.setdefault(key, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
         d["launches"] += 1
         d["ms"] += s.elapsed_time(e)
         d["flops"] += f
@@ -218,6 +225,7 @@ def load_peaks() -> tuple[dict, str]:
 
 
 def roofline(per: dict) -> dict:
+    """The dominant call group (entry point + shape) of one step, against the measured peak."""
     peaks, src = load_peaks()
     name, d = max(per.items(), key=lambda kv: kv[1]["ms"])
     total = sum(x["ms"] for x in per.values())
@@ -230,14 +238,17 @@ def roofline(per: dict) -> dict:
         peak, unit, bound = peaks["hbm_gbs"], "GB/s", "hbm"
         per_launch = d["bytes"] / d["launches"]
     traffic = None
-    tp = ROOT / "profiles" / "traffic.json"
+    tp = ROOT / "profiles" / "traffic.txt"   # "<call key> <DRAM bytes per launch>" from an ncu capture
     if tp.exists():
-        traffic = json.loads(tp.read_text()).get(name)
+        for line in tp.read_text().splitlines():
+            parts = line.split()
+            if len(parts) == 2 and parts[0] == name:
+                traffic = float(parts[1])
     return {"kernel": name, "bound": bound, "achieved": round(achieved, 2), "peak": peak, "unit": unit,
             "frac": round(achieved / peak, 4), "peak_source": f"{src} (sustained bf16)" if bound == "tensor" else src,
             "per_launch_algorithmic": per_launch, "avg_launch_ms": round(d["ms"] / d["launches"], 4),
             "share_of_step": round(d["ms"] / total, 4), "traffic": traffic,
-            "kernels": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per.items()}}
+            "calls": {k: {"launches": v["launches"], "ms": round(v["ms"], 3)} for k, v in per.items()}}
 
 
 # ----------------------------------------------------------------------------------------- CPU
@@ -359,7 +370,9 @@ def run_reference(args, info):
 
 
 def run_triton(args, info, device):
-    """The reference's Triton path from baseline/_ref on the same GPU (comparison only)."""
+    """The reference's own Triton path from baseline/_ref on the same GPU (comparison only).
+    If its backward cannot launch on this GPU (the dit14b last R step needs more shared memory
+    than a B200 has), the forward alone is timed and the line says so."""
     ref_dir = ROOT / "baseline" / "_ref"
     sys.path.insert(0, str(ref_dir))
     try:
@@ -371,16 +384,37 @@ def run_triton(args, info, device):
     q, k, v, do, de = make_inputs(w, seed=args.seed + seed_off, heads=heads)
     dev = [t.to(device) for t in (q, k, v, do, de)]
     dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(dev)]
-    step = make_step(w, ref)
+    full = make_step(w, ref)
+    mode, note = "forward+backward", None
+    try:
+        full(*dev)
+        torch.cuda.synchronize(device)
+        step = full
+    except Exception as exc:  # the reference's Triton backward may not fit this GPU
+        note = f"reference backward failed on this GPU: {type(exc).__name__}: {str(exc).splitlines()[0][:160]}"
+        mode = "forward only"
+        if w.kind == "vmonarch":
+            def step(q, k, v, do, de):
+                with torch.no_grad():
+                    return ref.vmonarch_attention(q, k, v, w.m, w.b, w.iters, recompute_tokens=w.recompute)
+        else:
+            def step(q, k, v, do, de):
+                with torch.no_grad():
+                    return ref.flash_entropy_attention(q, k, v)
     with ClockSampler(device) as clk:
         ms = time_steps(step, dev, args.steps, args.warmup, device)
     ms_max = shard.max_over_ranks(ms, device)
-    flops_job = scaled_flops(w, len(heads)) * (info.world if args.scaling == "weak" else 1)
+    f = w.flops()
+    per_head = (f["fwd"] + (f["bwd"] if mode == "forward+backward" else 0.0)) / w.H
+    flops_job = per_head * len(heads) * (info.world if args.scaling == "weak" else 1)
     if args.scaling == "strong":
-        flops_job = scaled_flops(w, w.H)
+        flops_job = per_head * w.H
     if info.rank != 0:
         return None
     line = base_line(args, w, info.world, ms_max, flops_job / (ms_max * 1e-3) / 1e12, impl="reference-triton")
+    line["mode"] = mode
+    if note:
+        line["note"] = note
     line["clocks"] = clk.summary()
     return line
 

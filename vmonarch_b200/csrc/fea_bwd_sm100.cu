@@ -34,7 +34,8 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;    // producer warp, MMA warp, two compute warpgroups on alternate tiles
+constexpr int kThreadsDq = 320;
 constexpr int kAtom128 = 128 * 128;  // swizzle-atom column block of 128 rows x 128 B
 constexpr int kAtom64 = 64 * 128;    // ... of 64 rows x 128 B
 
@@ -55,9 +56,10 @@ struct Sm100BwdParams {
 // Writes one 128-column fp32 TMEM row (this thread's lane) to a gradient row. The TMEM loads are
 // warp-collective and run on every lane; only lanes with `valid` rows store.
 template <typename T>
-__device__ __forceinline__ void store_row128(uint32_t taddr, void* base, int64_t off, bool acc, bool valid) {
+__device__ __forceinline__ void store_row128(uint32_t taddr, void* base, int64_t off, bool acc, bool valid,
+                                             int c_begin = 0, int c_end = 4) {
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
+  for (int c = c_begin; c < c_end; ++c) {
     uint32_t v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
@@ -95,7 +97,7 @@ struct DkdvCfg {
   static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
   static constexpr int RES = (2 + XA) * kAtom128;                 // resident K | X
   static constexpr int SLOT_T = (2 + DW / 64) * kAtom64;          // Q | dO tiles of one query tile
-  static constexpr int SLOT = SLOT_T + 1024;                      // + statistics (3 x 64 floats)
+  static constexpr int SLOT = SLOT_T + 1024;                      // + statistics: LSE2, c, g x 64
   static constexpr int SMEM = 1024 + RES + NQS * SLOT;
   static constexpr bool HAS_DV = XA > 0;
   static_assert(SMEM <= 232448, "shared memory budget");
@@ -109,7 +111,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
   constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);  // dK, dV (B MN-major)
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 7];
+  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -126,17 +128,13 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
   const uint32_t BAR_KV = bar0;
   auto BAR_QFULL = [&](int s) { return bar0 + 8u * (1 + s); };
   auto BAR_QEMPTY = [&](int s) { return bar0 + 8u * (1 + NQS + s); };
-  const uint32_t BAR_SPFULL = bar0 + 8u * (1 + 2 * NQS);
-  const uint32_t BAR_SPFREE = bar0 + 8u * (2 + 2 * NQS);
+  auto BAR_SPFULL = [&](int b) { return bar0 + 8u * (1 + 2 * NQS + b); };
   auto BAR_PDSFULL = [&](int b) { return bar0 + 8u * (3 + 2 * NQS + b); };
-  auto BAR_PDSFREE = [&](int b) { return bar0 + 8u * (5 + 2 * NQS + b); };
-  const uint32_t BAR_DONE = bar0 + 8u * (7 + 2 * NQS);
+  const uint32_t BAR_DONE = bar0 + 8u * (5 + 2 * NQS);
   volatile int* abort = &abort_sh;
   auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
   auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom64; };
-  auto slot_stats = [&](int s) {
-    return reinterpret_cast<float*>(smem_raw + (sSlots - smem_u32(smem_raw)) + s * C::SLOT + C::SLOT_T);
-  };
+  auto slot_stats = [&](int s) { return sSlots + s * C::SLOT + C::SLOT_T; };  // shared address
 
   if (threadIdx.x == 0) {
     abort_sh = 0;
@@ -145,11 +143,9 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
       mbar_init(BAR_QFULL(s), 1 + 32);
       mbar_init(BAR_QEMPTY(s), 1);
     }
-    mbar_init(BAR_SPFULL, 1);
-    mbar_init(BAR_SPFREE, 128);
     for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR_SPFULL(b), 1);
       mbar_init(BAR_PDSFULL(b), 128);
-      mbar_init(BAR_PDSFREE(b), 1);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -190,7 +186,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
         tma_load_3d(slot_q(s) + kAtom64, &p.tm_c, 64, i * 64, bi, BAR_QFULL(s));
         for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(slot_do(s) + a * kAtom64, &p.tm_d, 64 * a, i * 64, bi, BAR_QFULL(s));
       }
-      float* st = slot_stats(s);
+      float* st = reinterpret_cast<float*>(smem_raw + (slot_stats(s) - smem_u32(smem_raw)));
 #pragma unroll
       for (int h = 0; h < 2; ++h) {
         const int q = i * 64 + lane + 32 * h;
@@ -209,37 +205,37 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     }
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
+    // TMEM buffer b = query tile parity: S^T [128b, 128b+64), dP^T [128b+64, 128b+128); P^T and
+    // dS^T (bf16) are written over the first 32 columns of S^T / dP^T. dK [256,384), dV [384,512).
     if (lane == 0) {
       bool ok = mbar_wait(BAR_KV, 0, abort, &g_bwd_err, 2);
       auto issue_sp = [&](int i) -> bool {
         const int s = i % NQS;
         if (!mbar_wait(BAR_QFULL(s), (i / NQS) & 1, abort, &g_bwd_err, 2)) return false;
         tc_fence_after();
+        const uint32_t tb = tmem + 128 * (i & 1);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
           const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-          mma_ss(tmem + 0, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024),
-                 IDESC_SP, kk > 0);
+          mma_ss(tb, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024), IDESC_SP,
+                 kk > 0);
         }
 #pragma unroll
         for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
           const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-          mma_ss(tmem + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
+          mma_ss(tb + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
                  IDESC_SP, kk > 0);
         }
-        mma_commit(BAR_SPFULL);
+        mma_commit(BAR_SPFULL(i & 1));
         return true;
       };
       if (ok) ok = issue_sp(0);
+      if (ok && nq > 1) ok = issue_sp(1);
       for (int i = 0; ok && i < nq; ++i) {
-        if (i + 1 < nq) {
-          if (!mbar_wait(BAR_SPFREE, i & 1, abort, &g_bwd_err, 4)) break;
-          if (!issue_sp(i + 1)) break;
-        }
         if (!mbar_wait(BAR_PDSFULL(i & 1), (i >> 1) & 1, abort, &g_bwd_err, 4)) break;
         tc_fence_after();
         const int s = i % NQS;
-        const uint32_t pt = tmem + 128 + 32 * (i & 1), dst = tmem + 192 + 32 * (i & 1);
+        const uint32_t pt = tmem + 128 * (i & 1), dst = pt + 64;
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk)  // dK += dS^T Q   (K = 64 queries)
           mma_ts(tmem + 256, dst + kk * 8, smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
@@ -256,14 +252,17 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
             mma_ts(tmem + 384, pt + kk * 8, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
                    (i > 0 || kk > 0) ? 1u : 0u);
         }
-        mma_commit(BAR_PDSFREE(i & 1));
         mma_commit(BAR_QEMPTY(s));
+        // the next S^T / dP^T of this buffer is issued after the MMAs that read its P^T / dS^T
+        if (i + 2 < nq) ok = issue_sp(i + 2);
       }
       mma_commit(BAR_DONE);
       mbar_wait_drain(BAR_DONE, 0);
     }
   } else {
     // ---------------------------------------------------------------- compute: thread = key row
+    // two warpgroups: WG w owns the query tiles i = w, w+2, ... and TMEM buffer w
+    const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -271,46 +270,45 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
       const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
       return __all_sync(0xffffffffu, mine);
     };
+    const uint32_t ts = tmem + lane_off + 128 * wg, tdp = ts + 64;
     bool ok = true;
-    for (int i = 0; i < nq; ++i) {
+    for (int i = wg; i < nq; i += 2) {
       const int s = i % NQS;
-      if (!warp_wait(BAR_SPFULL, i & 1, 8)) { ok = false; break; }
+      if (!warp_wait(BAR_SPFULL(wg), (i >> 1) & 1, 8)) { ok = false; break; }
       if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
-      if (i >= 2 && !warp_wait(BAR_PDSFREE(i & 1), ((i - 2) >> 1) & 1, 8)) { ok = false; break; }
       tc_fence_after();
-      const float* st = slot_stats(s);
-      const uint32_t pt = tmem + lane_off + 128 + 32 * (i & 1), dst = tmem + lane_off + 192 + 32 * (i & 1);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(tmem + lane_off + c * 32, sv);
-        tmem_ld32(tmem + lane_off + 64 + c * 32, dv);
-        tmem_wait_ld();
-        if (c == 1) {
-          tc_fence_before();
-          mbar_arrive(BAR_SPFREE);
-        }
-        uint32_t pk[16], dk[16];
+      uint32_t sv[64], dv[64];
+      tmem_ld32(ts, sv);
+      tmem_ld32(ts + 32, sv + 32);
+      tmem_ld32(tdp, dv);
+      tmem_ld32(tdp + 32, dv + 32);
+      tmem_wait_ld();
+      const uint32_t st = slot_stats(s);
+      uint32_t pk[32], dk[32];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float pr[2], dr[2];
+      for (int e = 0; e < 64; e += 4) {
+        float l4[4], c4[4], g4[4];
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l4[0]), "=f"(l4[1]), "=f"(l4[2]), "=f"(l4[3]) : "r"(st + 4 * e));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c4[0]), "=f"(c4[1]), "=f"(c4[2]), "=f"(c4[3]) : "r"(st + 256 + 4 * e));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(g4[0]), "=f"(g4[1]), "=f"(g4[2]), "=f"(g4[3]) : "r"(st + 512 + 4 * e));
+        float pr[4], dr[4];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const int q = c * 32 + e + u;
-            const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
-            const float pv = fast_exp2(x - st[q]);
-            pr[u] = pv;
-            dr[u] = pv * (__uint_as_float(dv[e + u]) - st[64 + q] - st[128 + q] * x) * p.sm_scale;
-          }
-          pk[e >> 1] = Elem<T>::pack(pr[0], pr[1]);
-          dk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        for (int u = 0; u < 4; ++u) {
+          const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
+          const float pv = fast_exp2(x - l4[u]);
+          pr[u] = pv;
+          dr[u] = pv * (__uint_as_float(dv[e + u]) - c4[u] - g4[u] * x) * p.sm_scale;
         }
-        tmem_st16(pt + c * 16, pk);
-        tmem_st16(dst + c * 16, dk);
+        pk[e >> 1] = Elem<T>::pack(pr[0], pr[1]);
+        pk[(e >> 1) + 1] = Elem<T>::pack(pr[2], pr[3]);
+        dk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        dk[(e >> 1) + 1] = Elem<T>::pack(dr[2], dr[3]);
       }
+      tmem_st32(ts, pk);
+      tmem_st32(tdp, dk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(BAR_PDSFULL(i & 1));
+      mbar_arrive(BAR_PDSFULL(wg));
     }
     if (ok) ok = warp_wait(BAR_DONE, 0, 8);
     tc_fence_after();
@@ -318,9 +316,14 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     const bool kok = key < p.n_kv;
     const int64_t krow = kok ? key : 0;
     if (ok) {
-      store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok);
-      if (C::HAS_DV)
-        store_row128<T>(tmem + lane_off + 384, p.grad1, (int64_t)bi * p.g1_bs + krow * p.g1_cols, p.acc, kok);
+      // WG 0 writes dK, WG 1 writes dV (or, without dV, the second half of dK)
+      if (C::HAS_DV) {
+        if (wg == 0) store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok);
+        else store_row128<T>(tmem + lane_off + 384, p.grad1, (int64_t)bi * p.g1_bs + krow * p.g1_cols, p.acc, kok);
+      } else {
+        store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok, 2 * wg,
+                        2 * wg + 2);
+      }
     }
   }
 
@@ -341,7 +344,7 @@ struct DqCfg {
 };
 
 template <typename T, int XA, bool VK, int NSLOT>
-__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq_kernel(const __grid_constant__ Sm100BwdParams p) {
+__global__ void __launch_bounds__(kThreadsDq, 1) fea_bwd_dq_kernel(const __grid_constant__ Sm100BwdParams p) {
   using C = DqCfg<XA, VK, NSLOT>;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);
@@ -469,6 +472,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq_kernel(const __grid_co
       mbar_wait_drain(BAR_DONE, 0);
     }
   } else {
+    // two warpgroups: WG w owns the key tiles j = w, w+2, ... and TMEM buffer w; thread = query row
+    const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -482,39 +487,41 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq_kernel(const __grid_co
       const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
       return __all_sync(0xffffffffu, mine);
     };
+    const uint32_t ts = tmem + lane_off + 64 * wg, tdp = tmem + lane_off + 128 + 64 * wg;
+    const uint32_t tds = tmem + lane_off + 256 + 32 * wg;
     bool ok = true;
-    for (int j = 0; j < nk; ++j) {
-      if (!warp_wait(BAR_SPFULL(j & 1), (j >> 1) & 1, 128)) { ok = false; break; }
+    for (int j = wg; j < nk; j += 2) {
+      if (!warp_wait(BAR_SPFULL(wg), (j >> 1) & 1, 128)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t ts = tmem + lane_off + 64 * (j & 1), tdp = tmem + lane_off + 128 + 64 * (j & 1);
-      const uint32_t tds = tmem + lane_off + 256 + 32 * (j & 1);
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(ts + c * 32, sv);
-        tmem_ld32(tdp + c * 32, dv);
-        tmem_wait_ld();
-        uint32_t dk32[16];
+      uint32_t sv[64], dv[64];
+      tmem_ld32(ts, sv);
+      tmem_ld32(ts + 32, sv + 32);
+      tmem_ld32(tdp, dv);
+      tmem_ld32(tdp + 32, dv + 32);
+      tmem_wait_ld();
+      uint32_t pk[32];
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          float dr[2];
+      for (int e = 0; e < 64; e += 2) {
+        float dr[2];
 #pragma unroll
-          for (int u = 0; u < 2; ++u) {
-            const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
-            const float pv = fast_exp2(x - lse);
-            dr[u] = pv * (__uint_as_float(dv[e + u]) - cc - gg * x) * p.sm_scale;
-          }
-          dk32[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        for (int u = 0; u < 2; ++u) {
+          const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
+          const float pv = fast_exp2(x - lse);
+          dr[u] = pv * (__uint_as_float(dv[e + u]) - cc - gg * x) * p.sm_scale;
         }
-        tmem_st16(tds + c * 16, dk32);
+        pk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
       }
+      tmem_st32(tds, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(BAR_DSFULL(j & 1));
+      mbar_arrive(BAR_DSFULL(wg));
     }
+    ok = __all_sync(0xffffffffu, ok);
     if (ok) ok = warp_wait(BAR_DONE, 0, 128);
     tc_fence_after();
-    if (ok) store_row128<T>(tmem + lane_off + 384, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc, qok);
+    if (ok)
+      store_row128<T>(tmem + lane_off + 384, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc,
+                      qok, 2 * wg, 2 * wg + 2);
   }
 
   tc_fence_before();
@@ -525,11 +532,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq_kernel(const __grid_co
 
 // ================================================================================ host side
 template <typename Kern>
-cudaError_t run(Kern kern, int smem, int64_t blocks, const Sm100BwdParams& p, cudaStream_t st) {
+cudaError_t run(Kern kern, int smem, int64_t blocks, int threads, const Sm100BwdParams& p, cudaStream_t st) {
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
   if (e != cudaSuccess) return e;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  kern<<<(unsigned)blocks, kThreads, smem, st>>>(p);
+  kern<<<(unsigned)blocks, threads, smem, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -566,11 +573,11 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   cudaError_t e;
   const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
   if (vk && xa == 0) {
-    e = run(fea_bwd_dkdv_kernel<T, 0, true, 4>, DkdvCfg<0, true, 4>::SMEM, blocks_a, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 0, true, 4>, DkdvCfg<0, true, 4>::SMEM, blocks_a, kThreads, pa, st);
   } else if (vk) {
-    e = run(fea_bwd_dkdv_kernel<T, 2, true, 3>, DkdvCfg<2, true, 3>::SMEM, blocks_a, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 2, true, 3>, DkdvCfg<2, true, 3>::SMEM, blocks_a, kThreads, pa, st);
   } else {
-    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4>, DkdvCfg<2, false, 4>::SMEM, blocks_a, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4>, DkdvCfg<2, false, 4>::SMEM, blocks_a, kThreads, pa, st);
   }
   if (e != cudaSuccess) return e;
   // ---- dQ
@@ -597,9 +604,9 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pb.scale_log2 = b.scale_log2;
   pb.sm_scale = b.sm_scale;
   const int64_t blocks_b = (int64_t)pb.n_tiles * batch;
-  if (vk && xa == 0) return run(fea_bwd_dq_kernel<T, 0, true, 6>, DqCfg<0, true, 6>::SMEM, blocks_b, pb, st);
-  if (vk) return run(fea_bwd_dq_kernel<T, 2, true, 3>, DqCfg<2, true, 3>::SMEM, blocks_b, pb, st);
-  return run(fea_bwd_dq_kernel<T, 2, false, 4>, DqCfg<2, false, 4>::SMEM, blocks_b, pb, st);
+  if (vk && xa == 0) return run(fea_bwd_dq_kernel<T, 0, true, 6>, DqCfg<0, true, 6>::SMEM, blocks_b, kThreadsDq, pb, st);
+  if (vk) return run(fea_bwd_dq_kernel<T, 2, true, 3>, DqCfg<2, true, 3>::SMEM, blocks_b, kThreadsDq, pb, st);
+  return run(fea_bwd_dq_kernel<T, 2, false, 4>, DqCfg<2, false, 4>::SMEM, blocks_b, kThreadsDq, pb, st);
 }
 
 }  // namespace
