@@ -23,7 +23,10 @@
 namespace vmb {
 namespace {
 
-constexpr int kWarps = 4;
+// Warps (= grid columns) per CTA. There is no block-level barrier, so CTAs are kept small: the
+// per-warp shared memory (19-37 KB) then packs 6-11 warps per SM instead of one 4-warp CTA.
+constexpr int kWarpsFwd = 2;
+constexpr int kWarpsBwd = 1;
 
 template <int MP>
 struct Tile {
@@ -250,7 +253,7 @@ __device__ __forceinline__ void load_ent(float (&ent)[MP / 8][2], const float* e
 
 // ============================================================================ forward
 template <typename T, int MP, int D, bool LAST>
-__global__ void __launch_bounds__(kWarps * 32) lstep_fwd_mma_kernel(const LstepParams p) {
+__global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const LstepParams p) {
   constexpr int DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -260,7 +263,7 @@ __global__ void __launch_bounds__(kWarps * 32) lstep_fwd_mma_kernel(const LstepP
   T* sa = so + MP * OW;
   float* svec = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);
 
-  const int64_t col = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t col = (int64_t)blockIdx.x * kWarpsFwd + warp;
   if (col >= p.bh * p.b) return;  // no block-level barrier below: each warp is independent
   const int64_t bh = col / p.b;
   const int j = (int)(col % p.b), m = (int)p.m;
@@ -322,7 +325,7 @@ __global__ void __launch_bounds__(kWarps * 32) lstep_fwd_mma_kernel(const LstepP
 
 // ============================================================================ backward
 template <typename T, int MP, int D, bool LAST>
-__global__ void __launch_bounds__(kWarps * 32) lstep_bwd_mma_kernel(const LstepParams p) {
+__global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const LstepParams p) {
   constexpr int DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -333,7 +336,7 @@ __global__ void __launch_bounds__(kWarps * 32) lstep_bwd_mma_kernel(const LstepP
   T* sa = sg + MP * D;      // m x m staging (a or a*c)
   T* sd = sa + MP * Tile<MP>::SA;  // m x m staging (dlog)
 
-  const int64_t col = (int64_t)blockIdx.x * kWarps + warp;
+  const int64_t col = (int64_t)blockIdx.x * kWarpsBwd + warp;
   if (col >= p.bh * p.b) return;
   const int64_t bh = col / p.b;
   const int j = (int)(col % p.b), m = (int)p.m;
@@ -476,13 +479,14 @@ cudaError_t launch(const LstepParams& p, bool bwd, cudaStream_t st) {
   constexpr int OW = LAST ? 2 * D : D;
   const size_t per_warp = bwd ? (size_t)(2 * MP * D + MP * OW + 2 * MP * Tile<MP>::SA) * sizeof(T)
                               : (size_t)(MP * D + MP * OW + MP * Tile<MP>::SA) * sizeof(T) + MP * sizeof(float);
-  const size_t smem = per_warp * kWarps;
+  const int warps = bwd ? kWarpsBwd : kWarpsFwd;
+  const size_t smem = per_warp * warps;
   auto kern = bwd ? lstep_bwd_mma_kernel<T, MP, D, LAST> : lstep_fwd_mma_kernel<T, MP, D, LAST>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
-  const int64_t blocks = (p.bh * p.b + kWarps - 1) / kWarps;
+  const int64_t blocks = (p.bh * p.b + warps - 1) / warps;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  kern<<<(unsigned)blocks, kWarps * 32, smem, st>>>(p);
+  kern<<<(unsigned)blocks, warps * 32, smem, st>>>(p);
   return cudaGetLastError();
 }
 
