@@ -35,12 +35,13 @@ namespace {
 using namespace sm100;
 
 constexpr int kThreads = 320;    // producer warp, MMA warp, two compute warpgroups on alternate tiles
-constexpr int kThreadsDq = 320;
 constexpr int kAtom128 = 128 * 128;  // swizzle-atom column block of 128 rows x 128 B
 constexpr int kAtom64 = 64 * 128;    // ... of 64 rows x 128 B
 
 struct Sm100BwdParams {
-  CUtensorMap tm_a, tm_b, tm_c, tm_d;  // dkdv: K, X, Q, dO (box 128,128,64,64); dq: Q, dO, K, X (128,128,64,64)
+  CUtensorMap tm_a, tm_b, tm_c, tm_d;  // dkdv: K, X, Q, dO ; dq: Q, dO, K, X  (boxes of 64 cols x 64/128 rows)
+  const void* dout;  // dq kernel with dO in TMEM: [batch][n_q][DW] rows read directly
+  int64_t do_bs;
   const float* lse;
   const float* cc;
   const float* gg;
@@ -333,59 +334,79 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// ================================================================================ dQ kernel
-template <int XA, bool VK, int NSLOT>
-struct DqCfg {
+// ================================================================================ dQ kernel, 128-key tiles
+// CTA = 128 queries; walks 128-key tiles, so every MMA is a full-rate 128 x 128 x 16 instruction.
+// Both compute warpgroups work on the same tile: WG w owns keys [64w, 64w+64) of it.
+//   S = Q K^T (SS), dP = dO W^T (SS, or TS with dO resident in TMEM when DW = 256), dS (bf16)
+//   written over the first half of the warpgroup's own S columns, dQ += dS K (TS).
+// DOT = false: TMEM S0 [0,128) S1 [128,256) dP [256,384) dQ [384,512); S double-buffered, so
+//   S(j+2) is queued behind dQ(j) while dP(j+1) is issued as soon as tile j's dP has been read.
+// DOT = true (DW = 256): TMEM S [0,128) dP [128,256) dO [256,384) dQ [384,512); dO is staged into
+//   TMEM once by the compute threads, which frees the shared memory for 3-deep K and V2 rings.
+// K and X (V, or V2 when V aliases K) stream through separate rings: X(j) is released after dP(j),
+// K(j) after dQ(j).
+template <int XA, bool VK, bool DOT, int NK, int NX>
+struct DqCfg2 {
   static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
-  static constexpr int RES = (2 + DW / 64) * kAtom128;  // resident Q | dO
-  static constexpr int SLOT = (2 + XA) * kAtom64;       // K | X of one 64-key tile
-  static constexpr int SMEM = 1024 + RES + NSLOT * SLOT;
+  static constexpr int NS = DOT ? 1 : 2;
+  static constexpr int RES = 2 * kAtom128 + (DOT ? 0 : (DW / 64) * kAtom128);  // Q | dO
+  static constexpr int KSLOT = 2 * kAtom128;
+  static constexpr int XSLOT = XA * kAtom128;
+  static constexpr int SMEM = 1024 + RES + NK * KSLOT + NX * XSLOT;
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(!DOT || DW == 256, "dO in TMEM is laid out for DW = 256");
+  static_assert((XA == 0) == (NX == 0), "X ring present exactly when there is an X tile");
 };
 
-template <typename T, int XA, bool VK, int NSLOT>
-__global__ void __launch_bounds__(kThreadsDq, 1) fea_bwd_dq_kernel(const __grid_constant__ Sm100BwdParams p) {
-  using C = DqCfg<XA, VK, NSLOT>;
+template <typename T, int XA, bool VK, bool DOT, int NK, int NX>
+__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid_constant__ Sm100BwdParams p) {
+  using C = DqCfg2<XA, VK, DOT, NK, NX>;
+  constexpr int NS = C::NS;
+  constexpr int NXB = NX > 0 ? NX : 1;
   constexpr bool kBf16 = Elem<T>::is_bf16;
-  constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);
+  constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
   constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 128, false, true);
+  constexpr uint32_t T_DP = DOT ? 128 : 256, T_DO = 256, T_DQ = 384;
+  constexpr int B_Q = 0, B_KFULL = 1, B_KEMPTY = B_KFULL + NK, B_XFULL = B_KEMPTY + NK, B_XEMPTY = B_XFULL + NXB;
+  constexpr int B_SFULL = B_XEMPTY + NXB, B_DSFULL = B_SFULL + NS, B_DPFULL = B_DSFULL + NS;
+  constexpr int B_DPFREE = B_DPFULL + 1, B_DOT = B_DPFREE + 1, B_DONE = B_DOT + 1, NBARS = B_DONE + 1;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[1 + 3 * NSLOT + 5];
+  __shared__ __align__(8) uint64_t bars[NBARS];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bi = blockIdx.x / p.n_tiles;
   const int q0 = (blockIdx.x % p.n_tiles) * 128;
-  const int nk = (p.n_kv + 63) / 64;
+  const int nk = (p.n_kv + 127) / 128;
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = sbase, sDO = sbase + 2 * kAtom128;
-  const uint32_t sRing = sbase + C::RES;
+  const uint32_t sK = sbase + C::RES, sX = sK + NK * C::KSLOT;
   const uint32_t bar0 = smem_u32(bars);
-  const uint32_t BAR_Q = bar0;
-  auto BAR_KFULL = [&](int s) { return bar0 + 8u * (1 + s); };
-  auto BAR_VFULL = [&](int s) { return bar0 + 8u * (1 + NSLOT + s); };
-  auto BAR_EMPTY = [&](int s) { return bar0 + 8u * (1 + 2 * NSLOT + s); };
-  auto BAR_SPFULL = [&](int b) { return bar0 + 8u * (1 + 3 * NSLOT + b); };
-  auto BAR_DSFULL = [&](int b) { return bar0 + 8u * (3 + 3 * NSLOT + b); };
-  const uint32_t BAR_DONE = bar0 + 8u * (5 + 3 * NSLOT);
+  auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   volatile int* abort = &abort_sh;
 
   if (threadIdx.x == 0) {
     abort_sh = 0;
-    mbar_init(BAR_Q, 1);
-    for (int s = 0; s < NSLOT; ++s) {
-      mbar_init(BAR_KFULL(s), 1);
-      mbar_init(BAR_VFULL(s), 1);
-      mbar_init(BAR_EMPTY(s), 1);
+    mbar_init(BAR(B_Q), 1);
+    for (int s = 0; s < NK; ++s) {
+      mbar_init(BAR(B_KFULL + s), 1);
+      mbar_init(BAR(B_KEMPTY + s), 1);
     }
-    for (int b = 0; b < 2; ++b) {
-      mbar_init(BAR_SPFULL(b), 1);
-      mbar_init(BAR_DSFULL(b), 128);
+    for (int s = 0; s < NXB; ++s) {
+      mbar_init(BAR(B_XFULL + s), 1);
+      mbar_init(BAR(B_XEMPTY + s), 1);
     }
-    mbar_init(BAR_DONE, 1);
+    for (int b = 0; b < NS; ++b) {
+      mbar_init(BAR(B_SFULL + b), 1);
+      mbar_init(BAR(B_DSFULL + b), 256);
+    }
+    mbar_init(BAR(B_DPFULL), 1);
+    mbar_init(BAR(B_DPFREE), 256);
+    mbar_init(BAR(B_DOT), 256);
+    mbar_init(BAR(B_DONE), 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -398,81 +419,112 @@ __global__ void __launch_bounds__(kThreadsDq, 1) fea_bwd_dq_kernel(const __grid_
   const uint32_t tmem = tmem_base_sh;
 
   if (warp == 0) {
+    // ---------------------------------------------------------------- TMA producer
     if (lane == 0) {
       prefetch_tmap(&p.tm_a);
-      prefetch_tmap(&p.tm_b);
       prefetch_tmap(&p.tm_c);
-      mbar_expect_tx(BAR_Q, C::RES);
-      tma_load_3d(sQ, &p.tm_a, 0, q0, bi, BAR_Q);
-      tma_load_3d(sQ + kAtom128, &p.tm_a, 64, q0, bi, BAR_Q);
-      for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(sDO + a * kAtom128, &p.tm_b, 64 * a, q0, bi, BAR_Q);
-      int armed[NSLOT];
-      for (int s = 0; s < NSLOT; ++s) armed[s] = 0;
+      if (!DOT) prefetch_tmap(&p.tm_b);
+      if (XA > 0) prefetch_tmap(&p.tm_d);
+      mbar_expect_tx(BAR(B_Q), C::RES);
+      tma_load_3d(sQ, &p.tm_a, 0, q0, bi, BAR(B_Q));
+      tma_load_3d(sQ + kAtom128, &p.tm_a, 64, q0, bi, BAR(B_Q));
+      if (!DOT)
+        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(sDO + a * kAtom128, &p.tm_b, 64 * a, q0, bi, BAR(B_Q));
+      int karmed[NK], xarmed[NXB];
+      for (int s = 0; s < NK; ++s) karmed[s] = 0;
+      for (int s = 0; s < NXB; ++s) xarmed[s] = 0;
       for (int j = 0; j < nk; ++j) {
-        const int s = j % NSLOT;
-        if (j >= NSLOT && !mbar_wait(BAR_EMPTY(s), ((j / NSLOT) - 1) & 1, abort, &g_bwd_err, 16)) break;
-        const uint32_t slot = sRing + s * C::SLOT;
-        mbar_expect_tx(BAR_KFULL(s), 2 * kAtom64);
-        tma_load_3d(slot, &p.tm_c, 0, j * 64, bi, BAR_KFULL(s));
-        tma_load_3d(slot + kAtom64, &p.tm_c, 64, j * 64, bi, BAR_KFULL(s));
+        const int s = j % NK;
+        if (j >= NK && !mbar_wait(BAR(B_KEMPTY + s), ((j / NK) - 1) & 1, abort, &g_bwd_err, 16)) break;
+        mbar_expect_tx(BAR(B_KFULL + s), C::KSLOT);
+        tma_load_3d(sK + s * C::KSLOT, &p.tm_c, 0, j * 128, bi, BAR(B_KFULL + s));
+        tma_load_3d(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, j * 128, bi, BAR(B_KFULL + s));
+        karmed[s] = j / NK + 1;
         if (XA > 0) {
-          mbar_expect_tx(BAR_VFULL(s), XA * kAtom64);
-          for (int a = 0; a < XA; ++a) tma_load_3d(slot + (2 + a) * kAtom64, &p.tm_d, 64 * a, j * 64, bi, BAR_VFULL(s));
-        }
-        armed[s] = j / NSLOT + 1;
-      }
-      mbar_wait_drain(BAR_Q, 0);
-      for (int s = 0; s < NSLOT; ++s) {
-        if (armed[s] > 0) {
-          mbar_wait_drain(BAR_KFULL(s), (armed[s] - 1) & 1);
-          if (XA > 0) mbar_wait_drain(BAR_VFULL(s), (armed[s] - 1) & 1);
+          const int x = j % NXB;
+          if (j >= NXB && !mbar_wait(BAR(B_XEMPTY + x), ((j / NXB) - 1) & 1, abort, &g_bwd_err, 16)) break;
+          mbar_expect_tx(BAR(B_XFULL + x), C::XSLOT);
+          for (int a = 0; a < XA; ++a)
+            tma_load_3d(sX + x * C::XSLOT + a * kAtom128, &p.tm_d, 64 * a, j * 128, bi, BAR(B_XFULL + x));
+          xarmed[x] = j / NXB + 1;
         }
       }
+      mbar_wait_drain(BAR(B_Q), 0);
+      for (int s = 0; s < NK; ++s)
+        if (karmed[s] > 0) mbar_wait_drain(BAR(B_KFULL + s), (karmed[s] - 1) & 1);
+      if (XA > 0)
+        for (int s = 0; s < NXB; ++s)
+          if (xarmed[s] > 0) mbar_wait_drain(BAR(B_XFULL + s), (xarmed[s] - 1) & 1);
     }
   } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
     if (lane == 0) {
-      bool ok = mbar_wait(BAR_Q, 0, abort, &g_bwd_err, 32);
-      auto issue_sp = [&](int j) -> bool {
-        const int s = j % NSLOT;
-        const uint32_t slot = sRing + s * C::SLOT;
-        if (!mbar_wait(BAR_KFULL(s), (j / NSLOT) & 1, abort, &g_bwd_err, 32)) return false;
-        if (XA > 0 && !mbar_wait(BAR_VFULL(s), (j / NSLOT) & 1, abort, &g_bwd_err, 32)) return false;
+      bool ok = mbar_wait(BAR(B_Q), 0, abort, &g_bwd_err, 32);
+      if (DOT && ok) ok = mbar_wait(BAR(B_DOT), 0, abort, &g_bwd_err, 32);
+      auto issue_s = [&](int j) -> bool {
+        const int s = j % NK;
+        if (!mbar_wait(BAR(B_KFULL + s), (j / NK) & 1, abort, &g_bwd_err, 32)) return false;
         tc_fence_after();
-        const uint32_t ds = tmem + 64 * (j & 1), dp = tmem + 128 + 64 * (j & 1);
+        const uint32_t kb = sK + s * C::KSLOT;
+        const uint32_t d = tmem + 128u * (uint32_t)(j % NS);
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {  // S = Q K^T
-          const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-          mma_ss(ds, smem_desc_sw128(sQ + offa, 16, 1024), smem_desc_sw128(slot + offb, 16, 1024), IDESC_SP, kk > 0);
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
+          mma_ss(d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
         }
-        const uint32_t w = VK ? slot : slot + 2 * kAtom64;
-#pragma unroll
-        for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP = dO W^T
-          const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-          mma_ss(dp, smem_desc_sw128(sDO + offa, 16, 1024), smem_desc_sw128(w + offb, 16, 1024), IDESC_SP, kk > 0);
-        }
-        mma_commit(BAR_SPFULL(j & 1));
+        mma_commit(BAR(B_SFULL + j % NS));
         return true;
       };
-      if (ok) ok = issue_sp(0);
-      if (ok && nk > 1) ok = issue_sp(1);
-      for (int j = 0; ok && j < nk; ++j) {
-        if (!mbar_wait(BAR_DSFULL(j & 1), (j >> 1) & 1, abort, &g_bwd_err, 64)) break;
+      auto issue_dp = [&](int j) -> bool {
+        const int s = j % NK, x = j % NXB;
+        if (VK && !mbar_wait(BAR(B_KFULL + s), (j / NK) & 1, abort, &g_bwd_err, 32)) return false;
+        if (XA > 0 && !mbar_wait(BAR(B_XFULL + x), (j / NXB) & 1, abort, &g_bwd_err, 32)) return false;
         tc_fence_after();
-        const int s = j % NSLOT;
-        const uint32_t slot = sRing + s * C::SLOT;
-        const uint32_t dsb = tmem + 256 + 32 * (j & 1);
+        const uint32_t kb = sK + s * C::KSLOT, xb = sX + x * C::XSLOT;
 #pragma unroll
-        for (int kk = 0; kk < 4; ++kk)  // dQ += dS K  (K = 64 keys)
-          mma_ts(tmem + 384, dsb + kk * 8, smem_desc_sw128(slot + kk * 2048, kAtom64, 1024), IDESC_DQ,
+        for (int kk = 0; kk < C::DW / 16; ++kk) {
+          uint32_t boff;
+          if (VK) boff = kk < 8 ? kb + (kk >> 2) * kAtom128 + (kk & 3) * 32
+                                : xb + ((kk - 8) >> 2) * kAtom128 + ((kk - 8) & 3) * 32;
+          else boff = xb + (kk >> 2) * kAtom128 + (kk & 3) * 32;
+          const uint64_t bd = smem_desc_sw128(boff, 16, 1024);
+          if (DOT)
+            mma_ts(tmem + T_DP, tmem + T_DO + kk * 8, bd, IDESC_S, kk > 0);
+          else
+            mma_ss(tmem + T_DP, smem_desc_sw128(sDO + (kk >> 2) * kAtom128 + (kk & 3) * 32, 16, 1024), bd, IDESC_S,
+                   kk > 0);
+        }
+        mma_commit(BAR(B_DPFULL));
+        if (XA > 0) mma_commit(BAR(B_XEMPTY + x));
+        return true;
+      };
+      if (ok) ok = issue_s(0);
+      if (ok) ok = issue_dp(0);
+      if (ok && NS == 2 && nk > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < nk; ++j) {
+        if (j + 1 < nk) {
+          if (!mbar_wait(BAR(B_DPFREE), j & 1, abort, &g_bwd_err, 64)) break;
+          if (!issue_dp(j + 1)) break;
+        }
+        if (!mbar_wait(BAR(B_DSFULL + j % NS), (j / NS) & 1, abort, &g_bwd_err, 64)) break;
+        tc_fence_after();
+        const uint32_t kb = sK + (j % NK) * C::KSLOT;
+        const uint32_t sb = tmem + 128u * (uint32_t)(j % NS);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K ; keys [16kk, 16kk+16) of warpgroup kk/4
+          const uint32_t a_tm = sb + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
+          mma_ts(tmem + T_DQ, a_tm, smem_desc_sw128(kb + kk * 2048, kAtom128, 1024), IDESC_DQ,
                  (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(BAR_EMPTY(s));
-        if (j + 2 < nk) ok = issue_sp(j + 2);
+        }
+        mma_commit(BAR(B_KEMPTY + j % NK));
+        const int nxt = j + NS;  // the next tile that uses this S buffer
+        if (nxt < nk) ok = issue_s(nxt);
       }
-      mma_commit(BAR_DONE);
-      mbar_wait_drain(BAR_DONE, 0);
+      mma_commit(BAR(B_DONE));
+      mbar_wait_drain(BAR(B_DONE), 0);
     }
   } else {
-    // two warpgroups: WG w owns the key tiles j = w, w+2, ... and TMEM buffer w; thread = query row
+    // ---------------------------------------------------------------- compute: thread = query row
     const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
@@ -487,18 +539,41 @@ __global__ void __launch_bounds__(kThreadsDq, 1) fea_bwd_dq_kernel(const __grid_
       const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
       return __all_sync(0xffffffffu, mine);
     };
-    const uint32_t ts = tmem + lane_off + 64 * wg, tdp = tmem + lane_off + 128 + 64 * wg;
-    const uint32_t tds = tmem + lane_off + 256 + 32 * wg;
     bool ok = true;
-    for (int j = wg; j < nk; j += 2) {
-      if (!warp_wait(BAR_SPFULL(wg), (j >> 1) & 1, 128)) { ok = false; break; }
+    if (DOT) {
+      // dO row -> TMEM (bf16 pairs): warpgroup w stages elements [128w, 128w+128)
+      uint32_t w32[64];
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) + (int64_t)bi * p.do_bs +
+                                                        (int64_t)(qok ? q : 0) * C::DW + 128 * wg);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 v = qok ? src[i] : make_uint4(0, 0, 0, 0);
+        w32[4 * i] = v.x;
+        w32[4 * i + 1] = v.y;
+        w32[4 * i + 2] = v.z;
+        w32[4 * i + 3] = v.w;
+      }
+      tmem_st32(tmem + lane_off + T_DO + 64 * wg, w32);
+      tmem_st32(tmem + lane_off + T_DO + 64 * wg + 32, w32 + 32);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(BAR(B_DOT));
+    }
+    for (int j = 0; j < nk; ++j) {
+      const int b = j % NS;
+      if (!warp_wait(BAR(B_SFULL + b), (j / NS) & 1, 128)) { ok = false; break; }
+      if (!warp_wait(BAR(B_DPFULL), j & 1, 128)) { ok = false; break; }
       tc_fence_after();
+      const uint32_t ts = tmem + lane_off + 128u * (uint32_t)b + 64 * wg;
+      const uint32_t tdp = tmem + lane_off + T_DP + 64 * wg;
       uint32_t sv[64], dv[64];
       tmem_ld32(ts, sv);
       tmem_ld32(ts + 32, sv + 32);
       tmem_ld32(tdp, dv);
       tmem_ld32(tdp + 32, dv + 32);
       tmem_wait_ld();
+      tc_fence_before();
+      mbar_arrive(BAR(B_DPFREE));
       uint32_t pk[32];
 #pragma unroll
       for (int e = 0; e < 64; e += 2) {
@@ -511,17 +586,248 @@ __global__ void __launch_bounds__(kThreadsDq, 1) fea_bwd_dq_kernel(const __grid_
         }
         pk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
       }
-      tmem_st32(tds, pk);
+      tmem_st32(ts, pk);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(BAR_DSFULL(wg));
+      mbar_arrive(BAR(B_DSFULL + b));
     }
-    ok = __all_sync(0xffffffffu, ok);
-    if (ok) ok = warp_wait(BAR_DONE, 0, 128);
+    if (ok) ok = warp_wait(BAR(B_DONE), 0, 128);
     tc_fence_after();
     if (ok)
-      store_row128<T>(tmem + lane_off + 384, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc,
+      store_row128<T>(tmem + lane_off + T_DQ, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc,
                       qok, 2 * wg, 2 * wg + 2);
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ================================================================================ dK/dV kernel, 128-query tiles
+// CTA = 128 keys; walks 128-query tiles (full-rate N = 128 MMAs); WG w owns queries [64w, 64w+64)
+// of each tile. TMEM: S^T [0,128) dP^T [128,256) dK [256,384) dV [384,512); P^T / dS^T (bf16) are
+// written over the first half of each warpgroup's own S^T / dP^T columns, so tile i+1's S^T / dP^T
+// are issued behind tile i's dK / dV MMAs. Used for every mode whose 128-row query slot fits twice
+// in shared memory (all but the last VMonarch R step, whose dO is 256 wide).
+template <int XA, bool VK, int NQS>
+struct DkdvCfg2 {
+  static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
+  static constexpr int RES = (2 + XA) * kAtom128;
+  static constexpr int SLOT_T = (2 + DW / 64) * kAtom128;
+  static constexpr int SLOT = SLOT_T + 2048;  // + statistics: LSE2, c, g x 128
+  static constexpr int SMEM = 1024 + RES + NQS * SLOT;
+  static constexpr bool HAS_DV = XA > 0;
+  static_assert(SMEM <= 232448, "shared memory budget");
+};
+
+template <typename T, int XA, bool VK, int NQS>
+__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv128_kernel(const __grid_constant__ Sm100BwdParams p) {
+  using C = DkdvCfg2<XA, VK, NQS>;
+  constexpr bool kBf16 = Elem<T>::is_bf16;
+  constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);
+  constexpr int B_KV = 0, B_QFULL = 1, B_QEMPTY = 1 + NQS, B_SPFULL = 1 + 2 * NQS, B_PDSFULL = B_SPFULL + 1;
+  constexpr int B_DONE = B_PDSFULL + 1, NBARS = B_DONE + 1;
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[NBARS];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bi = blockIdx.x / p.n_tiles;
+  const int k0 = (blockIdx.x % p.n_tiles) * 128;
+  const int nq = (p.n_q + 127) / 128;
+
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sRes = sbase;
+  const uint32_t sW = VK ? sRes : sRes + 2 * kAtom128;
+  const uint32_t sSlots = sbase + C::RES;
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
+  volatile int* abort = &abort_sh;
+  auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
+  auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom128; };
+  auto slot_stats = [&](int s) { return sSlots + s * C::SLOT + C::SLOT_T; };
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    mbar_init(BAR(B_KV), 1);
+    for (int s = 0; s < NQS; ++s) {
+      mbar_init(BAR(B_QFULL + s), 1 + 32);
+      mbar_init(BAR(B_QEMPTY + s), 1);
+    }
+    mbar_init(BAR(B_SPFULL), 1);
+    mbar_init(BAR(B_PDSFULL), 256);
+    mbar_init(BAR(B_DONE), 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_base_sh), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------------- producer (whole warp)
+    int armed[NQS];
+    for (int s = 0; s < NQS; ++s) armed[s] = 0;
+    if (lane == 0) {
+      prefetch_tmap(&p.tm_a);
+      prefetch_tmap(&p.tm_c);
+      prefetch_tmap(&p.tm_d);
+      mbar_expect_tx(BAR(B_KV), C::RES);
+      tma_load_3d(sRes, &p.tm_a, 0, k0, bi, BAR(B_KV));
+      tma_load_3d(sRes + kAtom128, &p.tm_a, 64, k0, bi, BAR(B_KV));
+      for (int a = 0; a < XA; ++a) tma_load_3d(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bi, BAR(B_KV));
+    }
+    const float* lse = p.lse + (int64_t)bi * p.n_q;
+    const float* cc = p.cc + (int64_t)bi * p.n_q;
+    const float* gg = p.gg + (int64_t)bi * p.n_q;
+    for (int i = 0; i < nq; ++i) {
+      const int s = i % NQS;
+      bool ok = true;
+      if (lane == 0 && i >= NQS) ok = mbar_wait(BAR(B_QEMPTY + s), ((i / NQS) - 1) & 1, abort, &g_bwd_err, 1);
+      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      if (lane == 0) {
+        mbar_expect_tx(BAR(B_QFULL + s), C::SLOT_T);
+        tma_load_3d(slot_q(s), &p.tm_c, 0, i * 128, bi, BAR(B_QFULL + s));
+        tma_load_3d(slot_q(s) + kAtom128, &p.tm_c, 64, i * 128, bi, BAR(B_QFULL + s));
+        for (int a = 0; a < C::DW / 64; ++a)
+          tma_load_3d(slot_do(s) + a * kAtom128, &p.tm_d, 64 * a, i * 128, bi, BAR(B_QFULL + s));
+      }
+      float* st = reinterpret_cast<float*>(smem_raw + (slot_stats(s) - smem_u32(smem_raw)));
+#pragma unroll
+      for (int h = 0; h < 4; ++h) {
+        const int qq = i * 128 + lane + 32 * h;
+        const bool okq = qq < p.n_q;
+        st[lane + 32 * h] = okq ? lse[qq] : __int_as_float(0x7f800000);
+        st[128 + lane + 32 * h] = okq ? cc[qq] : 0.f;
+        st[256 + lane + 32 * h] = okq ? gg[qq] : 0.f;
+      }
+      mbar_arrive(BAR(B_QFULL + s));
+      armed[s] = i / NQS + 1;
+    }
+    if (lane == 0) {
+      mbar_wait_drain(BAR(B_KV), 0);
+      for (int s = 0; s < NQS; ++s)
+        if (armed[s] > 0) mbar_wait_drain(BAR(B_QFULL + s), (armed[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      bool ok = mbar_wait(BAR(B_KV), 0, abort, &g_bwd_err, 2);
+      auto issue_sp = [&](int i) -> bool {
+        const int s = i % NQS;
+        if (!mbar_wait(BAR(B_QFULL + s), (i / NQS) & 1, abort, &g_bwd_err, 2)) return false;
+        tc_fence_after();
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
+          const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
+          mma_ss(tmem, smem_desc_sw128(sRes + off, 16, 1024), smem_desc_sw128(slot_q(s) + off, 16, 1024), IDESC_SP,
+                 kk > 0);
+        }
+#pragma unroll
+        for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
+          const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
+          mma_ss(tmem + 128, smem_desc_sw128(sW + off, 16, 1024), smem_desc_sw128(slot_do(s) + off, 16, 1024),
+                 IDESC_SP, kk > 0);
+        }
+        mma_commit(BAR(B_SPFULL));
+        return true;
+      };
+      if (ok) ok = issue_sp(0);
+      for (int i = 0; ok && i < nq; ++i) {
+        if (!mbar_wait(BAR(B_PDSFULL), i & 1, abort, &g_bwd_err, 4)) break;
+        tc_fence_after();
+        const int s = i % NQS;
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {  // queries [16kk, 16kk+16) live in warpgroup kk/4's columns
+          const uint32_t col = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
+          const uint64_t bq = smem_desc_sw128(slot_q(s) + kk * 2048, kAtom128, 1024);
+          mma_ts(tmem + 256, tmem + 128 + col, bq, IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);  // dK += dS^T Q
+          if (VK)
+            mma_ts(tmem + 256, tmem + col, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom128, 1024), IDESC_ACC, 1u);
+          if (C::HAS_DV) {
+            const uint32_t vo = VK ? 2 * kAtom128 : 0;
+            mma_ts(tmem + 384, tmem + col, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom128, 1024), IDESC_ACC,
+                   (i > 0 || kk > 0) ? 1u : 0u);
+          }
+        }
+        mma_commit(BAR(B_QEMPTY + s));
+        if (i + 1 < nq) ok = issue_sp(i + 1);  // queued behind the MMAs that read P^T / dS^T
+      }
+      mma_commit(BAR(B_DONE));
+      mbar_wait_drain(BAR(B_DONE), 0);
+    }
+  } else {
+    // ---------------------------------------------------------------- compute: thread = key row
+    const int wg = (warp - 2) >> 2;
+    const int quad = warp & 3;
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+      const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
+      return __all_sync(0xffffffffu, mine);
+    };
+    const uint32_t ts = tmem + lane_off + 64 * wg, tdp = tmem + lane_off + 128 + 64 * wg;
+    bool ok = true;
+    for (int i = 0; i < nq; ++i) {
+      const int s = i % NQS;
+      if (!warp_wait(BAR(B_SPFULL), i & 1, 8)) { ok = false; break; }
+      if (!warp_wait(BAR(B_QFULL + s), (i / NQS) & 1, 8)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t sv[64], dv[64];
+      tmem_ld32(ts, sv);
+      tmem_ld32(ts + 32, sv + 32);
+      tmem_ld32(tdp, dv);
+      tmem_ld32(tdp + 32, dv + 32);
+      tmem_wait_ld();
+      const uint32_t st = slot_stats(s) + 4 * 64 * wg;  // this warpgroup's 64 queries
+      uint32_t pk[32], dk[32];
+#pragma unroll
+      for (int e = 0; e < 64; e += 4) {
+        float l4[4], c4[4], g4[4];
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l4[0]), "=f"(l4[1]), "=f"(l4[2]), "=f"(l4[3]) : "r"(st + 4 * e));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c4[0]), "=f"(c4[1]), "=f"(c4[2]), "=f"(c4[3]) : "r"(st + 512 + 4 * e));
+        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(g4[0]), "=f"(g4[1]), "=f"(g4[2]), "=f"(g4[3]) : "r"(st + 1024 + 4 * e));
+        float pr[4], dr[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
+          const float pv = fast_exp2(x - l4[u]);
+          pr[u] = pv;
+          dr[u] = pv * (__uint_as_float(dv[e + u]) - c4[u] - g4[u] * x) * p.sm_scale;
+        }
+        pk[e >> 1] = Elem<T>::pack(pr[0], pr[1]);
+        pk[(e >> 1) + 1] = Elem<T>::pack(pr[2], pr[3]);
+        dk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        dk[(e >> 1) + 1] = Elem<T>::pack(dr[2], dr[3]);
+      }
+      tmem_st32(ts, pk);
+      tmem_st32(tdp, dk);
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(BAR(B_PDSFULL));
+    }
+    if (ok) ok = warp_wait(BAR(B_DONE), 0, 8);
+    tc_fence_after();
+    const int key = k0 + row;
+    const bool kok = key < p.n_kv;
+    const int64_t krow = kok ? key : 0;
+    if (ok) {
+      if (C::HAS_DV) {
+        if (wg == 0) store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok);
+        else store_row128<T>(tmem + lane_off + 384, p.grad1, (int64_t)bi * p.g1_bs + krow * p.g1_cols, p.acc, kok);
+      } else {
+        store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok, 2 * wg,
+                        2 * wg + 2);
+      }
+    }
   }
 
   tc_fence_before();
@@ -544,18 +850,20 @@ template <typename T>
 cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaStream_t st) {
   const bool bf16 = Elem<T>::is_bf16;
   const int xa = vk ? (dv - 128) / 64 : dv / 64;  // value atoms beyond K (vk) or V atoms
-  // ---- dK / dV
+  const void* xsrc = vk ? b.v2 : b.v;
+  const int64_t xbs = vk ? b.v2_bs : b.v_bs;
+  // ---- dK / dV: 128-query tiles, except the last VMonarch R step (dO 256 wide) on 64-query tiles
+  const bool dkdv64 = vk && xa > 0;
+  const int qrows = dkdv64 ? 64 : 128;
   Sm100BwdParams pa{};
   if (!tma::make_map(&pa.tm_a, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
-    const void* xsrc = vk ? b.v2 : b.v;
-    const int64_t xbs = vk ? b.v2_bs : b.v_bs;
     if (!tma::make_map(&pa.tm_b, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 128)) return cudaErrorInvalidValue;
   } else {
     pa.tm_b = pa.tm_a;
   }
-  if (!tma::make_map(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.q_bs, 64)) return cudaErrorInvalidValue;
-  if (!tma::make_map(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.do_bs, 64)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.q_bs, qrows)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.do_bs, qrows)) return cudaErrorInvalidValue;
   pa.lse = b.lse;
   pa.cc = b.cc;
   pa.gg = b.gg;
@@ -572,26 +880,26 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.sm_scale = b.sm_scale;
   cudaError_t e;
   const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
-  if (vk && xa == 0) {
-    e = run(fea_bwd_dkdv_kernel<T, 0, true, 4>, DkdvCfg<0, true, 4>::SMEM, blocks_a, kThreads, pa, st);
-  } else if (vk) {
+  if (dkdv64) {
     e = run(fea_bwd_dkdv_kernel<T, 2, true, 3>, DkdvCfg<2, true, 3>::SMEM, blocks_a, kThreads, pa, st);
+  } else if (vk) {
+    e = run(fea_bwd_dkdv128_kernel<T, 0, true, 2>, DkdvCfg2<0, true, 2>::SMEM, blocks_a, kThreads, pa, st);
   } else {
-    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4>, DkdvCfg<2, false, 4>::SMEM, blocks_a, kThreads, pa, st);
+    e = run(fea_bwd_dkdv128_kernel<T, 2, false, 2>, DkdvCfg2<2, false, 2>::SMEM, blocks_a, kThreads, pa, st);
   }
   if (e != cudaSuccess) return e;
-  // ---- dQ
+  // ---- dQ: 128-key tiles (dO staged in TMEM when it is 256 wide)
   Sm100BwdParams pb{};
   if (!tma::make_map(&pb.tm_a, b.q, bf16, 128, b.n_q, batch, b.q_bs, 128)) return cudaErrorInvalidValue;
   if (!tma::make_map(&pb.tm_b, b.dout, bf16, dv, b.n_q, batch, b.do_bs, 128)) return cudaErrorInvalidValue;
-  if (!tma::make_map(&pb.tm_c, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 64)) return cudaErrorInvalidValue;
+  if (!tma::make_map(&pb.tm_c, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
-    const void* xsrc = vk ? b.v2 : b.v;
-    const int64_t xbs = vk ? b.v2_bs : b.v_bs;
-    if (!tma::make_map(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 64)) return cudaErrorInvalidValue;
+    if (!tma::make_map(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 128)) return cudaErrorInvalidValue;
   } else {
     pb.tm_d = pb.tm_c;
   }
+  pb.dout = b.dout;
+  pb.do_bs = b.do_bs;
   pb.lse = b.lse;
   pb.cc = b.cc;
   pb.gg = b.gg;
@@ -604,9 +912,14 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pb.scale_log2 = b.scale_log2;
   pb.sm_scale = b.sm_scale;
   const int64_t blocks_b = (int64_t)pb.n_tiles * batch;
-  if (vk && xa == 0) return run(fea_bwd_dq_kernel<T, 0, true, 6>, DqCfg<0, true, 6>::SMEM, blocks_b, kThreadsDq, pb, st);
-  if (vk) return run(fea_bwd_dq_kernel<T, 2, true, 3>, DqCfg<2, true, 3>::SMEM, blocks_b, kThreadsDq, pb, st);
-  return run(fea_bwd_dq_kernel<T, 2, false, 4>, DqCfg<2, false, 4>::SMEM, blocks_b, kThreadsDq, pb, st);
+  if (vk && xa == 0)
+    return run(fea_bwd_dq128_kernel<T, 0, true, false, 5, 0>, DqCfg2<0, true, false, 5, 0>::SMEM, blocks_b, kThreads,
+               pb, st);
+  if (vk)
+    return run(fea_bwd_dq128_kernel<T, 2, true, true, 3, 3>, DqCfg2<2, true, true, 3, 3>::SMEM, blocks_b, kThreads,
+               pb, st);
+  return run(fea_bwd_dq128_kernel<T, 2, false, false, 3, 2>, DqCfg2<2, false, false, 3, 2>::SMEM, blocks_b, kThreads,
+             pb, st);
 }
 
 }  // namespace
