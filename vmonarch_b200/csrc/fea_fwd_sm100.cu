@@ -5,8 +5,9 @@
 //
 // CTA = one 128-row query tile of one sequence; 6 warps:
 //   warp 0   TMA producer (Q once, then K / V tiles into an NSLOT-deep ring) + TMEM allocator
-//   warp 1   MMA issuer (one thread): S = Q K^T into a double-buffered TMEM S, O += P V with P
-//            read from TMEM (the bf16 probabilities are written over the first 64 columns of S)
+//   warp 1   MMA issuer (one elected lane of the converged warp): S = Q K^T into a double-buffered
+//            TMEM S, O += P V with P read from TMEM (the bf16 probabilities are written over the
+//            first 64 columns of S)
 //   warps 2-5 softmax + epilogue: thread = one query row = one TMEM lane; the whole 128-key row of
 //            S is in registers, so max / sum / entropy need no shuffles.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O [256, 256 + NV).
@@ -61,6 +62,54 @@ struct FwdCfg {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
+// Three-input max (sm_100: one instruction).
+__device__ __forceinline__ float fmax3(float a, float b, float c) {
+  float r;
+  asm("max.f32 %0, %1, %2, %3;" : "=f"(r) : "f"(a), "f"(b), "f"(c));
+  return r;
+}
+
+// Max of the raw scores of one 128-key row (keys >= valid ignored when MASK). The scale is applied
+// to the max afterwards, as the reference does (kernel.py:45: max(qk) * qk_scale). Four
+// independent chains of three-input maxima: with one softmax warp per scheduler a single long
+// chain is pure latency.
+template <bool MASK>
+__device__ __forceinline__ float row_max_raw(const uint32_t (&sr)[128], int valid) {
+  auto at = [&](int i) { return (MASK && i >= valid) ? -1e30f : __uint_as_float(sr[i]); };
+  float mr[4];
+#pragma unroll
+  for (int k = 0; k < 4; ++k) mr[k] = fmax3(at(3 * k), at(3 * k + 1), at(3 * k + 2));
+#pragma unroll
+  for (int i = 12; i < 128; i += 2) mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], at(i), at(i + 1));
+  return fmax3(fmaxf(mr[0], mr[1]), mr[2], mr[3]);
+}
+
+// p = 2^(s * scale - m) for one 128-key row, packed to the element type, with the row sum l and
+// the entropy sum h = sum p (x - m). Pairs of keys go through the packed f32x2 FMA / add (one
+// instruction per pair) into two chains each. Keys >= valid (MASK) get x - m = -1e30, so p = 0
+// and p (x - m) = 0 exactly.
+template <typename T, bool ENT, bool MASK>
+__device__ __forceinline__ void probs_row(const uint32_t (&sr)[128], uint32_t (&pk)[64], float sc, float m, int valid,
+                                          float& l, float& h) {
+  float2 la[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  float2 ha[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m, -m);
+#pragma unroll
+  for (int i = 0; i < 64; ++i) {
+    float2 d = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2);
+    if (MASK) {
+      if (2 * i >= valid) d.x = -1e30f;
+      if (2 * i + 1 >= valid) d.y = -1e30f;
+    }
+    const float2 pp = make_float2(fast_exp2(d.x), fast_exp2(d.y));
+    la[i & 1] = __fadd2_rn(la[i & 1], pp);
+    if (ENT) ha[i & 1] = __ffma2_rn(pp, d, ha[i & 1]);
+    pk[i] = Elem<T>::pack(pp.x, pp.y);
+  }
+  l += (la[0].x + la[0].y) + (la[1].x + la[1].y);
+  if (ENT) h += (ha[0].x + ha[0].y) + (ha[1].x + ha[1].y);
+}
+
 template <typename T, int XA, bool VK, int NSLOT, bool ENT>
 __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
   using C = FwdCfg<XA, VK, NSLOT>;
@@ -69,7 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
   constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, C::NV, false, true);
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[4 + 3 * NSLOT + 6];
+  __shared__ __align__(8) uint64_t bars[6 + 3 * NSLOT];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -88,8 +137,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
   auto BAR_EMPTY = [&](int s) { return bar0 + 8u * (1 + 2 * NSLOT + s); };
   auto BAR_SFULL = [&](int b) { return bar0 + 8u * (1 + 3 * NSLOT + b); };
   auto BAR_PFULL = [&](int b) { return bar0 + 8u * (3 + 3 * NSLOT + b); };
-  auto BAR_OBAR = [&](int b) { return bar0 + 8u * (5 + 3 * NSLOT + b); };
-  const uint32_t BAR_DONE = bar0 + 8u * (7 + 3 * NSLOT);
+  const uint32_t BAR_DONE = bar0 + 8u * (5 + 3 * NSLOT);
   volatile int* abort = &abort_sh;
 
   if (threadIdx.x == 0) {
@@ -103,7 +151,6 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SFULL(b), 1);
       mbar_init(BAR_PFULL(b), 128);
-      mbar_init(BAR_OBAR(b), 1);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -152,12 +199,18 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     }
   } else if (warp == 1) {
     // ------------------------------------------------------------------ MMA issuer
-    if (lane == 0) {
-      bool ok = mbar_wait(BAR_Q, 0, abort, &g_fwd_err, 2);
-      auto issue_s = [&](int j) -> bool {
-        const int s = j % NSLOT;
-        if (!mbar_wait(BAR_KFULL(s), (j / NSLOT) & 1, abort, &g_fwd_err, 2)) return false;
-        tc_fence_after();
+    // The whole warp walks the schedule (waits are made warp-uniform); one elected lane (always the
+    // same one, so its commits track all MMAs) issues. Two commits per KV tile: S -> SFULL, and
+    // P V -> EMPTY(slot), which both frees the ring slot and tells the softmax warps that O is done.
+    auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
+    };
+    bool ok = wwait(BAR_Q, 0, 2);
+    auto issue_s = [&](int j) -> bool {
+      const int s = j % NSLOT;
+      if (!wwait(BAR_KFULL(s), (j / NSLOT) & 1, 2)) return false;
+      tc_fence_after();
+      if (elect_one()) {
         const uint32_t kb = sRing + s * C::SLOT;
         const uint32_t d = tmem + (uint32_t)((j & 1) * 128);
 #pragma unroll
@@ -166,15 +219,18 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
           mma_ss(d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
         }
         mma_commit(BAR_SFULL(j & 1));
-        return true;
-      };
-      if (ok) ok = issue_s(0);
-      if (ok && n_kt > 1) ok = issue_s(1);
-      for (int j = 0; ok && j < n_kt; ++j) {
-        const int s = j % NSLOT;
-        if (!mbar_wait(BAR_PFULL(j & 1), (j >> 1) & 1, abort, &g_fwd_err, 4)) break;
-        if (XA > 0 && !mbar_wait(BAR_VFULL(s), (j / NSLOT) & 1, abort, &g_fwd_err, 4)) break;
-        tc_fence_after();
+      }
+      __syncwarp();
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    if (ok && n_kt > 1) ok = issue_s(1);
+    for (int j = 0; ok && j < n_kt; ++j) {
+      const int s = j % NSLOT;
+      if (!wwait(BAR_PFULL(j & 1), (j >> 1) & 1, 4)) break;
+      if (XA > 0 && !wwait(BAR_VFULL(s), (j / NSLOT) & 1, 4)) break;
+      tc_fence_after();
+      if (elect_one()) {
         const uint32_t vb = sRing + s * C::SLOT + C::PV_OFF;
         const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
 #pragma unroll
@@ -182,13 +238,16 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
           mma_ts(tmem + 256, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
                  (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit(BAR_EMPTY(s));
-        mma_commit(BAR_OBAR(j & 1));
-        if (j + 2 < n_kt) ok = issue_s(j + 2);
       }
-      // drain: all issued MMAs complete before TMEM can be freed
+      __syncwarp();
+      if (j + 2 < n_kt) ok = issue_s(j + 2);
+    }
+    // drain: all issued MMAs complete before TMEM can be freed
+    if (elect_one()) {
       mma_commit(BAR_DONE);
       mbar_wait_drain(BAR_DONE, 0);
     }
+    __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
@@ -203,11 +262,13 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       const bool mine = mbar_wait(bar, parity, abort, &g_fwd_err, code);
       return __all_sync(0xffffffffu, mine);
     };
-    // PV[t] is committed to OBAR[t & 1]; waiting in order keeps each barrier at most one phase ahead
+    // PV[t] is committed to EMPTY[t % NSLOT]. Waiting for every t in order keeps the wait at most
+    // one phase behind: PV[t + NSLOT] needs P[t + NSLOT - 1], which this warpgroup has not written
+    // when it waits for PV[t] (t <= j - 1 while it works on tile j).
     auto wait_pv = [&](int t) -> bool {
       while (pv_waited < t) {
         const int u = pv_waited + 1;
-        if (!warp_wait(BAR_OBAR(u & 1), (u >> 1) & 1, 8)) return false;
+        if (!warp_wait(BAR_EMPTY(u % NSLOT), (u / NSLOT) & 1, 8)) return false;
         pv_waited = u;
       }
       return true;
@@ -225,16 +286,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       tmem_ld32(tS + 64, sr + 64);
       tmem_ld32(tS + 96, sr + 96);
       tmem_wait_ld();
-      float x[128];
-      const int valid = p.n_kv - j * 128;
-      float mx = -1e30f;
-#pragma unroll
-      for (int i = 0; i < 128; ++i) {
-        float v = __uint_as_float(sr[i]) * p.scale_log2;
-        if (valid < 128 && i >= valid) v = -1e30f;
-        x[i] = v;
-        mx = fmaxf(mx, v);
-      }
+      const int valid = p.n_kv - j * 128;  // same for every thread: the branches below are uniform
+      const float mx = (valid < 128 ? row_max_raw<true>(sr, valid) : row_max_raw<false>(sr, 128)) * p.scale_log2;
       if (j == 0) {
         m_ref = mx;
       } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
@@ -259,18 +312,9 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         l *= alpha;
         m_ref = m_new;
       }
-      float ls = 0.f, hs = 0.f;
       uint32_t pk[64];
-#pragma unroll
-      for (int i = 0; i < 64; ++i) {
-        const float d0 = x[2 * i] - m_ref, d1 = x[2 * i + 1] - m_ref;
-        const float p0 = fast_exp2(d0), p1 = fast_exp2(d1);
-        ls += p0 + p1;
-        if (ENT) hs = fmaf(p0, d0, fmaf(p1, d1, hs));
-        pk[i] = Elem<T>::pack(p0, p1);
-      }
-      l += ls;
-      h += hs;
+      if (valid < 128) probs_row<T, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, l, h);
+      else probs_row<T, ENT, false>(sr, pk, p.scale_log2, m_ref, 128, l, h);
       tmem_st32(tS + 0, pk);
       tmem_st32(tS + 32, pk + 32);
       tmem_wait_st();
