@@ -209,6 +209,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     // TMEM buffer b = query tile parity: S^T [128b, 128b+64), dP^T [128b+64, 128b+128); P^T and
     // dS^T (bf16) are written over the first 32 columns of S^T / dP^T. dK [256,384), dV [384,512).
     // The whole warp walks the schedule with warp-uniform waits; one elected lane issues.
+    const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
     auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_bwd_err, code));
     };
@@ -218,23 +219,22 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
         const int s = i % NQS;
         if (!wwait(BAR_QFULL(s), (i / NQS) & 1, 2)) return false;
         tc_fence_after();
-        if (elect_one()) {
+        {
           const uint32_t tb = tmem + 128 * (i & 1);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
             const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-            mma_ss(tb, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024), IDESC_SP,
+            mma_ss_if(leader, tb, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024), IDESC_SP,
                    kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
             const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-            mma_ss(tb + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
+            mma_ss_if(leader, tb + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
                    IDESC_SP, kk > 0);
           }
-          mma_commit(BAR_SPFULL(i & 1));
+          mma_commit_if(leader, BAR_SPFULL(i & 1));
         }
-        __syncwarp();
         return true;
       };
       if (ok) ok = issue_sp(0);
@@ -243,27 +243,26 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
         if (!wwait(BAR_PDSFULL(i & 1), (i >> 1) & 1, 4)) break;
         tc_fence_after();
         const int s = i % NQS;
-        if (elect_one()) {
+        {
           const uint32_t pt = tmem + 128 * (i & 1), dst = pt + 64;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // dK += dS^T Q   (K = 64 queries)
-            mma_ts(tmem + 256, dst + kk * 8, smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
+            mma_ts_if(leader, tmem + 256, dst + kk * 8, smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
                    (i > 0 || kk > 0) ? 1u : 0u);
           if (VK) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dK += P^T dO[:, :128]  (value gradient of the K columns)
-              mma_ts(tmem + 256, pt + kk * 8, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
+              mma_ts_if(leader, tmem + 256, pt + kk * 8, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
           }
           if (C::HAS_DV) {
             const uint32_t vo = VK ? 2 * kAtom64 : 0;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dV += P^T dO[:, cols]
-              mma_ts(tmem + 384, pt + kk * 8, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
+              mma_ts_if(leader, tmem + 384, pt + kk * 8, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
                      (i > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(BAR_QEMPTY(s));
+          mma_commit_if(leader, BAR_QEMPTY(s));
         }
-        __syncwarp();
         // the next S^T / dP^T of this buffer is issued after the MMAs that read its P^T / dS^T
         if (i + 2 < nq) ok = issue_sp(i + 2);
       }
@@ -472,6 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp walks the schedule with warp-uniform waits; one elected lane issues.
+    const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
     auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_bwd_err, code));
     };
@@ -482,17 +482,16 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
         const int s = j % NK;
         if (!wwait(BAR(B_KFULL + s), (j / NK) & 1, 32)) return false;
         tc_fence_after();
-        if (elect_one()) {
+        {
           const uint32_t kb = sK + s * C::KSLOT;
           const uint32_t d = tmem + 128u * (uint32_t)(j % NS);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
-            mma_ss(d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
+            mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
           }
-          mma_commit(BAR(B_SFULL + j % NS));
+          mma_commit_if(leader, BAR(B_SFULL + j % NS));
         }
-        __syncwarp();
         return true;
       };
       auto issue_dp = [&](int j) -> bool {
@@ -500,7 +499,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
         if (VK && !wwait(BAR(B_KFULL + s), (j / NK) & 1, 32)) return false;
         if (XA > 0 && !wwait(BAR(B_XFULL + x), (j / NXB) & 1, 32)) return false;
         tc_fence_after();
-        if (elect_one()) {
+        {
           const uint32_t kb = sK + s * C::KSLOT, xb = sX + x * C::XSLOT;
 #pragma unroll
           for (int kk = 0; kk < C::DW / 16; ++kk) {
@@ -510,15 +509,14 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
             else boff = xb + (kk >> 2) * kAtom128 + (kk & 3) * 32;
             const uint64_t bd = smem_desc_sw128(boff, 16, 1024);
             if (DOT)
-              mma_ts(tmem + T_DP, tmem + T_DO + kk * 8, bd, IDESC_S, kk > 0);
+              mma_ts_if(leader, tmem + T_DP, tmem + T_DO + kk * 8, bd, IDESC_S, kk > 0);
             else
-              mma_ss(tmem + T_DP, smem_desc_sw128(sDO + (kk >> 2) * kAtom128 + (kk & 3) * 32, 16, 1024), bd, IDESC_S,
+              mma_ss_if(leader, tmem + T_DP, smem_desc_sw128(sDO + (kk >> 2) * kAtom128 + (kk & 3) * 32, 16, 1024), bd, IDESC_S,
                      kk > 0);
           }
-          mma_commit(BAR(B_DPFULL));
-          if (XA > 0) mma_commit(BAR(B_XEMPTY + x));
+          mma_commit_if(leader, BAR(B_DPFULL));
+          if (XA > 0) mma_commit_if(leader, BAR(B_XEMPTY + x));
         }
-        __syncwarp();
         return true;
       };
       if (ok) ok = issue_s(0);
@@ -531,18 +529,17 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
         }
         if (!wwait(BAR(B_DSFULL + j % NS), (j / NS) & 1, 64)) break;
         tc_fence_after();
-        if (elect_one()) {
+        {
           const uint32_t kb = sK + (j % NK) * C::KSLOT;
           const uint32_t sb = tmem + 128u * (uint32_t)(j % NS);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K ; keys [16kk, 16kk+16) of warpgroup kk/4
             const uint32_t a_tm = sb + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
-            mma_ts(tmem + T_DQ, a_tm, smem_desc_sw128(kb + kk * 2048, kAtom128, 1024), IDESC_DQ,
+            mma_ts_if(leader, tmem + T_DQ, a_tm, smem_desc_sw128(kb + kk * 2048, kAtom128, 1024), IDESC_DQ,
                    (j > 0 || kk > 0) ? 1u : 0u);
           }
-          mma_commit(BAR(B_KEMPTY + j % NK));
+          mma_commit_if(leader, BAR(B_KEMPTY + j % NK));
         }
-        __syncwarp();
         const int nxt = j + NS;  // the next tile that uses this S buffer
         if (nxt < nk) ok = issue_s(nxt);
       }
@@ -749,6 +746,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv128_kernel(const __gr
   } else if (warp == 1) {
     // ---------------------------------------------------------------- MMA issuer
     // The whole warp walks the schedule with warp-uniform waits; one elected lane issues.
+    const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
     auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_bwd_err, code));
     };
@@ -758,22 +756,21 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv128_kernel(const __gr
         const int s = i % NQS;
         if (!wwait(BAR(B_QFULL + s), (i / NQS) & 1, 2)) return false;
         tc_fence_after();
-        if (elect_one()) {
+        {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
             const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
-            mma_ss(tmem, smem_desc_sw128(sRes + off, 16, 1024), smem_desc_sw128(slot_q(s) + off, 16, 1024), IDESC_SP,
+            mma_ss_if(leader, tmem, smem_desc_sw128(sRes + off, 16, 1024), smem_desc_sw128(slot_q(s) + off, 16, 1024), IDESC_SP,
                    kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
             const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
-            mma_ss(tmem + 128, smem_desc_sw128(sW + off, 16, 1024), smem_desc_sw128(slot_do(s) + off, 16, 1024),
+            mma_ss_if(leader, tmem + 128, smem_desc_sw128(sW + off, 16, 1024), smem_desc_sw128(slot_do(s) + off, 16, 1024),
                    IDESC_SP, kk > 0);
           }
-          mma_commit(BAR(B_SPFULL));
+          mma_commit_if(leader, BAR(B_SPFULL));
         }
-        __syncwarp();
         return true;
       };
       if (ok) ok = issue_sp(0);
@@ -781,23 +778,22 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv128_kernel(const __gr
         if (!wwait(BAR(B_PDSFULL), i & 1, 4)) break;
         tc_fence_after();
         const int s = i % NQS;
-        if (elect_one()) {
+        {
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // queries [16kk, 16kk+16) live in warpgroup kk/4's columns
             const uint32_t col = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
             const uint64_t bq = smem_desc_sw128(slot_q(s) + kk * 2048, kAtom128, 1024);
-            mma_ts(tmem + 256, tmem + 128 + col, bq, IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);  // dK += dS^T Q
+            mma_ts_if(leader, tmem + 256, tmem + 128 + col, bq, IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);  // dK += dS^T Q
             if (VK)
-              mma_ts(tmem + 256, tmem + col, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom128, 1024), IDESC_ACC, 1u);
+              mma_ts_if(leader, tmem + 256, tmem + col, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom128, 1024), IDESC_ACC, 1u);
             if (C::HAS_DV) {
               const uint32_t vo = VK ? 2 * kAtom128 : 0;
-              mma_ts(tmem + 384, tmem + col, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom128, 1024), IDESC_ACC,
+              mma_ts_if(leader, tmem + 384, tmem + col, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom128, 1024), IDESC_ACC,
                      (i > 0 || kk > 0) ? 1u : 0u);
             }
           }
-          mma_commit(BAR(B_QEMPTY + s));
+          mma_commit_if(leader, BAR(B_QEMPTY + s));
         }
-        __syncwarp();
         if (i + 1 < nq) ok = issue_sp(i + 1);  // queued behind the MMAs that read P^T / dS^T
       }
       if (elect_one()) {

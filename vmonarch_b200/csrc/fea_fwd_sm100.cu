@@ -3,13 +3,13 @@
 // Reference semantics: video_monarch_attention/kernel.py:32-151 (online softmax with the running
 // entropy accumulator h = sum p (x - m), E = (log2 l - h / l) ln 2, LSE2 = m + log2 l).
 //
-// CTA = one 128-row query tile of one sequence; 6 warps:
+// CTA = one 128-row query tile of one sequence; 10 warps:
 //   warp 0   TMA producer (Q once, then K / V tiles into an NSLOT-deep ring) + TMEM allocator
 //   warp 1   MMA issuer (one elected lane of the converged warp): S = Q K^T into a double-buffered
 //            TMEM S, O += P V with P read from TMEM (the bf16 probabilities are written over the
 //            first 64 columns of S)
-//   warps 2-5 softmax + epilogue: thread = one query row = one TMEM lane; the whole 128-key row of
-//            S is in registers, so max / sum / entropy need no shuffles.
+//   warps 2-9 softmax + epilogue, two warpgroups: thread = one query row (TMEM lane) x one half
+//            (64 keys) of each 128-key tile; the half-row maxima are exchanged once per tile.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O [256, 256 + NV).
 // The max is rescaled lazily: O, l and h keep a stale reference max m_ref until a tile's max
 // exceeds it by more than 8 (p <= 256), the only point where O is read back and rescaled. The
@@ -39,7 +39,7 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 192;
+constexpr int kThreads = 320;
 constexpr int kAtom = 128 * 128;  // bytes of one swizzle atom column block: 128 rows x 128 B
 constexpr float kRescaleThreshold = 8.0f;
 
@@ -69,33 +69,32 @@ __device__ __forceinline__ float fmax3(float a, float b, float c) {
   return r;
 }
 
-// Max of the raw scores of one 128-key row (keys >= valid ignored when MASK). The scale is applied
-// to the max afterwards, as the reference does (kernel.py:45: max(qk) * qk_scale). Four
-// independent chains of three-input maxima: with one softmax warp per scheduler a single long
-// chain is pure latency.
-template <bool MASK>
-__device__ __forceinline__ float row_max_raw(const uint32_t (&sr)[128], int valid) {
+// Max of the raw scores of one row segment of N keys (keys >= valid ignored when MASK). The scale
+// is applied to the max afterwards, as the reference does (kernel.py:45: max(qk) * qk_scale).
+// Four independent chains of three-input maxima.
+template <int N, bool MASK>
+__device__ __forceinline__ float row_max_raw(const uint32_t (&sr)[N], int valid) {
   auto at = [&](int i) { return (MASK && i >= valid) ? -1e30f : __uint_as_float(sr[i]); };
   float mr[4];
 #pragma unroll
   for (int k = 0; k < 4; ++k) mr[k] = fmax3(at(3 * k), at(3 * k + 1), at(3 * k + 2));
 #pragma unroll
-  for (int i = 12; i < 128; i += 2) mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], at(i), at(i + 1));
+  for (int i = 12; i < N; i += 2) mr[(i >> 1) & 3] = fmax3(mr[(i >> 1) & 3], at(i), at(i + 1));
   return fmax3(fmaxf(mr[0], mr[1]), mr[2], mr[3]);
 }
 
-// p = 2^(s * scale - m) for one 128-key row, packed to the element type, with the row sum l and
-// the entropy sum h = sum p (x - m). Pairs of keys go through the packed f32x2 FMA / add (one
-// instruction per pair) into two chains each. Keys >= valid (MASK) get x - m = -1e30, so p = 0
-// and p (x - m) = 0 exactly.
-template <typename T, bool ENT, bool MASK>
-__device__ __forceinline__ void probs_row(const uint32_t (&sr)[128], uint32_t (&pk)[64], float sc, float m, int valid,
-                                          float& l, float& h) {
+// p = 2^(s * scale - m) for one row segment of N keys, packed to the element type, with the row
+// sum l and the entropy sum h = sum p (x - m). Pairs of keys go through the packed f32x2 FMA / add
+// (one instruction per pair) into two chains each. Keys >= valid (MASK) get x - m = -1e30, so
+// p = 0 and p (x - m) = 0 exactly.
+template <typename T, int N, bool ENT, bool MASK>
+__device__ __forceinline__ void probs_row(const uint32_t (&sr)[N], uint32_t (&pk)[N / 2], float sc, float m,
+                                          int valid, float& l, float& h) {
   float2 la[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float2 ha[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m, -m);
 #pragma unroll
-  for (int i = 0; i < 64; ++i) {
+  for (int i = 0; i < N / 2; ++i) {
     float2 d = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2);
     if (MASK) {
       if (2 * i >= valid) d.x = -1e30f;
@@ -150,7 +149,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SFULL(b), 1);
-      mbar_init(BAR_PFULL(b), 128);
+      mbar_init(BAR_PFULL(b), 256);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -202,6 +201,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     // The whole warp walks the schedule (waits are made warp-uniform); one elected lane (always the
     // same one, so its commits track all MMAs) issues. Two commits per KV tile: S -> SFULL, and
     // P V -> EMPTY(slot), which both frees the ring slot and tells the softmax warps that O is done.
+    const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
     auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
     };
@@ -210,17 +210,16 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       const int s = j % NSLOT;
       if (!wwait(BAR_KFULL(s), (j / NSLOT) & 1, 2)) return false;
       tc_fence_after();
-      if (elect_one()) {
+      {
         const uint32_t kb = sRing + s * C::SLOT;
         const uint32_t d = tmem + (uint32_t)((j & 1) * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          mma_ss(d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
+          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
         }
-        mma_commit(BAR_SFULL(j & 1));
+        mma_commit_if(leader, BAR_SFULL(j & 1));
       }
-      __syncwarp();
       return true;
     };
     if (ok) ok = issue_s(0);
@@ -230,16 +229,15 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       if (!wwait(BAR_PFULL(j & 1), (j >> 1) & 1, 4)) break;
       if (XA > 0 && !wwait(BAR_VFULL(s), (j / NSLOT) & 1, 4)) break;
       tc_fence_after();
-      if (elect_one()) {
+      {
         const uint32_t vb = sRing + s * C::SLOT + C::PV_OFF;
         const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ts(tmem + 256, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
+          mma_ts_if(leader, tmem + 256, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
                  (j > 0 || kk > 0) ? 1u : 0u);
-        mma_commit(BAR_EMPTY(s));
+        mma_commit_if(leader, BAR_EMPTY(s));
       }
-      __syncwarp();
       if (j + 2 < n_kt) ok = issue_s(j + 2);
     }
     // drain: all issued MMAs complete before TMEM can be freed
@@ -250,10 +248,22 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
+    // Two warpgroups split every 128-key tile by columns: warpgroup wg owns keys [64 wg, 64 wg + 64)
+    // of each row and O columns [wg NV/2, (wg + 1) NV/2). They exchange the half-row maxima once
+    // per tile through TMEM (named barrier 1), so both hold the same m_ref and take identical
+    // rescale decisions; l and h are per-warpgroup partial sums, added in the epilogue. Every named
+    // barrier is reached by all 256 threads and ANDs their status, so a failed wait in one
+    // warpgroup ends both at the same point.
+    // Exchange columns of the S buffer: warpgroup 0 writes its maximum into column 32 (its own half,
+    // already loaded; overwritten only by warpgroup 1's P after warpgroup 1 has read it), warpgroup
+    // 1 into column 64 (its own half; nothing writes it before the next S MMA into this buffer,
+    // which waits for both warpgroups' P).
+    const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const uint32_t tO = tmem + lane_off + 256;
+    constexpr int OCH = C::NV / 64;  // 32-column O chunks per warpgroup
     float m_ref = -1e30f, l = 0.f, h = 0.f;
     int pv_waited = -1;
     bool ok = true;
@@ -263,8 +273,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       return __all_sync(0xffffffffu, mine);
     };
     // PV[t] is committed to EMPTY[t % NSLOT]. Waiting for every t in order keeps the wait at most
-    // one phase behind: PV[t + NSLOT] needs P[t + NSLOT - 1], which this warpgroup has not written
-    // when it waits for PV[t] (t <= j - 1 while it works on tile j).
+    // one phase behind: PV[t + NSLOT] needs P[t + NSLOT], which is not written while this
+    // warpgroup waits for PV[t] (t <= j - 1 while it works on tile j).
     auto wait_pv = [&](int t) -> bool {
       while (pv_waited < t) {
         const int u = pv_waited + 1;
@@ -275,31 +285,44 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     };
 
     for (int j = 0; j < n_kt; ++j) {
-      if (!warp_wait(BAR_SFULL(j & 1), (j >> 1) & 1, 8)) { ok = false; break; }
+      bool good = ok && warp_wait(BAR_SFULL(j & 1), (j >> 1) & 1, 8);
       tc_fence_after();
       // S[j] complete implies PV[j-2] complete: consume that phase to keep the bookkeeping exact
-      if (j >= 2 && !wait_pv(j - 2)) { ok = false; break; }
+      if (good && j >= 2) good = wait_pv(j - 2);
       const uint32_t tS = tmem + lane_off + (uint32_t)((j & 1) * 128);
-      uint32_t sr[128];
-      tmem_ld32(tS + 0, sr);
-      tmem_ld32(tS + 32, sr + 32);
-      tmem_ld32(tS + 64, sr + 64);
-      tmem_ld32(tS + 96, sr + 96);
+      uint32_t sr[64];
+      const int valid = p.n_kv - j * 128 - wg * 64;  // keys of this half; uniform per warpgroup
+      float mh = -1e30f;
+      if (good) {
+        tmem_ld32(tS + wg * 64, sr);
+        tmem_ld32(tS + wg * 64 + 32, sr + 32);
+        tmem_wait_ld();
+        mh = valid < 64 ? row_max_raw<64, true>(sr, valid) : row_max_raw<64, false>(sr, 64);
+      }
+      if (good) {
+        tmem_st1(tS + (wg ? 64 : 32), __float_as_uint(mh));
+        tmem_wait_st();
+      }
+      tc_fence_before();
+      // both halves of S are in registers past this barrier, so P may overwrite S columns [0, 64)
+      if (!named_bar_and(1, 256, good)) { ok = false; break; }
+      tc_fence_after();
+      const float mo = __uint_as_float(tmem_ld1(tS + (wg ? 32 : 64)));
       tmem_wait_ld();
-      const int valid = p.n_kv - j * 128;  // same for every thread: the branches below are uniform
-      const float mx = (valid < 128 ? row_max_raw<true>(sr, valid) : row_max_raw<false>(sr, 128)) * p.scale_log2;
+      const float mx = fmaxf(mh, mo) * p.scale_log2;
       if (j == 0) {
         m_ref = mx;
       } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
         // The rescale touches TMEM with warp-collective loads / stores and waits on a barrier, so
         // the decision is taken per warp: every lane whose max grew adopts it (alpha < 1), the
-        // others keep their reference (alpha = 1).
-        if (!wait_pv(j - 1)) { ok = false; break; }
+        // others keep their reference (alpha = 1). The twin warp of the other warpgroup sees the
+        // same maxima and takes the same decision.
+        if (!wait_pv(j - 1)) ok = false;  // reported to the other warpgroup at the next barrier
         tc_fence_after();
         const float m_new = fmaxf(m_ref, mx);
         const float alpha = fast_exp2(m_ref - m_new);
 #pragma unroll 1
-        for (int c = 0; c < C::NV / 32; ++c) {
+        for (int c = wg * OCH; c < (wg + 1) * OCH; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_wait_ld();
@@ -312,11 +335,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         l *= alpha;
         m_ref = m_new;
       }
-      uint32_t pk[64];
-      if (valid < 128) probs_row<T, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, l, h);
-      else probs_row<T, ENT, false>(sr, pk, p.scale_log2, m_ref, 128, l, h);
-      tmem_st32(tS + 0, pk);
-      tmem_st32(tS + 32, pk + 32);
+      uint32_t pk[32];
+      if (valid < 64) probs_row<T, 64, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, l, h);
+      else probs_row<T, 64, ENT, false>(sr, pk, p.scale_log2, m_ref, 64, l, h);
+      tmem_st32(tS + wg * 32, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR_PFULL(j & 1));
@@ -324,12 +346,20 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 
     if (ok) ok = wait_pv(n_kt - 1);
     tc_fence_after();
-    // epilogue: O / l -> bf16 in the (now idle) ring, TMA store; LSE and entropy per row
+    // epilogue: add the partial sums (exchanged through the Q tile, idle once the last P V - and
+    // with it every S MMA - has completed), O / l -> bf16 in the (now idle) ring, TMA store; LSE
+    // and entropy per row
+    float* xch = reinterpret_cast<float*>(smem_raw + (sQ - smem_u32(smem_raw)));
+    xch[(2 * wg) * 128 + row] = l;
+    xch[(2 * wg + 1) * 128 + row] = h;
+    ok = named_bar_and(2, 256, ok);
     const uint32_t stage = sRing;
     if (ok) {
+      l += xch[(2 * (wg ^ 1)) * 128 + row];
+      h += xch[(2 * (wg ^ 1) + 1) * 128 + row];
       const float inv = 1.f / l;
 #pragma unroll 1
-      for (int c = 0; c < C::NV / 32; ++c) {
+      for (int c = wg * OCH; c < (wg + 1) * OCH; ++c) {
         uint32_t o[32];
         tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
@@ -348,7 +378,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         }
       }
       const int grow = q0 + row;
-      if (grow < p.n_q) {
+      if (wg == 0 && grow < p.n_q) {
         const float lg = log2f(l);
         const int64_t idx = (int64_t)bi * p.n_q + grow;
         if (p.lse) p.lse[idx] = m_ref + lg;
@@ -356,9 +386,322 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       }
     }
     fence_proxy_async_smem();
-    named_bar_sync(1, 128);
-    if (warp == 2 && lane == 0 && !*abort) {
+    named_bar_sync(3, 256);
+    if (warp == 2 && lane == 0 && ok && !*abort) {
       for (int a = 0; a < C::NV / 64; ++a) tma_store_3d(&p.tm_o, 64 * a, q0, bi, stage + a * kAtom);
+      tma_store_commit_and_wait();
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// ---------------------------------------------------------------------------------- Dv = 128
+// Two-stream forward for 128 output columns. The two softmax warpgroups own alternate KV tiles
+// (stream w = tiles j with j % 2 == w), each with its own TMEM S buffer, O accumulator and online
+// statistics (m_ref, l, h), like two split-KV partitions inside one CTA; the epilogue merges them
+// exactly (O = a_0 O_0 + a_1 O_1, l and h likewise, a_w = 2^(m_w - m)). The streams never wait for
+// each other, so one warpgroup's exponentials (MUFU-bound) overlap the other's TMEM loads and maxima.
+// TMEM: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
+// One tcgen05.commit per tile (S -> SFULL): S[j+2] is issued after P V[j] into the same buffers and
+// the tensor pipe executes one thread's MMAs in order, so S[j+2] complete implies P V[j] complete.
+// So a rescale of O_w at tile j needs no wait beyond S[j], and the stream that observes S[j] frees
+// the ring slots that are done (one elected thread arrives on the slot's EMPTY barrier): the K slot
+// of tile j (K read by S[j] only) and the V slot of tile j - 2 (read by P V[j-2]); with V aliasing K
+// the K slot of tile j - 2. The producer waits on those per-slot barriers, whose next phase needs
+// a tile it has not loaded yet, so no parity wait can be lapped.
+template <bool VK>
+struct Fwd2Cfg {
+  static constexpr int NK = VK ? 6 : 3;   // K ring slots (V aliases K: the K slot is also the V operand)
+  static constexpr int NVS = VK ? 0 : 3;  // V ring slots
+  static constexpr int Q_BYTES = 2 * kAtom;
+  static constexpr int SMEM = 1024 + Q_BYTES + (NK + NVS) * 2 * kAtom;
+  static_assert(SMEM <= 232448 - 1024, "shared memory budget");
+};
+
+template <typename T, bool VK, bool ENT>
+__global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
+  using C = Fwd2Cfg<VK>;
+  constexpr int NK = C::NK, NVS = C::NVS;
+  constexpr bool kBf16 = Elem<T>::is_bf16;
+  constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, 128, false, true);
+
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[6 + 2 * (NK + NVS)];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bi = blockIdx.x / p.n_qtiles;
+  const int q0 = (blockIdx.x % p.n_qtiles) * 128;
+  const int n_kt = (p.n_kv + 127) / 128;
+
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  const uint32_t sQ = sbase;
+  const uint32_t sK = sbase + C::Q_BYTES;
+  const uint32_t sV = sK + NK * 2 * kAtom;
+  const uint32_t bar0 = smem_u32(bars);
+  const uint32_t BAR_Q = bar0;
+  auto BAR_KFULL = [&](int s) { return bar0 + 8u * (1 + s); };
+  auto BAR_VFULL = [&](int s) { return bar0 + 8u * (1 + NK + s); };
+  auto BAR_KEMPTY = [&](int s) { return bar0 + 8u * (1 + NK + NVS + s); };
+  auto BAR_VEMPTY = [&](int s) { return bar0 + 8u * (1 + 2 * NK + NVS + s); };
+  auto BAR_SFULL = [&](int b) { return bar0 + 8u * (1 + 2 * (NK + NVS) + b); };
+  auto BAR_PFULL = [&](int b) { return bar0 + 8u * (3 + 2 * (NK + NVS) + b); };
+  const uint32_t BAR_DONE = bar0 + 8u * (5 + 2 * (NK + NVS));
+  volatile int* abort = &abort_sh;
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    mbar_init(BAR_Q, 1);
+    for (int s = 0; s < NK; ++s) {
+      mbar_init(BAR_KFULL(s), 1);
+      mbar_init(BAR_KEMPTY(s), 1);
+    }
+    for (int s = 0; s < NVS; ++s) {
+      mbar_init(BAR_VFULL(s), 1);
+      mbar_init(BAR_VEMPTY(s), 1);
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(BAR_SFULL(b), 1);
+      mbar_init(BAR_PFULL(b), 128);
+    }
+    mbar_init(BAR_DONE, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_base_sh), 512);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------------ TMA producers
+    // lane 0: Q, then the K ring; lane 1 (separate V only): the V ring.
+    if (lane == 0 || (!VK && lane == 1)) {
+      const bool kl = lane == 0;
+      const int nslot = kl ? NK : NVS;
+      if (kl) {
+        prefetch_tmap(&p.tm_q);
+        prefetch_tmap(&p.tm_k);
+        mbar_expect_tx(BAR_Q, C::Q_BYTES);
+        tma_load_3d(sQ, &p.tm_q, 0, q0, bi, BAR_Q);
+        tma_load_3d(sQ + kAtom, &p.tm_q, 64, q0, bi, BAR_Q);
+      } else {
+        prefetch_tmap(&p.tm_x);
+      }
+      int armed[NK > NVS ? NK : NVS];
+      for (int s = 0; s < nslot; ++s) armed[s] = 0;
+      for (int j = 0; j < n_kt; ++j) {
+        const int s = j % nslot;
+        const uint32_t empty = kl ? BAR_KEMPTY(s) : BAR_VEMPTY(s);
+        if (j >= nslot && !mbar_wait(empty, ((j / nslot) - 1) & 1, abort, &g_fwd_err, 1)) break;
+        const uint32_t full = kl ? BAR_KFULL(s) : BAR_VFULL(s);
+        const uint32_t slot = (kl ? sK : sV) + s * 2 * kAtom;
+        mbar_expect_tx(full, 2 * kAtom);
+        tma_load_3d(slot, kl ? &p.tm_k : &p.tm_x, 0, j * 128, bi, full);
+        tma_load_3d(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, j * 128, bi, full);
+        armed[s] = j / nslot + 1;
+      }
+      // drain: every armed phase must have landed before the CTA may exit
+      if (kl) mbar_wait_drain(BAR_Q, 0);
+      for (int s = 0; s < nslot; ++s)
+        if (armed[s] > 0) mbar_wait_drain(kl ? BAR_KFULL(s) : BAR_VFULL(s), (armed[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    // ------------------------------------------------------------------ MMA issuer
+    const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
+    auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
+    };
+    bool ok = wwait(BAR_Q, 0, 2);
+    auto issue_s = [&](int j) -> bool {
+      const int s = j % NK;
+      if (!wwait(BAR_KFULL(s), (j / NK) & 1, 2)) return false;
+      tc_fence_after();
+      {
+        const uint32_t kb = sK + s * 2 * kAtom;
+        const uint32_t d = tmem + (uint32_t)((j & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk) {
+          const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
+        }
+        mma_commit_if(leader, BAR_SFULL(j & 1));
+      }
+      return true;
+    };
+    if (ok) ok = issue_s(0);
+    if (ok && n_kt > 1) ok = issue_s(1);
+    for (int j = 0; ok && j < n_kt; ++j) {
+      if (!wwait(BAR_PFULL(j & 1), (j >> 1) & 1, 4)) break;
+      if (!VK && !wwait(BAR_VFULL(j % NVS), (j / NVS) & 1, 4)) break;
+      tc_fence_after();
+      {
+        const uint32_t vb = VK ? sK + (j % NK) * 2 * kAtom : sV + (j % NVS) * 2 * kAtom;
+        const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
+        const uint32_t o_tm = tmem + 256 + (uint32_t)((j & 1) * 128);
+#pragma unroll
+        for (int kk = 0; kk < 8; ++kk)
+          mma_ts_if(leader, o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
+                 (j >= 2 || kk > 0) ? 1u : 0u);
+      }
+      if (j + 2 < n_kt) ok = issue_s(j + 2);
+    }
+    // DONE: every MMA complete (the epilogue reads O; TMEM may be freed)
+    if (elect_one()) {
+      mma_commit(BAR_DONE);
+      mbar_wait_drain(BAR_DONE, 0);
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------------ softmax streams + epilogue
+    const int w = (warp - 2) >> 2;  // stream: KV tiles j = w, w + 2, ...
+    const int quad = warp & 3;      // TMEM lane quadrant this warp may access
+    const int row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    const uint32_t tS = tmem + lane_off + (uint32_t)(w * 128);
+    float m_ref = -1e30f, l = 0.f, h = 0.f;
+    bool ok = true;
+    auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
+    };
+
+    for (int j = w; j < n_kt; j += 2) {
+      if (!warp_wait(BAR_SFULL(w), (j >> 1) & 1, 8)) { ok = false; break; }
+      tc_fence_after();
+      if (warp == 2 + 4 * w && lane == 0) {  // ring slots done with (see above)
+        if (VK) {
+          if (j >= 2) mbar_arrive(BAR_KEMPTY((j - 2) % NK));
+        } else {
+          mbar_arrive(BAR_KEMPTY(j % NK));
+          if (j >= 2) mbar_arrive(BAR_VEMPTY((j - 2) % NVS));
+        }
+      }
+      uint32_t sr[128];
+      tmem_ld32(tS + 0, sr);
+      tmem_ld32(tS + 32, sr + 32);
+      tmem_ld32(tS + 64, sr + 64);
+      tmem_ld32(tS + 96, sr + 96);
+      tmem_wait_ld();
+      const int valid = p.n_kv - j * 128;  // same for every thread: the branches below are uniform
+      const float mx =
+          (valid < 128 ? row_max_raw<128, true>(sr, valid) : row_max_raw<128, false>(sr, 128)) * p.scale_log2;
+      if (j == w) {
+        m_ref = mx;
+      } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+        // Warp-uniform decision (warp-collective TMEM access): lanes whose max grew adopt it. Every
+        // earlier P V into O_w has completed (S[j] complete, see above).
+        const float m_new = fmaxf(m_ref, mx);
+        const float alpha = fast_exp2(m_ref - m_new);
+        const uint32_t tO = tmem + lane_off + 256 + (uint32_t)(w * 128);
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_wait_ld();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+        tmem_wait_st();
+        if (ENT) h = alpha * fmaf(m_ref - m_new, l, h);
+        l *= alpha;
+        m_ref = m_new;
+      }
+      // P in two 64-key halves: keys [64 k, 64 k + 64) -> columns [32 k, 32 k + 32). The second half
+      // of S is loaded again from TMEM (its columns are only overwritten by the second half of P),
+      // so the scores of the first half are the only ones live through the exponentials.
+      {
+        const uint32_t(&sh)[64] = *reinterpret_cast<const uint32_t(*)[64]>(&sr[0]);
+        uint32_t pk[32];
+        if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid, l, h);
+        else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+        tmem_st32(tS + 0, pk);
+      }
+      {
+        uint32_t sh[64];
+        tmem_ld32(tS + 64, sh);
+        tmem_ld32(tS + 96, sh + 32);
+        tmem_wait_ld();
+        uint32_t pk[32];
+        if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
+        else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+        tmem_st32(tS + 32, pk);
+      }
+      tmem_wait_st();
+      tc_fence_before();
+      mbar_arrive(BAR_PFULL(w));
+    }
+
+    // epilogue: wait for every MMA, merge the two streams' (m, l, h, O) per row (exchanged
+    // through the Q tile, idle once every S MMA has completed), O / l -> bf16 in the idle K ring,
+    // TMA store; LSE and entropy per row
+    if (ok) ok = warp_wait(BAR_DONE, 0, 8);
+    tc_fence_after();
+    float* xch = reinterpret_cast<float*>(smem_raw + (sQ - smem_u32(smem_raw)));
+    xch[(3 * w + 0) * 128 + row] = m_ref;
+    xch[(3 * w + 1) * 128 + row] = l;
+    xch[(3 * w + 2) * 128 + row] = h;
+    ok = named_bar_and(1, 256, ok);
+    const uint32_t stage = sK;
+    if (ok) {
+      const float m0 = xch[0 * 128 + row], l0 = xch[1 * 128 + row], h0 = xch[2 * 128 + row];
+      const float m1 = xch[3 * 128 + row], l1 = xch[4 * 128 + row], h1 = xch[5 * 128 + row];
+      const bool two = n_kt > 1;  // stream 1 owns no tile (and O_1 was never written) otherwise
+      const float m = two ? fmaxf(m0, m1) : m0;
+      const float a0 = fast_exp2(m0 - m), a1 = two ? fast_exp2(m1 - m) : 0.f;
+      const float lt = a0 * l0 + a1 * l1;
+      const float ht = two ? a0 * fmaf(m0 - m, l0, h0) + a1 * fmaf(m1 - m, l1, h1) : h0;
+      const float inv = 1.f / lt;
+      const float c0 = a0 * inv, c1 = a1 * inv;
+      const uint32_t tO0 = tmem + lane_off + 256, tO1 = tO0 + 128;
+#pragma unroll 1
+      for (int c = 2 * w; c < 2 * w + 2; ++c) {  // this warpgroup's 64 output columns
+        uint32_t o0[32], o1[32];
+        tmem_ld32(tO0 + c * 32, o0);
+        if (two) tmem_ld32(tO1 + c * 32, o1);
+        tmem_wait_ld();
+        if (!two) {
+#pragma unroll
+          for (int i = 0; i < 32; ++i) o1[i] = 0u;
+        }
+        uint32_t wv[16];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) {
+          const float x0 = fmaf(__uint_as_float(o0[2 * i]), c0, __uint_as_float(o1[2 * i]) * c1);
+          const float x1 = fmaf(__uint_as_float(o0[2 * i + 1]), c0, __uint_as_float(o1[2 * i + 1]) * c1);
+          wv[i] = Elem<T>::pack(x0, x1);
+        }
+        const int atom = c >> 1;
+#pragma unroll
+        for (int k = 0; k < 4; ++k) {
+          const int chunk = (c & 1) * 4 + k;
+          const uint32_t dst = stage + atom * kAtom + row * 128 + ((chunk ^ (row & 7)) << 4);
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(dst), "r"(wv[4 * k]), "r"(wv[4 * k + 1]),
+                       "r"(wv[4 * k + 2]), "r"(wv[4 * k + 3])
+                       : "memory");
+        }
+      }
+      const int grow = q0 + row;
+      if (w == 0 && grow < p.n_q) {
+        const float lg = log2f(lt);
+        const int64_t idx = (int64_t)bi * p.n_q + grow;
+        if (p.lse) p.lse[idx] = m + lg;
+        if (ENT && p.ent) p.ent[idx] = (lg - ht / lt) * kLn2;
+      }
+    }
+    fence_proxy_async_smem();
+    named_bar_sync(2, 256);
+    if (warp == 2 && lane == 0 && ok && !*abort) {
+      for (int a = 0; a < 2; ++a) tma_store_3d(&p.tm_o, 64 * a, q0, bi, stage + a * kAtom);
       tma_store_commit_and_wait();
     }
   }
@@ -382,13 +725,25 @@ cudaError_t launch(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   return cudaGetLastError();
 }
 
+template <typename T, bool VK, bool ENT>
+cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
+  using C = Fwd2Cfg<VK>;
+  auto kern = fea_fwd2_sm100_kernel<T, VK, ENT>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = (int64_t)p.n_qtiles * batch;
+  if (blocks > 0x7fffffff || batch > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  kern<<<(unsigned)blocks, kThreads, C::SMEM, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, bool ENT>
 cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bool vk, cudaStream_t st) {
   if (vk) {
-    if (dv == 128) return launch<T, 0, true, 4, ENT>(p, batch, st);
+    if (dv == 128) return launch2<T, true, ENT>(p, batch, st);
     if (dv == 256 && dv1 == 128) return launch<T, 2, true, 3, ENT>(p, batch, st);
   } else {
-    if (dv == 128) return launch<T, 2, false, 3, ENT>(p, batch, st);
+    if (dv == 128) return launch2<T, false, ENT>(p, batch, st);
     if (dv == 256) return launch<T, 4, false, 2, ENT>(p, batch, st);
   }
   return cudaErrorNotSupported;
