@@ -79,9 +79,13 @@ def test_noalloc_backward_matches_workspace_backward():
 
 
 def test_noalloc_rejects_requests_beyond_its_scratch():
+    # Placeholder pointers that are NOT 16-byte aligned: should the size check ever let this request
+    # through, vmb_fea_bwd's own validation rejects it before anything is launched on the device.
     a = N.FeaBwdArgs()
-    a.q = a.k = a.v = a.o = a.dout = a.lse = a.grad_q = a.grad_k = a.grad_v = 256
-    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 64, 32768, 32768, 128, 128, 128  # ~1 GiB of scratch
+    a.q = a.k = a.v = a.o = a.dout = a.lse = a.grad_q = a.grad_k = a.grad_v = 8
+    # 64 sequences of 2^20 queries: at least 768 MiB of scratch on every backward path
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 64, 1 << 20, 1 << 20, 128, 128, 128
     a.grad_mode, a.sm_scale = 0, 0.1
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) > 32 << 20
     assert N.lib.vmb_fea_bwd_noalloc(ctypes.byref(a), None) == 1
     assert b"scratch" in N.lib.vmb_last_error()

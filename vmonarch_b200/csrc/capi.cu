@@ -110,8 +110,15 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   return cuda_status(vmb::fea_fwd_mma(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, st), "vmb_fea_fwd");
 }
 
+// Workspace: the tcgen05 path keeps three folded statistics planes [batch][round_up(n_q, 128)];
+// the mma.sync path keeps c and g [batch][n_q] and, in grad_mode 0, an fp32 dQ accumulator.
+static bool bwd_uses_sm100(const vmb_fea_bwd_args* a) {
+  return vmb::fea_bwd_sm100_supported(a->d, a->dv, a->dv1, a->v_is_k != 0);
+}
+
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
   if (!a || a->batch < 0 || a->n_q < 0) return -1;
+  if (bwd_uses_sm100(a)) return 3 * round_up(a->batch * round_up(a->n_q, 128) * 4, 256);
   const int64_t rows = a->batch * a->n_q;
   int64_t bytes = 2 * round_up(rows * 4, 256);
   if (a->grad_mode == 0) bytes += round_up(rows * a->d * 4, 256);
@@ -147,15 +154,18 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
   const int64_t rows = a->batch * a->n_q;
   char* ws = static_cast<char*>(a->workspace);
-  float* cc = reinterpret_cast<float*>(ws);
-  float* gg = reinterpret_cast<float*>(ws + round_up(rows * 4, 256));
-  float* dq_acc = a->grad_mode == 0 ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
-
-  const bool sm100 = vmb::fea_bwd_sm100_supported(a->d, a->dv, a->dv1, a->v_is_k != 0);
-  if (sm100) dq_acc = nullptr;  // the tcgen05 dQ kernel writes grad_q directly in either mode
+  const bool sm100 = bwd_uses_sm100(a);
+  // tcgen05 path: folded planes (the dQ kernel writes grad_q directly in either grad mode)
+  const int64_t n_pad = round_up(a->n_q, 128);
+  float* fold = sm100 ? reinterpret_cast<float*>(ws) : nullptr;
+  // mma.sync path: c, g and the fp32 dQ accumulator of grad_mode 0
+  float* cc = sm100 ? nullptr : reinterpret_cast<float*>(ws);
+  float* gg = sm100 ? nullptr : reinterpret_cast<float*>(ws + round_up(rows * 4, 256));
+  float* dq_acc =
+      (!sm100 && a->grad_mode == 0) ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
   count(sm100 ? 3 : (dq_acc ? 3 : 2));
   cudaError_t e = vmb::fea_bwd_pre(a->o, a->o_bs, a->dout, a->do_bs, a->lse, a->ent, a->dent, cc, gg, a->batch,
-                                   (int)a->n_q, a->dv, bf16, st);
+                                   (int)a->n_q, a->dv, fold, n_pad, a->sm_scale, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(pre)");
   if (dq_acc) {
     e = cudaMemsetAsync(dq_acc, 0, rows * a->d * 4, st);
@@ -163,6 +173,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   }
   vmb::BwdParams p{};
   p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.dout = a->dout; p.lse = a->lse; p.cc = cc; p.gg = gg;
+  p.fold = fold; p.n_pad = n_pad;
   p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
   p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
   p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.do_bs = a->do_bs;

@@ -42,9 +42,10 @@ struct Sm100BwdParams {
   CUtensorMap tm_a, tm_b, tm_c, tm_d;  // dkdv: K, X, Q, dO ; dq: Q, dO, K, X  (boxes of 64 cols x 64/128 rows)
   const void* dout;  // dq kernel with dO in TMEM: [batch][n_q][DW] rows read directly
   int64_t do_bs;
-  const float* lse;
-  const float* cc;
-  const float* gg;
+  const float* nl;  // folded statistics planes [batch][n_pad] (fea_bwd_pre): -LSE2,
+  const float* nc;  //   -sm_scale (c + g LSE2),
+  const float* ng;  //   -sm_scale g
+  int64_t n_pad;
   void* grad0;   // dkdv: grad_k ; dq: grad_q
   void* grad1;   // dkdv: grad_v (or grad_v2 when v aliases k)
   int64_t g0_bs, g1_bs;
@@ -93,6 +94,24 @@ __device__ __forceinline__ void store_row128(uint32_t taddr, void* base, int64_t
 
 // ================================================================================ dK / dV kernel
 // XA: resident value atoms (V when !VK, V2 when VK); DW = width of W (and of dO).
+// Folded per-query statistics (written by fea_bwd_pre). With t = s * scale_log2 - LSE2 (the log2-
+// domain score minus the query's LSE2), P = 2^t and the reference's dS = sm_scale P (dP - c - g x),
+// x = t + LSE2, becomes dS = P (sm_scale dP + nc + ng t) with nl = -LSE2, nc = -sm_scale (c + g LSE2),
+// ng = -sm_scale g: two packed f32x2 FMAs and one multiply per pair of scores. Queries past n_q have
+// nl = -1e30 (finite, so ng t = 0 with ng = 0), hence P = 0 and dS = 0.
+
+// P and dS of two scores (s0, s1) with their dP (d0, d1), packed to the element type.
+template <typename T, bool WANT_P>
+__device__ __forceinline__ void prob_dscore(uint32_t s0, uint32_t s1, uint32_t d0, uint32_t d1, float2 sc2, float2 sm2,
+                                            float2 nl2, float2 nc2, float2 ng2, uint32_t& p_out, uint32_t& ds_out) {
+  const float2 t = __ffma2_rn(make_float2(__uint_as_float(s0), __uint_as_float(s1)), sc2, nl2);
+  const float2 pr = make_float2(fast_exp2(t.x), fast_exp2(t.y));
+  const float2 u = __ffma2_rn(ng2, t, __ffma2_rn(make_float2(__uint_as_float(d0), __uint_as_float(d1)), sm2, nc2));
+  const float2 ds = __fmul2_rn(pr, u);
+  if (WANT_P) p_out = Elem<T>::pack(pr.x, pr.y);
+  ds_out = Elem<T>::pack(ds.x, ds.y);
+}
+
 template <int XA, bool VK, int NQS>
 struct DkdvCfg {
   static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
@@ -141,7 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     abort_sh = 0;
     mbar_init(BAR_KV, 1);
     for (int s = 0; s < NQS; ++s) {
-      mbar_init(BAR_QFULL(s), 1 + 32);
+      mbar_init(BAR_QFULL(s), 1);
       mbar_init(BAR_QEMPTY(s), 1);
     }
     for (int b = 0; b < 2; ++b) {
@@ -173,30 +192,22 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
       tma_load_3d(sRes + kAtom128, &p.tm_a, 64, k0, bi, BAR_KV);
       for (int a = 0; a < XA; ++a) tma_load_3d(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bi, BAR_KV);
     }
-    const float* lse = p.lse + (int64_t)bi * p.n_q;
-    const float* cc = p.cc + (int64_t)bi * p.n_q;
-    const float* gg = p.gg + (int64_t)bi * p.n_q;
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
-      bool ok = true;
-      if (lane == 0 && i >= NQS) ok = mbar_wait(BAR_QEMPTY(s), ((i / NQS) - 1) & 1, abort, &g_bwd_err, 1);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+      if (i >= NQS &&
+          !__all_sync(0xffffffffu, mbar_wait(BAR_QEMPTY(s), ((i / NQS) - 1) & 1, abort, &g_bwd_err, 1)))
+        break;
       if (lane == 0) {
-        mbar_expect_tx(BAR_QFULL(s), C::SLOT_T);
+        mbar_expect_tx(BAR_QFULL(s), C::SLOT_T + 3 * 256);
         tma_load_3d(slot_q(s), &p.tm_c, 0, i * 64, bi, BAR_QFULL(s));
         tma_load_3d(slot_q(s) + kAtom64, &p.tm_c, 64, i * 64, bi, BAR_QFULL(s));
         for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(slot_do(s) + a * kAtom64, &p.tm_d, 64 * a, i * 64, bi, BAR_QFULL(s));
+        // the 64 queries' folded statistics: one 256-byte copy per plane (rows padded to 128)
+        const int64_t r0 = (int64_t)bi * p.n_pad + i * 64;
+        bulk_load(slot_stats(s), p.nl + r0, 256, BAR_QFULL(s));
+        bulk_load(slot_stats(s) + 256, p.nc + r0, 256, BAR_QFULL(s));
+        bulk_load(slot_stats(s) + 512, p.ng + r0, 256, BAR_QFULL(s));
       }
-      float* st = reinterpret_cast<float*>(smem_raw + (slot_stats(s) - smem_u32(smem_raw)));
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int q = i * 64 + lane + 32 * h;
-        const bool okq = q < p.n_q;
-        st[lane + 32 * h] = okq ? lse[q] : __int_as_float(0x7f800000);
-        st[64 + lane + 32 * h] = okq ? cc[q] : 0.f;
-        st[128 + lane + 32 * h] = okq ? gg[q] : 0.f;
-      }
-      mbar_arrive(BAR_QFULL(s));
       armed[s] = i / NQS + 1;
     }
     if (lane == 0) {
@@ -290,35 +301,32 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
       if (!warp_wait(BAR_SPFULL(wg), (i >> 1) & 1, 8)) { ok = false; break; }
       if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
       tc_fence_after();
-      uint32_t sv[64], dv[64];
-      tmem_ld32(ts, sv);
-      tmem_ld32(ts + 32, sv + 32);
-      tmem_ld32(tdp, dv);
-      tmem_ld32(tdp + 32, dv + 32);
-      tmem_wait_ld();
       const uint32_t st = slot_stats(s);
-      uint32_t pk[32], dk[32];
+      const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
+      // two halves of 32 queries: P^T / dS^T of half h go to columns [16h, 16h + 16) of S^T / dP^T,
+      // which half h (or the half before it) has already loaded
+#pragma unroll 1
+      for (int h = 0; h < 2; ++h) {
+        uint32_t sv[32], dv[32];
+        tmem_ld32(ts + 32 * h, sv);
+        tmem_ld32(tdp + 32 * h, dv);
+        tmem_wait_ld();
+        uint32_t pk[16], dk[16];
 #pragma unroll
-      for (int e = 0; e < 64; e += 4) {
-        float l4[4], c4[4], g4[4];
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l4[0]), "=f"(l4[1]), "=f"(l4[2]), "=f"(l4[3]) : "r"(st + 4 * e));
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c4[0]), "=f"(c4[1]), "=f"(c4[2]), "=f"(c4[3]) : "r"(st + 256 + 4 * e));
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(g4[0]), "=f"(g4[1]), "=f"(g4[2]), "=f"(g4[3]) : "r"(st + 512 + 4 * e));
-        float pr[4], dr[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
-          const float pv = fast_exp2(x - l4[u]);
-          pr[u] = pv;
-          dr[u] = pv * (__uint_as_float(dv[e + u]) - c4[u] - g4[u] * x) * p.sm_scale;
+        for (int e = 0; e < 32; e += 4) {
+          const uint32_t so = st + 4 * (32 * h + e);
+          float4 l4, c4, g4;
+          asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l4.x), "=f"(l4.y), "=f"(l4.z), "=f"(l4.w) : "r"(so));
+          asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c4.x), "=f"(c4.y), "=f"(c4.z), "=f"(c4.w) : "r"(so + 256));
+          asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(g4.x), "=f"(g4.y), "=f"(g4.z), "=f"(g4.w) : "r"(so + 512));
+          prob_dscore<T, true>(sv[e], sv[e + 1], dv[e], dv[e + 1], sc2, sm2, make_float2(l4.x, l4.y),
+                               make_float2(c4.x, c4.y), make_float2(g4.x, g4.y), pk[e >> 1], dk[e >> 1]);
+          prob_dscore<T, true>(sv[e + 2], sv[e + 3], dv[e + 2], dv[e + 3], sc2, sm2, make_float2(l4.z, l4.w),
+                               make_float2(c4.z, c4.w), make_float2(g4.z, g4.w), pk[(e >> 1) + 1], dk[(e >> 1) + 1]);
         }
-        pk[e >> 1] = Elem<T>::pack(pr[0], pr[1]);
-        pk[(e >> 1) + 1] = Elem<T>::pack(pr[2], pr[3]);
-        dk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
-        dk[(e >> 1) + 1] = Elem<T>::pack(dr[2], dr[3]);
+        tmem_st16(ts + 16 * h, pk);
+        tmem_st16(tdp + 16 * h, dk);
       }
-      tmem_st32(ts, pk);
-      tmem_st32(tdp, dk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR_PDSFULL(wg));
@@ -557,10 +565,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
     const int q = q0 + row;
     const bool qok = q < p.n_q;
-    const int64_t ridx = (int64_t)bi * p.n_q + q;
-    const float lse = qok ? p.lse[ridx] : __int_as_float(0x7f800000);
-    const float cc = qok ? p.cc[ridx] : 0.f;
-    const float gg = qok ? p.gg[ridx] : 0.f;
+    const int64_t fidx = (int64_t)bi * p.n_pad + q;  // q < n_pad (rows padded to 128)
+    const float fl = p.nl[fidx], fc = p.nc[fidx], fg = p.ng[fidx];
+    const float2 nl2 = make_float2(fl, fl), nc2 = make_float2(fc, fc), ng2 = make_float2(fg, fg);
+    const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
     auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
       const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
       return __all_sync(0xffffffffu, mine);
@@ -603,14 +611,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
       uint32_t pk[32];
 #pragma unroll
       for (int e = 0; e < 64; e += 2) {
-        float dr[2];
-#pragma unroll
-        for (int u = 0; u < 2; ++u) {
-          const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
-          const float pv = fast_exp2(x - lse);
-          dr[u] = pv * (__uint_as_float(dv[e + u]) - cc - gg * x) * p.sm_scale;
-        }
-        pk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
+        uint32_t unused;
+        prob_dscore<T, false>(sv[e], sv[e + 1], dv[e], dv[e + 1], sc2, sm2, nl2, nc2, ng2, unused, pk[e >> 1]);
       }
       tmem_st32(ts, pk);
       tmem_wait_st();
@@ -622,250 +624,6 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
     if (ok)
       store_row128<T>(tmem + lane_off + T_DQ, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc,
                       qok, 2 * wg, 2 * wg + 2);
-  }
-
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 512);
-}
-
-// ================================================================================ dK/dV kernel, 128-query tiles
-// CTA = 128 keys; walks 128-query tiles (full-rate N = 128 MMAs); WG w owns queries [64w, 64w+64)
-// of each tile. TMEM: S^T [0,128) dP^T [128,256) dK [256,384) dV [384,512); P^T / dS^T (bf16) are
-// written over the first half of each warpgroup's own S^T / dP^T columns, so tile i+1's S^T / dP^T
-// are issued behind tile i's dK / dV MMAs. Used for every mode whose 128-row query slot fits twice
-// in shared memory (all but the last VMonarch R step, whose dO is 256 wide).
-template <int XA, bool VK, int NQS>
-struct DkdvCfg2 {
-  static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
-  static constexpr int RES = (2 + XA) * kAtom128;
-  static constexpr int SLOT_T = (2 + DW / 64) * kAtom128;
-  static constexpr int SLOT = SLOT_T + 2048;  // + statistics: LSE2, c, g x 128
-  static constexpr int SMEM = 1024 + RES + NQS * SLOT;
-  static constexpr bool HAS_DV = XA > 0;
-  static_assert(SMEM <= 232448, "shared memory budget");
-};
-
-template <typename T, int XA, bool VK, int NQS>
-__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv128_kernel(const __grid_constant__ Sm100BwdParams p) {
-  using C = DkdvCfg2<XA, VK, NQS>;
-  constexpr bool kBf16 = Elem<T>::is_bf16;
-  constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 128, false, false);
-  constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);
-  constexpr int B_KV = 0, B_QFULL = 1, B_QEMPTY = 1 + NQS, B_SPFULL = 1 + 2 * NQS, B_PDSFULL = B_SPFULL + 1;
-  constexpr int B_DONE = B_PDSFULL + 1, NBARS = B_DONE + 1;
-
-  extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[NBARS];
-  __shared__ uint32_t tmem_base_sh;
-  __shared__ int abort_sh;
-
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bi = blockIdx.x / p.n_tiles;
-  const int k0 = (blockIdx.x % p.n_tiles) * 128;
-  const int nq = (p.n_q + 127) / 128;
-
-  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
-  const uint32_t sRes = sbase;
-  const uint32_t sW = VK ? sRes : sRes + 2 * kAtom128;
-  const uint32_t sSlots = sbase + C::RES;
-  const uint32_t bar0 = smem_u32(bars);
-  auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
-  volatile int* abort = &abort_sh;
-  auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
-  auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom128; };
-  auto slot_stats = [&](int s) { return sSlots + s * C::SLOT + C::SLOT_T; };
-
-  if (threadIdx.x == 0) {
-    abort_sh = 0;
-    mbar_init(BAR(B_KV), 1);
-    for (int s = 0; s < NQS; ++s) {
-      mbar_init(BAR(B_QFULL + s), 1 + 32);
-      mbar_init(BAR(B_QEMPTY + s), 1);
-    }
-    mbar_init(BAR(B_SPFULL), 1);
-    mbar_init(BAR(B_PDSFULL), 256);
-    mbar_init(BAR(B_DONE), 1);
-    fence_mbar_init();
-  }
-  if (warp == 0) {
-    tmem_alloc(smem_u32(&tmem_base_sh), 512);
-    tmem_relinquish();
-  }
-  tc_fence_before();
-  __syncthreads();
-  tc_fence_after();
-  const uint32_t tmem = tmem_base_sh;
-
-  if (warp == 0) {
-    // ---------------------------------------------------------------- producer (whole warp)
-    int armed[NQS];
-    for (int s = 0; s < NQS; ++s) armed[s] = 0;
-    if (lane == 0) {
-      prefetch_tmap(&p.tm_a);
-      prefetch_tmap(&p.tm_c);
-      prefetch_tmap(&p.tm_d);
-      mbar_expect_tx(BAR(B_KV), C::RES);
-      tma_load_3d(sRes, &p.tm_a, 0, k0, bi, BAR(B_KV));
-      tma_load_3d(sRes + kAtom128, &p.tm_a, 64, k0, bi, BAR(B_KV));
-      for (int a = 0; a < XA; ++a) tma_load_3d(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bi, BAR(B_KV));
-    }
-    const float* lse = p.lse + (int64_t)bi * p.n_q;
-    const float* cc = p.cc + (int64_t)bi * p.n_q;
-    const float* gg = p.gg + (int64_t)bi * p.n_q;
-    for (int i = 0; i < nq; ++i) {
-      const int s = i % NQS;
-      bool ok = true;
-      if (lane == 0 && i >= NQS) ok = mbar_wait(BAR(B_QEMPTY + s), ((i / NQS) - 1) & 1, abort, &g_bwd_err, 1);
-      if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
-      if (lane == 0) {
-        mbar_expect_tx(BAR(B_QFULL + s), C::SLOT_T);
-        tma_load_3d(slot_q(s), &p.tm_c, 0, i * 128, bi, BAR(B_QFULL + s));
-        tma_load_3d(slot_q(s) + kAtom128, &p.tm_c, 64, i * 128, bi, BAR(B_QFULL + s));
-        for (int a = 0; a < C::DW / 64; ++a)
-          tma_load_3d(slot_do(s) + a * kAtom128, &p.tm_d, 64 * a, i * 128, bi, BAR(B_QFULL + s));
-      }
-      float* st = reinterpret_cast<float*>(smem_raw + (slot_stats(s) - smem_u32(smem_raw)));
-#pragma unroll
-      for (int h = 0; h < 4; ++h) {
-        const int qq = i * 128 + lane + 32 * h;
-        const bool okq = qq < p.n_q;
-        st[lane + 32 * h] = okq ? lse[qq] : __int_as_float(0x7f800000);
-        st[128 + lane + 32 * h] = okq ? cc[qq] : 0.f;
-        st[256 + lane + 32 * h] = okq ? gg[qq] : 0.f;
-      }
-      mbar_arrive(BAR(B_QFULL + s));
-      armed[s] = i / NQS + 1;
-    }
-    if (lane == 0) {
-      mbar_wait_drain(BAR(B_KV), 0);
-      for (int s = 0; s < NQS; ++s)
-        if (armed[s] > 0) mbar_wait_drain(BAR(B_QFULL + s), (armed[s] - 1) & 1);
-    }
-  } else if (warp == 1) {
-    // ---------------------------------------------------------------- MMA issuer
-    // The whole warp walks the schedule with warp-uniform waits; one elected lane issues.
-    const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
-    auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_bwd_err, code));
-    };
-    {
-      bool ok = wwait(BAR(B_KV), 0, 2);
-      auto issue_sp = [&](int i) -> bool {
-        const int s = i % NQS;
-        if (!wwait(BAR(B_QFULL + s), (i / NQS) & 1, 2)) return false;
-        tc_fence_after();
-        {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
-            const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
-            mma_ss_if(leader, tmem, smem_desc_sw128(sRes + off, 16, 1024), smem_desc_sw128(slot_q(s) + off, 16, 1024), IDESC_SP,
-                   kk > 0);
-          }
-#pragma unroll
-          for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
-            const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
-            mma_ss_if(leader, tmem + 128, smem_desc_sw128(sW + off, 16, 1024), smem_desc_sw128(slot_do(s) + off, 16, 1024),
-                   IDESC_SP, kk > 0);
-          }
-          mma_commit_if(leader, BAR(B_SPFULL));
-        }
-        return true;
-      };
-      if (ok) ok = issue_sp(0);
-      for (int i = 0; ok && i < nq; ++i) {
-        if (!wwait(BAR(B_PDSFULL), i & 1, 4)) break;
-        tc_fence_after();
-        const int s = i % NQS;
-        {
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // queries [16kk, 16kk+16) live in warpgroup kk/4's columns
-            const uint32_t col = kk < 4 ? kk * 8 : 64 + (kk - 4) * 8;
-            const uint64_t bq = smem_desc_sw128(slot_q(s) + kk * 2048, kAtom128, 1024);
-            mma_ts_if(leader, tmem + 256, tmem + 128 + col, bq, IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);  // dK += dS^T Q
-            if (VK)
-              mma_ts_if(leader, tmem + 256, tmem + col, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom128, 1024), IDESC_ACC, 1u);
-            if (C::HAS_DV) {
-              const uint32_t vo = VK ? 2 * kAtom128 : 0;
-              mma_ts_if(leader, tmem + 384, tmem + col, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom128, 1024), IDESC_ACC,
-                     (i > 0 || kk > 0) ? 1u : 0u);
-            }
-          }
-          mma_commit_if(leader, BAR(B_QEMPTY + s));
-        }
-        if (i + 1 < nq) ok = issue_sp(i + 1);  // queued behind the MMAs that read P^T / dS^T
-      }
-      if (elect_one()) {
-        mma_commit(BAR(B_DONE));
-        mbar_wait_drain(BAR(B_DONE), 0);
-      }
-      __syncwarp();
-    }
-  } else {
-    // ---------------------------------------------------------------- compute: thread = key row
-    const int wg = (warp - 2) >> 2;
-    const int quad = warp & 3;
-    const int row = quad * 32 + lane;
-    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
-    auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
-      const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
-      return __all_sync(0xffffffffu, mine);
-    };
-    const uint32_t ts = tmem + lane_off + 64 * wg, tdp = tmem + lane_off + 128 + 64 * wg;
-    bool ok = true;
-    for (int i = 0; i < nq; ++i) {
-      const int s = i % NQS;
-      if (!warp_wait(BAR(B_SPFULL), i & 1, 8)) { ok = false; break; }
-      if (!warp_wait(BAR(B_QFULL + s), (i / NQS) & 1, 8)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t sv[64], dv[64];
-      tmem_ld32(ts, sv);
-      tmem_ld32(ts + 32, sv + 32);
-      tmem_ld32(tdp, dv);
-      tmem_ld32(tdp + 32, dv + 32);
-      tmem_wait_ld();
-      const uint32_t st = slot_stats(s) + 4 * 64 * wg;  // this warpgroup's 64 queries
-      uint32_t pk[32], dk[32];
-#pragma unroll
-      for (int e = 0; e < 64; e += 4) {
-        float l4[4], c4[4], g4[4];
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l4[0]), "=f"(l4[1]), "=f"(l4[2]), "=f"(l4[3]) : "r"(st + 4 * e));
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c4[0]), "=f"(c4[1]), "=f"(c4[2]), "=f"(c4[3]) : "r"(st + 512 + 4 * e));
-        asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(g4[0]), "=f"(g4[1]), "=f"(g4[2]), "=f"(g4[3]) : "r"(st + 1024 + 4 * e));
-        float pr[4], dr[4];
-#pragma unroll
-        for (int u = 0; u < 4; ++u) {
-          const float x = __uint_as_float(sv[e + u]) * p.scale_log2;
-          const float pv = fast_exp2(x - l4[u]);
-          pr[u] = pv;
-          dr[u] = pv * (__uint_as_float(dv[e + u]) - c4[u] - g4[u] * x) * p.sm_scale;
-        }
-        pk[e >> 1] = Elem<T>::pack(pr[0], pr[1]);
-        pk[(e >> 1) + 1] = Elem<T>::pack(pr[2], pr[3]);
-        dk[e >> 1] = Elem<T>::pack(dr[0], dr[1]);
-        dk[(e >> 1) + 1] = Elem<T>::pack(dr[2], dr[3]);
-      }
-      tmem_st32(ts, pk);
-      tmem_st32(tdp, dk);
-      tmem_wait_st();
-      tc_fence_before();
-      mbar_arrive(BAR(B_PDSFULL));
-    }
-    if (ok) ok = warp_wait(BAR(B_DONE), 0, 8);
-    tc_fence_after();
-    const int key = k0 + row;
-    const bool kok = key < p.n_kv;
-    const int64_t krow = kok ? key : 0;
-    if (ok) {
-      if (C::HAS_DV) {
-        if (wg == 0) store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok);
-        else store_row128<T>(tmem + lane_off + 384, p.grad1, (int64_t)bi * p.g1_bs + krow * p.g1_cols, p.acc, kok);
-      } else {
-        store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok, 2 * wg,
-                        2 * wg + 2);
-      }
-    }
   }
 
   tc_fence_before();
@@ -890,9 +648,8 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   const int xa = vk ? (dv - 128) / 64 : dv / 64;  // value atoms beyond K (vk) or V atoms
   const void* xsrc = vk ? b.v2 : b.v;
   const int64_t xbs = vk ? b.v2_bs : b.v_bs;
-  // ---- dK / dV: 128-query tiles, except the last VMonarch R step (dO 256 wide) on 64-query tiles
-  const bool dkdv64 = vk && xa > 0;
-  const int qrows = dkdv64 ? 64 : 128;
+  // ---- dK / dV: 64-query tiles (two warpgroups on alternate tiles, double-buffered S^T / dP^T)
+  const int qrows = 64;
   Sm100BwdParams pa{};
   if (!tma::make_map(&pa.tm_a, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
@@ -902,9 +659,10 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   }
   if (!tma::make_map(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.q_bs, qrows)) return cudaErrorInvalidValue;
   if (!tma::make_map(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.do_bs, qrows)) return cudaErrorInvalidValue;
-  pa.lse = b.lse;
-  pa.cc = b.cc;
-  pa.gg = b.gg;
+  pa.nl = b.fold;
+  pa.nc = b.fold + batch * b.n_pad;
+  pa.ng = b.fold + 2 * batch * b.n_pad;
+  pa.n_pad = b.n_pad;
   pa.grad0 = b.dk;
   pa.g0_bs = b.dk_bs;
   pa.grad1 = vk ? b.dv2 : b.dv;
@@ -918,12 +676,12 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.sm_scale = b.sm_scale;
   cudaError_t e;
   const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
-  if (dkdv64) {
+  if (vk && xa > 0) {
     e = run(fea_bwd_dkdv_kernel<T, 2, true, 3>, DkdvCfg<2, true, 3>::SMEM, blocks_a, kThreads, pa, st);
   } else if (vk) {
-    e = run(fea_bwd_dkdv128_kernel<T, 0, true, 2>, DkdvCfg2<0, true, 2>::SMEM, blocks_a, kThreads, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 0, true, 5>, DkdvCfg<0, true, 5>::SMEM, blocks_a, kThreads, pa, st);
   } else {
-    e = run(fea_bwd_dkdv128_kernel<T, 2, false, 2>, DkdvCfg2<2, false, 2>::SMEM, blocks_a, kThreads, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4>, DkdvCfg<2, false, 4>::SMEM, blocks_a, kThreads, pa, st);
   }
   if (e != cudaSuccess) return e;
   // ---- dQ: 128-key tiles (dO staged in TMEM when it is 256 wide)
@@ -938,9 +696,10 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   }
   pb.dout = b.dout;
   pb.do_bs = b.do_bs;
-  pb.lse = b.lse;
-  pb.cc = b.cc;
-  pb.gg = b.gg;
+  pb.nl = b.fold;
+  pb.nc = b.fold + batch * b.n_pad;
+  pb.ng = b.fold + 2 * batch * b.n_pad;
+  pb.n_pad = b.n_pad;
   pb.grad0 = b.dq;
   pb.g0_bs = b.dq_bs;
   pb.n_q = b.n_q;

@@ -27,6 +27,8 @@ struct BwdParams {
   const float* lse;   // [batch][n_q]
   const float* cc;    // [batch][n_q]  delta_i + dE_i * (E_i - LSE_i)
   const float* gg;    // [batch][n_q]  dE_i * ln(2)
+  const float* fold;  // tcgen05 path: planes nl, nc, ng, each [batch][n_pad] (see fea_bwd_pre)
+  int64_t n_pad;      // rows per sequence of the planes: n_q rounded up to 128
   float* dq;          // fp32 accumulator [batch][n_q][D] (batch stride dq_bs)
   void* dk;           // [batch][n_kv][D]      element type or fp32 (acc_kv)
   void* dv;           // [batch][n_kv][dv1]    unused when v aliases k

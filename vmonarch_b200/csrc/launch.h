@@ -33,7 +33,7 @@ cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out);
 cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
-                        bool bf16, cudaStream_t st);
+                        float* fold, int64_t n_pad, float sm_scale, bool bf16, cudaStream_t st);
 cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
                      bool bf16, cudaStream_t st);
 bool lstep_mma_supported(const LstepParams& p, bool last);

@@ -4,7 +4,12 @@
 // folds the entropy-gradient terms of kernel.py:202/241 into two per-row constants:
 //   c_i = sum_d o_id dO_id + dE_i (E_i - LSE_i)     (LSE_i natural: LSE2_i * ln 2)
 //   g_i = dE_i ln 2
-// so the main backward kernel computes dS = P (dP - c_i - g_i x_ij) with one extra FMA.
+// so the backward kernels compute dS = P (dP - c_i - g_i x_ij) with one extra FMA. For the tcgen05
+// kernels the constants are folded once more (t = x - LSE2, P = 2^t):
+//   nl_i = -LSE2_i,  nc_i = -sm_scale (c_i + g_i LSE2_i),  ng_i = -sm_scale g_i
+// so that dS = P (sm_scale dP + nc + ng t), and written as three planes [batch][n_pad] with the
+// rows past n_q set to (-1e30, 0, 0) (P = 0 and dS = 0 there): a query tile's statistics are
+// then one aligned bulk copy per plane.
 #include "common.cuh"
 #include "launch.h"
 
@@ -14,11 +19,22 @@ namespace vmb {
 template <typename T>
 __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_bs, const T* dout, int64_t do_bs,
                                                           const float* lse, const float* ent, const float* dent,
-                                                          float* cc, float* gg, int64_t rows, int n_q, int dv) {
+                                                          float* cc, float* gg, int64_t rows, int n_q, int dv,
+                                                          float* fold, int64_t n_pad, int64_t plane, float sm_scale) {
   const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
-  const int64_t bi = row / n_q, r = row % n_q;
+  const int64_t rp = fold ? n_pad : n_q;  // rows are [batch][rp]
+  const int64_t bi = row / rp, r = row % rp;
+  if (r >= n_q) {  // padding row of the folded planes
+    if (lane == 0) {
+      fold[row] = -1e30f;
+      fold[plane + row] = 0.f;
+      fold[2 * plane + row] = 0.f;
+    }
+    return;
+  }
+  const int64_t src = bi * n_q + r;  // row of the [batch][n_q] inputs
   const T* orow = o + bi * o_bs + r * dv;
   const T* drow = dout + bi * do_bs + r * dv;
   float acc = 0.f;
@@ -38,29 +54,38 @@ __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_
   if (lane == 0) {
     float c = acc, g = 0.f;
     if (dent) {
-      const float de = dent[row];
-      c = fmaf(de, ent[row] - lse[row] * kLn2, acc);
+      const float de = dent[src];
+      c = fmaf(de, ent[src] - lse[src] * kLn2, acc);
       g = de * kLn2;
     }
-    cc[row] = c;
-    gg[row] = g;
+    if (fold) {
+      const float l2 = lse[src];
+      fold[row] = -l2;
+      fold[plane + row] = -sm_scale * fmaf(g, l2, c);
+      fold[2 * plane + row] = -sm_scale * g;
+    } else {
+      cc[src] = c;
+      gg[src] = g;
+    }
   }
 }
 
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
-                        bool bf16, cudaStream_t st) {
-  const int64_t rows = batch * n_q;
+                        float* fold, int64_t n_pad, float sm_scale, bool bf16, cudaStream_t st) {
+  const int64_t rows = batch * (fold ? n_pad : n_q);
+  const int64_t plane = batch * n_pad;
   const int64_t blocks = (rows + 7) / 8;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   if (bf16)
     fea_bwd_pre_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
         static_cast<const __nv_bfloat16*>(o), o_bs, static_cast<const __nv_bfloat16*>(dout), do_bs, lse, ent, dent,
-        cc, gg, rows, n_q, dv);
+        cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale);
   else
     fea_bwd_pre_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __half*>(o), o_bs,
                                                                   static_cast<const __half*>(dout), do_bs, lse, ent,
-                                                                  dent, cc, gg, rows, n_q, dv);
+                                                                  dent, cc, gg, rows, n_q, dv, fold, n_pad, plane,
+                                                                  sm_scale);
   return cudaGetLastError();
 }
 

@@ -1,8 +1,9 @@
 // vmb_fea_bwd_noalloc: the FlashEntropyAttention backward for callers that cannot allocate device
 // memory.
 //
-// vmb_fea_bwd needs a caller-provided scratch workspace (two fp32 per-row constants and, when the
-// gradients are written in bf16/fp16, an fp32 dQ accumulator). Some hosts cannot hand one over:
+// vmb_fea_bwd needs a caller-provided scratch workspace (fp32 per-row statistics: three folded
+// planes on the tcgen05 path; on the mma.sync path two constants and, when the gradients are
+// written in bf16/fp16, an fp32 dQ accumulator). Some hosts cannot hand one over:
 // an engine plugin whose enqueue hook must not allocate because the host framework owns every
 // device buffer, a foreign-language binding that can only pass the tensors the user gave it, or a
 // latency-critical pipeline where a cudaMalloc (and the device-wide synchronisation it can imply)
