@@ -40,55 +40,62 @@ constexpr int kAtom64 = 64 * 128;    // ... of 64 rows x 128 B
 
 struct Sm100BwdParams {
   CUtensorMap tm_a, tm_b, tm_c, tm_d;  // dkdv: K, X, Q, dO ; dq: Q, dO, K, X  (boxes of 64 cols x 64/128 rows)
+  CUtensorMap tm_g0, tm_g1;            // gradient outputs (dkdv: dK, dV / dV2; dq: dQ): fp32 boxes of
+                                       // 32 x 128 when added into (acc), else 16-bit boxes of 64 x 128
   const void* dout;  // dq kernel with dO in TMEM: [batch][n_q][DW] rows read directly
   int64_t do_bs;
   const float* nl;  // folded statistics planes [batch][n_pad] (fea_bwd_pre): -LSE2,
   const float* nc;  //   -sm_scale (c + g LSE2),
   const float* ng;  //   -sm_scale g
   int64_t n_pad;
-  void* grad0;   // dkdv: grad_k ; dq: grad_q
-  void* grad1;   // dkdv: grad_v (or grad_v2 when v aliases k)
-  int64_t g0_bs, g1_bs;
-  int g1_cols;   // row width of grad1
   int n_q, n_kv, n_tiles;
-  int acc;       // 1: fp32 accumulate
+  int acc;       // 1: gradients are fp32 buffers added into (TMA reduce-add), else 16-bit stores
   float scale_log2, sm_scale;
 };
 
-// Writes one 128-column fp32 TMEM row (this thread's lane) to a gradient row. The TMEM loads are
-// warp-collective and run on every lane; only lanes with `valid` rows store.
+// Gradient epilogue. The 128 x 128 fp32 accumulator tile in TMEM (thread = row = TMEM lane) is
+// staged in shared memory with the 128-byte swizzle and written by TMA: reduce-add into fp32
+// gradients (acc), or stored as 16-bit values. The read-modify-write then runs in the memory system
+// instead of stalling the SM on load latency, and rows past the map's extent are clipped.
+// Staging layout: fp32 -> four [128 rows][32 floats] boxes at stage + c * 16 KB; 16-bit -> two
+// [128 rows][64 elements] boxes at stage + a * 16 KB.
 template <typename T>
-__device__ __forceinline__ void store_row128(uint32_t taddr, void* base, int64_t off, bool acc, bool valid,
-                                             int c_begin = 0, int c_end = 4) {
+__device__ __forceinline__ void stage_acc_rows(uint32_t taddr, uint32_t stage, int row, bool f32, int c_begin,
+                                               int c_end) {
 #pragma unroll 1
   for (int c = c_begin; c < c_end; ++c) {
     uint32_t v[32];
     tmem_ld32(taddr + c * 32, v);
     tmem_wait_ld();
-    if (!valid) continue;
-    if (acc) {
-      float* dst = static_cast<float*>(base) + off + c * 32;
+    if (f32) {
+      const uint32_t base = stage + c * 16384 + row * 128;
 #pragma unroll
-      for (int i = 0; i < 32; i += 4) {
-        float4 o = *reinterpret_cast<float4*>(dst + i);
-        o.x += __uint_as_float(v[i]);
-        o.y += __uint_as_float(v[i + 1]);
-        o.z += __uint_as_float(v[i + 2]);
-        o.w += __uint_as_float(v[i + 3]);
-        *reinterpret_cast<float4*>(dst + i) = o;
-      }
+      for (int k = 0; k < 8; ++k)
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((k ^ (row & 7)) << 4)), "r"(v[4 * k]),
+                     "r"(v[4 * k + 1]), "r"(v[4 * k + 2]), "r"(v[4 * k + 3])
+                     : "memory");
     } else {
-      T* dst = static_cast<T*>(base) + off + c * 32;
+      uint32_t w[16];
 #pragma unroll
-      for (int i = 0; i < 32; i += 8) {
-        uint4 w;
-        w.x = Elem<T>::pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1]));
-        w.y = Elem<T>::pack(__uint_as_float(v[i + 2]), __uint_as_float(v[i + 3]));
-        w.z = Elem<T>::pack(__uint_as_float(v[i + 4]), __uint_as_float(v[i + 5]));
-        w.w = Elem<T>::pack(__uint_as_float(v[i + 6]), __uint_as_float(v[i + 7]));
-        *reinterpret_cast<uint4*>(dst + i) = w;
+      for (int i = 0; i < 16; ++i) w[i] = Elem<T>::pack(__uint_as_float(v[2 * i]), __uint_as_float(v[2 * i + 1]));
+      const uint32_t base = stage + (c >> 1) * 16384 + row * 128;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) {
+        const int chunk = (c & 1) * 4 + k;
+        asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((chunk ^ (row & 7)) << 4)),
+                     "r"(w[4 * k]), "r"(w[4 * k + 1]), "r"(w[4 * k + 2]), "r"(w[4 * k + 3])
+                     : "memory");
       }
     }
+  }
+}
+
+// One thread, after the staging barrier: the whole 128-row tile starting at row0 of sequence bi.
+__device__ __forceinline__ void issue_grad_tile(const CUtensorMap* tm, uint32_t stage, int row0, int bi, bool f32) {
+  if (f32) {
+    for (int c = 0; c < 4; ++c) tma_reduce_add_3d(tm, 32 * c, row0, bi, stage + c * 16384);
+  } else {
+    for (int a = 0; a < 2; ++a) tma_store_3d(tm, 64 * a, row0, bi, stage + a * 16384);
   }
 }
 
@@ -333,18 +340,23 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     }
     if (ok) ok = warp_wait(BAR_DONE, 0, 8);
     tc_fence_after();
-    const int key = k0 + row;
-    const bool kok = key < p.n_kv;
-    const int64_t krow = kok ? key : 0;
+    // epilogue: stage dK (and dV) in the idle query slots, one thread writes them with TMA; WG 0
+    // stages dK, WG 1 dV (or, without dV, the second half of dK)
+    const uint32_t stage0 = sSlots, stage1 = sSlots + 65536;
     if (ok) {
-      // WG 0 writes dK, WG 1 writes dV (or, without dV, the second half of dK)
       if (C::HAS_DV) {
-        if (wg == 0) store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok);
-        else store_row128<T>(tmem + lane_off + 384, p.grad1, (int64_t)bi * p.g1_bs + krow * p.g1_cols, p.acc, kok);
+        if (wg == 0) stage_acc_rows<T>(tmem + lane_off + 256, stage0, row, p.acc, 0, 4);
+        else stage_acc_rows<T>(tmem + lane_off + 384, stage1, row, p.acc, 0, 4);
       } else {
-        store_row128<T>(tmem + lane_off + 256, p.grad0, (int64_t)bi * p.g0_bs + krow * 128, p.acc, kok, 2 * wg,
-                        2 * wg + 2);
+        stage_acc_rows<T>(tmem + lane_off + 256, stage0, row, p.acc, 2 * wg, 2 * wg + 2);
       }
+    }
+    fence_proxy_async_smem();
+    ok = named_bar_and(1, 256, ok);
+    if (warp == 2 && lane == 0 && ok && !*abort) {
+      issue_grad_tile(&p.tm_g0, stage0, k0, bi, p.acc);
+      if (C::HAS_DV) issue_grad_tile(&p.tm_g1, stage1, k0, bi, p.acc);
+      tma_store_commit_and_wait();
     }
   }
 
@@ -621,9 +633,14 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
     }
     if (ok) ok = warp_wait(BAR(B_DONE), 0, 128);
     tc_fence_after();
-    if (ok)
-      store_row128<T>(tmem + lane_off + T_DQ, p.grad0, (int64_t)bi * p.g0_bs + (int64_t)(qok ? q : 0) * 128, p.acc,
-                      qok, 2 * wg, 2 * wg + 2);
+    // epilogue: stage dQ in the idle K ring (WG w: columns [64w, 64w + 64)), one thread writes it
+    if (ok) stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc, 2 * wg, 2 * wg + 2);
+    fence_proxy_async_smem();
+    ok = named_bar_and(1, 256, ok);
+    if (warp == 2 && lane == 0 && ok && !*abort) {
+      issue_grad_tile(&p.tm_g0, sK, q0, bi, p.acc);
+      tma_store_commit_and_wait();
+    }
   }
 
   tc_fence_before();
@@ -663,11 +680,14 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.nc = b.fold + batch * b.n_pad;
   pa.ng = b.fold + 2 * batch * b.n_pad;
   pa.n_pad = b.n_pad;
-  pa.grad0 = b.dk;
-  pa.g0_bs = b.dk_bs;
-  pa.grad1 = vk ? b.dv2 : b.dv;
-  pa.g1_bs = vk ? b.dv2_bs : b.dv_bs;
-  pa.g1_cols = 128;
+  // gradient maps: dK, and dV (or dV2 when V aliases K) when the kernel has a value accumulator
+  auto grad_map = [&](CUtensorMap* m, void* base, int64_t rows, int64_t bs, bool f32) {
+    return f32 ? tma::make_map_f32(m, base, 128, rows, batch, bs, 128)
+               : tma::make_map(m, base, bf16, 128, rows, batch, bs, 128);
+  };
+  if (!grad_map(&pa.tm_g0, b.dk, b.n_kv, b.dk_bs, b.acc_kv)) return cudaErrorInvalidValue;
+  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, b.n_kv, vk ? b.dv2_bs : b.dv_bs, b.acc_kv))
+    return cudaErrorInvalidValue;
   pa.n_q = b.n_q;
   pa.n_kv = b.n_kv;
   pa.n_tiles = (b.n_kv + 127) / 128;
@@ -700,8 +720,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pb.nc = b.fold + batch * b.n_pad;
   pb.ng = b.fold + 2 * batch * b.n_pad;
   pb.n_pad = b.n_pad;
-  pb.grad0 = b.dq;
-  pb.g0_bs = b.dq_bs;
+  if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q)) return cudaErrorInvalidValue;
   pb.n_q = b.n_q;
   pb.n_kv = b.n_kv;
   pb.n_tiles = (b.n_q + 127) / 128;

@@ -82,6 +82,15 @@ __device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int x, int 
                "r"(x), "r"(y), "r"(z), "r"(src)
                : "memory");
 }
+// Element-wise global += smem tile (fp32 add performed by the memory system), rows past the map's
+// extent clipped.
+__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, int x, int y, int z, uint32_t src) {
+  asm volatile(
+      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+          reinterpret_cast<uint64_t>(map)),
+      "r"(x), "r"(y), "r"(z), "r"(src)
+      : "memory");
+}
 __device__ __forceinline__ void tma_store_commit_and_wait() {
   asm volatile("cp.async.bulk.commit_group;" ::: "memory");
   asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory");
