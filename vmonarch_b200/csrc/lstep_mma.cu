@@ -346,19 +346,35 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   if (LAST) gather<T, DCH>(sg, static_cast<const T*>(p.dz) + bh * N * D, D, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
   cp_async_commit();
   if (!LAST) {  // du is fp32: convert while the other rows are in flight
+    // four chunks' loads are issued before any is converted, so a warp waits for one memory round
+    // trip per four chunks instead of one per chunk
     const float* du = p.du + bh * N * D;
-    for (int c = lane; c < MP * DCH; c += 32) {
-      const int k = c / DCH, ch = c % DCH;
-      uint4 w = make_uint4(0, 0, 0, 0);
-      if (k < m) {
-        const float4 v0 = *reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * D + ch * 8);
-        const float4 v1 = *reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * D + ch * 8 + 4);
-        w.x = Elem<T>::pack(v0.x, v0.y);
-        w.y = Elem<T>::pack(v0.z, v0.w);
-        w.z = Elem<T>::pack(v1.x, v1.y);
-        w.w = Elem<T>::pack(v1.z, v1.w);
+    constexpr int kChunks = MP * DCH / 32;  // per lane
+    static_assert(kChunks % 4 == 0, "chunk batching");
+#pragma unroll 1
+    for (int t0 = 0; t0 < kChunks; t0 += 4) {
+      float4 v[4][2];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = lane + 32 * (t0 + u), k = c / DCH, ch = c % DCH;
+        if (k < m) {
+          const float4* src = reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * D + ch * 8);
+          v[u][0] = src[0];
+          v[u][1] = src[1];
+        } else {
+          v[u][0] = v[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
       }
-      *reinterpret_cast<uint4*>(sg + swz<DCH>(k, ch)) = w;
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = lane + 32 * (t0 + u), k = c / DCH, ch = c % DCH;
+        uint4 w;
+        w.x = Elem<T>::pack(v[u][0].x, v[u][0].y);
+        w.y = Elem<T>::pack(v[u][0].z, v[u][0].w);
+        w.z = Elem<T>::pack(v[u][1].x, v[u][1].y);
+        w.w = Elem<T>::pack(v[u][1].z, v[u][1].w);
+        *reinterpret_cast<uint4*>(sg + swz<DCH>(k, ch)) = w;
+      }
     }
   }
   float ent[MP / 8][2];
@@ -442,13 +458,13 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
         const int i = mt * 16 + (lane >> 2) + h * 8;
         if (i >= m) continue;
         float* dst = gdq + ((int64_t)i * p.b + j) * D + half * 64 + (lane & 3) * 2;
+        // fire-and-forget reductions: this warp alone owns these dq elements, so nothing waits
+        // for the old value
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt) {
-          float2 v = *reinterpret_cast<float2*>(dst + nt * 8);
-          v.x += acc[mt][nt][2 * h];
-          v.y += acc[mt][nt][2 * h + 1];
-          *reinterpret_cast<float2*>(dst + nt * 8) = v;
-        }
+        for (int nt = 0; nt < 8; ++nt)
+          asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(dst + nt * 8), "f"(acc[mt][nt][2 * h]),
+                       "f"(acc[mt][nt][2 * h + 1])
+                       : "memory");
       }
   }
   __syncwarp();
