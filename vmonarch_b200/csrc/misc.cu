@@ -15,59 +15,76 @@
 
 namespace vmb {
 
-// one warp per row, 16-byte loads
-template <typename T>
+// LPR lanes per row (dv / 32 of them: 2, 4 or 8), each loading four 16-byte chunks of o and of dO
+// up front, so a warp has 32 / LPR rows and eight loads per lane in flight.
+template <typename T, int LPR>
 __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_bs, const T* dout, int64_t do_bs,
                                                           const float* lse, const float* ent, const float* dent,
                                                           float* cc, float* gg, int64_t rows, int n_q, int dv,
                                                           float* fold, int64_t n_pad, int64_t plane, float sm_scale) {
-  const int64_t row = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
+  constexpr int RPW = 32 / LPR;
+  const int lane = threadIdx.x & 31, gl = lane % LPR;
+  const int64_t row = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW + lane / LPR;
   const int64_t rp = fold ? n_pad : n_q;  // rows are [batch][rp]
-  const int64_t bi = row / rp, r = row % rp;
-  if (r >= n_q) {  // padding row of the folded planes
-    if (lane == 0) {
-      fold[row] = -1e30f;
-      fold[plane + row] = 0.f;
-      fold[2 * plane + row] = 0.f;
+  const bool live = row < rows;
+  const int64_t bi = live ? row / rp : 0, r = live ? row % rp : 0;
+  const bool real = live && r < n_q;      // false: padding row of the folded planes
+  float acc = 0.f;
+  if (real) {
+    const uint4* po = reinterpret_cast<const uint4*>(o + bi * o_bs + r * dv);
+    const uint4* pd = reinterpret_cast<const uint4*>(dout + bi * do_bs + r * dv);
+    uint4 va[4], vb[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      va[u] = po[gl + u * LPR];
+      vb[u] = pd[gl + u * LPR];
     }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const uint32_t wa[4] = {va[u].x, va[u].y, va[u].z, va[u].w}, wb[4] = {vb[u].x, vb[u].y, vb[u].z, vb[u].w};
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float2 fa = Elem<T>::unpack(wa[e]), fb = Elem<T>::unpack(wb[e]);
+        acc = fmaf(fa.x, fb.x, acc);
+        acc = fmaf(fa.y, fb.y, acc);
+      }
+    }
+  }
+#pragma unroll
+  for (int off = LPR / 2; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
+  if (!live || gl != 0) return;
+  if (!real) {
+    fold[row] = -1e30f;
+    fold[plane + row] = 0.f;
+    fold[2 * plane + row] = 0.f;
     return;
   }
   const int64_t src = bi * n_q + r;  // row of the [batch][n_q] inputs
-  const T* orow = o + bi * o_bs + r * dv;
-  const T* drow = dout + bi * do_bs + r * dv;
-  float acc = 0.f;
-  for (int c = lane; c < dv / 8; c += 32) {
-    const uint4 a = *reinterpret_cast<const uint4*>(orow + c * 8);
-    const uint4 b = *reinterpret_cast<const uint4*>(drow + c * 8);
-    const uint32_t wa[4] = {a.x, a.y, a.z, a.w}, wb[4] = {b.x, b.y, b.z, b.w};
-#pragma unroll
-    for (int e = 0; e < 4; ++e) {
-      const float2 fa = Elem<T>::unpack(wa[e]), fb = Elem<T>::unpack(wb[e]);
-      acc = fmaf(fa.x, fb.x, acc);
-      acc = fmaf(fa.y, fb.y, acc);
-    }
+  float c = acc, g = 0.f;
+  if (dent) {
+    const float de = dent[src];
+    c = fmaf(de, ent[src] - lse[src] * kLn2, acc);
+    g = de * kLn2;
   }
-#pragma unroll
-  for (int off = 16; off; off >>= 1) acc += __shfl_xor_sync(0xffffffffu, acc, off);
-  if (lane == 0) {
-    float c = acc, g = 0.f;
-    if (dent) {
-      const float de = dent[src];
-      c = fmaf(de, ent[src] - lse[src] * kLn2, acc);
-      g = de * kLn2;
-    }
-    if (fold) {
-      const float l2 = lse[src];
-      fold[row] = -l2;
-      fold[plane + row] = -sm_scale * fmaf(g, l2, c);
-      fold[2 * plane + row] = -sm_scale * g;
-    } else {
-      cc[src] = c;
-      gg[src] = g;
-    }
+  if (fold) {
+    const float l2 = lse[src];
+    fold[row] = -l2;
+    fold[plane + row] = -sm_scale * fmaf(g, l2, c);
+    fold[2 * plane + row] = -sm_scale * g;
+  } else {
+    cc[src] = c;
+    gg[src] = g;
   }
+}
+
+template <typename T, int LPR>
+void launch_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse, const float* ent,
+                const float* dent, float* cc, float* gg, int64_t rows, int n_q, int dv, float* fold, int64_t n_pad,
+                int64_t plane, float sm_scale, cudaStream_t st) {
+  const int64_t warps = (rows + 32 / LPR - 1) / (32 / LPR);
+  fea_bwd_pre_kernel<T, LPR><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+      static_cast<const T*>(o), o_bs, static_cast<const T*>(dout), do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold,
+      n_pad, plane, sm_scale);
 }
 
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
@@ -75,17 +92,16 @@ cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t d
                         float* fold, int64_t n_pad, float sm_scale, bool bf16, cudaStream_t st) {
   const int64_t rows = batch * (fold ? n_pad : n_q);
   const int64_t plane = batch * n_pad;
-  const int64_t blocks = (rows + 7) / 8;
-  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  if (bf16)
-    fea_bwd_pre_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
-        static_cast<const __nv_bfloat16*>(o), o_bs, static_cast<const __nv_bfloat16*>(dout), do_bs, lse, ent, dent,
-        cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale);
-  else
-    fea_bwd_pre_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(static_cast<const __half*>(o), o_bs,
-                                                                  static_cast<const __half*>(dout), do_bs, lse, ent,
-                                                                  dent, cc, gg, rows, n_q, dv, fold, n_pad, plane,
-                                                                  sm_scale);
+  if ((rows + 3) / 4 / 8 + 1 > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if (dv != 64 && dv != 128 && dv != 256) return cudaErrorInvalidValue;
+  const int lpr = dv / 32;
+#define VMB_PRE(TT, L) launch_pre<TT, L>(o, o_bs, dout, do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale, st)
+  if (bf16) {
+    if (lpr == 2) VMB_PRE(__nv_bfloat16, 2); else if (lpr == 4) VMB_PRE(__nv_bfloat16, 4); else VMB_PRE(__nv_bfloat16, 8);
+  } else {
+    if (lpr == 2) VMB_PRE(__half, 2); else if (lpr == 4) VMB_PRE(__half, 4); else VMB_PRE(__half, 8);
+  }
+#undef VMB_PRE
   return cudaGetLastError();
 }
 
