@@ -34,7 +34,11 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 320;    // producer warp, MMA warp, two compute warpgroups on alternate tiles
+constexpr int kThreads = 320;          // producer warp, MMA warp, two compute warpgroups on alternate tiles
+constexpr int kDqWarpgroups = 4;       // dQ kernel: compute warpgroups (32 key columns each)
+constexpr int kDqThreads = 64 + 128 * kDqWarpgroups;
+constexpr int kDkdvWarpgroups = 4;     // dK/dV kernel: two per query-tile stream (32 queries each)
+constexpr int kDkdvThreads = 64 + 128 * kDkdvWarpgroups;
 constexpr int kAtom128 = 128 * 128;  // swizzle-atom column block of 128 rows x 128 B
 constexpr int kAtom64 = 64 * 128;    // ... of 64 rows x 128 B
 
@@ -130,12 +134,17 @@ struct DkdvCfg {
   static_assert(SMEM <= 232448, "shared memory budget");
 };
 
-template <typename T, int XA, bool VK, int NQS>
-__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_constant__ Sm100BwdParams p) {
+template <typename T, int XA, bool VK, int NQS, int NWG>
+__global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const __grid_constant__ Sm100BwdParams p) {
   using C = DkdvCfg<XA, VK, NQS>;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);   // S^T, dP^T
   constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);  // dK, dV (B MN-major)
+  static_assert(NWG == 2 || NWG == 4, "two or four compute warpgroups");
+  // Column of the packed P^T / dS^T of queries [16kk, 16kk + 16) inside a tile's S^T / dP^T:
+  // two warpgroups (one per tile) write halves h at [16h, 16h + 16); four (two per tile, one per
+  // 32-query half) write half h at [32h, 32h + 16), inside the range that warpgroup loaded itself.
+  auto pcol = [](int kk) -> uint32_t { return NWG == 4 ? 32 * (kk >> 1) + 8 * (kk & 1) : 8 * kk; };
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5];
@@ -172,7 +181,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SPFULL(b), 1);
-      mbar_init(BAR_PDSFULL(b), 128);
+      mbar_init(BAR_PDSFULL(b), 64 * NWG);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -265,18 +274,18 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
           const uint32_t pt = tmem + 128 * (i & 1), dst = pt + 64;
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // dK += dS^T Q   (K = 64 queries)
-            mma_ts_if(leader, tmem + 256, dst + kk * 8, smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
+            mma_ts_if(leader, tmem + 256, dst + pcol(kk), smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
                    (i > 0 || kk > 0) ? 1u : 0u);
           if (VK) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dK += P^T dO[:, :128]  (value gradient of the K columns)
-              mma_ts_if(leader, tmem + 256, pt + kk * 8, smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
+              mma_ts_if(leader, tmem + 256, pt + pcol(kk), smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
           }
           if (C::HAS_DV) {
             const uint32_t vo = VK ? 2 * kAtom64 : 0;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dV += P^T dO[:, cols]
-              mma_ts_if(leader, tmem + 384, pt + kk * 8, smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
+              mma_ts_if(leader, tmem + 384, pt + pcol(kk), smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
                      (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit_if(leader, BAR_QEMPTY(s));
@@ -292,8 +301,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
     }
   } else {
     // ---------------------------------------------------------------- compute: thread = key row
-    // two warpgroups: WG w owns the query tiles i = w, w+2, ... and TMEM buffer w
+    // stream st = tile parity (TMEM buffer st); with four warpgroups two share a stream and each
+    // takes one 32-query half of every tile
     const int wg = (warp - 2) >> 2;
+    const int stm = NWG == 4 ? wg >> 1 : wg;
+    const int h0 = NWG == 4 ? (wg & 1) : 0, h1 = NWG == 4 ? h0 + 1 : 2;
     const int quad = warp & 3;
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -301,27 +313,27 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
       const bool mine = mbar_wait(bar, parity, abort, &g_bwd_err, code);
       return __all_sync(0xffffffffu, mine);
     };
-    const uint32_t ts = tmem + lane_off + 128 * wg, tdp = ts + 64;
+    const uint32_t ts = tmem + lane_off + 128 * stm, tdp = ts + 64;
     bool ok = true;
-    for (int i = wg; i < nq; i += 2) {
+    for (int i = stm; i < nq; i += 2) {
       const int s = i % NQS;
-      if (!warp_wait(BAR_SPFULL(wg), (i >> 1) & 1, 8)) { ok = false; break; }
+      if (!warp_wait(BAR_SPFULL(stm), (i >> 1) & 1, 8)) { ok = false; break; }
       if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
       tc_fence_after();
       const uint32_t st = slot_stats(s);
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
-      // two halves of 32 queries: P^T / dS^T of half h go to columns [16h, 16h + 16) of S^T / dP^T,
-      // which half h (or the half before it) has already loaded
+      // 16-query chunks of this warpgroup's half(s): P^T / dS^T of chunk qc go to columns pcol(qc) of
+      // S^T / dP^T, which lie inside what this warpgroup has already loaded
 #pragma unroll 1
-      for (int h = 0; h < 2; ++h) {
-        uint32_t sv[32], dv[32];
-        tmem_ld32(ts + 32 * h, sv);
-        tmem_ld32(tdp + 32 * h, dv);
+      for (int qc = 2 * h0; qc < 2 * h1; ++qc) {  // 16-query chunks: P^T / dS^T of chunk qc -> pcol(qc)
+        uint32_t sv[16], dv[16];
+        tmem_ld16(ts + 16 * qc, sv);
+        tmem_ld16(tdp + 16 * qc, dv);
         tmem_wait_ld();
-        uint32_t pk[16], dk[16];
+        uint32_t pk[8], dk[8];
 #pragma unroll
-        for (int e = 0; e < 32; e += 4) {
-          const uint32_t so = st + 4 * (32 * h + e);
+        for (int e = 0; e < 16; e += 4) {
+          const uint32_t so = st + 4 * (16 * qc + e);
           float4 l4, c4, g4;
           asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(l4.x), "=f"(l4.y), "=f"(l4.z), "=f"(l4.w) : "r"(so));
           asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];" : "=f"(c4.x), "=f"(c4.y), "=f"(c4.z), "=f"(c4.w) : "r"(so + 256));
@@ -331,28 +343,32 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dkdv_kernel(const __grid_
           prob_dscore<T, true>(sv[e + 2], sv[e + 3], dv[e + 2], dv[e + 3], sc2, sm2, make_float2(l4.z, l4.w),
                                make_float2(c4.z, c4.w), make_float2(g4.z, g4.w), pk[(e >> 1) + 1], dk[(e >> 1) + 1]);
         }
-        tmem_st16(ts + 16 * h, pk);
-        tmem_st16(tdp + 16 * h, dk);
+        tmem_st8(ts + pcol(qc), pk);
+        tmem_st8(tdp + pcol(qc), dk);
       }
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(BAR_PDSFULL(wg));
+      mbar_arrive(BAR_PDSFULL(stm));
     }
     if (ok) ok = warp_wait(BAR_DONE, 0, 8);
     tc_fence_after();
-    // epilogue: stage dK (and dV) in the idle query slots, one thread writes them with TMA; WG 0
-    // stages dK, WG 1 dV (or, without dV, the second half of dK)
+    // epilogue: stage dK (and dV) in the idle query slots, one thread writes them with TMA. The
+    // warpgroups split the 32-column chunks: with dV, the first half of them stages dK, the second
+    // dV; without, all stage dK.
     const uint32_t stage0 = sSlots, stage1 = sSlots + 65536;
     if (ok) {
       if (C::HAS_DV) {
-        if (wg == 0) stage_acc_rows<T>(tmem + lane_off + 256, stage0, row, p.acc, 0, 4);
-        else stage_acc_rows<T>(tmem + lane_off + 384, stage1, row, p.acc, 0, 4);
+        constexpr int CPW = 8 / NWG;  // chunks per warpgroup
+        const int mat = wg / (NWG / 2), c0 = CPW * (wg % (NWG / 2));
+        if (mat == 0) stage_acc_rows<T>(tmem + lane_off + 256, stage0, row, p.acc, c0, c0 + CPW);
+        else stage_acc_rows<T>(tmem + lane_off + 384, stage1, row, p.acc, c0, c0 + CPW);
       } else {
-        stage_acc_rows<T>(tmem + lane_off + 256, stage0, row, p.acc, 2 * wg, 2 * wg + 2);
+        constexpr int CPW = 4 / NWG;
+        stage_acc_rows<T>(tmem + lane_off + 256, stage0, row, p.acc, CPW * wg, CPW * (wg + 1));
       }
     }
     fence_proxy_async_smem();
-    ok = named_bar_and(1, 256, ok);
+    ok = named_bar_and(1, 128 * NWG, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
       issue_grad_tile(&p.tm_g0, stage0, k0, bi, p.acc);
       if (C::HAS_DV) issue_grad_tile(&p.tm_g1, stage1, k0, bi, p.acc);
@@ -390,8 +406,8 @@ struct DqCfg2 {
   static_assert((XA == 0) == (NX == 0), "X ring present exactly when there is an X tile");
 };
 
-template <typename T, int XA, bool VK, bool DOT, int NK, int NX>
-__global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid_constant__ Sm100BwdParams p) {
+template <typename T, int XA, bool VK, bool DOT, int NK, int NX, int NWG>
+__global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const __grid_constant__ Sm100BwdParams p) {
   using C = DqCfg2<XA, VK, DOT, NK, NX>;
   constexpr int NS = C::NS;
   constexpr int NXB = NX > 0 ? NX : 1;
@@ -399,6 +415,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
   constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
   constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 128, false, true);
   constexpr uint32_t T_DP = DOT ? 128 : 256, T_DO = 256, T_DQ = 384;
+  constexpr int CW = 128 / NWG;          // key columns of a tile per compute warpgroup
+  constexpr int NCT = 128 * NWG;         // compute threads
   constexpr int B_Q = 0, B_KFULL = 1, B_KEMPTY = B_KFULL + NK, B_XFULL = B_KEMPTY + NK, B_XEMPTY = B_XFULL + NXB;
   constexpr int B_SFULL = B_XEMPTY + NXB, B_DSFULL = B_SFULL + NS, B_DPFULL = B_DSFULL + NS;
   constexpr int B_DPFREE = B_DPFULL + 1, B_DOT = B_DPFREE + 1, B_DONE = B_DOT + 1, NBARS = B_DONE + 1;
@@ -433,11 +451,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
     }
     for (int b = 0; b < NS; ++b) {
       mbar_init(BAR(B_SFULL + b), 1);
-      mbar_init(BAR(B_DSFULL + b), 256);
+      mbar_init(BAR(B_DSFULL + b), NCT);
     }
     mbar_init(BAR(B_DPFULL), 1);
-    mbar_init(BAR(B_DPFREE), 256);
-    mbar_init(BAR(B_DOT), 256);
+    mbar_init(BAR(B_DPFREE), NCT);
+    mbar_init(BAR(B_DOT), NCT);
     mbar_init(BAR(B_DONE), 1);
     fence_mbar_init();
   }
@@ -553,8 +571,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
           const uint32_t kb = sK + (j % NK) * C::KSLOT;
           const uint32_t sb = tmem + 128u * (uint32_t)(j % NS);
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K ; keys [16kk, 16kk+16) of warpgroup kk/4
-            const uint32_t a_tm = sb + (kk < 4 ? kk * 8 : 64 + (kk - 4) * 8);
+          for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K ; keys [16kk, 16kk+16) of warpgroup 16kk/CW
+            const uint32_t a_tm = sb + CW * (16 * kk / CW) + (16 * kk % CW) / 2;
             mma_ts_if(leader, tmem + T_DQ, a_tm, smem_desc_sw128(kb + kk * 2048, kAtom128, 1024), IDESC_DQ,
                    (j > 0 || kk > 0) ? 1u : 0u);
           }
@@ -587,20 +605,23 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
     };
     bool ok = true;
     if (DOT) {
-      // dO row -> TMEM (bf16 pairs): warpgroup w stages elements [128w, 128w+128)
-      uint32_t w32[64];
+      // dO row -> TMEM (bf16 pairs): warpgroup w stages elements [EW w, EW w + EW)
+      constexpr int EW = C::DW / NWG;  // elements per warpgroup (EW / 2 TMEM columns)
       const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) + (int64_t)bi * p.do_bs +
-                                                        (int64_t)(qok ? q : 0) * C::DW + 128 * wg);
+                                                        (int64_t)(qok ? q : 0) * C::DW + EW * wg);
 #pragma unroll
-      for (int i = 0; i < 16; ++i) {
-        const uint4 v = qok ? src[i] : make_uint4(0, 0, 0, 0);
-        w32[4 * i] = v.x;
-        w32[4 * i + 1] = v.y;
-        w32[4 * i + 2] = v.z;
-        w32[4 * i + 3] = v.w;
+      for (int h = 0; h < EW / 64; ++h) {
+        uint32_t w32[32];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          const uint4 v = qok ? src[8 * h + i] : make_uint4(0, 0, 0, 0);
+          w32[4 * i] = v.x;
+          w32[4 * i + 1] = v.y;
+          w32[4 * i + 2] = v.z;
+          w32[4 * i + 3] = v.w;
+        }
+        tmem_st32(tmem + lane_off + T_DO + EW / 2 * wg + 32 * h, w32);
       }
-      tmem_st32(tmem + lane_off + T_DO + 64 * wg, w32);
-      tmem_st32(tmem + lane_off + T_DO + 64 * wg + 32, w32 + 32);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR(B_DOT));
@@ -610,33 +631,35 @@ __global__ void __launch_bounds__(kThreads, 1) fea_bwd_dq128_kernel(const __grid
       if (!warp_wait(BAR(B_SFULL + b), (j / NS) & 1, 128)) { ok = false; break; }
       if (!warp_wait(BAR(B_DPFULL), j & 1, 128)) { ok = false; break; }
       tc_fence_after();
-      const uint32_t ts = tmem + lane_off + 128u * (uint32_t)b + 64 * wg;
-      const uint32_t tdp = tmem + lane_off + T_DP + 64 * wg;
-      uint32_t sv[64], dv[64];
-      tmem_ld32(ts, sv);
-      tmem_ld32(ts + 32, sv + 32);
-      tmem_ld32(tdp, dv);
-      tmem_ld32(tdp + 32, dv + 32);
+      const uint32_t ts = tmem + lane_off + 128u * (uint32_t)b + CW * wg;
+      const uint32_t tdp = tmem + lane_off + T_DP + CW * wg;
+      uint32_t sv[CW], dv[CW];
+#pragma unroll
+      for (int c = 0; c < CW / 32; ++c) {
+        tmem_ld32(ts + 32 * c, sv + 32 * c);
+        tmem_ld32(tdp + 32 * c, dv + 32 * c);
+      }
       tmem_wait_ld();
       tc_fence_before();
       mbar_arrive(BAR(B_DPFREE));
-      uint32_t pk[32];
+      uint32_t pk[CW / 2];
 #pragma unroll
-      for (int e = 0; e < 64; e += 2) {
+      for (int e = 0; e < CW; e += 2) {
         uint32_t unused;
         prob_dscore<T, false>(sv[e], sv[e + 1], dv[e], dv[e + 1], sc2, sm2, nl2, nc2, ng2, unused, pk[e >> 1]);
       }
-      tmem_st32(ts, pk);
+      if (CW == 64) tmem_st32(ts, pk);
+      else tmem_st16(ts, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR(B_DSFULL + b));
     }
     if (ok) ok = warp_wait(BAR(B_DONE), 0, 128);
     tc_fence_after();
-    // epilogue: stage dQ in the idle K ring (WG w: columns [64w, 64w + 64)), one thread writes it
-    if (ok) stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc, 2 * wg, 2 * wg + 2);
+    // epilogue: stage dQ in the idle K ring (WG w: columns [CW w, CW w + CW)), one thread writes it
+    if (ok) stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc, (CW / 32) * wg, (CW / 32) * (wg + 1));
     fence_proxy_async_smem();
-    ok = named_bar_and(1, 256, ok);
+    ok = named_bar_and(1, NCT, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
       issue_grad_tile(&p.tm_g0, sK, q0, bi, p.acc);
       tma_store_commit_and_wait();
@@ -697,11 +720,11 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   cudaError_t e;
   const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
   if (vk && xa > 0) {
-    e = run(fea_bwd_dkdv_kernel<T, 2, true, 3>, DkdvCfg<2, true, 3>::SMEM, blocks_a, kThreads, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 2, true, 3, kDkdvWarpgroups>, DkdvCfg<2, true, 3>::SMEM, blocks_a, kDkdvThreads, pa, st);
   } else if (vk) {
-    e = run(fea_bwd_dkdv_kernel<T, 0, true, 5>, DkdvCfg<0, true, 5>::SMEM, blocks_a, kThreads, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 0, true, 5, kDkdvWarpgroups>, DkdvCfg<0, true, 5>::SMEM, blocks_a, kDkdvThreads, pa, st);
   } else {
-    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4>, DkdvCfg<2, false, 4>::SMEM, blocks_a, kThreads, pa, st);
+    e = run(fea_bwd_dkdv_kernel<T, 2, false, 4, kDkdvWarpgroups>, DkdvCfg<2, false, 4>::SMEM, blocks_a, kDkdvThreads, pa, st);
   }
   if (e != cudaSuccess) return e;
   // ---- dQ: 128-key tiles (dO staged in TMEM when it is 256 wide)
@@ -729,12 +752,12 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pb.sm_scale = b.sm_scale;
   const int64_t blocks_b = (int64_t)pb.n_tiles * batch;
   if (vk && xa == 0)
-    return run(fea_bwd_dq128_kernel<T, 0, true, false, 5, 0>, DqCfg2<0, true, false, 5, 0>::SMEM, blocks_b, kThreads,
+    return run(fea_bwd_dq128_kernel<T, 0, true, false, 5, 0, kDqWarpgroups>, DqCfg2<0, true, false, 5, 0>::SMEM, blocks_b, kDqThreads,
                pb, st);
   if (vk)
-    return run(fea_bwd_dq128_kernel<T, 2, true, true, 3, 3>, DqCfg2<2, true, true, 3, 3>::SMEM, blocks_b, kThreads,
+    return run(fea_bwd_dq128_kernel<T, 2, true, true, 3, 3, kDqWarpgroups>, DqCfg2<2, true, true, 3, 3>::SMEM, blocks_b, kDqThreads,
                pb, st);
-  return run(fea_bwd_dq128_kernel<T, 2, false, false, 3, 2>, DqCfg2<2, false, false, 3, 2>::SMEM, blocks_b, kThreads,
+  return run(fea_bwd_dq128_kernel<T, 2, false, false, 3, 2, kDqWarpgroups>, DqCfg2<2, false, false, 3, 2>::SMEM, blocks_b, kDqThreads,
              pb, st);
 }
 
