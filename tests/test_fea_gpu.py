@@ -113,3 +113,37 @@ def test_growing_row_max_forces_rescales(D, Dv):
     v = torch.randn(1, 2, N, Dv, generator=gen).bfloat16().float()
     do, de = torch.randn(1, 2, N, Dv, generator=gen), torch.randn(1, 2, N, generator=gen)
     check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
+
+
+def test_split_key_range_backward_matches_and_is_deterministic():
+    # Few query tiles over a long key range: in fp32-accumulate mode the dQ kernel splits the key
+    # range over several CTAs (partial tiles summed in a fixed order). Check it against the
+    # unsplit 16-bit mode and that two runs are bitwise identical.
+    from vmonarch_b200 import _native as N, ops
+    import ctypes
+    gen = torch.Generator().manual_seed(21)
+    B, nq, nk, D = 2, 128, 4096, 128
+    q = torch.randn(B, nq, D, generator=gen).bfloat16().cuda()
+    k, v = (torch.randn(B, nk, D, generator=gen).bfloat16().cuda() for _ in range(2))
+    do = torch.randn(B, nq, D, generator=gen).bfloat16().cuda()
+    de = torch.randn(B, nq, generator=gen).cuda()
+    sm = D ** -0.5
+    o = torch.empty_like(q)
+    lse, ent = torch.empty(B, nq, device="cuda"), torch.empty(B, nq, device="cuda")
+    ops.fea_fwd(q, k, v, o, lse, ent, sm)
+    a = N.FeaBwdArgs()
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1, a.grad_mode = B, nq, nk, D, D, D, 1
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) > 3 * B * 128 * 4 * 2  # partial tiles present
+
+    ref = [torch.empty_like(t) for t in (q, k, v)]
+    ops.fea_bwd(q, k, v, o, do, lse, *ref, sm, ent=ent, dent=de, grad_mode=0)
+    runs = []
+    for _ in range(2):
+        acc = [torch.zeros(t.shape, device="cuda") for t in (q, k, v)]
+        ops.fea_bwd(q, k, v, o, do, lse, *acc, sm, ent=ent, dent=de, grad_mode=1)
+        runs.append(acc)
+    torch.cuda.synchronize()
+    for g, r in zip(runs[0], ref):
+        assert max_rel_err(g, r.float()) <= 1e-2
+    for g0, g1 in zip(*runs):
+        assert torch.equal(g0, g1)

@@ -110,15 +110,23 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   return cuda_status(vmb::fea_fwd_mma(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, st), "vmb_fea_fwd");
 }
 
-// Workspace: the tcgen05 path keeps three folded statistics planes [batch][round_up(n_q, 128)];
-// the mma.sync path keeps c and g [batch][n_q] and, in grad_mode 0, an fp32 dQ accumulator.
+// Workspace: the tcgen05 path keeps three folded statistics planes [batch][round_up(n_q, 128)]
+// and, when its dQ kernel splits the key range (long keys, few query tiles, grad_mode 1), the
+// partial dQ tiles [split][batch][round_up(n_q, 128)][128]; the mma.sync path keeps c and g
+// [batch][n_q] and, in grad_mode 0, an fp32 dQ accumulator.
 static bool bwd_uses_sm100(const vmb_fea_bwd_args* a) {
   return vmb::fea_bwd_sm100_supported(a->d, a->dv, a->dv1, a->v_is_k != 0);
 }
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
   if (!a || a->batch < 0 || a->n_q < 0) return -1;
-  if (bwd_uses_sm100(a)) return 3 * round_up(a->batch * round_up(a->n_q, 128) * 4, 256);
+  if (bwd_uses_sm100(a)) {
+    const int64_t n_pad = round_up(a->n_q, 128);
+    int64_t bytes = 3 * round_up(a->batch * n_pad * 4, 256);
+    const int split = vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode == 1);
+    if (split > 1) bytes += round_up((int64_t)split * a->batch * n_pad * 128 * 4, 256);
+    return bytes;
+  }
   const int64_t rows = a->batch * a->n_q;
   int64_t bytes = 2 * round_up(rows * 4, 256);
   if (a->grad_mode == 0) bytes += round_up(rows * a->d * 4, 256);
@@ -174,6 +182,9 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   vmb::BwdParams p{};
   p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.dout = a->dout; p.lse = a->lse; p.cc = cc; p.gg = gg;
   p.fold = fold; p.n_pad = n_pad;
+  p.dq_part = nullptr;
+  if (sm100 && vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode == 1) > 1)
+    p.dq_part = reinterpret_cast<float*>(ws + 3 * round_up(a->batch * n_pad * 4, 256));
   p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
   p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
   p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.do_bs = a->do_bs;

@@ -20,6 +20,8 @@
 // Both write their gradients directly (bf16, or added into fp32 accumulators in grad_mode 1).
 // Tails: rows past n_q / n_kv load as zeros (TMA), query statistics past n_q are (+inf, 0, 0) so
 // their P is 0; gradients are only stored for valid rows. Every wait is bounded (sm100.cuh).
+#include <algorithm>
+
 #include "common.cuh"
 #include "fea_params.h"
 #include "launch.h"
@@ -53,7 +55,9 @@ struct Sm100BwdParams {
   const float* ng;  //   -sm_scale g
   int64_t n_pad;
   int n_q, n_kv, n_tiles;
-  int acc;       // 1: gradients are fp32 buffers added into (TMA reduce-add), else 16-bit stores
+  int k_split, kt_per;  // dQ kernel: key range split over k_split CTAs of kt_per 128-key tiles each
+  int n_seq;            // sequences (batch) of the call
+  int acc;       // 1: fp32 gradients added into (TMA reduce-add); 2: fp32 stores; 0: 16-bit stores
   float scale_log2, sm_scale;
 };
 
@@ -95,9 +99,12 @@ __device__ __forceinline__ void stage_acc_rows(uint32_t taddr, uint32_t stage, i
 }
 
 // One thread, after the staging barrier: the whole 128-row tile starting at row0 of sequence bi.
-__device__ __forceinline__ void issue_grad_tile(const CUtensorMap* tm, uint32_t stage, int row0, int bi, bool f32) {
-  if (f32) {
+// mode 1: fp32 reduce-add; 2: fp32 store; 0: 16-bit store.
+__device__ __forceinline__ void issue_grad_tile(const CUtensorMap* tm, uint32_t stage, int row0, int bi, int mode) {
+  if (mode == 1) {
     for (int c = 0; c < 4; ++c) tma_reduce_add_3d(tm, 32 * c, row0, bi, stage + c * 16384);
+  } else if (mode == 2) {
+    for (int c = 0; c < 4; ++c) tma_store_3d(tm, 32 * c, row0, bi, stage + c * 16384);
   } else {
     for (int a = 0; a < 2; ++a) tma_store_3d(tm, 64 * a, row0, bi, stage + a * 16384);
   }
@@ -427,9 +434,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   __shared__ int abort_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bi = blockIdx.x / p.n_tiles;
-  const int q0 = (blockIdx.x % p.n_tiles) * 128;
-  const int nk = (p.n_kv + 127) / 128;
+  // block -> (sequence, query tile, key chunk); chunks of one query tile add their partial dQ
+  const int per_seq = p.n_tiles * p.k_split;
+  const int bi = blockIdx.x / per_seq;
+  const int q0 = ((blockIdx.x % per_seq) / p.k_split) * 128;
+  const int kt0 = (blockIdx.x % p.k_split) * p.kt_per;  // first key tile of this chunk
+  const int nk = min((p.n_kv + 127) / 128 - kt0, p.kt_per);  // >= 1 by the host's choice of split
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = sbase, sDO = sbase + 2 * kAtom128;
@@ -487,15 +497,15 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         const int s = j % NK;
         if (j >= NK && !mbar_wait(BAR(B_KEMPTY + s), ((j / NK) - 1) & 1, abort, &g_bwd_err, 16)) break;
         mbar_expect_tx(BAR(B_KFULL + s), C::KSLOT);
-        tma_load_3d(sK + s * C::KSLOT, &p.tm_c, 0, j * 128, bi, BAR(B_KFULL + s));
-        tma_load_3d(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, j * 128, bi, BAR(B_KFULL + s));
+        tma_load_3d(sK + s * C::KSLOT, &p.tm_c, 0, (kt0 + j) * 128, bi, BAR(B_KFULL + s));
+        tma_load_3d(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, (kt0 + j) * 128, bi, BAR(B_KFULL + s));
         karmed[s] = j / NK + 1;
         if (XA > 0) {
           const int x = j % NXB;
           if (j >= NXB && !mbar_wait(BAR(B_XEMPTY + x), ((j / NXB) - 1) & 1, abort, &g_bwd_err, 16)) break;
           mbar_expect_tx(BAR(B_XFULL + x), C::XSLOT);
           for (int a = 0; a < XA; ++a)
-            tma_load_3d(sX + x * C::XSLOT + a * kAtom128, &p.tm_d, 64 * a, j * 128, bi, BAR(B_XFULL + x));
+            tma_load_3d(sX + x * C::XSLOT + a * kAtom128, &p.tm_d, 64 * a, (kt0 + j) * 128, bi, BAR(B_XFULL + x));
           xarmed[x] = j / NXB + 1;
         }
       }
@@ -657,11 +667,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
     if (ok) ok = warp_wait(BAR(B_DONE), 0, 128);
     tc_fence_after();
     // epilogue: stage dQ in the idle K ring (WG w: columns [CW w, CW w + CW)), one thread writes it
-    if (ok) stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc, (CW / 32) * wg, (CW / 32) * (wg + 1));
+    if (ok) stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc != 0, (CW / 32) * wg, (CW / 32) * (wg + 1));
     fence_proxy_async_smem();
     ok = named_bar_and(1, NCT, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      issue_grad_tile(&p.tm_g0, sK, q0, bi, p.acc);
+      // a split key range writes its partial tile into its own slice: sequence index chunk * batch + bi
+      issue_grad_tile(&p.tm_g0, sK, q0, p.k_split > 1 ? (kt0 / p.kt_per) * p.n_seq + bi : bi, p.acc);
       tma_store_commit_and_wait();
     }
   }
@@ -670,6 +681,26 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// dq[bi][q] += sum over chunks c (in order) of part[c][bi][q]: the split key ranges' partial tiles
+__global__ void dq_split_reduce_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q, float* dq,
+                                       int64_t dq_bs) {
+  const int64_t total = batch * n_q * 32;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
+    const int64_t q = rem / 32, c4 = rem % 32;
+    float4* dst = reinterpret_cast<float4*>(dq + bi * dq_bs + q * 128) + c4;
+    float4 acc = *dst;
+    for (int c = 0; c < split; ++c) {
+      const float4 v = reinterpret_cast<const float4*>(part + (((int64_t)c * batch + bi) * n_pad + q) * 128)[c4];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    *dst = acc;
+  }
 }
 
 // ================================================================================ host side
@@ -743,25 +774,71 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pb.nc = b.fold + batch * b.n_pad;
   pb.ng = b.fold + 2 * batch * b.n_pad;
   pb.n_pad = b.n_pad;
-  if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q)) return cudaErrorInvalidValue;
+  pb.n_seq = (int)batch;
+  {
+    const int nkt = (b.n_kv + 127) / 128;
+    pb.k_split = fea_bwd_dq_split(batch, b.n_q, b.n_kv, b.acc_q != 0);
+    pb.kt_per = (nkt + pb.k_split - 1) / pb.k_split;
+  }
+  if (pb.k_split > 1) {
+    // each key chunk stores its partial dQ tile into slice [chunk][batch] of the workspace; a
+    // fixed-order sum adds them into dQ afterwards (deterministic, unlike concurrent reduce-adds)
+    if (!b.dq_part || !tma::make_map_f32(&pb.tm_g0, b.dq_part, 128, b.n_pad, (int64_t)pb.k_split * batch,
+                                         b.n_pad * 128, 128))
+      return cudaErrorInvalidValue;
+  } else if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q)) {
+    return cudaErrorInvalidValue;
+  }
   pb.n_q = b.n_q;
   pb.n_kv = b.n_kv;
   pb.n_tiles = (b.n_q + 127) / 128;
-  pb.acc = b.acc_q;
+  pb.acc = pb.k_split > 1 ? 2 : b.acc_q;
   pb.scale_log2 = b.scale_log2;
   pb.sm_scale = b.sm_scale;
-  const int64_t blocks_b = (int64_t)pb.n_tiles * batch;
+  const int64_t blocks_b = (int64_t)pb.n_tiles * pb.k_split * batch;
   if (vk && xa == 0)
-    return run(fea_bwd_dq128_kernel<T, 0, true, false, 5, 0, kDqWarpgroups>, DqCfg2<0, true, false, 5, 0>::SMEM, blocks_b, kDqThreads,
-               pb, st);
-  if (vk)
-    return run(fea_bwd_dq128_kernel<T, 2, true, true, 3, 3, kDqWarpgroups>, DqCfg2<2, true, true, 3, 3>::SMEM, blocks_b, kDqThreads,
-               pb, st);
-  return run(fea_bwd_dq128_kernel<T, 2, false, false, 3, 2, kDqWarpgroups>, DqCfg2<2, false, false, 3, 2>::SMEM, blocks_b, kDqThreads,
-             pb, st);
+    e = run(fea_bwd_dq128_kernel<T, 0, true, false, 5, 0, kDqWarpgroups>, DqCfg2<0, true, false, 5, 0>::SMEM, blocks_b,
+            kDqThreads, pb, st);
+  else if (vk)
+    e = run(fea_bwd_dq128_kernel<T, 2, true, true, 3, 3, kDqWarpgroups>, DqCfg2<2, true, true, 3, 3>::SMEM, blocks_b,
+            kDqThreads, pb, st);
+  else
+    e = run(fea_bwd_dq128_kernel<T, 2, false, false, 3, 2, kDqWarpgroups>, DqCfg2<2, false, false, 3, 2>::SMEM, blocks_b,
+            kDqThreads, pb, st);
+  if (e != cudaSuccess || pb.k_split == 1) return e;
+  const int64_t total = batch * b.n_q * 32;  // float4s of the valid dQ rows
+  const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
+  dq_split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.dq,
+                                                           b.dq_bs);
+  return cudaGetLastError();
 }
 
 }  // namespace
+
+int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc) {
+  // Split the key range when the query tiles alone fill the GPU poorly (few, long CTAs). Chosen
+  // to minimise waves x (key tiles per CTA + ~3 tiles of fixed cost); only the fp32-accumulate
+  // mode splits (its partial tiles are summed into the fp32 gradient).
+  if (!acc || batch <= 0 || n_q <= 0) return 1;
+  const int64_t n_tiles = (n_q + 127) / 128;
+  const int nkt = (n_kv + 127) / 128;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  int best = 1;
+  int64_t best_cost = 0;
+  for (int ks = 1; ks <= 8; ++ks) {
+    const int per = (nkt + ks - 1) / ks;
+    if ((ks - 1) * per >= nkt) break;  // every chunk owns at least one key tile
+    const int64_t waves = (n_tiles * batch * ks + sms - 1) / sms;
+    const int64_t cost = waves * (per + 3);
+    if (ks == 1 || cost * 100 < best_cost * 97) {
+      best = ks;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {
   if (d != 128) return false;

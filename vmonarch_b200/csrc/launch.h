@@ -29,6 +29,10 @@ cudaError_t fea_fwd_sm100(const FwdParams& p, int64_t batch, int d, int dv, bool
 cudaError_t fea_fwd_sm100_status(cudaStream_t st, int* out);
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk);
 cudaError_t fea_bwd_sm100(const BwdParams& p, int64_t batch, int dv, bool vk, bool bf16, cudaStream_t st);
+// Number of CTAs sharing one query tile's key range in the tcgen05 dQ kernel (1 = no split; only
+// the accumulate mode splits). The partial tiles need split * batch * round_up(n_q, 128) * 128
+// fp32 of workspace when the result is above 1.
+int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc);
 cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out);
 cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
