@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VMB_ABI_VERSION 1
+#define VMB_ABI_VERSION 2
 
 #define VMB_DTYPE_BF16 0
 #define VMB_DTYPE_F16 1
@@ -64,6 +64,13 @@ uint64_t vmb_kernel_launches(void);
  * Shapes: d in {64, 128}; dv in {64, 128, 256} with dv a multiple of d (the reference requires
  * Dv % D == 0 for its backward, kernel.py:260). o may be a strided view (o_bs) into a larger
  * tensor, which is how the exact first-frame recompute writes straight into z.
+ * workspace / workspace_bytes are optional (NULL / 0 is valid). With a workspace of
+ * vmb_fea_fwd_workspace_bytes() bytes the d = dv = 128 kernel may split each sequence's key range
+ * over several CTAs when the query tiles alone would fill the GPU poorly (few, long sequences, e.g.
+ * the recompute's r queries over all N keys on a few heads); the partial results are merged
+ * exactly by a second kernel. Without one, or when no split pays off, nothing changes. The
+ * workspace contents need not be initialised; it is 256-byte aligned when obtained from a
+ * caching allocator (16 bytes is required).
  */
 typedef struct vmb_fea_fwd_args {
   const void* q;  int64_t q_bs;   /* [batch][n_q][d]                               */
@@ -76,8 +83,12 @@ typedef struct vmb_fea_fwd_args {
   int64_t batch, n_q, n_kv;
   int32_t d, dv, dv1, dtype;
   float sm_scale;
+  void* workspace;  int64_t workspace_bytes;  /* optional, see above (ABI version 2) */
 } vmb_fea_fwd_args;
 
+/* Workspace that lets vmb_fea_fwd split long key ranges (0 when it would not split). No
+ * counterpart in the reference, whose forward launch allocates through torch. */
+int64_t vmb_fea_fwd_workspace_bytes(const vmb_fea_fwd_args* a);
 int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream);
 
 /*

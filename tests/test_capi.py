@@ -20,7 +20,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_abi():
     assert N.LIB_PATH.exists()
-    assert N.lib.vmb_abi_version() == 1
+    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 2
 
 
 def test_every_declared_symbol_is_exported_and_bound():
@@ -132,3 +132,20 @@ def test_lstep_validation():
     assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 1
     assert N.lib.vmb_lstep_bwd(ctypes.byref(a), None) == 1     # no gradients given
     assert N.lib.vmb_cast_f32(None, 0, None, 0, 1, 6, 0, None) == 1
+
+
+def test_fea_fwd_workspace_query():
+    # The workspace only exists for the d = dv = 128 kernel when a key-range split pays off: few
+    # query tiles over many keys. Many query tiles, other head dims and empty calls need none.
+    a = N.FeaFwdArgs()
+    a.q, a.k, a.v = 256, 512, 768
+    a.q_bs = a.k_bs = a.v_bs = 0
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 2, 128, 32768, 128, 128, 128
+    assert N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a)) > 0
+    a.batch, a.n_q, a.n_kv = 840, 1560, 1560
+    assert N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a)) == 0
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 2, 128, 32768, 64, 64, 64
+    assert N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a)) == 0
+    a.n_q = 0
+    assert N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a)) == 0
+    assert N.lib.vmb_fea_fwd_workspace_bytes(None) == -1

@@ -25,6 +25,9 @@ c_vp = ctypes.c_void_p
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 
+ABI_VERSION = 2  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+
+
 class FeaFwdArgs(ctypes.Structure):
     _fields_ = [
         ("q", c_vp), ("q_bs", c_i64),
@@ -36,6 +39,7 @@ class FeaFwdArgs(ctypes.Structure):
         ("batch", c_i64), ("n_q", c_i64), ("n_kv", c_i64),
         ("d", c_i32), ("dv", c_i32), ("dv1", c_i32), ("dtype", c_i32),
         ("sm_scale", ctypes.c_float),
+        ("workspace", c_vp), ("workspace_bytes", c_i64),
     ]
 
 
@@ -79,6 +83,7 @@ SIGNATURES = {
     "vmb_last_error": (ctypes.c_char_p, []),
     "vmb_kernel_launches": (ctypes.c_uint64, []),
     "vmb_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int32)]),
+    "vmb_fea_fwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaFwdArgs)]),
     "vmb_fea_fwd": (ctypes.c_int, [ctypes.POINTER(FeaFwdArgs), c_vp]),
     "vmb_fea_bwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaBwdArgs)]),
     "vmb_fea_bwd": (ctypes.c_int, [ctypes.POINTER(FeaBwdArgs), c_vp]),
@@ -94,6 +99,10 @@ def _load() -> ctypes.CDLL:
         raise ImportError(
             f"vmonarch_b200: CUDA library {LIB_PATH} is missing; build it with `python vmonarch_b200/build.py`")
     lib = ctypes.CDLL(str(LIB_PATH))
+    lib.vmb_abi_version.restype = ctypes.c_int
+    if lib.vmb_abi_version() != ABI_VERSION:
+        raise ImportError(f"vmonarch_b200: {LIB_PATH} has ABI version {lib.vmb_abi_version()}, the binding expects "
+                          f"{ABI_VERSION}; rebuild it with `python vmonarch_b200/build.py`")
     for name, (res, args) in SIGNATURES.items():
         fn = getattr(lib, name)
         fn.restype = res

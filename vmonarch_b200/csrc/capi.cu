@@ -85,6 +85,17 @@ int vmb_device_status(void* stream, int32_t* out) {
   return VMB_OK;
 }
 
+static bool fwd_v_is_k(const vmb_fea_fwd_args* a) {
+  return a->v == a->k && a->v_bs == a->k_bs && a->dv1 == a->d;
+}
+
+int64_t vmb_fea_fwd_workspace_bytes(const vmb_fea_fwd_args* a) {
+  if (!a || a->batch < 0 || a->n_q < 0 || a->n_kv < 1) return -1;
+  if (a->batch == 0 || a->n_q == 0 || a->n_q > 0x7fffffff || a->n_kv > 0x7fffffff) return 0;
+  return vmb::fea_fwd_sm100_workspace_bytes(a->batch, (int)a->n_q, (int)a->n_kv, a->d, a->dv, a->dv1,
+                                            fwd_v_is_k(a));
+}
+
 int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   if (!a) return fail(VMB_EINVAL, "vmb_fea_fwd: null args");
   int rc = check_common("vmb_fea_fwd", a->batch, a->n_q, a->n_kv, a->d, a->dv, a->dv1, a->dtype, a->v2);
@@ -95,18 +106,25 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
     return fail(VMB_EINVAL, "vmb_fea_fwd: tensors must be 16-byte aligned");
   if ((a->q_bs | a->k_bs | a->v_bs | a->o_bs | a->v2_bs) & 7)
     return fail(VMB_EINVAL, "vmb_fea_fwd: batch strides must be multiples of 8 elements");
+  if (a->workspace && (!aligned16(a->workspace) || a->workspace_bytes < 0))
+    return fail(VMB_EINVAL, "vmb_fea_fwd: workspace must be 16-byte aligned");
   vmb::FwdParams p{};
   p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.o = a->o; p.lse = a->lse; p.ent = a->ent;
   p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.o_bs = a->o_bs;
   p.n_q = (int)a->n_q; p.n_kv = (int)a->n_kv; p.dv1 = a->dv1;
   p.scale_log2 = a->sm_scale * kLog2eHost;
+  p.work = a->workspace;
+  p.work_bytes = a->workspace ? a->workspace_bytes : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
   // V aliasing K (the VMonarch R step): the key tile in shared memory doubles as the value tile
-  const bool vk = a->v == a->k && a->v_bs == a->k_bs && a->dv1 == a->d;
-  count(1);
-  if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk))
+  const bool vk = fwd_v_is_k(a);
+  if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk)) {
+    // a split key range adds the merge kernel
+    count(vmb::fea_fwd_sm100_split(a->batch, p.n_q, p.n_kv, a->dv, p.work, p.work_bytes) > 1 ? 2 : 1);
     return cuda_status(vmb::fea_fwd_sm100(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, vk, st), "vmb_fea_fwd");
+  }
+  count(1);
   return cuda_status(vmb::fea_fwd_mma(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, st), "vmb_fea_fwd");
 }
 

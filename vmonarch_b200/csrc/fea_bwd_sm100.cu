@@ -832,7 +832,7 @@ int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc) {
     if ((ks - 1) * per >= nkt) break;  // every chunk owns at least one key tile
     const int64_t waves = (n_tiles * batch * ks + sms - 1) / sms;
     const int64_t cost = waves * (per + 3);
-    if (ks == 1 || cost * 100 < best_cost * 97) {
+    if (ks == 1 || cost * 100 < best_cost * 90) {  // a split must gain 10 % (merge pass)
       best = ks;
       best_cost = cost;
     }

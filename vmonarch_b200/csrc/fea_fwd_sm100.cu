@@ -45,9 +45,13 @@ constexpr float kRescaleThreshold = 8.0f;
 
 struct Sm100FwdParams {
   CUtensorMap tm_q, tm_k, tm_x, tm_o;
+  CUtensorMap tm_po;  // key-range split: partial O tiles [split * batch][n_pad][128] fp32 (32 x 128 boxes)
   float* lse;
   float* ent;
+  float* pst;         // key-range split: partial (m, l, h) planes, each [split * batch * n_pad]
   int n_q, n_kv, n_qtiles;
+  int kv_split, kt_per, n_seq;  // split count, key tiles per chunk, sequences of the call
+  int64_t n_pad;      // n_q rounded up to 128
   float scale_log2;
 };
 
@@ -436,9 +440,13 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
   __shared__ int abort_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int bi = blockIdx.x / p.n_qtiles;
-  const int q0 = (blockIdx.x % p.n_qtiles) * 128;
-  const int n_kt = (p.n_kv + 127) / 128;
+  // block -> (sequence, query tile, key chunk); with kv_split == 1 a CTA walks all key tiles
+  const int per_seq = p.n_qtiles * p.kv_split;
+  const int bi = blockIdx.x / per_seq;
+  const int q0 = ((blockIdx.x % per_seq) / p.kv_split) * 128;
+  const int kchunk = blockIdx.x % p.kv_split;
+  const int kt0 = kchunk * p.kt_per;                                  // first key tile of the chunk
+  const int n_kt = min((p.n_kv + 127) / 128 - kt0, p.kt_per);       // >= 1 by the host's choice
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = sbase;
@@ -506,8 +514,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
         const uint32_t full = kl ? BAR_KFULL(s) : BAR_VFULL(s);
         const uint32_t slot = (kl ? sK : sV) + s * 2 * kAtom;
         mbar_expect_tx(full, 2 * kAtom);
-        tma_load_3d(slot, kl ? &p.tm_k : &p.tm_x, 0, j * 128, bi, full);
-        tma_load_3d(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, j * 128, bi, full);
+        tma_load_3d(slot, kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j) * 128, bi, full);
+        tma_load_3d(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j) * 128, bi, full);
         armed[s] = j / nslot + 1;
       }
       // drain: every armed phase must have landed before the CTA may exit
@@ -591,7 +599,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
       tmem_ld32(tS + 64, sr + 64);
       tmem_ld32(tS + 96, sr + 96);
       tmem_wait_ld();
-      const int valid = p.n_kv - j * 128;  // same for every thread: the branches below are uniform
+      const int valid = p.n_kv - (kt0 + j) * 128;  // same for every thread: the branches below are uniform
       const float mx =
           (valid < 128 ? row_max_raw<128, true>(sr, valid) : row_max_raw<128, false>(sr, 128)) * p.scale_log2;
       if (j == w) {
@@ -663,6 +671,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
       const float inv = 1.f / lt;
       const float c0 = a0 * inv, c1 = a1 * inv;
       const uint32_t tO0 = tmem + lane_off + 256, tO1 = tO0 + 128;
+      const bool part = p.kv_split > 1;  // key chunk: fp32 O normalised by this chunk's l, plus (m, l, h)
 #pragma unroll 1
       for (int c = 2 * w; c < 2 * w + 2; ++c) {  // this warpgroup's 64 output columns
         uint32_t o0[32], o1[32];
@@ -672,6 +681,21 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
         if (!two) {
 #pragma unroll
           for (int i = 0; i < 32; ++i) o1[i] = 0u;
+        }
+        if (part) {
+          // [128 rows][32 floats] box c of the fp32 staging (128-byte swizzle)
+          const uint32_t base = stage + c * 16384 + row * 128;
+#pragma unroll
+          for (int k4 = 0; k4 < 8; ++k4) {
+            float x[4];
+#pragma unroll
+            for (int e = 0; e < 4; ++e)
+              x[e] = fmaf(__uint_as_float(o0[4 * k4 + e]), c0, __uint_as_float(o1[4 * k4 + e]) * c1);
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((k4 ^ (row & 7)) << 4)), "f"(x[0]),
+                         "f"(x[1]), "f"(x[2]), "f"(x[3])
+                         : "memory");
+          }
+          continue;
         }
         uint32_t wv[16];
 #pragma unroll
@@ -691,7 +715,15 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
         }
       }
       const int grow = q0 + row;
-      if (w == 0 && grow < p.n_q) {
+      if (part) {
+        if (w == 0) {  // rows past n_q too (inside n_pad): never read by the merge
+          const int64_t plane = (int64_t)p.kv_split * p.n_seq * p.n_pad;
+          const int64_t idx = ((int64_t)kchunk * p.n_seq + bi) * p.n_pad + grow;
+          p.pst[idx] = m;
+          p.pst[plane + idx] = lt;
+          p.pst[2 * plane + idx] = ht;
+        }
+      } else if (w == 0 && grow < p.n_q) {
         const float lg = log2f(lt);
         const int64_t idx = (int64_t)bi * p.n_q + grow;
         if (p.lse) p.lse[idx] = m + lg;
@@ -701,7 +733,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
     fence_proxy_async_smem();
     named_bar_sync(2, 256);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      for (int a = 0; a < 2; ++a) tma_store_3d(&p.tm_o, 64 * a, q0, bi, stage + a * kAtom);
+      if (p.kv_split > 1) {
+        for (int c = 0; c < 4; ++c) tma_store_3d(&p.tm_po, 32 * c, q0, kchunk * p.n_seq + bi, stage + c * 16384);
+      } else {
+        for (int a = 0; a < 2; ++a) tma_store_3d(&p.tm_o, 64 * a, q0, bi, stage + a * kAtom);
+      }
       tma_store_commit_and_wait();
     }
   }
@@ -710,6 +746,81 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
   __syncthreads();
   tc_fence_after();
   if (warp == 0) tmem_dealloc(tmem, 512);
+}
+
+// Merge of the key chunks of a split key range (one warp per query row, lane = 4 columns):
+// m = max_c m_c, a_c = 2^(m_c - m), l = sum a_c l_c, h = sum a_c (h_c + (m_c - m) l_c),
+// o = sum (a_c l_c / l) o_c with o_c normalised by its own l_c; LSE2 = m + log2 l,
+// entropy = (log2 l - h / l) ln 2. Chunks are summed in order (deterministic).
+template <typename T>
+__global__ void __launch_bounds__(256) fwd_split_merge_kernel(const float* po, const float* pst, int split, int64_t n_seq,
+                                                              int64_t n_pad, int n_q, T* o, int64_t o_bs, float* lse,
+                                                              float* ent) {
+  const int64_t rg = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (rg >= n_seq * n_q) return;
+  const int64_t bi = rg / n_q, r = rg % n_q;
+  const int64_t plane = (int64_t)split * n_seq * n_pad;
+  float m = -3.0e38f;
+  for (int c = 0; c < split; ++c) m = fmaxf(m, pst[((int64_t)c * n_seq + bi) * n_pad + r]);
+  float l = 0.f, h = 0.f;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int c = 0; c < split; ++c) {
+    const int64_t idx = ((int64_t)c * n_seq + bi) * n_pad + r;
+    const float mc = pst[idx], lc = pst[plane + idx], hc = pst[2 * plane + idx];
+    const float a = fast_exp2(mc - m);
+    l = fmaf(a, lc, l);
+    h = fmaf(a, fmaf(mc - m, lc, hc), h);
+    const float wgt = a * lc;
+    const float4 v = reinterpret_cast<const float4*>(po + idx * 128)[lane];
+    acc.x = fmaf(wgt, v.x, acc.x);
+    acc.y = fmaf(wgt, v.y, acc.y);
+    acc.z = fmaf(wgt, v.z, acc.z);
+    acc.w = fmaf(wgt, v.w, acc.w);
+  }
+  const float inv = 1.f / l;
+  uint2 w;
+  w.x = Elem<T>::pack(acc.x * inv, acc.y * inv);
+  w.y = Elem<T>::pack(acc.z * inv, acc.w * inv);
+  reinterpret_cast<uint2*>(o + bi * o_bs + r * 128)[lane] = w;
+  if (lane == 0) {
+    const float lg = log2f(l);
+    if (lse) lse[bi * n_q + r] = m + lg;
+    if (ent) ent[bi * n_q + r] = (lg - h / l) * kLn2;
+  }
+}
+
+// Key-range split of the d = dv = 128 kernel: minimise waves x (key tiles per CTA + ~5 tiles of
+// fixed cost: Q load, TMEM set-up, merge and store), never leaving a chunk without a tile.
+int fwd2_split(int64_t batch, int n_q, int n_kv) {
+  if (batch <= 0 || n_q <= 0) return 1;
+  const int64_t n_qt = (n_q + 127) / 128;
+  const int nkt = (n_kv + 127) / 128;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  int best = 1;
+  int64_t best_cost = 0;
+  for (int ks = 1; ks <= 8; ++ks) {
+    const int per = (nkt + ks - 1) / ks;
+    if ((ks - 1) * per >= nkt) break;
+    const int64_t waves = (n_qt * batch * ks + sms - 1) / sms;
+    const int64_t cost = waves * (per + 5);
+    if (ks == 1 || cost * 100 < best_cost * 90) {  // a split must gain 10 % (merge pass)
+      best = ks;
+      best_cost = cost;
+    }
+  }
+  return best;
+}
+
+int64_t round_up256(int64_t x) { return (x + 255) / 256 * 256; }
+
+// Workspace of a split: partial O [split][batch][n_pad][128] fp32, then the (m, l, h) planes.
+int64_t split_bytes(int split, int64_t batch, int n_q) {
+  if (split <= 1) return 0;
+  const int64_t n_pad = (n_q + 127) / 128 * 128;
+  return round_up256((int64_t)split * batch * n_pad * 128 * 4) + round_up256(3 * (int64_t)split * batch * n_pad * 4);
 }
 
 // ---------------------------------------------------------------------------------- host side
@@ -731,7 +842,7 @@ cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   auto kern = fea_fwd2_sm100_kernel<T, VK, ENT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  const int64_t blocks = (int64_t)p.n_qtiles * batch;
+  const int64_t blocks = (int64_t)p.n_qtiles * p.kv_split * batch;
   if (blocks > 0x7fffffff || batch > 0x7fffffff) return cudaErrorInvalidConfiguration;
   kern<<<(unsigned)blocks, kThreads, C::SMEM, st>>>(p);
   return cudaGetLastError();
@@ -757,6 +868,17 @@ bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk) {
   return (dv == 128 || dv == 256) && dv1 == dv;
 }
 
+int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk) {
+  if (!fea_fwd_sm100_supported(d, dv, dv1, vk) || dv != 128) return 0;  // only the two-stream kernel splits
+  return split_bytes(fwd2_split(batch, n_q, n_kv), batch, n_q);
+}
+
+int fea_fwd_sm100_split(int64_t batch, int n_q, int n_kv, int dv, const void* work, int64_t work_bytes) {
+  if (dv != 128 || !work) return 1;
+  const int ks = fwd2_split(batch, n_q, n_kv);
+  return (ks > 1 && work_bytes >= split_bytes(ks, batch, n_q)) ? ks : 1;
+}
+
 cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, bool ent, bool bf16, bool vk,
                           cudaStream_t st) {
   Sm100FwdParams p;
@@ -776,10 +898,40 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
   p.n_kv = fp.n_kv;
   p.n_qtiles = (fp.n_q + 127) / 128;
   p.scale_log2 = fp.scale_log2;
+  // key-range split (two-stream kernel, with a large enough workspace)
+  const int nkt = (fp.n_kv + 127) / 128;
+  p.kv_split = fea_fwd_sm100_split(batch, fp.n_q, fp.n_kv, dv, fp.work, fp.work_bytes);
+  p.kt_per = (nkt + p.kv_split - 1) / p.kv_split;
+  p.n_seq = (int)batch;
+  p.n_pad = (fp.n_q + 127) / 128 * 128;
+  float* po = nullptr;
+  p.pst = nullptr;
+  if (p.kv_split > 1) {
+    po = static_cast<float*>(fp.work);
+    p.pst = reinterpret_cast<float*>(static_cast<char*>(fp.work) +
+                                     round_up256((int64_t)p.kv_split * batch * p.n_pad * 128 * 4));
+    if (!tma::make_map_f32(&p.tm_po, po, 128, p.n_pad, (int64_t)p.kv_split * batch, p.n_pad * 128, 128))
+      return cudaErrorInvalidValue;
+  }
+  cudaError_t e;
   if (bf16)
-    return ent ? dispatch<__nv_bfloat16, true>(p, batch, dv, dv1, vk, st)
-               : dispatch<__nv_bfloat16, false>(p, batch, dv, dv1, vk, st);
-  return ent ? dispatch<__half, true>(p, batch, dv, dv1, vk, st) : dispatch<__half, false>(p, batch, dv, dv1, vk, st);
+    e = ent ? dispatch<__nv_bfloat16, true>(p, batch, dv, dv1, vk, st)
+            : dispatch<__nv_bfloat16, false>(p, batch, dv, dv1, vk, st);
+  else
+    e = ent ? dispatch<__half, true>(p, batch, dv, dv1, vk, st) : dispatch<__half, false>(p, batch, dv, dv1, vk, st);
+  if (e != cudaSuccess || p.kv_split == 1) return e;
+  const int64_t rows = batch * fp.n_q;
+  const int64_t blocks = (rows + 7) / 8;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if (bf16)
+    fwd_split_merge_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
+        po, p.pst, p.kv_split, batch, p.n_pad, fp.n_q, static_cast<__nv_bfloat16*>(fp.o), fp.o_bs, fp.lse,
+        ent ? fp.ent : nullptr);
+  else
+    fwd_split_merge_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(po, p.pst, p.kv_split, batch, p.n_pad, fp.n_q,
+                                                                      static_cast<__half*>(fp.o), fp.o_bs, fp.lse,
+                                                                      ent ? fp.ent : nullptr);
+  return cudaGetLastError();
 }
 
 cudaError_t fea_fwd_sm100_status(cudaStream_t st, int* out) {

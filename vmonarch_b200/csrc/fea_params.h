@@ -16,6 +16,8 @@ struct FwdParams {
   int64_t q_bs, k_bs, v_bs, v2_bs, o_bs;  // batch strides in elements
   int n_q, n_kv, dv1, n_qtiles;
   float scale_log2;  // sm_scale * log2(e)
+  void* work;        // optional workspace (key-range split of the d = dv = 128 kernel), may be NULL
+  int64_t work_bytes;
 };
 
 struct BwdParams {

@@ -67,6 +67,11 @@ def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
     a.d, a.dv, a.dv1 = q3.size(2), o3.size(2), v3.size(2)
     a.dtype = N.dtype_code(q.dtype)
     a.sm_scale = float(sm_scale)
+    nbytes = N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a))
+    ws = None
+    if nbytes > 0:  # lets the kernel split long key ranges over more CTAs
+        ws = torch.empty(nbytes, dtype=torch.uint8, device=q.device)
+        a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
     _call("vmb_fea_fwd", N.lib.vmb_fea_fwd, a, q.device)
 
 
