@@ -98,6 +98,8 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream);
  * grad_mode 0: grad_q/grad_k/grad_v/grad_v2 are written in the element dtype (standalone op).
  * grad_mode 1: grad_* are fp32 buffers that the gradients are ADDED into (VMonarch chains
  *              several R steps and the recompute into one set of accumulators).
+ * grad_mode 2: grad_* are fp32 buffers that are OVERWRITTEN (the first contribution to a set of
+ *              accumulators, so they need no zero-fill).
  * v_is_k = 1: the value columns [0, dv1) are the key tensor itself (dv1 == d); their gradient is
  *              added into grad_k and grad_v must be NULL. This is the VMonarch R step
  *              (vmonarch.py:50).
@@ -157,7 +159,8 @@ int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream);
  * forward, last == 1: z  [bh][N][dw-d] Monarch output; tokens < skip_rows are left unwritten
  * backward, last == 0: du [bh][N][d] fp32 gradient of u
  * backward, last == 1: dz [bh][N][dw-d] gradient of z; tokens < skip_rows carry none
- * backward outputs: dq [bh][N][d] fp32 (ADDED into), dout [bh][N][dw] gradient of out.
+ * backward outputs: dq [bh][N][d] fp32 (ADDED into, or OVERWRITTEN when dq_store != 0),
+ *   dout [bh][N][dw] gradient of out.
  * m <= 64, d in {64, 128}, dw - d in {64, 128, 256} when last.
  */
 typedef struct vmb_lstep_args {
@@ -174,6 +177,7 @@ typedef struct vmb_lstep_args {
   int32_t d, dw, dtype, last;
   int64_t skip_rows;
   float scale, min_col_mass;
+  int32_t dq_store;  /* backward: 1 = write dq instead of adding into it (ABI version 2) */
 } vmb_lstep_args;
 
 int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream);

@@ -107,8 +107,9 @@ def test_fea_bwd_workspace_and_validation():
     a.v_is_k = 1                      # v_is_k with a separate grad_v is rejected
     assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1
     a.v_is_k = 0
-    a.grad_mode = 2
+    a.grad_mode = 3                   # modes are 0 (16-bit), 1 (fp32 add), 2 (fp32 overwrite)
     assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1
+    assert b"grad_mode" in N.lib.vmb_last_error()
     a.grad_mode = 1
     a.workspace, a.workspace_bytes = 256, 16   # too small
     assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1

@@ -147,3 +147,24 @@ def test_split_key_range_backward_matches_and_is_deterministic():
         assert max_rel_err(g, r.float()) <= 1e-2
     for g0, g1 in zip(*runs):
         assert torch.equal(g0, g1)
+
+
+@pytest.mark.parametrize("D", [128, 64])
+def test_grad_mode_overwrite_equals_add_into_zeros(D):
+    # grad_mode 2 overwrites fp32 gradient buffers (here pre-filled with NaN); it must give exactly
+    # what grad_mode 1 adds into zero-filled ones. D = 128 runs the tcgen05 kernels, D = 64 mma.sync.
+    from vmonarch_b200 import ops
+    gen = torch.Generator().manual_seed(5)
+    B, n = 3, 300
+    q, k, v, do = (torch.randn(B, n, D, generator=gen).bfloat16().cuda() for _ in range(4))
+    de = torch.randn(B, n, generator=gen).cuda()
+    o = torch.empty_like(q)
+    lse, ent = torch.empty(B, n, device="cuda"), torch.empty(B, n, device="cuda")
+    ops.fea_fwd(q, k, v, o, lse, ent, D ** -0.5)
+    add = [torch.zeros(t.shape, device="cuda") for t in (q, k, v)]
+    ops.fea_bwd(q, k, v, o, do, lse, *add, D ** -0.5, ent=ent, dent=de, grad_mode=1)
+    put = [torch.full(t.shape, float("nan"), device="cuda") for t in (q, k, v)]
+    ops.fea_bwd(q, k, v, o, do, lse, *put, D ** -0.5, ent=ent, dent=de, grad_mode=2)
+    torch.cuda.synchronize()
+    for a, p in zip(add, put):
+        assert torch.equal(a, p)

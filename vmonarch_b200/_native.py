@@ -74,6 +74,7 @@ class LstepArgs(ctypes.Structure):
         ("d", c_i32), ("dw", c_i32), ("dtype", c_i32), ("last", c_i32),
         ("skip_rows", c_i64),
         ("scale", ctypes.c_float), ("min_col_mass", ctypes.c_float),
+        ("dq_store", c_i32),
     ]
 
 

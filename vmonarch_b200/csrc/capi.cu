@@ -141,7 +141,7 @@ int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
   if (bwd_uses_sm100(a)) {
     const int64_t n_pad = round_up(a->n_q, 128);
     int64_t bytes = 3 * round_up(a->batch * n_pad * 4, 256);
-    const int split = vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode == 1);
+    const int split = vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode != 0);
     if (split > 1) bytes += round_up((int64_t)split * a->batch * n_pad * 128 * 4, 256);
     return bytes;
   }
@@ -155,7 +155,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   if (!a) return fail(VMB_EINVAL, "vmb_fea_bwd: null args");
   int rc = check_common("vmb_fea_bwd", a->batch, a->n_q, a->n_kv, a->d, a->dv, a->dv1, a->dtype, a->v2);
   if (rc) return rc;
-  if (a->grad_mode != 0 && a->grad_mode != 1) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_mode must be 0 or 1");
+  if (a->grad_mode < 0 || a->grad_mode > 2) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_mode must be 0, 1 or 2");
   if (a->v_is_k && (a->dv1 != a->d || a->grad_v != nullptr))
     return fail(VMB_EINVAL, "vmb_fea_bwd: v_is_k needs dv1 == d and grad_v == NULL");
   if (!a->v_is_k && !a->grad_v) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_v is NULL");
@@ -201,7 +201,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.dout = a->dout; p.lse = a->lse; p.cc = cc; p.gg = gg;
   p.fold = fold; p.n_pad = n_pad;
   p.dq_part = nullptr;
-  if (sm100 && vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode == 1) > 1)
+  if (sm100 && vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode != 0) > 1)
     p.dq_part = reinterpret_cast<float*>(ws + 3 * round_up(a->batch * n_pad * 4, 256));
   p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
   p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
@@ -214,6 +214,18 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.sm_scale = a->sm_scale;
   p.scale_log2 = a->sm_scale * kLog2eHost;
   if (sm100) return cuda_status(vmb::fea_bwd_sm100(p, a->batch, a->dv, a->v_is_k != 0, bf16, st), "vmb_fea_bwd");
+  if (a->grad_mode == 2) {
+    // the mma.sync kernels only add: clear the fp32 gradients, then accumulate
+    auto clear = [&](void* ptr, int64_t bs, int64_t rows, int cols) -> cudaError_t {
+      return ptr ? cudaMemset2DAsync(ptr, bs * 4, 0, rows * cols * 4, a->batch, st) : cudaSuccess;
+    };
+    e = clear(a->grad_q, a->grad_q_bs, a->n_q, a->d);
+    if (e == cudaSuccess) e = clear(a->grad_k, a->grad_k_bs, a->n_kv, a->d);
+    if (e == cudaSuccess) e = clear(a->grad_v, a->grad_v_bs, a->n_kv, a->dv1);
+    if (e == cudaSuccess) e = clear(a->grad_v2, a->grad_v2_bs, a->n_kv, a->dv - a->dv1);
+    if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(clear)");
+    p.acc_kv = p.acc_q = 1;
+  }
   e = vmb::fea_bwd_mma(p, a->batch, a->d, a->dv, a->v_is_k != 0, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd");
   if (dq_acc) {
@@ -255,6 +267,7 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
   p.dq = a->dq; p.dout = a->dout;
   p.bh = a->bh; p.m = a->m; p.b = a->b; p.d = a->d; p.dw = a->dw; p.skip_rows = a->skip_rows;
   p.scale = a->scale; p.min_col_mass = a->min_col_mass;
+  p.dq_store = a->dq_store != 0;
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (vmb::lstep_mma_supported(p, a->last != 0))

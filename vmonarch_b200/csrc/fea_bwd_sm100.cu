@@ -683,15 +683,16 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   if (warp == 0) tmem_dealloc(tmem, 512);
 }
 
-// dq[bi][q] += sum over chunks c (in order) of part[c][bi][q]: the split key ranges' partial tiles
+// dq[bi][q] (+)= sum over chunks c (in order) of part[c][bi][q]: the split key ranges' partial tiles
+// (added into dq, or written over it in the store mode)
 __global__ void dq_split_reduce_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q, float* dq,
-                                       int64_t dq_bs) {
+                                       int64_t dq_bs, int store) {
   const int64_t total = batch * n_q * 32;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
     const int64_t q = rem / 32, c4 = rem % 32;
     float4* dst = reinterpret_cast<float4*>(dq + bi * dq_bs + q * 128) + c4;
-    float4 acc = *dst;
+    float4 acc = store ? make_float4(0.f, 0.f, 0.f, 0.f) : *dst;
     for (int c = 0; c < split; ++c) {
       const float4 v = reinterpret_cast<const float4*>(part + (((int64_t)c * batch + bi) * n_pad + q) * 128)[c4];
       acc.x += v.x;
@@ -809,7 +810,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   const int64_t total = batch * b.n_q * 32;  // float4s of the valid dQ rows
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
   dq_split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.dq,
-                                                           b.dq_bs);
+                                                           b.dq_bs, b.acc_q == 2);
   return cudaGetLastError();
 }
 

@@ -14,12 +14,13 @@ struct LstepParams {
   void* z;            // fwd, last:     [bh][N][dw-D]
   const float* du;    // bwd, non-last: [bh][N][D] fp32 gradient of u
   const void* dz;     // bwd, last:     [bh][N][dw-D]
-  float* dq;          // bwd: [bh][N][D] fp32, added into
+  float* dq;          // bwd: [bh][N][D] fp32, added into (or written when dq_store)
   void* dout;         // bwd: [bh][N][dw] gradient of `out`
   int64_t bh, m, b;
   int d, dw;
   int64_t skip_rows;  // tokens [0, skip_rows) of every head are not produced / carry no gradient
   float scale, min_col_mass;
+  int dq_store;
 };
 
 cudaError_t fea_fwd_mma(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, cudaStream_t st);

@@ -308,7 +308,8 @@ __global__ void __launch_bounds__(kLstepThreads) lstep_bwd_kernel(const LstepPar
       acc = fmaf(s.da[i * (m + 1) + k], s.kr[k * (D + 1) + d], acc);
       if (!LAST) acc = fmaf(s.a[i * (m + 1) + k], s.y[k * (D + 1) + d], acc);
     }
-    dq[((int64_t)i * p.b + j) * D + d] += acc;
+    float& dst = dq[((int64_t)i * p.b + j) * D + d];
+    dst = p.dq_store ? acc : dst + acc;
   }
   // dout[k, :D] = scale * sum_i dlog_ik q_i
   for (int c = threadIdx.x; c < m * D; c += blockDim.x) {

@@ -458,13 +458,19 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
         const int i = mt * 16 + (lane >> 2) + h * 8;
         if (i >= m) continue;
         float* dst = gdq + ((int64_t)i * p.b + j) * D + half * 64 + (lane & 3) * 2;
-        // fire-and-forget reductions: this warp alone owns these dq elements, so nothing waits
-        // for the old value
+        // fire-and-forget reductions (or plain stores in the store mode): this warp alone owns
+        // these dq elements, so nothing waits for the old value
+        if (p.dq_store) {
 #pragma unroll
-        for (int nt = 0; nt < 8; ++nt)
-          asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(dst + nt * 8), "f"(acc[mt][nt][2 * h]),
-                       "f"(acc[mt][nt][2 * h + 1])
-                       : "memory");
+          for (int nt = 0; nt < 8; ++nt)
+            *reinterpret_cast<float2*>(dst + nt * 8) = make_float2(acc[mt][nt][2 * h], acc[mt][nt][2 * h + 1]);
+        } else {
+#pragma unroll
+          for (int nt = 0; nt < 8; ++nt)
+            asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(dst + nt * 8), "f"(acc[mt][nt][2 * h]),
+                         "f"(acc[mt][nt][2 * h + 1])
+                         : "memory");
+        }
       }
   }
   __syncwarp();

@@ -132,10 +132,12 @@ def lstep_fwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, *,
 
 
 def lstep_bwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, dq, dout, *, du=None, dz=None,
-              skip_rows: int = 0) -> None:
-    """Monarch L step backward: adds into dq (fp32), writes dout (gradient of the R-step output)."""
+              skip_rows: int = 0, dq_store: bool = False) -> None:
+    """Monarch L step backward: adds into dq (fp32; overwrites it when dq_store), writes dout (gradient
+    of the R-step output)."""
     a = _lstep_args(q, out, ent, m, b, scale, min_col_mass, dz is not None, skip_rows)
     a.du, a.dz, a.dq, a.dout = N.ptr(du), N.ptr(dz), dq.data_ptr(), dout.data_ptr()
+    a.dq_store = int(dq_store)
     _call("vmb_lstep_bwd", N.lib.vmb_lstep_bwd, a, q.device)
 
 

@@ -95,12 +95,13 @@ class _VMonarchAttention(torch.autograd.Function):
         dz = dz.to(dt).contiguous().view(BH, N, Dv)
         grid = lambda t: t.view(BH * m, b, t.size(-1))  # noqa: E731
 
-        dq_acc = torch.zeros((BH, N, D), device=dev, dtype=torch.float32)
-        dk_acc = torch.zeros((BH, N, D), device=dev, dtype=torch.float32)
-        dv_acc = torch.zeros((BH, N, Dv), device=dev, dtype=torch.float32)
-        if rr > 0:
-            ops.fea_bwd(qf[:, :rr], kf, vf, z[:, :rr], dz[:, :rr], lse_r, dq_acc[:, :rr], dk_acc, dv_acc, scale,
-                        grad_mode=1)
+        # fp32 accumulators. Each is first written by a call that covers all of its rows and
+        # OVERWRITES it (no zero-fill): dq by the last L step, dk / dv (and every R step's own dq,
+        # gq) by the last R step; later calls add. The recompute's contribution comes last.
+        dq_acc = torch.empty((BH, N, D), device=dev, dtype=torch.float32)
+        dk_acc = torch.empty((BH, N, D), device=dev, dtype=torch.float32)
+        dv_acc = torch.empty((BH, N, Dv), device=dev, dtype=torch.float32)
+        kv_fresh = True   # dk_acc / dv_acc not yet written
 
         du = None
         n_it = len(steps)
@@ -110,14 +111,32 @@ class _VMonarchAttention(torch.autograd.Function):
             last = it == n_it - 1
             dout = torch.empty_like(out)
             if last:
-                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, dz=dz, skip_rows=rr)
+                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, dz=dz, skip_rows=rr,
+                              dq_store=True)
             else:
                 ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, du=du)
-            gq = dq_acc if it == 0 else torch.zeros((BH, N, D), device=dev, dtype=torch.float32)
+            gq = dq_acc if it == 0 else torch.empty((BH, N, D), device=dev, dtype=torch.float32)
+            gq_fresh = it != 0
+            # one grad mode per call: overwrite only when every target is fresh, otherwise clear
+            # the fresh ones and add (only with num_iters != 2)
+            if gq_fresh and kv_fresh:
+                mode = 2
+            else:
+                if gq_fresh:
+                    gq.zero_()
+                if kv_fresh:
+                    dk_acc.zero_()
+                    dv_acc.zero_()
+                mode = 1
             ops.fea_bwd(grid(u), grid(kf), grid(kf), grid(out), grid(dout), lse.view(BH * m, b), grid(gq),
                         grid(dk_acc), None, sm, v2=grid(vf) if last else None,
-                        grad_v2=grid(dv_acc) if last else None, grad_mode=1, v_is_k=True)
+                        grad_v2=grid(dv_acc) if last else None, grad_mode=mode, v_is_k=True)
+            kv_fresh = False
             du = gq
+
+        if rr > 0:
+            ops.fea_bwd(qf[:, :rr], kf, vf, z[:, :rr], dz[:, :rr], lse_r, dq_acc[:, :rr], dk_acc, dv_acc, scale,
+                        grad_mode=1)
 
         dq = torch.empty((B, H, N, D), device=dev, dtype=dt)
         dk = torch.empty((B, H, N, D), device=dev, dtype=dt)
