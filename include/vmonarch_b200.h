@@ -127,6 +127,8 @@ typedef struct vmb_fea_bwd_args {
   int32_t d, dv, dv1, dtype;
   int32_t grad_mode, v_is_k;
   float sm_scale;
+  const float* delta;  /* optional [batch][n_q] fp32: sum_c o[c] dout[c] per query row, precomputed
+                          by the caller (vmb_lstep_bwd's delta_out); NULL: computed here (ABI 2) */
 } vmb_fea_bwd_args;
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);
@@ -178,6 +180,8 @@ typedef struct vmb_lstep_args {
   int64_t skip_rows;
   float scale, min_col_mass;
   int32_t dq_store;  /* backward: 1 = write dq instead of adding into it (ABI version 2) */
+  float* delta_out;  /* backward, optional [bh][N] fp32: sum_c out[c] dout[c] per token, the
+                        preprocessing of the R step's attention backward (its `delta`) */
 } vmb_lstep_args;
 
 int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream);

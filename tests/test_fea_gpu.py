@@ -167,4 +167,8 @@ def test_grad_mode_overwrite_equals_add_into_zeros(D):
     ops.fea_bwd(q, k, v, o, do, lse, *put, D ** -0.5, ent=ent, dent=de, grad_mode=2)
     torch.cuda.synchronize()
     for a, p in zip(add, put):
-        assert torch.equal(a, p)
+        assert torch.isfinite(p).all()
+        if D == 128:
+            assert torch.equal(a, p)
+        else:  # the mma.sync kernels add dQ with atomics: the summation order varies run to run
+            torch.testing.assert_close(p, a, rtol=1e-5, atol=1e-5)

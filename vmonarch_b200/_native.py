@@ -61,6 +61,7 @@ class FeaBwdArgs(ctypes.Structure):
         ("d", c_i32), ("dv", c_i32), ("dv1", c_i32), ("dtype", c_i32),
         ("grad_mode", c_i32), ("v_is_k", c_i32),
         ("sm_scale", ctypes.c_float),
+        ("delta", c_vp),
     ]
 
 
@@ -75,6 +76,7 @@ class LstepArgs(ctypes.Structure):
         ("skip_rows", c_i64),
         ("scale", ctypes.c_float), ("min_col_mass", ctypes.c_float),
         ("dq_store", c_i32),
+        ("delta_out", c_vp),
     ]
 
 

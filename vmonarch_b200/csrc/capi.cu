@@ -191,7 +191,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
       (!sm100 && a->grad_mode == 0) ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
   count(sm100 ? 3 : (dq_acc ? 3 : 2));
   cudaError_t e = vmb::fea_bwd_pre(a->o, a->o_bs, a->dout, a->do_bs, a->lse, a->ent, a->dent, cc, gg, a->batch,
-                                   (int)a->n_q, a->dv, fold, n_pad, a->sm_scale, bf16, st);
+                                   (int)a->n_q, a->dv, fold, n_pad, a->sm_scale, a->delta, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(pre)");
   if (dq_acc) {
     e = cudaMemsetAsync(dq_acc, 0, rows * a->d * 4, st);
@@ -251,6 +251,8 @@ static int lstep_check(const char* what, const vmb_lstep_args* a, bool bwd) {
   if (!bwd && !(a->last ? a->z : a->u)) return fail(VMB_EINVAL, "%s: null output pointer", what);
   if (bwd && (!a->dq || !a->dout || !(a->last ? (const void*)a->dz : (const void*)a->du)))
     return fail(VMB_EINVAL, "%s: null gradient pointer", what);
+  if (bwd && a->delta_out && a->dw != 64 && a->dw != 128 && a->dw != 256)
+    return fail(VMB_ENOTSUP, "%s: delta_out needs an out width of 64, 128 or 256 (got %d)", what, a->dw);
   const void* ptrs[] = {a->q, a->out, a->u, a->z, a->du, a->dz, a->dq, a->dout};
   for (const void* p : ptrs)
     if (p && !aligned16(p)) return fail(VMB_EINVAL, "%s: tensors must be 16-byte aligned", what);
@@ -268,11 +270,19 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
   p.bh = a->bh; p.m = a->m; p.b = a->b; p.d = a->d; p.dw = a->dw; p.skip_rows = a->skip_rows;
   p.scale = a->scale; p.min_col_mass = a->min_col_mass;
   p.dq_store = a->dq_store != 0;
+  p.delta_out = bwd ? a->delta_out : nullptr;
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   if (vmb::lstep_mma_supported(p, a->last != 0))
     return cuda_status(vmb::lstep_mma_launch(p, a->last != 0, bwd, bf16, st), what);
-  return cuda_status(vmb::lstep_launch(p, a->last != 0, bwd, bf16, st), what);
+  cudaError_t e = vmb::lstep_launch(p, a->last != 0, bwd, bf16, st);
+  if (e == cudaSuccess && p.delta_out) {
+    // the generic kernel does not fold delta in: sum out . dout per token, like the preprocess
+    count(1);
+    e = vmb::fea_bwd_pre(a->out, p.m * p.b * a->dw, a->dout, p.m * p.b * a->dw, nullptr, nullptr, nullptr,
+                         p.delta_out, nullptr, a->bh, (int)(p.m * p.b), a->dw, nullptr, 0, 0.f, nullptr, bf16, st);
+  }
+  return cuda_status(e, what);
 }
 
 int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream) { return lstep_run("vmb_lstep_fwd", a, false, stream); }

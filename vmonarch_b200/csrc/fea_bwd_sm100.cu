@@ -230,6 +230,13 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         bulk_load(slot_stats(s), p.nl + r0, 256, BAR_QFULL(s));
         bulk_load(slot_stats(s) + 256, p.nc + r0, 256, BAR_QFULL(s));
         bulk_load(slot_stats(s) + 512, p.ng + r0, 256, BAR_QFULL(s));
+        // bring the tile NQS loads ahead into L2: a slot is reloaded only ~NQS - 2 tiles before
+        // its use, less than a DRAM round trip under this kernel's load
+        if (i + NQS < nq) {
+          tma_prefetch_3d(&p.tm_c, 0, (i + NQS) * 64, bi);
+          tma_prefetch_3d(&p.tm_c, 64, (i + NQS) * 64, bi);
+          for (int a = 0; a < C::DW / 64; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, (i + NQS) * 64, bi);
+        }
       }
       armed[s] = i / NQS + 1;
     }
@@ -499,6 +506,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         mbar_expect_tx(BAR(B_KFULL + s), C::KSLOT);
         tma_load_3d(sK + s * C::KSLOT, &p.tm_c, 0, (kt0 + j) * 128, bi, BAR(B_KFULL + s));
         tma_load_3d(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, (kt0 + j) * 128, bi, BAR(B_KFULL + s));
+        if (j + NK < nk) {  // the K tile NK loads ahead into L2
+          tma_prefetch_3d(&p.tm_c, 0, (kt0 + j + NK) * 128, bi);
+          tma_prefetch_3d(&p.tm_c, 64, (kt0 + j + NK) * 128, bi);
+        }
         karmed[s] = j / NK + 1;
         if (XA > 0) {
           const int x = j % NXB;
@@ -506,6 +517,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
           mbar_expect_tx(BAR(B_XFULL + x), C::XSLOT);
           for (int a = 0; a < XA; ++a)
             tma_load_3d(sX + x * C::XSLOT + a * kAtom128, &p.tm_d, 64 * a, (kt0 + j) * 128, bi, BAR(B_XFULL + x));
+          if (j + NXB < nk)
+            for (int a = 0; a < XA; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, (kt0 + j + NXB) * 128, bi);
           xarmed[x] = j / NXB + 1;
         }
       }

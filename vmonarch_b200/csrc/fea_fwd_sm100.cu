@@ -189,6 +189,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
           mbar_expect_tx(BAR_VFULL(s), XA * kAtom);
           for (int a = 0; a < XA; ++a) tma_load_3d(slot + (2 + a) * kAtom, &p.tm_x, 64 * a, j * 128, bi, BAR_VFULL(s));
         }
+        if (j + NSLOT < n_kt) {  // the tiles one ring ahead into L2
+          tma_prefetch_3d(&p.tm_k, 0, (j + NSLOT) * 128, bi);
+          tma_prefetch_3d(&p.tm_k, 64, (j + NSLOT) * 128, bi);
+          for (int a = 0; a < XA; ++a) tma_prefetch_3d(&p.tm_x, 64 * a, (j + NSLOT) * 128, bi);
+        }
         armed[s] = j / NSLOT + 1;
       }
       // drain: every armed phase must have landed before the CTA may exit
@@ -516,6 +521,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
         mbar_expect_tx(full, 2 * kAtom);
         tma_load_3d(slot, kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j) * 128, bi, full);
         tma_load_3d(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j) * 128, bi, full);
+        if (j + nslot < n_kt) {  // the tile one ring ahead into L2
+          tma_prefetch_3d(kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j + nslot) * 128, bi);
+          tma_prefetch_3d(kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j + nslot) * 128, bi);
+        }
         armed[s] = j / nslot + 1;
       }
       // drain: every armed phase must have landed before the CTA may exit

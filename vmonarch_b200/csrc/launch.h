@@ -21,6 +21,7 @@ struct LstepParams {
   int64_t skip_rows;  // tokens [0, skip_rows) of every head are not produced / carry no gradient
   float scale, min_col_mass;
   int dq_store;
+  float* delta_out;   // bwd, optional: [bh][N] fp32 sum_c out[c] dout[c] per token
 };
 
 cudaError_t fea_fwd_mma(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, cudaStream_t st);
@@ -42,7 +43,7 @@ cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out);
 cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
-                        float* fold, int64_t n_pad, float sm_scale, bool bf16, cudaStream_t st);
+                        float* fold, int64_t n_pad, float sm_scale, const float* delta, bool bf16, cudaStream_t st);
 cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
                      bool bf16, cudaStream_t st);
 bool lstep_mma_supported(const LstepParams& p, bool last);

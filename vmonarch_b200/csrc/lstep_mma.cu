@@ -158,6 +158,29 @@ __device__ __forceinline__ void stage_rows64(T* S, int c0, const float (&v)[MP /
     }
 }
 
+// stage_rows64 for the dout tile, which is written over the out tile: before each pair is
+// overwritten, its out values are multiplied with the bf16-rounded dout values that replace them,
+// and the products are summed per row (this lane's share of sum_c out[c] dout[c]).
+template <typename T, int MP, int CH>
+__device__ __forceinline__ void stage_rows64_dot(T* S, int c0, const float (&v)[MP / 16][8][4],
+                                                 float (&dot)[MP / 16][2], int lane) {
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = mt * 16 + (lane >> 2) + h * 8;
+#pragma unroll
+      for (int nt = 0; nt < 8; ++nt) {
+        const int col = c0 * 8 + nt * 8 + (lane & 3) * 2;
+        uint32_t* p = reinterpret_cast<uint32_t*>(S + swz<CH>(r, col >> 3) + (col & 7));
+        const uint32_t w = Elem<T>::pack(v[mt][nt][2 * h], v[mt][nt][2 * h + 1]);
+        const float2 o = Elem<T>::unpack(*p), g = Elem<T>::unpack(w);
+        dot[mt][h] = fmaf(o.x, g.x, fmaf(o.y, g.y, dot[mt][h]));
+        *p = w;
+      }
+    }
+}
+
 // Gathers rows i < m (token i*b + j) of a [N][W] tensor, columns [c0*8, (c0+nch)*8), into a
 // swizzled [MP][CH] tile; rows >= m, and rows whose token < skip, are zero-filled.
 template <typename T, int CH>
@@ -474,14 +497,19 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
       }
   }
   __syncwarp();
-  // dout_k[:D] = sum_i (scale dlog_ik) q_i ; last: dout_k[D:] = sum_i a_ik dz_i   (staged in so)
+  // dout_k[:D] = sum_i (scale dlog_ik) q_i ; last: dout_k[D:] = sum_i a_ik dz_i   (staged in so,
+  // over out; delta_k = sum_c out_k[c] dout_k[c] is summed on the way, the preprocessing of the
+  // R step's attention backward)
   T* gdo = static_cast<T*>(p.dout) + bh * N * p.dw;
+  float dot[MP / 16][2];
+#pragma unroll
+  for (int mt = 0; mt < MP / 16; ++mt) dot[mt][0] = dot[mt][1] = 0.f;
 #pragma unroll 1
   for (int half = 0; half < D / 64; ++half) {
     float acc[MP / 16][8][4];
     zero<MP>(acc);
     mm_tn64<T, MP, DCH>(acc, sd, sq, half * 8, lane);
-    stage_rows64<T, MP, OCH>(so, half * 8, acc, nullptr, lane);
+    stage_rows64_dot<T, MP, OCH>(so, half * 8, acc, dot, lane);
   }
   if (LAST) {
 #pragma unroll 1
@@ -489,8 +517,20 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
       float acc[MP / 16][8][4];
       zero<MP>(acc);
       mm_tn64<T, MP, DCH>(acc, sa, sg, half * 8, lane);
-      stage_rows64<T, MP, OCH>(so, DCH + half * 8, acc, nullptr, lane);
+      stage_rows64_dot<T, MP, OCH>(so, DCH + half * 8, acc, dot, lane);
     }
+  }
+  if (p.delta_out) {
+#pragma unroll
+    for (int mt = 0; mt < MP / 16; ++mt)
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        float d = dot[mt][h];
+        d += __shfl_xor_sync(0xffffffffu, d, 1);
+        d += __shfl_xor_sync(0xffffffffu, d, 2);
+        const int r = mt * 16 + (lane >> 2) + h * 8;
+        if ((lane & 3) == 0 && r < m) p.delta_out[bh * N + (int64_t)r * p.b + j] = d;
+      }
   }
   __syncwarp();
   scatter<T, OCH>(gdo, so, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);

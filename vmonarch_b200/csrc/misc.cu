@@ -21,7 +21,8 @@ template <typename T, int LPR>
 __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_bs, const T* dout, int64_t do_bs,
                                                           const float* lse, const float* ent, const float* dent,
                                                           float* cc, float* gg, int64_t rows, int n_q, int dv,
-                                                          float* fold, int64_t n_pad, int64_t plane, float sm_scale) {
+                                                          float* fold, int64_t n_pad, int64_t plane, float sm_scale,
+                                                          const float* delta) {
   constexpr int RPW = 32 / LPR;
   const int lane = threadIdx.x & 31, gl = lane % LPR;
   const int64_t row = ((int64_t)blockIdx.x * 8 + (threadIdx.x >> 5)) * RPW + lane / LPR;
@@ -30,7 +31,7 @@ __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_
   const int64_t bi = live ? row / rp : 0, r = live ? row % rp : 0;
   const bool real = live && r < n_q;      // false: padding row of the folded planes
   float acc = 0.f;
-  if (real) {
+  if (real && !delta) {
     const uint4* po = reinterpret_cast<const uint4*>(o + bi * o_bs + r * dv);
     const uint4* pd = reinterpret_cast<const uint4*>(dout + bi * do_bs + r * dv);
     uint4 va[4], vb[4];
@@ -60,6 +61,7 @@ __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_
     return;
   }
   const int64_t src = bi * n_q + r;  // row of the [batch][n_q] inputs
+  if (delta) acc = delta[src];       // sum o dO precomputed by the caller
   float c = acc, g = 0.f;
   if (dent) {
     const float de = dent[src];
@@ -73,29 +75,29 @@ __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_
     fold[2 * plane + row] = -sm_scale * g;
   } else {
     cc[src] = c;
-    gg[src] = g;
+    if (gg) gg[src] = g;
   }
 }
 
 template <typename T, int LPR>
 void launch_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse, const float* ent,
                 const float* dent, float* cc, float* gg, int64_t rows, int n_q, int dv, float* fold, int64_t n_pad,
-                int64_t plane, float sm_scale, cudaStream_t st) {
+                int64_t plane, float sm_scale, const float* delta, cudaStream_t st) {
   const int64_t warps = (rows + 32 / LPR - 1) / (32 / LPR);
   fea_bwd_pre_kernel<T, LPR><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
       static_cast<const T*>(o), o_bs, static_cast<const T*>(dout), do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold,
-      n_pad, plane, sm_scale);
+      n_pad, plane, sm_scale, delta);
 }
 
 cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
-                        float* fold, int64_t n_pad, float sm_scale, bool bf16, cudaStream_t st) {
+                        float* fold, int64_t n_pad, float sm_scale, const float* delta, bool bf16, cudaStream_t st) {
   const int64_t rows = batch * (fold ? n_pad : n_q);
   const int64_t plane = batch * n_pad;
   if ((rows + 3) / 4 / 8 + 1 > 0x7fffffff) return cudaErrorInvalidConfiguration;
   if (dv != 64 && dv != 128 && dv != 256) return cudaErrorInvalidValue;
   const int lpr = dv / 32;
-#define VMB_PRE(TT, L) launch_pre<TT, L>(o, o_bs, dout, do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale, st)
+#define VMB_PRE(TT, L) launch_pre<TT, L>(o, o_bs, dout, do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale, delta, st)
   if (bf16) {
     if (lpr == 2) VMB_PRE(__nv_bfloat16, 2); else if (lpr == 4) VMB_PRE(__nv_bfloat16, 4); else VMB_PRE(__nv_bfloat16, 8);
   } else {

@@ -76,7 +76,7 @@ def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
 
 
 def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, ent=None, dent=None, v2=None,
-            grad_v2=None, grad_mode: int = 0, v_is_k: bool = False) -> None:
+            grad_v2=None, grad_mode: int = 0, v_is_k: bool = False, delta=None) -> None:
     """Backward of :func:`fea_fwd`; see ``vmb_fea_bwd`` in the header for the modes."""
     q3, k3, v3, o3, do3 = _flat3(q), _flat3(k), _flat3(v), _flat3(o), _flat3(dout)
     a = N.FeaBwdArgs()
@@ -89,6 +89,7 @@ def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, e
     a.o, a.o_bs = o3.data_ptr(), _bs(o3)
     a.dout, a.do_bs = do3.data_ptr(), _bs(do3)
     a.lse, a.ent, a.dent = N.ptr(lse), N.ptr(ent), N.ptr(dent)
+    a.delta = N.ptr(delta)  # optional sum o . dout per query row (e.g. from lstep_bwd's delta_out)
     gq3, gk3 = _flat3(grad_q), _flat3(grad_k)
     a.grad_q, a.grad_q_bs = gq3.data_ptr(), _bs(gq3)
     a.grad_k, a.grad_k_bs = gk3.data_ptr(), _bs(gk3)
@@ -132,12 +133,13 @@ def lstep_fwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, *,
 
 
 def lstep_bwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, dq, dout, *, du=None, dz=None,
-              skip_rows: int = 0, dq_store: bool = False) -> None:
+              skip_rows: int = 0, dq_store: bool = False, delta_out=None) -> None:
     """Monarch L step backward: adds into dq (fp32; overwrites it when dq_store), writes dout (gradient
-    of the R-step output)."""
+    of the R-step output) and, when given, delta_out = sum out . dout per token (fp32)."""
     a = _lstep_args(q, out, ent, m, b, scale, min_col_mass, dz is not None, skip_rows)
     a.du, a.dz, a.dq, a.dout = N.ptr(du), N.ptr(dz), dq.data_ptr(), dout.data_ptr()
     a.dq_store = int(dq_store)
+    a.delta_out = N.ptr(delta_out)
     _call("vmb_lstep_bwd", N.lib.vmb_lstep_bwd, a, q.device)
 
 

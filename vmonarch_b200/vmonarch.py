@@ -110,11 +110,15 @@ class _VMonarchAttention(torch.autograd.Function):
             sm = ctx.sms[it]
             last = it == n_it - 1
             dout = torch.empty_like(out)
+            # the L step also produces the R-step backward's delta = sum out . dout per token, so
+            # the attention backward skips its own pass over out and dout
+            delta = (torch.empty((BH, N), device=dev, dtype=torch.float32)
+                     if out.size(-1) in (64, 128, 256) else None)
             if last:
                 ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, dz=dz, skip_rows=rr,
-                              dq_store=True)
+                              dq_store=True, delta_out=delta)
             else:
-                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, du=du)
+                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, du=du, delta_out=delta)
             gq = dq_acc if it == 0 else torch.empty((BH, N, D), device=dev, dtype=torch.float32)
             gq_fresh = it != 0
             # one grad mode per call: overwrite only when every target is fresh, otherwise clear
@@ -130,7 +134,8 @@ class _VMonarchAttention(torch.autograd.Function):
                 mode = 1
             ops.fea_bwd(grid(u), grid(kf), grid(kf), grid(out), grid(dout), lse.view(BH * m, b), grid(gq),
                         grid(dk_acc), None, sm, v2=grid(vf) if last else None,
-                        grad_v2=grid(dv_acc) if last else None, grad_mode=mode, v_is_k=True)
+                        grad_v2=grid(dv_acc) if last else None, grad_mode=mode, v_is_k=True,
+                        delta=delta.view(BH * m, b) if delta is not None else None)
             kv_fresh = False
             du = gq
 
