@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VMB_ABI_VERSION 2
+#define VMB_ABI_VERSION 3
 
 #define VMB_DTYPE_BF16 0
 #define VMB_DTYPE_F16 1
@@ -129,6 +129,9 @@ typedef struct vmb_fea_bwd_args {
   float sm_scale;
   const float* delta;  /* optional [batch][n_q] fp32: sum_c o[c] dout[c] per query row, precomputed
                           by the caller (vmb_lstep_bwd's delta_out); NULL: computed here (ABI 2) */
+  int32_t deterministic; /* nonzero: bitwise reproducible gradients. Zero lets grad_mode 1 / 2 with
+                            v_is_k, dv == d == 128 and n_kv <= 4096 form dQ with concurrent fp32
+                            reductions (one kernel fewer; summation order varies) (ABI 3) */
 } vmb_fea_bwd_args;
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);

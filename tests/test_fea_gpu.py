@@ -172,3 +172,39 @@ def test_grad_mode_overwrite_equals_add_into_zeros(D):
             assert torch.equal(a, p)
         else:  # the mma.sync kernels add dQ with atomics: the summation order varies run to run
             torch.testing.assert_close(p, a, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("n", [300, 1560, 4096])
+@pytest.mark.parametrize("mode", [1, 2])
+def test_fused_dq_backward_v_is_k(n, mode):
+    # V aliasing K with Dv = D = 128 and <= 32 key tiles (the first VMonarch R step): dQ is formed
+    # inside the dK kernel and reduce-added into fp32. Check it against the deterministic two-kernel
+    # path, against the fp32 oracle (k in both roles), and the overwrite mode over NaN-filled buffers.
+    from vmonarch_b200 import ops
+    gen = torch.Generator().manual_seed(n + mode)
+    B, D = 3, 128
+    q, k, do = (torch.randn(B, n, D, generator=gen).bfloat16() for _ in range(3))
+    de = torch.randn(B, n, generator=gen) * 0.1
+    sm = D ** -0.5
+    qc, kc, doc, dec = q.cuda(), k.cuda(), do.cuda(), de.cuda()
+    o = torch.empty_like(qc)
+    lse, ent = torch.empty(B, n, device="cuda"), torch.empty(B, n, device="cuda")
+    ops.fea_fwd(qc, kc, kc, o, lse, ent, sm)
+    out = {}
+    for det in (True, False):
+        fill = float("nan") if mode == 2 else 0.0
+        gq, gk = (torch.full((B, n, D), fill, device="cuda") for _ in range(2))
+        ops.fea_bwd(qc, kc, kc, o, doc, lse, gq, gk, None, sm, ent=ent, dent=dec, grad_mode=mode, v_is_k=True,
+                    deterministic=det)
+        out[det] = (gq.cpu(), gk.cpu())
+    torch.cuda.synchronize()
+    for g_f, g_d in zip(out[False], out[True]):
+        assert torch.isfinite(g_f).all()
+        assert max_rel_err(g_f, g_d) <= 1e-3
+    if n == 300:
+        ql, kl = q.float().requires_grad_(), k.float().requires_grad_()
+        o_r, e_r = oracle.entropy_attention(ql, kl, kl, sm)
+        gq_r, gk_r = torch.autograd.grad((o_r * do.float()).sum() + (e_r * de).sum(), (ql, kl))
+        for g, r in zip(out[False], (gq_r, gk_r)):
+            assert max_rel_err(g, r) <= 3e-2
+            assert (g - r).abs().max() <= max(5e-2, 8e-3 * r.abs().max().item())

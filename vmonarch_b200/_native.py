@@ -25,7 +25,7 @@ c_vp = ctypes.c_void_p
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 
-ABI_VERSION = 2  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+ABI_VERSION = 3  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
 
 
 class FeaFwdArgs(ctypes.Structure):
@@ -62,6 +62,7 @@ class FeaBwdArgs(ctypes.Structure):
         ("grad_mode", c_i32), ("v_is_k", c_i32),
         ("sm_scale", ctypes.c_float),
         ("delta", c_vp),
+        ("deterministic", c_i32),
     ]
 
 

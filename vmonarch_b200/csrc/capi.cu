@@ -136,12 +136,23 @@ static bool bwd_uses_sm100(const vmb_fea_bwd_args* a) {
   return vmb::fea_bwd_sm100_supported(a->d, a->dv, a->dv1, a->v_is_k != 0);
 }
 
+// tcgen05 path: dQ formed inside the dK kernel (no dq kernel, no split)
+static bool bwd_fuses_dq(const vmb_fea_bwd_args* a) {
+  return vmb::fea_bwd_fuses_dq((int)a->n_kv, a->dv, a->v_is_k != 0, a->grad_mode, a->deterministic != 0);
+}
+
+// tcgen05 path: CTAs sharing one query tile's key range in the dq kernel (1: no split)
+static int bwd_dq_split(const vmb_fea_bwd_args* a) {
+  if (bwd_fuses_dq(a)) return 1;
+  return vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode != 0);
+}
+
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
   if (!a || a->batch < 0 || a->n_q < 0) return -1;
   if (bwd_uses_sm100(a)) {
     const int64_t n_pad = round_up(a->n_q, 128);
     int64_t bytes = 3 * round_up(a->batch * n_pad * 4, 256);
-    const int split = vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode != 0);
+    const int split = bwd_dq_split(a);
     if (split > 1) bytes += round_up((int64_t)split * a->batch * n_pad * 128 * 4, 256);
     return bytes;
   }
@@ -189,7 +200,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   float* gg = sm100 ? nullptr : reinterpret_cast<float*>(ws + round_up(rows * 4, 256));
   float* dq_acc =
       (!sm100 && a->grad_mode == 0) ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
-  count(sm100 ? 3 : (dq_acc ? 3 : 2));
+  count(sm100 ? (bwd_fuses_dq(a) ? 2 : (bwd_dq_split(a) > 1 ? 4 : 3)) : (dq_acc ? 3 : 2));
   cudaError_t e = vmb::fea_bwd_pre(a->o, a->o_bs, a->dout, a->do_bs, a->lse, a->ent, a->dent, cc, gg, a->batch,
                                    (int)a->n_q, a->dv, fold, n_pad, a->sm_scale, a->delta, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(pre)");
@@ -201,7 +212,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.dout = a->dout; p.lse = a->lse; p.cc = cc; p.gg = gg;
   p.fold = fold; p.n_pad = n_pad;
   p.dq_part = nullptr;
-  if (sm100 && vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode != 0) > 1)
+  if (sm100 && bwd_dq_split(a) > 1)
     p.dq_part = reinterpret_cast<float*>(ws + 3 * round_up(a->batch * n_pad * 4, 256));
   p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
   p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
@@ -213,6 +224,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.acc_q = a->grad_mode;
   p.sm_scale = a->sm_scale;
   p.scale_log2 = a->sm_scale * kLog2eHost;
+  p.deterministic = a->deterministic != 0;
   if (sm100) return cuda_status(vmb::fea_bwd_sm100(p, a->batch, a->dv, a->v_is_k != 0, bf16, st), "vmb_fea_bwd");
   if (a->grad_mode == 2) {
     // the mma.sync kernels only add: clear the fp32 gradients, then accumulate

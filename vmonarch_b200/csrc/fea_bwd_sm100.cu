@@ -3,8 +3,8 @@
 // per-row constants c_i, g_i computed by fea_bwd_pre: dS = P (dP - c_i - g_i x_ij)).
 //
 // TMEM holds 512 fp32 columns per SM, too few for S^T, dP^T, dK, dV and dQ of one tile at once, so
-// the backward is two kernels (7 MMAs per 128x64 tile pair instead of 5, but no atomics and a
-// deterministic result):
+// in general the backward is two kernels (7 MMAs per 128x64 tile pair instead of 5, but no atomics
+// and a deterministic result):
 //
 // dkdv kernel: CTA = 128 keys of one sequence, walks the query tiles (64 rows):
 //   S^T = K Q^T, dP^T = W dO^T                  (SS MMAs, M = 128 keys, N = 64 queries)
@@ -13,11 +13,20 @@
 //   dK += dS^T Q;  dV += P^T dO                  (TS MMAs, A = P^T / dS^T from TMEM)
 //   With V aliasing K (the VMonarch R step, W = [K | V2]) the value gradient of the K columns is
 //   added into dK by one more TS MMA (dK += P^T dO[:, :128]) and dV holds the V2 columns.
-//   TMEM: S^T [0,64) dP^T [64,128) P^T 2x32 [128,192) dS^T 2x32 [192,256) dK [256,384) dV [384,512)
-// dq kernel: CTA = 128 queries, walks the key tiles (64 rows):
+//   TMEM: buffer b (query tile parity) S^T [128b, 128b+64) dP^T [128b+64, 128b+128),
+//   dK [256,384), dV [384,512)
+// dq kernel: CTA = 128 queries, walks the key tiles (128 rows):
 //   S = Q K^T, dP = dO W^T (SS, double-buffered in TMEM), dS (thread = query row) -> TMEM,
-//   dQ += dS K (TS). TMEM: S 2x64 [0,128) dP 2x64 [128,256) dS 2x32 [256,320) dQ [384,512)
+//   dQ += dS K (TS).
 // Both write their gradients directly (bf16, or added into fp32 accumulators in grad_mode 1).
+//
+// Fused dQ (FQ, V aliasing K with no V2, fp32 dQ, few key tiles per sequence: the first VMonarch R
+// step): the dK kernel also stages dS^T (bf16) in shared memory and forms dQ^T = K^T dS^T
+// (SS MMA, both operands M/N-major, M = 128 head dims, N = 64 queries) into the free dV columns
+// (two buffers [384 + 64b, 448 + 64b)); the compute threads reduce-add it into the fp32 dQ
+// (thread = head-dim row, a warp covers 128 contiguous bytes of one query row), and the dq kernel
+// is not run: 5 MMAs per tile pair, at the price of n_kv / 128 fp32 reductions per dQ element
+// (summation order varies between runs).
 // Tails: rows past n_q / n_kv load as zeros (TMA), query statistics past n_q are (+inf, 0, 0) so
 // their P is 0; gradients are only stored for valid rows. Every wait is bounded (sm100.cuh).
 #include <algorithm>
@@ -59,6 +68,8 @@ struct Sm100BwdParams {
   int n_seq;            // sequences (batch) of the call
   int acc;       // 1: fp32 gradients added into (TMA reduce-add); 2: fp32 stores; 0: 16-bit stores
   float scale_log2, sm_scale;
+  float* dq;     // fused dQ: fp32 [batch][n_q][128] (batch stride dq_bs), added into
+  int64_t dq_bs;
 };
 
 // Gradient epilogue. The 128 x 128 fp32 accumulator tile in TMEM (thread = row = TMEM lane) is
@@ -130,24 +141,32 @@ __device__ __forceinline__ void prob_dscore(uint32_t s0, uint32_t s1, uint32_t d
   ds_out = Elem<T>::pack(ds.x, ds.y);
 }
 
-template <int XA, bool VK, int NQS>
+template <int XA, bool VK, int NQS, bool FQ = false>
 struct DkdvCfg {
   static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
   static constexpr int RES = (2 + XA) * kAtom128;                 // resident K | X
+  static constexpr int DS = FQ ? 2 * kAtom128 : 0;                // fused dQ: dS^T of both streams
   static constexpr int SLOT_T = (2 + DW / 64) * kAtom64;          // Q | dO tiles of one query tile
   static constexpr int SLOT = SLOT_T + 1024;                      // + statistics: LSE2, c, g x 64
-  static constexpr int SMEM = 1024 + RES + NQS * SLOT;
+  static constexpr int SMEM = 1024 + RES + DS + NQS * SLOT;
   static constexpr bool HAS_DV = XA > 0;
   static_assert(SMEM <= 232448, "shared memory budget");
+  static_assert(!FQ || (VK && XA == 0), "fused dQ needs the dV columns of TMEM");
 };
 
-template <typename T, int XA, bool VK, int NQS, int NWG>
+__device__ __forceinline__ void red_add_f32(float* ptr, float v) {
+  asm volatile("red.global.add.f32 [%0], %1;" ::"l"(ptr), "f"(v) : "memory");
+}
+
+template <typename T, int XA, bool VK, int NQS, int NWG, bool FQ = false>
 __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const __grid_constant__ Sm100BwdParams p) {
-  using C = DkdvCfg<XA, VK, NQS>;
+  using C = DkdvCfg<XA, VK, NQS, FQ>;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);   // S^T, dP^T
   constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);  // dK, dV (B MN-major)
+  constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 64, true, true);     // dQ^T = K^T dS^T (both MN-major)
   static_assert(NWG == 2 || NWG == 4, "two or four compute warpgroups");
+  static_assert(!FQ || NWG == 4, "fused dQ: two warpgroups per stream, 32 queries each");
   // Column of the packed P^T / dS^T of queries [16kk, 16kk + 16) inside a tile's S^T / dP^T:
   // two warpgroups (one per tile) write halves h at [16h, 16h + 16); four (two per tile, one per
   // 32-query half) write half h at [32h, 32h + 16), inside the range that warpgroup loaded itself.
@@ -162,11 +181,16 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   const int bi = blockIdx.x / p.n_tiles;
   const int k0 = (blockIdx.x % p.n_tiles) * 128;
   const int nq = (p.n_q + 63) / 64;
+  // Query tile of step i. With fused dQ the key tiles of a sequence start their walks at different
+  // query tiles, so the concurrent reductions into one dQ row come from different steps.
+  const int rot = FQ ? (2 * (blockIdx.x % p.n_tiles)) % nq : 0;
+  auto qtile = [&](int i) { return FQ ? (i + rot < nq ? i + rot : i + rot - nq) : i; };
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sRes = sbase;                       // K atoms, then X atoms
   const uint32_t sW = VK ? sRes : sRes + 2 * kAtom128;
-  const uint32_t sSlots = sbase + C::RES;
+  const uint32_t sDS = sbase + C::RES;               // fused dQ: dS^T of stream b at sDS + b * kAtom128
+  const uint32_t sSlots = sbase + C::RES + C::DS;
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t BAR_KV = bar0;
   auto BAR_QFULL = [&](int s) { return bar0 + 8u * (1 + s); };
@@ -221,21 +245,23 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
           !__all_sync(0xffffffffu, mbar_wait(BAR_QEMPTY(s), ((i / NQS) - 1) & 1, abort, &g_bwd_err, 1)))
         break;
       if (lane == 0) {
+        const int q0 = qtile(i) * 64;
         mbar_expect_tx(BAR_QFULL(s), C::SLOT_T + 3 * 256);
-        tma_load_3d(slot_q(s), &p.tm_c, 0, i * 64, bi, BAR_QFULL(s));
-        tma_load_3d(slot_q(s) + kAtom64, &p.tm_c, 64, i * 64, bi, BAR_QFULL(s));
-        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(slot_do(s) + a * kAtom64, &p.tm_d, 64 * a, i * 64, bi, BAR_QFULL(s));
+        tma_load_3d(slot_q(s), &p.tm_c, 0, q0, bi, BAR_QFULL(s));
+        tma_load_3d(slot_q(s) + kAtom64, &p.tm_c, 64, q0, bi, BAR_QFULL(s));
+        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(slot_do(s) + a * kAtom64, &p.tm_d, 64 * a, q0, bi, BAR_QFULL(s));
         // the 64 queries' folded statistics: one 256-byte copy per plane (rows padded to 128)
-        const int64_t r0 = (int64_t)bi * p.n_pad + i * 64;
+        const int64_t r0 = (int64_t)bi * p.n_pad + q0;
         bulk_load(slot_stats(s), p.nl + r0, 256, BAR_QFULL(s));
         bulk_load(slot_stats(s) + 256, p.nc + r0, 256, BAR_QFULL(s));
         bulk_load(slot_stats(s) + 512, p.ng + r0, 256, BAR_QFULL(s));
         // bring the tile NQS loads ahead into L2: a slot is reloaded only ~NQS - 2 tiles before
         // its use, less than a DRAM round trip under this kernel's load
         if (i + NQS < nq) {
-          tma_prefetch_3d(&p.tm_c, 0, (i + NQS) * 64, bi);
-          tma_prefetch_3d(&p.tm_c, 64, (i + NQS) * 64, bi);
-          for (int a = 0; a < C::DW / 64; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, (i + NQS) * 64, bi);
+          const int qa = qtile(i + NQS) * 64;
+          tma_prefetch_3d(&p.tm_c, 0, qa, bi);
+          tma_prefetch_3d(&p.tm_c, 64, qa, bi);
+          for (int a = 0; a < C::DW / 64; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, qa, bi);
         }
       }
       armed[s] = i / NQS + 1;
@@ -303,8 +329,17 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
                      (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit_if(leader, BAR_QEMPTY(s));
+          if (FQ) {
+            // dQ^T = K^T dS^T over the 128 keys (A: the resident K read M-major; B: the staged dS^T)
+            const uint32_t dqt = tmem + 384 + 64 * (i & 1), sds = sDS + (i & 1) * kAtom128;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk)
+              mma_ss_if(leader, dqt, smem_desc_sw128(sRes + kk * 2048, kAtom128, 1024),
+                        smem_desc_sw128(sds + kk * 2048, kAtom128, 1024), IDESC_DQ, kk > 0);
+          }
         }
         // the next S^T / dP^T of this buffer is issued after the MMAs that read its P^T / dS^T
+        // (and, with fused dQ, after dQ^T of this tile: its completion also completes dQ^T)
         if (i + 2 < nq) ok = issue_sp(i + 2);
       }
       if (elect_one()) {
@@ -328,12 +363,26 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       return __all_sync(0xffffffffu, mine);
     };
     const uint32_t ts = tmem + lane_off + 128 * stm, tdp = ts + 64;
+    // fused dQ: reduce-add this warpgroup's 32 queries of dQ^T(j) (thread = head-dim row) into dQ
+    auto drain_dq = [&](int j) {
+      uint32_t v[32];
+      tmem_ld32(tmem + lane_off + 384 + 64 * (j & 1) + 32 * h0, v);
+      tmem_wait_ld();
+      const int q0 = qtile(j) * 64 + 32 * h0;
+      float* dst = p.dq + (int64_t)bi * p.dq_bs + (int64_t)q0 * 128 + row;
+      const int nv = min(32, p.n_q - q0);
+#pragma unroll
+      for (int c = 0; c < 32; ++c)
+        if (c < nv) red_add_f32(dst + c * 128, __uint_as_float(v[c]));
+    };
     bool ok = true;
     for (int i = stm; i < nq; i += 2) {
       const int s = i % NQS;
       if (!warp_wait(BAR_SPFULL(stm), (i >> 1) & 1, 8)) { ok = false; break; }
       if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
       tc_fence_after();
+      // S^T(i) was issued after dQ^T(i - 2), so that tile's dQ^T is complete and its dS^T buffer free
+      if (FQ && i >= 2) drain_dq(i - 2);
       const uint32_t st = slot_stats(s);
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
       // 16-query chunks of this warpgroup's half(s): P^T / dS^T of chunk qc go to columns pcol(qc) of
@@ -359,13 +408,27 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         }
         tmem_st8(ts + pcol(qc), pk);
         tmem_st8(tdp + pcol(qc), dk);
+        if (FQ) {  // dS^T row (key) `row`, queries [16qc, 16qc + 16): 16-byte chunks 2qc, 2qc + 1, swizzled
+          const uint32_t rb = sDS + stm * kAtom128 + row * 128;
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + (((2 * qc) ^ (row & 7)) << 4)), "r"(dk[0]),
+                       "r"(dk[1]), "r"(dk[2]), "r"(dk[3])
+                       : "memory");
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + (((2 * qc + 1) ^ (row & 7)) << 4)),
+                       "r"(dk[4]), "r"(dk[5]), "r"(dk[6]), "r"(dk[7])
+                       : "memory");
+        }
       }
       tmem_wait_st();
+      if (FQ) fence_proxy_async_smem();  // dS^T is read by the dQ^T MMA (async proxy)
       tc_fence_before();
       mbar_arrive(BAR_PDSFULL(stm));
     }
     if (ok) ok = warp_wait(BAR_DONE, 0, 8);
     tc_fence_after();
+    if (FQ && ok) {  // the stream's last tile
+      const int last = stm + 2 * ((nq - 1 - stm) >> 1);
+      if (stm < nq) drain_dq(last);
+    }
     // epilogue: stage dK (and dV) in the idle query slots, one thread writes them with TMA. The
     // warpgroups split the 32-column chunks: with dV, the first half of them stages dK, the second
     // dV; without, all stage dK.
@@ -764,6 +827,17 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.sm_scale = b.sm_scale;
   cudaError_t e;
   const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
+  if (fea_bwd_fuses_dq(b.n_kv, dv, vk, b.acc_q, b.deterministic)) {
+    // dQ comes from the dK kernel as reductions into fp32: clear it first in the overwrite mode
+    if (b.acc_q == 2) {
+      e = cudaMemset2DAsync(b.dq, b.dq_bs * 4, 0, (size_t)b.n_q * 128 * 4, batch, st);
+      if (e != cudaSuccess) return e;
+    }
+    pa.dq = b.dq;
+    pa.dq_bs = b.dq_bs;
+    return run(fea_bwd_dkdv_kernel<T, 0, true, 4, kDkdvWarpgroups, true>, DkdvCfg<0, true, 4, true>::SMEM, blocks_a,
+               kDkdvThreads, pa, st);
+  }
   if (vk && xa > 0) {
     e = run(fea_bwd_dkdv_kernel<T, 2, true, 3, kDkdvWarpgroups>, DkdvCfg<2, true, 3>::SMEM, blocks_a, kDkdvThreads, pa, st);
   } else if (vk) {
@@ -852,6 +926,12 @@ int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc) {
     }
   }
   return best;
+}
+
+bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) {
+  // dQ from the dK kernel (no dq kernel) when V aliases K without V2 (free TMEM columns), dQ is
+  // fp32 (reductions) and each dQ element receives at most 32 of them (<= 32 key tiles)
+  return vk && dv == 128 && acc_q != 0 && !deterministic && (n_kv + 127) / 128 <= 32;
 }
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {

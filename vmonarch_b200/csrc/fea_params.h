@@ -42,6 +42,7 @@ struct BwdParams {
   int acc_q;          // 1: dq is an fp32 buffer that is added into (else element dtype)
   float scale_log2;   // sm_scale * log2(e)
   float sm_scale;
+  bool deterministic;  // bitwise reproducible results (no concurrent fp32 reductions into dq)
 };
 
 }  // namespace vmb

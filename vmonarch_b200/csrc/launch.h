@@ -35,6 +35,8 @@ cudaError_t fea_bwd_sm100(const BwdParams& p, int64_t batch, int dv, bool vk, bo
 // the accumulate mode splits). The partial tiles need split * batch * round_up(n_q, 128) * 128
 // fp32 of workspace when the result is above 1.
 int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc);
+// True when the tcgen05 backward forms dQ inside the dK kernel (fp32 reductions, no dq kernel).
+bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic);
 // Workspace bytes that let the tcgen05 forward split long key ranges (0: it would not split).
 int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk);
 // Key-range split the tcgen05 forward will use with this workspace (1 = none).

@@ -76,8 +76,11 @@ def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
 
 
 def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, ent=None, dent=None, v2=None,
-            grad_v2=None, grad_mode: int = 0, v_is_k: bool = False, delta=None) -> None:
-    """Backward of :func:`fea_fwd`; see ``vmb_fea_bwd`` in the header for the modes."""
+            grad_v2=None, grad_mode: int = 0, v_is_k: bool = False, delta=None, deterministic=None) -> None:
+    """Backward of :func:`fea_fwd`; see ``vmb_fea_bwd`` in the header for the modes. ``deterministic``
+    (default: ``torch.are_deterministic_algorithms_enabled()``) rules out concurrent fp32 reductions."""
+    if deterministic is None:
+        deterministic = torch.are_deterministic_algorithms_enabled()
     q3, k3, v3, o3, do3 = _flat3(q), _flat3(k), _flat3(v), _flat3(o), _flat3(dout)
     a = N.FeaBwdArgs()
     a.q, a.q_bs = q3.data_ptr(), _bs(q3)
@@ -105,6 +108,7 @@ def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, e
     a.grad_mode = grad_mode
     a.v_is_k = int(v_is_k)
     a.sm_scale = float(sm_scale)
+    a.deterministic = int(bool(deterministic))
     nbytes = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
