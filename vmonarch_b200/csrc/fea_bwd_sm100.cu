@@ -27,8 +27,8 @@
 // (thread = head-dim row, a warp covers 128 contiguous bytes of one query row), and the dq kernel
 // is not run: 5 MMAs per tile pair, at the price of n_kv / 128 fp32 reductions per dQ element
 // (summation order varies between runs).
-// Tails: rows past n_q / n_kv load as zeros (TMA), query statistics past n_q are (+inf, 0, 0) so
-// their P is 0; gradients are only stored for valid rows. Every wait is bounded (sm100.cuh).
+// Tails: rows past n_q / n_kv load as zeros (TMA), the folded statistics of queries past n_q are
+// (-1e30, 0, 0) so their P and dS are 0; gradients are only stored for valid rows. Every wait is bounded (sm100.cuh).
 #include <algorithm>
 
 #include "common.cuh"
@@ -173,7 +173,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   auto pcol = [](int kk) -> uint32_t { return NWG == 4 ? 32 * (kk >> 1) + 8 * (kk & 1) : 8 * kk; };
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5];
+  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5 + (FQ ? 2 : 0)];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -198,6 +198,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   auto BAR_SPFULL = [&](int b) { return bar0 + 8u * (1 + 2 * NQS + b); };
   auto BAR_PDSFULL = [&](int b) { return bar0 + 8u * (3 + 2 * NQS + b); };
   const uint32_t BAR_DONE = bar0 + 8u * (5 + 2 * NQS);
+  // fused dQ: stream b has drained dQ^T of its previous tile and staged dS^T of the current one
+  auto BAR_DQFREE = [&](int b) { return bar0 + 8u * (6 + 2 * NQS + b); };
   volatile int* abort = &abort_sh;
   auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
   auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom64; };
@@ -213,6 +215,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SPFULL(b), 1);
       mbar_init(BAR_PDSFULL(b), 64 * NWG);
+      if (FQ) mbar_init(BAR_DQFREE(b), 64 * NWG);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -330,7 +333,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
           }
           mma_commit_if(leader, BAR_QEMPTY(s));
           if (FQ) {
-            // dQ^T = K^T dS^T over the 128 keys (A: the resident K read M-major; B: the staged dS^T)
+            // dQ^T = K^T dS^T over the 128 keys (A: the resident K read M-major; B: the staged dS^T),
+            // once the stream has drained the dQ^T of its previous tile from this buffer
+            if (!wwait(BAR_DQFREE(i & 1), (i >> 1) & 1, 5)) break;
+            tc_fence_after();
             const uint32_t dqt = tmem + 384 + 64 * (i & 1), sds = sDS + (i & 1) * kAtom128;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
@@ -381,8 +387,6 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       if (!warp_wait(BAR_SPFULL(stm), (i >> 1) & 1, 8)) { ok = false; break; }
       if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
       tc_fence_after();
-      // S^T(i) was issued after dQ^T(i - 2), so that tile's dQ^T is complete and its dS^T buffer free
-      if (FQ && i >= 2) drain_dq(i - 2);
       const uint32_t st = slot_stats(s);
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
       // 16-query chunks of this warpgroup's half(s): P^T / dS^T of chunk qc go to columns pcol(qc) of
@@ -422,6 +426,13 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       if (FQ) fence_proxy_async_smem();  // dS^T is read by the dQ^T MMA (async proxy)
       tc_fence_before();
       mbar_arrive(BAR_PDSFULL(stm));
+      if (FQ) {
+        // while the MMA warp runs this tile's dK MMAs: drain dQ^T(i - 2), complete since S^T(i) was
+        // issued after it; then its buffer may take dQ^T(i)
+        if (i >= 2) drain_dq(i - 2);
+        tc_fence_before();
+        mbar_arrive(BAR_DQFREE(stm));
+      }
     }
     if (ok) ok = warp_wait(BAR_DONE, 0, 8);
     tc_fence_after();
