@@ -208,3 +208,37 @@ def test_fused_dq_backward_v_is_k(n, mode):
         for g, r in zip(out[False], (gq_r, gk_r)):
             assert max_rel_err(g, r) <= 3e-2
             assert (g - r).abs().max() <= max(5e-2, 8e-3 * r.abs().max().item())
+
+
+@pytest.mark.parametrize("n", [300, 1560])
+@pytest.mark.parametrize("mode", [0, 1, 2])
+def test_backward_keys_as_values_with_v2(n, mode):
+    # The last VMonarch R step: values [K | V2] (Dv = 256) with V aliasing K. Gradients of q, of k
+    # (key and value roles summed) and of v2 against the fp32 oracle, in every write mode.
+    from vmonarch_b200 import ops
+    gen = torch.Generator().manual_seed(7 * n + mode)
+    B, D = 2, 128
+    q, k, v2 = (torch.randn(B, n, D, generator=gen).bfloat16() for _ in range(3))
+    do = torch.randn(B, n, 2 * D, generator=gen).bfloat16()
+    de = torch.randn(B, n, generator=gen) * 0.1
+    sm = D ** -0.5
+    qc, kc, v2c, doc, dec = q.cuda(), k.cuda(), v2.cuda(), do.cuda(), de.cuda()
+    o = torch.empty(B, n, 2 * D, dtype=torch.bfloat16, device="cuda")
+    lse, ent = torch.empty(B, n, device="cuda"), torch.empty(B, n, device="cuda")
+    ops.fea_fwd(qc, kc, kc, o, lse, ent, sm, v2=v2c)
+    if mode == 0:
+        gq, gk, gv2 = (torch.empty(B, n, D, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    else:
+        fill = float("nan") if mode == 2 else 0.0
+        gq, gk, gv2 = (torch.full((B, n, D), fill, device="cuda") for _ in range(3))
+    ops.fea_bwd(qc, kc, kc, o, doc, lse, gq, gk, None, sm, ent=ent, dent=dec, v2=v2c, grad_v2=gv2, grad_mode=mode,
+                v_is_k=True)
+    torch.cuda.synchronize()
+    ql, kl, vl = q.float().requires_grad_(), k.float().requires_grad_(), v2.float().requires_grad_()
+    o_r, e_r = oracle.entropy_attention(ql, kl, torch.cat([kl, vl], -1), sm)
+    refs = torch.autograd.grad((o_r * do.float()).sum() + (e_r * de).sum(), (ql, kl, vl))
+    for g, r in zip((gq, gk, gv2), refs):
+        g = g.float().cpu()
+        assert torch.isfinite(g).all()
+        assert max_rel_err(g, r) <= 3e-2
+        assert (g - r).abs().max() <= max(5e-2, 8e-3 * r.abs().max().item())

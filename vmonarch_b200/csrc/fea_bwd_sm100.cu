@@ -45,7 +45,6 @@ namespace {
 
 using namespace sm100;
 
-constexpr int kThreads = 320;          // producer warp, MMA warp, two compute warpgroups on alternate tiles
 constexpr int kDqWarpgroups = 4;       // dQ kernel: compute warpgroups (32 key columns each)
 constexpr int kDqThreads = 64 + 128 * kDqWarpgroups;
 constexpr int kDkdvWarpgroups = 4;     // dK/dV kernel: two per query-tile stream (32 queries each)
@@ -478,9 +477,13 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
 // DOT = false: TMEM S0 [0,128) S1 [128,256) dP [256,384) dQ [384,512); S double-buffered, so
 //   S(j+2) is queued behind dQ(j) while dP(j+1) is issued as soon as tile j's dP has been read.
 // DOT = true (DW = 256): TMEM S [0,128) dP [128,256) dO [256,384) dQ [384,512); dO is staged into
-//   TMEM once by the compute threads, which frees the shared memory for 3-deep K and V2 rings.
-// K and X (V, or V2 when V aliases K) stream through separate rings: X(j) is released after dP(j),
-// K(j) after dQ(j).
+//   TMEM once by the compute threads (dP is a TS MMA). S is single-buffered, so dS goes to shared
+//   memory (K-major, thread = query row) and dQ += dS K is an SS MMA: S(j+1) and dP(j+1) are
+//   issued as soon as tile j's S and dP are in registers and run under the dS math of tile j.
+//   dS(j) is written into the V2 slot of tile j, which dP(j) has finished reading; the slot is
+//   released after dQ(j), so no tile waits for the previous tile's dQ.
+// K and X (V, or V2 when V aliases K) stream through separate rings: X(j) is released after dP(j)
+// (DOT: after dQ(j), whose dS it holds), K(j) after dQ(j).
 template <int XA, bool VK, bool DOT, int NK, int NX>
 struct DqCfg2 {
   static constexpr int DW = VK ? 128 + 64 * XA : 64 * XA;
@@ -489,8 +492,9 @@ struct DqCfg2 {
   static constexpr int KSLOT = 2 * kAtom128;
   static constexpr int XSLOT = XA * kAtom128;
   static constexpr int SMEM = 1024 + RES + NK * KSLOT + NX * XSLOT;
+  static_assert(NK * KSLOT >= 4 * 16384, "the dQ epilogue stages 64 KB in the K ring");
   static_assert(SMEM <= 232448, "shared memory budget");
-  static_assert(!DOT || DW == 256, "dO in TMEM is laid out for DW = 256");
+  static_assert(!DOT || (DW == 256 && XA == 2), "dO in TMEM is laid out for DW = 256; dS fills a V2 slot");
   static_assert((XA == 0) == (NX == 0), "X ring present exactly when there is an X tile");
 };
 
@@ -525,6 +529,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = sbase, sDO = sbase + 2 * kAtom128;
   const uint32_t sK = sbase + C::RES, sX = sK + NK * C::KSLOT;
+  // DOT: dS [128 queries][128 keys] bf16 (two K-major atoms) of tile j in V2 slot j % NX
+  auto sDS = [&](int j) { return sX + (uint32_t)(j % NXB) * C::XSLOT; };
   const uint32_t bar0 = smem_u32(bars);
   auto BAR = [&](int i) { return bar0 + 8u * (uint32_t)i; };
   volatile int* abort = &abort_sh;
@@ -650,7 +656,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
                      kk > 0);
           }
           mma_commit_if(leader, BAR(B_DPFULL));
-          if (XA > 0) mma_commit_if(leader, BAR(B_XEMPTY + x));
+          if (XA > 0 && !DOT) mma_commit_if(leader, BAR(B_XEMPTY + x));  // DOT: after dQ (dS lives there)
         }
         return true;
       };
@@ -660,6 +666,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
       for (int j = 0; ok && j < nk; ++j) {
         if (j + 1 < nk) {
           if (!wwait(BAR(B_DPFREE), j & 1, 64)) break;
+          // DOT: tile j's S is in registers and its dS goes to shared memory, so S(j + 1) may be
+          // written into the one S buffer now
+          if (DOT && !issue_s(j + 1)) break;
           if (!issue_dp(j + 1)) break;
         }
         if (!wwait(BAR(B_DSFULL + j % NS), (j / NS) & 1, 64)) break;
@@ -669,14 +678,20 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
           const uint32_t sb = tmem + 128u * (uint32_t)(j % NS);
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K ; keys [16kk, 16kk+16) of warpgroup 16kk/CW
-            const uint32_t a_tm = sb + CW * (16 * kk / CW) + (16 * kk % CW) / 2;
-            mma_ts_if(leader, tmem + T_DQ, a_tm, smem_desc_sw128(kb + kk * 2048, kAtom128, 1024), IDESC_DQ,
-                   (j > 0 || kk > 0) ? 1u : 0u);
+            const uint64_t bd = smem_desc_sw128(kb + kk * 2048, kAtom128, 1024);
+            if (DOT) {
+              const uint32_t a_sm = sDS(j) + (kk >> 2) * kAtom128 + (kk & 3) * 32;
+              mma_ss_if(leader, tmem + T_DQ, smem_desc_sw128(a_sm, 16, 1024), bd, IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
+            } else {
+              const uint32_t a_tm = sb + CW * (16 * kk / CW) + (16 * kk % CW) / 2;
+              mma_ts_if(leader, tmem + T_DQ, a_tm, bd, IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
+            }
           }
           mma_commit_if(leader, BAR(B_KEMPTY + j % NK));
+          if (DOT) mma_commit_if(leader, BAR(B_XEMPTY + j % NXB));  // V2 slot, then dS of tile j
         }
-        const int nxt = j + NS;  // the next tile that uses this S buffer
-        if (nxt < nk) ok = issue_s(nxt);
+        const int nxt = j + NS;  // the next tile that uses this S buffer (DOT: issued above)
+        if (!DOT && nxt < nk) ok = issue_s(nxt);
       }
       if (elect_one()) {
         mma_commit(BAR(B_DONE));
@@ -745,9 +760,22 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         uint32_t unused;
         prob_dscore<T, false>(sv[e], sv[e + 1], dv[e], dv[e + 1], sc2, sm2, nl2, nc2, ng2, unused, pk[e >> 1]);
       }
-      if (CW == 64) tmem_st32(ts, pk);
-      else tmem_st16(ts, pk);
-      tmem_wait_st();
+      if (DOT) {
+        // dS row `row`, keys [CW wg, CW wg + CW) -> K-major atom (CW wg) / 64, 16-byte chunks from
+        // ((CW wg) % 64) / 8, swizzled, into tile j's V2 slot (dP(j), its reader, has completed)
+        const uint32_t rb = sDS(j) + ((CW * wg) >> 6) * kAtom128 + row * 128;
+        const int c0 = ((CW * wg) & 63) >> 3;
+#pragma unroll
+        for (int t = 0; t < CW / 8; ++t)
+          asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + (((c0 + t) ^ (row & 7)) << 4)),
+                       "r"(pk[4 * t]), "r"(pk[4 * t + 1]), "r"(pk[4 * t + 2]), "r"(pk[4 * t + 3])
+                       : "memory");
+        fence_proxy_async_smem();  // read by the dQ MMA (async proxy)
+      } else {
+        if (CW == 64) tmem_st32(ts, pk);
+        else tmem_st16(ts, pk);
+        tmem_wait_st();
+      }
       tc_fence_before();
       mbar_arrive(BAR(B_DSFULL + b));
     }
