@@ -77,11 +77,12 @@ uint64_t vmb_kernel_launches(void) { return g_launches.load(std::memory_order_re
 
 int vmb_device_status(void* stream, int32_t* out) {
   if (!out) return fail(VMB_EINVAL, "vmb_device_status: null output");
-  int v = 0, w = 0;
+  int v = 0, w = 0, x = 0;
   cudaError_t e = vmb::fea_fwd_sm100_status(static_cast<cudaStream_t>(stream), &v);
   if (e == cudaSuccess) e = vmb::fea_bwd_sm100_status(static_cast<cudaStream_t>(stream), &w);
+  if (e == cudaSuccess) e = vmb::lstep_tc_status(static_cast<cudaStream_t>(stream), &x);
   if (e != cudaSuccess) return cuda_status(e, "vmb_device_status");
-  *out = v | (w << 8);
+  *out = v | (w << 8) | (x << 16);
   return VMB_OK;
 }
 
@@ -285,6 +286,8 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
   p.delta_out = bwd ? a->delta_out : nullptr;
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
+  if (vmb::lstep_tc_supported(p, a->last != 0, bwd))
+    return cuda_status(vmb::lstep_tc_launch(p, a->last != 0, bwd, bf16, st), what);
   if (vmb::lstep_mma_supported(p, a->last != 0))
     return cuda_status(vmb::lstep_mma_launch(p, a->last != 0, bwd, bf16, st), what);
   cudaError_t e = vmb::lstep_launch(p, a->last != 0, bwd, bf16, st);

@@ -51,6 +51,11 @@ cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs
 bool lstep_mma_supported(const LstepParams& p, bool last);
 cudaError_t lstep_mma_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
 cudaError_t lstep_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
+// tcgen05 / TMA L step (D = 128, stacked columns); forward only, and the last step only without
+// skipped tokens.
+bool lstep_tc_supported(const LstepParams& p, bool last, bool bwd);
+cudaError_t lstep_tc_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st);
+cudaError_t lstep_tc_status(cudaStream_t st, int* out);
 size_t lstep_smem_bytes(int m, int d, int dw, bool last, bool bwd);
 
 // Records `code` and a printf-style message as the calling thread's last error; returns `code`.

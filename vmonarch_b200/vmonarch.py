@@ -57,7 +57,9 @@ class _VMonarchAttention(torch.autograd.Function):
                         v2=grid(vf) if last else None)
             if last:
                 z = torch.empty((BH, N, Dv), device=dev, dtype=dt)
-                ops.lstep_fwd(qf, out, ent, m, b, scale, min_col_mass, z=z, skip_rows=rr)
+                # every token of z is produced here (the tensor-core L step writes whole stacked
+                # columns); the exact recompute below then overwrites tokens [0, rr)
+                ops.lstep_fwd(qf, out, ent, m, b, scale, min_col_mass, z=z, skip_rows=0)
                 nxt = None
             else:
                 nxt = torch.empty((BH, N, D), device=dev, dtype=dt)
