@@ -29,12 +29,13 @@ def oracle_lstep(q, out, ent, m, b, D, last, scale, mcm):
 
 @pytest.mark.parametrize("m, b, D, Dv", [(21, 37, 128, 128), (4, 64, 64, 64), (64, 9, 64, 128), (1, 33, 128, 128),
                                          (32, 16, 128, 128)])
-@pytest.mark.parametrize("last", [False, True])
-def test_lstep_forward_and_backward(m, b, D, Dv, last):
+@pytest.mark.parametrize("last, skip_half", [(False, False), (True, False), (True, True)])
+def test_lstep_forward_and_backward(m, b, D, Dv, last, skip_half):
+    # D = 128 forwards without skipped tokens run the tcgen05 kernel, the others mma.sync
     scale, mcm = D ** -0.5, 0.3
     q, out, ent = inputs(m, b, D, Dv, last, m * 7 + b)
     qc, oc, ec = q.cuda(), out.cuda(), ent.cuda()
-    skip = b // 2 if last else 0
+    skip = b // 2 if skip_half else 0
     if last:
         z = torch.zeros(2, m * b, Dv, dtype=torch.bfloat16, device="cuda")
         ops.lstep_fwd(qc, oc, ec, m, b, scale, mcm, z=z, skip_rows=skip)

@@ -37,19 +37,19 @@ struct Tile {
 // contraction starts at chunk xc0 / yc0).
 template <typename T, int MP, int D, int XCH, int YCH>
 __device__ __forceinline__ void mm_rows(float (&acc)[MP / 16][MP / 8][4], const T* X, int xc0, const T* Y, int yc0,
-                                        int lane) {
+                                        int zr, int lane) {
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     uint32_t a[MP / 16][4];
 #pragma unroll
     for (int mt = 0; mt < MP / 16; ++mt)
-      ldsm_x4(smem_u32(X + swz<XCH>(mt * 16 + (lane & 15), xc0 + kk * 2 + (lane >> 4))), a[mt][0], a[mt][1],
-              a[mt][2], a[mt][3]);
+      ldsm_x4(smem_u32(X + swz<XCH>(min(mt * 16 + (lane & 15), zr), xc0 + kk * 2 + (lane >> 4))), a[mt][0],
+              a[mt][1], a[mt][2], a[mt][3]);
 #pragma unroll
     for (int np = 0; np < MP / 16; ++np) {
       uint32_t b0, b1, b2, b3;
-      ldsm_x4(smem_u32(Y + swz<YCH>(np * 16 + (lane & 7) + ((lane >> 4) << 3), yc0 + kk * 2 + ((lane >> 3) & 1))), b0,
-              b1, b2, b3);
+      ldsm_x4(smem_u32(Y + swz<YCH>(min(np * 16 + (lane & 7) + ((lane >> 4) << 3), zr), yc0 + kk * 2 + ((lane >> 3) & 1))),
+              b0, b1, b2, b3);
 #pragma unroll
       for (int mt = 0; mt < MP / 16; ++mt) {
         mma16816<T>(acc[mt][2 * np], a[mt], b0, b1);
@@ -85,7 +85,7 @@ __device__ __forceinline__ void stage_mm(T* S, const float (&v)[MP / 16][MP / 8]
 // out[r][n] (r: MP rows, n: 64 columns from chunk bc0 of B) = sum_i A[r][i] * B[i][n]
 // where A comes from the [MP][SA] staging tile TRANSPOSED (A[r][i] = S[i][r]) and B rows are i.
 template <typename T, int MP, int BCH>
-__device__ __forceinline__ void mm_tn64(float (&acc)[MP / 16][8][4], const T* S, const T* B, int bc0, int lane) {
+__device__ __forceinline__ void mm_tn64(float (&acc)[MP / 16][8][4], const T* S, const T* B, int bc0, int zr, int lane) {
 #pragma unroll
   for (int kk = 0; kk < MP / 16; ++kk) {
     uint32_t a[MP / 16][4];
@@ -94,7 +94,7 @@ __device__ __forceinline__ void mm_tn64(float (&acc)[MP / 16][8][4], const T* S,
     for (int mt = 0; mt < MP / 16; ++mt)
       ldsm_x4_t(smem_u32(S + (kk * 16 + (lane & 7) + ((mi >> 1) << 3)) * Tile<MP>::SA + mt * 16 + ((mi & 1) << 3)),
                 a[mt][0], a[mt][1], a[mt][2], a[mt][3]);
-    const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+    const int r = min(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), zr);
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t b0, b1, b2, b3;
@@ -111,13 +111,13 @@ __device__ __forceinline__ void mm_tn64(float (&acc)[MP / 16][8][4], const T* S,
 // out[i][n] += sum_k A[i][k] * B[k][n] with A given in accumulator layout (registers).
 template <typename T, int MP, int BCH>
 __device__ __forceinline__ void mm_rn64(float (&acc)[MP / 16][8][4], const float (&A)[MP / 16][MP / 8][4], const T* B,
-                                        int bc0, int lane) {
+                                        int bc0, int zr, int lane) {
 #pragma unroll
   for (int kk = 0; kk < MP / 16; ++kk) {
     uint32_t a[MP / 16][4];
 #pragma unroll
     for (int mt = 0; mt < MP / 16; ++mt) frag_from_acc<T, MP>(A, mt, kk, a[mt]);
-    const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
+    const int r = min(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), zr);
 #pragma unroll
     for (int np = 0; np < 4; ++np) {
       uint32_t b0, b1, b2, b3;
@@ -142,12 +142,13 @@ __device__ __forceinline__ void zero(float (&a)[MP / 16][8][4]) {
 // 64 output columns (half of D = 128 or all of D = 64) of an accumulator -> swizzled staging rows.
 template <typename T, int MP, int CH>
 __device__ __forceinline__ void stage_rows64(T* S, int c0, const float (&v)[MP / 16][8][4], const float* rowscale,
-                                             int lane) {
+                                             int m, int lane) {
 #pragma unroll
   for (int mt = 0; mt < MP / 16; ++mt)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = mt * 16 + (lane >> 2) + h * 8;
+      if (r >= m) continue;  // tiles hold rows [0, m) and the zero row m
       const float s = rowscale ? rowscale[r] : 1.f;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
@@ -163,12 +164,13 @@ __device__ __forceinline__ void stage_rows64(T* S, int c0, const float (&v)[MP /
 // and the products are summed per row (this lane's share of sum_c out[c] dout[c]).
 template <typename T, int MP, int CH>
 __device__ __forceinline__ void stage_rows64_dot(T* S, int c0, const float (&v)[MP / 16][8][4],
-                                                 float (&dot)[MP / 16][2], int lane) {
+                                                 float (&dot)[MP / 16][2], int m, int lane) {
 #pragma unroll
   for (int mt = 0; mt < MP / 16; ++mt)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = mt * 16 + (lane >> 2) + h * 8;
+      if (r >= m) continue;
 #pragma unroll
       for (int nt = 0; nt < 8; ++nt) {
         const int col = c0 * 8 + nt * 8 + (lane & 3) * 2;
@@ -182,16 +184,30 @@ __device__ __forceinline__ void stage_rows64_dot(T* S, int c0, const float (&v)[
 }
 
 // Gathers rows i < m (token i*b + j) of a [N][W] tensor, columns [c0*8, (c0+nch)*8), into a
-// swizzled [MP][CH] tile; rows >= m, and rows whose token < skip, are zero-filled.
+// swizzled [m + 1][CH] tile; rows whose token < skip are zero-filled. Row m is the tile's zero row
+// (zero_row), which the MMA loaders read for every row index >= m.
 template <typename T, int CH>
 __device__ __forceinline__ void gather(T* dst, const T* src, int64_t W, int c0, int nch, int m, int64_t b, int j,
-                                       int64_t skip, int MP, int lane) {
-  for (int c = lane; c < MP * nch; c += 32) {
+                                       int64_t skip, int lane) {
+  for (int c = lane; c < m * nch; c += 32) {
     const int i = c / nch, ch = c % nch;
     const int64_t tok = (int64_t)i * b + j;
-    const bool ok = i < m && tok >= skip;
+    const bool ok = tok >= skip;
     cp_async16(smem_u32(dst + swz<CH>(i, c0 + ch)), src + (ok ? tok : 0) * W + (c0 + ch) * 8, ok ? 16 : 0);
   }
+}
+template <typename T, int CH>
+__device__ __forceinline__ void zero_row(T* dst, int m, int lane) {
+  for (int ch = lane; ch < CH; ch += 32) *reinterpret_cast<uint4*>(dst + m * CH * 8 + ch * 8) = make_uint4(0, 0, 0, 0);
+}
+
+// Per-warp shared memory (bytes) of the L-step kernels: gathered tiles of m + 1 rows (the last one
+// zero) and m x m staging tiles of MP rows. The layout below follows the same order.
+template <int MP>
+__host__ __device__ __forceinline__ size_t lstep_warp_bytes(int m, int D, int OW, bool bwd, int esize) {
+  const size_t rows = (size_t)m + 1;
+  return bwd ? (rows * (2 * D + OW) + 2 * (size_t)MP * (MP + 8)) * esize
+             : (rows * (D + OW) + (size_t)MP * (MP + 8)) * esize + MP * sizeof(float);
 }
 
 // Writes rows r < m of a swizzled [MP][CH] staging tile to token r*b + j of a [N][W] tensor.
@@ -280,22 +296,24 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
   constexpr int DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr size_t PER_WARP = (size_t)(MP * D + MP * OW + MP * Tile<MP>::SA) * sizeof(T) + MP * sizeof(float);
-  T* sq = reinterpret_cast<T*>(smem_raw + warp * PER_WARP);
-  T* so = sq + MP * D;
-  T* sa = so + MP * OW;
+  const int m = (int)p.m;
+  T* sq = reinterpret_cast<T*>(smem_raw + warp * lstep_warp_bytes<MP>(m, D, OW, false, sizeof(T)));
+  T* so = sq + (m + 1) * D;
+  T* sa = so + (m + 1) * OW;
   float* svec = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);
 
   const int64_t col = (int64_t)blockIdx.x * kWarpsFwd + warp;
   if (col >= p.bh * p.b) return;  // no block-level barrier below: each warp is independent
   const int64_t bh = col / p.b;
-  const int j = (int)(col % p.b), m = (int)p.m;
+  const int j = (int)(col % p.b);
   const int64_t N = p.m * p.b;
   const T* gq = static_cast<const T*>(p.q) + bh * N * D;
   const T* go = static_cast<const T*>(p.out) + bh * N * p.dw;
-  gather<T, DCH>(sq, gq, D, 0, DCH, m, p.b, j, 0, MP, lane);
-  gather<T, OCH>(so, go, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);
+  gather<T, DCH>(sq, gq, D, 0, DCH, m, p.b, j, 0, lane);
+  gather<T, OCH>(so, go, p.dw, 0, OCH, m, p.b, j, 0, lane);
   cp_async_commit();
+  zero_row<T, DCH>(sq, m, lane);
+  zero_row<T, OCH>(so, m, lane);
   float ent[MP / 8][2];
   load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
   cp_async_wait<0>();
@@ -306,7 +324,7 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
   for (int mt = 0; mt < MP / 16; ++mt)
 #pragma unroll
     for (int nt = 0; nt < MP / 8; ++nt) a[mt][nt][0] = a[mt][nt][1] = a[mt][nt][2] = a[mt][nt][3] = 0.f;
-  mm_rows<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, lane);
+  mm_rows<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, m, lane);
   softmax_rows<MP>(a, ent, p.scale, m, lane);
 
   if (LAST) {
@@ -317,8 +335,8 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
     for (int half = 0; half < D / 64; ++half) {
       float z[MP / 16][8][4];
       zero<MP>(z);
-      mm_rn64<T, MP, OCH>(z, a, so, DCH + half * 8, lane);
-      stage_rows64<T, MP, DCH>(sq, half * 8, z, nullptr, lane);
+      mm_rn64<T, MP, OCH>(z, a, so, DCH + half * 8, m, lane);
+      stage_rows64<T, MP, DCH>(sq, half * 8, z, nullptr, m, lane);
     }
     __syncwarp();
     scatter<T, DCH>(gz, sq, D, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
@@ -338,8 +356,8 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
     for (int half = 0; half < D / 64; ++half) {
       float u[MP / 16][8][4];
       zero<MP>(u);
-      mm_tn64<T, MP, DCH>(u, sa, sq, half * 8, lane);
-      stage_rows64<T, MP, OCH>(so, half * 8, u, svec, lane);  // so (out_D) is free after the logits
+      mm_tn64<T, MP, DCH>(u, sa, sq, half * 8, m, lane);
+      stage_rows64<T, MP, OCH>(so, half * 8, u, svec, m, lane);  // so (out_D) is free after the logits
     }
     __syncwarp();
     scatter<T, OCH>(gu, so, D, 0, DCH, m, p.b, j, 0, MP, lane);
@@ -352,28 +370,30 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   constexpr int DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  constexpr size_t PER_WARP = (size_t)(2 * MP * D + MP * OW + 2 * MP * Tile<MP>::SA) * sizeof(T);
-  T* sq = reinterpret_cast<T*>(smem_raw + warp * PER_WARP);
-  T* so = sq + MP * D;      // out rows (kr | y), later the dout staging
-  T* sg = so + MP * OW;     // du (non-last) or dz (last), element dtype
-  T* sa = sg + MP * D;      // m x m staging (a or a*c)
+  const int m = (int)p.m;
+  T* sq = reinterpret_cast<T*>(smem_raw + warp * lstep_warp_bytes<MP>(m, D, OW, true, sizeof(T)));
+  T* so = sq + (m + 1) * D;     // out rows (kr | y), later the dout staging
+  T* sg = so + (m + 1) * OW;    // du (non-last) or dz (last), element dtype
+  T* sa = sg + (m + 1) * D;     // m x m staging (a or a*c)
   T* sd = sa + MP * Tile<MP>::SA;  // m x m staging (dlog)
 
   const int64_t col = (int64_t)blockIdx.x * kWarpsBwd + warp;
   if (col >= p.bh * p.b) return;
   const int64_t bh = col / p.b;
-  const int j = (int)(col % p.b), m = (int)p.m;
+  const int j = (int)(col % p.b);
   const int64_t N = p.m * p.b;
-  gather<T, DCH>(sq, static_cast<const T*>(p.q) + bh * N * D, D, 0, DCH, m, p.b, j, 0, MP, lane);
-  gather<T, OCH>(so, static_cast<const T*>(p.out) + bh * N * p.dw, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);
-  if (LAST) gather<T, DCH>(sg, static_cast<const T*>(p.dz) + bh * N * D, D, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
+  gather<T, DCH>(sq, static_cast<const T*>(p.q) + bh * N * D, D, 0, DCH, m, p.b, j, 0, lane);
+  gather<T, OCH>(so, static_cast<const T*>(p.out) + bh * N * p.dw, p.dw, 0, OCH, m, p.b, j, 0, lane);
+  if (LAST) gather<T, DCH>(sg, static_cast<const T*>(p.dz) + bh * N * D, D, 0, DCH, m, p.b, j, p.skip_rows, lane);
   cp_async_commit();
+  zero_row<T, DCH>(sq, m, lane);
+  zero_row<T, OCH>(so, m, lane);
+  zero_row<T, DCH>(sg, m, lane);
   if (!LAST) {  // du is fp32: convert while the other rows are in flight
     // four chunks' loads are issued before any is converted, so a warp waits for one memory round
     // trip per four chunks instead of one per chunk
     const float* du = p.du + bh * N * D;
-    constexpr int kChunks = MP * DCH / 32;  // per lane
-    static_assert(kChunks % 4 == 0, "chunk batching");
+    const int kChunks = (m * DCH + 31) / 32;  // per lane, rows < m
 #pragma unroll 1
     for (int t0 = 0; t0 < kChunks; t0 += 4) {
       float4 v[4][2];
@@ -391,6 +411,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
 #pragma unroll
       for (int u = 0; u < 4; ++u) {
         const int c = lane + 32 * (t0 + u), k = c / DCH, ch = c % DCH;
+        if (k >= m) continue;
         uint4 w;
         w.x = Elem<T>::pack(v[u][0].x, v[u][0].y);
         w.y = Elem<T>::pack(v[u][0].z, v[u][0].w);
@@ -412,15 +433,15 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
     for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 4; ++e) a[mt][nt][e] = g[mt][nt][e] = ac[mt][nt][e] = 0.f;
-  mm_rows<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, lane);
+  mm_rows<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, m, lane);
   softmax_rows<MP>(a, ent, p.scale, m, lane);
 
   if (LAST) {
     // dA = dz y^T
-    mm_rows<T, MP, D, DCH, OCH>(g, sg, 0, so, DCH, lane);
+    mm_rows<T, MP, D, DCH, OCH>(g, sg, 0, so, DCH, m, lane);
   } else {
     // G = q du^T ; dc_k = sum_i a_ik G_ik ; dA = c_k G_ik + dcm_k ; ac = a * c for the dq term
-    mm_rows<T, MP, D, DCH, DCH>(g, sq, 0, sg, 0, lane);
+    mm_rows<T, MP, D, DCH, DCH>(g, sq, 0, sg, 0, m, lane);
     float cs[MP / 8][2], dc[MP / 8][2];
     col_sums<MP>(a, cs);
 #pragma unroll
@@ -472,8 +493,8 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   for (int half = 0; half < D / 64; ++half) {
     float acc[MP / 16][8][4];
     zero<MP>(acc);
-    mm_rn64<T, MP, OCH>(acc, g, so, half * 8, lane);
-    if (!LAST) mm_rn64<T, MP, DCH>(acc, ac, sg, half * 8, lane);
+    mm_rn64<T, MP, OCH>(acc, g, so, half * 8, m, lane);
+    if (!LAST) mm_rn64<T, MP, DCH>(acc, ac, sg, half * 8, m, lane);
 #pragma unroll
     for (int mt = 0; mt < MP / 16; ++mt)
 #pragma unroll
@@ -508,16 +529,16 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   for (int half = 0; half < D / 64; ++half) {
     float acc[MP / 16][8][4];
     zero<MP>(acc);
-    mm_tn64<T, MP, DCH>(acc, sd, sq, half * 8, lane);
-    stage_rows64_dot<T, MP, OCH>(so, half * 8, acc, dot, lane);
+    mm_tn64<T, MP, DCH>(acc, sd, sq, half * 8, m, lane);
+    stage_rows64_dot<T, MP, OCH>(so, half * 8, acc, dot, m, lane);
   }
   if (LAST) {
 #pragma unroll 1
     for (int half = 0; half < D / 64; ++half) {
       float acc[MP / 16][8][4];
       zero<MP>(acc);
-      mm_tn64<T, MP, DCH>(acc, sa, sg, half * 8, lane);
-      stage_rows64_dot<T, MP, OCH>(so, DCH + half * 8, acc, dot, lane);
+      mm_tn64<T, MP, DCH>(acc, sa, sg, half * 8, m, lane);
+      stage_rows64_dot<T, MP, OCH>(so, DCH + half * 8, acc, dot, m, lane);
     }
   }
   if (p.delta_out) {
@@ -539,8 +560,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
 template <typename T, int MP, int D, bool LAST>
 cudaError_t launch(const LstepParams& p, bool bwd, cudaStream_t st) {
   constexpr int OW = LAST ? 2 * D : D;
-  const size_t per_warp = bwd ? (size_t)(2 * MP * D + MP * OW + 2 * MP * Tile<MP>::SA) * sizeof(T)
-                              : (size_t)(MP * D + MP * OW + MP * Tile<MP>::SA) * sizeof(T) + MP * sizeof(float);
+  const size_t per_warp = lstep_warp_bytes<MP>((int)p.m, D, OW, bwd, sizeof(T));
   const int warps = bwd ? kWarpsBwd : kWarpsFwd;
   const size_t smem = per_warp * warps;
   auto kern = bwd ? lstep_bwd_mma_kernel<T, MP, D, LAST> : lstep_fwd_mma_kernel<T, MP, D, LAST>;
