@@ -422,18 +422,25 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 // of tile j (K read by S[j] only) and the V slot of tile j - 2 (read by P V[j-2]); with V aliasing K
 // the K slot of tile j - 2. The producer waits on those per-slot barriers, whose next phase needs
 // a tile it has not loaded yet, so no parity wait can be lapped.
-template <bool VK>
+// NS = 1 (V aliasing K, short sequences): one stream, S [0,128) and O [128,256), so two CTAs share
+// an SM (96 KB of shared memory, 256 TMEM columns each) and one CTA's Q load and epilogue overlap
+// the other's key loop; S(j+1) is issued behind P V(j).
+template <bool VK, int NS = 2>
 struct Fwd2Cfg {
-  static constexpr int NK = VK ? 6 : 3;   // K ring slots (V aliases K: the K slot is also the V operand)
-  static constexpr int NVS = VK ? 0 : 3;  // V ring slots
+  static_assert(NS == 2 || (NS == 1 && VK), "one stream only with V aliasing K");
+  static constexpr int NK = NS == 1 ? 2 : (VK ? 6 : 3);  // K ring slots (V aliasing K: also the V operand)
+  static constexpr int NVS = VK ? 0 : 3;                 // V ring slots
   static constexpr int Q_BYTES = 2 * kAtom;
   static constexpr int SMEM = 1024 + Q_BYTES + (NK + NVS) * 2 * kAtom;
+  static constexpr int THREADS = 64 + 128 * NS;
   static_assert(SMEM <= 232448 - 1024, "shared memory budget");
+  static_assert(NS == 2 || 2 * (SMEM + 1024) <= 233472, "two CTAs per SM");
 };
 
-template <typename T, bool VK, bool ENT>
-__global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
-  using C = Fwd2Cfg<VK>;
+template <typename T, bool VK, bool ENT, int NS = 2>
+__global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
+  using C = Fwd2Cfg<VK, NS>;
+  constexpr uint32_t kTmemCols = NS == 2 ? 512 : 256;
   constexpr int NK = C::NK, NVS = C::NVS;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
@@ -487,7 +494,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
     fence_mbar_init();
   }
   if (warp == 0) {
-    tmem_alloc(smem_u32(&tmem_base_sh), 512);
+    tmem_alloc(smem_u32(&tmem_base_sh), kTmemCols);
     tmem_relinquish();
   }
   tc_fence_before();
@@ -545,32 +552,32 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
       tc_fence_after();
       {
         const uint32_t kb = sK + s * 2 * kAtom;
-        const uint32_t d = tmem + (uint32_t)((j & 1) * 128);
+        const uint32_t d = tmem + (uint32_t)((j % NS) * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
           mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
         }
-        mma_commit_if(leader, BAR_SFULL(j & 1));
+        mma_commit_if(leader, BAR_SFULL(j % NS));
       }
       return true;
     };
     if (ok) ok = issue_s(0);
-    if (ok && n_kt > 1) ok = issue_s(1);
+    if (ok && NS == 2 && n_kt > 1) ok = issue_s(1);
     for (int j = 0; ok && j < n_kt; ++j) {
-      if (!wwait(BAR_PFULL(j & 1), (j >> 1) & 1, 4)) break;
+      if (!wwait(BAR_PFULL(j % NS), (j / NS) & 1, 4)) break;
       if (!VK && !wwait(BAR_VFULL(j % NVS), (j / NVS) & 1, 4)) break;
       tc_fence_after();
       {
         const uint32_t vb = VK ? sK + (j % NK) * 2 * kAtom : sV + (j % NVS) * 2 * kAtom;
-        const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
-        const uint32_t o_tm = tmem + 256 + (uint32_t)((j & 1) * 128);
+        const uint32_t a_tm = tmem + (uint32_t)((j % NS) * 128);
+        const uint32_t o_tm = tmem + NS * 128 + (uint32_t)((j % NS) * 128);
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
           mma_ts_if(leader, o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
-                 (j >= 2 || kk > 0) ? 1u : 0u);
+                 (j >= NS || kk > 0) ? 1u : 0u);
       }
-      if (j + 2 < n_kt) ok = issue_s(j + 2);
+      if (j + NS < n_kt) ok = issue_s(j + NS);
     }
     // DONE: every MMA complete (the epilogue reads O; TMEM may be freed)
     if (elect_one()) {
@@ -591,15 +598,15 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
     };
 
-    for (int j = w; j < n_kt; j += 2) {
-      if (!warp_wait(BAR_SFULL(w), (j >> 1) & 1, 8)) { ok = false; break; }
+    for (int j = w; j < n_kt; j += NS) {
+      if (!warp_wait(BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
       tc_fence_after();
       if (warp == 2 + 4 * w && lane == 0) {  // ring slots done with (see above)
         if (VK) {
-          if (j >= 2) mbar_arrive(BAR_KEMPTY((j - 2) % NK));
+          if (j >= NS) mbar_arrive(BAR_KEMPTY((j - NS) % NK));
         } else {
           mbar_arrive(BAR_KEMPTY(j % NK));
-          if (j >= 2) mbar_arrive(BAR_VEMPTY((j - 2) % NVS));
+          if (j >= NS) mbar_arrive(BAR_VEMPTY((j - NS) % NVS));
         }
       }
       uint32_t sr[128];
@@ -618,7 +625,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
         // earlier P V into O_w has completed (S[j] complete, see above).
         const float m_new = fmaxf(m_ref, mx);
         const float alpha = fast_exp2(m_ref - m_new);
-        const uint32_t tO = tmem + lane_off + 256 + (uint32_t)(w * 128);
+        const uint32_t tO = tmem + lane_off + NS * 128 + (uint32_t)(w * 128);
 #pragma unroll 1
         for (int c = 0; c < 4; ++c) {
           uint32_t o[32];
@@ -667,22 +674,23 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
     xch[(3 * w + 0) * 128 + row] = m_ref;
     xch[(3 * w + 1) * 128 + row] = l;
     xch[(3 * w + 2) * 128 + row] = h;
-    ok = named_bar_and(1, 256, ok);
+    ok = named_bar_and(1, 128 * NS, ok);
     const uint32_t stage = sK;
     if (ok) {
       const float m0 = xch[0 * 128 + row], l0 = xch[1 * 128 + row], h0 = xch[2 * 128 + row];
-      const float m1 = xch[3 * 128 + row], l1 = xch[4 * 128 + row], h1 = xch[5 * 128 + row];
-      const bool two = n_kt > 1;  // stream 1 owns no tile (and O_1 was never written) otherwise
+      const bool two = NS == 2 && n_kt > 1;  // stream 1 owns no tile (and O_1 was never written) otherwise
+      const float m1 = two ? xch[3 * 128 + row] : 0.f, l1 = two ? xch[4 * 128 + row] : 0.f;
+      const float h1 = two ? xch[5 * 128 + row] : 0.f;
       const float m = two ? fmaxf(m0, m1) : m0;
       const float a0 = fast_exp2(m0 - m), a1 = two ? fast_exp2(m1 - m) : 0.f;
       const float lt = a0 * l0 + a1 * l1;
       const float ht = two ? a0 * fmaf(m0 - m, l0, h0) + a1 * fmaf(m1 - m, l1, h1) : h0;
       const float inv = 1.f / lt;
       const float c0 = a0 * inv, c1 = a1 * inv;
-      const uint32_t tO0 = tmem + lane_off + 256, tO1 = tO0 + 128;
+      const uint32_t tO0 = tmem + lane_off + NS * 128, tO1 = tO0 + 128;
       const bool part = p.kv_split > 1;  // key chunk: fp32 O normalised by this chunk's l, plus (m, l, h)
 #pragma unroll 1
-      for (int c = 2 * w; c < 2 * w + 2; ++c) {  // this warpgroup's 64 output columns
+      for (int c = (4 / NS) * w; c < (4 / NS) * (w + 1); ++c) {  // this warpgroup's output columns
         uint32_t o0[32], o1[32];
         tmem_ld32(tO0 + c * 32, o0);
         if (two) tmem_ld32(tO1 + c * 32, o1);
@@ -740,7 +748,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
       }
     }
     fence_proxy_async_smem();
-    named_bar_sync(2, 256);
+    named_bar_sync(2, 128 * NS);
     if (warp == 2 && lane == 0 && ok && !*abort) {
       if (p.kv_split > 1) {
         for (int c = 0; c < 4; ++c) tma_store_3d(&p.tm_po, 32 * c, q0, kchunk * p.n_seq + bi, stage + c * 16384);
@@ -754,7 +762,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd2_sm100_kernel(const __gri
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
-  if (warp == 0) tmem_dealloc(tmem, 512);
+  if (warp == 0) tmem_dealloc(tmem, kTmemCols);
 }
 
 // Merge of the key chunks of a split key range (one warp per query row, lane = 4 columns):
@@ -845,21 +853,26 @@ cudaError_t launch(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-template <typename T, bool VK, bool ENT>
+template <typename T, bool VK, bool ENT, int NS = 2>
 cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
-  using C = Fwd2Cfg<VK>;
-  auto kern = fea_fwd2_sm100_kernel<T, VK, ENT>;
+  using C = Fwd2Cfg<VK, NS>;
+  auto kern = fea_fwd2_sm100_kernel<T, VK, ENT, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.n_qtiles * p.kv_split * batch;
   if (blocks > 0x7fffffff || batch > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  kern<<<(unsigned)blocks, kThreads, C::SMEM, st>>>(p);
+  kern<<<(unsigned)blocks, C::THREADS, C::SMEM, st>>>(p);
   return cudaGetLastError();
 }
+
+// Short key ranges (V aliasing K): the one-stream kernel, two CTAs per SM, hides the Q load and
+// the epilogue of one CTA under the other's key loop; long ranges keep the two-stream kernel.
+bool fwd_one_stream(int n_kv, int kv_split) { return kv_split == 1 && n_kv <= 16 * 128; }
 
 template <typename T, bool ENT>
 cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bool vk, cudaStream_t st) {
   if (vk) {
+    if (dv == 128 && fwd_one_stream(p.n_kv, p.kv_split)) return launch2<T, true, ENT, 1>(p, batch, st);
     if (dv == 128) return launch2<T, true, ENT>(p, batch, st);
     if (dv == 256 && dv1 == 128) return launch<T, 2, true, 3, ENT>(p, batch, st);
   } else {
