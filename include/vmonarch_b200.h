@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VMB_ABI_VERSION 3
+#define VMB_ABI_VERSION 4
 
 #define VMB_DTYPE_BF16 0
 #define VMB_DTYPE_F16 1
@@ -100,6 +100,11 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream);
  *              several R steps and the recompute into one set of accumulators).
  * grad_mode 2: grad_* are fp32 buffers that are OVERWRITTEN (the first contribution to a set of
  *              accumulators, so they need no zero-fill).
+ * grad_mode 3: the last contribution: grad_* are written in the element dtype as the sum of the
+ *              fp32 accumulator fin_* (same shape, batch stride fin_*_bs) and this call's gradient,
+ *              which saves a separate fp32 -> 16-bit pass. fin_q/fin_k (and fin_v / fin_v2 where
+ *              grad_v / grad_v2 are given) are required; their contents are unspecified afterwards
+ *              (shapes without a tcgen05 kernel add into them before converting).
  * v_is_k = 1: the value columns [0, dv1) are the key tensor itself (dv1 == d); their gradient is
  *              added into grad_k and grad_v must be NULL. This is the VMonarch R step
  *              (vmonarch.py:50).
@@ -132,6 +137,10 @@ typedef struct vmb_fea_bwd_args {
   int32_t deterministic; /* nonzero: bitwise reproducible gradients. Zero lets grad_mode 1 / 2 with
                             v_is_k, dv == d == 128 and n_kv <= 4096 form dQ with concurrent fp32
                             reductions (one kernel fewer; summation order varies) (ABI 3) */
+  const float* fin_q;  int64_t fin_q_bs;   /* grad_mode 3 accumulators (ABI 4) */
+  const float* fin_k;  int64_t fin_k_bs;
+  const float* fin_v;  int64_t fin_v_bs;
+  const float* fin_v2; int64_t fin_v2_bs;
 } vmb_fea_bwd_args;
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);

@@ -20,7 +20,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_abi():
     assert N.LIB_PATH.exists()
-    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 3
+    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 4
 
 
 def test_every_declared_symbol_is_exported_and_bound():
@@ -107,9 +107,12 @@ def test_fea_bwd_workspace_and_validation():
     a.v_is_k = 1                      # v_is_k with a separate grad_v is rejected
     assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1
     a.v_is_k = 0
-    a.grad_mode = 3                   # modes are 0 (16-bit), 1 (fp32 add), 2 (fp32 overwrite)
+    a.grad_mode = 4                   # modes are 0 (16-bit), 1 (fp32 add), 2 (fp32 overwrite), 3 (finalize)
     assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1
     assert b"grad_mode" in N.lib.vmb_last_error()
+    a.grad_mode = 3                   # finalize without its fp32 accumulators
+    assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1
+    assert b"accumulator" in N.lib.vmb_last_error()
     a.grad_mode = 1
     a.workspace, a.workspace_bytes = 256, 16   # too small
     assert N.lib.vmb_fea_bwd(ctypes.byref(a), None) == 1

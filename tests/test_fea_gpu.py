@@ -242,3 +242,42 @@ def test_backward_keys_as_values_with_v2(n, mode):
         assert torch.isfinite(g).all()
         assert max_rel_err(g, r) <= 3e-2
         assert (g - r).abs().max() <= max(5e-2, 8e-3 * r.abs().max().item())
+
+
+@pytest.mark.parametrize("case", ["plain", "split", "v2", "d64"])
+def test_grad_mode_finalize_equals_add_then_cast(case):
+    # grad_mode 3 writes 16-bit gradients as fp32 accumulator + this call's gradient; it must equal
+    # adding into the accumulators (grad_mode 1) and converting afterwards, bit for bit.
+    from vmonarch_b200 import ops
+    gen = torch.Generator().manual_seed(hash(case) % 1000)
+    B, nq, nk, D = {"plain": (3, 300, 300, 128), "split": (2, 128, 4096, 128), "v2": (2, 300, 300, 128),
+                    "d64": (2, 200, 200, 64)}[case]
+    q = torch.randn(B, nq, D, generator=gen).bfloat16().cuda()
+    k, v = (torch.randn(B, nk, D, generator=gen).bfloat16().cuda() for _ in range(2))
+    v_is_k, v2 = case == "v2", None
+    if v_is_k:
+        v, v2 = k, v
+    dv_w = 2 * D if v_is_k else D
+    do = torch.randn(B, nq, dv_w, generator=gen).bfloat16().cuda()
+    sm = D ** -0.5
+    o = torch.empty(B, nq, dv_w, dtype=torch.bfloat16, device="cuda")
+    lse, ent = torch.empty(B, nq, device="cuda"), torch.empty(B, nq, device="cuda")
+    ops.fea_fwd(q, k, v, o, lse, ent, sm, v2=v2)
+    shapes = [(B, nq, D), (B, nk, D), (B, nk, D)]
+    acc = [torch.randn(s_, generator=gen).cuda() for s_ in shapes]
+    add = [a.clone() for a in acc]
+    gv = None if v_is_k else add[2]
+    ops.fea_bwd(q, k, v, o, do, lse, add[0], add[1], gv, sm, v2=v2, grad_v2=add[2] if v_is_k else None,
+                grad_mode=1, v_is_k=v_is_k, deterministic=True)
+    ref = [a.bfloat16() for a in add]
+    out = [torch.empty(s_, dtype=torch.bfloat16, device="cuda") for s_ in shapes]
+    fin = [a.clone() for a in acc]
+    ops.fea_bwd(q, k, v, o, do, lse, out[0], out[1], None if v_is_k else out[2], sm, v2=v2,
+                grad_v2=out[2] if v_is_k else None, grad_mode=3, v_is_k=v_is_k, deterministic=True, fin_q=fin[0],
+                fin_k=fin[1], fin_v=None if v_is_k else fin[2], fin_v2=fin[2] if v_is_k else None)
+    torch.cuda.synchronize()
+    for name, g, r in zip(("dq", "dk", "dv"), out, ref):
+        if D == 128:
+            assert torch.equal(g, r), name
+        else:  # the mma.sync kernels add with atomics: the summation order varies run to run
+            torch.testing.assert_close(g.float(), r.float(), rtol=1e-2, atol=1e-2)

@@ -25,7 +25,7 @@ c_vp = ctypes.c_void_p
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 
-ABI_VERSION = 3  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+ABI_VERSION = 4  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
 
 
 class FeaFwdArgs(ctypes.Structure):
@@ -63,6 +63,10 @@ class FeaBwdArgs(ctypes.Structure):
         ("sm_scale", ctypes.c_float),
         ("delta", c_vp),
         ("deterministic", c_i32),
+        ("fin_q", c_vp), ("fin_q_bs", c_i64),
+        ("fin_k", c_vp), ("fin_k_bs", c_i64),
+        ("fin_v", c_vp), ("fin_v_bs", c_i64),
+        ("fin_v2", c_vp), ("fin_v2_bs", c_i64),
     ]
 
 

@@ -167,7 +167,16 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   if (!a) return fail(VMB_EINVAL, "vmb_fea_bwd: null args");
   int rc = check_common("vmb_fea_bwd", a->batch, a->n_q, a->n_kv, a->d, a->dv, a->dv1, a->dtype, a->v2);
   if (rc) return rc;
-  if (a->grad_mode < 0 || a->grad_mode > 2) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_mode must be 0, 1 or 2");
+  if (a->grad_mode < 0 || a->grad_mode > 3) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_mode must be 0, 1, 2 or 3");
+  if (a->grad_mode == 3) {
+    if (!a->fin_q || !a->fin_k || (a->grad_v && !a->fin_v) || (a->grad_v2 && !a->fin_v2))
+      return fail(VMB_EINVAL, "vmb_fea_bwd: grad_mode 3 needs an fp32 accumulator for every gradient");
+    const void* fins[] = {a->fin_q, a->fin_k, a->fin_v, a->fin_v2};
+    for (const void* ptr : fins)
+      if (ptr && !aligned16(ptr)) return fail(VMB_EINVAL, "vmb_fea_bwd: accumulators must be 16-byte aligned");
+    if ((a->fin_q_bs | a->fin_k_bs | a->fin_v_bs | a->fin_v2_bs) & 3)
+      return fail(VMB_EINVAL, "vmb_fea_bwd: accumulator batch strides must be multiples of 4 elements");
+  }
   if (a->v_is_k && (a->dv1 != a->d || a->grad_v != nullptr))
     return fail(VMB_EINVAL, "vmb_fea_bwd: v_is_k needs dv1 == d and grad_v == NULL");
   if (!a->v_is_k && !a->grad_v) return fail(VMB_EINVAL, "vmb_fea_bwd: grad_v is NULL");
@@ -226,7 +235,30 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.sm_scale = a->sm_scale;
   p.scale_log2 = a->sm_scale * kLog2eHost;
   p.deterministic = a->deterministic != 0;
+  p.fin_q = a->fin_q; p.fin_k = a->fin_k; p.fin_v = a->fin_v; p.fin_v2 = a->fin_v2;
+  p.fin_q_bs = a->fin_q_bs; p.fin_k_bs = a->fin_k_bs; p.fin_v_bs = a->fin_v_bs; p.fin_v2_bs = a->fin_v2_bs;
   if (sm100) return cuda_status(vmb::fea_bwd_sm100(p, a->batch, a->dv, a->v_is_k != 0, bf16, st), "vmb_fea_bwd");
+  if (a->grad_mode == 3) {
+    // the mma.sync kernels add into the fp32 accumulators, which are then converted to grad_*
+    p.dq = const_cast<float*>(a->fin_q);
+    p.dq_bs = a->fin_q_bs;
+    p.dk = const_cast<float*>(a->fin_k);
+    p.dv = const_cast<float*>(a->fin_v);
+    p.dv2 = const_cast<float*>(a->fin_v2);
+    p.dk_bs = a->fin_k_bs; p.dv_bs = a->fin_v_bs; p.dv2_bs = a->fin_v2_bs;
+    p.acc_kv = p.acc_q = 1;
+    e = vmb::fea_bwd_mma(p, a->batch, a->d, a->dv, a->v_is_k != 0, bf16, st);
+    auto conv = [&](const float* src, int64_t sbs, void* dst, int64_t dbs, int64_t n) -> cudaError_t {
+      if (!dst) return cudaSuccess;
+      count(1);
+      return vmb::cast_f32(src, sbs, dst, dbs, a->batch, n, bf16, st);
+    };
+    if (e == cudaSuccess) e = conv(a->fin_q, a->fin_q_bs, a->grad_q, a->grad_q_bs, a->n_q * a->d);
+    if (e == cudaSuccess) e = conv(a->fin_k, a->fin_k_bs, a->grad_k, a->grad_k_bs, a->n_kv * a->d);
+    if (e == cudaSuccess) e = conv(a->fin_v, a->fin_v_bs, a->grad_v, a->grad_v_bs, a->n_kv * a->dv1);
+    if (e == cudaSuccess) e = conv(a->fin_v2, a->fin_v2_bs, a->grad_v2, a->grad_v2_bs, a->n_kv * (a->dv - a->dv1));
+    return cuda_status(e, "vmb_fea_bwd");
+  }
   if (a->grad_mode == 2) {
     // the mma.sync kernels only add: clear the fp32 gradients, then accumulate
     auto clear = [&](void* ptr, int64_t bs, int64_t rows, int cols) -> cudaError_t {

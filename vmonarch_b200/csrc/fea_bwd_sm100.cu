@@ -65,11 +65,46 @@ struct Sm100BwdParams {
   int n_q, n_kv, n_tiles;
   int k_split, kt_per;  // dQ kernel: key range split over k_split CTAs of kt_per 128-key tiles each
   int n_seq;            // sequences (batch) of the call
-  int acc;       // 1: fp32 gradients added into (TMA reduce-add); 2: fp32 stores; 0: 16-bit stores
+  int acc;       // 1: fp32 gradients added into (TMA reduce-add); 2: fp32 stores; 0: 16-bit stores;
+                 // 3: 16-bit stores of (fp32 accumulator tile + this call's gradient)
   float scale_log2, sm_scale;
   float* dq;     // fused dQ: fp32 [batch][n_q][128] (batch stride dq_bs), added into
   int64_t dq_bs;
+  CUtensorMap tm_f0, tm_f1;  // acc 3: the fp32 accumulators of tm_g0 / tm_g1 (boxes of 32 x 128)
 };
+
+// acc 3: out16 = 16-bit(TMEM accumulator + fp32 accumulator tile staged at `fin`), for the 32-column
+// chunks [c_begin, c_end) of row `row`; fp32 staging as in stage_acc_rows, 16-bit output as two
+// [128 rows][64 elements] boxes at out + a * 16 KB.
+template <typename T>
+__device__ __forceinline__ void finalize_rows(uint32_t taddr, uint32_t fin, uint32_t out, int row, int c_begin,
+                                              int c_end) {
+#pragma unroll 1
+  for (int c = c_begin; c < c_end; ++c) {
+    uint32_t v[32];
+    tmem_ld32(taddr + c * 32, v);
+    tmem_wait_ld();
+    const uint32_t src = fin + c * 16384 + row * 128;
+    uint32_t w[16];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) {
+      float4 a;
+      asm volatile("ld.shared.v4.f32 {%0,%1,%2,%3}, [%4];"
+                   : "=f"(a.x), "=f"(a.y), "=f"(a.z), "=f"(a.w)
+                   : "r"(src + ((k ^ (row & 7)) << 4)));
+      w[2 * k] = Elem<T>::pack(__uint_as_float(v[4 * k]) + a.x, __uint_as_float(v[4 * k + 1]) + a.y);
+      w[2 * k + 1] = Elem<T>::pack(__uint_as_float(v[4 * k + 2]) + a.z, __uint_as_float(v[4 * k + 3]) + a.w);
+    }
+    const uint32_t base = out + (c >> 1) * 16384 + row * 128;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) {
+      const int chunk = (c & 1) * 4 + k;
+      asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((chunk ^ (row & 7)) << 4)), "r"(w[4 * k]),
+                   "r"(w[4 * k + 1]), "r"(w[4 * k + 2]), "r"(w[4 * k + 3])
+                   : "memory");
+    }
+  }
+}
 
 // Gradient epilogue. The 128 x 128 fp32 accumulator tile in TMEM (thread = row = TMEM lane) is
 // staged in shared memory with the 128-byte swizzle and written by TMA: reduce-add into fp32
@@ -172,7 +207,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   auto pcol = [](int kk) -> uint32_t { return NWG == 4 ? 32 * (kk >> 1) + 8 * (kk & 1) : 8 * kk; };
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5 + (FQ ? 2 : 0)];
+  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5 + 2 + 1];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -199,6 +234,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   const uint32_t BAR_DONE = bar0 + 8u * (5 + 2 * NQS);
   // fused dQ: stream b has drained dQ^T of its previous tile and staged dS^T of the current one
   auto BAR_DQFREE = [&](int b) { return bar0 + 8u * (6 + 2 * NQS + b); };
+  const uint32_t BAR_FIN = bar0 + 8u * (8 + 2 * NQS);  // acc 3: the fp32 accumulator tiles landed
   volatile int* abort = &abort_sh;
   auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
   auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom64; };
@@ -217,6 +253,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       if (FQ) mbar_init(BAR_DQFREE(b), 64 * NWG);
     }
     mbar_init(BAR_DONE, 1);
+    mbar_init(BAR_FIN, 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -264,6 +301,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
           tma_prefetch_3d(&p.tm_c, 0, qa, bi);
           tma_prefetch_3d(&p.tm_c, 64, qa, bi);
           for (int a = 0; a < C::DW / 64; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, qa, bi);
+        }
+        if (p.acc == 3 && i == nq - 1) {  // the accumulator tiles the epilogue reads, into L2
+          for (int c = 0; c < 4; ++c) {
+            tma_prefetch_3d(&p.tm_f0, 32 * c, k0, bi);
+            if (C::HAS_DV) tma_prefetch_3d(&p.tm_f1, 32 * c, k0, bi);
+          }
         }
       }
       armed[s] = i / NQS + 1;
@@ -441,9 +484,27 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
     }
     // epilogue: stage dK (and dV) in the idle query slots, one thread writes them with TMA. The
     // warpgroups split the 32-column chunks: with dV, the first half of them stages dK, the second
-    // dV; without, all stage dK.
+    // dV; without, all stage dK. acc 3: the fp32 accumulator tiles are loaded into those slots
+    // and the 16-bit sums staged in the idle resident K | X tiles.
     const uint32_t stage0 = sSlots, stage1 = sSlots + 65536;
-    if (ok) {
+    const bool fin = p.acc == 3;
+    bool fin_issued = false;
+    if (fin) {
+      if (warp == 2 && lane == 0 && ok) {
+        fin_issued = true;
+        mbar_expect_tx(BAR_FIN, (C::HAS_DV ? 2 : 1) * 65536);
+        for (int c = 0; c < 4; ++c) {
+          tma_load_3d(stage0 + c * 16384, &p.tm_f0, 32 * c, k0, bi, BAR_FIN);
+          if (C::HAS_DV) tma_load_3d(stage1 + c * 16384, &p.tm_f1, 32 * c, k0, bi, BAR_FIN);
+        }
+      }
+      if (ok) ok = warp_wait(BAR_FIN, 0, 8);
+    }
+    if (ok && fin) {
+      constexpr int CPW = C::HAS_DV ? 8 / NWG : 4 / NWG;
+      const int mat = C::HAS_DV ? wg / (NWG / 2) : 0, c0 = C::HAS_DV ? CPW * (wg % (NWG / 2)) : CPW * wg;
+      finalize_rows<T>(tmem + lane_off + 256 + 128 * mat, mat ? stage1 : stage0, sRes + mat * 32768, row, c0, c0 + CPW);
+    } else if (ok) {
       if (C::HAS_DV) {
         constexpr int CPW = 8 / NWG;  // chunks per warpgroup
         const int mat = wg / (NWG / 2), c0 = CPW * (wg % (NWG / 2));
@@ -457,10 +518,11 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
     fence_proxy_async_smem();
     ok = named_bar_and(1, 128 * NWG, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      issue_grad_tile(&p.tm_g0, stage0, k0, bi, p.acc);
-      if (C::HAS_DV) issue_grad_tile(&p.tm_g1, stage1, k0, bi, p.acc);
+      issue_grad_tile(&p.tm_g0, fin ? sRes : stage0, k0, bi, fin ? 0 : p.acc);
+      if (C::HAS_DV) issue_grad_tile(&p.tm_g1, fin ? sRes + 32768 : stage1, k0, bi, fin ? 0 : p.acc);
       tma_store_commit_and_wait();
     }
+    if (fin_issued) mbar_wait_drain(BAR_FIN, 0);  // loads still in flight after a timeout
   }
 
   tc_fence_before();
@@ -511,7 +573,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   constexpr int NCT = 128 * NWG;         // compute threads
   constexpr int B_Q = 0, B_KFULL = 1, B_KEMPTY = B_KFULL + NK, B_XFULL = B_KEMPTY + NK, B_XEMPTY = B_XFULL + NXB;
   constexpr int B_SFULL = B_XEMPTY + NXB, B_DSFULL = B_SFULL + NS, B_DPFULL = B_DSFULL + NS;
-  constexpr int B_DPFREE = B_DPFULL + 1, B_DOT = B_DPFREE + 1, B_DONE = B_DOT + 1, NBARS = B_DONE + 1;
+  constexpr int B_DPFREE = B_DPFULL + 1, B_DOT = B_DPFREE + 1, B_DONE = B_DOT + 1, B_FIN = B_DONE + 1;
+  constexpr int NBARS = B_FIN + 1;
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[NBARS];
@@ -554,6 +617,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
     mbar_init(BAR(B_DPFREE), NCT);
     mbar_init(BAR(B_DOT), NCT);
     mbar_init(BAR(B_DONE), 1);
+    mbar_init(BAR(B_FIN), 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -590,6 +654,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
           tma_prefetch_3d(&p.tm_c, 0, (kt0 + j + NK) * 128, bi);
           tma_prefetch_3d(&p.tm_c, 64, (kt0 + j + NK) * 128, bi);
         }
+        if (p.acc == 3 && j == nk - 1)  // the accumulator tile the epilogue reads, into L2
+          for (int c = 0; c < 4; ++c) tma_prefetch_3d(&p.tm_f0, 32 * c, q0, bi);
         karmed[s] = j / NK + 1;
         if (XA > 0) {
           const int x = j % NXB;
@@ -781,15 +847,31 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
     }
     if (ok) ok = warp_wait(BAR(B_DONE), 0, 128);
     tc_fence_after();
-    // epilogue: stage dQ in the idle K ring (WG w: columns [CW w, CW w + CW)), one thread writes it
-    if (ok) stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc != 0, (CW / 32) * wg, (CW / 32) * (wg + 1));
+    // epilogue: stage dQ in the idle K ring (WG w: columns [CW w, CW w + CW)), one thread writes it.
+    // acc 3: the fp32 accumulator tile is loaded into the K ring and the 16-bit sum staged in the
+    // idle Q tile.
+    const bool fin = p.acc == 3;
+    bool fin_issued = false;
+    if (fin) {
+      if (warp == 2 && lane == 0 && ok) {
+        fin_issued = true;
+        mbar_expect_tx(BAR(B_FIN), 65536);
+        for (int c = 0; c < 4; ++c) tma_load_3d(sK + c * 16384, &p.tm_f0, 32 * c, q0, bi, BAR(B_FIN));
+      }
+      if (ok) ok = warp_wait(BAR(B_FIN), 0, 128);
+      if (ok) finalize_rows<T>(tmem + lane_off + T_DQ, sK, sQ, row, (CW / 32) * wg, (CW / 32) * (wg + 1));
+    } else if (ok) {
+      stage_acc_rows<T>(tmem + lane_off + T_DQ, sK, row, p.acc != 0, (CW / 32) * wg, (CW / 32) * (wg + 1));
+    }
     fence_proxy_async_smem();
     ok = named_bar_and(1, NCT, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
       // a split key range writes its partial tile into its own slice: sequence index chunk * batch + bi
-      issue_grad_tile(&p.tm_g0, sK, q0, p.k_split > 1 ? (kt0 / p.kt_per) * p.n_seq + bi : bi, p.acc);
+      issue_grad_tile(&p.tm_g0, fin ? sQ : sK, q0, p.k_split > 1 ? (kt0 / p.kt_per) * p.n_seq + bi : bi,
+                      fin ? 0 : p.acc);
       tma_store_commit_and_wait();
     }
+    if (fin_issued) mbar_wait_drain(BAR(B_FIN), 0);  // loads still in flight after a timeout
   }
 
   tc_fence_before();
@@ -816,6 +898,29 @@ __global__ void dq_split_reduce_kernel(const float* part, int split, int64_t bat
       acc.w += v.w;
     }
     *dst = acc;
+  }
+}
+
+// out16[bi][q] = 16-bit(fin[bi][q] + sum over chunks c (in order) of part[c][bi][q]) (acc 3)
+template <typename T>
+__global__ void dq_split_finalize_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q,
+                                         const float* fin, int64_t fin_bs, T* out, int64_t out_bs) {
+  const int64_t total = batch * n_q * 32;
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
+    const int64_t q = rem / 32, c4 = rem % 32;
+    float4 acc = reinterpret_cast<const float4*>(fin + bi * fin_bs + q * 128)[c4];
+    for (int c = 0; c < split; ++c) {
+      const float4 v = reinterpret_cast<const float4*>(part + (((int64_t)c * batch + bi) * n_pad + q) * 128)[c4];
+      acc.x += v.x;
+      acc.y += v.y;
+      acc.z += v.z;
+      acc.w += v.w;
+    }
+    uint2 w;
+    w.x = Elem<T>::pack(acc.x, acc.y);
+    w.y = Elem<T>::pack(acc.z, acc.w);
+    reinterpret_cast<uint2*>(out + bi * out_bs + q * 128)[c4] = w;
   }
 }
 
@@ -855,9 +960,16 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     return f32 ? tma::make_map_f32(m, base, 128, rows, batch, bs, 128)
                : tma::make_map(m, base, bf16, 128, rows, batch, bs, 128);
   };
-  if (!grad_map(&pa.tm_g0, b.dk, b.n_kv, b.dk_bs, b.acc_kv)) return cudaErrorInvalidValue;
-  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, b.n_kv, vk ? b.dv2_bs : b.dv_bs, b.acc_kv))
+  const bool f32_kv = b.acc_kv == 1 || b.acc_kv == 2;  // acc 3 writes 16-bit values
+  if (!grad_map(&pa.tm_g0, b.dk, b.n_kv, b.dk_bs, f32_kv)) return cudaErrorInvalidValue;
+  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, b.n_kv, vk ? b.dv2_bs : b.dv_bs, f32_kv))
     return cudaErrorInvalidValue;
+  if (b.acc_kv == 3) {
+    if (!tma::make_map_f32(&pa.tm_f0, b.fin_k, 128, b.n_kv, batch, b.fin_k_bs, 128)) return cudaErrorInvalidValue;
+    if (xa > 0 && !tma::make_map_f32(&pa.tm_f1, vk ? b.fin_v2 : b.fin_v, 128, b.n_kv, batch,
+                                     vk ? b.fin_v2_bs : b.fin_v_bs, 128))
+      return cudaErrorInvalidValue;
+  }
   pa.n_q = b.n_q;
   pa.n_kv = b.n_kv;
   pa.n_tiles = (b.n_kv + 127) / 128;
@@ -913,8 +1025,10 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     if (!b.dq_part || !tma::make_map_f32(&pb.tm_g0, b.dq_part, 128, b.n_pad, (int64_t)pb.k_split * batch,
                                          b.n_pad * 128, 128))
       return cudaErrorInvalidValue;
-  } else if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q)) {
-    return cudaErrorInvalidValue;
+  } else {
+    if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
+    if (b.acc_q == 3 && !tma::make_map_f32(&pb.tm_f0, b.fin_q, 128, b.n_q, batch, b.fin_q_bs, 128))
+      return cudaErrorInvalidValue;
   }
   pb.n_q = b.n_q;
   pb.n_kv = b.n_kv;
@@ -935,8 +1049,12 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   if (e != cudaSuccess || pb.k_split == 1) return e;
   const int64_t total = batch * b.n_q * 32;  // float4s of the valid dQ rows
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
-  dq_split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.dq,
-                                                           b.dq_bs, b.acc_q == 2);
+  if (b.acc_q == 3)
+    dq_split_finalize_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.fin_q,
+                                                                  b.fin_q_bs, reinterpret_cast<T*>(b.dq), b.dq_bs);
+  else
+    dq_split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.dq,
+                                                             b.dq_bs, b.acc_q == 2);
   return cudaGetLastError();
 }
 
@@ -970,7 +1088,7 @@ int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc) {
 bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) {
   // dQ from the dK kernel (no dq kernel) when V aliases K without V2 (free TMEM columns), dQ is
   // fp32 (reductions) and each dQ element receives at most 32 of them (<= 32 key tiles)
-  return vk && dv == 128 && acc_q != 0 && !deterministic && (n_kv + 127) / 128 <= 32;
+  return vk && dv == 128 && (acc_q == 1 || acc_q == 2) && !deterministic && (n_kv + 127) / 128 <= 32;
 }
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {

@@ -43,6 +43,12 @@ struct BwdParams {
   float scale_log2;   // sm_scale * log2(e)
   float sm_scale;
   bool deterministic;  // bitwise reproducible results (no concurrent fp32 reductions into dq)
+  // grad_mode 3: fp32 accumulators whose values are added before the 16-bit gradients are written
+  const float* fin_q;
+  const float* fin_k;
+  const float* fin_v;
+  const float* fin_v2;
+  int64_t fin_q_bs, fin_k_bs, fin_v_bs, fin_v2_bs;
 };
 
 }  // namespace vmb

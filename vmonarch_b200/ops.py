@@ -76,9 +76,11 @@ def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
 
 
 def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, ent=None, dent=None, v2=None,
-            grad_v2=None, grad_mode: int = 0, v_is_k: bool = False, delta=None, deterministic=None) -> None:
+            grad_v2=None, grad_mode: int = 0, v_is_k: bool = False, delta=None, deterministic=None, fin_q=None,
+            fin_k=None, fin_v=None, fin_v2=None) -> None:
     """Backward of :func:`fea_fwd`; see ``vmb_fea_bwd`` in the header for the modes. ``deterministic``
-    (default: ``torch.are_deterministic_algorithms_enabled()``) rules out concurrent fp32 reductions."""
+    (default: ``torch.are_deterministic_algorithms_enabled()``) rules out concurrent fp32 reductions;
+    ``fin_*`` are the fp32 accumulators of grad_mode 3 (16-bit grad_* = fin_* + this gradient)."""
     if deterministic is None:
         deterministic = torch.are_deterministic_algorithms_enabled()
     q3, k3, v3, o3, do3 = _flat3(q), _flat3(k), _flat3(v), _flat3(o), _flat3(dout)
@@ -109,6 +111,11 @@ def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, e
     a.v_is_k = int(v_is_k)
     a.sm_scale = float(sm_scale)
     a.deterministic = int(bool(deterministic))
+    for name, t in (("fin_q", fin_q), ("fin_k", fin_k), ("fin_v", fin_v), ("fin_v2", fin_v2)):
+        if t is not None:
+            t3 = _flat3(t)
+            setattr(a, name, t3.data_ptr())
+            setattr(a, name + "_bs", _bs(t3))
     nbytes = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a))
     ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
@@ -148,7 +155,12 @@ def lstep_bwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, dq
 
 
 def cast_f32(src: torch.Tensor, dst: torch.Tensor) -> None:
-    """dst = src (fp32 -> dst.dtype); both contiguous with the same number of elements."""
-    n = src.numel()
-    N.check(N.lib.vmb_cast_f32(src.data_ptr(), n, dst.data_ptr(), n, 1, n, N.dtype_code(dst.dtype),
+    """dst = src (fp32 -> dst.dtype). Both [batch][rows][cols] views with contiguous rows and the same
+    shape (e.g. the same row range of two per-head tensors)."""
+    s3, d3 = _flat3(src), _flat3(dst)
+    assert s3.shape == d3.shape
+    n = s3.size(1) * s3.size(2)
+    if n == 0 or s3.size(0) == 0:
+        return
+    N.check(N.lib.vmb_cast_f32(s3.data_ptr(), _bs(s3), d3.data_ptr(), _bs(d3), s3.size(0), n, N.dtype_code(dst.dtype),
                                N.stream_ptr(src.device)), "vmb_cast_f32")

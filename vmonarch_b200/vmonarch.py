@@ -141,17 +141,20 @@ class _VMonarchAttention(torch.autograd.Function):
             kv_fresh = False
             du = gq
 
+        dq = torch.empty((BH, N, D), device=dev, dtype=dt)
+        dk = torch.empty((BH, N, D), device=dev, dtype=dt)
+        dv = torch.empty((BH, N, Dv), device=dev, dtype=dt)
         if rr > 0:
-            ops.fea_bwd(qf[:, :rr], kf, vf, z[:, :rr], dz[:, :rr], lse_r, dq_acc[:, :rr], dk_acc, dv_acc, scale,
-                        grad_mode=1)
-
-        dq = torch.empty((B, H, N, D), device=dev, dtype=dt)
-        dk = torch.empty((B, H, N, D), device=dev, dtype=dt)
-        dv = torch.empty((B, H, N, Dv), device=dev, dtype=dt)
-        ops.cast_f32(dq_acc, dq)
-        ops.cast_f32(dk_acc, dk)
-        ops.cast_f32(dv_acc, dv)
-        return dq, dk, dv, None, None, None, None, None
+            # the recompute is the last contribution to dk, dv (every key) and dq[:rr]: it writes them
+            # in the element dtype as accumulator + its own gradient (grad_mode 3)
+            ops.fea_bwd(qf[:, :rr], kf, vf, z[:, :rr], dz[:, :rr], lse_r, dq[:, :rr], dk, dv, scale, grad_mode=3,
+                        fin_q=dq_acc[:, :rr], fin_k=dk_acc, fin_v=dv_acc)
+            ops.cast_f32(dq_acc[:, rr:], dq[:, rr:])
+        else:
+            ops.cast_f32(dq_acc, dq)
+            ops.cast_f32(dk_acc, dk)
+            ops.cast_f32(dv_acc, dv)
+        return dq.view(B, H, N, D), dk.view(B, H, N, D), dv.view(B, H, N, Dv), None, None, None, None, None
 
 
 def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_tokens=0, min_col_mass=0.01):
