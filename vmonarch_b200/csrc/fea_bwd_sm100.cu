@@ -567,6 +567,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   constexpr int NXB = NX > 0 ? NX : 1;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_S32 = idesc_f16(kBf16, 128, 32, false, false);  // a last key tile of <= 32 keys
   constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 128, false, true);
   constexpr uint32_t T_DP = DOT ? 128 : 256, T_DO = 256, T_DQ = 384;
   constexpr int CW = 128 / NWG;          // key columns of a tile per compute warpgroup
@@ -685,6 +686,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
     {
       bool ok = wwait(BAR(B_Q), 0, 32);
       if (DOT && ok) ok = wwait(BAR(B_DOT), 0, 32);
+      // a last key tile of <= 32 keys: S and dP at N = 32, dQ over its first 32 keys only (the
+      // scores of the other columns are stale TMEM and never reach an MMA)
+      auto tail32 = [&](int j) { return p.n_kv - (kt0 + j) * 128 <= 32; };
       auto issue_s = [&](int j) -> bool {
         const int s = j % NK;
         if (!wwait(BAR(B_KFULL + s), (j / NK) & 1, 32)) return false;
@@ -692,10 +696,11 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         {
           const uint32_t kb = sK + s * C::KSLOT;
           const uint32_t d = tmem + 128u * (uint32_t)(j % NS);
+          const uint32_t idesc = tail32(j) ? IDESC_S32 : IDESC_S;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {
             const uint32_t off = (kk >> 2) * kAtom128 + (kk & 3) * 32;
-            mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
+            mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
           }
           mma_commit_if(leader, BAR(B_SFULL + j % NS));
         }
@@ -708,6 +713,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         tc_fence_after();
         {
           const uint32_t kb = sK + s * C::KSLOT, xb = sX + x * C::XSLOT;
+          const uint32_t idesc = tail32(j) ? IDESC_S32 : IDESC_S;
 #pragma unroll
           for (int kk = 0; kk < C::DW / 16; ++kk) {
             uint32_t boff;
@@ -716,9 +722,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
             else boff = xb + (kk >> 2) * kAtom128 + (kk & 3) * 32;
             const uint64_t bd = smem_desc_sw128(boff, 16, 1024);
             if (DOT)
-              mma_ts_if(leader, tmem + T_DP, tmem + T_DO + kk * 8, bd, IDESC_S, kk > 0);
+              mma_ts_if(leader, tmem + T_DP, tmem + T_DO + kk * 8, bd, idesc, kk > 0);
             else
-              mma_ss_if(leader, tmem + T_DP, smem_desc_sw128(sDO + (kk >> 2) * kAtom128 + (kk & 3) * 32, 16, 1024), bd, IDESC_S,
+              mma_ss_if(leader, tmem + T_DP, smem_desc_sw128(sDO + (kk >> 2) * kAtom128 + (kk & 3) * 32, 16, 1024), bd, idesc,
                      kk > 0);
           }
           mma_commit_if(leader, BAR(B_DPFULL));
@@ -742,15 +748,17 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         {
           const uint32_t kb = sK + (j % NK) * C::KSLOT;
           const uint32_t sb = tmem + 128u * (uint32_t)(j % NS);
+          const uint32_t kmask = tail32(j) ? 0x3u : 0xffu;  // key steps (16 keys each) of the tile
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // dQ += dS K ; keys [16kk, 16kk+16) of warpgroup 16kk/CW
             const uint64_t bd = smem_desc_sw128(kb + kk * 2048, kAtom128, 1024);
+            const uint32_t on = leader & ((kmask >> kk) & 1u);
             if (DOT) {
               const uint32_t a_sm = sDS(j) + (kk >> 2) * kAtom128 + (kk & 3) * 32;
-              mma_ss_if(leader, tmem + T_DQ, smem_desc_sw128(a_sm, 16, 1024), bd, IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
+              mma_ss_if(on, tmem + T_DQ, smem_desc_sw128(a_sm, 16, 1024), bd, IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
             } else {
               const uint32_t a_tm = sb + CW * (16 * kk / CW) + (16 * kk % CW) / 2;
-              mma_ts_if(leader, tmem + T_DQ, a_tm, bd, IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
+              mma_ts_if(on, tmem + T_DQ, a_tm, bd, IDESC_DQ, (j > 0 || kk > 0) ? 1u : 0u);
             }
           }
           mma_commit_if(leader, BAR(B_KEMPTY + j % NK));

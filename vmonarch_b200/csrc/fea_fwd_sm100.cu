@@ -118,6 +118,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
   using C = FwdCfg<XA, VK, NSLOT>;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_S32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 keys
   constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, C::NV, false, true);
 
   extern __shared__ uint8_t smem_raw[];
@@ -222,10 +223,12 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       {
         const uint32_t kb = sRing + s * C::SLOT;
         const uint32_t d = tmem + (uint32_t)((j & 1) * 128);
+        // a last tile of <= 32 keys: N = 32 (the softmax masks the columns past n_kv by index)
+        const uint32_t idesc = p.n_kv - j * 128 <= 32 ? IDESC_S32 : IDESC_S;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
+          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
         }
         mma_commit_if(leader, BAR_SFULL(j & 1));
       }
@@ -241,10 +244,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       {
         const uint32_t vb = sRing + s * C::SLOT + C::PV_OFF;
         const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
+        const int ksteps = p.n_kv - j * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ts_if(leader, tmem + 256, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
-                 (j > 0 || kk > 0) ? 1u : 0u);
+          mma_ts_if(leader & (kk < ksteps ? 1u : 0u), tmem + 256, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
+                    IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit_if(leader, BAR_EMPTY(s));
       }
       if (j + 2 < n_kt) ok = issue_s(j + 2);
@@ -444,6 +448,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   constexpr int NK = C::NK, NVS = C::NVS;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_S32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 keys
   constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, 128, false, true);
 
   extern __shared__ uint8_t smem_raw[];
@@ -553,10 +558,12 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       {
         const uint32_t kb = sK + s * 2 * kAtom;
         const uint32_t d = tmem + (uint32_t)((j % NS) * 128);
+        // a last tile of <= 32 keys: N = 32 (the softmax masks the columns past n_kv by index)
+        const uint32_t idesc = p.n_kv - (kt0 + j) * 128 <= 32 ? IDESC_S32 : IDESC_S;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S, kk > 0);
+          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
         }
         mma_commit_if(leader, BAR_SFULL(j % NS));
       }
@@ -572,10 +579,11 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         const uint32_t vb = VK ? sK + (j % NK) * 2 * kAtom : sV + (j % NVS) * 2 * kAtom;
         const uint32_t a_tm = tmem + (uint32_t)((j % NS) * 128);
         const uint32_t o_tm = tmem + NS * 128 + (uint32_t)((j % NS) * 128);
+        const int ksteps = p.n_kv - (kt0 + j) * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk)
-          mma_ts_if(leader, o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV,
-                 (j >= NS || kk > 0) ? 1u : 0u);
+          mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
+                    IDESC_PV, (j >= NS || kk > 0) ? 1u : 0u);
       }
       if (j + NS < n_kt) ok = issue_s(j + NS);
     }
