@@ -199,6 +199,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);   // S^T, dP^T
   constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);  // dK, dV (B MN-major)
   constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 64, true, true);     // dQ^T = K^T dS^T (both MN-major)
+  constexpr uint32_t IDESC_SP32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 queries
+  constexpr uint32_t IDESC_DQ32 = idesc_f16(kBf16, 128, 32, true, true);
   static_assert(NWG == 2 || NWG == 4, "two or four compute warpgroups");
   static_assert(!FQ || NWG == 4, "fused dQ: two warpgroups per stream, 32 queries each");
   // Column of the packed P^T / dS^T of queries [16kk, 16kk + 16) inside a tile's S^T / dP^T:
@@ -219,6 +221,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   // query tiles, so the concurrent reductions into one dQ row come from different steps.
   const int rot = FQ ? (2 * (blockIdx.x % p.n_tiles)) % nq : 0;
   auto qtile = [&](int i) { return FQ ? (i + rot < nq ? i + rot : i + rot - nq) : i; };
+  // a last query tile of <= 32 queries: S^T, dP^T (and dQ^T) at N = 32, the query contractions over
+  // its first 32 queries (the other columns are stale TMEM that no MMA reads)
+  auto qtail = [&](int i) { return p.n_q - qtile(i) * 64 <= 32; };
 
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sRes = sbase;                       // K atoms, then X atoms
@@ -333,17 +338,18 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         tc_fence_after();
         {
           const uint32_t tb = tmem + 128 * (i & 1);
+          const uint32_t idesc = qtail(i) ? IDESC_SP32 : IDESC_SP;
 #pragma unroll
           for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
             const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-            mma_ss_if(leader, tb, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024), IDESC_SP,
+            mma_ss_if(leader, tb, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024), idesc,
                    kk > 0);
           }
 #pragma unroll
           for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
             const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
             mma_ss_if(leader, tb + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
-                   IDESC_SP, kk > 0);
+                   idesc, kk > 0);
           }
           mma_commit_if(leader, BAR_SPFULL(i & 1));
         }
@@ -357,21 +363,24 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         const int s = i % NQS;
         {
           const uint32_t pt = tmem + 128 * (i & 1), dst = pt + 64;
+          const bool tail = qtail(i);
+          const uint32_t qmask = tail ? 0x3u : 0xfu;  // 16-query steps of the tile
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // dK += dS^T Q   (K = 64 queries)
-            mma_ts_if(leader, tmem + 256, dst + pcol(kk), smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC,
-                   (i > 0 || kk > 0) ? 1u : 0u);
+            mma_ts_if(leader & ((qmask >> kk) & 1u), tmem + 256, dst + pcol(kk),
+                      smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
           if (VK) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dK += P^T dO[:, :128]  (value gradient of the K columns)
-              mma_ts_if(leader, tmem + 256, pt + pcol(kk), smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
+              mma_ts_if(leader & ((qmask >> kk) & 1u), tmem + 256, pt + pcol(kk),
+                        smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
           }
           if (C::HAS_DV) {
             const uint32_t vo = VK ? 2 * kAtom64 : 0;
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dV += P^T dO[:, cols]
-              mma_ts_if(leader, tmem + 384, pt + pcol(kk), smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC,
-                     (i > 0 || kk > 0) ? 1u : 0u);
+              mma_ts_if(leader & ((qmask >> kk) & 1u), tmem + 384, pt + pcol(kk),
+                        smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit_if(leader, BAR_QEMPTY(s));
           if (FQ) {
@@ -380,10 +389,11 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
             if (!wwait(BAR_DQFREE(i & 1), (i >> 1) & 1, 5)) break;
             tc_fence_after();
             const uint32_t dqt = tmem + 384 + 64 * (i & 1), sds = sDS + (i & 1) * kAtom128;
+            const uint32_t idq = tail ? IDESC_DQ32 : IDESC_DQ;
 #pragma unroll
             for (int kk = 0; kk < 8; ++kk)
               mma_ss_if(leader, dqt, smem_desc_sw128(sRes + kk * 2048, kAtom128, 1024),
-                        smem_desc_sw128(sds + kk * 2048, kAtom128, 1024), IDESC_DQ, kk > 0);
+                        smem_desc_sw128(sds + kk * 2048, kAtom128, 1024), idq, kk > 0);
           }
         }
         // the next S^T / dP^T of this buffer is issued after the MMAs that read its P^T / dS^T
