@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VMB_ABI_VERSION 4
+#define VMB_ABI_VERSION 5
 
 #define VMB_DTYPE_BF16 0
 #define VMB_DTYPE_F16 1
@@ -144,6 +144,12 @@ typedef struct vmb_fea_bwd_args {
 } vmb_fea_bwd_args;
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);
+/* The smallest workspace vmb_fea_bwd accepts (ABI 5). vmb_fea_bwd_workspace_bytes reports the
+ * preferred size, which for the last VMonarch R step (v_is_k, dv = 2 d, n_kv <= 4096) adds a dS^T
+ * buffer (batch x round_up(n_kv, 128) x round_up(n_q, 64) 16-bit values) so that dQ comes from
+ * dS by a GEMM instead of a kernel recomputing S and dP; a workspace between the two sizes runs
+ * the latter. -1 for malformed sizes. */
+int64_t vmb_fea_bwd_min_workspace_bytes(const vmb_fea_bwd_args* a);
 int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream);
 
 /*

@@ -6,6 +6,8 @@ Tolerances, checked both ways:
   north-star absolute bounds: o max-abs 2e-2 and mean-abs 2e-3; e within 1e-3 of max|e|;
       gradients max-abs 5e-2 (floored at 8e-3 * max|grad|, the bf16 rounding of large gradients).
 """
+import ctypes
+
 import pytest
 import torch
 
@@ -286,3 +288,42 @@ def test_grad_mode_finalize_equals_add_then_cast(case):
             assert torch.equal(g, r), name
         else:  # the mma.sync kernels add with atomics: the summation order varies run to run
             torch.testing.assert_close(g.float(), r.float(), rtol=1e-2, atol=1e-2)
+
+
+def test_last_r_step_dq_with_and_without_the_ds_workspace(monkeypatch):
+    # The last VMonarch R step (V aliasing K, V2) takes dQ = dS K from the dS^T the dK/dV kernel
+    # stores when the workspace holds it, and otherwise (the minimal workspace, as the no-alloc
+    # entry point passes) runs the dq kernel that recomputes S and dP. Both must agree.
+    from vmonarch_b200 import _native as N, ops
+    gen = torch.Generator().manual_seed(11)
+    B, n, D = 2, 1560, 128
+    q, k, v2 = (torch.randn(B, n, D, generator=gen).bfloat16().cuda() for _ in range(3))
+    do = torch.randn(B, n, 2 * D, generator=gen).bfloat16().cuda()
+    sm = D ** -0.5
+    o = torch.empty(B, n, 2 * D, dtype=torch.bfloat16, device="cuda")
+    lse, ent = torch.empty(B, n, device="cuda"), torch.empty(B, n, device="cuda")
+    ops.fea_fwd(q, k, k, o, lse, ent, sm, v2=v2)
+
+    def run():
+        g = [torch.zeros(B, n, D, device="cuda") for _ in range(3)]
+        ops.fea_bwd(q, k, k, o, do, lse, g[0], g[1], None, sm, v2=v2, grad_v2=g[2], grad_mode=1, v_is_k=True)
+        torch.cuda.synchronize()
+        return g
+
+    full = run()
+    args = _bwd_args(B, n, D)
+    least = N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(args))
+    ds = B * ((n + 127) // 128 * 128) * ((n + 63) // 64 * 64) * 2
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(args)) >= 3 * B * n * 4 + ds  # holds dS^T
+    monkeypatch.setattr(N.lib, "vmb_fea_bwd_workspace_bytes", lambda a: least)
+    small = run()
+    for name, a, b in zip(("dq", "dk", "dv2"), full, small):
+        assert torch.isfinite(a).all() and torch.isfinite(b).all()
+        assert max_rel_err(a, b) <= 1e-2, name
+
+
+def _bwd_args(B, n, D):
+    from vmonarch_b200 import _native as N
+    a = N.FeaBwdArgs()
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1, a.grad_mode, a.v_is_k = B, n, n, D, 2 * D, D, 1, 1
+    return a

@@ -25,7 +25,7 @@ c_vp = ctypes.c_void_p
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 
-ABI_VERSION = 4  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+ABI_VERSION = 5  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
 
 
 class FeaFwdArgs(ctypes.Structure):
@@ -94,6 +94,7 @@ SIGNATURES = {
     "vmb_fea_fwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaFwdArgs)]),
     "vmb_fea_fwd": (ctypes.c_int, [ctypes.POINTER(FeaFwdArgs), c_vp]),
     "vmb_fea_bwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaBwdArgs)]),
+    "vmb_fea_bwd_min_workspace_bytes": (c_i64, [ctypes.POINTER(FeaBwdArgs)]),
     "vmb_fea_bwd": (ctypes.c_int, [ctypes.POINTER(FeaBwdArgs), c_vp]),
     "vmb_fea_bwd_noalloc": (ctypes.c_int, [ctypes.POINTER(FeaBwdArgs), c_vp]),
     "vmb_lstep_fwd": (ctypes.c_int, [ctypes.POINTER(LstepArgs), c_vp]),

@@ -142,25 +142,45 @@ static bool bwd_fuses_dq(const vmb_fea_bwd_args* a) {
   return vmb::fea_bwd_fuses_dq((int)a->n_kv, a->dv, a->v_is_k != 0, a->grad_mode, a->deterministic != 0);
 }
 
+// tcgen05 path: dQ = dS K from the dS^T the dK/dV kernel stores (no dq kernel, no split)
+static bool bwd_ds_gemm(const vmb_fea_bwd_args* a) {
+  return vmb::fea_bwd_ds_gemm((int)a->n_q, (int)a->n_kv, a->dv, a->v_is_k != 0, a->grad_mode);
+}
+
 // tcgen05 path: CTAs sharing one query tile's key range in the dq kernel (1: no split)
-static int bwd_dq_split(const vmb_fea_bwd_args* a) {
-  if (bwd_fuses_dq(a)) return 1;
+static int bwd_dq_split(const vmb_fea_bwd_args* a, bool use_ds) {
+  if (bwd_fuses_dq(a) || use_ds) return 1;
   return vmb::fea_bwd_dq_split(a->batch, (int)a->n_q, (int)a->n_kv, a->grad_mode != 0);
 }
 
+// tcgen05 workspace: three statistics planes, then either the split key range's partial dQ tiles
+// (dq kernel) or the dS^T buffer (dQ from dS, taken when the workspace holds it)
+static int64_t bwd_planes_bytes(const vmb_fea_bwd_args* a) {
+  return 3 * round_up(a->batch * round_up(a->n_q, 128) * 4, 256);
+}
+static int64_t bwd_min_bytes(const vmb_fea_bwd_args* a) {
+  const int split = bwd_dq_split(a, false);
+  return bwd_planes_bytes(a) + (split > 1 ? round_up((int64_t)split * a->batch * round_up(a->n_q, 128) * 128 * 4, 256) : 0);
+}
+static int64_t bwd_ds_need(const vmb_fea_bwd_args* a) {
+  return bwd_planes_bytes(a) + round_up(vmb::fea_bwd_ds_bytes(a->batch, (int)a->n_q, (int)a->n_kv), 256);
+}
+
+
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a) {
   if (!a || a->batch < 0 || a->n_q < 0) return -1;
-  if (bwd_uses_sm100(a)) {
-    const int64_t n_pad = round_up(a->n_q, 128);
-    int64_t bytes = 3 * round_up(a->batch * n_pad * 4, 256);
-    const int split = bwd_dq_split(a);
-    if (split > 1) bytes += round_up((int64_t)split * a->batch * n_pad * 128 * 4, 256);
-    return bytes;
-  }
+  if (bwd_uses_sm100(a))  // the preferred size: room for dS^T where it is used
+    return bwd_ds_gemm(a) ? std::max(bwd_min_bytes(a), bwd_ds_need(a)) : bwd_min_bytes(a);
   const int64_t rows = a->batch * a->n_q;
   int64_t bytes = 2 * round_up(rows * 4, 256);
   if (a->grad_mode == 0) bytes += round_up(rows * a->d * 4, 256);
   return bytes;
+}
+
+int64_t vmb_fea_bwd_min_workspace_bytes(const vmb_fea_bwd_args* a) {
+  if (!a || a->batch < 0 || a->n_q < 0) return -1;
+  if (!bwd_uses_sm100(a)) return vmb_fea_bwd_workspace_bytes(a);
+  return bwd_min_bytes(a);
 }
 
 int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
@@ -193,9 +213,11 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
        a->grad_v2_bs) & 7)
     return fail(VMB_EINVAL, "vmb_fea_bwd: batch strides must be multiples of 8 elements");
   if (a->batch == 0) return VMB_OK;
-  const int64_t need = vmb_fea_bwd_workspace_bytes(a);
+  // at least the minimal workspace; the tcgen05 path takes dQ from dS when the workspace also holds dS^T
+  const int64_t need = bwd_uses_sm100(a) ? bwd_min_bytes(a) : vmb_fea_bwd_workspace_bytes(a);
   if (!a->workspace || a->workspace_bytes < need)
     return fail(VMB_EINVAL, "vmb_fea_bwd: workspace of %lld bytes needed", (long long)need);
+  const bool use_ds = bwd_uses_sm100(a) && bwd_ds_gemm(a) && a->workspace_bytes >= bwd_ds_need(a);
   if (a->n_q == 0) return VMB_OK;  // no query: no gradient contribution (grad_mode 1 adds nothing)
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
@@ -210,7 +232,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   float* gg = sm100 ? nullptr : reinterpret_cast<float*>(ws + round_up(rows * 4, 256));
   float* dq_acc =
       (!sm100 && a->grad_mode == 0) ? reinterpret_cast<float*>(ws + 2 * round_up(rows * 4, 256)) : nullptr;
-  count(sm100 ? (bwd_fuses_dq(a) ? 2 : (bwd_dq_split(a) > 1 ? 4 : 3)) : (dq_acc ? 3 : 2));
+  count(sm100 ? (bwd_fuses_dq(a) ? 2 : (bwd_dq_split(a, use_ds) > 1 ? 4 : 3)) : (dq_acc ? 3 : 2));
   cudaError_t e = vmb::fea_bwd_pre(a->o, a->o_bs, a->dout, a->do_bs, a->lse, a->ent, a->dent, cc, gg, a->batch,
                                    (int)a->n_q, a->dv, fold, n_pad, a->sm_scale, a->delta, bf16, st);
   if (e != cudaSuccess) return cuda_status(e, "vmb_fea_bwd(pre)");
@@ -222,8 +244,8 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.q = a->q; p.k = a->k; p.v = a->v; p.v2 = a->v2; p.dout = a->dout; p.lse = a->lse; p.cc = cc; p.gg = gg;
   p.fold = fold; p.n_pad = n_pad;
   p.dq_part = nullptr;
-  if (sm100 && bwd_dq_split(a) > 1)
-    p.dq_part = reinterpret_cast<float*>(ws + 3 * round_up(a->batch * n_pad * 4, 256));
+  if (sm100 && bwd_dq_split(a, use_ds) > 1) p.dq_part = reinterpret_cast<float*>(ws + bwd_planes_bytes(a));
+  p.ds = use_ds ? static_cast<void*>(ws + bwd_planes_bytes(a)) : nullptr;
   p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
   p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
   p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.do_bs = a->do_bs;
@@ -348,3 +370,7 @@ int vmb_cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, in
 }
 
 }  // extern "C"
+
+namespace vmb {
+int64_t fea_bwd_min_workspace_bytes(const vmb_fea_bwd_args* a) { return vmb_fea_bwd_min_workspace_bytes(a); }
+}  // namespace vmb

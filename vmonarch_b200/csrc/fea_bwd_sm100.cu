@@ -71,6 +71,8 @@ struct Sm100BwdParams {
   float* dq;     // fused dQ: fp32 [batch][n_q][128] (batch stride dq_bs), added into
   int64_t dq_bs;
   CUtensorMap tm_f0, tm_f1;  // acc 3: the fp32 accumulators of tm_g0 / tm_g1 (boxes of 32 x 128)
+  void* ds;                  // dK/dV kernel: dS^T out [batch][ds_rows][ds_ld] (16-bit), or null
+  int64_t ds_ld, ds_bs;      // row stride (queries, padded to 64) and batch stride (elements)
 };
 
 // acc 3: out16 = 16-bit(TMEM accumulator + fp32 accumulator tile staged at `fin`), for the 32-column
@@ -464,6 +466,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         }
         tmem_st8(ts + pcol(qc), pk);
         tmem_st8(tdp + pcol(qc), dk);
+        if (p.ds) {  // dS^T row (key k0 + row), queries [64 qtile + 16 qc, +16) for the dQ GEMM
+          uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.ds) + (int64_t)bi * p.ds_bs + (int64_t)(k0 + row) * p.ds_ld +
+                                                qtile(i) * 64 + 16 * qc);
+          dst[0] = make_uint4(dk[0], dk[1], dk[2], dk[3]);
+          dst[1] = make_uint4(dk[4], dk[5], dk[6], dk[7]);
+        }
         if (FQ) {  // dS^T row (key) `row`, queries [16qc, 16qc + 16): 16-byte chunks 2qc, 2qc + 1, swizzled
           const uint32_t rb = sDS + stm * kAtom128 + row * 128;
           asm volatile("st.shared.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(rb + (((2 * qc) ^ (row & 7)) << 4)), "r"(dk[0]),
@@ -942,6 +950,133 @@ __global__ void dq_split_finalize_kernel(const float* part, int split, int64_t b
   }
 }
 
+// ================================================================================ dQ = dS K
+// CTA = 128 queries of one sequence; streams the dS^T rows (keys) the dK/dV kernel stored and the
+// K tile, 64 keys per stage: dQ += dS K with A = dS read M-major from the dS^T rows and B = K
+// read N-major (M = N = 128, 4 MMAs of 16 keys per stage). HBM-bound (dS is read once); the
+// epilogue writes dQ like the dq kernel (16-bit store, fp32 reduce-add or store).
+constexpr int kGemmStages = 4;
+constexpr int kGemmStage = 4 * kAtom64;  // dS^T 2 atoms (64 queries x 64 keys) | K 2 atoms (64 d x 64 keys)
+
+template <typename T>
+__global__ void __launch_bounds__(192, 1) dq_from_ds_kernel(const __grid_constant__ Sm100BwdParams p) {
+  constexpr bool kBf16 = Elem<T>::is_bf16;
+  constexpr uint32_t IDESC = idesc_f16(kBf16, 128, 128, true, true);
+  constexpr int NS = kGemmStages;
+  extern __shared__ uint8_t smem_raw[];
+  __shared__ __align__(8) uint64_t bars[2 * NS + 2];
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ int abort_sh;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int bi = blockIdx.x / p.n_tiles;
+  const int q0 = (blockIdx.x % p.n_tiles) * 128;
+  const int nkc = (p.n_kv + 63) / 64;
+  const uint32_t BAR_FIN_OFF = 8u * (2 * NS + 1);
+  const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
+  auto stage = [&](int s) { return sbase + (uint32_t)s * kGemmStage; };
+  const uint32_t bar0 = smem_u32(bars);
+  auto BAR_FULL = [&](int s) { return bar0 + 8u * s; };
+  auto BAR_EMPTY = [&](int s) { return bar0 + 8u * (NS + s); };
+  const uint32_t BAR_DONE = bar0 + 8u * (2 * NS);
+  volatile int* abort = &abort_sh;
+
+  if (threadIdx.x == 0) {
+    abort_sh = 0;
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(BAR_FULL(s), 1);
+      mbar_init(BAR_EMPTY(s), 1);
+    }
+    mbar_init(BAR_DONE, 1);
+    mbar_init(bar0 + BAR_FIN_OFF, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(smem_u32(&tmem_base_sh), 128);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      prefetch_tmap(&p.tm_a);
+      prefetch_tmap(&p.tm_c);
+      int armed[NS];
+      for (int s = 0; s < NS; ++s) armed[s] = 0;
+      for (int c = 0; c < nkc; ++c) {
+        const int s = c % NS;
+        if (c >= NS && !mbar_wait(BAR_EMPTY(s), ((c / NS) - 1) & 1, abort, &g_bwd_err, 64)) break;
+        mbar_expect_tx(BAR_FULL(s), kGemmStage);
+        for (int a = 0; a < 2; ++a) {
+          tma_load_3d(stage(s) + a * kAtom64, &p.tm_a, q0 + 64 * a, 64 * c, bi, BAR_FULL(s));
+          tma_load_3d(stage(s) + (2 + a) * kAtom64, &p.tm_c, 64 * a, 64 * c, bi, BAR_FULL(s));
+        }
+        armed[s] = c / NS + 1;
+        if (p.acc == 3 && c == nkc - 1)  // the accumulator tile the epilogue reads, into L2
+          for (int x = 0; x < 4; ++x) tma_prefetch_3d(&p.tm_f0, 32 * x, q0, bi);
+      }
+      for (int s = 0; s < NS; ++s)
+        if (armed[s] > 0) mbar_wait_drain(BAR_FULL(s), (armed[s] - 1) & 1);
+    }
+  } else if (warp == 1) {
+    const uint32_t leader = elect_one() ? 1u : 0u;
+    bool ok = true;
+    for (int c = 0; c < nkc; ++c) {
+      const int s = c % NS;
+      if (!__all_sync(0xffffffffu, mbar_wait(BAR_FULL(s), (c / NS) & 1, abort, &g_bwd_err, 64))) {
+        ok = false;
+        break;
+      }
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 0; kk < 4; ++kk)
+        mma_ss_if(leader, tmem, smem_desc_sw128(stage(s) + kk * 2048, kAtom64, 1024),
+                  smem_desc_sw128(stage(s) + 2 * kAtom64 + kk * 2048, kAtom64, 1024), IDESC, (c > 0 || kk > 0) ? 1u : 0u);
+      mma_commit_if(leader, BAR_EMPTY(s));
+    }
+    (void)ok;
+    if (elect_one()) {
+      mma_commit(BAR_DONE);
+      mbar_wait_drain(BAR_DONE, 0);
+    }
+    __syncwarp();
+  } else {
+    const int quad = warp & 3, row = quad * 32 + lane;
+    const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
+    bool ok = __all_sync(0xffffffffu, mbar_wait(BAR_DONE, 0, abort, &g_bwd_err, 64));
+    tc_fence_after();
+    const uint32_t st = stage(0), out16 = stage(2);  // every stage is idle once DONE
+    const bool fin = p.acc == 3;  // 16-bit dQ = fp32 accumulator tile + this call's dQ
+    bool fin_issued = false;
+    if (fin) {
+      const uint32_t bfin = bar0 + BAR_FIN_OFF;
+      if (warp == 2 && lane == 0 && ok) {
+        fin_issued = true;
+        mbar_expect_tx(bfin, 65536);
+        for (int x = 0; x < 4; ++x) tma_load_3d(st + x * 16384, &p.tm_f0, 32 * x, q0, bi, bfin);
+      }
+      if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bfin, 0, abort, &g_bwd_err, 64));
+      if (ok) finalize_rows<T>(tmem + lane_off, st, out16, row, 0, 4);
+    } else if (ok) {
+      stage_acc_rows<T>(tmem + lane_off, st, row, p.acc != 0, 0, 4);
+    }
+    fence_proxy_async_smem();
+    ok = named_bar_and(1, 128, ok);
+    if (warp == 2 && lane == 0 && ok && !*abort) {
+      issue_grad_tile(&p.tm_g0, fin ? out16 : st, q0, bi, fin ? 0 : p.acc);
+      tma_store_commit_and_wait();
+    }
+    if (fin_issued) mbar_wait_drain(bar0 + BAR_FIN_OFF, 0);  // loads still in flight after a timeout
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  if (warp == 0) tmem_dealloc(tmem, 128);
+}
+
 // ================================================================================ host side
 template <typename Kern>
 cudaError_t run(Kern kern, int smem, int64_t blocks, int threads, const Sm100BwdParams& p, cudaStream_t st) {
@@ -992,6 +1127,12 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.n_kv = b.n_kv;
   pa.n_tiles = (b.n_kv + 127) / 128;
   pa.acc = b.acc_kv;
+  const bool ds_gemm = b.ds != nullptr && fea_bwd_ds_gemm(b.n_q, b.n_kv, dv, vk, b.acc_q);
+  if (ds_gemm) {
+    pa.ds = b.ds;
+    pa.ds_ld = (b.n_q + 63) / 64 * 64;
+    pa.ds_bs = (int64_t)(b.n_kv + 127) / 128 * 128 * pa.ds_ld;
+  }
   pa.scale_log2 = b.scale_log2;
   pa.sm_scale = b.sm_scale;
   cudaError_t e;
@@ -1015,6 +1156,21 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     e = run(fea_bwd_dkdv_kernel<T, 2, false, 4, kDkdvWarpgroups>, DkdvCfg<2, false, 4>::SMEM, blocks_a, kDkdvThreads, pa, st);
   }
   if (e != cudaSuccess) return e;
+  if (ds_gemm) {
+    // ---- dQ = dS K from the dS^T rows the dK/dV kernel stored
+    Sm100BwdParams pg{};
+    if (!tma::make_map(&pg.tm_a, b.ds, bf16, pa.ds_ld, pa.ds_bs / pa.ds_ld, batch, pa.ds_bs, 64)) return cudaErrorInvalidValue;
+    if (!tma::make_map(&pg.tm_c, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 64)) return cudaErrorInvalidValue;
+    if (!grad_map(&pg.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
+    if (b.acc_q == 3 && !tma::make_map_f32(&pg.tm_f0, b.fin_q, 128, b.n_q, batch, b.fin_q_bs, 128))
+      return cudaErrorInvalidValue;
+    pg.n_q = b.n_q;
+    pg.n_kv = b.n_kv;
+    pg.n_tiles = (b.n_q + 127) / 128;
+    pg.acc = b.acc_q;
+    constexpr int smem = 1024 + kGemmStages * kGemmStage;
+    return run(dq_from_ds_kernel<T>, smem, (int64_t)pg.n_tiles * batch, 192, pg, st);
+  }
   // ---- dQ: 128-key tiles (dO staged in TMEM when it is 256 wide)
   Sm100BwdParams pb{};
   if (!tma::make_map(&pb.tm_a, b.q, bf16, 128, b.n_q, batch, b.q_bs, 128)) return cudaErrorInvalidValue;
@@ -1107,6 +1263,17 @@ bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) 
   // dQ from the dK kernel (no dq kernel) when V aliases K without V2 (free TMEM columns), dQ is
   // fp32 (reductions) and each dQ element receives at most 32 of them (<= 32 key tiles)
   return vk && dv == 128 && (acc_q == 1 || acc_q == 2) && !deterministic && (n_kv + 127) / 128 <= 32;
+}
+
+bool fea_bwd_ds_gemm(int n_q, int n_kv, int dv, bool vk, int acc_q) {
+  // the last VMonarch R step: the 256-wide dP makes recomputing S and dP in a dq kernel cost more
+  // than one HBM round trip of dS (short sequences: the buffer is batch x n_kv x n_q x 2 bytes)
+  (void)acc_q;  // every write mode, the finalize mode included
+  return vk && dv == 256 && (n_kv + 127) / 128 <= 32 && n_q <= 4096;
+}
+
+int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv) {
+  return batch * ((int64_t)(n_kv + 127) / 128 * 128) * ((int64_t)(n_q + 63) / 64 * 64) * 2;
 }
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {

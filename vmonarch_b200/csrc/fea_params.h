@@ -32,6 +32,7 @@ struct BwdParams {
   const float* fold;  // tcgen05 path: planes nl, nc, ng, each [batch][n_pad] (see fea_bwd_pre)
   int64_t n_pad;      // rows per sequence of the planes: n_q rounded up to 128
   float* dq_part;     // tcgen05 path, split key range: partial dQ tiles [split][batch][n_pad][D]
+  void* ds;           // tcgen05 path, dQ from dS: dS^T [batch][round_up(n_kv, 128)][round_up(n_q, 64)] 16-bit
   float* dq;          // fp32 accumulator [batch][n_q][D] (batch stride dq_bs)
   void* dk;           // [batch][n_kv][D]      element type or fp32 (acc_kv)
   void* dv;           // [batch][n_kv][dv1]    unused when v aliases k

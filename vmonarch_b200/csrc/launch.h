@@ -4,6 +4,8 @@
 #include <stdint.h>
 #include "fea_params.h"
 
+struct vmb_fea_bwd_args;
+
 namespace vmb {
 
 struct LstepParams {
@@ -37,6 +39,14 @@ cudaError_t fea_bwd_sm100(const BwdParams& p, int64_t batch, int dv, bool vk, bo
 int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc);
 // True when the tcgen05 backward forms dQ inside the dK kernel (fp32 reductions, no dq kernel).
 bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic);
+// True when the tcgen05 backward takes dQ from dS: the dK/dV kernel stores dS^T (16-bit) and a
+// GEMM forms dQ = dS K, instead of a dq kernel recomputing S and dP (V aliasing K with V2).
+bool fea_bwd_ds_gemm(int n_q, int n_kv, int dv, bool vk, int acc_q);
+// Bytes of that dS^T buffer.
+int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv);
+// Smallest workspace vmb_fea_bwd accepts for these arguments (vmb_fea_bwd_workspace_bytes
+// reports the preferred size, which may add optional buffers such as dS^T).
+int64_t fea_bwd_min_workspace_bytes(const vmb_fea_bwd_args* a);
 // Workspace bytes that let the tcgen05 forward split long key ranges (0: it would not split).
 int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk);
 // Key-range split the tcgen05 forward will use with this workspace (1 = none).

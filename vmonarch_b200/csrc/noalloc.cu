@@ -58,7 +58,7 @@ int scratch_address(void** out) {
 
 extern "C" int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream) {
   if (!a) return vmb::set_error(VMB_EINVAL, "vmb_fea_bwd_noalloc: null args");
-  const int64_t need = vmb_fea_bwd_workspace_bytes(a);
+  const int64_t need = vmb::fea_bwd_min_workspace_bytes(a);  // optional extras (dS^T) are skipped
   if (need < 0) return vmb::set_error(VMB_EINVAL, "vmb_fea_bwd_noalloc: bad sizes");
   if (need > kNoAllocScratchBytes)
     return vmb::set_error(VMB_EINVAL,
