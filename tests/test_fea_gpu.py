@@ -290,40 +290,54 @@ def test_grad_mode_finalize_equals_add_then_cast(case):
             torch.testing.assert_close(g.float(), r.float(), rtol=1e-2, atol=1e-2)
 
 
-def test_last_r_step_dq_with_and_without_the_ds_workspace(monkeypatch):
-    # The last VMonarch R step (V aliasing K, V2) takes dQ = dS K from the dS^T the dK/dV kernel
-    # stores when the workspace holds it, and otherwise (the minimal workspace, as the no-alloc
-    # entry point passes) runs the dq kernel that recomputes S and dP. Both must agree.
+@pytest.mark.parametrize("case", ["last_r", "plain"])
+def test_dq_with_and_without_the_ds_workspace(monkeypatch, case):
+    # dQ = dS K from the dS^T the dK/dV kernel stores (when the workspace holds it) against the dq
+    # kernel that recomputes S and dP (the minimal workspace, as the no-alloc entry point passes)
+    # for the last VMonarch R step (V aliasing K, V2); a plain dv = 128 call has one path, and its
+    # preferred and minimal sizes agree. Both must give the same gradients.
     from vmonarch_b200 import _native as N, ops
     gen = torch.Generator().manual_seed(11)
-    B, n, D = 2, 1560, 128
-    q, k, v2 = (torch.randn(B, n, D, generator=gen).bfloat16().cuda() for _ in range(3))
-    do = torch.randn(B, n, 2 * D, generator=gen).bfloat16().cuda()
+    D = 128
+    B, nq, nk = (2, 1560, 1560) if case == "last_r" else (24, 1560, 2048)
+    vk = case == "last_r"
+    q = torch.randn(B, nq, D, generator=gen).bfloat16().cuda()
+    k, v = (torch.randn(B, nk, D, generator=gen).bfloat16().cuda() for _ in range(2))
+    v2 = v if vk else None
+    vv = k if vk else v
+    dvw = 2 * D if vk else D
+    do = torch.randn(B, nq, dvw, generator=gen).bfloat16().cuda()
     sm = D ** -0.5
-    o = torch.empty(B, n, 2 * D, dtype=torch.bfloat16, device="cuda")
-    lse, ent = torch.empty(B, n, device="cuda"), torch.empty(B, n, device="cuda")
-    ops.fea_fwd(q, k, k, o, lse, ent, sm, v2=v2)
+    o = torch.empty(B, nq, dvw, dtype=torch.bfloat16, device="cuda")
+    lse, ent = torch.empty(B, nq, device="cuda"), torch.empty(B, nq, device="cuda")
+    ops.fea_fwd(q, k, vv, o, lse, ent, sm, v2=v2)
 
     def run():
-        g = [torch.zeros(B, n, D, device="cuda") for _ in range(3)]
-        ops.fea_bwd(q, k, k, o, do, lse, g[0], g[1], None, sm, v2=v2, grad_v2=g[2], grad_mode=1, v_is_k=True)
+        g = [torch.zeros(B, n_, D, device="cuda") for n_ in (nq, nk, nk)]
+        ops.fea_bwd(q, k, vv, o, do, lse, g[0], g[1], None if vk else g[2], sm, v2=v2, grad_v2=g[2] if vk else None,
+                    grad_mode=1, v_is_k=vk)
         torch.cuda.synchronize()
         return g
 
     full = run()
-    args = _bwd_args(B, n, D)
+    args = _bwd_args(B, nq, nk, D, vk)
     least = N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(args))
-    ds = B * ((n + 127) // 128 * 128) * ((n + 63) // 64 * 64) * 2
-    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(args)) >= 3 * B * n * 4 + ds  # holds dS^T
+    ds = B * ((nk + 127) // 128 * 128) * ((nq + 63) // 64 * 64) * 2
+    preferred = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(args))
+    if vk:
+        assert preferred >= ds  # the preferred size holds dS^T
+    else:
+        assert preferred == least
     monkeypatch.setattr(N.lib, "vmb_fea_bwd_workspace_bytes", lambda a: least)
     small = run()
-    for name, a, b in zip(("dq", "dk", "dv2"), full, small):
+    for name, a, b in zip(("dq", "dk", "dv"), full, small):
         assert torch.isfinite(a).all() and torch.isfinite(b).all()
         assert max_rel_err(a, b) <= 1e-2, name
 
 
-def _bwd_args(B, n, D):
+def _bwd_args(B, nq, nk, D, vk):
     from vmonarch_b200 import _native as N
     a = N.FeaBwdArgs()
-    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1, a.grad_mode, a.v_is_k = B, n, n, D, 2 * D, D, 1, 1
+    a.batch, a.n_q, a.n_kv, a.d = B, nq, nk, D
+    a.dv, a.dv1, a.grad_mode, a.v_is_k = (2 * D if vk else D), D, 1, int(vk)
     return a

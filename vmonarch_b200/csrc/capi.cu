@@ -144,7 +144,7 @@ static bool bwd_fuses_dq(const vmb_fea_bwd_args* a) {
 
 // tcgen05 path: dQ = dS K from the dS^T the dK/dV kernel stores (no dq kernel, no split)
 static bool bwd_ds_gemm(const vmb_fea_bwd_args* a) {
-  return vmb::fea_bwd_ds_gemm((int)a->n_q, (int)a->n_kv, a->dv, a->v_is_k != 0, a->grad_mode);
+  return vmb::fea_bwd_ds_gemm(a->batch, (int)a->n_q, (int)a->n_kv, a->dv, a->v_is_k != 0, a->grad_mode);
 }
 
 // tcgen05 path: CTAs sharing one query tile's key range in the dq kernel (1: no split)

@@ -1127,7 +1127,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.n_kv = b.n_kv;
   pa.n_tiles = (b.n_kv + 127) / 128;
   pa.acc = b.acc_kv;
-  const bool ds_gemm = b.ds != nullptr && fea_bwd_ds_gemm(b.n_q, b.n_kv, dv, vk, b.acc_q);
+  const bool ds_gemm = b.ds != nullptr && fea_bwd_ds_gemm(batch, b.n_q, b.n_kv, dv, vk, b.acc_q);
   if (ds_gemm) {
     pa.ds = b.ds;
     pa.ds_ld = (b.n_q + 63) / 64 * 64;
@@ -1265,9 +1265,12 @@ bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) 
   return vk && dv == 128 && (acc_q == 1 || acc_q == 2) && !deterministic && (n_kv + 127) / 128 <= 32;
 }
 
-bool fea_bwd_ds_gemm(int n_q, int n_kv, int dv, bool vk, int acc_q) {
-  // the last VMonarch R step: the 256-wide dP makes recomputing S and dP in a dq kernel cost more
-  // than one HBM round trip of dS (short sequences: the buffer is batch x n_kv x n_q x 2 bytes)
+bool fea_bwd_ds_gemm(int64_t batch, int n_q, int n_kv, int dv, bool vk, int acc_q) {
+  // The last VMonarch R step (short sequences): with a 256-wide dP, recomputing S and dP in a dq
+  // kernel costs more tensor work (and energy under the power cap) than one HBM round trip of dS.
+  // With dv = 128 (the recompute's shape class) the dq kernel is cheaper: storing dS^T slowed the
+  // dK/dV kernel as much as the GEMM saved (measured), so those calls keep it.
+  (void)batch;
   (void)acc_q;  // every write mode, the finalize mode included
   return vk && dv == 256 && (n_kv + 127) / 128 <= 32 && n_q <= 4096;
 }

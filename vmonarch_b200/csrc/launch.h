@@ -40,8 +40,8 @@ int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc);
 // True when the tcgen05 backward forms dQ inside the dK kernel (fp32 reductions, no dq kernel).
 bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic);
 // True when the tcgen05 backward takes dQ from dS: the dK/dV kernel stores dS^T (16-bit) and a
-// GEMM forms dQ = dS K, instead of a dq kernel recomputing S and dP (V aliasing K with V2).
-bool fea_bwd_ds_gemm(int n_q, int n_kv, int dv, bool vk, int acc_q);
+// GEMM forms dQ = dS K, instead of a dq kernel recomputing S and dP.
+bool fea_bwd_ds_gemm(int64_t batch, int n_q, int n_kv, int dv, bool vk, int acc_q);
 // Bytes of that dS^T buffer.
 int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv);
 // Smallest workspace vmb_fea_bwd accepts for these arguments (vmb_fea_bwd_workspace_bytes
