@@ -162,8 +162,9 @@ static int64_t bwd_min_bytes(const vmb_fea_bwd_args* a) {
   const int split = bwd_dq_split(a, false);
   return bwd_planes_bytes(a) + (split > 1 ? round_up((int64_t)split * a->batch * round_up(a->n_q, 128) * 128 * 4, 256) : 0);
 }
+// + 256 bytes: dS^T starts at a 256-byte boundary (the dK/dV kernel stores it 32 bytes at a time)
 static int64_t bwd_ds_need(const vmb_fea_bwd_args* a) {
-  return bwd_planes_bytes(a) + round_up(vmb::fea_bwd_ds_bytes(a->batch, (int)a->n_q, (int)a->n_kv), 256);
+  return bwd_planes_bytes(a) + round_up(vmb::fea_bwd_ds_bytes(a->batch, (int)a->n_q, (int)a->n_kv), 256) + 256;
 }
 
 
@@ -245,7 +246,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   p.fold = fold; p.n_pad = n_pad;
   p.dq_part = nullptr;
   if (sm100 && bwd_dq_split(a, use_ds) > 1) p.dq_part = reinterpret_cast<float*>(ws + bwd_planes_bytes(a));
-  p.ds = use_ds ? static_cast<void*>(ws + bwd_planes_bytes(a)) : nullptr;
+  p.ds = use_ds ? reinterpret_cast<void*>(round_up(reinterpret_cast<intptr_t>(ws + bwd_planes_bytes(a)), 256)) : nullptr;
   p.dq = dq_acc ? dq_acc : static_cast<float*>(a->grad_q);
   p.dk = a->grad_k; p.dv = a->grad_v; p.dv2 = a->grad_v2;
   p.q_bs = a->q_bs; p.k_bs = a->k_bs; p.v_bs = a->v_bs; p.v2_bs = a->v2_bs; p.do_bs = a->do_bs;

@@ -194,6 +194,13 @@ __device__ __forceinline__ void red_add_f32(float* ptr, float v) {
   asm volatile("red.global.add.f32 [%0], %1;" ::"l"(ptr), "f"(v) : "memory");
 }
 
+// 32 bytes to a 32-byte aligned global address (one 256-bit store, sm_100)
+__device__ __forceinline__ void st_global_v8(void* ptr, const uint32_t* v) {
+  asm volatile("st.global.v8.b32 [%0], {%1, %2, %3, %4, %5, %6, %7, %8};" ::"l"(ptr), "r"(v[0]), "r"(v[1]), "r"(v[2]),
+               "r"(v[3]), "r"(v[4]), "r"(v[5]), "r"(v[6]), "r"(v[7])
+               : "memory");
+}
+
 template <typename T, int XA, bool VK, int NQS, int NWG, bool FQ = false>
 __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const __grid_constant__ Sm100BwdParams p) {
   using C = DkdvCfg<XA, VK, NQS, FQ>;
@@ -443,6 +450,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       tc_fence_after();
       const uint32_t st = slot_stats(s);
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
+      // dS^T for the dQ GEMM (four warpgroups): the two 16-query chunks of this warpgroup's half
+      // are 64 contiguous bytes of the key's row, held here and stored after the tile is handed
+      // to the MMA warp, off the TMEM load -> exponentials -> TMEM store chain
+      uint32_t ds_hold[2][8];
       // 16-query chunks of this warpgroup's half(s): P^T / dS^T of chunk qc go to columns pcol(qc) of
       // S^T / dP^T, which lie inside what this warpgroup has already loaded
 #pragma unroll 1
@@ -466,7 +477,15 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         }
         tmem_st8(ts + pcol(qc), pk);
         tmem_st8(tdp + pcol(qc), dk);
-        if (p.ds) {  // dS^T row (key k0 + row), queries [64 qtile + 16 qc, +16) for the dQ GEMM
+        if (NWG == 4 && p.ds) {
+#pragma unroll
+          for (int e = 0; e < 8; ++e) {
+            if (qc & 1)
+              ds_hold[1][e] = dk[e];
+            else
+              ds_hold[0][e] = dk[e];
+          }
+        } else if (p.ds) {  // dS^T row (key k0 + row), queries [64 qtile + 16 qc, +16) for the dQ GEMM
           uint4* dst = reinterpret_cast<uint4*>(static_cast<T*>(p.ds) + (int64_t)bi * p.ds_bs + (int64_t)(k0 + row) * p.ds_ld +
                                                 qtile(i) * 64 + 16 * qc);
           dst[0] = make_uint4(dk[0], dk[1], dk[2], dk[3]);
@@ -486,6 +505,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       if (FQ) fence_proxy_async_smem();  // dS^T is read by the dQ^T MMA (async proxy)
       tc_fence_before();
       mbar_arrive(BAR_PDSFULL(stm));
+      if (NWG == 4 && p.ds) {  // dS^T row (key k0 + row), queries [64 qtile + 32 h0, +32)
+        uint8_t* dst = reinterpret_cast<uint8_t*>(static_cast<T*>(p.ds) + (int64_t)bi * p.ds_bs +
+                                                  (int64_t)(k0 + row) * p.ds_ld + qtile(i) * 64 + 32 * h0);
+        st_global_v8(dst, ds_hold[0]);
+        st_global_v8(dst + 32, ds_hold[1]);
+      }
       if (FQ) {
         // while the MMA warp runs this tile's dK MMAs: drain dQ^T(i - 2), complete since S^T(i) was
         // issued after it; then its buffer may take dQ^T(i)
@@ -954,15 +979,17 @@ __global__ void dq_split_finalize_kernel(const float* part, int split, int64_t b
 // CTA = 128 queries of one sequence; streams the dS^T rows (keys) the dK/dV kernel stored and the
 // K tile, 64 keys per stage: dQ += dS K with A = dS read M-major from the dS^T rows and B = K
 // read N-major (M = N = 128, 4 MMAs of 16 keys per stage). HBM-bound (dS is read once); the
-// epilogue writes dQ like the dq kernel (16-bit store, fp32 reduce-add or store).
-constexpr int kGemmStages = 4;
+// epilogue writes dQ like the dq kernel (16-bit store, fp32 reduce-add or store). Three stages
+// (96 KB) hold the epilogue's fp32 tile and keep two CTAs per SM, so one CTA's epilogue and
+// pipeline fill overlap the other's stream of dS.
+constexpr int kGemmStages = 3;
 constexpr int kGemmStage = 4 * kAtom64;  // dS^T 2 atoms (64 queries x 64 keys) | K 2 atoms (64 d x 64 keys)
 
-template <typename T>
-__global__ void __launch_bounds__(192, 1) dq_from_ds_kernel(const __grid_constant__ Sm100BwdParams p) {
+template <typename T, int NS>
+__global__ void __launch_bounds__(192, NS <= 3 ? 2 : 1) dq_from_ds_kernel(const __grid_constant__ Sm100BwdParams p) {
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC = idesc_f16(kBf16, 128, 128, true, true);
-  constexpr int NS = kGemmStages;
+  static_assert(NS >= 3, "the epilogue stages 96 KB in the pipeline stages");
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[2 * NS + 2];
   __shared__ uint32_t tmem_base_sh;
@@ -1169,7 +1196,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     pg.n_tiles = (b.n_q + 127) / 128;
     pg.acc = b.acc_q;
     constexpr int smem = 1024 + kGemmStages * kGemmStage;
-    return run(dq_from_ds_kernel<T>, smem, (int64_t)pg.n_tiles * batch, 192, pg, st);
+    return run(dq_from_ds_kernel<T, kGemmStages>, smem, (int64_t)pg.n_tiles * batch, 192, pg, st);
   }
   // ---- dQ: 128-key tiles (dO staged in TMEM when it is 256 wide)
   Sm100BwdParams pb{};
