@@ -122,6 +122,26 @@ def test_growing_row_max_forces_rescales(D, Dv):
     check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
 
 
+@pytest.mark.parametrize("Dv, steps", [(128, (320, 704)), (128, (256, 960)), (256, (320, 704))])
+def test_row_max_jumps_inside_a_key_tile(Dv, steps):
+    # The scores of half the rows jump far past the lazy-rescale threshold at fixed keys: at the
+    # second 64-key half of a tile (320, 704), or at a tile start (256, 960). Full tiles after a
+    # stream's first take the exponentials against the running reference and redo a half whose
+    # max passed it, so this covers the redo in either half, with rows of one warp disagreeing.
+    gen = torch.Generator().manual_seed(23)
+    N, D = 1152, 128
+    q = torch.randn(1, 2, N, D, generator=gen)
+    k = torch.randn(1, 2, N, D, generator=gen)
+    c = torch.randn(1, 2, 1, D, generator=gen)
+    q = (q + 1.5 * c * (torch.rand(1, 2, N, 1, generator=gen) > 0.5)).bfloat16().float()
+    for st in steps:
+        k[:, :, st:] += 1.5 * c
+    k = k.bfloat16().float()
+    v = torch.randn(1, 2, N, Dv, generator=gen).bfloat16().float()
+    do, de = torch.randn(1, 2, N, Dv, generator=gen), torch.randn(1, 2, N, generator=gen)
+    check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
+
+
 def test_split_key_range_backward_matches_and_is_deterministic():
     # Few query tiles over a long key range: in fp32-accumulate mode the dQ kernel splits the key
     # range over several CTAs (partial tiles summed in a fixed order). Check it against the

@@ -90,15 +90,19 @@ __device__ __forceinline__ float row_max_raw(const uint32_t (&sr)[N], int valid)
 // p = 2^(s * scale - m) for one row segment of N keys, packed to the element type, with the row
 // sum l and the entropy sum h = sum p (x - m). Pairs of keys go through the packed f32x2 FMA / add
 // (one instruction per pair) into two chains each. Keys >= valid (MASK) get x - m = -1e30, so
-// p = 0 and p (x - m) = 0 exactly.
-template <typename T, int N, bool ENT, bool MASK>
-__device__ __forceinline__ void probs_row(const uint32_t (&sr)[N], uint32_t (&pk)[N / 2], float sc, float m,
-                                          int valid, float& l, float& h) {
+// p = 0 and p (x - m) = 0 exactly. MAXO (unmasked segments): also returns the segment's max of
+// s * scale (four chains of three-input maxima beside the exponentials), else -1e30.
+template <typename T, int N, bool ENT, bool MASK, bool MAXO = false>
+__device__ __forceinline__ float probs_row(const uint32_t (&sr)[N], uint32_t (&pk)[N / 2], float sc, float m,
+                                           int valid, float& l, float& h) {
+  static_assert(!MASK || !MAXO, "masked segments take a separate max");
   float2 la[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float2 ha[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+  float mr[4] = {-1e30f, -1e30f, -1e30f, -1e30f};
   const float2 sc2 = make_float2(sc, sc), nm2 = make_float2(-m, -m);
 #pragma unroll
   for (int i = 0; i < N / 2; ++i) {
+    if (MAXO) mr[i & 3] = fmax3(mr[i & 3], __uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1]));
     float2 d = __ffma2_rn(make_float2(__uint_as_float(sr[2 * i]), __uint_as_float(sr[2 * i + 1])), sc2, nm2);
     if (MASK) {
       if (2 * i >= valid) d.x = -1e30f;
@@ -111,7 +115,10 @@ __device__ __forceinline__ void probs_row(const uint32_t (&sr)[N], uint32_t (&pk
   }
   l += (la[0].x + la[0].y) + (la[1].x + la[1].y);
   if (ENT) h += (ha[0].x + ha[0].y) + (ha[1].x + ha[1].y);
+  return MAXO ? fmaxf(fmaxf(mr[0], mr[1]), fmaxf(mr[2], mr[3])) * sc : -1e30f;
 }
+
+
 
 template <typename T, int XA, bool VK, int NSLOT, bool ENT>
 __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
@@ -419,6 +426,14 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 // exactly (O = a_0 O_0 + a_1 O_1, l and h likewise, a_w = 2^(m_w - m)). The streams never wait for
 // each other, so one warpgroup's exponentials (MUFU-bound) overlap the other's TMEM loads and maxima.
 // TMEM: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
+// A tile's P goes out in two 64-key halves: BAR_PHALF after the first lets the MMA warp issue
+// P V for those keys while the softmax works on the second (the chain softmax -> own P V -> next S
+// bounds each stream's cycle). Full tiles after a stream's first skip the separate max pass: the
+// exponentials run against the current reference m_ref with each half's max taken beside them,
+// and a half whose max passes m_ref + threshold is redone from its scores (still in registers)
+// after the rescale; a redo in the second half first waits for BAR_PVH, the commit behind the
+// first half's P V, which adds into O. The stream's first tile and a ragged last tile take the
+// max first.
 // One tcgen05.commit per tile (S -> SFULL): S[j+2] is issued after P V[j] into the same buffers and
 // the tensor pipe executes one thread's MMAs in order, so S[j+2] complete implies P V[j] complete.
 // So a rescale of O_w at tile j needs no wait beyond S[j], and the stream that observes S[j] frees
@@ -452,7 +467,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, 128, false, true);
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[6 + 2 * (NK + NVS)];
+  __shared__ __align__(8) uint64_t bars[10 + 2 * (NK + NVS)];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -478,6 +493,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   auto BAR_SFULL = [&](int b) { return bar0 + 8u * (1 + 2 * (NK + NVS) + b); };
   auto BAR_PFULL = [&](int b) { return bar0 + 8u * (3 + 2 * (NK + NVS) + b); };
   const uint32_t BAR_DONE = bar0 + 8u * (5 + 2 * (NK + NVS));
+  auto BAR_PHALF = [&](int b) { return bar0 + 8u * (6 + 2 * (NK + NVS) + b); };  // P of keys [0, 64) in TMEM
+  auto BAR_PVH = [&](int b) { return bar0 + 8u * (8 + 2 * (NK + NVS) + b); };    // that half of P V complete
   volatile int* abort = &abort_sh;
 
   if (threadIdx.x == 0) {
@@ -494,6 +511,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SFULL(b), 1);
       mbar_init(BAR_PFULL(b), 128);
+      mbar_init(BAR_PHALF(b), 128);
+      mbar_init(BAR_PVH(b), 1);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -571,20 +590,27 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     };
     if (ok) ok = issue_s(0);
     if (ok && NS == 2 && n_kt > 1) ok = issue_s(1);
+    // P V in two 64-key halves: the first is issued once the softmax has stored P of keys [0, 64)
+    // (BAR_PHALF), so it runs while the softmax computes the second half
     for (int j = 0; ok && j < n_kt; ++j) {
-      if (!wwait(BAR_PFULL(j % NS), (j / NS) & 1, 4)) break;
+      const uint32_t vb = VK ? sK + (j % NK) * 2 * kAtom : sV + (j % NVS) * 2 * kAtom;
+      const uint32_t a_tm = tmem + (uint32_t)((j % NS) * 128);
+      const uint32_t o_tm = tmem + NS * 128 + (uint32_t)((j % NS) * 128);
+      const int ksteps = p.n_kv - (kt0 + j) * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
+      if (!wwait(BAR_PHALF(j % NS), (j / NS) & 1, 4)) break;
       if (!VK && !wwait(BAR_VFULL(j % NVS), (j / NVS) & 1, 4)) break;
       tc_fence_after();
-      {
-        const uint32_t vb = VK ? sK + (j % NK) * 2 * kAtom : sV + (j % NVS) * 2 * kAtom;
-        const uint32_t a_tm = tmem + (uint32_t)((j % NS) * 128);
-        const uint32_t o_tm = tmem + NS * 128 + (uint32_t)((j % NS) * 128);
-        const int ksteps = p.n_kv - (kt0 + j) * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
-                    IDESC_PV, (j >= NS || kk > 0) ? 1u : 0u);
-      }
+      for (int kk = 0; kk < 4; ++kk)
+        mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
+                  IDESC_PV, (j >= NS || kk > 0) ? 1u : 0u);
+      mma_commit_if(leader, BAR_PVH(j % NS));  // a softmax that rescales O mid-tile waits for it
+      if (!wwait(BAR_PFULL(j % NS), (j / NS) & 1, 4)) break;
+      tc_fence_after();
+#pragma unroll
+      for (int kk = 4; kk < 8; ++kk)
+        mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
+                  IDESC_PV, 1u);
       if (j + NS < n_kt) ok = issue_s(j + NS);
     }
     // DONE: every MMA complete (the epilogue reads O; TMEM may be freed)
@@ -617,20 +643,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           if (j >= NS) mbar_arrive(BAR_VEMPTY((j - NS) % NVS));
         }
       }
-      uint32_t sr[128];
-      tmem_ld32(tS + 0, sr);
-      tmem_ld32(tS + 32, sr + 32);
-      tmem_ld32(tS + 64, sr + 64);
-      tmem_ld32(tS + 96, sr + 96);
-      tmem_wait_ld();
       const int valid = p.n_kv - (kt0 + j) * 128;  // same for every thread: the branches below are uniform
-      const float mx =
-          (valid < 128 ? row_max_raw<128, true>(sr, valid) : row_max_raw<128, false>(sr, 128)) * p.scale_log2;
-      if (j == w) {
-        m_ref = mx;
-      } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-        // Warp-uniform decision (warp-collective TMEM access): lanes whose max grew adopt it. Every
-        // earlier P V into O_w has completed (S[j] complete, see above).
+      // O, l, h to the reference max(m_ref, mx). Warp-uniform (warp-collective TMEM access): lanes
+      // whose max grew adopt it. The caller guarantees no P V into O_w is in flight.
+      auto rescale = [&](float mx) {
         const float m_new = fmaxf(m_ref, mx);
         const float alpha = fast_exp2(m_ref - m_new);
         const uint32_t tO = tmem + lane_off + NS * 128 + (uint32_t)(w * 128);
@@ -647,26 +663,93 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         if (ENT) h = alpha * fmaf(m_ref - m_new, l, h);
         l *= alpha;
         m_ref = m_new;
-      }
-      // P in two 64-key halves: keys [64 k, 64 k + 64) -> columns [32 k, 32 k + 32). The second half
-      // of S is loaded again from TMEM (its columns are only overwritten by the second half of P),
-      // so the scores of the first half are the only ones live through the exponentials.
-      {
-        const uint32_t(&sh)[64] = *reinterpret_cast<const uint32_t(*)[64]>(&sr[0]);
-        uint32_t pk[32];
-        if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid, l, h);
-        else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
-        tmem_st32(tS + 0, pk);
-      }
-      {
-        uint32_t sh[64];
-        tmem_ld32(tS + 64, sh);
-        tmem_ld32(tS + 96, sh + 32);
+      };
+      // P in two 64-key halves: keys [64 k, 64 k + 64) -> columns [32 k, 32 k + 32); BAR_PHALF
+      // after the first lets P V of those keys start.
+      if (j != w && valid >= 128) {
+        // A full tile after the stream's first: the exponentials go against the current reference
+        // while the half's max is taken beside them; a half whose max passes the reference by
+        // more than the threshold (rare: the reference only grows) is redone after the rescale,
+        // from the scores still in registers.
+        {
+          uint32_t sa[64];
+          tmem_ld32(tS + 0, sa);
+          tmem_ld32(tS + 32, sa + 32);
+          tmem_wait_ld();
+          uint32_t pk[32];
+          float lt = 0.f, ht = 0.f;
+          const float mx = probs_row<T, 64, ENT, false, true>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
+          if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+            // every earlier P V into O_w has completed (S[j] complete); P V(j) is not issued yet
+            rescale(mx);
+            lt = 0.f;
+            ht = 0.f;
+            probs_row<T, 64, ENT, false>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
+          }
+          l += lt;
+          h += ht;
+          tmem_st32(tS + 0, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(BAR_PHALF(w));
+        }
+        {
+          uint32_t sb[64];
+          tmem_ld32(tS + 64, sb);
+          tmem_ld32(tS + 96, sb + 32);
+          tmem_wait_ld();
+          uint32_t pk[32];
+          float lt = 0.f, ht = 0.f;
+          const float mx = probs_row<T, 64, ENT, false, true>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
+          if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+            // the first half of P V(j) may still be adding into O_w: wait for its commit
+            if (!warp_wait(BAR_PVH(w), (j / NS) & 1, 16)) { ok = false; break; }
+            tc_fence_after();
+            rescale(mx);
+            lt = 0.f;
+            ht = 0.f;
+            probs_row<T, 64, ENT, false>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
+          }
+          l += lt;
+          h += ht;
+          tmem_st32(tS + 32, pk);
+        }
+      } else {
+        // the stream's first tile (sets the reference) and the ragged last tile: the tile max first
+        uint32_t sr[128];
+        tmem_ld32(tS + 0, sr);
+        tmem_ld32(tS + 32, sr + 32);
+        tmem_ld32(tS + 64, sr + 64);
+        tmem_ld32(tS + 96, sr + 96);
         tmem_wait_ld();
-        uint32_t pk[32];
-        if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
-        else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
-        tmem_st32(tS + 32, pk);
+        const float mx =
+            (valid < 128 ? row_max_raw<128, true>(sr, valid) : row_max_raw<128, false>(sr, 128)) * p.scale_log2;
+        if (j == w) {
+          m_ref = mx;
+        } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+          rescale(mx);  // every earlier P V into O_w has completed (S[j] complete, see above)
+        }
+        {  // the second half of S is loaded again from TMEM (its columns are only overwritten by the
+           // second half of P), so the first half's scores are the only ones live through the exponentials
+          const uint32_t(&sh)[64] = *reinterpret_cast<const uint32_t(*)[64]>(&sr[0]);
+          uint32_t pk[32];
+          if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid, l, h);
+          else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          tmem_st32(tS + 0, pk);
+          tmem_wait_st();
+          tc_fence_before();
+          mbar_arrive(BAR_PHALF(w));
+        }
+        {
+          uint32_t sh[64];
+          tmem_ld32(tS + 64, sh);
+          tmem_ld32(tS + 96, sh + 32);
+          tmem_wait_ld();
+          uint32_t pk[32];
+          if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
+          else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          tmem_st32(tS + 32, pk);
+        }
       }
       tmem_wait_st();
       tc_fence_before();
