@@ -269,11 +269,13 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
   } else {
     // ------------------------------------------------------------------ softmax + epilogue
     // Two warpgroups split every 128-key tile by columns: warpgroup wg owns keys [64 wg, 64 wg + 64)
-    // of each row and O columns [wg NV/2, (wg + 1) NV/2). They exchange the half-row maxima once
-    // per tile through TMEM (named barrier 1), so both hold the same m_ref and take identical
-    // rescale decisions; l and h are per-warpgroup partial sums, added in the epilogue. Every named
-    // barrier is reached by all 256 threads and ANDs their status, so a failed wait in one
-    // warpgroup ends both at the same point.
+    // of each row and O columns [wg NV/2, (wg + 1) NV/2). Both hold the same m_ref and take
+    // identical rescale decisions: on full tiles after the first, the exponentials run against
+    // m_ref and one OR barrier (named barrier 1) confirms that no row's max passed it; otherwise
+    // they exchange the half-row maxima through TMEM (named barrier 1 again) and compute P against
+    // the agreed reference. l and h are per-warpgroup partial sums, added in the epilogue. Every
+    // named barrier is reached by all 256 threads and reduces their status, so a failed wait in
+    // one warpgroup ends both at the same point.
     // Exchange columns of the S buffer: warpgroup 0 writes its maximum into column 32 (its own half,
     // already loaded; overwritten only by warpgroup 1's P after warpgroup 1 has read it), warpgroup
     // 1 into column 64 (its own half; nothing writes it before the next S MMA into this buffer,
@@ -312,52 +314,76 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       const uint32_t tS = tmem + lane_off + (uint32_t)((j & 1) * 128);
       uint32_t sr[64];
       const int valid = p.n_kv - j * 128 - wg * 64;  // keys of this half; uniform per warpgroup
-      float mh = -1e30f;
       if (good) {
         tmem_ld32(tS + wg * 64, sr);
         tmem_ld32(tS + wg * 64 + 32, sr + 32);
         tmem_wait_ld();
-        mh = valid < 64 ? row_max_raw<64, true>(sr, valid) : row_max_raw<64, false>(sr, 64);
-      }
-      if (good) {
-        tmem_st1(tS + (wg ? 64 : 32), __float_as_uint(mh));
-        tmem_wait_st();
-      }
-      tc_fence_before();
-      // both halves of S are in registers past this barrier, so P may overwrite S columns [0, 64)
-      if (!named_bar_and(1, 256, good)) { ok = false; break; }
-      tc_fence_after();
-      const float mo = __uint_as_float(tmem_ld1(tS + (wg ? 32 : 64)));
-      tmem_wait_ld();
-      const float mx = fmaxf(mh, mo) * p.scale_log2;
-      if (j == 0) {
-        m_ref = mx;
-      } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-        // The rescale touches TMEM with warp-collective loads / stores and waits on a barrier, so
-        // the decision is taken per warp: every lane whose max grew adopts it (alpha < 1), the
-        // others keep their reference (alpha = 1). The twin warp of the other warpgroup sees the
-        // same maxima and takes the same decision.
-        if (!wait_pv(j - 1)) ok = false;  // reported to the other warpgroup at the next barrier
-        tc_fence_after();
-        const float m_new = fmaxf(m_ref, mx);
-        const float alpha = fast_exp2(m_ref - m_new);
-#pragma unroll 1
-        for (int c = wg * OCH; c < (wg + 1) * OCH; ++c) {
-          uint32_t o[32];
-          tmem_ld32(tO + c * 32, o);
-          tmem_wait_ld();
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
-          tmem_st32(tO + c * 32, o);
-        }
-        tmem_wait_st();
-        if (ENT) h = alpha * fmaf(m_ref - m_new, l, h);
-        l *= alpha;
-        m_ref = m_new;
       }
       uint32_t pk[32];
-      if (valid < 64) probs_row<T, 64, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, l, h);
-      else probs_row<T, 64, ENT, false>(sr, pk, p.scale_log2, m_ref, 64, l, h);
+      float lt = 0.f, ht = 0.f;
+      // A full tile after the first: the exponentials against the current reference with the
+      // half's max beside them. One barrier tells both warpgroups whether any row's max passed the
+      // reference by more than the threshold (or a wait failed); it also orders both halves' S
+      // loads before the P stores over S columns [0, 64). Otherwise (first tile, ragged tile, or
+      // a row past the threshold) the half-row maxima are exchanged as below and P is computed
+      // (again) against the agreed reference.
+      bool redo = true;
+      const bool fast = j > 0 && p.n_kv - j * 128 >= 128;  // the same branch in both warpgroups (one barrier)
+      if (fast) {
+        float mh = -1e30f;
+        if (good) mh = probs_row<T, 64, ENT, false, true>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+        redo = named_bar_or(1, 256, !good || mh > m_ref + kRescaleThreshold);
+      }
+      if (redo) {
+        float mh = -1e30f;
+        if (good) mh = valid < 64 ? row_max_raw<64, true>(sr, valid) : row_max_raw<64, false>(sr, 64);
+        if (good) {
+          tmem_st1(tS + (wg ? 64 : 32), __float_as_uint(mh));
+          tmem_wait_st();
+        }
+        tc_fence_before();
+        // both halves of S are in registers past this barrier, so P may overwrite S columns [0, 64)
+        if (!named_bar_and(1, 256, good)) { ok = false; break; }
+        tc_fence_after();
+        const float mo = __uint_as_float(tmem_ld1(tS + (wg ? 32 : 64)));
+        tmem_wait_ld();
+        const float mx = fmaxf(mh, mo) * p.scale_log2;
+        bool fresh = !fast;  // P not yet computed against the reference
+        if (j == 0) {
+          m_ref = mx;
+        } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+          // The rescale touches TMEM with warp-collective loads / stores and waits on a barrier, so
+          // the decision is taken per warp: every lane whose max grew adopts it (alpha < 1), the
+          // others keep their reference (alpha = 1). The twin warp of the other warpgroup sees the
+          // same maxima and takes the same decision.
+          if (!wait_pv(j - 1)) ok = false;  // reported to the other warpgroup at the next barrier
+          tc_fence_after();
+          const float m_new = fmaxf(m_ref, mx);
+          const float alpha = fast_exp2(m_ref - m_new);
+#pragma unroll 1
+          for (int c = wg * OCH; c < (wg + 1) * OCH; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_wait_ld();
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[i] = __float_as_uint(__uint_as_float(o[i]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+          tmem_wait_st();
+          if (ENT) h = alpha * fmaf(m_ref - m_new, l, h);
+          l *= alpha;
+          m_ref = m_new;
+          fresh = true;
+        }
+        if (fresh) {
+          lt = 0.f;
+          ht = 0.f;
+          if (valid < 64) probs_row<T, 64, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, lt, ht);
+          else probs_row<T, 64, ENT, false>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+        }
+      }
+      l += lt;
+      h += ht;
       tmem_st32(tS + wg * 32, pk);
       tmem_wait_st();
       tc_fence_before();

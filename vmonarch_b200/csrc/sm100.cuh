@@ -263,6 +263,16 @@ __device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
 }
 // Named barrier that also ANDs a predicate over the participating threads: groups that must stop
 // together (a failed wait in one of them) learn it at the barrier they all reach anyway.
+// Named barrier that returns whether `pred` held in any of the nthreads threads.
+__device__ __forceinline__ bool named_bar_or(int id, int nthreads, bool pred) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\tbar.red.or.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)pred), "r"(id), "r"(nthreads)
+      : "memory");
+  return r != 0;
+}
 __device__ __forceinline__ bool named_bar_and(int id, int nthreads, bool pred) {
   uint32_t r;
   asm volatile(
