@@ -98,9 +98,13 @@ def test_fea_bwd_workspace_and_validation():
     assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280 + ((rows * 64 * 4 + 255) // 256) * 256
     a.grad_mode = 1
     assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280
-    # D = 128 runs on the tcgen05 kernels: three folded statistics planes of 3 x round_up(100, 128) rows
+    # D = 128 runs on the tcgen05 kernels: three folded statistics planes of 3 x round_up(100, 128)
+    # rows; the preferred size adds the dS^T buffer (2 bytes x round_up(100, 128) keys x
+    # round_up(100, 64) queries per sequence, on a 256-byte boundary), the minimum does not
     a.d, a.dv, a.dv1 = 128, 128, 128
-    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 3 * ((3 * 128 * 4 + 255) // 256) * 256
+    planes = 3 * ((3 * 128 * 4 + 255) // 256) * 256
+    assert N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a)) == planes
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == planes + 3 * 128 * 128 * 2 + 256
     a.d, a.dv, a.dv1 = 64, 64, 64
     a.q = a.k = a.v = a.o = a.dout = a.lse = a.grad_q = a.grad_k = a.grad_v = 256
     a.dtype = 0

@@ -1293,13 +1293,16 @@ bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) 
 }
 
 bool fea_bwd_ds_gemm(int64_t batch, int n_q, int n_kv, int dv, bool vk, int acc_q) {
-  // The last VMonarch R step (short sequences): with a 256-wide dP, recomputing S and dP in a dq
-  // kernel costs more tensor work (and energy under the power cap) than one HBM round trip of dS.
-  // With dv = 128 (the recompute's shape class) the dq kernel is cheaper: storing dS^T slowed the
-  // dK/dV kernel as much as the GEMM saved (measured), so those calls keep it.
+  // One HBM round trip of dS^T (stored by the dK/dV kernel, read by dq_from_ds) instead of a dq
+  // kernel that recomputes S and dP. Taken for the last VMonarch R step (V aliasing K with a
+  // 256-wide dP, short sequences) and for separate-V calls with few queries (the exact recompute:
+  // n_q = r rows against the whole sequence), where the dq kernel's recomputation outweighs the
+  // dS^T bytes (measured: last R-step backward 4.57 -> 4.10 ms, recompute backward 3.63 -> 3.28
+  // ms). The first R step (V aliasing K, dv = 128) fuses dQ into the dK/dV kernel instead.
   (void)batch;
   (void)acc_q;  // every write mode, the finalize mode included
-  return vk && dv == 256 && (n_kv + 127) / 128 <= 32 && n_q <= 4096;
+  if (vk) return dv == 256 && (n_kv + 127) / 128 <= 32 && n_q <= 4096;
+  return dv == 128 && n_q <= 4096;
 }
 
 int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv) {
