@@ -58,7 +58,8 @@ int scratch_address(void** out) {
 
 extern "C" int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream) {
   if (!a) return vmb::set_error(VMB_EINVAL, "vmb_fea_bwd_noalloc: null args");
-  const int64_t need = vmb::fea_bwd_min_workspace_bytes(a);  // optional extras (dS^T) are skipped
+  // the minimum; a call whose optional dS^T buffer also fits the scratch takes that route
+  const int64_t need = vmb::fea_bwd_min_workspace_bytes(a);
   if (need < 0) return vmb::set_error(VMB_EINVAL, "vmb_fea_bwd_noalloc: bad sizes");
   if (need > kNoAllocScratchBytes)
     return vmb::set_error(VMB_EINVAL,
