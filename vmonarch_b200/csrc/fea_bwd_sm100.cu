@@ -206,6 +206,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   using C = DkdvCfg<XA, VK, NQS, FQ>;
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_SP = idesc_f16(kBf16, 128, 64, false, false);   // S^T, dP^T
+  constexpr uint32_t IDESC_SPK = idesc_f16(kBf16, 128, 128, false, false);  // [S^T | dP^T] = K [Q | dO_K]^T (V aliasing K)
   constexpr uint32_t IDESC_ACC = idesc_f16(kBf16, 128, 128, false, true);  // dK, dV (B MN-major)
   constexpr uint32_t IDESC_DQ = idesc_f16(kBf16, 128, 64, true, true);     // dQ^T = K^T dS^T (both MN-major)
   constexpr uint32_t IDESC_SP32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 queries
@@ -250,8 +251,15 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   auto BAR_DQFREE = [&](int b) { return bar0 + 8u * (6 + 2 * NQS + b); };
   const uint32_t BAR_FIN = bar0 + 8u * (8 + 2 * NQS);  // acc 3: the fp32 accumulator tiles landed
   volatile int* abort = &abort_sh;
-  auto slot_q = [&](int s) { return sSlots + s * C::SLOT; };
-  auto slot_do = [&](int s) { return sSlots + s * C::SLOT + 2 * kAtom64; };
+  // Query slot: 64-query tiles of Q (2 atoms of 64 columns) and dO (DW / 64 atoms). With V aliasing
+  // K the first two dO atoms interleave with Q's (Q0 dO0 Q1 dO1 [dO2 dO3]), so that Q atom a and
+  // dO atom a form one 128-row K-major operand: S^T and the K part of dP^T are then one N = 128
+  // MMA group, [S^T | dP^T] = K [Q | dO_K]^T, which reads the resident K once for both.
+  auto q_atom = [&](int s, int a) -> uint32_t { return sSlots + s * C::SLOT + (VK ? 2 * a : a) * kAtom64; };
+  auto do_atom = [&](int s, int a) -> uint32_t {
+    return sSlots + s * C::SLOT + (VK ? (a < 2 ? 2 * a + 1 : a + 2) : 2 + a) * kAtom64;
+  };
+  constexpr uint32_t kQLbo = VK ? 2 * kAtom64 : kAtom64;  // distance between Q's (and dO_K's) two atoms
   auto slot_stats = [&](int s) { return sSlots + s * C::SLOT + C::SLOT_T; };  // shared address
 
   if (threadIdx.x == 0) {
@@ -300,9 +308,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       if (lane == 0) {
         const int q0 = qtile(i) * 64;
         mbar_expect_tx(BAR_QFULL(s), C::SLOT_T + 3 * 256);
-        tma_load_3d(slot_q(s), &p.tm_c, 0, q0, bi, BAR_QFULL(s));
-        tma_load_3d(slot_q(s) + kAtom64, &p.tm_c, 64, q0, bi, BAR_QFULL(s));
-        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(slot_do(s) + a * kAtom64, &p.tm_d, 64 * a, q0, bi, BAR_QFULL(s));
+        tma_load_3d(q_atom(s, 0), &p.tm_c, 0, q0, bi, BAR_QFULL(s));
+        tma_load_3d(q_atom(s, 1), &p.tm_c, 64, q0, bi, BAR_QFULL(s));
+        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(do_atom(s, a), &p.tm_d, 64 * a, q0, bi, BAR_QFULL(s));
         // the 64 queries' folded statistics: one 256-byte copy per plane (rows padded to 128)
         const int64_t r0 = (int64_t)bi * p.n_pad + q0;
         bulk_load(slot_stats(s), p.nl + r0, 256, BAR_QFULL(s));
@@ -347,18 +355,31 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         tc_fence_after();
         {
           const uint32_t tb = tmem + 128 * (i & 1);
+          int kd0 = 0;  // first step of dP^T = W dO^T still to issue (16 columns of W per step)
+          if (VK && !qtail(i)) {
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {  // [S^T | dP^T] = K [Q | dO_K]^T over D: columns [0, 128) of the buffer
+              const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32;
+              mma_ss_if(leader, tb, smem_desc_sw128(sRes + offa, 16, 1024),
+                        smem_desc_sw128(q_atom(s, kk >> 2) + (kk & 3) * 32, 16, 1024), IDESC_SPK, kk > 0);
+            }
+            kd0 = 8;
+          } else {
+            const uint32_t idesc = qtail(i) ? IDESC_SP32 : IDESC_SP;
+#pragma unroll
+            for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
+              const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32;
+              mma_ss_if(leader, tb, smem_desc_sw128(sRes + offa, 16, 1024),
+                        smem_desc_sw128(q_atom(s, kk >> 2) + (kk & 3) * 32, 16, 1024), idesc, kk > 0);
+            }
+          }
           const uint32_t idesc = qtail(i) ? IDESC_SP32 : IDESC_SP;
 #pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {  // S^T = K Q^T over D
-            const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-            mma_ss_if(leader, tb, smem_desc_sw128(sRes + offa, 16, 1024), smem_desc_sw128(slot_q(s) + offb, 16, 1024), idesc,
-                   kk > 0);
-          }
-#pragma unroll
-          for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T = W dO^T over DW
-            const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32, offb = (kk >> 2) * kAtom64 + (kk & 3) * 32;
-            mma_ss_if(leader, tb + 64, smem_desc_sw128(sW + offa, 16, 1024), smem_desc_sw128(slot_do(s) + offb, 16, 1024),
-                   idesc, kk > 0);
+          for (int kk = 0; kk < C::DW / 16; ++kk) {  // dP^T (+)= W dO^T over the rest of DW
+            if (kk < kd0) continue;
+            const uint32_t offa = (kk >> 2) * kAtom128 + (kk & 3) * 32;
+            mma_ss_if(leader, tb + 64, smem_desc_sw128(sW + offa, 16, 1024),
+                      smem_desc_sw128(do_atom(s, kk >> 2) + (kk & 3) * 32, 16, 1024), idesc, kk > 0 ? 1u : 0u);
           }
           mma_commit_if(leader, BAR_SPFULL(i & 1));
         }
@@ -377,19 +398,19 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
 #pragma unroll
           for (int kk = 0; kk < 4; ++kk)  // dK += dS^T Q   (K = 64 queries)
             mma_ts_if(leader & ((qmask >> kk) & 1u), tmem + 256, dst + pcol(kk),
-                      smem_desc_sw128(slot_q(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
+                      smem_desc_sw128(q_atom(s, 0) + kk * 2048, kQLbo, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
           if (VK) {
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dK += P^T dO[:, :128]  (value gradient of the K columns)
               mma_ts_if(leader & ((qmask >> kk) & 1u), tmem + 256, pt + pcol(kk),
-                        smem_desc_sw128(slot_do(s) + kk * 2048, kAtom64, 1024), IDESC_ACC, 1u);
+                        smem_desc_sw128(do_atom(s, 0) + kk * 2048, kQLbo, 1024), IDESC_ACC, 1u);
           }
           if (C::HAS_DV) {
-            const uint32_t vo = VK ? 2 * kAtom64 : 0;
+            const uint32_t vb = do_atom(s, VK ? 2 : 0);  // the value columns of dO (contiguous atoms)
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // dV += P^T dO[:, cols]
               mma_ts_if(leader & ((qmask >> kk) & 1u), tmem + 384, pt + pcol(kk),
-                        smem_desc_sw128(slot_do(s) + vo + kk * 2048, kAtom64, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
+                        smem_desc_sw128(vb + kk * 2048, kAtom64, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit_if(leader, BAR_QEMPTY(s));
           if (FQ) {
