@@ -99,12 +99,19 @@ def test_fea_bwd_workspace_and_validation():
     a.grad_mode = 1
     assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280
     # D = 128 runs on the tcgen05 kernels: three folded statistics planes of 3 x round_up(100, 128)
-    # rows; the preferred size adds the dS^T buffer (2 bytes x round_up(100, 128) keys x
-    # round_up(100, 64) queries per sequence, on a 256-byte boundary), the minimum does not
+    # rows. Three query tiles cannot fill the GPU, so the dS^T route is not taken: no dS^T buffer.
     a.d, a.dv, a.dv1 = 128, 128, 128
     planes = 3 * ((3 * 128 * 4 + 255) // 256) * 256
     assert N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a)) == planes
-    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == planes + 3 * 128 * 128 * 2 + 256
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == planes
+    # 400 sequences (400 query tiles, two or more per SM): the preferred size adds the dS^T buffer
+    # (2 bytes x round_up(100, 128) keys x round_up(100, 64) queries per sequence, on a 256-byte
+    # boundary); the minimum does not
+    a.batch = 400
+    planes = 3 * ((400 * 128 * 4 + 255) // 256) * 256
+    assert N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a)) == planes
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == planes + 400 * 128 * 128 * 2 + 256
+    a.batch = 3
     a.d, a.dv, a.dv1 = 64, 64, 64
     a.q = a.k = a.v = a.o = a.dout = a.lse = a.grad_q = a.grad_k = a.grad_v = 256
     a.dtype = 0

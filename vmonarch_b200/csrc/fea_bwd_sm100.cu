@@ -1316,14 +1316,19 @@ bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) 
 bool fea_bwd_ds_gemm(int64_t batch, int n_q, int n_kv, int dv, bool vk, int acc_q) {
   // One HBM round trip of dS^T (stored by the dK/dV kernel, read by dq_from_ds) instead of a dq
   // kernel that recomputes S and dP. Taken for the last VMonarch R step (V aliasing K with a
-  // 256-wide dP, short sequences) and for separate-V calls with few queries (the exact recompute:
-  // n_q = r rows against the whole sequence), where the dq kernel's recomputation outweighs the
+  // 256-wide dP, short sequences) and for separate-V calls with few queries per sequence (the exact
+  // recompute: n_q = r rows against the whole sequence), where the dq kernel's recomputation outweighs the
   // dS^T bytes (measured: last R-step backward 4.57 -> 4.10 ms, recompute backward 3.63 -> 3.28
   // ms). The first R step (V aliasing K, dv = 128) fuses dQ into the dK/dV kernel instead.
-  (void)batch;
+  // Separate V also needs enough query tiles to fill the GPU (two GEMM CTAs per SM): with few
+  // sequences (strong scaling, small batches) the dq kernel's key-range split balances better.
   (void)acc_q;  // every write mode, the finalize mode included
   if (vk) return dv == 256 && (n_kv + 127) / 128 <= 32 && n_q <= 4096;
-  return dv == 128 && n_q <= 4096;
+  if (dv != 128 || n_q > 4096) return false;
+  int sms = 148, dev = 0;
+  if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  if (sms <= 0) sms = 148;
+  return batch * ((n_q + 127) / 128) >= 2 * (int64_t)sms;
 }
 
 int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv) {
