@@ -129,7 +129,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
   constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, C::NV, false, true);
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[6 + 3 * NSLOT];
+  __shared__ __align__(8) uint64_t bars[8 + 3 * NSLOT];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -149,6 +149,9 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
   auto BAR_SFULL = [&](int b) { return bar0 + 8u * (1 + 3 * NSLOT + b); };
   auto BAR_PFULL = [&](int b) { return bar0 + 8u * (3 + 3 * NSLOT + b); };
   const uint32_t BAR_DONE = bar0 + 8u * (5 + 3 * NSLOT);
+  // P V(j) complete (commit behind it, alternating by tile parity): a rescale of O at tile j waits
+  // for P V(j - 1), the only one that can be in flight then, so no parity wait can be lapped
+  auto BAR_PVD = [&](int b) { return bar0 + 8u * (6 + 3 * NSLOT + b); };
   volatile int* abort = &abort_sh;
 
   if (threadIdx.x == 0) {
@@ -162,6 +165,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SFULL(b), 1);
       mbar_init(BAR_PFULL(b), 256);
+      mbar_init(BAR_PVD(b), 1);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -253,10 +257,11 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
         const int ksteps = p.n_kv - j * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)
-          mma_ts_if(leader & (kk < ksteps ? 1u : 0u), tmem + 256, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
-                    IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < 8; ++kk)  // P of keys [64 h, 64 h + 64) sits in columns [64 h, 64 h + 32)
+          mma_ts_if(leader & (kk < ksteps ? 1u : 0u), tmem + 256, a_tm + (kk >> 2) * 64 + (kk & 3) * 8,
+                    smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit_if(leader, BAR_EMPTY(s));
+        mma_commit_if(leader, BAR_PVD(j & 1));
       }
       if (j + 2 < n_kt) ok = issue_s(j + 2);
     }
@@ -276,10 +281,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     // the agreed reference. l and h are per-warpgroup partial sums, added in the epilogue. Every
     // named barrier is reached by all 256 threads and reduces their status, so a failed wait in
     // one warpgroup ends both at the same point.
-    // Exchange columns of the S buffer: warpgroup 0 writes its maximum into column 32 (its own half,
-    // already loaded; overwritten only by warpgroup 1's P after warpgroup 1 has read it), warpgroup
-    // 1 into column 64 (its own half; nothing writes it before the next S MMA into this buffer,
-    // which waits for both warpgroups' P).
+    // Each warpgroup writes its P (bf16) over the first 32 columns of its own half of S (columns
+    // [64 wg, 64 wg + 32), already loaded), so neither waits for the other before storing it; the
+    // maxima are exchanged through column 64 wg + 32 of its half (not written by any P; the next S
+    // MMA into this buffer waits for both warpgroups' P).
     const int wg = (warp - 2) >> 2;
     const int quad = warp & 3;  // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
@@ -287,30 +292,16 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     const uint32_t tO = tmem + lane_off + 256;
     constexpr int OCH = C::NV / 64;  // 32-column O chunks per warpgroup
     float m_ref = -1e30f, l = 0.f, h = 0.f;
-    int pv_waited = -1;
     bool ok = true;
 
     auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
       const bool mine = mbar_wait(bar, parity, abort, &g_fwd_err, code);
       return __all_sync(0xffffffffu, mine);
     };
-    // PV[t] is committed to EMPTY[t % NSLOT]. Waiting for every t in order keeps the wait at most
-    // one phase behind: PV[t + NSLOT] needs P[t + NSLOT], which is not written while this
-    // warpgroup waits for PV[t] (t <= j - 1 while it works on tile j).
-    auto wait_pv = [&](int t) -> bool {
-      while (pv_waited < t) {
-        const int u = pv_waited + 1;
-        if (!warp_wait(BAR_EMPTY(u % NSLOT), (u / NSLOT) & 1, 8)) return false;
-        pv_waited = u;
-      }
-      return true;
-    };
 
     for (int j = 0; j < n_kt; ++j) {
       bool good = ok && warp_wait(BAR_SFULL(j & 1), (j >> 1) & 1, 8);
       tc_fence_after();
-      // S[j] complete implies PV[j-2] complete: consume that phase to keep the bookkeeping exact
-      if (good && j >= 2) good = wait_pv(j - 2);
       const uint32_t tS = tmem + lane_off + (uint32_t)((j & 1) * 128);
       uint32_t sr[64];
       const int valid = p.n_kv - j * 128 - wg * 64;  // keys of this half; uniform per warpgroup
@@ -322,30 +313,31 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       uint32_t pk[32];
       float lt = 0.f, ht = 0.f;
       // A full tile after the first: the exponentials against the current reference with the
-      // half's max beside them. One barrier tells both warpgroups whether any row's max passed the
-      // reference by more than the threshold (or a wait failed); it also orders both halves' S
-      // loads before the P stores over S columns [0, 64). Otherwise (first tile, ragged tile, or
-      // a row past the threshold) the half-row maxima are exchanged as below and P is computed
-      // (again) against the agreed reference.
+      // half's max beside them, P stored at once. One barrier tells both warpgroups whether any
+      // row's max passed the reference by more than the threshold (or a wait failed). Otherwise
+      // (first tile, ragged tile, or a row past the threshold) the half-row maxima are exchanged
+      // as below and P is computed (again) against the agreed reference and stored.
       bool redo = true;
       const bool fast = j > 0 && p.n_kv - j * 128 >= 128;  // the same branch in both warpgroups (one barrier)
       if (fast) {
         float mh = -1e30f;
-        if (good) mh = probs_row<T, 64, ENT, false, true>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+        if (good) {
+          mh = probs_row<T, 64, ENT, false, true>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+          tmem_st32(tS + wg * 64, pk);  // this warpgroup's own half of S (already loaded)
+        }
         redo = named_bar_or(1, 256, !good || mh > m_ref + kRescaleThreshold);
       }
       if (redo) {
         float mh = -1e30f;
         if (good) mh = valid < 64 ? row_max_raw<64, true>(sr, valid) : row_max_raw<64, false>(sr, 64);
         if (good) {
-          tmem_st1(tS + (wg ? 64 : 32), __float_as_uint(mh));
+          tmem_st1(tS + 64 * wg + 32, __float_as_uint(mh));  // past this warpgroup's P columns
           tmem_wait_st();
         }
         tc_fence_before();
-        // both halves of S are in registers past this barrier, so P may overwrite S columns [0, 64)
         if (!named_bar_and(1, 256, good)) { ok = false; break; }
         tc_fence_after();
-        const float mo = __uint_as_float(tmem_ld1(tS + (wg ? 32 : 64)));
+        const float mo = __uint_as_float(tmem_ld1(tS + 64 * (wg ^ 1) + 32));
         tmem_wait_ld();
         const float mx = fmaxf(mh, mo) * p.scale_log2;
         bool fresh = !fast;  // P not yet computed against the reference
@@ -356,7 +348,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
           // the decision is taken per warp: every lane whose max grew adopts it (alpha < 1), the
           // others keep their reference (alpha = 1). The twin warp of the other warpgroup sees the
           // same maxima and takes the same decision.
-          if (!wait_pv(j - 1)) ok = false;  // reported to the other warpgroup at the next barrier
+          if (!warp_wait(BAR_PVD((j - 1) & 1), ((j - 1) >> 1) & 1, 8)) ok = false;  // reported at the next barrier
           tc_fence_after();
           const float m_new = fmaxf(m_ref, mx);
           const float alpha = fast_exp2(m_ref - m_new);
@@ -381,16 +373,16 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
           if (valid < 64) probs_row<T, 64, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, lt, ht);
           else probs_row<T, 64, ENT, false>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
         }
+        if (good) tmem_st32(tS + wg * 64, pk);
       }
       l += lt;
       h += ht;
-      tmem_st32(tS + wg * 32, pk);
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(BAR_PFULL(j & 1));
     }
 
-    if (ok) ok = wait_pv(n_kt - 1);
+    if (ok) ok = warp_wait(BAR_PVD((n_kt - 1) & 1), ((n_kt - 1) >> 1) & 1, 8);  // the last P V
     tc_fence_after();
     // epilogue: add the partial sums (exchanged through the Q tile, idle once the last P V - and
     // with it every S MMA - has completed), O / l -> bf16 in the (now idle) ring, TMA store; LSE
