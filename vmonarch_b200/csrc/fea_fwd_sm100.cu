@@ -482,10 +482,17 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   constexpr bool kBf16 = Elem<T>::is_bf16;
   constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
   constexpr uint32_t IDESC_S32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 keys
+  constexpr uint32_t IDESC_S64 = idesc_f16(kBf16, 128, 64, false, false);  // one 64-key half of S
   constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, 128, false, true);
+  // HS (the one-stream instance): S in two 64-key halves, S_A = keys [0, 64) -> columns [0, 64) and
+  // S_B = keys [64, 128) -> columns [64, 128), with P of each half over the first 32 columns of its
+  // own half. S_A(j + NS) is issued right behind P V of the first half of tile j and S_B(j + NS)
+  // behind the second, so the softmax finds each half of its next S ready instead of waiting for
+  // P V(j) and the whole of S(j + NS) after finishing tile j.
+  constexpr bool HS = NS == 1;
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[10 + 2 * (NK + NVS)];
+  __shared__ __align__(8) uint64_t bars[14 + 2 * (NK + NVS)];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -513,6 +520,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   const uint32_t BAR_DONE = bar0 + 8u * (5 + 2 * (NK + NVS));
   auto BAR_PHALF = [&](int b) { return bar0 + 8u * (6 + 2 * (NK + NVS) + b); };  // P of keys [0, 64) in TMEM
   auto BAR_PVH = [&](int b) { return bar0 + 8u * (8 + 2 * (NK + NVS) + b); };    // that half of P V complete
+  auto BAR_SA = [&](int b) { return bar0 + 8u * (10 + 2 * (NK + NVS) + b); };    // HS: S_A complete
+  auto BAR_PVB = [&](int b) { return bar0 + 8u * (12 + 2 * (NK + NVS) + b); };   // HS: P V of keys [64, 128) complete
   volatile int* abort = &abort_sh;
 
   if (threadIdx.x == 0) {
@@ -531,6 +540,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       mbar_init(BAR_PFULL(b), 128);
       mbar_init(BAR_PHALF(b), 128);
       mbar_init(BAR_PVH(b), 1);
+      mbar_init(BAR_SA(b), 1);
+      mbar_init(BAR_PVB(b), 1);
     }
     mbar_init(BAR_DONE, 1);
     fence_mbar_init();
@@ -606,8 +617,45 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       }
       return true;
     };
-    if (ok) ok = issue_s(0);
-    if (ok && NS == 2 && n_kt > 1) ok = issue_s(1);
+    // HS: the two halves of S(j); S_B is skipped when no key of the tile lies in [64, 128), and the
+    // K slot (and with separate V the V slot) is released by commits behind the last MMA reading it
+    auto issue_sa = [&](int j) -> bool {
+      const int s = j % NK;
+      if (!wwait(BAR_KFULL(s), (j / NK) & 1, 2)) return false;
+      tc_fence_after();
+      const uint32_t kb = sK + s * 2 * kAtom;
+      const uint32_t d = tmem + (uint32_t)((j % NS) * 128);
+      const uint32_t idesc = p.n_kv - (kt0 + j) * 128 <= 32 ? IDESC_S32 : IDESC_S64;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+        mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
+      }
+      mma_commit_if(leader, BAR_SA(j % NS));
+      return true;
+    };
+    auto issue_sb = [&](int j) {  // K(j) has landed (issue_sa)
+      const int s = j % NK;
+      const uint32_t kb = sK + s * 2 * kAtom + 64 * 128;  // key rows [64, 128)
+      const uint32_t d = tmem + (uint32_t)((j % NS) * 128) + 64;
+      const uint32_t on = p.n_kv - (kt0 + j) * 128 > 64 ? leader : 0u;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
+        mma_ss_if(on, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S64, kk > 0);
+      }
+      mma_commit_if(leader, BAR_SFULL(j % NS));
+      if (!VK) mma_commit_if(leader, BAR_KEMPTY(s));  // separate V: K(j) is read by S(j) only
+    };
+    if (HS) {
+      for (int j = 0; ok && j < NS && j < n_kt; ++j) {
+        ok = issue_sa(j);
+        if (ok) issue_sb(j);
+      }
+    } else {
+      if (ok) ok = issue_s(0);
+      if (ok && NS == 2 && n_kt > 1) ok = issue_s(1);
+    }
     // P V in two 64-key halves: the first is issued once the softmax has stored P of keys [0, 64)
     // (BAR_PHALF), so it runs while the softmax computes the second half
     for (int j = 0; ok && j < n_kt; ++j) {
@@ -623,13 +671,20 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
                   IDESC_PV, (j >= NS || kk > 0) ? 1u : 0u);
       mma_commit_if(leader, BAR_PVH(j % NS));  // a softmax that rescales O mid-tile waits for it
+      if (HS && j + NS < n_kt && !(ok = issue_sa(j + NS))) break;
       if (!wwait(BAR_PFULL(j % NS), (j / NS) & 1, 4)) break;
       tc_fence_after();
 #pragma unroll
-      for (int kk = 4; kk < 8; ++kk)
-        mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
-                  IDESC_PV, 1u);
-      if (j + NS < n_kt) ok = issue_s(j + NS);
+      for (int kk = 4; kk < 8; ++kk)  // HS: P of keys [64, 128) sits in columns [64, 96)
+        mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + (HS ? 64 + (kk - 4) * 8 : kk * 8),
+                  smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV, 1u);
+      if (HS) {
+        mma_commit_if(leader, BAR_PVB(j % NS));
+        mma_commit_if(leader, VK ? BAR_KEMPTY(j % NK) : BAR_VEMPTY(j % NVS));  // the slot P V(j) read
+        if (j + NS < n_kt) issue_sb(j + NS);
+      } else if (j + NS < n_kt) {
+        ok = issue_s(j + NS);
+      }
     }
     // DONE: every MMA complete (the epilogue reads O; TMEM may be freed)
     if (elect_one()) {
@@ -651,9 +706,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     };
 
     for (int j = w; j < n_kt; j += NS) {
-      if (!warp_wait(BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
+      // HS: S_A first (S_B is waited for before the second half); otherwise all of S
+      if (!warp_wait(HS ? BAR_SA(w) : BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
       tc_fence_after();
-      if (warp == 2 + 4 * w && lane == 0) {  // ring slots done with (see above)
+      if (!HS && warp == 2 + 4 * w && lane == 0) {  // ring slots done with (see above)
         if (VK) {
           if (j >= NS) mbar_arrive(BAR_KEMPTY((j - NS) % NK));
         } else {
@@ -698,7 +754,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           float lt = 0.f, ht = 0.f;
           const float mx = probs_row<T, 64, ENT, false, true>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
           if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-            // every earlier P V into O_w has completed (S[j] complete); P V(j) is not issued yet
+            // every earlier P V into O_w has completed (S[j] complete; HS: S_A(j) only follows the
+            // first half of P V(j - NS), so wait for the second); P V(j) is not issued yet
+            if (HS && !warp_wait(BAR_PVB(w), ((j / NS) - 1) & 1, 16)) { ok = false; break; }
+            tc_fence_after();
             rescale(mx);
             lt = 0.f;
             ht = 0.f;
@@ -710,6 +769,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(BAR_PHALF(w));
+        }
+        if (HS) {
+          if (!warp_wait(BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
+          tc_fence_after();
         }
         {
           uint32_t sb[64];
@@ -730,10 +793,14 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           }
           l += lt;
           h += ht;
-          tmem_st32(tS + 32, pk);
+          tmem_st32(tS + (HS ? 64 : 32), pk);
         }
       } else {
         // the stream's first tile (sets the reference) and the ragged last tile: the tile max first
+        if (HS) {
+          if (!warp_wait(BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
+          tc_fence_after();
+        }
         uint32_t sr[128];
         tmem_ld32(tS + 0, sr);
         tmem_ld32(tS + 32, sr + 32);
@@ -745,7 +812,11 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         if (j == w) {
           m_ref = mx;
         } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-          rescale(mx);  // every earlier P V into O_w has completed (S[j] complete, see above)
+          // every earlier P V into O_w has completed (S[j] complete, see above; HS: the second
+          // half of P V(j - NS) is waited for)
+          if (HS && !warp_wait(BAR_PVB(w), ((j / NS) - 1) & 1, 16)) { ok = false; break; }
+          tc_fence_after();
+          rescale(mx);
         }
         {  // the second half of S is loaded again from TMEM (its columns are only overwritten by the
            // second half of P), so the first half's scores are the only ones live through the exponentials
@@ -766,7 +837,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           uint32_t pk[32];
           if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
           else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
-          tmem_st32(tS + 32, pk);
+          tmem_st32(tS + (HS ? 64 : 32), pk);
         }
       }
       tmem_wait_st();
