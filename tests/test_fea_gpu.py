@@ -142,6 +142,39 @@ def test_row_max_jumps_inside_a_key_tile(Dv, steps):
     check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
 
 
+@pytest.mark.parametrize("steps", [(320, 704), (256, 960), (64, 448)])
+def test_values_aliasing_keys_with_row_max_jumps(steps):
+    # V passed as the same tensor as K with D = 128 and <= 2048 keys: the one-stream forward (S in
+    # 64-key halves, each issued behind P V of the previous tile's same half), whose rescale of O
+    # waits for the previous tile's second P V half (a jump in a tile's first half) or for this
+    # tile's first (a jump in the second half). Half the rows see the jumps (each ~12 in log2 units,
+    # past the threshold of 8), with steps small enough that the values (= keys) stay O(1) for the
+    # absolute output bound.
+    gen = torch.Generator().manual_seed(29)
+    N, D = 1152, 128
+    q = torch.randn(1, 2, N, D, generator=gen)
+    k = torch.randn(1, 2, N, D, generator=gen)
+    c = torch.randn(1, 2, 1, D, generator=gen)
+    q = (q + 1.5 * c * (torch.rand(1, 2, N, 1, generator=gen) > 0.5)).bfloat16().float()
+    for st in steps:
+        k[:, :, st:] += 0.5 * c
+    k = k.bfloat16().float()
+    do, de = torch.randn(1, 2, N, D, generator=gen), torch.randn(1, 2, N, generator=gen)
+
+    qc, kc = (t.cuda().bfloat16().requires_grad_() for t in (q, k))
+    o, e = flash_entropy_attention(qc, kc, kc)
+    gq, gk = torch.autograd.grad((o.float() * do.cuda()).sum() + (e * de.cuda()).sum(), (qc, kc))
+    torch.cuda.synchronize()
+    got = [t.detach().float().cpu() for t in (o, e, gq, gk)]
+
+    qr, kr = (t.float().clone().requires_grad_() for t in (q, k))
+    o_r, e_r = oracle.entropy_attention(qr, kr, kr, D ** -0.5)
+    gq_r, gk_r = torch.autograd.grad((o_r * do).sum() + (e_r * de).sum(), (qr, kr))
+    ref = [o_r.detach(), e_r.detach(), gq_r, gk_r]
+    # check() pairs gradients by position: (dq, dk) here, dk holding both the key and value roles
+    check(got, ref)
+
+
 def test_split_key_range_backward_matches_and_is_deterministic(monkeypatch):
     # Few query tiles over a long key range: in fp32-accumulate mode the dQ kernel splits the key
     # range over several CTAs (partial tiles summed in a fixed order). The workspace is held to the
