@@ -438,12 +438,13 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 }
 
 // ---------------------------------------------------------------------------------- Dv = 128
-// Two-stream forward for 128 output columns. The two softmax warpgroups own alternate KV tiles
-// (stream w = tiles j with j % 2 == w), each with its own TMEM S buffer, O accumulator and online
-// statistics (m_ref, l, h), like two split-KV partitions inside one CTA; the epilogue merges them
-// exactly (O = a_0 O_0 + a_1 O_1, l and h likewise, a_w = 2^(m_w - m)). The streams never wait for
-// each other, so one warpgroup's exponentials (MUFU-bound) overlap the other's TMEM loads and maxima.
-// TMEM: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512).
+// Two-stream forward for 128 output columns. CTA = two 128-row query tiles of one sequence; the two
+// softmax warpgroups are two independent streams, stream w owning query tile w, each with its own
+// TMEM S buffer, O accumulator and online statistics (m_ref, l, h), both walking the same key tiles:
+// every K / V tile is loaded once for two query tiles. The streams never wait for each other, so
+// one warpgroup's exponentials overlap the other's TMEM loads and the tensor work of its tile.
+// TMEM: S_0 [0,128), S_1 [128,256), O_0 [256,384), O_1 [384,512). The MMA warp walks steps
+// j = 2 t + w (stream w, key tile t).
 // A tile's P goes out in two 64-key halves: BAR_PHALF after the first lets the MMA warp issue
 // P V for those keys while the softmax works on the second (the chain softmax -> own P V -> next S
 // bounds each stream's cycle). Full tiles after a stream's first skip the separate max pass: the
@@ -452,22 +453,22 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 // after the rescale; a redo in the second half first waits for BAR_PVH, the commit behind the
 // first half's P V, which adds into O. The stream's first tile and a ragged last tile take the
 // max first.
-// One tcgen05.commit per tile (S -> SFULL): S[j+2] is issued after P V[j] into the same buffers and
-// the tensor pipe executes one thread's MMAs in order, so S[j+2] complete implies P V[j] complete.
-// So a rescale of O_w at tile j needs no wait beyond S[j], and the stream that observes S[j] frees
-// the ring slots that are done (one elected thread arrives on the slot's EMPTY barrier): the K slot
-// of tile j (K read by S[j] only) and the V slot of tile j - 2 (read by P V[j-2]); with V aliasing K
-// the K slot of tile j - 2. The producer waits on those per-slot barriers, whose next phase needs
-// a tile it has not loaded yet, so no parity wait can be lapped.
-// NS = 1 (V aliasing K, short sequences): one stream, S [0,128) and O [128,256), so two CTAs share
-// an SM (96 KB of shared memory, 256 TMEM columns each) and one CTA's Q load and epilogue overlap
-// the other's key loop; S(j+1) is issued behind P V(j).
+// One tcgen05.commit per step (S -> SFULL): S_w(t+1) is issued after P V_w(t) into the same buffers
+// and the tensor pipe executes one thread's MMAs in order, so S_w(t+1) complete implies P V_w(t)
+// complete. So a rescale of O_w at key tile t needs no wait beyond S_w(t), and each stream that
+// observes S_w(t) arrives on the EMPTY barriers (two arrivals each) of the ring slots it is done
+// with: the K slot of tile t (K read by the S MMAs only) and the V slot of tile t - 1 (read by
+// P V(t - 1)); with V aliasing K the K slot of tile t - 1. The producer waits on those per-slot
+// barriers, whose next phase needs a tile it has not loaded yet, so no parity wait can be lapped.
+// NS = 1 (V aliasing K, short sequences): one stream and one query tile, S [0,128) and O [128,256),
+// so two CTAs share an SM (96 KB of shared memory, 256 TMEM columns each) and one CTA's Q load and
+// epilogue overlap the other's key loop; S goes out in two halves (HS, below).
 template <bool VK, int NS = 2>
 struct Fwd2Cfg {
   static_assert(NS == 2 || (NS == 1 && VK), "one stream only with V aliasing K");
-  static constexpr int NK = NS == 1 ? 2 : (VK ? 6 : 3);  // K ring slots (V aliasing K: also the V operand)
-  static constexpr int NVS = VK ? 0 : 3;                 // V ring slots
-  static constexpr int Q_BYTES = 2 * kAtom;
+  static constexpr int NK = NS == 1 ? 2 : (VK ? 5 : 3);  // K ring slots (V aliasing K: also the V operand)
+  static constexpr int NVS = VK ? 0 : 2;                 // V ring slots
+  static constexpr int Q_BYTES = NS * 2 * kAtom;         // one 128-row query tile per stream
   static constexpr int SMEM = 1024 + Q_BYTES + (NK + NVS) * 2 * kAtom;
   static constexpr int THREADS = 64 + 128 * NS;
   static_assert(SMEM <= 232448 - 1024, "shared memory budget");
@@ -497,10 +498,12 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   __shared__ int abort_sh;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  // block -> (sequence, query tile, key chunk); with kv_split == 1 a CTA walks all key tiles
-  const int per_seq = p.n_qtiles * p.kv_split;
+  // block -> (sequence, NS query tiles, key chunk); with kv_split == 1 a CTA walks all key tiles.
+  // Stream w owns query tile rows [q0 + 128 w, q0 + 128 w + 128) (past n_q: zero-filled, clipped).
+  const int n_units = (p.n_qtiles + NS - 1) / NS;
+  const int per_seq = n_units * p.kv_split;
   const int bi = blockIdx.x / per_seq;
-  const int q0 = ((blockIdx.x % per_seq) / p.kv_split) * 128;
+  const int q0 = ((blockIdx.x % per_seq) / p.kv_split) * 128 * NS;
   const int kchunk = blockIdx.x % p.kv_split;
   const int kt0 = kchunk * p.kt_per;                                  // first key tile of the chunk
   const int n_kt = min((p.n_kv + 127) / 128 - kt0, p.kt_per);       // >= 1 by the host's choice
@@ -527,13 +530,14 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   if (threadIdx.x == 0) {
     abort_sh = 0;
     mbar_init(BAR_Q, 1);
+    // slot releases: one commit behind the last MMA reading the slot (HS), else one arrival per stream
     for (int s = 0; s < NK; ++s) {
       mbar_init(BAR_KFULL(s), 1);
-      mbar_init(BAR_KEMPTY(s), 1);
+      mbar_init(BAR_KEMPTY(s), HS ? 1 : NS);
     }
     for (int s = 0; s < NVS; ++s) {
       mbar_init(BAR_VFULL(s), 1);
-      mbar_init(BAR_VEMPTY(s), 1);
+      mbar_init(BAR_VEMPTY(s), HS ? 1 : NS);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(BAR_SFULL(b), 1);
@@ -565,8 +569,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         prefetch_tmap(&p.tm_q);
         prefetch_tmap(&p.tm_k);
         mbar_expect_tx(BAR_Q, C::Q_BYTES);
-        tma_load_3d(sQ, &p.tm_q, 0, q0, bi, BAR_Q);
-        tma_load_3d(sQ + kAtom, &p.tm_q, 64, q0, bi, BAR_Q);
+        for (int w = 0; w < NS; ++w) {
+          tma_load_3d(sQ + w * 2 * kAtom, &p.tm_q, 0, q0 + 128 * w, bi, BAR_Q);
+          tma_load_3d(sQ + w * 2 * kAtom + kAtom, &p.tm_q, 64, q0 + 128 * w, bi, BAR_Q);
+        }
       } else {
         prefetch_tmap(&p.tm_x);
       }
@@ -599,27 +605,28 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
     };
     bool ok = wwait(BAR_Q, 0, 2);
+    // Step j: stream w = j % NS (query tile w) with key tile t = j / NS.
     auto issue_s = [&](int j) -> bool {
-      const int s = j % NK;
-      if (!wwait(BAR_KFULL(s), (j / NK) & 1, 2)) return false;
+      const int w = j % NS, t = j / NS, s = t % NK;
+      if (!wwait(BAR_KFULL(s), (t / NK) & 1, 2)) return false;
       tc_fence_after();
       {
-        const uint32_t kb = sK + s * 2 * kAtom;
-        const uint32_t d = tmem + (uint32_t)((j % NS) * 128);
+        const uint32_t kb = sK + s * 2 * kAtom, qb = sQ + w * 2 * kAtom;
+        const uint32_t d = tmem + (uint32_t)(w * 128);
         // a last tile of <= 32 keys: N = 32 (the softmax masks the columns past n_kv by index)
-        const uint32_t idesc = p.n_kv - (kt0 + j) * 128 <= 32 ? IDESC_S32 : IDESC_S;
+        const uint32_t idesc = p.n_kv - (kt0 + t) * 128 <= 32 ? IDESC_S32 : IDESC_S;
 #pragma unroll
         for (int kk = 0; kk < 8; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
+          mma_ss_if(leader, d, smem_desc_sw128(qb + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
         }
-        mma_commit_if(leader, BAR_SFULL(j % NS));
+        mma_commit_if(leader, BAR_SFULL(w));
       }
       return true;
     };
     // HS: the two halves of S(j); S_B is skipped when no key of the tile lies in [64, 128), and the
     // K slot (and with separate V the V slot) is released by commits behind the last MMA reading it
-    auto issue_sa = [&](int j) -> bool {
+    auto issue_sa = [&](int j) -> bool {  // NS = 1: key tile t = j
       const int s = j % NK;
       if (!wwait(BAR_KFULL(s), (j / NK) & 1, 2)) return false;
       tc_fence_after();
@@ -647,42 +654,41 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       mma_commit_if(leader, BAR_SFULL(j % NS));
       if (!VK) mma_commit_if(leader, BAR_KEMPTY(s));  // separate V: K(j) is read by S(j) only
     };
+    const int n_steps = NS * n_kt;
     if (HS) {
-      for (int j = 0; ok && j < NS && j < n_kt; ++j) {
-        ok = issue_sa(j);
-        if (ok) issue_sb(j);
-      }
+      if (ok) ok = issue_sa(0);
+      if (ok) issue_sb(0);
     } else {
-      if (ok) ok = issue_s(0);
-      if (ok && NS == 2 && n_kt > 1) ok = issue_s(1);
+      for (int j = 0; ok && j < NS; ++j) ok = issue_s(j);  // key tile 0 of every stream
     }
     // P V in two 64-key halves: the first is issued once the softmax has stored P of keys [0, 64)
     // (BAR_PHALF), so it runs while the softmax computes the second half
-    for (int j = 0; ok && j < n_kt; ++j) {
-      const uint32_t vb = VK ? sK + (j % NK) * 2 * kAtom : sV + (j % NVS) * 2 * kAtom;
-      const uint32_t a_tm = tmem + (uint32_t)((j % NS) * 128);
-      const uint32_t o_tm = tmem + NS * 128 + (uint32_t)((j % NS) * 128);
-      const int ksteps = p.n_kv - (kt0 + j) * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
-      if (!wwait(BAR_PHALF(j % NS), (j / NS) & 1, 4)) break;
-      if (!VK && !wwait(BAR_VFULL(j % NVS), (j / NVS) & 1, 4)) break;
+    for (int j = 0; ok && j < n_steps; ++j) {
+      const int w = j % NS, t = j / NS;
+      const uint32_t vb = VK ? sK + (t % NK) * 2 * kAtom : sV + (t % NVS) * 2 * kAtom;
+      const uint32_t a_tm = tmem + (uint32_t)(w * 128);
+      const uint32_t o_tm = tmem + NS * 128 + (uint32_t)(w * 128);
+      const int ksteps = p.n_kv - (kt0 + t) * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
+      if (!wwait(BAR_PHALF(w), t & 1, 4)) break;
+      if (!VK && !wwait(BAR_VFULL(t % NVS), (t / NVS) & 1, 4)) break;
       tc_fence_after();
 #pragma unroll
       for (int kk = 0; kk < 4; ++kk)
         mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
-                  IDESC_PV, (j >= NS || kk > 0) ? 1u : 0u);
-      mma_commit_if(leader, BAR_PVH(j % NS));  // a softmax that rescales O mid-tile waits for it
-      if (HS && j + NS < n_kt && !(ok = issue_sa(j + NS))) break;
-      if (!wwait(BAR_PFULL(j % NS), (j / NS) & 1, 4)) break;
+                  IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+      mma_commit_if(leader, BAR_PVH(w));  // a softmax that rescales O mid-tile waits for it
+      if (HS && j + NS < n_steps && !(ok = issue_sa(j + NS))) break;
+      if (!wwait(BAR_PFULL(w), t & 1, 4)) break;
       tc_fence_after();
 #pragma unroll
       for (int kk = 4; kk < 8; ++kk)  // HS: P of keys [64, 128) sits in columns [64, 96)
         mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + (HS ? 64 + (kk - 4) * 8 : kk * 8),
                   smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV, 1u);
       if (HS) {
-        mma_commit_if(leader, BAR_PVB(j % NS));
-        mma_commit_if(leader, VK ? BAR_KEMPTY(j % NK) : BAR_VEMPTY(j % NVS));  // the slot P V(j) read
-        if (j + NS < n_kt) issue_sb(j + NS);
-      } else if (j + NS < n_kt) {
+        mma_commit_if(leader, BAR_PVB(w));
+        mma_commit_if(leader, VK ? BAR_KEMPTY(t % NK) : BAR_VEMPTY(t % NVS));  // the slot P V(j) read
+        if (j + NS < n_steps) issue_sb(j + NS);
+      } else if (j + NS < n_steps) {
         ok = issue_s(j + NS);
       }
     }
@@ -694,7 +700,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     __syncwarp();
   } else {
     // ------------------------------------------------------------------ softmax streams + epilogue
-    const int w = (warp - 2) >> 2;  // stream: KV tiles j = w, w + 2, ...
+    const int w = (warp - 2) >> 2;  // stream: query tile w, every key tile of the CTA's range
     const int quad = warp & 3;      // TMEM lane quadrant this warp may access
     const int row = quad * 32 + lane;
     const uint32_t lane_off = (uint32_t)(quad * 32) << 16;
@@ -705,19 +711,21 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
     };
 
-    for (int j = w; j < n_kt; j += NS) {
+    for (int t = 0; t < n_kt; ++t) {  // key tile t of this stream (step j = NS t + w)
       // HS: S_A first (S_B is waited for before the second half); otherwise all of S
-      if (!warp_wait(HS ? BAR_SA(w) : BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
+      if (!warp_wait(HS ? BAR_SA(w) : BAR_SFULL(w), t & 1, 8)) { ok = false; break; }
       tc_fence_after();
       if (!HS && warp == 2 + 4 * w && lane == 0) {  // ring slots done with (see above)
+        // S_w(t) complete: every stream's arrival frees the K slot of key tile t (separate V: read
+        // by the S MMAs only) or of t - 1 (V aliasing K: read by P V too), and the V slot of t - 1
         if (VK) {
-          if (j >= NS) mbar_arrive(BAR_KEMPTY((j - NS) % NK));
+          if (t >= 1) mbar_arrive(BAR_KEMPTY((t - 1) % NK));
         } else {
-          mbar_arrive(BAR_KEMPTY(j % NK));
-          if (j >= NS) mbar_arrive(BAR_VEMPTY((j - NS) % NVS));
+          mbar_arrive(BAR_KEMPTY(t % NK));
+          if (t >= 1) mbar_arrive(BAR_VEMPTY((t - 1) % NVS));
         }
       }
-      const int valid = p.n_kv - (kt0 + j) * 128;  // same for every thread: the branches below are uniform
+      const int valid = p.n_kv - (kt0 + t) * 128;  // same for every thread: the branches below are uniform
       // O, l, h to the reference max(m_ref, mx). Warp-uniform (warp-collective TMEM access): lanes
       // whose max grew adopt it. The caller guarantees no P V into O_w is in flight.
       auto rescale = [&](float mx) {
@@ -740,7 +748,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       };
       // P in two 64-key halves: keys [64 k, 64 k + 64) -> columns [32 k, 32 k + 32); BAR_PHALF
       // after the first lets P V of those keys start.
-      if (j != w && valid >= 128) {
+      if (t > 0 && valid >= 128) {
         // A full tile after the stream's first: the exponentials go against the current reference
         // while the half's max is taken beside them; a half whose max passes the reference by
         // more than the threshold (rare: the reference only grows) is redone after the rescale,
@@ -754,9 +762,9 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           float lt = 0.f, ht = 0.f;
           const float mx = probs_row<T, 64, ENT, false, true>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
           if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-            // every earlier P V into O_w has completed (S[j] complete; HS: S_A(j) only follows the
-            // first half of P V(j - NS), so wait for the second); P V(j) is not issued yet
-            if (HS && !warp_wait(BAR_PVB(w), ((j / NS) - 1) & 1, 16)) { ok = false; break; }
+            // every earlier P V into O_w has completed (S_w(t) complete; HS: S_A(t) only follows the
+            // first half of P V(t - 1), so wait for the second); P V(t) is not issued yet
+            if (HS && !warp_wait(BAR_PVB(w), (t - 1) & 1, 16)) { ok = false; break; }
             tc_fence_after();
             rescale(mx);
             lt = 0.f;
@@ -771,7 +779,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           mbar_arrive(BAR_PHALF(w));
         }
         if (HS) {
-          if (!warp_wait(BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
+          if (!warp_wait(BAR_SFULL(w), t & 1, 8)) { ok = false; break; }
           tc_fence_after();
         }
         {
@@ -783,8 +791,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           float lt = 0.f, ht = 0.f;
           const float mx = probs_row<T, 64, ENT, false, true>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
           if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-            // the first half of P V(j) may still be adding into O_w: wait for its commit
-            if (!warp_wait(BAR_PVH(w), (j / NS) & 1, 16)) { ok = false; break; }
+            // the first half of P V(t) may still be adding into O_w: wait for its commit
+            if (!warp_wait(BAR_PVH(w), t & 1, 16)) { ok = false; break; }
             tc_fence_after();
             rescale(mx);
             lt = 0.f;
@@ -798,7 +806,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       } else {
         // the stream's first tile (sets the reference) and the ragged last tile: the tile max first
         if (HS) {
-          if (!warp_wait(BAR_SFULL(w), (j / NS) & 1, 8)) { ok = false; break; }
+          if (!warp_wait(BAR_SFULL(w), t & 1, 8)) { ok = false; break; }
           tc_fence_after();
         }
         uint32_t sr[128];
@@ -809,12 +817,12 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         tmem_wait_ld();
         const float mx =
             (valid < 128 ? row_max_raw<128, true>(sr, valid) : row_max_raw<128, false>(sr, 128)) * p.scale_log2;
-        if (j == w) {
+        if (t == 0) {
           m_ref = mx;
         } else if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
-          // every earlier P V into O_w has completed (S[j] complete, see above; HS: the second
-          // half of P V(j - NS) is waited for)
-          if (HS && !warp_wait(BAR_PVB(w), ((j / NS) - 1) & 1, 16)) { ok = false; break; }
+          // every earlier P V into O_w has completed (S_w(t) complete, see above; HS: the second
+          // half of P V(t - 1) is waited for)
+          if (HS && !warp_wait(BAR_PVB(w), (t - 1) & 1, 16)) { ok = false; break; }
           tc_fence_after();
           rescale(mx);
         }
@@ -845,62 +853,37 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       mbar_arrive(BAR_PFULL(w));
     }
 
-    // epilogue: wait for every MMA, merge the two streams' (m, l, h, O) per row (exchanged
-    // through the Q tile, idle once every S MMA has completed), O / l -> bf16 in the idle K ring,
-    // TMA store; LSE and entropy per row
+    // epilogue: wait for every MMA; each stream normalises its own O (O / l) into 16-bit (or, for a
+    // key chunk, fp32 O / l plus (m, l, h)) in the idle ring, one thread stores every stream's tile
+    // with TMA (rows past n_q / n_pad clipped); LSE and entropy per row
     if (ok) ok = warp_wait(BAR_DONE, 0, 8);
     tc_fence_after();
-    float* xch = reinterpret_cast<float*>(smem_raw + (sQ - smem_u32(smem_raw)));
-    xch[(3 * w + 0) * 128 + row] = m_ref;
-    xch[(3 * w + 1) * 128 + row] = l;
-    xch[(3 * w + 2) * 128 + row] = h;
-    ok = named_bar_and(1, 128 * NS, ok);
-    const uint32_t stage = sK;
+    const bool part = p.kv_split > 1;  // key chunk: fp32 O normalised by this chunk's l, plus (m, l, h)
+    const uint32_t stage = sK + (uint32_t)w * (part ? 4 : 2) * kAtom;  // this stream's tile (fp32: 64 KB)
+    const int grow = q0 + 128 * w + row;
     if (ok) {
-      const float m0 = xch[0 * 128 + row], l0 = xch[1 * 128 + row], h0 = xch[2 * 128 + row];
-      const bool two = NS == 2 && n_kt > 1;  // stream 1 owns no tile (and O_1 was never written) otherwise
-      const float m1 = two ? xch[3 * 128 + row] : 0.f, l1 = two ? xch[4 * 128 + row] : 0.f;
-      const float h1 = two ? xch[5 * 128 + row] : 0.f;
-      const float m = two ? fmaxf(m0, m1) : m0;
-      const float a0 = fast_exp2(m0 - m), a1 = two ? fast_exp2(m1 - m) : 0.f;
-      const float lt = a0 * l0 + a1 * l1;
-      const float ht = two ? a0 * fmaf(m0 - m, l0, h0) + a1 * fmaf(m1 - m, l1, h1) : h0;
-      const float inv = 1.f / lt;
-      const float c0 = a0 * inv, c1 = a1 * inv;
-      const uint32_t tO0 = tmem + lane_off + NS * 128, tO1 = tO0 + 128;
-      const bool part = p.kv_split > 1;  // key chunk: fp32 O normalised by this chunk's l, plus (m, l, h)
+      const float inv = 1.f / l;
+      const uint32_t tO = tmem + lane_off + NS * 128 + (uint32_t)(w * 128);
 #pragma unroll 1
-      for (int c = (4 / NS) * w; c < (4 / NS) * (w + 1); ++c) {  // this warpgroup's output columns
-        uint32_t o0[32], o1[32];
-        tmem_ld32(tO0 + c * 32, o0);
-        if (two) tmem_ld32(tO1 + c * 32, o1);
+      for (int c = 0; c < 4; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
         tmem_wait_ld();
-        if (!two) {
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o1[i] = 0u;
-        }
         if (part) {
           // [128 rows][32 floats] box c of the fp32 staging (128-byte swizzle)
           const uint32_t base = stage + c * 16384 + row * 128;
 #pragma unroll
-          for (int k4 = 0; k4 < 8; ++k4) {
-            float x[4];
-#pragma unroll
-            for (int e = 0; e < 4; ++e)
-              x[e] = fmaf(__uint_as_float(o0[4 * k4 + e]), c0, __uint_as_float(o1[4 * k4 + e]) * c1);
-            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((k4 ^ (row & 7)) << 4)), "f"(x[0]),
-                         "f"(x[1]), "f"(x[2]), "f"(x[3])
+          for (int k4 = 0; k4 < 8; ++k4)
+            asm volatile("st.shared.v4.f32 [%0], {%1, %2, %3, %4};" ::"r"(base + ((k4 ^ (row & 7)) << 4)),
+                         "f"(__uint_as_float(o[4 * k4]) * inv), "f"(__uint_as_float(o[4 * k4 + 1]) * inv),
+                         "f"(__uint_as_float(o[4 * k4 + 2]) * inv), "f"(__uint_as_float(o[4 * k4 + 3]) * inv)
                          : "memory");
-          }
           continue;
         }
         uint32_t wv[16];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) {
-          const float x0 = fmaf(__uint_as_float(o0[2 * i]), c0, __uint_as_float(o1[2 * i]) * c1);
-          const float x1 = fmaf(__uint_as_float(o0[2 * i + 1]), c0, __uint_as_float(o1[2 * i + 1]) * c1);
-          wv[i] = Elem<T>::pack(x0, x1);
-        }
+        for (int i = 0; i < 16; ++i)
+          wv[i] = Elem<T>::pack(__uint_as_float(o[2 * i]) * inv, __uint_as_float(o[2 * i + 1]) * inv);
         const int atom = c >> 1;
 #pragma unroll
         for (int k = 0; k < 4; ++k) {
@@ -911,29 +894,32 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
                        : "memory");
         }
       }
-      const int grow = q0 + row;
       if (part) {
-        if (w == 0) {  // rows past n_q too (inside n_pad): never read by the merge
+        if (grow < p.n_pad) {  // rows past n_q too (inside n_pad): never read by the merge
           const int64_t plane = (int64_t)p.kv_split * p.n_seq * p.n_pad;
           const int64_t idx = ((int64_t)kchunk * p.n_seq + bi) * p.n_pad + grow;
-          p.pst[idx] = m;
-          p.pst[plane + idx] = lt;
-          p.pst[2 * plane + idx] = ht;
+          p.pst[idx] = m_ref;
+          p.pst[plane + idx] = l;
+          p.pst[2 * plane + idx] = h;
         }
-      } else if (w == 0 && grow < p.n_q) {
-        const float lg = log2f(lt);
+      } else if (grow < p.n_q) {
+        const float lg = log2f(l);
         const int64_t idx = (int64_t)bi * p.n_q + grow;
-        if (p.lse) p.lse[idx] = m + lg;
-        if (ENT && p.ent) p.ent[idx] = (lg - ht / lt) * kLn2;
+        if (p.lse) p.lse[idx] = m_ref + lg;
+        if (ENT && p.ent) p.ent[idx] = (lg - h / l) * kLn2;
       }
     }
     fence_proxy_async_smem();
-    named_bar_sync(2, 128 * NS);
+    ok = named_bar_and(2, 128 * NS, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      if (p.kv_split > 1) {
-        for (int c = 0; c < 4; ++c) tma_store_3d(&p.tm_po, 32 * c, q0, kchunk * p.n_seq + bi, stage + c * 16384);
-      } else {
-        for (int a = 0; a < 2; ++a) tma_store_3d(&p.tm_o, 64 * a, q0, bi, stage + a * kAtom);
+      for (int ws = 0; ws < NS; ++ws) {
+        const uint32_t st = sK + (uint32_t)ws * (part ? 4 : 2) * kAtom;
+        const int qr = q0 + 128 * ws;
+        if (part) {
+          for (int c = 0; c < 4; ++c) tma_store_3d(&p.tm_po, 32 * c, qr, kchunk * p.n_seq + bi, st + c * 16384);
+        } else {
+          for (int a = 0; a < 2; ++a) tma_store_3d(&p.tm_o, 64 * a, qr, bi, st + a * kAtom);
+        }
       }
       tma_store_commit_and_wait();
     }
@@ -991,7 +977,7 @@ __global__ void __launch_bounds__(256) fwd_split_merge_kernel(const float* po, c
 // fixed cost: Q load, TMEM set-up, merge and store), never leaving a chunk without a tile.
 int fwd2_split(int64_t batch, int n_q, int n_kv) {
   if (batch <= 0 || n_q <= 0) return 1;
-  const int64_t n_qt = (n_q + 127) / 128;
+  const int64_t n_qt = (n_q + 255) / 256;  // CTAs per sequence and key chunk: two query tiles each
   const int nkt = (n_kv + 127) / 128;
   int sms = 148, dev = 0;
   if (cudaGetDevice(&dev) == cudaSuccess) cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
@@ -1039,7 +1025,7 @@ cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   auto kern = fea_fwd2_sm100_kernel<T, VK, ENT, NS>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
-  const int64_t blocks = (int64_t)p.n_qtiles * p.kv_split * batch;
+  const int64_t blocks = (int64_t)((p.n_qtiles + NS - 1) / NS) * p.kv_split * batch;  // NS query tiles per CTA
   if (blocks > 0x7fffffff || batch > 0x7fffffff) return cudaErrorInvalidConfiguration;
   kern<<<(unsigned)blocks, C::THREADS, C::SMEM, st>>>(p);
   return cudaGetLastError();
