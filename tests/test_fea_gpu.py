@@ -175,6 +175,26 @@ def test_values_aliasing_keys_with_row_max_jumps(steps):
     check(got, ref)
 
 
+def test_values_aliasing_keys_long_sequence():
+    # V passed as K with more than 2048 keys: the two-stream forward (two query tiles per CTA, 17
+    # of them here, so the last CTA's second stream runs on a zero-filled tile), with V aliasing K
+    # each K slot freed only after both streams' P V of that key tile; forward and gradients against
+    # the oracle.
+    gen = torch.Generator().manual_seed(31)
+    N, D = 2100, 128
+    q, k = (torch.randn(1, 2, N, D, generator=gen).bfloat16().float() for _ in range(2))
+    do, de = torch.randn(1, 2, N, D, generator=gen), torch.randn(1, 2, N, generator=gen)
+    qc, kc = (t.cuda().bfloat16().requires_grad_() for t in (q, k))
+    o, e = flash_entropy_attention(qc, kc, kc)
+    gq, gk = torch.autograd.grad((o.float() * do.cuda()).sum() + (e * de.cuda()).sum(), (qc, kc))
+    torch.cuda.synchronize()
+    got = [t.detach().float().cpu() for t in (o, e, gq, gk)]
+    qr, kr = (t.float().clone().requires_grad_() for t in (q, k))
+    o_r, e_r = oracle.entropy_attention(qr, kr, kr, D ** -0.5)
+    gq_r, gk_r = torch.autograd.grad((o_r * do).sum() + (e_r * de).sum(), (qr, kr))
+    check(got, [o_r.detach(), e_r.detach(), gq_r, gk_r])
+
+
 def test_split_key_range_backward_matches_and_is_deterministic(monkeypatch):
     # Few query tiles over a long key range: in fp32-accumulate mode the dQ kernel splits the key
     # range over several CTAs (partial tiles summed in a fixed order). The workspace is held to the
