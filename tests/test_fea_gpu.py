@@ -176,10 +176,10 @@ def test_values_aliasing_keys_with_row_max_jumps(steps):
 
 
 def test_values_aliasing_keys_long_sequence():
-    # V passed as K with more than 2048 keys: the two-stream forward (two query tiles per CTA, 17
-    # of them here, so the last CTA's second stream runs on a zero-filled tile), with V aliasing K
-    # each K slot freed only after both streams' P V of that key tile; forward and gradients against
-    # the oracle.
+    # V passed as K over 2100 keys on two sequences: the forward splits the key range (a workspace
+    # is given), which runs the two-stream kernel (two query tiles per CTA, 17 of them here, so the
+    # last CTA's second stream runs on a zero-filled tile); with V aliasing K each K slot is freed
+    # only after both streams' P V of that key tile. Forward and gradients against the oracle.
     gen = torch.Generator().manual_seed(31)
     N, D = 2100, 128
     q, k = (torch.randn(1, 2, N, D, generator=gen).bfloat16().float() for _ in range(2))
@@ -193,6 +193,32 @@ def test_values_aliasing_keys_long_sequence():
     o_r, e_r = oracle.entropy_attention(qr, kr, kr, D ** -0.5)
     gq_r, gk_r = torch.autograd.grad((o_r * do).sum() + (e_r * de).sum(), (qr, kr))
     check(got, [o_r.detach(), e_r.detach(), gq_r, gk_r])
+
+
+def test_values_aliasing_keys_long_unsplit():
+    # V passed as K over 2100 keys on 40 sequences: too many CTAs for a key-range split (no forward
+    # workspace), so the forward runs the one-stream kernel over 17 key tiles, the last one 52 keys
+    # wide (its second S half is not issued). All 40 sequences run on the GPU; the oracle checks
+    # the first three, the others only for finite values.
+    from vmonarch_b200 import _native as N
+    gen = torch.Generator().manual_seed(37)
+    H, N_, D, n_chk = 40, 2100, 128, 3
+    a = N.FeaFwdArgs()
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = H, N_, N_, D, D, D
+    a.dtype = N.dtype_code(torch.bfloat16)
+    assert N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a)) == 0
+    q, k = (torch.randn(1, H, N_, D, generator=gen).bfloat16().float() for _ in range(2))
+    do, de = torch.randn(1, H, N_, D, generator=gen), torch.randn(1, H, N_, generator=gen)
+    qc, kc = (t.cuda().bfloat16().requires_grad_() for t in (q, k))
+    o, e = flash_entropy_attention(qc, kc, kc)
+    gq, gk = torch.autograd.grad((o.float() * do.cuda()).sum() + (e * de.cuda()).sum(), (qc, kc))
+    torch.cuda.synchronize()
+    got = [t.detach().float().cpu() for t in (o, e, gq, gk)]
+    assert all(torch.isfinite(t).all() for t in got)
+    qr, kr = (t[:, :n_chk].clone().requires_grad_() for t in (q, k))
+    o_r, e_r = oracle.entropy_attention(qr, kr, kr, D ** -0.5)
+    gq_r, gk_r = torch.autograd.grad((o_r * do[:, :n_chk]).sum() + (e_r * de[:, :n_chk]).sum(), (qr, kr))
+    check([t[:, :n_chk] for t in got], [o_r.detach(), e_r.detach(), gq_r, gk_r])
 
 
 def test_split_key_range_backward_matches_and_is_deterministic(monkeypatch):

@@ -1031,9 +1031,10 @@ cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-// Short key ranges (V aliasing K): the one-stream kernel, two CTAs per SM, hides the Q load and
-// the epilogue of one CTA under the other's key loop; long ranges keep the two-stream kernel.
-bool fwd_one_stream(int n_kv, int kv_split) { return kv_split == 1 && n_kv <= 16 * 128; }
+// V aliasing K: the one-stream kernel (two CTAs per SM, S in halves) hides the Q load and the
+// epilogue of one CTA under the other's key loop; it runs every unsplit key range (measured faster
+// than the two-stream kernel from 1560 to 32768 keys). A split key range keeps the two-stream kernel.
+bool fwd_one_stream(int n_kv, int kv_split) { (void)n_kv; return kv_split == 1; }
 
 template <typename T, bool ENT>
 cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bool vk, cudaStream_t st) {
