@@ -142,14 +142,18 @@ def test_row_max_jumps_inside_a_key_tile(Dv, steps):
     check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
 
 
+@pytest.mark.parametrize("copies", [1, 20])
 @pytest.mark.parametrize("steps", [(320, 704), (256, 960), (64, 448)])
-def test_values_aliasing_keys_with_row_max_jumps(steps):
-    # V passed as the same tensor as K with D = 128 and <= 2048 keys: the one-stream forward (S in
-    # 64-key halves, each issued behind P V of the previous tile's same half), whose rescale of O
-    # waits for the previous tile's second P V half (a jump in a tile's first half) or for this
-    # tile's first (a jump in the second half). Half the rows see the jumps (each ~12 in log2 units,
-    # past the threshold of 8), with steps small enough that the values (= keys) stay O(1) for the
-    # absolute output bound.
+def test_values_aliasing_keys_with_row_max_jumps(steps, copies):
+    # V passed as the same tensor as K with D = 128, two sequences of 1152 keys. Alone (copies = 1)
+    # the forward splits the key range and runs the two-stream kernel; repeated 20 times there are
+    # too many CTAs for a split, and the one-stream kernel runs (S in 64-key halves, each issued
+    # behind P V of the previous tile's same half), whose rescale of O waits for the previous
+    # tile's second P V half (a jump in a tile's first half) or for this tile's first (a jump in
+    # the second half). Half the rows see the jumps (each ~12 in log2 units, past the threshold of
+    # 8), with steps small enough that the values (= keys) stay O(1) for the absolute output bound.
+    # The oracle checks the first two sequences.
+    from vmonarch_b200 import _native as N_
     gen = torch.Generator().manual_seed(29)
     N, D = 1152, 128
     q = torch.randn(1, 2, N, D, generator=gen)
@@ -161,11 +165,16 @@ def test_values_aliasing_keys_with_row_max_jumps(steps):
     k = k.bfloat16().float()
     do, de = torch.randn(1, 2, N, D, generator=gen), torch.randn(1, 2, N, generator=gen)
 
-    qc, kc = (t.cuda().bfloat16().requires_grad_() for t in (q, k))
+    a = N_.FeaFwdArgs()
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 2 * copies, N, N, D, D, D
+    a.dtype = N_.dtype_code(torch.bfloat16)
+    assert (N_.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a)) == 0) == (copies > 1)
+    rep = lambda t: t.repeat(1, copies, *([1] * (t.dim() - 2)))  # noqa: E731
+    qc, kc = (rep(t).cuda().bfloat16().requires_grad_() for t in (q, k))
     o, e = flash_entropy_attention(qc, kc, kc)
-    gq, gk = torch.autograd.grad((o.float() * do.cuda()).sum() + (e * de.cuda()).sum(), (qc, kc))
+    gq, gk = torch.autograd.grad((o.float() * rep(do).cuda()).sum() + (e * rep(de).cuda()).sum(), (qc, kc))
     torch.cuda.synchronize()
-    got = [t.detach().float().cpu() for t in (o, e, gq, gk)]
+    got = [t.detach().float().cpu()[:, :2] for t in (o, e, gq, gk)]
 
     qr, kr = (t.float().clone().requires_grad_() for t in (q, k))
     o_r, e_r = oracle.entropy_attention(qr, kr, kr, D ** -0.5)
