@@ -2,7 +2,7 @@
 """Benchmark of the VMonarch attention hot path on B200 (one JSON line on rank 0).
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|triton]
-                    [--workload dit14b] [--scaling weak|strong]
+                    [--workload dit14b] [--scaling weak|strong] [--graph]
 
 A step is one forward + backward of VMonarch attention over one synthetic layer of the workload
 (default: the video-DiT 14B-class layer B=1, H=40, m=21, b=1560, D=128, 2 iterations, 1560 recomputed
@@ -54,6 +54,8 @@ def parse_args():
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads of the layer (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
+    ap.add_argument("--graph", action="store_true",
+                    help="time `value` as replays of one CUDA graph holding the whole step (launch-bound sizes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget-s", type=float, default=150.0, help="wall-clock cap of the CPU reference arm")
     return ap.parse_args()
@@ -147,20 +149,30 @@ def scaled_flops(w: Workload, n_heads: int) -> float:
     return (f["fwd"] + f["bwd"]) * n_heads / w.H
 
 
-def time_steps(step, args_dev, steps: int, warmup: int, device) -> float:
-    """ms per step: W warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events."""
+def time_steps(step, args_dev, steps: int, warmup: int, device, launches=None) -> float:
+    """ms per step: W warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events.
+    `launches`, when given, is a list that receives this library's kernel launches issued by the
+    K timed steps (warm-up excluded)."""
+    count = lambda: 0  # noqa: E731  (other arms load nothing of this library)
+    if launches is not None:
+        from vmonarch_b200 import ops
+        count = ops.kernel_launches
     for _ in range(warmup):
         step(*args_dev)
     torch.cuda.synchronize(device)
     shard.barrier()
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    n0 = count()
     start.record()
     for _ in range(steps):
         step(*args_dev)
     end.record()
+    n1 = count()
     torch.cuda.synchronize(device)
     shard.barrier()
+    if launches is not None:
+        launches.append(n1 - n0)
     return start.elapsed_time(end) / steps
 
 
@@ -339,6 +351,32 @@ def cpu_reference_sample(w: Workload, seed: int, budget_s: float, steps: int, wa
 
 
 # ----------------------------------------------------------------------------------------- arms
+def capture_step(step, args_dev, warmup: int, device):
+    """Captures one step in a CUDA graph after `warmup` eager steps on a side stream (the pattern
+    torch documents for whole-network capture). Returns the graph, the outputs every replay
+    rewrites, and the number of this library's kernels one replay launches."""
+    from vmonarch_b200 import ops
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream(device))
+    with torch.cuda.stream(side):
+        for _ in range(max(warmup, 1)):
+            step(*args_dev)
+    torch.cuda.current_stream(device).wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    n0 = ops.kernel_launches()
+    with torch.cuda.graph(graph):
+        outs = step(*args_dev)
+    return graph, outs, ops.kernel_launches() - n0
+
+
+def l2_note(w: Workload) -> str:
+    """How the timed steps relate to the 126 MB L2 (no flush is done between steps)."""
+    q_bytes = w.B * w.H * w.N * w.D * 2
+    if q_bytes > 126 * 2**20:
+        return "inputs and activations larger than L2 (no flush needed)"
+    return f"not flushed: q is {q_bytes / 2**20:.0f} MB, the step's working set may stay in L2 (small, launch-bound size)"
+
+
 def base_line(args, w, n_gpus, ms, value, impl=None) -> dict:
     line = {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": n_gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": args.scaling,
@@ -347,7 +385,7 @@ def base_line(args, w, n_gpus, ms, value, impl=None) -> dict:
                        "D": w.D, "num_iters": w.iters, "recompute_tokens": w.recompute,
                        "layers_per_job": n_gpus if args.scaling == "weak" else 1,
                        "parallelism": f"heads x{n_gpus}, no collective",
-                       "l2": "inputs and activations larger than L2 (no flush needed)"}}
+                       "l2": l2_note(w)}}
     if impl:
         line["impl"] = impl
     return line
@@ -368,10 +406,17 @@ def run_ours(args, info, device):
     if args.scaling == "strong":
         flops_job = scaled_flops(w, w.H)
 
-    launches0 = ops.kernel_launches()
-    with ClockSampler(device) as clk:
-        ms = time_steps(step, dev, args.steps, args.warmup, device)
-    launches = ops.kernel_launches() - launches0
+    if args.graph:
+        graph, graph_outs, per_replay = capture_step(step, dev, args.warmup, device)
+        with ClockSampler(device) as clk:
+            ms = time_steps(lambda *_: graph.replay(), dev, args.steps, args.warmup, device)
+        launches = per_replay * args.steps
+        del graph, graph_outs
+    else:
+        counted = []
+        with ClockSampler(device) as clk:
+            ms = time_steps(step, dev, args.steps, args.warmup, device, launches=counted)
+        launches = counted[0]
     ms_max = shard.max_over_ranks(ms, device)
     value = flops_job / (ms_max * 1e-3) / 1e12
     per = profile_step(step, dev, device)
@@ -394,6 +439,7 @@ def run_ours(args, info, device):
         return None
     line = base_line(args, w, info.world, ms_max, value)
     f = w.flops()
+    line["config"]["cuda_graph"] = bool(args.graph)
     line["dense_equivalent_tflops"] = round(3.5 * f["dense_fwd"] * n_local / w.H * layers / (ms_max * 1e-3) / 1e12, 2)
     line["flops_per_step"] = flops_job
     line["roofline"] = roofline(per)
