@@ -459,7 +459,9 @@ def run_reference(args, info):
     cpu = cpu_reference_sample(w, args.seed, args.cpu_budget_s, args.steps, args.warmup)
     ms = scaled_flops(w, w.H) / (cpu["value"] * 1e12) * 1e3  # one full layer, extrapolated from the heads
     line = base_line(args, w, info.world, ms, cpu["value"], impl="reference")
+    line["value"] = cpu["value"]  # the same figure as cpu_baseline and e2e, not re-rounded
     line["steps"] = cpu["timed_samples"]
+    line["config"]["l2"] = "host cores (no GPU cache involved)"
     line["cpu_baseline"] = cpu
     line["e2e"] = {"value": cpu["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     line["gpu_launches"] = 0
