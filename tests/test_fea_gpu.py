@@ -84,6 +84,26 @@ def test_fp16_and_custom_scale():
     check(got, run_oracle(q, k, v, do, de, 0.05))
 
 
+@pytest.mark.parametrize("N", [300, 2100])
+def test_fp16_values_aliasing_keys(N):
+    # fp16, D = 128, V passed as K: the one-stream forward (300 keys on 40 sequences: no split) and
+    # the split two-stream one (2100 keys on 2 sequences), then the V-aliasing backward
+    H = 40 if N == 300 else 2
+    gen = torch.Generator().manual_seed(N + 5)
+    q, k = (torch.randn(1, H, N, 128, generator=gen).half().float() for _ in range(2))
+    do, de = torch.randn(1, H, N, 128, generator=gen), torch.randn(1, H, N, generator=gen)
+    qc, kc = (t.cuda().half().requires_grad_() for t in (q, k))
+    o, e = flash_entropy_attention(qc, kc, kc)
+    gq, gk = torch.autograd.grad((o.float() * do.cuda()).sum() + (e * de.cuda()).sum(), (qc, kc))
+    torch.cuda.synchronize()
+    n = min(H, 3)
+    got = [t.detach().float().cpu()[:, :n] for t in (o, e, gq, gk)]
+    qr, kr = (t[:, :n].clone().requires_grad_() for t in (q, k))
+    o_r, e_r = oracle.entropy_attention(qr, kr, kr, 128 ** -0.5)
+    gq_r, gk_r = torch.autograd.grad((o_r * do[:, :n]).sum() + (e_r * de[:, :n]).sum(), (qr, kr))
+    check(got, [o_r.detach(), e_r.detach(), gq_r, gk_r])
+
+
 def test_noncontiguous_inputs_and_no_mutation():
     gen = torch.Generator().manual_seed(8)
     base = torch.randn(1, 200, 2, 64, generator=gen).bfloat16().cuda()

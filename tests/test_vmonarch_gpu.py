@@ -94,6 +94,18 @@ def test_fp16_vmonarch():
     check(run_cuda(q, k, v, dz, 4, 96, 2, 96, dtype=torch.float16), run_oracle(q, k, v, dz, 4, 96, 2, 96))
 
 
+@pytest.mark.parametrize("H, m, b, iters, r", [(2, 8, 200, 2, 200), (8, 21, 130, 3, 100)])
+def test_fp16_vmonarch_head_dim_128(H, m, b, iters, r):
+    # D = 128 in fp16 runs the tcgen05 kernels with f16 operands: the R-step forward with V
+    # aliasing K (16 grid rows: few enough that the key range splits, two-stream kernel; 168 grid
+    # rows: no split, one-stream kernel), the Dv = 256 last R step, the tcgen05 L-step forward,
+    # the dK/dV kernels and the recompute
+    gen = torch.Generator().manual_seed(m * b + 1)
+    q, k, v = (torch.randn(1, H, m * b, 128, generator=gen).half().float() for _ in range(3))
+    dz = torch.randn(1, H, m * b, 128, generator=gen)
+    check(run_cuda(q, k, v, dz, m, b, iters, r, dtype=torch.float16), run_oracle(q, k, v, dz, m, b, iters, r))
+
+
 def test_module_readme_usage():
     attn = VMonarchAttention(num_blocks=16, block_size=256, num_iters=2)
     B, H, N, D = 2, 4, 16 * 256, 128
