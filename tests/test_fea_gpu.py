@@ -471,3 +471,45 @@ def _bwd_args(B, nq, nk, D, vk):
     a.batch, a.n_q, a.n_kv, a.d = B, nq, nk, D
     a.dv, a.dv1, a.grad_mode, a.v_is_k = (2 * D if vk else D), D, 1, int(vk)
     return a
+
+
+def test_forward_workspace_absent_or_short_runs_unsplit():
+    # Through the C ABI, V passed as K over 2100 keys on two sequences: with the workspace the
+    # query asks for, the key range splits (two-stream kernel + merge); with no workspace or a
+    # shorter one the call still succeeds, unsplit (one-stream kernel). The two unsplit runs are
+    # bitwise identical; the split one agrees within float rounding of the merge.
+    from vmonarch_b200 import _native as N
+    gen = torch.Generator().manual_seed(47)
+    B, n, D = 2, 2100, 128
+    q, k = (torch.randn(B, n, D, generator=gen).bfloat16().cuda() for _ in range(2))
+
+    def run(ws_bytes):
+        o = torch.empty(B, n, D, dtype=torch.bfloat16, device="cuda")
+        lse, ent = torch.empty(B, n, device="cuda"), torch.empty(B, n, device="cuda")
+        a = N.FeaFwdArgs()
+        a.q, a.q_bs, a.k, a.k_bs, a.v, a.v_bs = q.data_ptr(), n * D, k.data_ptr(), n * D, k.data_ptr(), n * D
+        a.o, a.o_bs, a.lse, a.ent = o.data_ptr(), n * D, lse.data_ptr(), ent.data_ptr()
+        a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = B, n, n, D, D, D
+        a.dtype, a.sm_scale = N.dtype_code(torch.bfloat16), D ** -0.5
+        need = N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a))
+        ws = None
+        if ws_bytes is not None:
+            ws = torch.empty(max(need if ws_bytes == "full" else ws_bytes, 16), dtype=torch.uint8, device="cuda")
+            a.workspace, a.workspace_bytes = ws.data_ptr(), ws.numel() if ws_bytes == "full" else ws_bytes
+        rc = N.lib.vmb_fea_fwd(ctypes.byref(a), N.stream_ptr(q.device))
+        assert rc == 0, N.lib.vmb_last_error()
+        torch.cuda.synchronize()
+        return need, [t.float().cpu() for t in (o, lse, ent)]
+
+    need, full = run("full")
+    assert need > 0
+    _, none = run(None)
+    _, short = run(need // 2)
+    for a_, b_ in zip(none, short):
+        assert torch.equal(a_, b_)
+    o_r, e_r = oracle.entropy_attention(q.float().cpu().unsqueeze(0), k.float().cpu().unsqueeze(0),
+                                        k.float().cpu().unsqueeze(0), D ** -0.5)
+    for got in (full, none):
+        assert (got[0] - o_r[0]).abs().max() <= 2e-2 and max_rel_err(got[2], e_r[0]) <= 2e-2
+    # o: at most about one bf16 rounding step apart; lse: fp32 merge rounding
+    assert (full[0] - none[0]).abs().max() <= 2e-2 and (full[1] - none[1]).abs().max() <= 1e-4
