@@ -1,5 +1,5 @@
-"""Parity at the benchmark's full sizes (BASELINE configs 3 and 4), where the CPU oracle is too slow
-for whole tensors: one full head is checked against the same fp32 formulas evaluated on the GPU
+"""Parity at the benchmark's full sizes (4 and 5), where the CPU oracle is too
+slow for whole tensors: whole heads are checked against the same fp32 formulas evaluated on the GPU
 (the oracle's torch code on CUDA tensors, or a dense fp32 attention), and every head is checked
 through size-independent properties (entropy in [0, ln N], outputs inside the convex hull of V)."""
 import math
@@ -39,27 +39,51 @@ def test_fea_config3_full_size():
         assert (g[0, h].float() - gr).abs().max() <= max(5e-2, 8e-3 * gr.abs().max().item())
 
 
-def test_vmonarch_config4_one_full_head():
-    w = WORKLOADS["dit14b"]  # m=21, b=1560, D=128, 2 iterations, r=1560
-    dev = torch.device("cuda")
-    q, k, v, do, _ = (t.to(dev) for t in make_inputs(w, seed=1, heads=range(3, 4)))
+def _layer_with_checked_heads(w, check_heads, seed):
+    """Full (B=1, H, N, D) bf16 q, k, v, dz on the GPU. The checked heads hold the benchmark's seeded
+    values (make_inputs); the other heads are seeded N(0,1) filler. Heads never interact, so the
+    filler only sets the sizes, and with them the kernel routes, that the whole layer takes."""
+    gen = torch.Generator(device="cuda").manual_seed(seed + 77)
+    t = [torch.randn(w.B, w.H, w.N, w.D, device="cuda", generator=gen).bfloat16() for _ in range(4)]
+    for h in check_heads:
+        q, k, v, do, _ = make_inputs(w, seed=seed, heads=range(h, h + 1))
+        for i, x in enumerate((q, k, v, do)):
+            t[i][:, h:h + 1] = x.cuda()
+    return t
+
+
+def _check_vmonarch_layer(w, check_heads, seed):
+    """Forward + backward of the whole layer; each checked head against the fp32 oracle evaluated on
+    the GPU, with the reference's relative tolerances and the north-star absolute bounds (z max-abs
+    2e-2, mean-abs 2e-3; gradients max-abs 5e-2, floored at the bf16 rounding of large ones)."""
+    q, k, v, dz = _layer_with_checked_heads(w, check_heads, seed)
     leaves = [t.requires_grad_() for t in (q, k, v)]
     z = vmonarch_attention(*leaves, w.m, w.b, w.iters, recompute_tokens=w.recompute)
-    grads = torch.autograd.grad(z, leaves, do)
-    ref_leaves = [t.detach().float().requires_grad_() for t in (q, k, v)]
-    z_r = oracle.vmonarch_attention(*ref_leaves, w.m, w.b, w.iters, recompute_tokens=w.recompute)
-    g_r = torch.autograd.grad(z_r, ref_leaves, do.float())
-    assert max_rel_err(z, z_r) <= 3e-2
-    for g, gr in zip(grads, g_r):
-        assert max_rel_err(g, gr) <= 5e-2
+    grads = torch.autograd.grad(z, leaves, dz)
+    torch.cuda.synchronize()
+    assert torch.isfinite(z.float()).all() and all(torch.isfinite(g.float()).all() for g in grads)
+    for h in check_heads:
+        ref_leaves = [t.detach()[:, h:h + 1].float().requires_grad_() for t in (q, k, v)]
+        z_r = oracle.vmonarch_attention(*ref_leaves, w.m, w.b, w.iters, recompute_tokens=w.recompute)
+        g_r = torch.autograd.grad(z_r, ref_leaves, dz[:, h:h + 1].float())
+        err = (z[:, h:h + 1].float() - z_r).abs()
+        assert max_rel_err(z[:, h:h + 1], z_r) <= 3e-2
+        assert err.max() <= 2e-2 and err.mean() <= 2e-3, (h, err.max().item(), err.mean().item())
+        for g, gr in zip(grads, g_r):
+            assert max_rel_err(g[:, h:h + 1], gr) <= 5e-2
+            gerr = (g[:, h:h + 1].float() - gr).abs().max().item()
+            assert gerr <= max(5e-2, 8e-3 * gr.abs().max().item()), (h, gerr)
+        del ref_leaves, z_r, g_r
+        torch.cuda.empty_cache()
 
 
-def test_vmonarch_config5_forward_one_head():
-    w = WORKLOADS["long720p"]  # m=32, b=3600, 3 iterations, r=3600
-    dev = torch.device("cuda")
-    q, k, v, _, _ = (t.to(dev) for t in make_inputs(w, seed=2, heads=range(0, 1)))
-    with torch.no_grad():
-        z = vmonarch_attention(q, k, v, w.m, w.b, w.iters, recompute_tokens=w.recompute)
-        z_r = oracle.vmonarch_attention(q.float(), k.float(), v.float(), w.m, w.b, w.iters,
-                                        recompute_tokens=w.recompute)
-    assert max_rel_err(z, z_r) <= 3e-2
+def test_vmonarch_config4_forty_heads():
+    # BASELINE config 4 at its full size (H=40, m=21, b=1560, D=128, 2 iterations, r=1560): the
+    # kernel routes the benchmark takes, four heads checked in full
+    _check_vmonarch_layer(WORKLOADS["dit14b"], (0, 13, 27, 39), seed=1)
+
+
+def test_vmonarch_config5_forty_heads():
+    # BASELINE config 5 at its full size (H=40, m=32, b=3600, D=128, 3 iterations, r=3600), forward
+    # and backward, two heads checked in full
+    _check_vmonarch_layer(WORKLOADS["long720p"], (0, 39), seed=2)

@@ -1,6 +1,12 @@
 """VMonarch attention on the B200 against the fp32 oracle (the reference's own fp32 graph) and the
-reference's golden vectors. Tolerances follow tests/test_vmonarch.py:45-66 (max-relative: z 3e-2,
-gradients 5e-2)."""
+reference's golden vectors.
+
+Tolerances, checked both ways:
+  reference convention (tests/test_vmonarch.py:45-66): max|x - ref| <= tol * max|ref|, z 3e-2,
+      gradients 5e-2;
+  north-star absolute bounds: z max-abs 2e-2 and mean-abs 2e-3; gradients max-abs 5e-2 (floored
+      at 8e-3 * max|grad|, the bf16 rounding of large gradients).
+"""
 import pytest
 import torch
 import torch.nn.functional as F
@@ -28,9 +34,15 @@ def run_oracle(q, k, v, dz, m, b, iters, r, device="cpu"):
 
 
 def check(got, ref):
-    assert max_rel_err(got[0], ref[0]) <= 3e-2
+    """got, ref: [z, dq, dk, dv] (ref in fp32)."""
+    z, z_r = got[0].float(), ref[0].float()
+    assert max_rel_err(z, z_r) <= 3e-2
+    err = (z - z_r).abs()
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max().item(), err.mean().item())
     for a, b in zip(got[1:], ref[1:]):
         assert max_rel_err(a, b) <= 5e-2
+        gerr = (a.float() - b.float()).abs().max().item()
+        assert gerr <= max(5e-2, 8e-3 * b.float().abs().max().item()), gerr
 
 
 @pytest.mark.parametrize("name", VM_GOLDEN)
@@ -107,13 +119,24 @@ def test_fp16_vmonarch_head_dim_128(H, m, b, iters, r):
 
 
 def test_module_readme_usage():
+    # BASELINE config 2 (the README shape): B=2, H=4, m=16, b=256, D=128, 2 iterations, r=256,
+    # forward and backward through the module; two (batch, head) slices checked in full against the
+    # fp32 oracle evaluated on the GPU
     attn = VMonarchAttention(num_blocks=16, block_size=256, num_iters=2)
     B, H, N, D = 2, 4, 16 * 256, 128
-    q, k, v = (torch.randn(B, H, N, D, dtype=torch.bfloat16, device="cuda") for _ in range(3))
+    gen = torch.Generator(device="cuda").manual_seed(5)
+    q, k, v = (torch.randn(B, H, N, D, dtype=torch.bfloat16, device="cuda", generator=gen).requires_grad_()
+               for _ in range(3))
+    dz = torch.randn(B, H, N, D, device="cuda", generator=gen).bfloat16()
     o = attn(q, k, v, recompute_tokens=256)
+    grads = torch.autograd.grad(o, (q, k, v), dz)
     assert o.shape == (B, H, N, D) and o.dtype == torch.bfloat16 and torch.isfinite(o.float()).all()
-    ref = oracle.vmonarch_attention(q[:1, :1].float(), k[:1, :1].float(), v[:1, :1].float(), 16, 256, 2, 256)
-    assert max_rel_err(o[:1, :1].float(), ref) <= 3e-2
+    for bi, h in ((0, 0), (1, 3)):
+        sl = (slice(bi, bi + 1), slice(h, h + 1))
+        leaves = [t.detach()[sl].float().requires_grad_() for t in (q, k, v)]
+        ref = oracle.vmonarch_attention(*leaves, 16, 256, 2, 256)
+        ref_g = torch.autograd.grad(ref, leaves, dz[sl].float())
+        check([o[sl]] + [g[sl] for g in grads], [ref.detach(), *ref_g])
 
 
 def test_inference_mode_saves_nothing():
