@@ -16,13 +16,20 @@ impl reference  the reference's CPU path (the fp32 oracle restating the referenc
                 on the host cores, on a bounded sample (whole heads) of the same workload.
 impl triton     the reference's own Triton kernels (installed in baseline/_ref) on the same GPU;
                 reported for comparison, not part of the driver's contract.
-Multi-GPU (torchrun): (batch x head) units are sharded with no collective on the hot path;
-`--scaling weak` (default) gives every rank one full layer, `strong` splits one layer's heads.
+Multi-GPU (torchrun): (batch x head) units are sharded with no collective on the hot path.
+`--scaling strong` (default) splits one layer's heads over the ranks (rank g of N runs heads
+[g*H/N, (g+1)*H/N)); after the timed region the outputs and gradients of every head are gathered
+over NCCL and rank 0 checks two of them against its own single-GPU run. `--scaling weak` gives
+every rank one full layer.
+At N = 1 the line also carries the FlashEntropyAttention forward on the fea32k configuration
+(B=1, H=24, N=32768, D=128), timed with CUDA events beside the reference's Triton forward when
+baseline/_ref holds the reference.
 """
 from __future__ import annotations
 
 import argparse
 import contextlib
+import importlib.util
 import json
 import os
 import statistics
@@ -37,8 +44,21 @@ import torch
 ROOT = Path(__file__).resolve().parent
 sys.path.insert(0, str(ROOT))
 
-from vmonarch_b200 import shard  # noqa: E402
-from vmonarch_b200.configs import WORKLOADS, Workload, make_inputs  # noqa: E402
+
+
+def _standalone(name: str, rel: str):
+    """Loads one self-contained module of the package by path, without the package __init__ (which
+    loads the CUDA library): the reference arm must not map this repository's library."""
+    spec = importlib.util.spec_from_file_location(name, ROOT / rel)
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+shard = _standalone("_vmb_bench_shard", "vmonarch_b200/shard.py")
+_configs = _standalone("_vmb_bench_configs", "vmonarch_b200/configs.py")
+WORKLOADS, Workload, make_inputs = _configs.WORKLOADS, _configs.Workload, _configs.make_inputs
 
 METRIC = "VMonarch fwd+bwd effective TFLOP/s (N~32K, H=40, D=128, bf16)"
 
@@ -50,13 +70,16 @@ def parse_args():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference", "triton"], default="ours")
     ap.add_argument("--workload", choices=sorted(WORKLOADS), default="dit14b")
-    ap.add_argument("--scaling", choices=["weak", "strong"], default="weak")
+    ap.add_argument("--scaling", choices=["weak", "strong"], default="strong")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--heads", type=int, default=0, help="run only this many heads of the layer (profiling)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--graph", action="store_true",
                     help="time `value` as replays of one CUDA graph holding the whole step (launch-bound sizes)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-verify", action="store_true", help="skip the gather + single-GPU check after timing")
+    ap.add_argument("--no-fea-forward", action="store_true", help="skip the fea32k forward timing (N = 1)")
+    ap.add_argument("--fwd-only", action="store_true", help="impl triton: time the forward alone")
     ap.add_argument("--cpu-budget-s", type=float, default=150.0, help="wall-clock cap of the CPU reference arm")
     return ap.parse_args()
 
@@ -317,8 +340,11 @@ def roofline(per: dict) -> dict:
 
 
 # ----------------------------------------------------------------------------------------- CPU
-def cpu_reference_sample(w: Workload, seed: int, budget_s: float, steps: int, warmup: int) -> dict:
-    """The reference's CPU path (fp32 oracle) on whole heads of the workload; TFLOP/s of fwd+bwd."""
+def cpu_reference_sample(w: Workload, seed: int, budget_s: float, steps: int, warmup: int,
+                         min_seconds: float = 0.0) -> dict:
+    """The reference's CPU path (fp32 oracle) on whole heads of the workload; TFLOP/s of fwd+bwd.
+    `warmup` untimed samples (at most one), then at least `steps` timed samples and at least
+    `min_seconds` of timed work, stopping early only when `budget_s` of wall clock is spent."""
     import oracle
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
@@ -337,7 +363,7 @@ def cpu_reference_sample(w: Workload, seed: int, budget_s: float, steps: int, wa
     for _ in range(min(warmup, 1)):
         one()
     times = []
-    while len(times) < max(steps, 1):
+    while len(times) < max(steps, 1) or sum(times) < min_seconds:
         t = time.perf_counter()
         one()
         times.append(time.perf_counter() - t)
@@ -377,26 +403,123 @@ def l2_note(w: Workload) -> str:
     return f"not flushed: q is {q_bytes / 2**20:.0f} MB, the step's working set may stay in L2 (small, launch-bound size)"
 
 
+def data_note(w: Workload) -> str:
+    if w.shared == "frame":
+        return f"synthetic (seeded N(0,1) + per-frame shared mean, std {w.shared_std})"
+    if w.shared == "block1024":
+        return f"synthetic (seeded N(0,1) + per-1024-token-block shared component, std {w.shared_std})"
+    return "synthetic (seeded N(0,1))"
+
+
 def base_line(args, w, n_gpus, ms, value, impl=None) -> dict:
+    """The contract's keys. `config` is built from the arguments alone, so both arms of one
+    command line report the same config."""
+    strong = args.scaling == "strong"
+    per_rank = f"{-(-w.H // n_gpus)}" if w.H % n_gpus else f"{w.H // n_gpus}"
     line = {"metric": METRIC, "value": round(value, 3), "unit": "TFLOP/s", "n_gpus": n_gpus, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True, "scaling": args.scaling,
-            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded N(0,1) + per-frame shared mean, std 0.3)",
+            "vs_baseline": None, "dtype": "bf16", "data": data_note(w),
             "config": {"workload": w.name, "B": w.B, "H": w.H, "num_blocks": w.m, "block_size": w.b, "N": w.N,
                        "D": w.D, "num_iters": w.iters, "recompute_tokens": w.recompute,
-                       "layers_per_job": n_gpus if args.scaling == "weak" else 1,
-                       "parallelism": f"heads x{n_gpus}, no collective",
-                       "l2": l2_note(w)}}
+                       "layers_per_job": 1 if strong else n_gpus,
+                       "parallelism": (f"heads split over {n_gpus} GPUs ({per_rank} per GPU), no collective on the "
+                                       "hot path" if strong else f"one full layer per GPU x{n_gpus}, no collective"),
+                       "l2": l2_note(w), "cuda_graph": bool(args.graph)}}
     if impl:
         line["impl"] = impl
     return line
 
 
+def verify_shards(w: Workload, step, dev, info, device, seed: int) -> dict:
+    """Multi-GPU check, outside the timed region: one more step on every rank, an NCCL all_gather of
+    z (or o) and the three input gradients of every head, then rank 0 runs two heads on its GPU
+    alone (across the boundary between ranks 0 and 1 when N > 1) and compares. Heads are
+    independent problems, but the kernels' work split depends on how many heads a call holds, so
+    the comparison allows fp32-summation-order differences (1e-2 of max|ref| + 1e-3)."""
+    out, grads = step(*dev)
+    names = ("z" if w.kind == "vmonarch" else "o", "dq", "dk", "dv")
+    # units on dim 0: (B, Hs, N, C) -> (Hs, B, N, C)
+    local = [t.detach().transpose(0, 1).contiguous() for t in (out, *grads)]
+    del out, grads
+    full = [shard.gather_units(t, w.H, info.world) for t in local]
+    del local
+    res = {"gathered": list(names), "heads_gathered": w.H, "collective": "all_gather" if info.world > 1 else "none"}
+    if info.rank == 0:
+        h0 = max(shard.unit_range(w.H, 1, info.world).start - 1, 0) if info.world > 1 else 0
+        h0 = min(h0, w.H - 2)
+        q, k, v, do, de = make_inputs(w, seed=seed, heads=range(h0, h0 + 2))
+        ref_dev = [t.to(device) for t in (q, k, v, do, de)]
+        ref_dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(ref_dev)]
+        r_out, r_grads = step(*ref_dev)
+        ok, diffs = True, {}
+        for n, got, want in zip(names, full, (r_out, *r_grads)):
+            want = want.detach().transpose(0, 1).float()
+            err = (got[h0:h0 + 2].float() - want).abs().max().item()
+            tol = 1e-2 * want.abs().max().item() + 1e-3
+            diffs[n] = round(err, 6)
+            ok = ok and err <= tol and bool(torch.isfinite(got.float()).all())
+        res.update({"heads_checked": [h0, h0 + 1], "max_abs_diff": diffs, "ok": ok,
+                    "checksum_abs_sum": {n: round(t.float().abs().sum().item(), 3) for n, t in zip(names, full)}})
+    del full
+    shard.barrier()
+    return res
+
+
+def fea_forward_probe(args, device) -> dict:
+    """FlashEntropyAttention forward at the fea32k configuration (B=1, H=24, N=32768, D=128; the
+    configuration the forward-throughput target is quoted on): this library's forward and, when
+    baseline/_ref holds the reference, the reference's Triton forward on the same inputs, each with
+    3 warm-up calls (the reference autotunes on its first) and the mean of 10 timed calls (CUDA
+    events on the current stream)."""
+    import vmonarch_b200 as api
+    w = WORKLOADS["fea32k"]
+    q, k, v, _, _ = (t.to(device) for t in make_inputs(w, seed=args.seed))
+    flops = w.flops()["fwd"]
+    peaks, src = load_peaks()
+
+    def timed(fn, n=10, warm=3):
+        with torch.no_grad():
+            for _ in range(warm):
+                fn()
+            torch.cuda.synchronize(device)
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(n):
+                fn()
+            e.record()
+            torch.cuda.synchronize(device)
+        return s.elapsed_time(e) / n
+
+    ms = timed(lambda: api.flash_entropy_attention(q, k, v))
+    tf = flops / (ms * 1e-3) / 1e12
+    res = {"workload": "fea32k forward (B=1, H=24, N=32768, D=Dv=128)", "flops": flops, "ms": round(ms, 4),
+           "tflops": round(tf, 2), "frac_of_measured_burst": round(tf / peaks["bf16_tflops"], 4),
+           "frac_of_nominal_2250": round(tf / 2250.0, 4), "peak_source": src}
+    ref_dir = ROOT / "baseline" / "_ref"
+    if (ref_dir / "video_monarch_attention").is_dir():
+        sys.path.insert(0, str(ref_dir))
+        try:
+            import video_monarch_attention as ref
+            rms = timed(lambda: ref.flash_entropy_attention(q, k, v))
+            res["triton_reference_ms"] = round(rms, 4)
+            res["triton_reference_tflops"] = round(flops / (rms * 1e-3) / 1e12, 2)
+        except Exception as exc:  # pragma: no cover - depends on the box
+            res["triton_reference"] = f"unavailable: {type(exc).__name__}: {str(exc).splitlines()[0][:160]}"
+        finally:
+            sys.path.remove(str(ref_dir))
+    else:
+        res["triton_reference"] = "unavailable: baseline/_ref does not hold the reference"
+    del q, k, v
+    return res
+
+
 def run_ours(args, info, device):
     import vmonarch_b200 as api
-    from vmonarch_b200 import ops
     w = restrict_heads(WORKLOADS[args.workload], args.heads)
     heads, seed_off, layers = unit_plan(w, info, args.scaling)
     q, k, v, do, de = make_inputs(w, seed=args.seed + seed_off, heads=heads, pin=True)
+    if w.kind == "vmonarch":
+        de = de[..., :0]  # not an input of the VMonarch step: nothing to copy
     dev = [t.to(device, non_blocking=True) for t in (q, k, v, do, de)]
     dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(dev)]
     step = make_step(w, api)
@@ -428,28 +551,52 @@ def run_ours(args, info, device):
         ms_e2e = time_e2e(step, (q, k, v, do, de), n_e2e, device)
         ms_e2e = shard.max_over_ranks(ms_e2e, device)
         h2d = sum(t.numel() * t.element_size() for t in (q, k, v, do, de))
+        h2d_job = h2d * info.world if args.scaling == "weak" else sum(
+            t.numel() * t.element_size() // max(n_local, 1) * w.H for t in (q, k, v, do, de))
         e2e = {"value": round(flops_job / (ms_e2e * 1e-3) / 1e12, 3), "unit": "TFLOP/s",
-               "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,
-               "steps": n_e2e,
-               "method": "every step copies its inputs from pinned host memory (on a copy stream, "
-                         "overlapping the previous step's compute, double-buffered) and reads its loss back; "
-                         "the first step's copy and the last step's compute are inside the timed region"}
+               "ms_per_step": round(ms_e2e, 3), "h2d_bytes_per_step": h2d_job, "d2h_bytes_per_step": 4 * info.world,
+               "h2d_bytes_per_rank": h2d, "steps": n_e2e,
+               "method": "every step copies its inputs (each rank its own heads) from pinned host memory (on a "
+                         "copy stream, overlapping the previous step's compute, double-buffered) and reads its "
+                         "loss back; the first step's copy and the last step's compute are inside the timed region"}
+
+    verification = None
+    if not args.no_verify and args.scaling == "strong" and w.H >= 2:
+        verification = verify_shards(w, step, dev, info, device, args.seed)
+
+    fea_fwd = None
+    if info.world == 1 and not args.no_fea_forward:
+        fea_fwd = fea_forward_probe(args, device)
 
     if info.rank != 0:
         return None
     line = base_line(args, w, info.world, ms_max, value)
     f = w.flops()
-    line["config"]["cuda_graph"] = bool(args.graph)
     line["dense_equivalent_tflops"] = round(3.5 * f["dense_fwd"] * n_local / w.H * layers / (ms_max * 1e-3) / 1e12, 2)
     line["flops_per_step"] = flops_job
     line["roofline"] = roofline(per)
     line["e2e"] = e2e
     line["gpu_launches"] = int(launches)
     line["clocks"] = clk.summary()
+    if verification is not None:
+        line["verification"] = verification
+    if fea_fwd is not None:
+        line["fea_forward"] = fea_fwd
     line["cpu_baseline"] = None
     if info.world == 1 and not args.no_cpu_baseline:
-        line["cpu_baseline"] = cpu_reference_sample(w, args.seed, 60.0, 1, 0)
+        line["cpu_baseline"] = cpu_reference_sample(w, args.seed, 30.0, 3, 1, min_seconds=10.0)
     return line
+
+
+def repo_libraries_mapped() -> list[str]:
+    """Shared objects of this repository mapped into the process (Linux /proc/self/maps)."""
+    try:
+        maps = Path("/proc/self/maps").read_text()
+    except OSError:
+        return []
+    root = str(ROOT)
+    return sorted({ln.split()[-1] for ln in maps.splitlines() if ln.split() and ln.split()[-1].startswith(root)
+                   and ".so" in ln.split()[-1]})
 
 
 def run_reference(args, info):
@@ -461,17 +608,17 @@ def run_reference(args, info):
     line = base_line(args, w, info.world, ms, cpu["value"], impl="reference")
     line["value"] = cpu["value"]  # the same figure as cpu_baseline and e2e, not re-rounded
     line["steps"] = cpu["timed_samples"]
-    line["config"]["l2"] = "host cores (no GPU cache involved)"
     line["cpu_baseline"] = cpu
     line["e2e"] = {"value": cpu["value"], "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}
     line["gpu_launches"] = 0
+    line["repo_libraries_mapped"] = repo_libraries_mapped()
     return line
 
 
 def run_triton(args, info, device):
     """The reference's own Triton path from baseline/_ref on the same GPU (comparison only).
     If its backward cannot launch on this GPU (the dit14b last R step needs more shared memory
-    than a B200 has), the forward alone is timed and the line says so."""
+    than a B200 has), or with --fwd-only, the forward alone is timed and the line says so."""
     ref_dir = ROOT / "baseline" / "_ref"
     sys.path.insert(0, str(ref_dir))
     try:
@@ -485,13 +632,17 @@ def run_triton(args, info, device):
     dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(dev)]
     full = make_step(w, ref)
     mode, note = "forward+backward", None
-    try:
-        full(*dev)
-        torch.cuda.synchronize(device)
-        step = full
-    except Exception as exc:  # the reference's Triton backward may not fit this GPU
-        note = f"reference backward failed on this GPU: {type(exc).__name__}: {str(exc).splitlines()[0][:160]}"
+    step = full
+    if args.fwd_only:
         mode = "forward only"
+    else:
+        try:
+            full(*dev)
+            torch.cuda.synchronize(device)
+        except Exception as exc:  # the reference's Triton backward may not fit this GPU
+            note = f"reference backward failed on this GPU: {type(exc).__name__}: {str(exc).splitlines()[0][:160]}"
+            mode = "forward only"
+    if mode == "forward only":
         if w.kind == "vmonarch":
             def step(q, k, v, do, de):
                 with torch.no_grad():
