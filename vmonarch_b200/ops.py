@@ -6,10 +6,18 @@ taken from the tensors. Work is enqueued on the current torch stream of that dev
 from __future__ import annotations
 
 import ctypes
+import os
 
 import torch
 
 from . import _native as N
+
+# Upper bound (bytes) of the workspace one backward call allocates. A call's preferred workspace can
+# hold a dS^T buffer (2 bytes per query x key: 4.5 GB for the last R step of the 14B-class layer,
+# ~35 GB for the 720p-class one); above the bound the call is issued over chunks of its batch that
+# each fit, reusing one workspace, or with the minimal workspace (the dQ kernel that recomputes S
+# and dP) when no chunk size keeps the dS^T route. VMONARCH_B200_WORKSPACE_LIMIT overrides it.
+_workspace_limit = int(os.environ.get("VMONARCH_B200_WORKSPACE_LIMIT", 16 << 30))
 
 # Optional per-call timer: a callable (name, flops_or_None) -> context manager, installed by the
 # benchmark to bracket each C-ABI call with CUDA events on the current stream.
@@ -116,10 +124,80 @@ def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, e
             t3 = _flat3(t)
             setattr(a, name, t3.data_ptr())
             setattr(a, name + "_bs", _bs(t3))
-    nbytes = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a))
-    ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    chunk, nbytes = bwd_plan(a)
+    try:
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
+    except torch.OutOfMemoryError:
+        # no room for the preferred workspace: one call with the minimal one
+        chunk, nbytes = a.batch, N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a))
+        ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
-    _call("vmb_fea_bwd", N.lib.vmb_fea_bwd, a, q.device)
+    if chunk >= a.batch:
+        _call("vmb_fea_bwd", N.lib.vmb_fea_bwd, a, q.device)
+        return
+    for start in range(0, a.batch, chunk):
+        _call("vmb_fea_bwd", N.lib.vmb_fea_bwd, _bwd_chunk(a, start, min(chunk, a.batch - start)), q.device)
+
+
+def set_workspace_limit(nbytes: int) -> None:
+    """Sets the upper bound (bytes) of one backward call's workspace (see ``bwd_plan``)."""
+    global _workspace_limit
+    _workspace_limit = int(nbytes)
+
+
+def workspace_limit() -> int:
+    return _workspace_limit
+
+
+def bwd_plan(a: N.FeaBwdArgs) -> tuple[int, int]:
+    """(sequences per call, workspace bytes) of a backward call under the workspace bound: the whole
+    batch with its preferred workspace when that fits; else the fewest equal batch chunks whose
+    preferred workspace fits and still holds the dS^T buffer; else the whole batch with the minimal
+    workspace."""
+    pref = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a))
+    low = N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a))
+    batch = a.batch
+    if pref <= _workspace_limit or pref <= low or batch <= 1:
+        return batch, pref
+    b = _copy_args(a)
+    c = max(2, -(-pref // max(_workspace_limit, 1)))
+    while c <= batch:
+        b.batch = -(-batch // c)
+        p = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(b))
+        if p <= _workspace_limit:
+            if p > N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(b)):
+                return b.batch, p
+            break  # chunks this small no longer take the dS^T route
+        c += 1
+    return batch, low
+
+
+def _copy_args(a):
+    b = type(a)()
+    ctypes.memmove(ctypes.byref(b), ctypes.byref(a), ctypes.sizeof(a))
+    return b
+
+
+def _bwd_chunk(a: N.FeaBwdArgs, start: int, count: int) -> N.FeaBwdArgs:
+    """The arguments of sequences [start, start + count) of a backward call (same workspace)."""
+    b = _copy_args(a)
+    b.batch = count
+    g = 4 if a.grad_mode in (1, 2) else 2  # element size of the gradients
+
+    def off(name, stride_elems, elem):
+        base = getattr(a, name)
+        if base:
+            setattr(b, name, base + start * stride_elems * elem)
+
+    for name, bs in (("q", "q_bs"), ("k", "k_bs"), ("v", "v_bs"), ("v2", "v2_bs"), ("o", "o_bs"), ("dout", "do_bs")):
+        off(name, getattr(a, bs), 2)
+    for name in ("lse", "ent", "dent", "delta"):
+        off(name, a.n_q, 4)
+    for name in ("grad_q", "grad_k", "grad_v", "grad_v2"):
+        off(name, getattr(a, name + "_bs"), g)
+    for name in ("fin_q", "fin_k", "fin_v", "fin_v2"):
+        off(name, getattr(a, name + "_bs"), 4)
+    return b
 
 
 def _lstep_args(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, last: bool, skip_rows: int):
