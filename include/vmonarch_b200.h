@@ -160,9 +160,14 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream);
  * cannot hand over a workspace: plugins whose enqueue hook must not allocate because the host
  * framework owns all device memory, foreign-language bindings that can only pass the user's
  * tensors, and pipelines that cannot afford cudaMalloc inside a step.
- *  - Calls whose workspace need (vmb_fea_bwd_workspace_bytes) exceeds 32 MiB return VMB_EINVAL.
+ *  - Calls whose minimal workspace (vmb_fea_bwd_min_workspace_bytes) exceeds 32 MiB return
+ *    VMB_EINVAL. A call whose preferred workspace (vmb_fea_bwd_workspace_bytes, which adds the
+ *    dS^T buffer of the dQ-from-dS route) also fits takes that route; otherwise it runs the dQ
+ *    kernel that recomputes S and dP, with the same results.
  *  - The first call on a device looks the buffer's address up with that device current; make
- *    that first call before any stream capture begins.
+ *    that first call before any stream capture begins. The address is kept for the process: after
+ *    cudaDeviceReset (which unloads the library's module) or from a context other than the
+ *    device's primary context this entry point must not be used.
  *  - All calls share the buffer, which keeps the previous call's contents (the backward clears
  *    what must start at zero). Calls that overlap on the GPU race on it: serialise them.
  *  - Calls no cudaMalloc, cudaFree or other allocating routine.

@@ -13,9 +13,14 @@
 // Limits and contract:
 //  - The scratch is kNoAllocScratchBytes (32 MiB) per device, a static __device__ array: every GPU
 //    on which the library's module is loaded holds it until the process exits. Calls whose
-//    workspace need (vmb_fea_bwd_workspace_bytes) exceeds it are rejected with VMB_EINVAL.
+//    minimal workspace (vmb_fea_bwd_min_workspace_bytes) exceeds it are rejected with
+//    VMB_EINVAL; a call whose preferred workspace (with the dS^T buffer of the dQ-from-dS route)
+//    also fits takes that route, otherwise the dQ kernel that recomputes S and dP.
 //  - The first call on a device looks the array's device address up (cudaGetSymbolAddress) with
-//    that device current; make that first call before any stream capture begins.
+//    that device current; make that first call before any stream capture begins. The address is
+//    cached per device ordinal for the life of the process, so the entry point must not be used
+//    after cudaDeviceReset (which unloads the module and frees the array) or from a context other
+//    than the device's primary context.
 //  - All calls share the one array and it keeps the previous call's contents; the backward clears
 //    what must start at zero (the dQ accumulator) on every call. Calls whose work overlaps on the
 //    GPU (different streams, or different host threads on the same device) race on the array and
