@@ -26,14 +26,14 @@
 extern "C" {
 #endif
 
-#define VMB_ABI_VERSION 5
+#define VMB_ABI_VERSION 6
 
 #define VMB_DTYPE_BF16 0
 #define VMB_DTYPE_F16 1
 
 #define VMB_OK 0
 #define VMB_EINVAL 1   /* malformed argument: null pointer, bad size, misalignment */
-#define VMB_ENOTSUP 2  /* head dimensions without a kernel */
+#define VMB_ENOTSUP 2  /* head dimensions without a kernel, or a strided layout a kernel cannot take */
 #define VMB_ECUDA 3    /* CUDA runtime error while launching */
 
 /* ABI version (VMB_ABI_VERSION of the library that was loaded). */
@@ -49,9 +49,42 @@ const char* vmb_last_error(void);
  * are then invalid. No counterpart in the reference (Triton kernels have no such check). */
 int vmb_device_status(void* stream, int32_t* out);
 
+/* Test hook of the pipeline-timeout path; no counterpart in the reference. wait_cycles > 0
+ * shortens the tcgen05 forward kernels' pipeline wait limit to that many SM cycles; hold_loads != 0
+ * (only with 0 < wait_cycles <= 1e8) makes their load producers issue no copy, so the consumers'
+ * first waits run out: the kernels record their codes (vmb_device_status), drain, free their
+ * tensor memory and exit with their outputs invalid. (0, 0) restores normal operation. The
+ * setting is process-wide and read at each vmb_fea_fwd call; it exists for tests only. */
+int vmb_test_pipeline_timeout(int64_t wait_cycles, int32_t hold_loads);
+
 /* Number of kernels this library has launched in the process so far (all threads, all devices).
  * Diagnostic with no reference counterpart: the benchmark reports it as its launch count. */
 uint64_t vmb_kernel_launches(void);
+
+/*
+ * Strided layouts (ABI version 6). By default every tensor is dense [batch][rows][cols] with the
+ * batch stride given in its *_bs field. A call may instead pass a layout that gives each tensor a
+ * view: element (s, r, c) of batch entry s, row r, column c lies at
+ *     c + r * row + (s % n1) * s1 + (s / n1 % n2) * s2 + (s / (n1 * n2)) * s3
+ * elements from the tensor's base, with (n1, n2) shared by the call's tensors (batch must be a
+ * multiple of n1 * n2). This is how token-major callers are served without transposes: the
+ * reference's Video-DiT caller holds tokens as (B, N, H, D) (README.md:74-76), whose head h of
+ * batch b is rows of stride H * D starting at (b * N * H + h) * D, so FlashEntropyAttention over
+ * its B * H sequences is the view {H * D, D, 0, N * H * D} with (n1, n2) = (H, 1), and the VMonarch
+ * R step over its B * H * m grid rows of b tokens is {H * D, b * H * D, D, N * H * D} with
+ * (n1, n2) = (m, H). Strides are in elements and multiples of 8 (4 for fp32 tensors); row >= cols.
+ * Statistics (lse, ent, dent, delta) stay dense [batch][rows] in every layout. Only the D = 128
+ * kernels take non-uniform views (a view is uniform when row == cols and entry s starts at s * X);
+ * other head dimensions return VMB_ENOTSUP for them.
+ */
+typedef struct vmb_view {
+  int64_t row, s1, s2, s3;
+} vmb_view;
+
+typedef struct vmb_fea_layout {
+  int64_t n1, n2;
+  vmb_view q, k, v, v2, o, dout, grad_q, grad_k, grad_v, grad_v2, fin_q, fin_k, fin_v, fin_v2;
+} vmb_fea_layout;
 
 /*
  * FlashEntropyAttention forward over `batch` independent sequences:
@@ -61,7 +94,7 @@ uint64_t vmb_kernel_launches(void);
  * (video_monarch_attention/kernel.py:346-353) and the F.pad / slice of flash_entropy_attention
  * (kernel.py:399-402): sequences of any length are handled without padding. The optional second
  * value tensor replaces the torch.cat([kg, vg], -1) of the last R step (vmonarch.py:50).
- * Shapes: d in {64, 128}; dv in {64, 128, 256} with dv a multiple of d (the reference requires
+ * Shapes: d, dv in {16, 32, 64, 128, 256} with dv a multiple of d (the reference requires
  * Dv % D == 0 for its backward, kernel.py:260). o may be a strided view (o_bs) into a larger
  * tensor, which is how the exact first-frame recompute writes straight into z.
  * workspace / workspace_bytes are optional (NULL / 0 is valid). With a workspace of
@@ -84,6 +117,8 @@ typedef struct vmb_fea_fwd_args {
   int32_t d, dv, dv1, dtype;
   float sm_scale;
   void* workspace;  int64_t workspace_bytes;  /* optional, see above (ABI version 2) */
+  const vmb_fea_layout* layout;  /* optional strided layout of q, k, v, v2, o (ABI version 6);
+                                    NULL: dense with the *_bs batch strides */
 } vmb_fea_fwd_args;
 
 /* Workspace that lets vmb_fea_fwd split long key ranges (0 when it would not split). No
@@ -141,6 +176,8 @@ typedef struct vmb_fea_bwd_args {
   const float* fin_k;  int64_t fin_k_bs;
   const float* fin_v;  int64_t fin_v_bs;
   const float* fin_v2; int64_t fin_v2_bs;
+  const vmb_fea_layout* layout;  /* optional strided layout of every tensor but the statistics
+                                    (ABI version 6); NULL: dense with the *_bs batch strides */
 } vmb_fea_bwd_args;
 
 int64_t vmb_fea_bwd_workspace_bytes(const vmb_fea_bwd_args* a);
@@ -186,8 +223,17 @@ int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream);
  * backward, last == 1: dz [bh][N][dw-d] gradient of z; tokens < skip_rows carry none
  * backward outputs: dq [bh][N][d] fp32 (ADDED into, or OVERWRITTEN when dq_store != 0),
  *   dout [bh][N][dw] gradient of out.
- * m <= 64, d in {64, 128}, dw - d in {64, 128, 256} when last.
+ * m <= 64, d in {16, 32, 64, 128}, dw - d in {16, ..., 256} and a multiple of d when last.
  */
+/* Strided layout of an L-step call (ABI version 6): each tensor is a [bh][N][cols] view (rows =
+ * tokens) whose head hb starts at (hb % n1) * s1 + (hb / n1) * s3 (s2 unused); a token-major
+ * (B, N, H, D) tensor is {H * D, D, 0, N * H * D} with n1 = H. ent and delta_out stay dense. The
+ * D = 128 kernels (m <= 32) take any view; other shapes need uniform views. */
+typedef struct vmb_lstep_layout {
+  int64_t n1;
+  vmb_view q, out, u, z, du, dz, dq, dout;
+} vmb_lstep_layout;
+
 typedef struct vmb_lstep_args {
   const void* q;
   const void* out;
@@ -205,7 +251,9 @@ typedef struct vmb_lstep_args {
   int32_t dq_store;  /* backward: 1 = write dq instead of adding into it (ABI version 2) */
   float* delta_out;  /* backward, optional [bh][N] fp32: sum_c out[c] dout[c] per token, the
                         preprocessing of the R step's attention backward (its `delta`) */
+  const vmb_lstep_layout* layout;  /* optional (ABI version 6), see above; NULL: dense */
 } vmb_lstep_args;
+
 
 int vmb_lstep_fwd(const vmb_lstep_args* a, void* stream);
 int vmb_lstep_bwd(const vmb_lstep_args* a, void* stream);
@@ -214,6 +262,12 @@ int vmb_lstep_bwd(const vmb_lstep_args* a, void* stream);
  * Converts the fp32 gradient accumulators of grad_mode 1 to the element dtype. */
 int vmb_cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
                  int32_t dtype, void* stream);
+
+/* dst(s, r, c) = (dtype) src(s, r, c) over [batch][rows][cols] views with batch split (n1, n2)
+ * (ABI version 6): the fp32 accumulator of a strided (e.g. token-major) gradient converted into
+ * the caller's tensor. cols a multiple of 4; src rows 16-byte aligned, dst rows 8-byte aligned. */
+int vmb_cast_f32_view(const float* src, const vmb_view* src_view, void* dst, const vmb_view* dst_view, int64_t n1,
+                      int64_t n2, int64_t batch, int64_t rows, int64_t cols, int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

@@ -20,7 +20,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_abi():
     assert N.LIB_PATH.exists()
-    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 5
+    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 6
 
 
 def test_every_declared_symbol_is_exported_and_bound():
@@ -32,7 +32,8 @@ def test_every_declared_symbol_is_exported_and_bound():
     assert set(N.SIGNATURES) == set(names)
 
 
-STRUCTS = {"vmb_fea_fwd_args": N.FeaFwdArgs, "vmb_fea_bwd_args": N.FeaBwdArgs, "vmb_lstep_args": N.LstepArgs}
+STRUCTS = {"vmb_fea_fwd_args": N.FeaFwdArgs, "vmb_fea_bwd_args": N.FeaBwdArgs, "vmb_lstep_args": N.LstepArgs,
+           "vmb_view": N.View, "vmb_fea_layout": N.FeaLayout, "vmb_lstep_layout": N.LstepLayout}
 
 
 def test_struct_layouts_match_c_header():
@@ -136,8 +137,10 @@ def test_lstep_validation():
     a.bh, a.m, a.b, a.d, a.dw, a.dtype = 1, 65, 4, 64, 64, 0
     assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # m > 64
     a.m = 4
-    a.d = a.dw = 32
-    assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # d = 32
+    a.d = a.dw = 256
+    assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # d = 256 (D + Dv <= 256 in VMonarch)
+    a.d = a.dw = 48
+    assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # d = 48
     a.d, a.dw, a.last = 64, 100, 1
     assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # value width 36
     a.dw, a.last = 64, 0

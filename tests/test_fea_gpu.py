@@ -65,6 +65,18 @@ def test_flash_entropy_attention(N, D, Dv):
     check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
 
 
+@pytest.mark.parametrize("N", [100, 300])
+@pytest.mark.parametrize("D, Dv", [(16, 16), (16, 64), (32, 32), (32, 256), (256, 256)])
+def test_head_dims_16_32_256(N, D, Dv):
+    # the remaining head dims the reference accepts (kernel.py:324: D, Dv in {16, ..., 256},
+    # Dv % D == 0), on the warp-level MMA kernels with 64-column shared-memory rows
+    gen = torch.Generator().manual_seed(N + D + Dv)
+    q, k = (torch.randn(2, 3, N, D, generator=gen).bfloat16().float() for _ in range(2))
+    v = torch.randn(2, 3, N, Dv, generator=gen).bfloat16().float()
+    do, de = torch.randn(2, 3, N, Dv, generator=gen), torch.randn(2, 3, N, generator=gen)
+    check(run_cuda(q, k, v, do, de), run_oracle(q, k, v, do, de, D ** -0.5))
+
+
 @pytest.mark.parametrize("N", [1, 17, 64, 127, 129, 150, 333])
 @pytest.mark.parametrize("D", [64, 128])
 def test_ragged_and_tiny_sequences(N, D):

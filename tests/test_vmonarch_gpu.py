@@ -62,6 +62,16 @@ def test_vmonarch_attention(m, b, num_iters):
     check(run_cuda(q, k, v, dz, m, b, num_iters, b), run_oracle(q, k, v, dz, m, b, num_iters, b))
 
 
+@pytest.mark.parametrize("D, m, b, iters, r", [(16, 4, 100, 2, 100), (32, 6, 70, 3, 20), (32, 40, 24, 2, 0)])
+def test_vmonarch_head_dims_16_32(D, m, b, iters, r):
+    # head dims 16 and 32 (the reference accepts them, kernel.py:324): warp-level MMA attention and
+    # the generic L step (m = 40 > 32 included)
+    gen = torch.Generator().manual_seed(D * m + b)
+    q, k, v = (torch.randn(1, 2, m * b, D, generator=gen).bfloat16().float() for _ in range(3))
+    dz = torch.randn(1, 2, m * b, D, generator=gen)
+    check(run_cuda(q, k, v, dz, m, b, iters, r), run_oracle(q, k, v, dz, m, b, iters, r))
+
+
 @pytest.mark.parametrize("m, b, iters, r", [(16, 256, 2, 256), (21, 200, 2, 200), (5, 130, 3, 0), (1, 64, 2, 10)])
 def test_vmonarch_head_dim_128(m, b, iters, r):
     gen = torch.Generator().manual_seed(m * b)

@@ -5,6 +5,7 @@ over its batch, or falls back to the minimal workspace when no chunk keeps that 
 import ctypes
 
 import pytest
+import torch
 
 from vmonarch_b200 import _native as N
 from vmonarch_b200 import ops
@@ -43,7 +44,7 @@ def test_720p_layer_is_chunked_under_the_bound(limit):
         assert pref > 16 << 30
         chunk, nbytes = ops.bwd_plan(a)
         assert chunk < a.batch and nbytes <= 16 << 30
-        b = ops._bwd_chunk(a, 0, chunk)
+        b = _args(chunk, a.n_q, a.n_kv, a.dv, a.v_is_k, a.grad_mode)
         assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(b)) == nbytes
         assert nbytes > N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(b))  # still the dS^T route
 
@@ -54,18 +55,49 @@ def test_bound_below_any_useful_chunk_uses_the_minimal_workspace(limit):
     assert ops.bwd_plan(a) == (40, N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a)))
 
 
-def test_chunk_offsets_every_pointer_by_its_batch_stride():
-    a = _args(10, 100, 300, 256, True, grad_mode=1)
-    base = 1 << 40
-    for i, name in enumerate(("q", "k", "v", "v2", "o", "dout", "lse", "ent", "dent", "delta", "grad_q", "grad_k",
-                              "grad_v2", "fin_q")):
-        setattr(a, name, base + (i << 32))
-    a.v2_bs, a.o_bs, a.do_bs = 300 * 128, 100 * 256, 100 * 256
-    a.grad_q_bs, a.grad_k_bs, a.grad_v2_bs, a.fin_q_bs = 100 * 128, 300 * 128, 300 * 128, 100 * 128
-    b = ops._bwd_chunk(a, 3, 4)
-    assert b.batch == 4 and a.batch == 10
-    assert b.q - a.q == 3 * a.q_bs * 2 and b.v2 - a.v2 == 3 * a.v2_bs * 2 and b.dout - a.dout == 3 * a.do_bs * 2
-    assert b.lse - a.lse == 3 * 100 * 4 and b.delta - a.delta == 3 * 100 * 4
-    assert b.grad_k - a.grad_k == 3 * a.grad_k_bs * 4  # fp32 gradients in grad_mode 1
-    assert b.fin_q - a.fin_q == 3 * a.fin_q_bs * 4
-    assert b.grad_v is None and b.fin_k is None  # absent pointers stay absent
+def test_chunks_follow_the_middle_batch_dimension(limit):
+    # VMonarch's last R step in (B, H, m) batch form: chunks are whole heads (m grid rows each) and
+    # never cross a batch entry
+    a = _args(2 * 40 * 32, 3600, 3600, 256, True, grad_mode=2)
+    limit(16 << 30)
+    chunk, nbytes = ops.bwd_plan(a, unit=32, group=40 * 32)
+    assert chunk % 32 == 0 and chunk <= 40 * 32 and nbytes <= 16 << 30
+
+
+def test_token_major_views():
+    # a (B, N, H, D) buffer seen as (B, H, N, D): the layout the header documents
+    B, H, m, b, D = 2, 5, 3, 16, 128
+    N_ = m * b
+    base = torch.empty(B, N_, H, D, dtype=torch.bfloat16)
+    q = base.transpose(1, 2)
+    assert ops.viewable(q) and not q.is_contiguous()
+    # FlashEntropyAttention over B * H sequences: (n1, n2) = (H, B)
+    v = ops._view(q, 2)
+    assert (v.row, v.s1, v.s2, v.s3) == (H * D, D, N_ * H * D, 0) and ops._split(q.shape[:-2]) == (H, B)
+    # the R step over B * H * m grid rows of b tokens: (n1, n2) = (m, H)
+    g = q.unflatten(2, (m, b))
+    v = ops._view(g, 3)
+    assert (v.row, v.s1, v.s2, v.s3) == (H * D, b * H * D, D, N_ * H * D) and ops._split(g.shape[:-2]) == (m, H)
+    # element (s, r, c) of the view formula == torch's indexing
+    for s_ in (0, 7, B * H * m - 1):
+        c1, c2, c3 = s_ % m, s_ // m % H, s_ // (m * H)
+        r = 5
+        off = r * v.row + c1 * v.s1 + c2 * v.s2 + c3 * v.s3
+        assert g[c3, c2, c1, r].data_ptr() == base.data_ptr() + 2 * off
+
+
+def test_backward_args_of_a_chunk_slice():
+    # the arguments of chunk (heads 2..3 of batch entry 1) point at that slice's first element, with
+    # statistics rows of those sequences
+    B, H, m, b, D = 2, 4, 3, 16, 128
+    tm = lambda c: torch.empty(B, m * b, H, c, dtype=torch.bfloat16).transpose(1, 2).unflatten(2, (m, b))  # noqa: E731
+    t = dict(q=tm(D), k=tm(D), v=None, o=torch.empty(B, H, m, b, 2 * D, dtype=torch.bfloat16),
+             lse=torch.empty(B * H * m * b), grad_q=torch.empty(B, H, m, b, D))
+    t["v"] = t["k"]
+    idx = (1, slice(2, 4))
+    sub = {n: (x.view(B, H, m, b)[idx].reshape(-1) if n == "lse" else x[idx]) for n, x in t.items()}
+    a, lay = ops.bwd_args(sub, 1.0, 2, True, True)
+    assert a.batch == 2 * m and (lay.n1, lay.n2) == (m, 2)
+    assert a.q == t["q"][1, 2].data_ptr() and a.o == t["o"][1, 2].data_ptr()
+    assert a.lse == t["lse"].data_ptr() + 4 * ((1 * H + 2) * m * b)
+    assert (lay.q.row, lay.q.s1, lay.q.s2) == (H * D, b * H * D, D)

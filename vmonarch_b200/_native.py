@@ -25,7 +25,22 @@ c_vp = ctypes.c_void_p
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 
-ABI_VERSION = 5  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+ABI_VERSION = 6  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+
+
+class View(ctypes.Structure):
+    """vmb_view: element (s, r, c) at c + r*row + (s % n1)*s1 + (s / n1 % n2)*s2 + (s / (n1 n2))*s3."""
+    _fields_ = [("row", c_i64), ("s1", c_i64), ("s2", c_i64), ("s3", c_i64)]
+
+
+class FeaLayout(ctypes.Structure):
+    _fields_ = [("n1", c_i64), ("n2", c_i64)] + [(n, View) for n in (
+        "q", "k", "v", "v2", "o", "dout", "grad_q", "grad_k", "grad_v", "grad_v2", "fin_q", "fin_k", "fin_v",
+        "fin_v2")]
+
+
+class LstepLayout(ctypes.Structure):
+    _fields_ = [("n1", c_i64)] + [(n, View) for n in ("q", "out", "u", "z", "du", "dz", "dq", "dout")]
 
 
 class FeaFwdArgs(ctypes.Structure):
@@ -40,6 +55,7 @@ class FeaFwdArgs(ctypes.Structure):
         ("d", c_i32), ("dv", c_i32), ("dv1", c_i32), ("dtype", c_i32),
         ("sm_scale", ctypes.c_float),
         ("workspace", c_vp), ("workspace_bytes", c_i64),
+        ("layout", ctypes.POINTER(FeaLayout)),
     ]
 
 
@@ -67,6 +83,7 @@ class FeaBwdArgs(ctypes.Structure):
         ("fin_k", c_vp), ("fin_k_bs", c_i64),
         ("fin_v", c_vp), ("fin_v_bs", c_i64),
         ("fin_v2", c_vp), ("fin_v2_bs", c_i64),
+        ("layout", ctypes.POINTER(FeaLayout)),
     ]
 
 
@@ -82,6 +99,7 @@ class LstepArgs(ctypes.Structure):
         ("scale", ctypes.c_float), ("min_col_mass", ctypes.c_float),
         ("dq_store", c_i32),
         ("delta_out", c_vp),
+        ("layout", ctypes.POINTER(LstepLayout)),
     ]
 
 
@@ -90,6 +108,7 @@ SIGNATURES = {
     "vmb_abi_version": (ctypes.c_int, []),
     "vmb_last_error": (ctypes.c_char_p, []),
     "vmb_kernel_launches": (ctypes.c_uint64, []),
+    "vmb_test_pipeline_timeout": (ctypes.c_int, [c_i64, c_i32]),
     "vmb_device_status": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_int32)]),
     "vmb_fea_fwd_workspace_bytes": (c_i64, [ctypes.POINTER(FeaFwdArgs)]),
     "vmb_fea_fwd": (ctypes.c_int, [ctypes.POINTER(FeaFwdArgs), c_vp]),
@@ -100,6 +119,8 @@ SIGNATURES = {
     "vmb_lstep_fwd": (ctypes.c_int, [ctypes.POINTER(LstepArgs), c_vp]),
     "vmb_lstep_bwd": (ctypes.c_int, [ctypes.POINTER(LstepArgs), c_vp]),
     "vmb_cast_f32": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp]),
+    "vmb_cast_f32_view": (ctypes.c_int, [c_vp, ctypes.POINTER(View), c_vp, ctypes.POINTER(View), c_i64, c_i64, c_i64,
+                                         c_i64, c_i64, c_i32, c_vp]),
 }
 
 

@@ -56,8 +56,9 @@ struct Sm100BwdParams {
   CUtensorMap tm_a, tm_b, tm_c, tm_d;  // dkdv: K, X, Q, dO ; dq: Q, dO, K, X  (boxes of 64 cols x 64/128 rows)
   CUtensorMap tm_g0, tm_g1;            // gradient outputs (dkdv: dK, dV / dV2; dq: dQ): fp32 boxes of
                                        // 32 x 128 when added into (acc), else 16-bit boxes of 64 x 128
-  const void* dout;  // dq kernel with dO in TMEM: [batch][n_q][DW] rows read directly
-  int64_t do_bs;
+  const void* dout;  // dq kernel with dO in TMEM: [batch][n_q][DW] rows read directly (view dov)
+  View dov;
+  int n1, n2;        // batch split of every view and of the maps over caller tensors
   const float* nl;  // folded statistics planes [batch][n_pad] (fea_bwd_pre): -LSE2,
   const float* nc;  //   -sm_scale (c + g LSE2),
   const float* ng;  //   -sm_scale g
@@ -68,7 +69,7 @@ struct Sm100BwdParams {
   int acc;       // 1: fp32 gradients added into (TMA reduce-add); 2: fp32 stores; 0: 16-bit stores;
                  // 3: 16-bit stores of (fp32 accumulator tile + this call's gradient)
   float scale_log2, sm_scale;
-  float* dq;     // fused dQ: fp32 [batch][n_q][128] (batch stride dq_bs), added into
+  float* dq;     // fused dQ: dense fp32 [batch][n_q][128] with batch stride dq_bs, added into
   int64_t dq_bs;
   CUtensorMap tm_f0, tm_f1;  // acc 3: the fp32 accumulators of tm_g0 / tm_g1 (boxes of 32 x 128)
   void* ds;                  // dK/dV kernel: dS^T out [batch][ds_rows][ds_ld] (16-bit), or null
@@ -147,13 +148,13 @@ __device__ __forceinline__ void stage_acc_rows(uint32_t taddr, uint32_t stage, i
 
 // One thread, after the staging barrier: the whole 128-row tile starting at row0 of sequence bi.
 // mode 1: fp32 reduce-add; 2: fp32 store; 0: 16-bit store.
-__device__ __forceinline__ void issue_grad_tile(const CUtensorMap* tm, uint32_t stage, int row0, int bi, int mode) {
+__device__ __forceinline__ void issue_grad_tile(const CUtensorMap* tm, uint32_t stage, int row0, BIdx bi, int mode) {
   if (mode == 1) {
-    for (int c = 0; c < 4; ++c) tma_reduce_add_3d(tm, 32 * c, row0, bi, stage + c * 16384);
+    for (int c = 0; c < 4; ++c) tma_reduce_add(tm, 32 * c, row0, bi, stage + c * 16384);
   } else if (mode == 2) {
-    for (int c = 0; c < 4; ++c) tma_store_3d(tm, 32 * c, row0, bi, stage + c * 16384);
+    for (int c = 0; c < 4; ++c) tma_store(tm, 32 * c, row0, bi, stage + c * 16384);
   } else {
-    for (int a = 0; a < 2; ++a) tma_store_3d(tm, 64 * a, row0, bi, stage + a * 16384);
+    for (int a = 0; a < 2; ++a) tma_store(tm, 64 * a, row0, bi, stage + a * 16384);
   }
 }
 
@@ -225,6 +226,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bi = blockIdx.x / p.n_tiles;
+  const BIdx bx = bidx(bi, p.n1, p.n2);
   const int k0 = (blockIdx.x % p.n_tiles) * 128;
   const int nq = (p.n_q + 63) / 64;
   // Query tile of step i. With fused dQ the key tiles of a sequence start their walks at different
@@ -296,9 +298,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       prefetch_tmap(&p.tm_c);
       prefetch_tmap(&p.tm_d);
       mbar_expect_tx(BAR_KV, C::RES);
-      tma_load_3d(sRes, &p.tm_a, 0, k0, bi, BAR_KV);
-      tma_load_3d(sRes + kAtom128, &p.tm_a, 64, k0, bi, BAR_KV);
-      for (int a = 0; a < XA; ++a) tma_load_3d(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bi, BAR_KV);
+      tma_load(sRes, &p.tm_a, 0, k0, bx, BAR_KV);
+      tma_load(sRes + kAtom128, &p.tm_a, 64, k0, bx, BAR_KV);
+      for (int a = 0; a < XA; ++a) tma_load(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bx, BAR_KV);
     }
     for (int i = 0; i < nq; ++i) {
       const int s = i % NQS;
@@ -308,9 +310,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       if (lane == 0) {
         const int q0 = qtile(i) * 64;
         mbar_expect_tx(BAR_QFULL(s), C::SLOT_T + 3 * 256);
-        tma_load_3d(q_atom(s, 0), &p.tm_c, 0, q0, bi, BAR_QFULL(s));
-        tma_load_3d(q_atom(s, 1), &p.tm_c, 64, q0, bi, BAR_QFULL(s));
-        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(do_atom(s, a), &p.tm_d, 64 * a, q0, bi, BAR_QFULL(s));
+        tma_load(q_atom(s, 0), &p.tm_c, 0, q0, bx, BAR_QFULL(s));
+        tma_load(q_atom(s, 1), &p.tm_c, 64, q0, bx, BAR_QFULL(s));
+        for (int a = 0; a < C::DW / 64; ++a) tma_load(do_atom(s, a), &p.tm_d, 64 * a, q0, bx, BAR_QFULL(s));
         // the 64 queries' folded statistics: one 256-byte copy per plane (rows padded to 128)
         const int64_t r0 = (int64_t)bi * p.n_pad + q0;
         bulk_load(slot_stats(s), p.nl + r0, 256, BAR_QFULL(s));
@@ -320,14 +322,14 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         // its use, less than a DRAM round trip under this kernel's load
         if (i + NQS < nq) {
           const int qa = qtile(i + NQS) * 64;
-          tma_prefetch_3d(&p.tm_c, 0, qa, bi);
-          tma_prefetch_3d(&p.tm_c, 64, qa, bi);
-          for (int a = 0; a < C::DW / 64; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, qa, bi);
+          tma_prefetch(&p.tm_c, 0, qa, bx);
+          tma_prefetch(&p.tm_c, 64, qa, bx);
+          for (int a = 0; a < C::DW / 64; ++a) tma_prefetch(&p.tm_d, 64 * a, qa, bx);
         }
         if (p.acc == 3 && i == nq - 1) {  // the accumulator tiles the epilogue reads, into L2
           for (int c = 0; c < 4; ++c) {
-            tma_prefetch_3d(&p.tm_f0, 32 * c, k0, bi);
-            if (C::HAS_DV) tma_prefetch_3d(&p.tm_f1, 32 * c, k0, bi);
+            tma_prefetch(&p.tm_f0, 32 * c, k0, bx);
+            if (C::HAS_DV) tma_prefetch(&p.tm_f1, 32 * c, k0, bx);
           }
         }
       }
@@ -457,6 +459,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       tmem_ld32(tmem + lane_off + 384 + 64 * (j & 1) + 32 * h0, v);
       tmem_wait_ld();
       const int q0 = qtile(j) * 64 + 32 * h0;
+      // dQ is plain here (the host fuses only a dense [batch][n_q][128] dQ): batch stride dq_bs,
+      // rows of 128 floats, so the 32 reductions take immediate offsets
       float* dst = p.dq + (int64_t)bi * p.dq_bs + (int64_t)q0 * 128 + row;
       const int nv = min(32, p.n_q - q0);
 #pragma unroll
@@ -558,8 +562,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         fin_issued = true;
         mbar_expect_tx(BAR_FIN, (C::HAS_DV ? 2 : 1) * 65536);
         for (int c = 0; c < 4; ++c) {
-          tma_load_3d(stage0 + c * 16384, &p.tm_f0, 32 * c, k0, bi, BAR_FIN);
-          if (C::HAS_DV) tma_load_3d(stage1 + c * 16384, &p.tm_f1, 32 * c, k0, bi, BAR_FIN);
+          tma_load(stage0 + c * 16384, &p.tm_f0, 32 * c, k0, bx, BAR_FIN);
+          if (C::HAS_DV) tma_load(stage1 + c * 16384, &p.tm_f1, 32 * c, k0, bx, BAR_FIN);
         }
       }
       if (ok) ok = warp_wait(BAR_FIN, 0, 8);
@@ -582,8 +586,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
     fence_proxy_async_smem();
     ok = named_bar_and(1, 128 * NWG, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      issue_grad_tile(&p.tm_g0, fin ? sRes : stage0, k0, bi, fin ? 0 : p.acc);
-      if (C::HAS_DV) issue_grad_tile(&p.tm_g1, fin ? sRes + 32768 : stage1, k0, bi, fin ? 0 : p.acc);
+      issue_grad_tile(&p.tm_g0, fin ? sRes : stage0, k0, bx, fin ? 0 : p.acc);
+      if (C::HAS_DV) issue_grad_tile(&p.tm_g1, fin ? sRes + 32768 : stage1, k0, bx, fin ? 0 : p.acc);
       tma_store_commit_and_wait();
     }
     if (fin_issued) mbar_wait_drain(BAR_FIN, 0);  // loads still in flight after a timeout
@@ -650,6 +654,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
   // block -> (sequence, query tile, key chunk); chunks of one query tile add their partial dQ
   const int per_seq = p.n_tiles * p.k_split;
   const int bi = blockIdx.x / per_seq;
+  const BIdx bx = bidx(bi, p.n1, p.n2);
   const int q0 = ((blockIdx.x % per_seq) / p.k_split) * 128;
   const int kt0 = (blockIdx.x % p.k_split) * p.kt_per;  // first key tile of this chunk
   const int nk = min((p.n_kv + 127) / 128 - kt0, p.kt_per);  // >= 1 by the host's choice of split
@@ -702,10 +707,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
       if (!DOT) prefetch_tmap(&p.tm_b);
       if (XA > 0) prefetch_tmap(&p.tm_d);
       mbar_expect_tx(BAR(B_Q), C::RES);
-      tma_load_3d(sQ, &p.tm_a, 0, q0, bi, BAR(B_Q));
-      tma_load_3d(sQ + kAtom128, &p.tm_a, 64, q0, bi, BAR(B_Q));
+      tma_load(sQ, &p.tm_a, 0, q0, bx, BAR(B_Q));
+      tma_load(sQ + kAtom128, &p.tm_a, 64, q0, bx, BAR(B_Q));
       if (!DOT)
-        for (int a = 0; a < C::DW / 64; ++a) tma_load_3d(sDO + a * kAtom128, &p.tm_b, 64 * a, q0, bi, BAR(B_Q));
+        for (int a = 0; a < C::DW / 64; ++a) tma_load(sDO + a * kAtom128, &p.tm_b, 64 * a, q0, bx, BAR(B_Q));
       int karmed[NK], xarmed[NXB];
       for (int s = 0; s < NK; ++s) karmed[s] = 0;
       for (int s = 0; s < NXB; ++s) xarmed[s] = 0;
@@ -713,23 +718,23 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         const int s = j % NK;
         if (j >= NK && !mbar_wait(BAR(B_KEMPTY + s), ((j / NK) - 1) & 1, abort, &g_bwd_err, 16)) break;
         mbar_expect_tx(BAR(B_KFULL + s), C::KSLOT);
-        tma_load_3d(sK + s * C::KSLOT, &p.tm_c, 0, (kt0 + j) * 128, bi, BAR(B_KFULL + s));
-        tma_load_3d(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, (kt0 + j) * 128, bi, BAR(B_KFULL + s));
+        tma_load(sK + s * C::KSLOT, &p.tm_c, 0, (kt0 + j) * 128, bx, BAR(B_KFULL + s));
+        tma_load(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, (kt0 + j) * 128, bx, BAR(B_KFULL + s));
         if (j + NK < nk) {  // the K tile NK loads ahead into L2
-          tma_prefetch_3d(&p.tm_c, 0, (kt0 + j + NK) * 128, bi);
-          tma_prefetch_3d(&p.tm_c, 64, (kt0 + j + NK) * 128, bi);
+          tma_prefetch(&p.tm_c, 0, (kt0 + j + NK) * 128, bx);
+          tma_prefetch(&p.tm_c, 64, (kt0 + j + NK) * 128, bx);
         }
         if (p.acc == 3 && j == nk - 1)  // the accumulator tile the epilogue reads, into L2
-          for (int c = 0; c < 4; ++c) tma_prefetch_3d(&p.tm_f0, 32 * c, q0, bi);
+          for (int c = 0; c < 4; ++c) tma_prefetch(&p.tm_f0, 32 * c, q0, bx);
         karmed[s] = j / NK + 1;
         if (XA > 0) {
           const int x = j % NXB;
           if (j >= NXB && !mbar_wait(BAR(B_XEMPTY + x), ((j / NXB) - 1) & 1, abort, &g_bwd_err, 16)) break;
           mbar_expect_tx(BAR(B_XFULL + x), C::XSLOT);
           for (int a = 0; a < XA; ++a)
-            tma_load_3d(sX + x * C::XSLOT + a * kAtom128, &p.tm_d, 64 * a, (kt0 + j) * 128, bi, BAR(B_XFULL + x));
+            tma_load(sX + x * C::XSLOT + a * kAtom128, &p.tm_d, 64 * a, (kt0 + j) * 128, bx, BAR(B_XFULL + x));
           if (j + NXB < nk)
-            for (int a = 0; a < XA; ++a) tma_prefetch_3d(&p.tm_d, 64 * a, (kt0 + j + NXB) * 128, bi);
+            for (int a = 0; a < XA; ++a) tma_prefetch(&p.tm_d, 64 * a, (kt0 + j + NXB) * 128, bx);
           xarmed[x] = j / NXB + 1;
         }
       }
@@ -857,8 +862,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
     if (DOT) {
       // dO row -> TMEM (bf16 pairs): warpgroup w stages elements [EW w, EW w + EW)
       constexpr int EW = C::DW / NWG;  // elements per warpgroup (EW / 2 TMEM columns)
-      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) + (int64_t)bi * p.do_bs +
-                                                        (int64_t)(qok ? q : 0) * C::DW + EW * wg);
+      const uint4* src = reinterpret_cast<const uint4*>(static_cast<const T*>(p.dout) +
+                                                        view_offset(p.dov, p.n1, p.n2, bi, qok ? q : 0) + EW * wg);
 #pragma unroll
       for (int h = 0; h < EW / 64; ++h) {
         uint32_t w32[32];
@@ -928,7 +933,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
       if (warp == 2 && lane == 0 && ok) {
         fin_issued = true;
         mbar_expect_tx(BAR(B_FIN), 65536);
-        for (int c = 0; c < 4; ++c) tma_load_3d(sK + c * 16384, &p.tm_f0, 32 * c, q0, bi, BAR(B_FIN));
+        for (int c = 0; c < 4; ++c) tma_load(sK + c * 16384, &p.tm_f0, 32 * c, q0, bx, BAR(B_FIN));
       }
       if (ok) ok = warp_wait(BAR(B_FIN), 0, 128);
       if (ok) finalize_rows<T>(tmem + lane_off + T_DQ, sK, sQ, row, (CW / 32) * wg, (CW / 32) * (wg + 1));
@@ -939,7 +944,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
     ok = named_bar_and(1, NCT, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
       // a split key range writes its partial tile into its own slice: sequence index chunk * batch + bi
-      issue_grad_tile(&p.tm_g0, fin ? sQ : sK, q0, p.k_split > 1 ? (kt0 / p.kt_per) * p.n_seq + bi : bi,
+      issue_grad_tile(&p.tm_g0, fin ? sQ : sK, q0, p.k_split > 1 ? BIdx((kt0 / p.kt_per) * p.n_seq + bi) : bx,
                       fin ? 0 : p.acc);
       tma_store_commit_and_wait();
     }
@@ -955,12 +960,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
 // dq[bi][q] (+)= sum over chunks c (in order) of part[c][bi][q]: the split key ranges' partial tiles
 // (added into dq, or written over it in the store mode)
 __global__ void dq_split_reduce_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q, float* dq,
-                                       int64_t dq_bs, int store) {
+                                       View dqv, int n1, int n2, int store) {
   const int64_t total = batch * n_q * 32;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
     const int64_t q = rem / 32, c4 = rem % 32;
-    float4* dst = reinterpret_cast<float4*>(dq + bi * dq_bs + q * 128) + c4;
+    float4* dst = reinterpret_cast<float4*>(dq + view_offset(dqv, n1, n2, bi, q)) + c4;
     float4 acc = store ? make_float4(0.f, 0.f, 0.f, 0.f) : *dst;
     for (int c = 0; c < split; ++c) {
       const float4 v = reinterpret_cast<const float4*>(part + (((int64_t)c * batch + bi) * n_pad + q) * 128)[c4];
@@ -976,12 +981,12 @@ __global__ void dq_split_reduce_kernel(const float* part, int split, int64_t bat
 // out16[bi][q] = 16-bit(fin[bi][q] + sum over chunks c (in order) of part[c][bi][q]) (acc 3)
 template <typename T>
 __global__ void dq_split_finalize_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q,
-                                         const float* fin, int64_t fin_bs, T* out, int64_t out_bs) {
+                                         const float* fin, View finv, T* out, View outv, int n1, int n2) {
   const int64_t total = batch * n_q * 32;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
     const int64_t q = rem / 32, c4 = rem % 32;
-    float4 acc = reinterpret_cast<const float4*>(fin + bi * fin_bs + q * 128)[c4];
+    float4 acc = reinterpret_cast<const float4*>(fin + view_offset(finv, n1, n2, bi, q))[c4];
     for (int c = 0; c < split; ++c) {
       const float4 v = reinterpret_cast<const float4*>(part + (((int64_t)c * batch + bi) * n_pad + q) * 128)[c4];
       acc.x += v.x;
@@ -992,7 +997,7 @@ __global__ void dq_split_finalize_kernel(const float* part, int split, int64_t b
     uint2 w;
     w.x = Elem<T>::pack(acc.x, acc.y);
     w.y = Elem<T>::pack(acc.z, acc.w);
-    reinterpret_cast<uint2*>(out + bi * out_bs + q * 128)[c4] = w;
+    reinterpret_cast<uint2*>(out + view_offset(outv, n1, n2, bi, q))[c4] = w;
   }
 }
 
@@ -1018,6 +1023,7 @@ __global__ void __launch_bounds__(192, NS <= 3 ? 2 : 1) dq_from_ds_kernel(const 
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bi = blockIdx.x / p.n_tiles;
+  const BIdx bx = bidx(bi, p.n1, p.n2);
   const int q0 = (blockIdx.x % p.n_tiles) * 128;
   const int nkc = (p.n_kv + 63) / 64;
   const uint32_t BAR_FIN_OFF = 8u * (2 * NS + 1);
@@ -1059,12 +1065,12 @@ __global__ void __launch_bounds__(192, NS <= 3 ? 2 : 1) dq_from_ds_kernel(const 
         if (c >= NS && !mbar_wait(BAR_EMPTY(s), ((c / NS) - 1) & 1, abort, &g_bwd_err, 64)) break;
         mbar_expect_tx(BAR_FULL(s), kGemmStage);
         for (int a = 0; a < 2; ++a) {
-          tma_load_3d(stage(s) + a * kAtom64, &p.tm_a, q0 + 64 * a, 64 * c, bi, BAR_FULL(s));
-          tma_load_3d(stage(s) + (2 + a) * kAtom64, &p.tm_c, 64 * a, 64 * c, bi, BAR_FULL(s));
+          tma_load(stage(s) + a * kAtom64, &p.tm_a, q0 + 64 * a, 64 * c, bi, BAR_FULL(s));
+          tma_load(stage(s) + (2 + a) * kAtom64, &p.tm_c, 64 * a, 64 * c, bx, BAR_FULL(s));
         }
         armed[s] = c / NS + 1;
         if (p.acc == 3 && c == nkc - 1)  // the accumulator tile the epilogue reads, into L2
-          for (int x = 0; x < 4; ++x) tma_prefetch_3d(&p.tm_f0, 32 * x, q0, bi);
+          for (int x = 0; x < 4; ++x) tma_prefetch(&p.tm_f0, 32 * x, q0, bx);
       }
       for (int s = 0; s < NS; ++s)
         if (armed[s] > 0) mbar_wait_drain(BAR_FULL(s), (armed[s] - 1) & 1);
@@ -1104,7 +1110,7 @@ __global__ void __launch_bounds__(192, NS <= 3 ? 2 : 1) dq_from_ds_kernel(const 
       if (warp == 2 && lane == 0 && ok) {
         fin_issued = true;
         mbar_expect_tx(bfin, 65536);
-        for (int x = 0; x < 4; ++x) tma_load_3d(st + x * 16384, &p.tm_f0, 32 * x, q0, bi, bfin);
+        for (int x = 0; x < 4; ++x) tma_load(st + x * 16384, &p.tm_f0, 32 * x, q0, bx, bfin);
       }
       if (ok) ok = __all_sync(0xffffffffu, mbar_wait(bfin, 0, abort, &g_bwd_err, 64));
       if (ok) finalize_rows<T>(tmem + lane_off, st, out16, row, 0, 4);
@@ -1114,7 +1120,7 @@ __global__ void __launch_bounds__(192, NS <= 3 ? 2 : 1) dq_from_ds_kernel(const 
     fence_proxy_async_smem();
     ok = named_bar_and(1, 128, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      issue_grad_tile(&p.tm_g0, fin ? out16 : st, q0, bi, fin ? 0 : p.acc);
+      issue_grad_tile(&p.tm_g0, fin ? out16 : st, q0, bx, fin ? 0 : p.acc);
       tma_store_commit_and_wait();
     }
     if (fin_issued) mbar_wait_drain(bar0 + BAR_FIN_OFF, 0);  // loads still in flight after a timeout
@@ -1140,35 +1146,39 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   const bool bf16 = Elem<T>::is_bf16;
   const int xa = vk ? (dv - 128) / 64 : dv / 64;  // value atoms beyond K (vk) or V atoms
   const void* xsrc = vk ? b.v2 : b.v;
-  const int64_t xbs = vk ? b.v2_bs : b.v_bs;
+  const View xv = vk ? b.v2v : b.vv;
+  const int n1 = b.n1, n2 = b.n2;
   // ---- dK / dV: 64-query tiles (two warpgroups on alternate tiles, double-buffered S^T / dP^T)
   const int qrows = 64;
   Sm100BwdParams pa{};
-  if (!tma::make_map(&pa.tm_a, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 128)) return cudaErrorInvalidValue;
+  pa.n1 = n1;
+  pa.n2 = n2;
+  if (!tma::make_map_view(&pa.tm_a, b.k, bf16, 128, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
-    if (!tma::make_map(&pa.tm_b, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 128)) return cudaErrorInvalidValue;
+    if (!tma::make_map_view(&pa.tm_b, xsrc, bf16, 64 * xa, b.n_kv, batch, xv, n1, n2, 128)) return cudaErrorInvalidValue;
   } else {
     pa.tm_b = pa.tm_a;
   }
-  if (!tma::make_map(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.q_bs, qrows)) return cudaErrorInvalidValue;
-  if (!tma::make_map(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.do_bs, qrows)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.qv, n1, n2, qrows)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.dov, n1, n2, qrows)) return cudaErrorInvalidValue;
   pa.nl = b.fold;
   pa.nc = b.fold + batch * b.n_pad;
   pa.ng = b.fold + 2 * batch * b.n_pad;
   pa.n_pad = b.n_pad;
   // gradient maps: dK, and dV (or dV2 when V aliases K) when the kernel has a value accumulator
-  auto grad_map = [&](CUtensorMap* m, void* base, int64_t rows, int64_t bs, bool f32) {
-    return f32 ? tma::make_map_f32(m, base, 128, rows, batch, bs, 128)
-               : tma::make_map(m, base, bf16, 128, rows, batch, bs, 128);
+  auto grad_map = [&](CUtensorMap* m, void* base, int64_t rows, const View& v, bool f32) {
+    return f32 ? tma::make_map_view_f32(m, base, 128, rows, batch, v, n1, n2, 128)
+               : tma::make_map_view(m, base, bf16, 128, rows, batch, v, n1, n2, 128);
   };
   const bool f32_kv = b.acc_kv == 1 || b.acc_kv == 2;  // acc 3 writes 16-bit values
-  if (!grad_map(&pa.tm_g0, b.dk, b.n_kv, b.dk_bs, f32_kv)) return cudaErrorInvalidValue;
-  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, b.n_kv, vk ? b.dv2_bs : b.dv_bs, f32_kv))
+  if (!grad_map(&pa.tm_g0, b.dk, b.n_kv, b.dkv, f32_kv)) return cudaErrorInvalidValue;
+  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, b.n_kv, vk ? b.dv2v : b.dvv, f32_kv))
     return cudaErrorInvalidValue;
   if (b.acc_kv == 3) {
-    if (!tma::make_map_f32(&pa.tm_f0, b.fin_k, 128, b.n_kv, batch, b.fin_k_bs, 128)) return cudaErrorInvalidValue;
-    if (xa > 0 && !tma::make_map_f32(&pa.tm_f1, vk ? b.fin_v2 : b.fin_v, 128, b.n_kv, batch,
-                                     vk ? b.fin_v2_bs : b.fin_v_bs, 128))
+    if (!tma::make_map_view_f32(&pa.tm_f0, b.fin_k, 128, b.n_kv, batch, b.finkv, n1, n2, 128))
+      return cudaErrorInvalidValue;
+    if (xa > 0 && !tma::make_map_view_f32(&pa.tm_f1, vk ? b.fin_v2 : b.fin_v, 128, b.n_kv, batch,
+                                          vk ? b.finv2v : b.finvv, n1, n2, 128))
       return cudaErrorInvalidValue;
   }
   pa.n_q = b.n_q;
@@ -1192,7 +1202,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
       if (e != cudaSuccess) return e;
     }
     pa.dq = b.dq;
-    pa.dq_bs = b.dq_bs;
+    pa.dq_bs = b.dq_bs;  // the host fuses only a uniform dQ view (one batch stride, rows of 128)
     return run(fea_bwd_dkdv_kernel<T, 0, true, 4, kDkdvWarpgroups, true>, DkdvCfg<0, true, 4, true>::SMEM, blocks_a,
                kDkdvThreads, pa, st);
   }
@@ -1208,9 +1218,11 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     // ---- dQ = dS K from the dS^T rows the dK/dV kernel stored
     Sm100BwdParams pg{};
     if (!tma::make_map(&pg.tm_a, b.ds, bf16, pa.ds_ld, pa.ds_bs / pa.ds_ld, batch, pa.ds_bs, 64)) return cudaErrorInvalidValue;
-    if (!tma::make_map(&pg.tm_c, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 64)) return cudaErrorInvalidValue;
-    if (!grad_map(&pg.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
-    if (b.acc_q == 3 && !tma::make_map_f32(&pg.tm_f0, b.fin_q, 128, b.n_q, batch, b.fin_q_bs, 128))
+    pg.n1 = n1;
+    pg.n2 = n2;
+    if (!tma::make_map_view(&pg.tm_c, b.k, bf16, 128, b.n_kv, batch, b.kv, n1, n2, 64)) return cudaErrorInvalidValue;
+    if (!grad_map(&pg.tm_g0, b.dq, b.n_q, b.dqv, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
+    if (b.acc_q == 3 && !tma::make_map_view_f32(&pg.tm_f0, b.fin_q, 128, b.n_q, batch, b.finqv, n1, n2, 128))
       return cudaErrorInvalidValue;
     pg.n_q = b.n_q;
     pg.n_kv = b.n_kv;
@@ -1221,16 +1233,18 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   }
   // ---- dQ: 128-key tiles (dO staged in TMEM when it is 256 wide)
   Sm100BwdParams pb{};
-  if (!tma::make_map(&pb.tm_a, b.q, bf16, 128, b.n_q, batch, b.q_bs, 128)) return cudaErrorInvalidValue;
-  if (!tma::make_map(&pb.tm_b, b.dout, bf16, dv, b.n_q, batch, b.do_bs, 128)) return cudaErrorInvalidValue;
-  if (!tma::make_map(&pb.tm_c, b.k, bf16, 128, b.n_kv, batch, b.k_bs, 128)) return cudaErrorInvalidValue;
+  pb.n1 = n1;
+  pb.n2 = n2;
+  if (!tma::make_map_view(&pb.tm_a, b.q, bf16, 128, b.n_q, batch, b.qv, n1, n2, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pb.tm_b, b.dout, bf16, dv, b.n_q, batch, b.dov, n1, n2, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pb.tm_c, b.k, bf16, 128, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
-    if (!tma::make_map(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xbs, 128)) return cudaErrorInvalidValue;
+    if (!tma::make_map_view(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xv, n1, n2, 128)) return cudaErrorInvalidValue;
   } else {
     pb.tm_d = pb.tm_c;
   }
   pb.dout = b.dout;
-  pb.do_bs = b.do_bs;
+  pb.dov = b.dov;
   pb.nl = b.fold;
   pb.nc = b.fold + batch * b.n_pad;
   pb.ng = b.fold + 2 * batch * b.n_pad;
@@ -1248,8 +1262,8 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
                                          b.n_pad * 128, 128))
       return cudaErrorInvalidValue;
   } else {
-    if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dq_bs, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
-    if (b.acc_q == 3 && !tma::make_map_f32(&pb.tm_f0, b.fin_q, 128, b.n_q, batch, b.fin_q_bs, 128))
+    if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dqv, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
+    if (b.acc_q == 3 && !tma::make_map_view_f32(&pb.tm_f0, b.fin_q, 128, b.n_q, batch, b.finqv, n1, n2, 128))
       return cudaErrorInvalidValue;
   }
   pb.n_q = b.n_q;
@@ -1273,10 +1287,10 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
   if (b.acc_q == 3)
     dq_split_finalize_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.fin_q,
-                                                                  b.fin_q_bs, reinterpret_cast<T*>(b.dq), b.dq_bs);
+                                                                  b.finqv, reinterpret_cast<T*>(b.dq), b.dqv, n1, n2);
   else
     dq_split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.dq,
-                                                             b.dq_bs, b.acc_q == 2);
+                                                             b.dqv, n1, n2, b.acc_q == 2);
   return cudaGetLastError();
 }
 

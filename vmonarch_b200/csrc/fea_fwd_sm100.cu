@@ -51,6 +51,9 @@ struct Sm100FwdParams {
   float* pst;         // key-range split: partial (m, l, h) planes, each [split * batch * n_pad]
   int n_q, n_kv, n_qtiles;
   int kv_split, kt_per, n_seq;  // split count, key tiles per chunk, sequences of the call
+  int n1, n2;                   // batch split of the q / k / v / o maps (fea_params.h View)
+  long long wait_limit;         // pipeline wait limit in cycles (0: kWaitCycles); shortened by tests
+  int hold_loads;               // test of the timeout path: the producers issue no load
   int64_t n_pad;      // n_q rounded up to 128
   float scale_log2;
 };
@@ -135,6 +138,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int bi = blockIdx.x / p.n_qtiles;
+  const BIdx bx = bidx(bi, p.n1, p.n2);
   const int q0 = (blockIdx.x % p.n_qtiles) * 128;
   const int n_kt = (p.n_kv + 127) / 128;
 
@@ -181,30 +185,31 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producer
-    if (lane == 0) {
+    // (hold_loads, a test of the timeout path: no load is issued, so every consumer wait runs out)
+    if (lane == 0 && !p.hold_loads) {
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       if (XA > 0) prefetch_tmap(&p.tm_x);
       mbar_expect_tx(BAR_Q, C::Q_BYTES);
-      tma_load_3d(sQ, &p.tm_q, 0, q0, bi, BAR_Q);
-      tma_load_3d(sQ + kAtom, &p.tm_q, 64, q0, bi, BAR_Q);
+      tma_load(sQ, &p.tm_q, 0, q0, bx, BAR_Q);
+      tma_load(sQ + kAtom, &p.tm_q, 64, q0, bx, BAR_Q);
       int armed[NSLOT];
       for (int s = 0; s < NSLOT; ++s) armed[s] = 0;
       for (int j = 0; j < n_kt; ++j) {
         const int s = j % NSLOT;
-        if (j >= NSLOT && !mbar_wait(BAR_EMPTY(s), ((j / NSLOT) - 1) & 1, abort, &g_fwd_err, 1)) break;
+        if (j >= NSLOT && !mbar_wait(BAR_EMPTY(s), ((j / NSLOT) - 1) & 1, abort, &g_fwd_err, 1, p.wait_limit)) break;
         const uint32_t slot = sRing + s * C::SLOT;
         mbar_expect_tx(BAR_KFULL(s), 2 * kAtom);
-        tma_load_3d(slot, &p.tm_k, 0, j * 128, bi, BAR_KFULL(s));
-        tma_load_3d(slot + kAtom, &p.tm_k, 64, j * 128, bi, BAR_KFULL(s));
+        tma_load(slot, &p.tm_k, 0, j * 128, bx, BAR_KFULL(s));
+        tma_load(slot + kAtom, &p.tm_k, 64, j * 128, bx, BAR_KFULL(s));
         if (XA > 0) {
           mbar_expect_tx(BAR_VFULL(s), XA * kAtom);
-          for (int a = 0; a < XA; ++a) tma_load_3d(slot + (2 + a) * kAtom, &p.tm_x, 64 * a, j * 128, bi, BAR_VFULL(s));
+          for (int a = 0; a < XA; ++a) tma_load(slot + (2 + a) * kAtom, &p.tm_x, 64 * a, j * 128, bx, BAR_VFULL(s));
         }
         if (j + NSLOT < n_kt) {  // the tiles one ring ahead into L2
-          tma_prefetch_3d(&p.tm_k, 0, (j + NSLOT) * 128, bi);
-          tma_prefetch_3d(&p.tm_k, 64, (j + NSLOT) * 128, bi);
-          for (int a = 0; a < XA; ++a) tma_prefetch_3d(&p.tm_x, 64 * a, (j + NSLOT) * 128, bi);
+          tma_prefetch(&p.tm_k, 0, (j + NSLOT) * 128, bx);
+          tma_prefetch(&p.tm_k, 64, (j + NSLOT) * 128, bx);
+          for (int a = 0; a < XA; ++a) tma_prefetch(&p.tm_x, 64 * a, (j + NSLOT) * 128, bx);
         }
         armed[s] = j / NSLOT + 1;
       }
@@ -224,7 +229,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     // P V -> EMPTY(slot), which both frees the ring slot and tells the softmax warps that O is done.
     const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
     auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code, p.wait_limit));
     };
     bool ok = wwait(BAR_Q, 0, 2);
     auto issue_s = [&](int j) -> bool {
@@ -295,7 +300,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     bool ok = true;
 
     auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
-      const bool mine = mbar_wait(bar, parity, abort, &g_fwd_err, code);
+      const bool mine = mbar_wait(bar, parity, abort, &g_fwd_err, code, p.wait_limit);
       return __all_sync(0xffffffffu, mine);
     };
 
@@ -426,7 +431,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     fence_proxy_async_smem();
     named_bar_sync(3, 256);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      for (int a = 0; a < C::NV / 64; ++a) tma_store_3d(&p.tm_o, 64 * a, q0, bi, stage + a * kAtom);
+      for (int a = 0; a < C::NV / 64; ++a) tma_store(&p.tm_o, 64 * a, q0, bx, stage + a * kAtom);
       tma_store_commit_and_wait();
     }
   }
@@ -503,6 +508,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   const int n_units = (p.n_qtiles + NS - 1) / NS;
   const int per_seq = n_units * p.kv_split;
   const int bi = blockIdx.x / per_seq;
+  const BIdx bx = bidx(bi, p.n1, p.n2);
   const int q0 = ((blockIdx.x % per_seq) / p.kv_split) * 128 * NS;
   const int kchunk = blockIdx.x % p.kv_split;
   const int kt0 = kchunk * p.kt_per;                                  // first key tile of the chunk
@@ -561,8 +567,9 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
 
   if (warp == 0) {
     // ------------------------------------------------------------------ TMA producers
-    // lane 0: Q, then the K ring; lane 1 (separate V only): the V ring.
-    if (lane == 0 || (!VK && lane == 1)) {
+    // lane 0: Q, then the K ring; lane 1 (separate V only): the V ring. (hold_loads, a test of the
+    // timeout path: no load is issued, so every consumer wait runs out)
+    if ((lane == 0 || (!VK && lane == 1)) && !p.hold_loads) {
       const bool kl = lane == 0;
       const int nslot = kl ? NK : NVS;
       if (kl) {
@@ -570,8 +577,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         prefetch_tmap(&p.tm_k);
         mbar_expect_tx(BAR_Q, C::Q_BYTES);
         for (int w = 0; w < NS; ++w) {
-          tma_load_3d(sQ + w * 2 * kAtom, &p.tm_q, 0, q0 + 128 * w, bi, BAR_Q);
-          tma_load_3d(sQ + w * 2 * kAtom + kAtom, &p.tm_q, 64, q0 + 128 * w, bi, BAR_Q);
+          tma_load(sQ + w * 2 * kAtom, &p.tm_q, 0, q0 + 128 * w, bx, BAR_Q);
+          tma_load(sQ + w * 2 * kAtom + kAtom, &p.tm_q, 64, q0 + 128 * w, bx, BAR_Q);
         }
       } else {
         prefetch_tmap(&p.tm_x);
@@ -581,15 +588,15 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       for (int j = 0; j < n_kt; ++j) {
         const int s = j % nslot;
         const uint32_t empty = kl ? BAR_KEMPTY(s) : BAR_VEMPTY(s);
-        if (j >= nslot && !mbar_wait(empty, ((j / nslot) - 1) & 1, abort, &g_fwd_err, 1)) break;
+        if (j >= nslot && !mbar_wait(empty, ((j / nslot) - 1) & 1, abort, &g_fwd_err, 1, p.wait_limit)) break;
         const uint32_t full = kl ? BAR_KFULL(s) : BAR_VFULL(s);
         const uint32_t slot = (kl ? sK : sV) + s * 2 * kAtom;
         mbar_expect_tx(full, 2 * kAtom);
-        tma_load_3d(slot, kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j) * 128, bi, full);
-        tma_load_3d(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j) * 128, bi, full);
+        tma_load(slot, kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j) * 128, bx, full);
+        tma_load(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j) * 128, bx, full);
         if (j + nslot < n_kt) {  // the tile one ring ahead into L2
-          tma_prefetch_3d(kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j + nslot) * 128, bi);
-          tma_prefetch_3d(kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j + nslot) * 128, bi);
+          tma_prefetch(kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j + nslot) * 128, bx);
+          tma_prefetch(kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j + nslot) * 128, bx);
         }
         armed[s] = j / nslot + 1;
       }
@@ -602,7 +609,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     // ------------------------------------------------------------------ MMA issuer
     const uint32_t leader = elect_one() ? 1u : 0u;  // the lane that issues (warp converged here)
     auto wwait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code, p.wait_limit));
     };
     bool ok = wwait(BAR_Q, 0, 2);
     // Step j: stream w = j % NS (query tile w) with key tile t = j / NS.
@@ -708,7 +715,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     float m_ref = -1e30f, l = 0.f, h = 0.f;
     bool ok = true;
     auto warp_wait = [&](uint32_t bar, uint32_t parity, int code) -> bool {
-      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code));
+      return __all_sync(0xffffffffu, mbar_wait(bar, parity, abort, &g_fwd_err, code, p.wait_limit));
     };
 
     for (int t = 0; t < n_kt; ++t) {  // key tile t of this stream (step j = NS t + w)
@@ -916,9 +923,9 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         const uint32_t st = sK + (uint32_t)ws * (part ? 4 : 2) * kAtom;
         const int qr = q0 + 128 * ws;
         if (part) {
-          for (int c = 0; c < 4; ++c) tma_store_3d(&p.tm_po, 32 * c, qr, kchunk * p.n_seq + bi, st + c * 16384);
+          for (int c = 0; c < 4; ++c) tma_store(&p.tm_po, 32 * c, qr, kchunk * p.n_seq + bi, st + c * 16384);
         } else {
-          for (int a = 0; a < 2; ++a) tma_store_3d(&p.tm_o, 64 * a, qr, bi, st + a * kAtom);
+          for (int a = 0; a < 2; ++a) tma_store(&p.tm_o, 64 * a, qr, bx, st + a * kAtom);
         }
       }
       tma_store_commit_and_wait();
@@ -937,8 +944,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
 // entropy = (log2 l - h / l) ln 2. Chunks are summed in order (deterministic).
 template <typename T>
 __global__ void __launch_bounds__(256) fwd_split_merge_kernel(const float* po, const float* pst, int split, int64_t n_seq,
-                                                              int64_t n_pad, int n_q, T* o, int64_t o_bs, float* lse,
-                                                              float* ent) {
+                                                              int64_t n_pad, int n_q, T* o, View ov, int n1, int n2,
+                                                              float* lse, float* ent) {
   const int64_t rg = (int64_t)blockIdx.x * 8 + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (rg >= n_seq * n_q) return;
@@ -965,7 +972,7 @@ __global__ void __launch_bounds__(256) fwd_split_merge_kernel(const float* po, c
   uint2 w;
   w.x = Elem<T>::pack(acc.x * inv, acc.y * inv);
   w.y = Elem<T>::pack(acc.z * inv, acc.w * inv);
-  reinterpret_cast<uint2*>(o + bi * o_bs + r * 128)[lane] = w;
+  reinterpret_cast<uint2*>(o + view_offset(ov, n1, n2, bi, r))[lane] = w;
   if (lane == 0) {
     const float lg = log2f(l);
     if (lse) lse[bi * n_q + r] = m + lg;
@@ -1072,15 +1079,21 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
                           cudaStream_t st) {
   Sm100FwdParams p;
   const int dv1 = fp.dv1;
-  if (!tma::make_map(&p.tm_q, fp.q, bf16, d, fp.n_q, batch, fp.q_bs, 128)) return cudaErrorInvalidValue;
-  if (!tma::make_map(&p.tm_k, fp.k, bf16, d, fp.n_kv, batch, fp.k_bs, 128)) return cudaErrorInvalidValue;
+  const int n1 = fp.n1, n2 = fp.n2;
+  if (!tma::make_map_view(&p.tm_q, fp.q, bf16, d, fp.n_q, batch, fp.qv, n1, n2, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&p.tm_k, fp.k, bf16, d, fp.n_kv, batch, fp.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (vk) {
-    if (dv > dv1 && !tma::make_map(&p.tm_x, fp.v2, bf16, dv - dv1, fp.n_kv, batch, fp.v2_bs, 128)) return cudaErrorInvalidValue;
+    if (dv > dv1 && !tma::make_map_view(&p.tm_x, fp.v2, bf16, dv - dv1, fp.n_kv, batch, fp.v2v, n1, n2, 128))
+      return cudaErrorInvalidValue;
     if (dv == dv1) p.tm_x = p.tm_k;
   } else {
-    if (!tma::make_map(&p.tm_x, fp.v, bf16, dv, fp.n_kv, batch, fp.v_bs, 128)) return cudaErrorInvalidValue;
+    if (!tma::make_map_view(&p.tm_x, fp.v, bf16, dv, fp.n_kv, batch, fp.vv, n1, n2, 128)) return cudaErrorInvalidValue;
   }
-  if (!tma::make_map(&p.tm_o, fp.o, bf16, dv, fp.n_q, batch, fp.o_bs, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&p.tm_o, fp.o, bf16, dv, fp.n_q, batch, fp.ov, n1, n2, 128)) return cudaErrorInvalidValue;
+  p.n1 = n1;
+  p.n2 = n2;
+  p.wait_limit = fp.wait_limit;
+  p.hold_loads = fp.hold_loads;
   p.lse = fp.lse;
   p.ent = fp.ent;
   p.n_q = fp.n_q;
@@ -1114,11 +1127,11 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   if (bf16)
     fwd_split_merge_kernel<__nv_bfloat16><<<(unsigned)blocks, 256, 0, st>>>(
-        po, p.pst, p.kv_split, batch, p.n_pad, fp.n_q, static_cast<__nv_bfloat16*>(fp.o), fp.o_bs, fp.lse,
+        po, p.pst, p.kv_split, batch, p.n_pad, fp.n_q, static_cast<__nv_bfloat16*>(fp.o), fp.ov, n1, n2, fp.lse,
         ent ? fp.ent : nullptr);
   else
     fwd_split_merge_kernel<__half><<<(unsigned)blocks, 256, 0, st>>>(po, p.pst, p.kv_split, batch, p.n_pad, fp.n_q,
-                                                                      static_cast<__half*>(fp.o), fp.o_bs, fp.lse,
+                                                                      static_cast<__half*>(fp.o), fp.ov, n1, n2, fp.lse,
                                                                       ent ? fp.ent : nullptr);
   return cudaGetLastError();
 }

@@ -1,4 +1,5 @@
-// FlashEntropyAttention on warp-level MMA (mma.sync m16n8k16), all (D, Dv) shapes.
+// FlashEntropyAttention on warp-level MMA (mma.sync m16n8k16), every (D, Dv) the reference accepts:
+// D, Dv in {16, 32, 64, 128, 256} with Dv % D == 0 (video_monarch_attention/kernel.py:260, 324).
 //
 // Forward  (reference: video_monarch_attention/kernel.py:32-67 inner loop, 106-151 kernel):
 //   per query row i:  x_ij = s_ij * sm_scale * log2(e),  m = running max,  p = 2^(x - m)
@@ -26,10 +27,14 @@ template <typename T, int D, int DV, bool ENT>
 __global__ void __launch_bounds__(128) fea_fwd_mma_kernel(const FwdParams p) {
   constexpr int BM = 64, BN = 64;
   constexpr int DCH = D / 8, VCH = DV / 8;
+  // shared-memory rows are at least 64 elements wide (the swizzle spans 8 chunks of 16 bytes);
+  // for head dims 16 and 32 only the first D / DV columns are loaded and read
+  constexpr int DP = D < 64 ? 64 : D, VP = DV < 64 ? 64 : DV;
+  constexpr int DPCH = DP / 8, VPCH = VP / 8;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   T* sQ = reinterpret_cast<T*>(smem_raw);
-  T* sK = sQ + BM * D;       // [2][BN*D]
-  T* sV = sK + 2 * BN * D;   // [2][BN*DV]
+  T* sK = sQ + BM * DP;       // [2][BN*DP]
+  T* sV = sK + 2 * BN * DP;   // [2][BN*VP]
 
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t bi = blockIdx.x / p.n_qtiles;
@@ -43,21 +48,21 @@ __global__ void __launch_bounds__(128) fea_fwd_mma_kernel(const FwdParams p) {
   for (int c = tid; c < BM * DCH; c += 128) {
     const int r = c / DCH, ch = c % DCH, gr = q0 + r;
     const T* src = gq + (int64_t)min(gr, p.n_q - 1) * D + ch * 8;
-    cp_async16(smem_u32(sQ + swz<DCH>(r, ch)), src, gr < p.n_q ? 16 : 0);
+    cp_async16(smem_u32(sQ + swz<DPCH>(r, ch)), src, gr < p.n_q ? 16 : 0);
   }
   auto load_kv = [&](int t, int stage) {
     const int k0 = t * BN;
-    T* dK = sK + stage * BN * D;
-    T* dV = sV + stage * BN * DV;
+    T* dK = sK + stage * BN * DP;
+    T* dV = sV + stage * BN * VP;
     for (int c = tid; c < BN * DCH; c += 128) {
       const int r = c / DCH, ch = c % DCH, gr = k0 + r;
       const T* src = gk + (int64_t)min(gr, p.n_kv - 1) * D + ch * 8;
-      cp_async16(smem_u32(dK + swz<DCH>(r, ch)), src, gr < p.n_kv ? 16 : 0);
+      cp_async16(smem_u32(dK + swz<DPCH>(r, ch)), src, gr < p.n_kv ? 16 : 0);
     }
     for (int c = tid; c < BN * VCH; c += 128) {
       const int r = c / VCH, ch = c % VCH, gr = min(k0 + r, p.n_kv - 1), col = ch * 8;
       const T* src = col < dv1 ? gv + (int64_t)gr * dv1 + col : gv2 + (int64_t)gr * dv2 + (col - dv1);
-      cp_async16(smem_u32(dV + swz<VCH>(r, ch)), src, k0 + r < p.n_kv ? 16 : 0);
+      cp_async16(smem_u32(dV + swz<VPCH>(r, ch)), src, k0 + r < p.n_kv ? 16 : 0);
     }
   };
 
@@ -75,8 +80,8 @@ __global__ void __launch_bounds__(128) fea_fwd_mma_kernel(const FwdParams p) {
     cp_async_commit();
     cp_async_wait<1>();
     __syncthreads();
-    const T* cK = sK + (t & 1) * BN * D;
-    const T* cV = sV + (t & 1) * BN * DV;
+    const T* cK = sK + (t & 1) * BN * DP;
+    const T* cV = sV + (t & 1) * BN * VP;
 
     float s[BN / 8][4];
 #pragma unroll
@@ -84,12 +89,12 @@ __global__ void __launch_bounds__(128) fea_fwd_mma_kernel(const FwdParams p) {
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t a[4];
-      ldsm_x4(smem_u32(sQ + swz<DCH>(warp * 16 + (lane & 15), kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
+      ldsm_x4(smem_u32(sQ + swz<DPCH>(warp * 16 + (lane & 15), kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
 #pragma unroll
       for (int np = 0; np < BN / 16; ++np) {
         uint32_t b0, b1, b2, b3;
         const int r = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-        ldsm_x4(smem_u32(cK + swz<DCH>(r, kk * 2 + ((lane >> 3) & 1))), b0, b1, b2, b3);
+        ldsm_x4(smem_u32(cK + swz<DPCH>(r, kk * 2 + ((lane >> 3) & 1))), b0, b1, b2, b3);
         mma16816<T>(s[2 * np], a, b0, b1);
         mma16816<T>(s[2 * np + 1], a, b2, b3);
       }
@@ -150,7 +155,7 @@ __global__ void __launch_bounds__(128) fea_fwd_mma_kernel(const FwdParams p) {
       for (int np = 0; np < DV / 16; ++np) {
         uint32_t b0, b1, b2, b3;
         const int r = kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3);
-        ldsm_x4_t(smem_u32(cV + swz<VCH>(r, np * 2 + (lane >> 4))), b0, b1, b2, b3);
+        ldsm_x4_t(smem_u32(cV + swz<VPCH>(r, np * 2 + (lane >> 4))), b0, b1, b2, b3);
         mma16816<T>(o_acc[2 * np], a, b0, b1);
         mma16816<T>(o_acc[2 * np + 1], a, b2, b3);
       }
@@ -192,13 +197,15 @@ template <typename T, int D, int DV, bool VK>
 __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
   constexpr int BN = 64, BQ = 32, SDS = BQ + 8;
   constexpr int DCH = D / 8, VCH = DV / 8;
+  constexpr int DP = D < 64 ? 64 : D, VP = DV < 64 ? 64 : DV;  // shared-memory row widths (>= 64)
+  constexpr int DPCH = DP / 8, VPCH = VP / 8;
   constexpr int DVA = VK ? DV - D : DV;  // columns held by the separate dV accumulator
   extern __shared__ __align__(128) uint8_t smem_raw[];
-  T* sK = reinterpret_cast<T*>(smem_raw);     // BN*D
-  T* sV = sK + BN * D;                        // BN*DV
-  T* sQ = sV + BN * DV;                       // [2][BQ*D]
-  T* sO = sQ + 2 * BQ * D;                    // [2][BQ*DV]  (dO)
-  T* sS = sO + 2 * BQ * DV;                   // BN*SDS  dS^T (scaled)
+  T* sK = reinterpret_cast<T*>(smem_raw);     // BN*DP
+  T* sV = sK + BN * DP;                       // BN*VP
+  T* sQ = sV + BN * VP;                       // [2][BQ*DP]
+  T* sO = sQ + 2 * BQ * DP;                   // [2][BQ*VP]  (dO)
+  T* sS = sO + 2 * BQ * VP;                   // BN*SDS  dS^T (scaled)
   float* sL = reinterpret_cast<float*>(sS + BN * SDS);  // [2][BQ]
   float* sC = sL + 2 * BQ;
   float* sG = sC + 2 * BQ;
@@ -219,24 +226,24 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
 
   for (int c = tid; c < BN * DCH; c += 128) {
     const int r = c / DCH, ch = c % DCH, gr = k0 + r;
-    cp_async16(smem_u32(sK + swz<DCH>(r, ch)), gk + (int64_t)min(gr, p.n_kv - 1) * D + ch * 8, gr < p.n_kv ? 16 : 0);
+    cp_async16(smem_u32(sK + swz<DPCH>(r, ch)), gk + (int64_t)min(gr, p.n_kv - 1) * D + ch * 8, gr < p.n_kv ? 16 : 0);
   }
   for (int c = tid; c < BN * VCH; c += 128) {
     const int r = c / VCH, ch = c % VCH, gr = min(k0 + r, p.n_kv - 1), col = ch * 8;
     const T* src = col < dv1 ? gv + (int64_t)gr * dv1 + col : gv2 + (int64_t)gr * dv2 + (col - dv1);
-    cp_async16(smem_u32(sV + swz<VCH>(r, ch)), src, k0 + r < p.n_kv ? 16 : 0);
+    cp_async16(smem_u32(sV + swz<VPCH>(r, ch)), src, k0 + r < p.n_kv ? 16 : 0);
   }
   auto load_q = [&](int t, int stage) {
     const int q0 = t * BQ;
-    T* dQ = sQ + stage * BQ * D;
-    T* dO = sO + stage * BQ * DV;
+    T* dQ = sQ + stage * BQ * DP;
+    T* dO = sO + stage * BQ * VP;
     for (int c = tid; c < BQ * DCH; c += 128) {
       const int r = c / DCH, ch = c % DCH, gr = q0 + r;
-      cp_async16(smem_u32(dQ + swz<DCH>(r, ch)), gq + (int64_t)min(gr, p.n_q - 1) * D + ch * 8, gr < p.n_q ? 16 : 0);
+      cp_async16(smem_u32(dQ + swz<DPCH>(r, ch)), gq + (int64_t)min(gr, p.n_q - 1) * D + ch * 8, gr < p.n_q ? 16 : 0);
     }
     for (int c = tid; c < BQ * VCH; c += 128) {
       const int r = c / VCH, ch = c % VCH, gr = q0 + r;
-      cp_async16(smem_u32(dO + swz<VCH>(r, ch)), gdo + (int64_t)min(gr, p.n_q - 1) * DV + ch * 8, gr < p.n_q ? 16 : 0);
+      cp_async16(smem_u32(dO + swz<VPCH>(r, ch)), gdo + (int64_t)min(gr, p.n_q - 1) * DV + ch * 8, gr < p.n_q ? 16 : 0);
     }
     if (tid < BQ) {
       const int gr = q0 + tid;
@@ -268,8 +275,8 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
     cp_async_wait<1>();
     __syncthreads();
     const int st = t & 1;
-    const T* cQ = sQ + st * BQ * D;
-    const T* cO = sO + st * BQ * DV;
+    const T* cQ = sQ + st * BQ * DP;
+    const T* cO = sO + st * BQ * VP;
     const float* cL = sL + st * BQ;
     const float* cC = sC + st * BQ;
     const float* cG = sG + st * BQ;
@@ -284,12 +291,12 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
 #pragma unroll
     for (int kk = 0; kk < D / 16; ++kk) {
       uint32_t a[4];
-      ldsm_x4(smem_u32(sK + swz<DCH>(warp * 16 + (lane & 15), kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
+      ldsm_x4(smem_u32(sK + swz<DPCH>(warp * 16 + (lane & 15), kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
 #pragma unroll
       for (int np = 0; np < BQ / 16; ++np) {
         uint32_t b0, b1, b2, b3;
         const int r = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-        ldsm_x4(smem_u32(cQ + swz<DCH>(r, kk * 2 + ((lane >> 3) & 1))), b0, b1, b2, b3);
+        ldsm_x4(smem_u32(cQ + swz<DPCH>(r, kk * 2 + ((lane >> 3) & 1))), b0, b1, b2, b3);
         mma16816<T>(s[2 * np], a, b0, b1);
         mma16816<T>(s[2 * np + 1], a, b2, b3);
       }
@@ -297,12 +304,12 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
 #pragma unroll
     for (int kk = 0; kk < DV / 16; ++kk) {
       uint32_t a[4];
-      ldsm_x4(smem_u32(sV + swz<VCH>(warp * 16 + (lane & 15), kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
+      ldsm_x4(smem_u32(sV + swz<VPCH>(warp * 16 + (lane & 15), kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
 #pragma unroll
       for (int np = 0; np < BQ / 16; ++np) {
         uint32_t b0, b1, b2, b3;
         const int r = np * 16 + (lane & 7) + ((lane >> 4) << 3);
-        ldsm_x4(smem_u32(cO + swz<VCH>(r, kk * 2 + ((lane >> 3) & 1))), b0, b1, b2, b3);
+        ldsm_x4(smem_u32(cO + swz<VPCH>(r, kk * 2 + ((lane >> 3) & 1))), b0, b1, b2, b3);
         mma16816<T>(dp[2 * np], a, b0, b1);
         mma16816<T>(dp[2 * np + 1], a, b2, b3);
       }
@@ -337,11 +344,11 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
 #pragma unroll
       for (int np = 0; np < D / 16; ++np) {
         uint32_t b0, b1, b2, b3;
-        ldsm_x4_t(smem_u32(cQ + swz<DCH>(r, np * 2 + (lane >> 4))), b0, b1, b2, b3);
+        ldsm_x4_t(smem_u32(cQ + swz<DPCH>(r, np * 2 + (lane >> 4))), b0, b1, b2, b3);
         mma16816<T>(dk_acc[2 * np], as, b0, b1);
         mma16816<T>(dk_acc[2 * np + 1], as, b2, b3);
         if (VK) {
-          ldsm_x4_t(smem_u32(cO + swz<VCH>(r, np * 2 + (lane >> 4))), b0, b1, b2, b3);
+          ldsm_x4_t(smem_u32(cO + swz<VPCH>(r, np * 2 + (lane >> 4))), b0, b1, b2, b3);
           mma16816<T>(dk_acc[2 * np], ap, b0, b1);
           mma16816<T>(dk_acc[2 * np + 1], ap, b2, b3);
         }
@@ -350,7 +357,7 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
       for (int np = 0; np < DVA / 16; ++np) {
         uint32_t b0, b1, b2, b3;
         const int cb = (VK ? D / 8 : 0) + np * 2;
-        ldsm_x4_t(smem_u32(cO + swz<VCH>(r, cb + (lane >> 4))), b0, b1, b2, b3);
+        ldsm_x4_t(smem_u32(cO + swz<VPCH>(r, cb + (lane >> 4))), b0, b1, b2, b3);
         mma16816<T>(dv_acc[2 * np], ap, b0, b1);
         mma16816<T>(dv_acc[2 * np + 1], ap, b2, b3);
       }
@@ -365,8 +372,10 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
     }
     __syncthreads();
     {
-      constexpr int DH = D / 2;  // d columns per warp
+      // d columns per warp: two warps per query half split D; at D = 16 one warp takes all 16
+      constexpr int DH = D >= 32 ? D / 2 : D;
       const int qw = (warp & 1) * 16, dw = (warp >> 1) * DH;
+      if (D >= 32 || warp < 2) {
       float acc[DH / 8][4];
 #pragma unroll
       for (int j = 0; j < DH / 8; ++j) acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.f;
@@ -381,7 +390,7 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
 #pragma unroll
         for (int np = 0; np < DH / 16; ++np) {
           uint32_t b0, b1, b2, b3;
-          ldsm_x4_t(smem_u32(sK + swz<DCH>(r, dw / 8 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
+          ldsm_x4_t(smem_u32(sK + swz<DPCH>(r, dw / 8 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
           mma16816<T>(acc[2 * np], a, b0, b1);
           mma16816<T>(acc[2 * np + 1], a, b2, b3);
         }
@@ -396,6 +405,7 @@ __global__ void __launch_bounds__(128) fea_bwd_mma_kernel(const BwdParams p) {
           for (int j = 0; j < DH / 8; ++j)
             atomicAdd(reinterpret_cast<float2*>(dst + j * 8), make_float2(acc[j][2 * i], acc[j][2 * i + 1]));
         }
+      }
       }
     }
   }
@@ -444,7 +454,8 @@ template <typename T, int D, int DV, bool ENT>
 static cudaError_t launch_fwd_t(const FwdParams& p0, int64_t batch, cudaStream_t st) {
   FwdParams p = p0;
   p.n_qtiles = (p.n_q + 63) / 64;
-  const size_t smem = (size_t)(64 * D + 2 * 64 * D + 2 * 64 * DV) * sizeof(T);
+  constexpr int DP = D < 64 ? 64 : D, VP = DV < 64 ? 64 : DV;
+  const size_t smem = (size_t)(64 * DP + 2 * 64 * DP + 2 * 64 * VP) * sizeof(T);
   auto kern = fea_fwd_mma_kernel<T, D, DV, ENT>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -458,7 +469,8 @@ template <typename T, int D, int DV, bool VK>
 static cudaError_t launch_bwd_t(const BwdParams& p0, int64_t batch, cudaStream_t st) {
   BwdParams p = p0;
   p.n_ktiles = (p.n_kv + 63) / 64;
-  const size_t smem = (size_t)(64 * D + 64 * DV + 2 * 32 * D + 2 * 32 * DV + 64 * 40) * sizeof(T) + 6 * 32 * sizeof(float);
+  constexpr int DP = D < 64 ? 64 : D, VP = DV < 64 ? 64 : DV;
+  const size_t smem = (size_t)(64 * DP + 64 * VP + 2 * 32 * DP + 2 * 32 * VP + 64 * 40) * sizeof(T) + 6 * 32 * sizeof(float);
   auto kern = fea_bwd_mma_kernel<T, D, DV, VK>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
@@ -473,11 +485,21 @@ static cudaError_t dispatch_fwd(const FwdParams& p, int64_t batch, int d, int dv
 #define VMB_FWD(DD, VV)                                                                  \
   if (d == DD && dv == VV)                                                               \
     return ent ? launch_fwd_t<T, DD, VV, true>(p, batch, st) : launch_fwd_t<T, DD, VV, false>(p, batch, st);
+  VMB_FWD(16, 16)
+  VMB_FWD(16, 32)
+  VMB_FWD(16, 64)
+  VMB_FWD(16, 128)
+  VMB_FWD(16, 256)
+  VMB_FWD(32, 32)
+  VMB_FWD(32, 64)
+  VMB_FWD(32, 128)
+  VMB_FWD(32, 256)
   VMB_FWD(64, 64)
   VMB_FWD(64, 128)
   VMB_FWD(64, 256)
   VMB_FWD(128, 128)
   VMB_FWD(128, 256)
+  VMB_FWD(256, 256)
 #undef VMB_FWD
   return cudaErrorNotSupported;
 }
@@ -487,12 +509,26 @@ static cudaError_t dispatch_bwd(const BwdParams& p, int64_t batch, int d, int dv
 #define VMB_BWD(DD, VV)                                                                  \
   if (d == DD && dv == VV)                                                               \
     return vk ? launch_bwd_t<T, DD, VV, true>(p, batch, st) : launch_bwd_t<T, DD, VV, false>(p, batch, st);
+  // values aliasing keys (the VMonarch R step) exist only with dv = d or 2 d
+#define VMB_BWD_SEP(DD, VV)                                                              \
+  if (d == DD && dv == VV && !vk) return launch_bwd_t<T, DD, VV, false>(p, batch, st);
+  VMB_BWD(16, 16)
+  VMB_BWD(16, 32)
+  VMB_BWD_SEP(16, 64)
+  VMB_BWD_SEP(16, 128)
+  VMB_BWD_SEP(16, 256)
+  VMB_BWD(32, 32)
+  VMB_BWD(32, 64)
+  VMB_BWD_SEP(32, 128)
+  VMB_BWD_SEP(32, 256)
   VMB_BWD(64, 64)
   VMB_BWD(64, 128)
   VMB_BWD(64, 256)
   VMB_BWD(128, 128)
   VMB_BWD(128, 256)
+  VMB_BWD(256, 256)
 #undef VMB_BWD
+#undef VMB_BWD_SEP
   return cudaErrorNotSupported;
 }
 

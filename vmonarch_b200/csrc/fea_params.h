@@ -5,6 +5,29 @@
 
 namespace vmb {
 
+// A tensor seen as [batch][rows][cols] (16-bit or fp32 elements, contiguous columns). The batch
+// index s of a call splits as c1 = s % n1, c2 = s / n1 % n2, c3 = s / (n1 * n2), with (n1, n2)
+// shared by every tensor of the call, and element (s, r, c) lies at
+//   c + r * rs + c1 * s1 + c2 * s2 + c3 * s3   (elements).
+// A dense tensor with batch stride bs is dense_view(cols, bs, n1, n2); a token-major caller tensor
+// (B, N, H, D) has rs = H * D and head stride D, so no transpose is ever made.
+struct View {
+  int64_t rs, s1, s2, s3;
+};
+
+inline View dense_view(int64_t cols, int64_t bs, int n1, int n2) {
+  return View{cols, bs, bs * n1, bs * (int64_t)n1 * n2};
+}
+
+#ifdef __CUDACC__
+__host__ __device__
+#endif
+inline int64_t view_offset(const View& v, int n1, int n2, int64_t s, int64_t r) {
+  // batch indices fit 32 bits (the launch grids bound them), so the split is 32-bit arithmetic
+  const int si = (int)s, t = si / n1, c1 = si - t * n1, c3 = t / n2, c2 = t - c3 * n2;
+  return r * v.rs + c1 * v.s1 + c2 * v.s2 + c3 * v.s3;
+}
+
 struct FwdParams {
   const void* q;   // [batch][n_q][D]
   const void* k;   // [batch][n_kv][D]
@@ -13,11 +36,15 @@ struct FwdParams {
   void* o;         // [batch][n_q][DV]
   float* lse;      // [batch][n_q]  log2-domain LSE of x = s * sm_scale * log2(e)
   float* ent;      // [batch][n_q]  natural-log row entropy
-  int64_t q_bs, k_bs, v_bs, v2_bs, o_bs;  // batch strides in elements
+  int64_t q_bs, k_bs, v_bs, v2_bs, o_bs;  // batch strides in elements (dense layout)
+  View qv, kv, vv, v2v, ov;                // the same tensors as strided views (tcgen05 kernels)
+  int n1, n2;                              // batch split of the views
   int n_q, n_kv, dv1, n_qtiles;
   float scale_log2;  // sm_scale * log2(e)
   void* work;        // optional workspace (key-range split of the d = dv = 128 kernel), may be NULL
   int64_t work_bytes;
+  long long wait_limit;  // tcgen05 kernels' pipeline wait limit in cycles (0: the default ~2 s)
+  int hold_loads;        // test of the timeout path: the tcgen05 producers issue no load
 };
 
 struct BwdParams {
@@ -37,7 +64,10 @@ struct BwdParams {
   void* dk;           // [batch][n_kv][D]      element type or fp32 (acc_kv)
   void* dv;           // [batch][n_kv][dv1]    unused when v aliases k
   void* dv2;          // [batch][n_kv][DV-dv1]
-  int64_t q_bs, k_bs, v_bs, v2_bs, do_bs, dq_bs, dk_bs, dv_bs, dv2_bs;
+  int64_t q_bs, k_bs, v_bs, v2_bs, do_bs, dq_bs, dk_bs, dv_bs, dv2_bs;  // dense layout
+  View qv, kv, vv, v2v, dov, dqv, dkv, dvv, dv2v;  // strided views (tcgen05 kernels)
+  View finqv, finkv, finvv, finv2v;
+  int n1, n2;                                      // batch split of the views
   int n_q, n_kv, dv1, n_ktiles;
   int acc_kv;         // 1: dk/dv/dv2 are fp32 buffers that are added into
   int acc_q;          // 1: dq is an fp32 buffer that is added into (else element dtype)

@@ -24,6 +24,10 @@ struct LstepParams {
   float scale, min_col_mass;
   int dq_store;
   float* delta_out;   // bwd, optional: [bh][N] fp32 sum_c out[c] dout[c] per token
+  // The tensors above as [bh][N][cols] views (fea_params.h) with head split (n1, n2 = 1): token t
+  // of head hb at t * rs + (hb % n1) * s1 + (hb / n1) * s3. ent and delta_out stay dense [bh][N].
+  View qv, outv, uv, zv, duv, dzv, dqv, doutv;
+  int n1;
 };
 
 cudaError_t fea_fwd_mma(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, cudaStream_t st);
@@ -53,9 +57,12 @@ int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, i
 int fea_fwd_sm100_split(int64_t batch, int n_q, int n_kv, int dv, const void* work, int64_t work_bytes);
 cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out);
 cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
-cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
+cudaError_t fea_bwd_pre(const void* o, View ov, const void* dout, View dov, int n1, int n2, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
                         float* fold, int64_t n_pad, float sm_scale, const float* delta, bool bf16, cudaStream_t st);
+// dst = (16-bit) src over [batch][rows][cols] views with batch split (n1, n2); cols % 4 == 0.
+cudaError_t cast_f32_view(const float* src, const View& sv, void* dst, const View& dvw, int n1, int n2, int64_t batch,
+                          int64_t rows, int64_t cols, bool bf16, cudaStream_t st);
 cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
                      bool bf16, cudaStream_t st);
 bool lstep_mma_supported(const LstepParams& p, bool last);

@@ -345,6 +345,8 @@ static cudaError_t launch_lstep_t(const LstepParams& p, bool bwd, cudaStream_t s
 
 template <typename T>
 static cudaError_t dispatch_lstep(const LstepParams& p, bool last, bool bwd, cudaStream_t st) {
+  if (p.d == 16) return last ? launch_lstep_t<T, 16, true>(p, bwd, st) : launch_lstep_t<T, 16, false>(p, bwd, st);
+  if (p.d == 32) return last ? launch_lstep_t<T, 32, true>(p, bwd, st) : launch_lstep_t<T, 32, false>(p, bwd, st);
   if (p.d == 64) return last ? launch_lstep_t<T, 64, true>(p, bwd, st) : launch_lstep_t<T, 64, false>(p, bwd, st);
   if (p.d == 128) return last ? launch_lstep_t<T, 128, true>(p, bwd, st) : launch_lstep_t<T, 128, false>(p, bwd, st);
   return cudaErrorNotSupported;

@@ -186,6 +186,12 @@ __device__ __forceinline__ void stage_rows64_dot(T* S, int c0, const float (&v)[
 // Gathers rows i < m (token i*b + j) of a [N][W] tensor, columns [c0*8, (c0+nch)*8), into a
 // swizzled [m + 1][CH] tile; rows whose token < skip are zero-filled. Row m is the tile's zero row
 // (zero_row), which the MMA loaders read for every row index >= m.
+// Offset (elements) of head hb of a [bh][N][cols] view split (n1, 1): (hb % n1) s1 + (hb / n1) s3.
+__device__ __forceinline__ int64_t head_off(const View& v, int n1, int64_t hb) {
+  const int64_t c3 = hb / n1;
+  return (hb - c3 * n1) * v.s1 + c3 * v.s3;
+}
+
 template <typename T, int CH>
 __device__ __forceinline__ void gather(T* dst, const T* src, int64_t W, int c0, int nch, int m, int64_t b, int j,
                                        int64_t skip, int lane) {
@@ -307,10 +313,10 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
   const int64_t bh = col / p.b;
   const int j = (int)(col % p.b);
   const int64_t N = p.m * p.b;
-  const T* gq = static_cast<const T*>(p.q) + bh * N * D;
-  const T* go = static_cast<const T*>(p.out) + bh * N * p.dw;
-  gather<T, DCH>(sq, gq, D, 0, DCH, m, p.b, j, 0, lane);
-  gather<T, OCH>(so, go, p.dw, 0, OCH, m, p.b, j, 0, lane);
+  const T* gq = static_cast<const T*>(p.q) + head_off(p.qv, p.n1, bh);
+  const T* go = static_cast<const T*>(p.out) + head_off(p.outv, p.n1, bh);
+  gather<T, DCH>(sq, gq, p.qv.rs, 0, DCH, m, p.b, j, 0, lane);
+  gather<T, OCH>(so, go, p.outv.rs, 0, OCH, m, p.b, j, 0, lane);
   cp_async_commit();
   zero_row<T, DCH>(sq, m, lane);
   zero_row<T, OCH>(so, m, lane);
@@ -330,7 +336,7 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
   if (LAST) {
     // z_i = sum_k a_ik y_k -> staged in sq (q no longer needed)
     __syncwarp();
-    T* gz = static_cast<T*>(p.z) + bh * N * D;
+    T* gz = static_cast<T*>(p.z) + head_off(p.zv, p.n1, bh);
 #pragma unroll 1
     for (int half = 0; half < D / 64; ++half) {
       float z[MP / 16][8][4];
@@ -339,7 +345,7 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
       stage_rows64<T, MP, DCH>(sq, half * 8, z, nullptr, m, lane);
     }
     __syncwarp();
-    scatter<T, DCH>(gz, sq, D, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
+    scatter<T, DCH>(gz, sq, p.zv.rs, 0, DCH, m, p.b, j, p.skip_rows, MP, lane);
   } else {
     float cs[MP / 8][2];
     col_sums<MP>(a, cs);
@@ -351,7 +357,7 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
     }
     stage_mm<T, MP>(sa, a, lane);
     __syncwarp();
-    T* gu = static_cast<T*>(p.u) + bh * N * D;
+    T* gu = static_cast<T*>(p.u) + head_off(p.uv, p.n1, bh);
 #pragma unroll 1
     for (int half = 0; half < D / 64; ++half) {
       float u[MP / 16][8][4];
@@ -360,7 +366,7 @@ __global__ void __launch_bounds__(kWarpsFwd * 32) lstep_fwd_mma_kernel(const Lst
       stage_rows64<T, MP, OCH>(so, half * 8, u, svec, m, lane);  // so (out_D) is free after the logits
     }
     __syncwarp();
-    scatter<T, OCH>(gu, so, D, 0, DCH, m, p.b, j, 0, MP, lane);
+    scatter<T, OCH>(gu, so, p.uv.rs, 0, DCH, m, p.b, j, 0, MP, lane);
   }
 }
 
@@ -382,9 +388,11 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   const int64_t bh = col / p.b;
   const int j = (int)(col % p.b);
   const int64_t N = p.m * p.b;
-  gather<T, DCH>(sq, static_cast<const T*>(p.q) + bh * N * D, D, 0, DCH, m, p.b, j, 0, lane);
-  gather<T, OCH>(so, static_cast<const T*>(p.out) + bh * N * p.dw, p.dw, 0, OCH, m, p.b, j, 0, lane);
-  if (LAST) gather<T, DCH>(sg, static_cast<const T*>(p.dz) + bh * N * D, D, 0, DCH, m, p.b, j, p.skip_rows, lane);
+  gather<T, DCH>(sq, static_cast<const T*>(p.q) + head_off(p.qv, p.n1, bh), p.qv.rs, 0, DCH, m, p.b, j, 0, lane);
+  gather<T, OCH>(so, static_cast<const T*>(p.out) + head_off(p.outv, p.n1, bh), p.outv.rs, 0, OCH, m, p.b, j, 0, lane);
+  if (LAST)
+    gather<T, DCH>(sg, static_cast<const T*>(p.dz) + head_off(p.dzv, p.n1, bh), p.dzv.rs, 0, DCH, m, p.b, j,
+                   p.skip_rows, lane);
   cp_async_commit();
   zero_row<T, DCH>(sq, m, lane);
   zero_row<T, OCH>(so, m, lane);
@@ -392,7 +400,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   if (!LAST) {  // du is fp32: convert while the other rows are in flight
     // four chunks' loads are issued before any is converted, so a warp waits for one memory round
     // trip per four chunks instead of one per chunk
-    const float* du = p.du + bh * N * D;
+    const float* du = p.du + head_off(p.duv, p.n1, bh);
     const int kChunks = (m * DCH + 31) / 32;  // per lane, rows < m
 #pragma unroll 1
     for (int t0 = 0; t0 < kChunks; t0 += 4) {
@@ -401,7 +409,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
       for (int u = 0; u < 4; ++u) {
         const int c = lane + 32 * (t0 + u), k = c / DCH, ch = c % DCH;
         if (k < m) {
-          const float4* src = reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * D + ch * 8);
+          const float4* src = reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * p.duv.rs + ch * 8);
           v[u][0] = src[0];
           v[u][1] = src[1];
         } else {
@@ -488,7 +496,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   __syncwarp();
 
   // dq_i += sum_k (scale dlog_ik) out_k  [non-last: + sum_k (a_ik c_k) du_k]
-  float* gdq = p.dq + bh * N * D;
+  float* gdq = p.dq + head_off(p.dqv, p.n1, bh);
 #pragma unroll 1
   for (int half = 0; half < D / 64; ++half) {
     float acc[MP / 16][8][4];
@@ -501,7 +509,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
       for (int h = 0; h < 2; ++h) {
         const int i = mt * 16 + (lane >> 2) + h * 8;
         if (i >= m) continue;
-        float* dst = gdq + ((int64_t)i * p.b + j) * D + half * 64 + (lane & 3) * 2;
+        float* dst = gdq + ((int64_t)i * p.b + j) * p.dqv.rs + half * 64 + (lane & 3) * 2;
         // fire-and-forget reductions (or plain stores in the store mode): this warp alone owns
         // these dq elements, so nothing waits for the old value
         if (p.dq_store) {
@@ -521,7 +529,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   // dout_k[:D] = sum_i (scale dlog_ik) q_i ; last: dout_k[D:] = sum_i a_ik dz_i   (staged in so,
   // over out; delta_k = sum_c out_k[c] dout_k[c] is summed on the way, the preprocessing of the
   // R step's attention backward)
-  T* gdo = static_cast<T*>(p.dout) + bh * N * p.dw;
+  T* gdo = static_cast<T*>(p.dout) + head_off(p.doutv, p.n1, bh);
   float dot[MP / 16][2];
 #pragma unroll
   for (int mt = 0; mt < MP / 16; ++mt) dot[mt][0] = dot[mt][1] = 0.f;
@@ -554,7 +562,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
       }
   }
   __syncwarp();
-  scatter<T, OCH>(gdo, so, p.dw, 0, OCH, m, p.b, j, 0, MP, lane);
+  scatter<T, OCH>(gdo, so, p.doutv.rs, 0, OCH, m, p.b, j, 0, MP, lane);
 }
 
 template <typename T, int MP, int D, bool LAST>

@@ -43,28 +43,31 @@ struct LstepTcParams {
   const float* ent;              // [bh][N]
   int64_t b, n;                  // columns per head, tokens per head (m b)
   int m, nblk;                   // rows per column, column groups per head
+  int n1;                        // head index split of the column maps (hb % n1, hb / n1)
   int64_t n_groups;              // bh * nblk
   float scale, min_col_mass;
 };
 
-__device__ __forceinline__ void tma_load_4d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, int w,
-                                            uint32_t bar) {
+// Column maps are rank 5: (element, grid column j, grid row i, c1, c3), the head index hb split as
+// c1 = hb % n1 and c3 = hb / n1 (make_map_col); callers split hb once per column group.
+__device__ __forceinline__ void tma_load_col(uint32_t dst, const CUtensorMap* map, int x, int j, int c1, int c3,
+                                             uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
-      "[%6];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(w), "r"(bar)
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(j), "r"(0), "r"(c1), "r"(c3), "r"(bar)
       : "memory");
 }
-__device__ __forceinline__ void tma_store_4d(const CUtensorMap* map, int x, int y, int z, int w, uint32_t src) {
-  asm volatile("cp.async.bulk.tensor.4d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4}], [%5];" ::"l"(
+__device__ __forceinline__ void tma_store_col(const CUtensorMap* map, int x, int j, int c1, int c3, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z), "r"(w), "r"(src)
+               "r"(x), "r"(j), "r"(0), "r"(c1), "r"(c3), "r"(src)
                : "memory");
 }
-__device__ __forceinline__ void tma_prefetch_4d(const CUtensorMap* map, int x, int y, int z, int w) {
-  asm volatile("cp.async.bulk.prefetch.tensor.4d.L2.global.tile [%0, {%1, %2, %3, %4}];" ::"l"(
+__device__ __forceinline__ void tma_prefetch_col(const CUtensorMap* map, int x, int j, int c1, int c3) {
+  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z), "r"(w)
+               "r"(x), "r"(j), "r"(0), "r"(c1), "r"(c3)
                : "memory");
 }
 __device__ __forceinline__ void st_shared_v4(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
@@ -141,20 +144,22 @@ __global__ void __launch_bounds__(128, 3) lstep_fwd_tc_kernel(const __grid_const
 
   auto load_group = [&](int64_t g) {  // thread 0
     const int hb = (int)(g / p.nblk), j0 = (int)(g % p.nblk) * kCols;
+    const int c3 = hb / p.n1, c1 = hb - c3 * p.n1;
     mbar_expect_tx(bar_ld, kLoadBytes);
     for (int c = 0; c < kCols; ++c) {
       const uint32_t ro = c * 32 * 128;
-      tma_load_4d(sQ + ro, &p.tm_q, 0, j0 + c, 0, hb, bar_ld);
-      tma_load_4d(sQ + kAtom + ro, &p.tm_q, 64, j0 + c, 0, hb, bar_ld);
-      for (int a = 0; a < C::OATOMS; ++a) tma_load_4d(sO + a * kAtom + ro, &p.tm_o, 64 * a, j0 + c, 0, hb, bar_ld);
+      tma_load_col(sQ + ro, &p.tm_q, 0, j0 + c, c1, c3, bar_ld);
+      tma_load_col(sQ + kAtom + ro, &p.tm_q, 64, j0 + c, c1, c3, bar_ld);
+      for (int a = 0; a < C::OATOMS; ++a) tma_load_col(sO + a * kAtom + ro, &p.tm_o, 64 * a, j0 + c, c1, c3, bar_ld);
     }
   };
   auto prefetch_group = [&](int64_t g) {  // thread 0: the boxes of a later group into L2
     const int hb = (int)(g / p.nblk), j0 = (int)(g % p.nblk) * kCols;
+    const int c3 = hb / p.n1, c1 = hb - c3 * p.n1;
     for (int c = 0; c < kCols; ++c) {
-      tma_prefetch_4d(&p.tm_q, 0, j0 + c, 0, hb);
-      tma_prefetch_4d(&p.tm_q, 64, j0 + c, 0, hb);
-      for (int a = 0; a < C::OATOMS; ++a) tma_prefetch_4d(&p.tm_o, 64 * a, j0 + c, 0, hb);
+      tma_prefetch_col(&p.tm_q, 0, j0 + c, c1, c3);
+      tma_prefetch_col(&p.tm_q, 64, j0 + c, c1, c3);
+      for (int a = 0; a < C::OATOMS; ++a) tma_prefetch_col(&p.tm_o, 64 * a, j0 + c, c1, c3);
     }
   };
 
@@ -283,9 +288,10 @@ __global__ void __launch_bounds__(128, 3) lstep_fwd_tc_kernel(const __grid_const
     ok = __syncthreads_and(ok ? 1 : 0) != 0;
     tc_fence_after();
     if (tid == 0 && ok && !*abort) {
+      const int c3 = hb / p.n1, c1 = hb - c3 * p.n1;
       for (int c = 0; c < kCols; ++c) {
-        tma_store_4d(&p.tm_y, 0, j0 + c, 0, hb, sQ + c * 32 * 128);
-        tma_store_4d(&p.tm_y, 64, j0 + c, 0, hb, sQ + kAtom + c * 32 * 128);
+        tma_store_col(&p.tm_y, 0, j0 + c, c1, c3, sQ + c * 32 * 128);
+        tma_store_col(&p.tm_y, 64, j0 + c, c1, c3, sQ + kAtom + c * 32 * 128);
       }
       tma_store_commit_and_wait();  // the staging (Q's atoms) is read before the next group's load
       if (g + gridDim.x < p.n_groups) {
@@ -304,16 +310,26 @@ __global__ void __launch_bounds__(128, 3) lstep_fwd_tc_kernel(const __grid_const
   if (warp == 0) tmem_dealloc(tmem, 128);
 }
 
-// 4-D map over one [bh][m][b][W] tensor of 16-bit elements (token i b + j of head h at row
-// (h m + i) b + j), boxes {64 elements, 1 column, m rows, 1 head}, 128-byte swizzle.
-bool make_map_col(CUtensorMap* map, const void* ptr, bool bf16, int W, int64_t b, int64_t m, int64_t bh) {
+// 5-D map over the view `v` of one [bh][N][W] tensor of 16-bit elements (token i b + j of head hb
+// at row i b + j): dims (W, b, m, n1, bh / n1), boxes {64 elements, 1 column, 32 rows, 1, 1},
+// 128-byte swizzle. Rows past m are zero-filled on load and skipped on store. The view's split
+// must have n2 = 1 (hb = c1 + n1 c3).
+bool make_map_col(CUtensorMap* map, const void* ptr, bool bf16, int W, int64_t b, int64_t m, int64_t bh,
+                  const View& v, int n1) {
   tma::EncodeTiledFn enc = tma::encode_fn();
-  if (!enc) return false;
-  cuuint64_t dims[4] = {(cuuint64_t)W, (cuuint64_t)b, (cuuint64_t)m, (cuuint64_t)bh};
-  cuuint64_t strides[3] = {(cuuint64_t)W * 2, (cuuint64_t)(b * W * 2), (cuuint64_t)(m * b * W * 2)};
-  cuuint32_t box[4] = {64, 1, 32, 1};  // rows past m: zero-filled on load, skipped on store
-  cuuint32_t estr[4] = {1, 1, 1, 1};
-  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 4, const_cast<void*>(ptr),
+  if (!enc || n1 < 1 || bh % n1) return false;
+  const int64_t n3 = bh / n1;
+  cuuint64_t dims[5] = {(cuuint64_t)W, (cuuint64_t)b, (cuuint64_t)m, (cuuint64_t)n1, (cuuint64_t)n3};
+  int64_t st[4] = {v.rs * 2, v.rs * b * 2, v.s1 * 2, v.s3 * 2};
+  const int64_t ext[4] = {b, m, n1, n3};
+  for (int i = 0; i < 4; ++i) {
+    if (ext[i] == 1 && (st[i] <= 0 || st[i] % 16)) st[i] = v.rs * b * m * 2;  // unused stride
+    if (st[i] <= 0 || st[i] % 16) return false;
+  }
+  cuuint64_t strides[4] = {(cuuint64_t)st[0], (cuuint64_t)st[1], (cuuint64_t)st[2], (cuuint64_t)st[3]};
+  cuuint32_t box[5] = {64, 1, 32, 1, 1};  // rows past m: zero-filled on load, skipped on store
+  cuuint32_t estr[5] = {1, 1, 1, 1, 1};
+  return enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 5, const_cast<void*>(ptr),
              dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -330,9 +346,11 @@ cudaError_t launch_fwd(const LstepParams& lp, cudaStream_t st) {
   p.ent = lp.ent;
   p.scale = lp.scale;
   p.min_col_mass = lp.min_col_mass;
-  if (!make_map_col(&p.tm_q, lp.q, bf16, 128, lp.b, lp.m, lp.bh)) return cudaErrorInvalidValue;
-  if (!make_map_col(&p.tm_o, lp.out, bf16, lp.dw, lp.b, lp.m, lp.bh)) return cudaErrorInvalidValue;
-  if (!make_map_col(&p.tm_y, LAST ? lp.z : lp.u, bf16, 128, lp.b, lp.m, lp.bh)) return cudaErrorInvalidValue;
+  p.n1 = lp.n1;
+  if (!make_map_col(&p.tm_q, lp.q, bf16, 128, lp.b, lp.m, lp.bh, lp.qv, lp.n1)) return cudaErrorInvalidValue;
+  if (!make_map_col(&p.tm_o, lp.out, bf16, lp.dw, lp.b, lp.m, lp.bh, lp.outv, lp.n1)) return cudaErrorInvalidValue;
+  if (!make_map_col(&p.tm_y, LAST ? lp.z : lp.u, bf16, 128, lp.b, lp.m, lp.bh, LAST ? lp.zv : lp.uv, lp.n1))
+    return cudaErrorInvalidValue;
   auto kern = lstep_fwd_tc_kernel<T, LAST>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, FwdCfg<LAST>::SMEM);
   if (e != cudaSuccess) return e;

@@ -15,10 +15,11 @@
 
 namespace vmb {
 
-// LPR lanes per row (dv / 32 of them: 2, 4 or 8), each loading four 16-byte chunks of o and of dO
-// up front, so a warp has 32 / LPR rows and eight loads per lane in flight.
-template <typename T, int LPR>
-__global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_bs, const T* dout, int64_t do_bs,
+// LPR lanes per row, each loading CPL 16-byte chunks of o and of dO up front (dv = 8 CPL LPR: 16
+// and 32 take one lane with two or four chunks, 64 / 128 / 256 take 2 / 4 / 8 lanes with four), so
+// a warp has 32 / LPR rows and 2 CPL loads per lane in flight.
+template <typename T, int LPR, int CPL>
+__global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, View ov, const T* dout, View dov, int n1, int n2,
                                                           const float* lse, const float* ent, const float* dent,
                                                           float* cc, float* gg, int64_t rows, int n_q, int dv,
                                                           float* fold, int64_t n_pad, int64_t plane, float sm_scale,
@@ -32,16 +33,16 @@ __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_
   const bool real = live && r < n_q;      // false: padding row of the folded planes
   float acc = 0.f;
   if (real && !delta) {
-    const uint4* po = reinterpret_cast<const uint4*>(o + bi * o_bs + r * dv);
-    const uint4* pd = reinterpret_cast<const uint4*>(dout + bi * do_bs + r * dv);
-    uint4 va[4], vb[4];
+    const uint4* po = reinterpret_cast<const uint4*>(o + view_offset(ov, n1, n2, bi, r));
+    const uint4* pd = reinterpret_cast<const uint4*>(dout + view_offset(dov, n1, n2, bi, r));
+    uint4 va[CPL], vb[CPL];
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < CPL; ++u) {
       va[u] = po[gl + u * LPR];
       vb[u] = pd[gl + u * LPR];
     }
 #pragma unroll
-    for (int u = 0; u < 4; ++u) {
+    for (int u = 0; u < CPL; ++u) {
       const uint32_t wa[4] = {va[u].x, va[u].y, va[u].z, va[u].w}, wb[4] = {vb[u].x, vb[u].y, vb[u].z, vb[u].w};
 #pragma unroll
       for (int e = 0; e < 4; ++e) {
@@ -79,30 +80,38 @@ __global__ void __launch_bounds__(256) fea_bwd_pre_kernel(const T* o, int64_t o_
   }
 }
 
-template <typename T, int LPR>
-void launch_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse, const float* ent,
+template <typename T, int LPR, int CPL>
+void launch_pre(const void* o, View ov, const void* dout, View dov, int n1, int n2, const float* lse, const float* ent,
                 const float* dent, float* cc, float* gg, int64_t rows, int n_q, int dv, float* fold, int64_t n_pad,
                 int64_t plane, float sm_scale, const float* delta, cudaStream_t st) {
   const int64_t warps = (rows + 32 / LPR - 1) / (32 / LPR);
-  fea_bwd_pre_kernel<T, LPR><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
-      static_cast<const T*>(o), o_bs, static_cast<const T*>(dout), do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold,
+  fea_bwd_pre_kernel<T, LPR, CPL><<<(unsigned)((warps + 7) / 8), 256, 0, st>>>(
+      static_cast<const T*>(o), ov, static_cast<const T*>(dout), dov, n1, n2, lse, ent, dent, cc, gg, rows, n_q, dv, fold,
       n_pad, plane, sm_scale, delta);
 }
 
-cudaError_t fea_bwd_pre(const void* o, int64_t o_bs, const void* dout, int64_t do_bs, const float* lse,
+cudaError_t fea_bwd_pre(const void* o, View ov, const void* dout, View dov, int n1, int n2, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
                         float* fold, int64_t n_pad, float sm_scale, const float* delta, bool bf16, cudaStream_t st) {
   const int64_t rows = batch * (fold ? n_pad : n_q);
   const int64_t plane = batch * n_pad;
   if ((rows + 3) / 4 / 8 + 1 > 0x7fffffff) return cudaErrorInvalidConfiguration;
-  if (dv != 64 && dv != 128 && dv != 256) return cudaErrorInvalidValue;
-  const int lpr = dv / 32;
-#define VMB_PRE(TT, L) launch_pre<TT, L>(o, o_bs, dout, do_bs, lse, ent, dent, cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale, delta, st)
-  if (bf16) {
-    if (lpr == 2) VMB_PRE(__nv_bfloat16, 2); else if (lpr == 4) VMB_PRE(__nv_bfloat16, 4); else VMB_PRE(__nv_bfloat16, 8);
-  } else {
-    if (lpr == 2) VMB_PRE(__half, 2); else if (lpr == 4) VMB_PRE(__half, 4); else VMB_PRE(__half, 8);
+#define VMB_PRE(TT, L, C) launch_pre<TT, L, C>(o, ov, dout, dov, n1, n2, lse, ent, dent, cc, gg, rows, n_q, dv, fold, n_pad, plane, sm_scale, delta, st)
+#define VMB_PRE_ALL(TT)                          \
+  switch (dv) {                                  \
+    case 16: VMB_PRE(TT, 1, 2); break;           \
+    case 32: VMB_PRE(TT, 1, 4); break;           \
+    case 64: VMB_PRE(TT, 2, 4); break;           \
+    case 128: VMB_PRE(TT, 4, 4); break;          \
+    case 256: VMB_PRE(TT, 8, 4); break;          \
+    default: return cudaErrorInvalidValue;       \
   }
+  if (bf16) {
+    VMB_PRE_ALL(__nv_bfloat16)
+  } else {
+    VMB_PRE_ALL(__half)
+  }
+#undef VMB_PRE_ALL
 #undef VMB_PRE
   return cudaGetLastError();
 }
@@ -133,6 +142,41 @@ cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs
     cast_f32_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, src_bs, static_cast<__nv_bfloat16*>(dst), dst_bs, n4, total4);
   else
     cast_f32_kernel<__half><<<blocks, 256, 0, st>>>(src, src_bs, static_cast<__half*>(dst), dst_bs, n4, total4);
+  return cudaGetLastError();
+}
+
+// dst(s, r, c) = (T) src(s, r, c) over [batch][rows][cols] views (cols % 4 == 0, 16-byte aligned
+// rows): the fp32 accumulator of a strided (e.g. token-major) gradient converted in place of
+// cast_f32's flat rows. One thread per 4 columns of a row.
+template <typename T>
+__global__ void cast_f32_view_kernel(const float* src, View sv, T* dst, View dvw, int n1, int n2, int64_t rows,
+                                     int64_t c4, int64_t total4) {
+  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total4; idx += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t row = idx / c4, c = (idx % c4) * 4;
+    const int64_t bi = row / rows, r = row % rows;
+    const float4 v = *reinterpret_cast<const float4*>(src + view_offset(sv, n1, n2, bi, r) + c);
+    uint2 w;
+    w.x = Elem<T>::pack(v.x, v.y);
+    w.y = Elem<T>::pack(v.z, v.w);
+    *reinterpret_cast<uint2*>(dst + view_offset(dvw, n1, n2, bi, r) + c) = w;
+  }
+}
+
+cudaError_t cast_f32_view(const float* src, const View& sv, void* dst, const View& dvw, int n1, int n2, int64_t batch,
+                          int64_t rows, int64_t cols, bool bf16, cudaStream_t st) {
+  const int64_t c4 = cols / 4, total4 = batch * rows * c4;
+  if (total4 == 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t want = (total4 + 255) / 256;
+  const unsigned blocks = (unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  if (bf16)
+    cast_f32_view_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, sv, static_cast<__nv_bfloat16*>(dst), dvw, n1, n2,
+                                                                rows, c4, total4);
+  else
+    cast_f32_view_kernel<__half><<<blocks, 256, 0, st>>>(src, sv, static_cast<__half*>(dst), dvw, n1, n2, rows, c4,
+                                                         total4);
   return cudaGetLastError();
 }
 

@@ -38,13 +38,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // error word and sets `abort`, so the whole CTA drains and frees its TMEM instead of hanging.
 constexpr long long kWaitCycles = 4000000000ll;
 
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err, int code) {
+// `limit` (cycles) shortens the time limit for a test of this path (0: kWaitCycles).
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, volatile int* abort, int* err, int code,
+                                          long long limit = 0) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
+  const long long lim = limit > 0 ? limit : kWaitCycles;
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
     if (*abort) return false;
-    if (clock64() - t0 > kWaitCycles) {
+    if (clock64() - t0 > lim) {
       *abort = 1;
       atomicOr(err, code);
       return false;
@@ -62,11 +65,24 @@ __device__ __forceinline__ bool mbar_wait_drain(uint32_t bar, uint32_t parity) {
 }
 
 // ---------------------------------------------------------------------------------- TMA
-__device__ __forceinline__ void tma_load_3d(uint32_t dst, const CUtensorMap* map, int x, int y, int z, uint32_t bar) {
+// Every tensor map is rank 5 (tma_host.h): (column, row, c1, c2, c3), where (c1, c2, c3) is a
+// batch entry split by the call's (n1, n2). An int converts to (0, 0, z): the coordinate of a map
+// built without a split (n1 = n2 = 1).
+struct BIdx {
+  int c1, c2, c3;
+  __device__ __forceinline__ BIdx(int z) : c1(0), c2(0), c3(z) {}
+  __device__ __forceinline__ BIdx(int a, int b, int c) : c1(a), c2(b), c3(c) {}
+};
+__device__ __forceinline__ BIdx bidx(int s, int n1, int n2) {
+  const int t = s / n1;
+  return BIdx(s - t * n1, t % n2, t / n2);
+}
+
+__device__ __forceinline__ void tma_load(uint32_t dst, const CUtensorMap* map, int x, int y, BIdx b, uint32_t bar) {
   asm volatile(
-      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
-      "[%5];" ::"r"(dst),
-      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(bar)
+      "cp.async.bulk.tensor.5d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5, "
+      "%6}], [%7];" ::"r"(dst),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(b.c1), "r"(b.c2), "r"(b.c3), "r"(bar)
       : "memory");
 }
 // Plain (untiled) bulk copy global -> shared, completing on `bar`; both addresses 16-byte aligned,
@@ -77,25 +93,25 @@ __device__ __forceinline__ void bulk_load(uint32_t dst, const void* src, uint32_
                : "memory");
 }
 // Prefetch of a tile into L2 (no shared memory, no barrier): hides DRAM latency of a later load.
-__device__ __forceinline__ void tma_prefetch_3d(const CUtensorMap* map, int x, int y, int z) {
-  asm volatile("cp.async.bulk.prefetch.tensor.3d.L2.global.tile [%0, {%1, %2, %3}];" ::"l"(
+__device__ __forceinline__ void tma_prefetch(const CUtensorMap* map, int x, int y, BIdx b) {
+  asm volatile("cp.async.bulk.prefetch.tensor.5d.L2.global.tile [%0, {%1, %2, %3, %4, %5}];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z)
+               "r"(x), "r"(y), "r"(b.c1), "r"(b.c2), "r"(b.c3)
                : "memory");
 }
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, int x, int y, int z, uint32_t src) {
-  asm volatile("cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+__device__ __forceinline__ void tma_store(const CUtensorMap* map, int x, int y, BIdx b, uint32_t src) {
+  asm volatile("cp.async.bulk.tensor.5d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(
                    reinterpret_cast<uint64_t>(map)),
-               "r"(x), "r"(y), "r"(z), "r"(src)
+               "r"(x), "r"(y), "r"(b.c1), "r"(b.c2), "r"(b.c3), "r"(src)
                : "memory");
 }
 // Element-wise global += smem tile (fp32 add performed by the memory system), rows past the map's
 // extent clipped.
-__device__ __forceinline__ void tma_reduce_add_3d(const CUtensorMap* map, int x, int y, int z, uint32_t src) {
+__device__ __forceinline__ void tma_reduce_add(const CUtensorMap* map, int x, int y, BIdx b, uint32_t src) {
   asm volatile(
-      "cp.reduce.async.bulk.tensor.3d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(
+      "cp.reduce.async.bulk.tensor.5d.global.shared::cta.add.tile.bulk_group [%0, {%1, %2, %3, %4, %5}], [%6];" ::"l"(
           reinterpret_cast<uint64_t>(map)),
-      "r"(x), "r"(y), "r"(z), "r"(src)
+      "r"(x), "r"(y), "r"(b.c1), "r"(b.c2), "r"(b.c3), "r"(src)
       : "memory");
 }
 __device__ __forceinline__ void tma_store_commit_and_wait() {

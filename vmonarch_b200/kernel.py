@@ -4,6 +4,8 @@ Drop-in for ``video_monarch_attention.kernel`` (reference ``video_monarch_attent
 same function name, arguments, return values and assertion behaviour. The forward and backward
 run on the hand-written sm_100a kernels behind the C ABI (``include/vmonarch_b200.h``); there is
 no padding copy (the reference pads N to a multiple of 128, kernel.py:399-400) and no autotuning.
+Token-major inputs ((B, N, H, D) buffers seen as (B, H, N, D) through transpose(1, 2)) are read in
+place and o is returned in the same layout.
 """
 from __future__ import annotations
 
@@ -36,8 +38,14 @@ class _FlashEntropyAttention(torch.autograd.Function):
         del warp_specialize  # accepted for API compatibility; the kernels are always specialised
         B, H, N, D = q.shape
         Dv = v.shape[-1]
-        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-        o = torch.empty((B, H, N, Dv), device=q.device, dtype=q.dtype)
+        # dense or token-major ((B, N, H, D) seen through transpose(1, 2)) inputs are read in place
+        # by the D = Dv = 128 kernels; other head dims take dense copies
+        strided = D == 128 and Dv == 128
+        q, k, v = (t if strided and ops.viewable(t) else t.contiguous() for t in (q, k, v))
+        if q.size(1) > 1 and N > 1 and q.stride(1) < q.stride(2):   # token-major: o in the same layout
+            o = torch.empty((B, N, H, Dv), device=q.device, dtype=q.dtype).transpose(1, 2)
+        else:
+            o = torch.empty((B, H, N, Dv), device=q.device, dtype=q.dtype)
         lse = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
         ent = torch.empty((B, H, N), device=q.device, dtype=torch.float32)
         ops.fea_fwd(q, k, v, o, lse, ent, sm_scale)
@@ -51,9 +59,11 @@ class _FlashEntropyAttention(torch.autograd.Function):
         q, k, v, o, lse, ent = ctx.saved_tensors
         if do is None:
             do = torch.zeros_like(o)
-        do = do.to(q.dtype).contiguous()
+        do = do.to(q.dtype)
+        do = do if q.size(-1) == 128 and do.size(-1) == 128 and ops.viewable(do) else do.contiguous()
         if de is not None:
             de = de.float().contiguous()
+        # empty_like keeps a dense or token-major input's strides for its gradient
         dq, dk, dv = torch.empty_like(q), torch.empty_like(k), torch.empty_like(v)
         ops.fea_bwd(q, k, v, o, do, lse, dq, dk, dv, ctx.sm_scale, ent=ent, dent=de, grad_mode=0)
         return dq, dk, dv, None, None

@@ -1,11 +1,18 @@
 """Thin tensor-level wrappers around the C-ABI entry points (one function per entry point).
 
-All tensors must be CUDA tensors on the same device, with contiguous rows; batch strides are
-taken from the tensors. Work is enqueued on the current torch stream of that device.
+Every tensor is a CUDA tensor of shape (*batch, rows, cols) with contiguous columns; all tensors
+of a call share the batch shape, which has one to three dimensions. The tensors' own strides are
+handed to the kernels as a strided layout (``vmb_fea_layout`` / ``vmb_lstep_layout`` in
+include/vmonarch_b200.h), so a token-major caller tensor, a (B, N, H, D) buffer seen as
+(B, H, N, D) through ``transpose(1, 2)``, is read and written in place: with batch shape (B, H)
+the innermost batch dimension H is the layout's n1 and B its n2; with (B, H, m) grid rows (the
+VMonarch R step) m is n1, H is n2 and B the outermost. Statistics (lse, ent, dent, delta) are
+dense fp32 [batch][rows]. Work is enqueued on the current torch stream of the tensors' device.
 """
 from __future__ import annotations
 
 import ctypes
+import math
 import os
 
 import torch
@@ -42,37 +49,68 @@ def _call(name: str, fn, arg, dev) -> None:
         N.check(fn(ctypes.byref(arg), N.stream_ptr(dev)), name)
 
 
-def _bs(t: torch.Tensor, rows_dims: int = 2) -> int:
-    """Batch stride (elements) of a tensor viewed as [batch][rows][cols] with contiguous rows."""
-    if t.stride(-1) != 1 or (t.dim() >= 2 and t.size(-2) > 1 and t.stride(-2) != t.size(-1)):
-        raise AssertionError("rows must be contiguous")
-    return t.stride(-3) if t.dim() >= 3 else t.size(-2) * t.size(-1)
+# ----------------------------------------------------------------------------------------- layouts
+def viewable(t: torch.Tensor) -> bool:
+    """True when the kernels can read or write `t` (shape (..., rows, cols)) in place: contiguous
+    columns, 16-byte aligned base, every other stride a non-negative multiple of 16 bytes and rows
+    at least `cols` apart. Otherwise the caller passes ``t.contiguous()``."""
+    if t.dim() < 3 or t.stride(-1) != 1 or t.data_ptr() % 16:
+        return False
+    align = 16 // t.element_size()
+    for i in range(t.dim() - 1):
+        if t.size(i) > 1 and (t.stride(i) < 0 or t.stride(i) % align):
+            return False
+    return t.size(-2) <= 1 or t.stride(-2) >= t.size(-1)
 
 
-def _flat3(t: torch.Tensor) -> torch.Tensor:
-    """View [..., rows, cols] as [batch, rows, cols] without copying (batch dims must be uniform).
+def _view(t: torch.Tensor, nb: int) -> N.View:
+    """The vmb_view of a (*batch[nb], rows, cols) tensor: row stride, then the strides of the
+    innermost, middle and outermost batch dimension (0 for absent or size-1 dimensions)."""
+    if t.stride(-1) != 1 and t.size(-1) > 1:
+        raise AssertionError("columns must be contiguous")
+    rows, cols = t.size(-2), t.size(-1)
+    rs = t.stride(-2) if rows > 1 else cols
+    st = [t.stride(-3 - i) if t.size(-3 - i) > 1 else 0 for i in range(nb)] + [0] * (3 - nb)
+    return N.View(rs, st[0], st[1], st[2])
 
-    ``view`` (not ``reshape``) so that an output can never silently become a copy."""
-    if t.dim() == 3:
-        return t
-    return t.view(-1, t.size(-2), t.size(-1))
+
+def _split(batch_shape) -> tuple[int, int]:
+    """(n1, n2) of a batch shape: the innermost dimension, then the next one (1 if absent)."""
+    if not 1 <= len(batch_shape) <= 3:
+        raise AssertionError(f"batch shape {tuple(batch_shape)} must have one to three dimensions")
+    return int(batch_shape[-1]), int(batch_shape[-2]) if len(batch_shape) >= 2 else 1
 
 
+def _stats(t, batch: int, rows: int):
+    if t is None:
+        return None
+    if not t.is_contiguous() or t.numel() != batch * rows or t.dtype != torch.float32:
+        raise AssertionError("statistics must be contiguous fp32 [batch][rows]")
+    return t.data_ptr()
+
+
+# ----------------------------------------------------------------------------------------- forward
 def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
-    """o[b] = softmax(sm_scale q[b] k[b]^T) [v[b] | v2[b]]; lse/ent per query row (see header)."""
-    q3, k3, v3, o3 = _flat3(q), _flat3(k), _flat3(v), _flat3(o)
-    v23 = _flat3(v2) if v2 is not None else None
+    """o = softmax(sm_scale q k^T) [v | v2] per batch entry; lse/ent per query row (see header)."""
+    bshape = q.shape[:-2]
+    nb = len(bshape)
+    for t in (k, v, o, v2):
+        if t is not None and t.shape[:-2] != bshape:
+            raise AssertionError("q, k, v, v2 and o must share their batch shape")
+    n1, n2 = _split(bshape)
+    batch = math.prod(bshape)
+    lay = N.FeaLayout()
+    lay.n1, lay.n2 = n1, n2
     a = N.FeaFwdArgs()
-    a.q, a.q_bs = q3.data_ptr(), _bs(q3)
-    a.k, a.k_bs = k3.data_ptr(), _bs(k3)
-    a.v, a.v_bs = v3.data_ptr(), _bs(v3)
-    if v23 is not None:
-        a.v2, a.v2_bs = v23.data_ptr(), _bs(v23)
-    a.o, a.o_bs = o3.data_ptr(), _bs(o3)
-    a.lse = N.ptr(lse)
-    a.ent = N.ptr(ent)
-    a.batch, a.n_q, a.n_kv = q3.size(0), q3.size(1), k3.size(1)
-    a.d, a.dv, a.dv1 = q3.size(2), o3.size(2), v3.size(2)
+    for name, t in (("q", q), ("k", k), ("v", v), ("v2", v2), ("o", o)):
+        if t is not None:
+            setattr(a, name, t.data_ptr())
+            setattr(lay, name, _view(t, nb))
+    a.layout = ctypes.pointer(lay)
+    a.lse = _stats(lse, batch, q.size(-2))
+    a.ent = _stats(ent, batch, q.size(-2))
+    a.batch, a.n_q, a.n_kv = batch, q.size(-2), k.size(-2)
+    a.d, a.dv, a.dv1 = q.size(-1), o.size(-1), v.size(-1)
     a.dtype = N.dtype_code(q.dtype)
     a.sm_scale = float(sm_scale)
     nbytes = N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a))
@@ -83,6 +121,44 @@ def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
     _call("vmb_fea_fwd", N.lib.vmb_fea_fwd, a, q.device)
 
 
+# ----------------------------------------------------------------------------------------- backward
+_BWD_TENSORS = ("q", "k", "v", "v2", "o", "dout", "grad_q", "grad_k", "grad_v", "grad_v2", "fin_q", "fin_k", "fin_v",
+                "fin_v2")
+_BWD_STATS = ("lse", "ent", "dent", "delta")
+
+
+def bwd_args(t: dict, sm_scale: float, grad_mode: int, v_is_k: bool, deterministic: bool):
+    """vmb_fea_bwd_args (and the layout it points to) for the tensors in `t` (names of
+    _BWD_TENSORS and _BWD_STATS, absent or None when unused)."""
+    q, k, o, v = t["q"], t["k"], t["o"], t["v"]
+    bshape = q.shape[:-2]
+    nb = len(bshape)
+    n1, n2 = _split(bshape)
+    batch = math.prod(bshape)
+    lay = N.FeaLayout()
+    lay.n1, lay.n2 = n1, n2
+    a = N.FeaBwdArgs()
+    for name in _BWD_TENSORS:
+        x = t.get(name)
+        if x is None:
+            continue
+        if x.shape[:-2] != bshape:
+            raise AssertionError(f"{name} does not share the batch shape {tuple(bshape)}")
+        setattr(a, name, x.data_ptr())
+        setattr(lay, name, _view(x, nb))
+    a.layout = ctypes.pointer(lay)
+    for name in _BWD_STATS:
+        setattr(a, name, _stats(t.get(name), batch, q.size(-2)))
+    a.batch, a.n_q, a.n_kv = batch, q.size(-2), k.size(-2)
+    a.d, a.dv, a.dv1 = q.size(-1), o.size(-1), v.size(-1)
+    a.dtype = N.dtype_code(q.dtype)
+    a.grad_mode = grad_mode
+    a.v_is_k = int(v_is_k)
+    a.sm_scale = float(sm_scale)
+    a.deterministic = int(bool(deterministic))
+    return a, lay
+
+
 def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, ent=None, dent=None, v2=None,
             grad_v2=None, grad_mode: int = 0, v_is_k: bool = False, delta=None, deterministic=None, fin_q=None,
             fin_k=None, fin_v=None, fin_v2=None) -> None:
@@ -91,52 +167,50 @@ def fea_bwd(q, k, v, o, dout, lse, grad_q, grad_k, grad_v, sm_scale: float, *, e
     ``fin_*`` are the fp32 accumulators of grad_mode 3 (16-bit grad_* = fin_* + this gradient)."""
     if deterministic is None:
         deterministic = torch.are_deterministic_algorithms_enabled()
-    q3, k3, v3, o3, do3 = _flat3(q), _flat3(k), _flat3(v), _flat3(o), _flat3(dout)
-    a = N.FeaBwdArgs()
-    a.q, a.q_bs = q3.data_ptr(), _bs(q3)
-    a.k, a.k_bs = k3.data_ptr(), _bs(k3)
-    a.v, a.v_bs = v3.data_ptr(), _bs(v3)
-    if v2 is not None:
-        v23 = _flat3(v2)
-        a.v2, a.v2_bs = v23.data_ptr(), _bs(v23)
-    a.o, a.o_bs = o3.data_ptr(), _bs(o3)
-    a.dout, a.do_bs = do3.data_ptr(), _bs(do3)
-    a.lse, a.ent, a.dent = N.ptr(lse), N.ptr(ent), N.ptr(dent)
-    a.delta = N.ptr(delta)  # optional sum o . dout per query row (e.g. from lstep_bwd's delta_out)
-    gq3, gk3 = _flat3(grad_q), _flat3(grad_k)
-    a.grad_q, a.grad_q_bs = gq3.data_ptr(), _bs(gq3)
-    a.grad_k, a.grad_k_bs = gk3.data_ptr(), _bs(gk3)
-    if grad_v is not None:
-        gv3 = _flat3(grad_v)
-        a.grad_v, a.grad_v_bs = gv3.data_ptr(), _bs(gv3)
-    if grad_v2 is not None:
-        gv23 = _flat3(grad_v2)
-        a.grad_v2, a.grad_v2_bs = gv23.data_ptr(), _bs(gv23)
-    a.batch, a.n_q, a.n_kv = q3.size(0), q3.size(1), k3.size(1)
-    a.d, a.dv, a.dv1 = q3.size(2), o3.size(2), v3.size(2)
-    a.dtype = N.dtype_code(q.dtype)
-    a.grad_mode = grad_mode
-    a.v_is_k = int(v_is_k)
-    a.sm_scale = float(sm_scale)
-    a.deterministic = int(bool(deterministic))
-    for name, t in (("fin_q", fin_q), ("fin_k", fin_k), ("fin_v", fin_v), ("fin_v2", fin_v2)):
-        if t is not None:
-            t3 = _flat3(t)
-            setattr(a, name, t3.data_ptr())
-            setattr(a, name + "_bs", _bs(t3))
-    chunk, nbytes = bwd_plan(a)
+    t = dict(q=q, k=k, v=v, v2=v2, o=o, dout=dout, grad_q=grad_q, grad_k=grad_k, grad_v=grad_v, grad_v2=grad_v2,
+             fin_q=fin_q, fin_k=fin_k, fin_v=fin_v, fin_v2=fin_v2, lse=lse, ent=ent, dent=dent, delta=delta)
+    a, lay = bwd_args(t, sm_scale, grad_mode, v_is_k, deterministic)
+    bshape = q.shape[:-2]
+    cdim = 1 if len(bshape) >= 2 else 0          # batch dimension the chunks run along
+    unit = math.prod(bshape[cdim + 1:])          # sequences per index of that dimension
+    chunk, nbytes = bwd_plan(a, unit=unit, group=unit * bshape[cdim])
     try:
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
     except torch.OutOfMemoryError:
         # no room for the preferred workspace: one call with the minimal one
         chunk, nbytes = a.batch, N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a))
         ws = torch.empty(max(nbytes, 1), dtype=torch.uint8, device=q.device)
-    a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
     if chunk >= a.batch:
+        a.workspace, a.workspace_bytes = ws.data_ptr(), nbytes
         _call("vmb_fea_bwd", N.lib.vmb_fea_bwd, a, q.device)
         return
-    for start in range(0, a.batch, chunk):
-        _call("vmb_fea_bwd", N.lib.vmb_fea_bwd, _bwd_chunk(a, start, min(chunk, a.batch - start)), q.device)
+    # chunks of `chunk // unit` indices along batch dimension cdim, for every index of the outer ones
+    n_q = q.size(-2)
+    per = chunk // unit
+    for outer in _outer_indices(bshape[:cdim]):
+        for i0 in range(0, bshape[cdim], per):
+            idx = outer + (slice(i0, min(i0 + per, bshape[cdim])),)
+            sub = {}
+            for name, x in t.items():
+                if x is None:
+                    continue
+                if name in _BWD_STATS:
+                    x = x.view(*bshape, n_q)
+                sub[name] = x[idx]
+                if name in _BWD_STATS:
+                    sub[name] = sub[name].reshape(-1)  # contiguous: only outer dims are fixed
+            b, lay_b = bwd_args(sub, sm_scale, grad_mode, v_is_k, deterministic)
+            b.workspace, b.workspace_bytes = ws.data_ptr(), nbytes
+            _call("vmb_fea_bwd", N.lib.vmb_fea_bwd, b, q.device)
+
+
+def _outer_indices(shape):
+    if not shape:
+        yield ()
+        return
+    for i in range(shape[0]):
+        for rest in _outer_indices(shape[1:]):
+            yield (i,) + rest
 
 
 def set_workspace_limit(nbytes: int) -> None:
@@ -149,75 +223,74 @@ def workspace_limit() -> int:
     return _workspace_limit
 
 
-def bwd_plan(a: N.FeaBwdArgs) -> tuple[int, int]:
+def bwd_plan(a: N.FeaBwdArgs, unit: int = 1, group: int = 0) -> tuple[int, int]:
     """(sequences per call, workspace bytes) of a backward call under the workspace bound: the whole
-    batch with its preferred workspace when that fits; else the fewest equal batch chunks whose
-    preferred workspace fits and still holds the dS^T buffer; else the whole batch with the minimal
-    workspace."""
+    batch with its preferred workspace when that fits; else the largest chunk (a multiple of `unit`
+    sequences, at most `group`, so chunks never cross a `group` boundary) whose preferred workspace
+    fits and still holds the dS^T buffer; else the whole batch with the minimal workspace."""
     pref = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a))
     low = N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(a))
     batch = a.batch
-    if pref <= _workspace_limit or pref <= low or batch <= 1:
+    group = group or batch
+    if pref <= _workspace_limit or pref <= low or batch <= unit:
         return batch, pref
-    b = _copy_args(a)
-    c = max(2, -(-pref // max(_workspace_limit, 1)))
-    while c <= batch:
-        b.batch = -(-batch // c)
+    b = type(a)()
+    ctypes.memmove(ctypes.byref(b), ctypes.byref(a), ctypes.sizeof(a))
+    b.layout = None  # workspace sizes do not depend on the layout
+    per = max(1, group // unit)  # indices of the chunked dimension
+    last = None
+    for c in range(1, per + 1):
+        k = -(-per // c)
+        if k == last:
+            continue
+        last = k
+        b.batch = k * unit
+        if b.batch >= batch:
+            continue  # not a split
         p = N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(b))
         if p <= _workspace_limit:
-            if p > N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(b)):
-                return b.batch, p
-            break  # chunks this small no longer take the dS^T route
-        c += 1
+            return (b.batch, p) if p > N.lib.vmb_fea_bwd_min_workspace_bytes(ctypes.byref(b)) else (batch, low)
     return batch, low
 
 
-def _copy_args(a):
-    b = type(a)()
-    ctypes.memmove(ctypes.byref(b), ctypes.byref(a), ctypes.sizeof(a))
-    return b
-
-
-def _bwd_chunk(a: N.FeaBwdArgs, start: int, count: int) -> N.FeaBwdArgs:
-    """The arguments of sequences [start, start + count) of a backward call (same workspace)."""
-    b = _copy_args(a)
-    b.batch = count
-    g = 4 if a.grad_mode in (1, 2) else 2  # element size of the gradients
-
-    def off(name, stride_elems, elem):
-        base = getattr(a, name)
-        if base:
-            setattr(b, name, base + start * stride_elems * elem)
-
-    for name, bs in (("q", "q_bs"), ("k", "k_bs"), ("v", "v_bs"), ("v2", "v2_bs"), ("o", "o_bs"), ("dout", "do_bs")):
-        off(name, getattr(a, bs), 2)
-    for name in ("lse", "ent", "dent", "delta"):
-        off(name, a.n_q, 4)
-    for name in ("grad_q", "grad_k", "grad_v", "grad_v2"):
-        off(name, getattr(a, name + "_bs"), g)
-    for name in ("fin_q", "fin_k", "fin_v", "fin_v2"):
-        off(name, getattr(a, name + "_bs"), 4)
-    return b
-
-
-def _lstep_args(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, last: bool, skip_rows: int):
+# ----------------------------------------------------------------------------------------- L step
+def _lstep_args(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, last: bool, skip_rows: int,
+                tensors: dict):
+    """Arguments and layout of an L-step call. q, out and the tensors in `tensors` are (BH, N, C) or
+    (B, H, N, C) with N = m * b tokens; ent (and delta_out) are dense fp32 [bh][N]."""
+    bshape = q.shape[:-2]
+    nb = len(bshape)
+    if nb not in (1, 2):
+        raise AssertionError("L-step tensors are (BH, N, C) or (B, H, N, C)")
+    lay = N.LstepLayout()
+    lay.n1 = int(bshape[-1])
     a = N.LstepArgs()
-    a.q, a.out, a.ent = q.data_ptr(), out.data_ptr(), ent.data_ptr()
-    a.bh = q.numel() // (m * b * q.size(-1))
+    for name, t in dict(q=q, out=out, **tensors).items():
+        if t is None or name == "delta_out":
+            continue
+        if t.shape[:-2] != bshape or t.size(-2) != m * b:
+            raise AssertionError(f"{name} must be {tuple(bshape)} x {m * b} tokens")
+        setattr(a, name, t.data_ptr())
+        v = _view(t, nb)
+        setattr(lay, name, N.View(v.row, v.s1, 0, v.s2))  # L-step views: head hb at (hb % n1) s1 + (hb / n1) s3
+    bh = math.prod(bshape)
+    a.layout = ctypes.pointer(lay)
+    a.ent = _stats(ent, bh, m * b)
+    a.delta_out = _stats(tensors.get("delta_out"), bh, m * b)
+    a.bh = bh
     a.m, a.b = m, b
     a.d, a.dw = q.size(-1), out.size(-1)
     a.dtype = N.dtype_code(q.dtype)
     a.last = int(last)
     a.skip_rows = skip_rows
     a.scale, a.min_col_mass = float(scale), float(min_col_mass)
-    return a
+    return a, lay
 
 
 def lstep_fwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, *, u=None, z=None,
               skip_rows: int = 0) -> None:
     """Monarch L step forward: writes u (non-last) or z (last, tokens >= skip_rows)."""
-    a = _lstep_args(q, out, ent, m, b, scale, min_col_mass, z is not None, skip_rows)
-    a.u, a.z = N.ptr(u), N.ptr(z)
+    a, lay = _lstep_args(q, out, ent, m, b, scale, min_col_mass, z is not None, skip_rows, dict(u=u, z=z))
     _call("vmb_lstep_fwd", N.lib.vmb_lstep_fwd, a, q.device)
 
 
@@ -225,20 +298,23 @@ def lstep_bwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, dq
               skip_rows: int = 0, dq_store: bool = False, delta_out=None) -> None:
     """Monarch L step backward: adds into dq (fp32; overwrites it when dq_store), writes dout (gradient
     of the R-step output) and, when given, delta_out = sum out . dout per token (fp32)."""
-    a = _lstep_args(q, out, ent, m, b, scale, min_col_mass, dz is not None, skip_rows)
-    a.du, a.dz, a.dq, a.dout = N.ptr(du), N.ptr(dz), dq.data_ptr(), dout.data_ptr()
+    a, lay = _lstep_args(q, out, ent, m, b, scale, min_col_mass, dz is not None, skip_rows,
+                         dict(du=du, dz=dz, dq=dq, dout=dout, delta_out=delta_out))
     a.dq_store = int(dq_store)
-    a.delta_out = N.ptr(delta_out)
     _call("vmb_lstep_bwd", N.lib.vmb_lstep_bwd, a, q.device)
 
 
 def cast_f32(src: torch.Tensor, dst: torch.Tensor) -> None:
-    """dst = src (fp32 -> dst.dtype). Both [batch][rows][cols] views with contiguous rows and the same
-    shape (e.g. the same row range of two per-head tensors)."""
-    s3, d3 = _flat3(src), _flat3(dst)
-    assert s3.shape == d3.shape
-    n = s3.size(1) * s3.size(2)
-    if n == 0 or s3.size(0) == 0:
+    """dst = src (fp32 -> dst.dtype), both (*batch, rows, cols) with the same shape, any strides the
+    kernels can read in place (e.g. the same row range of an fp32 accumulator and of a token-major
+    gradient)."""
+    assert src.shape == dst.shape and src.dtype == torch.float32
+    bshape = src.shape[:-2]
+    nb = len(bshape)
+    if src.numel() == 0:
         return
-    N.check(N.lib.vmb_cast_f32(s3.data_ptr(), _bs(s3), d3.data_ptr(), _bs(d3), s3.size(0), n, N.dtype_code(dst.dtype),
-                               N.stream_ptr(src.device)), "vmb_cast_f32")
+    n1, n2 = _split(bshape)
+    sv, dv = _view(src, nb), _view(dst, nb)
+    N.check(N.lib.vmb_cast_f32_view(src.data_ptr(), ctypes.byref(sv), dst.data_ptr(), ctypes.byref(dv), n1, n2,
+                                    math.prod(bshape), src.size(-2), src.size(-1), N.dtype_code(dst.dtype),
+                                    N.stream_ptr(src.device)), "vmb_cast_f32_view")

@@ -7,6 +7,11 @@ approximated by a Monarch matrix: R = m dense (b x b) blocks mixing tokens insid
 L = b dense (m x m) blocks mixing tokens inside a grid column, fitted by `num_iters` steps of
 alternating minimisation (reference vmonarch.py:1-11).
 
+Layouts: q, k, v may be dense (B, H, N, D) or token-major, i.e. (B, N, H, D) buffers seen through
+transpose(1, 2) as the Video-DiT caller holds them (reference README.md:74-76); the kernels read and
+write them in place through strided layouts, and z and the gradients come back in the same layout
+family (no transposes on either side).
+
 Execution per iteration (all on the C ABI, no torch math on the hot path):
   R step: FlashEntropyAttention over the B*H*m grid rows (vmb_fea_fwd, entropy on). The first
           iteration folds the reference's u = q * scale (vmonarch.py:47) into sm_scale, and the last
@@ -27,82 +32,101 @@ from . import ops
 from .kernel import _check_inputs
 
 
+def _token_major(t: torch.Tensor) -> bool:
+    """(B, H, N, D) tensor whose tokens are further apart than its heads: a (B, N, H, D) buffer
+    seen through transpose(1, 2), the Video-DiT layout (reference README.md:74-76)."""
+    return t.size(1) > 1 and t.size(2) > 1 and t.stride(1) < t.stride(2)
+
+
+def _alloc_like_layout(ref: torch.Tensor, cols: int, dtype) -> torch.Tensor:
+    """(B, H, N, cols) output in `ref`'s layout family: token-major when `ref` is, else dense."""
+    B, H, N, _ = ref.shape
+    if _token_major(ref):
+        return torch.empty((B, N, H, cols), device=ref.device, dtype=dtype).transpose(1, 2)
+    return torch.empty((B, H, N, cols), device=ref.device, dtype=dtype)
+
+
+def _in_place(t: torch.Tensor, strided: bool) -> torch.Tensor:
+    """`t` itself when the kernels can read it through its strides (dense or token-major; the D = 128
+    kernels with m <= 32 take any such layout), else a dense copy."""
+    return t if strided and ops.viewable(t) else t.contiguous()
+
+
 class _VMonarchAttention(torch.autograd.Function):
+    """Tensors keep the caller's layout: q, k, v, z and the gradients are (B, H, N, .) views, dense
+    or token-major, read and written in place through strided layouts; the R-step outputs, the next
+    queries u and the fp32 gradient accumulators are dense internal buffers."""
 
     @staticmethod
     def forward(ctx, q, k, v, num_blocks, block_size, num_iters, recompute_tokens, min_col_mass):
         B, H, N, D = q.shape
         Dv = v.shape[-1]
         m, b = num_blocks, block_size
-        BH = B * H
         scale = D ** -0.5
-        qf = q.contiguous().view(BH, N, D)
-        kf = k.contiguous().view(BH, N, D)
-        vf = v.contiguous().view(BH, N, Dv)
+        strided = D == 128 and Dv == 128 and m <= 32
+        qs, ks, vs = (_in_place(t, strided) for t in (q, k, v))
         dev, dt = q.device, q.dtype
         rr = min(max(int(recompute_tokens), 0), N)
-        grid = lambda t: t.view(BH * m, b, t.size(-1))  # noqa: E731  (grid rows as FEA batches)
+        grid = lambda t: t.unflatten(2, (m, b))  # noqa: E731  (B, H, m, b, .): grid rows as FEA batches
 
         steps = []
-        u = qf
+        u = qs
         z = None
         for it in range(num_iters):
             last = it == num_iters - 1
             Dw = D + Dv if last else D
-            out = torch.empty((BH, N, Dw), device=dev, dtype=dt)
-            lse = torch.empty((BH, N), device=dev, dtype=torch.float32)
-            ent = torch.empty((BH, N), device=dev, dtype=torch.float32)
+            out = torch.empty((B, H, N, Dw), device=dev, dtype=dt)
+            lse = torch.empty((B, H, N), device=dev, dtype=torch.float32)
+            ent = torch.empty((B, H, N), device=dev, dtype=torch.float32)
             sm = scale if it == 0 else 1.0
-            ops.fea_fwd(grid(u), grid(kf), grid(kf), grid(out), lse.view(BH * m, b), ent.view(BH * m, b), sm,
-                        v2=grid(vf) if last else None)
+            ops.fea_fwd(grid(u), grid(ks), grid(ks), grid(out), lse, ent, sm, v2=grid(vs) if last else None)
             if last:
-                z = torch.empty((BH, N, Dv), device=dev, dtype=dt)
+                z = _alloc_like_layout(qs, Dv, dt)
                 # every token of z is produced here (the tensor-core L step writes whole stacked
                 # columns); the exact recompute below then overwrites tokens [0, rr)
-                ops.lstep_fwd(qf, out, ent, m, b, scale, min_col_mass, z=z, skip_rows=0)
+                ops.lstep_fwd(qs, out, ent, m, b, scale, min_col_mass, z=z, skip_rows=0)
                 nxt = None
             else:
-                nxt = torch.empty((BH, N, D), device=dev, dtype=dt)
-                ops.lstep_fwd(qf, out, ent, m, b, scale, min_col_mass, u=nxt)
+                nxt = torch.empty((B, H, N, D), device=dev, dtype=dt)
+                ops.lstep_fwd(qs, out, ent, m, b, scale, min_col_mass, u=nxt)
             steps.append((u, out, lse, ent, sm))
             u = nxt
 
         lse_r = None
         if rr > 0:
-            lse_r = torch.empty((BH, rr), device=dev, dtype=torch.float32)
-            ops.fea_fwd(qf[:, :rr], kf, vf, z[:, :rr], lse_r, None, scale)
+            lse_r = torch.empty((B, H, rr), device=dev, dtype=torch.float32)
+            ops.fea_fwd(qs[:, :, :rr], ks, vs, z[:, :, :rr], lse_r, None, scale)
 
-        ctx.meta = (B, H, N, D, Dv, m, b, rr, scale, min_col_mass)
+        ctx.meta = (B, H, N, D, Dv, m, b, rr, scale, min_col_mass, strided)
         if any(ctx.needs_input_grad[:3]):
-            flat = [qf, kf, vf, z] + ([lse_r] if lse_r is not None else [])
-            for s in steps:
-                flat.extend(s[:4])
+            flat = [qs, ks, vs, z] + ([lse_r] if lse_r is not None else [])
+            for st in steps:
+                flat.extend(st[:4])
             ctx.save_for_backward(*flat)
-            ctx.sms = [s[4] for s in steps]
-        return z.view(B, H, N, Dv)
+            ctx.sms = [st[4] for st in steps]
+        return z
 
     @staticmethod
     def backward(ctx, dz):
-        B, H, N, D, Dv, m, b, rr, scale, min_col_mass = ctx.meta
-        BH = B * H
+        B, H, N, D, Dv, m, b, rr, scale, min_col_mass, strided = ctx.meta
         saved = ctx.saved_tensors
-        qf, kf, vf, z = saved[:4]
+        qs, ks, vs, z = saved[:4]
         pos = 4
         lse_r = None
         if rr > 0:
             lse_r = saved[4]
             pos = 5
         steps = [saved[pos + 4 * i: pos + 4 * i + 4] for i in range(len(ctx.sms))]
-        dev, dt = qf.device, qf.dtype
-        dz = dz.to(dt).contiguous().view(BH, N, Dv)
-        grid = lambda t: t.view(BH * m, b, t.size(-1))  # noqa: E731
+        dev, dt = qs.device, qs.dtype
+        dz = _in_place(dz.to(dt), strided)
+        grid = lambda t: t.unflatten(2, (m, b))  # noqa: E731
 
         # fp32 accumulators. Each is first written by a call that covers all of its rows and
         # OVERWRITES it (no zero-fill): dq by the last L step, dk / dv (and every R step's own dq,
         # gq) by the last R step; later calls add. The recompute's contribution comes last.
-        dq_acc = torch.empty((BH, N, D), device=dev, dtype=torch.float32)
-        dk_acc = torch.empty((BH, N, D), device=dev, dtype=torch.float32)
-        dv_acc = torch.empty((BH, N, Dv), device=dev, dtype=torch.float32)
+        dq_acc = torch.empty((B, H, N, D), device=dev, dtype=torch.float32)
+        dk_acc = torch.empty((B, H, N, D), device=dev, dtype=torch.float32)
+        dv_acc = torch.empty((B, H, N, Dv), device=dev, dtype=torch.float32)
         kv_fresh = True   # dk_acc / dv_acc not yet written
 
         du = None
@@ -114,14 +138,13 @@ class _VMonarchAttention(torch.autograd.Function):
             dout = torch.empty_like(out)
             # the L step also produces the R-step backward's delta = sum out . dout per token, so
             # the attention backward skips its own pass over out and dout
-            delta = (torch.empty((BH, N), device=dev, dtype=torch.float32)
-                     if out.size(-1) in (64, 128, 256) else None)
+            delta = torch.empty((B, H, N), device=dev, dtype=torch.float32)
             if last:
-                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, dz=dz, skip_rows=rr,
+                ops.lstep_bwd(qs, out, ent, m, b, scale, min_col_mass, dq_acc, dout, dz=dz, skip_rows=rr,
                               dq_store=True, delta_out=delta)
             else:
-                ops.lstep_bwd(qf, out, ent, m, b, scale, min_col_mass, dq_acc, dout, du=du, delta_out=delta)
-            gq = dq_acc if it == 0 else torch.empty((BH, N, D), device=dev, dtype=torch.float32)
+                ops.lstep_bwd(qs, out, ent, m, b, scale, min_col_mass, dq_acc, dout, du=du, delta_out=delta)
+            gq = dq_acc if it == 0 else torch.empty((B, H, N, D), device=dev, dtype=torch.float32)
             gq_fresh = it != 0
             # one grad mode per call: overwrite only when every target is fresh, otherwise clear
             # the fresh ones and add (only with num_iters != 2)
@@ -134,27 +157,26 @@ class _VMonarchAttention(torch.autograd.Function):
                     dk_acc.zero_()
                     dv_acc.zero_()
                 mode = 1
-            ops.fea_bwd(grid(u), grid(kf), grid(kf), grid(out), grid(dout), lse.view(BH * m, b), grid(gq),
-                        grid(dk_acc), None, sm, v2=grid(vf) if last else None,
-                        grad_v2=grid(dv_acc) if last else None, grad_mode=mode, v_is_k=True,
-                        delta=delta.view(BH * m, b) if delta is not None else None)
+            ops.fea_bwd(grid(u), grid(ks), grid(ks), grid(out), grid(dout), lse, grid(gq), grid(dk_acc), None, sm,
+                        v2=grid(vs) if last else None, grad_v2=grid(dv_acc) if last else None, grad_mode=mode,
+                        v_is_k=True, delta=delta)
             kv_fresh = False
             du = gq
 
-        dq = torch.empty((BH, N, D), device=dev, dtype=dt)
-        dk = torch.empty((BH, N, D), device=dev, dtype=dt)
-        dv = torch.empty((BH, N, Dv), device=dev, dtype=dt)
+        dq = _alloc_like_layout(qs, D, dt)
+        dk = _alloc_like_layout(ks, D, dt)
+        dv = _alloc_like_layout(vs, Dv, dt)
         if rr > 0:
             # the recompute is the last contribution to dk, dv (every key) and dq[:rr]: it writes them
             # in the element dtype as accumulator + its own gradient (grad_mode 3)
-            ops.fea_bwd(qf[:, :rr], kf, vf, z[:, :rr], dz[:, :rr], lse_r, dq[:, :rr], dk, dv, scale, grad_mode=3,
-                        fin_q=dq_acc[:, :rr], fin_k=dk_acc, fin_v=dv_acc)
-            ops.cast_f32(dq_acc[:, rr:], dq[:, rr:])
+            ops.fea_bwd(qs[:, :, :rr], ks, vs, z[:, :, :rr], dz[:, :, :rr], lse_r, dq[:, :, :rr], dk, dv, scale,
+                        grad_mode=3, fin_q=dq_acc[:, :, :rr], fin_k=dk_acc, fin_v=dv_acc)
+            ops.cast_f32(dq_acc[:, :, rr:], dq[:, :, rr:])
         else:
             ops.cast_f32(dq_acc, dq)
             ops.cast_f32(dk_acc, dk)
             ops.cast_f32(dv_acc, dv)
-        return dq.view(B, H, N, D), dk.view(B, H, N, D), dv.view(B, H, N, Dv), None, None, None, None, None
+        return dq, dk, dv, None, None, None, None, None
 
 
 def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_tokens=0, min_col_mass=0.01):
