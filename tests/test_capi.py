@@ -93,12 +93,16 @@ def test_fea_fwd_empty_batch_is_a_no_op():
 
 def test_fea_bwd_workspace_and_validation():
     a = N.FeaBwdArgs()
-    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 3, 100, 100, 64, 64, 64
+    # D = 32 runs on the warp-level MMA kernels: c and g per row, and an fp32 dQ in grad_mode 0
+    a.batch, a.n_q, a.n_kv, a.d, a.dv, a.dv1 = 3, 100, 100, 32, 32, 32
     a.grad_mode = 0
     rows = 300
-    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280 + ((rows * 64 * 4 + 255) // 256) * 256
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280 + ((rows * 32 * 4 + 255) // 256) * 256
     a.grad_mode = 1
     assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280
+    # D = Dv = 64 runs the tcgen05 kernels over 64-column maps: the folded statistics planes only
+    a.d, a.dv, a.dv1, a.grad_mode = 64, 64, 64, 0
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 3 * ((3 * 128 * 4 + 255) // 256) * 256
     # D = 128 runs on the tcgen05 kernels: three folded statistics planes of 3 x round_up(100, 128)
     # rows. Three query tiles cannot fill the GPU, so the dS^T route is not taken: no dS^T buffer.
     a.d, a.dv, a.dv1 = 128, 128, 128

@@ -300,10 +300,11 @@ def test_split_key_range_backward_matches_and_is_deterministic(monkeypatch):
         assert torch.equal(g0, g1)
 
 
-@pytest.mark.parametrize("D", [128, 64])
+@pytest.mark.parametrize("D", [128, 64, 32])
 def test_grad_mode_overwrite_equals_add_into_zeros(D):
     # grad_mode 2 overwrites fp32 gradient buffers (here pre-filled with NaN); it must give exactly
-    # what grad_mode 1 adds into zero-filled ones. D = 128 runs the tcgen05 kernels, D = 64 mma.sync.
+    # what grad_mode 1 adds into zero-filled ones. D = 128 and 64 run the tcgen05 kernels (64: over
+    # 64-column tensor maps), D = 32 mma.sync.
     from vmonarch_b200 import ops
     gen = torch.Generator().manual_seed(5)
     B, n = 3, 300
@@ -319,7 +320,7 @@ def test_grad_mode_overwrite_equals_add_into_zeros(D):
     torch.cuda.synchronize()
     for a, p in zip(add, put):
         assert torch.isfinite(p).all()
-        if D == 128:
+        if D in (64, 128):
             assert torch.equal(a, p)
         else:  # the mma.sync kernels add dQ with atomics: the summation order varies run to run
             torch.testing.assert_close(p, a, rtol=1e-5, atol=1e-5)
@@ -395,14 +396,14 @@ def test_backward_keys_as_values_with_v2(n, mode):
         assert (g - r).abs().max() <= max(5e-2, 8e-3 * r.abs().max().item())
 
 
-@pytest.mark.parametrize("case", ["plain", "split", "v2", "d64"])
+@pytest.mark.parametrize("case", ["plain", "split", "v2", "d64", "split64", "d32"])
 def test_grad_mode_finalize_equals_add_then_cast(case):
     # grad_mode 3 writes 16-bit gradients as fp32 accumulator + this call's gradient; it must equal
     # adding into the accumulators (grad_mode 1) and converting afterwards, bit for bit.
     from vmonarch_b200 import ops
     gen = torch.Generator().manual_seed(hash(case) % 1000)
     B, nq, nk, D = {"plain": (3, 300, 300, 128), "split": (2, 128, 4096, 128), "v2": (2, 300, 300, 128),
-                    "d64": (2, 200, 200, 64)}[case]
+                    "d64": (2, 200, 200, 64), "split64": (2, 128, 4096, 64), "d32": (2, 200, 200, 32)}[case]
     q = torch.randn(B, nq, D, generator=gen).bfloat16().cuda()
     k, v = (torch.randn(B, nk, D, generator=gen).bfloat16().cuda() for _ in range(2))
     v_is_k, v2 = case == "v2", None
@@ -428,7 +429,7 @@ def test_grad_mode_finalize_equals_add_then_cast(case):
                 fin_k=fin[1], fin_v=None if v_is_k else fin[2], fin_v2=fin[2] if v_is_k else None)
     torch.cuda.synchronize()
     for name, g, r in zip(("dq", "dk", "dv"), out, ref):
-        if D == 128:
+        if D in (64, 128):
             assert torch.equal(g, r), name
         else:  # the mma.sync kernels add with atomics: the summation order varies run to run
             torch.testing.assert_close(g.float(), r.float(), rtol=1e-2, atol=1e-2)

@@ -27,7 +27,9 @@ def _worker(rank, world, port, q, k, v, out_q):
     full = shard.gather_units(o, q.shape[0], info.world)
     t = shard.max_over_ranks(float(rank + 1), torch.device("cpu"))
     if rank == 0:
-        out_q.put((full, t))
+        # numpy, pickled by value: a tensor would be shared through a file descriptor that dies with
+        # this process, which may exit before the parent reads the queue
+        out_q.put((full.numpy(), t))
     shard.barrier()
     dist.destroy_process_group()
 
@@ -49,6 +51,7 @@ def test_two_rank_gloo_shard_and_gather():
     for p in procs:
         p.start()
     full, t = out_q.get(timeout=120)
+    full = torch.from_numpy(full)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

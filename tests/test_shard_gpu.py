@@ -46,9 +46,9 @@ def _worker(rank, world, port, q, k, v, do, out_q):
     sl = slice(units.start, units.stop)
     outs = _run(q[sl], k[sl], v[sl], do[sl], device)
     torch.cuda.synchronize(device)
-    full = [shard.gather_units(t, q.shape[0], info.world).cpu() for t in outs]
+    full = [shard.gather_units(t, q.shape[0], info.world).float().cpu() for t in outs]
     if rank == 0:
-        out_q.put(full)
+        out_q.put([t.numpy() for t in full])  # by value: this process may exit before the parent reads
     shard.barrier()
     dist.destroy_process_group()
 
@@ -62,7 +62,7 @@ def test_two_rank_nccl_head_shard_matches_one_gpu():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q, k, v, do, out_q)) for r in range(2)]
     for p in procs:
         p.start()
-    full = out_q.get(timeout=300)
+    full = [torch.from_numpy(t) for t in out_q.get(timeout=300)]
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0

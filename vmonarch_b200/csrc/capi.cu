@@ -179,8 +179,9 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   p.work_bytes = a->workspace ? a->workspace_bytes : 0;
   const cudaStream_t st = static_cast<cudaStream_t>(stream);
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
-  // V aliasing K (the VMonarch R step): the key tile in shared memory doubles as the value tile
-  const bool vk = fwd_v_is_k(a);
+  // V aliasing K (the VMonarch R step): the key tile in shared memory doubles as the value tile.
+  // At d = 64 the separate-values kernel reads the same tensor twice instead (its only tcgen05 route).
+  const bool vk = fwd_v_is_k(a) && a->d != 64;
   if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk)) {
     // a split key range adds the merge kernel
     count(vmb::fea_fwd_sm100_split(a->batch, p.n_q, p.n_kv, a->dv, p.work, p.work_bytes) > 1 ? 2 : 1);
@@ -355,6 +356,7 @@ int vmb_fea_bwd(const vmb_fea_bwd_args* a, void* stream) {
   count(sm100 ? (bwd_fuses_dq(a) ? 2 : (bwd_dq_split(a, use_ds) > 1 ? 4 : 3)) : (dq_acc ? 3 : 2));
   vmb::BwdParams p{};
   p.n1 = w.n1; p.n2 = w.n2;
+  p.d = a->d;
   p.qv = w.q; p.kv = w.k; p.vv = w.v; p.v2v = w.v2; p.dov = w.dout;
   p.dqv = w.gq; p.dkv = w.gk; p.dvv = w.gv; p.dv2v = w.gv2;
   p.finqv = w.fq; p.finkv = w.fk; p.finvv = w.fv; p.finv2v = w.fv2;

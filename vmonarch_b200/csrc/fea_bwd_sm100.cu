@@ -960,11 +960,12 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
 // dq[bi][q] (+)= sum over chunks c (in order) of part[c][bi][q]: the split key ranges' partial tiles
 // (added into dq, or written over it in the store mode)
 __global__ void dq_split_reduce_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q, float* dq,
-                                       View dqv, int n1, int n2, int store) {
+                                       View dqv, int n1, int n2, int store, int c4n) {
   const int64_t total = batch * n_q * 32;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
     const int64_t q = rem / 32, c4 = rem % 32;
+    if (c4 >= c4n) continue;  // columns past d (d = 64)
     float4* dst = reinterpret_cast<float4*>(dq + view_offset(dqv, n1, n2, bi, q)) + c4;
     float4 acc = store ? make_float4(0.f, 0.f, 0.f, 0.f) : *dst;
     for (int c = 0; c < split; ++c) {
@@ -981,11 +982,12 @@ __global__ void dq_split_reduce_kernel(const float* part, int split, int64_t bat
 // out16[bi][q] = 16-bit(fin[bi][q] + sum over chunks c (in order) of part[c][bi][q]) (acc 3)
 template <typename T>
 __global__ void dq_split_finalize_kernel(const float* part, int split, int64_t batch, int64_t n_pad, int n_q,
-                                         const float* fin, View finv, T* out, View outv, int n1, int n2) {
+                                         const float* fin, View finv, T* out, View outv, int n1, int n2, int c4n) {
   const int64_t total = batch * n_q * 32;
   for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total; idx += (int64_t)gridDim.x * blockDim.x) {
     const int64_t bi = idx / ((int64_t)n_q * 32), rem = idx % ((int64_t)n_q * 32);
     const int64_t q = rem / 32, c4 = rem % 32;
+    if (c4 >= c4n) continue;  // columns past d (d = 64)
     float4 acc = reinterpret_cast<const float4*>(fin + view_offset(finv, n1, n2, bi, q))[c4];
     for (int c = 0; c < split; ++c) {
       const float4 v = reinterpret_cast<const float4*>(part + (((int64_t)c * batch + bi) * n_pad + q) * 128)[c4];
@@ -1153,31 +1155,35 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   Sm100BwdParams pa{};
   pa.n1 = n1;
   pa.n2 = n2;
-  if (!tma::make_map_view(&pa.tm_a, b.k, bf16, 128, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
+  // d = 64 (keys, queries and dQ / dK 64 wide): the maps are 64 columns wide, so the kernels' second
+  // 64-column atom loads as zeros and stores nothing (the contraction over 128 columns is exact)
+  const int d = b.d;
+  if (!tma::make_map_view(&pa.tm_a, b.k, bf16, d, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
     if (!tma::make_map_view(&pa.tm_b, xsrc, bf16, 64 * xa, b.n_kv, batch, xv, n1, n2, 128)) return cudaErrorInvalidValue;
   } else {
     pa.tm_b = pa.tm_a;
   }
-  if (!tma::make_map_view(&pa.tm_c, b.q, bf16, 128, b.n_q, batch, b.qv, n1, n2, qrows)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pa.tm_c, b.q, bf16, d, b.n_q, batch, b.qv, n1, n2, qrows)) return cudaErrorInvalidValue;
   if (!tma::make_map_view(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.dov, n1, n2, qrows)) return cudaErrorInvalidValue;
   pa.nl = b.fold;
   pa.nc = b.fold + batch * b.n_pad;
   pa.ng = b.fold + 2 * batch * b.n_pad;
   pa.n_pad = b.n_pad;
   // gradient maps: dK, and dV (or dV2 when V aliases K) when the kernel has a value accumulator
-  auto grad_map = [&](CUtensorMap* m, void* base, int64_t rows, const View& v, bool f32) {
-    return f32 ? tma::make_map_view_f32(m, base, 128, rows, batch, v, n1, n2, 128)
-               : tma::make_map_view(m, base, bf16, 128, rows, batch, v, n1, n2, 128);
+  auto grad_map = [&](CUtensorMap* m, void* base, int64_t cols, int64_t rows, const View& v, bool f32) {
+    return f32 ? tma::make_map_view_f32(m, base, cols, rows, batch, v, n1, n2, 128)
+               : tma::make_map_view(m, base, bf16, cols, rows, batch, v, n1, n2, 128);
   };
+  const int xcols = vk ? dv - 128 : dv;  // columns of the value gradient the kernel writes
   const bool f32_kv = b.acc_kv == 1 || b.acc_kv == 2;  // acc 3 writes 16-bit values
-  if (!grad_map(&pa.tm_g0, b.dk, b.n_kv, b.dkv, f32_kv)) return cudaErrorInvalidValue;
-  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, b.n_kv, vk ? b.dv2v : b.dvv, f32_kv))
+  if (!grad_map(&pa.tm_g0, b.dk, d, b.n_kv, b.dkv, f32_kv)) return cudaErrorInvalidValue;
+  if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, xcols, b.n_kv, vk ? b.dv2v : b.dvv, f32_kv))
     return cudaErrorInvalidValue;
   if (b.acc_kv == 3) {
-    if (!tma::make_map_view_f32(&pa.tm_f0, b.fin_k, 128, b.n_kv, batch, b.finkv, n1, n2, 128))
+    if (!tma::make_map_view_f32(&pa.tm_f0, b.fin_k, d, b.n_kv, batch, b.finkv, n1, n2, 128))
       return cudaErrorInvalidValue;
-    if (xa > 0 && !tma::make_map_view_f32(&pa.tm_f1, vk ? b.fin_v2 : b.fin_v, 128, b.n_kv, batch,
+    if (xa > 0 && !tma::make_map_view_f32(&pa.tm_f1, vk ? b.fin_v2 : b.fin_v, xcols, b.n_kv, batch,
                                           vk ? b.finv2v : b.finvv, n1, n2, 128))
       return cudaErrorInvalidValue;
   }
@@ -1220,9 +1226,9 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     if (!tma::make_map(&pg.tm_a, b.ds, bf16, pa.ds_ld, pa.ds_bs / pa.ds_ld, batch, pa.ds_bs, 64)) return cudaErrorInvalidValue;
     pg.n1 = n1;
     pg.n2 = n2;
-    if (!tma::make_map_view(&pg.tm_c, b.k, bf16, 128, b.n_kv, batch, b.kv, n1, n2, 64)) return cudaErrorInvalidValue;
-    if (!grad_map(&pg.tm_g0, b.dq, b.n_q, b.dqv, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
-    if (b.acc_q == 3 && !tma::make_map_view_f32(&pg.tm_f0, b.fin_q, 128, b.n_q, batch, b.finqv, n1, n2, 128))
+    if (!tma::make_map_view(&pg.tm_c, b.k, bf16, d, b.n_kv, batch, b.kv, n1, n2, 64)) return cudaErrorInvalidValue;
+    if (!grad_map(&pg.tm_g0, b.dq, d, b.n_q, b.dqv, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
+    if (b.acc_q == 3 && !tma::make_map_view_f32(&pg.tm_f0, b.fin_q, d, b.n_q, batch, b.finqv, n1, n2, 128))
       return cudaErrorInvalidValue;
     pg.n_q = b.n_q;
     pg.n_kv = b.n_kv;
@@ -1235,9 +1241,9 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   Sm100BwdParams pb{};
   pb.n1 = n1;
   pb.n2 = n2;
-  if (!tma::make_map_view(&pb.tm_a, b.q, bf16, 128, b.n_q, batch, b.qv, n1, n2, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pb.tm_a, b.q, bf16, d, b.n_q, batch, b.qv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (!tma::make_map_view(&pb.tm_b, b.dout, bf16, dv, b.n_q, batch, b.dov, n1, n2, 128)) return cudaErrorInvalidValue;
-  if (!tma::make_map_view(&pb.tm_c, b.k, bf16, 128, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
+  if (!tma::make_map_view(&pb.tm_c, b.k, bf16, d, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
     if (!tma::make_map_view(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xv, n1, n2, 128)) return cudaErrorInvalidValue;
   } else {
@@ -1262,8 +1268,8 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
                                          b.n_pad * 128, 128))
       return cudaErrorInvalidValue;
   } else {
-    if (!grad_map(&pb.tm_g0, b.dq, b.n_q, b.dqv, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
-    if (b.acc_q == 3 && !tma::make_map_view_f32(&pb.tm_f0, b.fin_q, 128, b.n_q, batch, b.finqv, n1, n2, 128))
+    if (!grad_map(&pb.tm_g0, b.dq, d, b.n_q, b.dqv, b.acc_q == 1 || b.acc_q == 2)) return cudaErrorInvalidValue;
+    if (b.acc_q == 3 && !tma::make_map_view_f32(&pb.tm_f0, b.fin_q, d, b.n_q, batch, b.finqv, n1, n2, 128))
       return cudaErrorInvalidValue;
   }
   pb.n_q = b.n_q;
@@ -1283,14 +1289,15 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
     e = run(fea_bwd_dq128_kernel<T, 2, false, false, 3, 2, kDqWarpgroups>, DqCfg2<2, false, false, 3, 2>::SMEM, blocks_b,
             kDqThreads, pb, st);
   if (e != cudaSuccess || pb.k_split == 1) return e;
-  const int64_t total = batch * b.n_q * 32;  // float4s of the valid dQ rows
+  const int64_t total = batch * b.n_q * 32;  // threads: 32 per dQ row (lanes past d / 4 idle)
   const int64_t blocks = std::min<int64_t>((total + 255) / 256, 148 * 16);
   if (b.acc_q == 3)
     dq_split_finalize_kernel<T><<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.fin_q,
-                                                                  b.finqv, reinterpret_cast<T*>(b.dq), b.dqv, n1, n2);
+                                                                  b.finqv, reinterpret_cast<T*>(b.dq), b.dqv, n1, n2,
+                                                                  d / 4);
   else
     dq_split_reduce_kernel<<<(unsigned)blocks, 256, 0, st>>>(b.dq_part, pb.k_split, batch, b.n_pad, b.n_q, b.dq,
-                                                             b.dqv, n1, n2, b.acc_q == 2);
+                                                             b.dqv, n1, n2, b.acc_q == 2, d / 4);
   return cudaGetLastError();
 }
 
@@ -1350,6 +1357,8 @@ int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv) {
 }
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {
+  // d = dv = 64 with separate values: the 128-column kernels over 64-column maps (zero second atom)
+  if (d == 64) return !vk && dv == 64 && dv1 == 64;
   if (d != 128) return false;
   if (vk) return dv1 == 128 && (dv == 128 || dv == 256);
   return dv == 128 && dv1 == 128;

@@ -1050,7 +1050,9 @@ cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bo
     if (dv == 128) return launch2<T, true, ENT>(p, batch, st);
     if (dv == 256 && dv1 == 128) return launch<T, 2, true, 3, ENT>(p, batch, st);
   } else {
-    if (dv == 128) return launch2<T, false, ENT>(p, batch, st);
+    // dv = 64 (d = 64): the 128-column kernel over 64-column maps; the second atoms load as zeros
+    // and the second half of O is clipped on store
+    if (dv == 128 || dv == 64) return launch2<T, false, ENT>(p, batch, st);
     if (dv == 256) return launch<T, 4, false, 2, ENT>(p, batch, st);
   }
   return cudaErrorNotSupported;
@@ -1059,13 +1061,14 @@ cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bo
 }  // namespace
 
 bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk) {
+  if (d == 64) return !vk && dv == 64 && dv1 == 64;  // no key-range split (its merge is 128 wide)
   if (d != 128) return false;
   if (vk) return dv == 128 || (dv == 256 && dv1 == 128);
   return (dv == 128 || dv == 256) && dv1 == dv;
 }
 
 int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk) {
-  if (!fea_fwd_sm100_supported(d, dv, dv1, vk) || dv != 128) return 0;  // only the two-stream kernel splits
+  if (!fea_fwd_sm100_supported(d, dv, dv1, vk) || dv != 128) return 0;  // only the two-stream kernel splits (d = 128)
   return split_bytes(fwd2_split(batch, n_q, n_kv), batch, n_q);
 }
 

@@ -68,6 +68,7 @@ struct BwdParams {
   View qv, kv, vv, v2v, dov, dqv, dkv, dvv, dv2v;  // strided views (tcgen05 kernels)
   View finqv, finkv, finvv, finv2v;
   int n1, n2;                                      // batch split of the views
+  int d;                                           // head dim of q / k (64 or 128 on the tcgen05 path)
   int n_q, n_kv, dv1, n_ktiles;
   int acc_kv;         // 1: dk/dv/dv2 are fp32 buffers that are added into
   int acc_q;          // 1: dq is an fp32 buffer that is added into (else element dtype)

@@ -39,8 +39,8 @@ class _FlashEntropyAttention(torch.autograd.Function):
         B, H, N, D = q.shape
         Dv = v.shape[-1]
         # dense or token-major ((B, N, H, D) seen through transpose(1, 2)) inputs are read in place
-        # by the D = Dv = 128 kernels; other head dims take dense copies
-        strided = D == 128 and Dv == 128
+        # by the tcgen05 kernels (D = Dv = 128 or 64); other head dims take dense copies
+        strided = (D, Dv) in ((128, 128), (64, 64))
         q, k, v = (t if strided and ops.viewable(t) else t.contiguous() for t in (q, k, v))
         if q.size(1) > 1 and N > 1 and q.stride(1) < q.stride(2):   # token-major: o in the same layout
             o = torch.empty((B, N, H, Dv), device=q.device, dtype=q.dtype).transpose(1, 2)
@@ -60,7 +60,7 @@ class _FlashEntropyAttention(torch.autograd.Function):
         if do is None:
             do = torch.zeros_like(o)
         do = do.to(q.dtype)
-        do = do if q.size(-1) == 128 and do.size(-1) == 128 and ops.viewable(do) else do.contiguous()
+        do = do if (q.size(-1), do.size(-1)) in ((128, 128), (64, 64)) and ops.viewable(do) else do.contiguous()
         if de is not None:
             de = de.float().contiguous()
         # empty_like keeps a dense or token-major input's strides for its gradient
