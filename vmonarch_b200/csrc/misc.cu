@@ -147,36 +147,49 @@ cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs
 
 // dst(s, r, c) = (T) src(s, r, c) over [batch][rows][cols] views (cols % 4 == 0, 16-byte aligned
 // rows): the fp32 accumulator of a strided (e.g. token-major) gradient converted in place of
-// cast_f32's flat rows. One thread per 4 columns of a row.
+// cast_f32's flat rows. Grid row y = batch entries y, y + gridDim.y, ...; one warp per tensor row,
+// lane = 4 columns, so the view offsets are computed once per batch entry and there is no division
+// per element.
 template <typename T>
-__global__ void cast_f32_view_kernel(const float* src, View sv, T* dst, View dvw, int n1, int n2, int64_t rows,
-                                     int64_t c4, int64_t total4) {
-  for (int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; idx < total4; idx += (int64_t)gridDim.x * blockDim.x) {
-    const int64_t row = idx / c4, c = (idx % c4) * 4;
-    const int64_t bi = row / rows, r = row % rows;
-    const float4 v = *reinterpret_cast<const float4*>(src + view_offset(sv, n1, n2, bi, r) + c);
-    uint2 w;
-    w.x = Elem<T>::pack(v.x, v.y);
-    w.y = Elem<T>::pack(v.z, v.w);
-    *reinterpret_cast<uint2*>(dst + view_offset(dvw, n1, n2, bi, r) + c) = w;
+__global__ void __launch_bounds__(256) cast_f32_view_kernel(const float* src, View sv, T* dst, View dvw, int n1, int n2,
+                                                            int64_t batch, int64_t rows, int c4n) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t bi = blockIdx.y; bi < batch; bi += gridDim.y) {
+    const float* s0 = src + view_offset(sv, n1, n2, bi, 0);
+    T* d0 = dst + view_offset(dvw, n1, n2, bi, 0);
+    for (int64_t r = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (int64_t)gridDim.x * warps) {
+      const float* sr = s0 + r * sv.rs;
+      T* dr = d0 + r * dvw.rs;
+      for (int c = lane; c < c4n; c += 32) {
+        const float4 v = *reinterpret_cast<const float4*>(sr + 4 * c);
+        uint2 w;
+        w.x = Elem<T>::pack(v.x, v.y);
+        w.y = Elem<T>::pack(v.z, v.w);
+        *reinterpret_cast<uint2*>(dr + 4 * c) = w;
+      }
+    }
   }
 }
 
 cudaError_t cast_f32_view(const float* src, const View& sv, void* dst, const View& dvw, int n1, int n2, int64_t batch,
                           int64_t rows, int64_t cols, bool bf16, cudaStream_t st) {
-  const int64_t c4 = cols / 4, total4 = batch * rows * c4;
-  if (total4 == 0) return cudaSuccess;
+  if (batch == 0 || rows == 0 || cols == 0) return cudaSuccess;
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  const int64_t want = (total4 + 255) / 256;
-  const unsigned blocks = (unsigned)(want < (int64_t)sms * 8 ? want : (int64_t)sms * 8);
+  // about 16 resident warps' worth of rows per SM over the whole grid
+  const int64_t gy = batch < 65535 ? batch : 65535;
+  int64_t gx = ((int64_t)sms * 8 + gy - 1) / gy;
+  const int64_t need = (rows + 7) / 8;
+  if (gx > need) gx = need;
+  if (gx < 1) gx = 1;
+  const dim3 grid((unsigned)gx, (unsigned)gy);
+  const int c4n = (int)(cols / 4);
   if (bf16)
-    cast_f32_view_kernel<__nv_bfloat16><<<blocks, 256, 0, st>>>(src, sv, static_cast<__nv_bfloat16*>(dst), dvw, n1, n2,
-                                                                rows, c4, total4);
+    cast_f32_view_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(src, sv, static_cast<__nv_bfloat16*>(dst), dvw, n1, n2,
+                                                              batch, rows, c4n);
   else
-    cast_f32_view_kernel<__half><<<blocks, 256, 0, st>>>(src, sv, static_cast<__half*>(dst), dvw, n1, n2, rows, c4,
-                                                         total4);
+    cast_f32_view_kernel<__half><<<grid, 256, 0, st>>>(src, sv, static_cast<__half*>(dst), dvw, n1, n2, batch, rows, c4n);
   return cudaGetLastError();
 }
 
