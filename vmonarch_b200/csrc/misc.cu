@@ -147,9 +147,9 @@ cudaError_t cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs
 
 // dst(s, r, c) = (T) src(s, r, c) over [batch][rows][cols] views (cols % 4 == 0, 16-byte aligned
 // rows): the fp32 accumulator of a strided (e.g. token-major) gradient converted in place of
-// cast_f32's flat rows. Grid row y = batch entries y, y + gridDim.y, ...; one warp per tensor row,
-// lane = 4 columns, so the view offsets are computed once per batch entry and there is no division
-// per element.
+// cast_f32's flat rows. Grid row y = batch entries y, y + gridDim.y, ...; one warp per four tensor
+// rows, lane = 4 columns, so the view offsets are computed once per batch entry and there is no
+// division per element.
 template <typename T>
 __global__ void __launch_bounds__(256) cast_f32_view_kernel(const float* src, View sv, T* dst, View dvw, int n1, int n2,
                                                             int64_t batch, int64_t rows, int c4n) {
@@ -157,15 +157,24 @@ __global__ void __launch_bounds__(256) cast_f32_view_kernel(const float* src, Vi
   for (int64_t bi = blockIdx.y; bi < batch; bi += gridDim.y) {
     const float* s0 = src + view_offset(sv, n1, n2, bi, 0);
     T* d0 = dst + view_offset(dvw, n1, n2, bi, 0);
-    for (int64_t r = (int64_t)blockIdx.x * warps + (threadIdx.x >> 5); r < rows; r += (int64_t)gridDim.x * warps) {
-      const float* sr = s0 + r * sv.rs;
-      T* dr = d0 + r * dvw.rs;
+    // four rows per warp and pass: four 16-byte loads in flight per lane before the stores
+    for (int64_t r0 = ((int64_t)blockIdx.x * warps + (threadIdx.x >> 5)) * 4; r0 < rows;
+         r0 += (int64_t)gridDim.x * warps * 4) {
+      const int nr = rows - r0 < 4 ? (int)(rows - r0) : 4;
       for (int c = lane; c < c4n; c += 32) {
-        const float4 v = *reinterpret_cast<const float4*>(sr + 4 * c);
-        uint2 w;
-        w.x = Elem<T>::pack(v.x, v.y);
-        w.y = Elem<T>::pack(v.z, v.w);
-        *reinterpret_cast<uint2*>(dr + 4 * c) = w;
+        float4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u < nr) v[u] = *reinterpret_cast<const float4*>(s0 + (r0 + u) * sv.rs + 4 * c);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (u < nr) {
+            uint2 w;
+            w.x = Elem<T>::pack(v[u].x, v[u].y);
+            w.y = Elem<T>::pack(v[u].z, v[u].w);
+            *reinterpret_cast<uint2*>(d0 + (r0 + u) * dvw.rs + 4 * c) = w;
+          }
+        }
       }
     }
   }
@@ -177,10 +186,10 @@ cudaError_t cast_f32_view(const float* src, const View& sv, void* dst, const Vie
   int dev = 0, sms = 148;
   cudaGetDevice(&dev);
   cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  // about 16 resident warps' worth of rows per SM over the whole grid
+  // about eight 256-thread blocks per SM over the whole grid
   const int64_t gy = batch < 65535 ? batch : 65535;
   int64_t gx = ((int64_t)sms * 8 + gy - 1) / gy;
-  const int64_t need = (rows + 7) / 8;
+  const int64_t need = (rows + 31) / 32;  // 8 warps x 4 rows per block and pass
   if (gx > need) gx = need;
   if (gx < 1) gx = 1;
   const dim3 grid((unsigned)gx, (unsigned)gy);
