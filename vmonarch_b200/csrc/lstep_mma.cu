@@ -108,6 +108,53 @@ __device__ __forceinline__ void mm_tn64(float (&acc)[MP / 16][8][4], const T* S,
   }
 }
 
+// Transpose of an 8 x 8 block of 16-bit values held one row per four lanes (row lane / 4, columns
+// 2 (lane % 4) and 2 (lane % 4) + 1, low half first): the result holds the transposed block in
+// the same layout.
+__device__ __forceinline__ uint32_t movt(uint32_t x) {
+  uint32_t y;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
+
+// m16n8k16 A fragments of the TRANSPOSE of an accumulator-layout MP x MP matrix V (rows i, columns
+// k): at[rt][kk] covers rows [16 rt, 16 rt + 16) (k) and columns [16 kk, 16 kk + 16) (i) of V^T.
+// Each register is one packed 8 x 8 block of V moved across the lanes, so the fragments hold the
+// same 16-bit values a transposed ldmatrix of V staged in shared memory would load.
+template <typename T, int MP>
+__device__ __forceinline__ void frag_t_from_acc(const float (&v)[MP / 16][MP / 8][4],
+                                                uint32_t (&at)[MP / 16][MP / 16][4]) {
+#pragma unroll
+  for (int rt = 0; rt < MP / 16; ++rt)
+#pragma unroll
+    for (int kk = 0; kk < MP / 16; ++kk) {
+      at[rt][kk][0] = movt(Elem<T>::pack(v[kk][2 * rt][0], v[kk][2 * rt][1]));
+      at[rt][kk][1] = movt(Elem<T>::pack(v[kk][2 * rt + 1][0], v[kk][2 * rt + 1][1]));
+      at[rt][kk][2] = movt(Elem<T>::pack(v[kk][2 * rt][2], v[kk][2 * rt][3]));
+      at[rt][kk][3] = movt(Elem<T>::pack(v[kk][2 * rt + 1][2], v[kk][2 * rt + 1][3]));
+    }
+}
+
+// mm_tn64 with the transposed A in registers (frag_t_from_acc) instead of a staging tile.
+template <typename T, int MP, int BCH>
+__device__ __forceinline__ void mm_tn64_reg(float (&acc)[MP / 16][8][4], const uint32_t (&at)[MP / 16][MP / 16][4],
+                                            const T* B, int bc0, int zr, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < MP / 16; ++kk) {
+    const int r = min(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), zr);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(smem_u32(B + swz<BCH>(r, bc0 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
+#pragma unroll
+      for (int mt = 0; mt < MP / 16; ++mt) {
+        mma16816<T>(acc[mt][2 * np], at[mt][kk], b0, b1);
+        mma16816<T>(acc[mt][2 * np + 1], at[mt][kk], b2, b3);
+      }
+    }
+  }
+}
+
 // out[i][n] += sum_k A[i][k] * B[k][n] with A given in accumulator layout (registers).
 template <typename T, int MP, int BCH>
 __device__ __forceinline__ void mm_rn64(float (&acc)[MP / 16][8][4], const float (&A)[MP / 16][MP / 8][4], const T* B,
@@ -183,14 +230,15 @@ __device__ __forceinline__ void stage_rows64_dot(T* S, int c0, const float (&v)[
     }
 }
 
-// Gathers rows i < m (token i*b + j) of a [N][W] tensor, columns [c0*8, (c0+nch)*8), into a
-// swizzled [m + 1][CH] tile; rows whose token < skip are zero-filled. Row m is the tile's zero row
-// (zero_row), which the MMA loaders read for every row index >= m.
 // Offset (elements) of head hb of a [bh][N][cols] view split (n1, 1): (hb % n1) s1 + (hb / n1) s3.
 __device__ __forceinline__ int64_t head_off(const View& v, int n1, int64_t hb) {
   const int64_t c3 = hb / n1;
   return (hb - c3 * n1) * v.s1 + c3 * v.s3;
 }
+
+// Gathers rows i < m (token i*b + j) of a [N][W] tensor, columns [c0*8, (c0+nch)*8), into a
+// swizzled [m + 1][CH] tile; rows whose token < skip are zero-filled. Row m is the tile's zero row
+// (zero_row), which the MMA loaders read for every row index >= m.
 
 template <typename T, int CH>
 __device__ __forceinline__ void gather(T* dst, const T* src, int64_t W, int c0, int nch, int m, int64_t b, int j,
@@ -208,11 +256,12 @@ __device__ __forceinline__ void zero_row(T* dst, int m, int lane) {
 }
 
 // Per-warp shared memory (bytes) of the L-step kernels: gathered tiles of m + 1 rows (the last one
-// zero) and m x m staging tiles of MP rows. The layout below follows the same order.
+// zero); the forward adds an m x m staging tile of MP rows and MP column scales. The layout below
+// follows the same order.
 template <int MP>
 __host__ __device__ __forceinline__ size_t lstep_warp_bytes(int m, int D, int OW, bool bwd, int esize) {
   const size_t rows = (size_t)m + 1;
-  return bwd ? (rows * (2 * D + OW) + 2 * (size_t)MP * (MP + 8)) * esize
+  return bwd ? rows * (2 * D + OW) * esize
              : (rows * (D + OW) + (size_t)MP * (MP + 8)) * esize + MP * sizeof(float);
 }
 
@@ -380,8 +429,6 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   T* sq = reinterpret_cast<T*>(smem_raw + warp * lstep_warp_bytes<MP>(m, D, OW, true, sizeof(T)));
   T* so = sq + (m + 1) * D;     // out rows (kr | y), later the dout staging
   T* sg = so + (m + 1) * OW;    // du (non-last) or dz (last), element dtype
-  T* sa = sg + (m + 1) * D;     // m x m staging (a or a*c)
-  T* sd = sa + MP * Tile<MP>::SA;  // m x m staging (dlog)
 
   const int64_t col = (int64_t)blockIdx.x * kWarpsBwd + warp;
   if (col >= p.bh * p.b) return;
@@ -491,9 +538,9 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
 #pragma unroll
         for (int e = 0; e < 2; ++e) g[mt][nt][2 * h + e] = a[mt][nt][2 * h + e] * (g[mt][nt][2 * h + e] - rs) * p.scale;
     }
-  stage_mm<T, MP>(sd, g, lane);
-  if (LAST) stage_mm<T, MP>(sa, a, lane);
-  __syncwarp();
+  // a^T (last) as transposed A fragments for dout[D:] = a^T dz; a is not needed after this
+  uint32_t at[MP / 16][MP / 16][4];
+  if (LAST) frag_t_from_acc<T, MP>(a, at);
 
   // dq_i += sum_k (scale dlog_ik) out_k  [non-last: + sum_k (a_ik c_k) du_k]
   float* gdq = p.dq + head_off(p.dqv, p.n1, bh);
@@ -530,6 +577,8 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   // over out; delta_k = sum_c out_k[c] dout_k[c] is summed on the way, the preprocessing of the
   // R step's attention backward)
   T* gdo = static_cast<T*>(p.dout) + head_off(p.doutv, p.n1, bh);
+  uint32_t gt[MP / 16][MP / 16][4];  // (scale dlog)^T as transposed A fragments
+  frag_t_from_acc<T, MP>(g, gt);
   float dot[MP / 16][2];
 #pragma unroll
   for (int mt = 0; mt < MP / 16; ++mt) dot[mt][0] = dot[mt][1] = 0.f;
@@ -537,7 +586,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   for (int half = 0; half < D / 64; ++half) {
     float acc[MP / 16][8][4];
     zero<MP>(acc);
-    mm_tn64<T, MP, DCH>(acc, sd, sq, half * 8, m, lane);
+    mm_tn64_reg<T, MP, DCH>(acc, gt, sq, half * 8, m, lane);
     stage_rows64_dot<T, MP, OCH>(so, half * 8, acc, dot, m, lane);
   }
   if (LAST) {
@@ -545,7 +594,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
     for (int half = 0; half < D / 64; ++half) {
       float acc[MP / 16][8][4];
       zero<MP>(acc);
-      mm_tn64<T, MP, DCH>(acc, sa, sg, half * 8, m, lane);
+      mm_tn64_reg<T, MP, DCH>(acc, at, sg, half * 8, m, lane);
       stage_rows64_dot<T, MP, OCH>(so, DCH + half * 8, acc, dot, m, lane);
     }
   }
@@ -573,6 +622,9 @@ cudaError_t launch(const LstepParams& p, bool bwd, cudaStream_t st) {
   const size_t smem = per_warp * warps;
   auto kern = bwd ? lstep_bwd_mma_kernel<T, MP, D, LAST> : lstep_fwd_mma_kernel<T, MP, D, LAST>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  // residency is bounded by shared memory: ask for the largest carveout
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
   if (e != cudaSuccess) return e;
   const int64_t blocks = (p.bh * p.b + warps - 1) / warps;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
