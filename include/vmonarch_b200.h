@@ -228,7 +228,7 @@ int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream);
 /* Strided layout of an L-step call (ABI version 6): each tensor is a [bh][N][cols] view (rows =
  * tokens) whose head hb starts at (hb % n1) * s1 + (hb / n1) * s3 (s2 unused); a token-major
  * (B, N, H, D) tensor is {H * D, D, 0, N * H * D} with n1 = H. ent and delta_out stay dense. The
- * D = 128 kernels (m <= 32) take any view; other shapes need uniform views. */
+ * kernels for m <= 64 with d in {64, 128} take any view; other shapes need dense tensors. */
 typedef struct vmb_lstep_layout {
   int64_t n1;
   vmb_view q, out, u, z, du, dz, dq, dout;

@@ -523,7 +523,7 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
     if (!dense(p.qv, a->d, a->q) || !dense(p.outv, a->dw, a->out) || !dense(p.uv, a->d, a->u) ||
         !dense(p.zv, dv, a->z) || (bwd && (!dense(p.duv, a->d, a->du) || !dense(p.dzv, dv, a->dz) ||
                                            !dense(p.dqv, a->d, a->dq) || !dense(p.doutv, a->dw, a->dout))))
-      return fail(VMB_ENOTSUP, "%s: strided layouts need m <= 32 (got m=%lld, d=%d)", what, (long long)a->m, a->d);
+      return fail(VMB_ENOTSUP, "%s: strided layouts need m <= 64 and d in {64, 128} (got m=%lld, d=%d)", what, (long long)a->m, a->d);
   }
   cudaError_t e = vmb::lstep_launch(p, a->last != 0, bwd, bf16, st);
   if (e == cudaSuccess && p.delta_out) {

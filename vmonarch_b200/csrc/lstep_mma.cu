@@ -1,9 +1,10 @@
-// Monarch L step on warp-level tensor-core MMA (mma.sync m16n8k16, fp32 accumulate), m <= 32.
+// Monarch L step on warp-level tensor-core MMA (mma.sync m16n8k16, fp32 accumulate), m <= 64.
 //
 // Same mathematics as lstep.cu (reference video_monarch_attention/vmonarch.py:51-63 and its
-// autograd backward); this is the fast path for the shapes VMonarch uses (Dv == D, m <= 32).
-// One warp owns one grid column j of one (batch, head): it gathers the m rows q_i = q[i*b + j]
-// and out_k = out[k*b + j] (16-byte cp.async, rows padded to MP = 16 or 32 with zeros), and
+// autograd backward); this is the fast path for the shapes VMonarch uses (Dv == D, m <= 64).
+// For m <= 32 one warp owns one grid column j of one (batch, head) (for m <= 64, one CTA of four
+// warps: see the kernels at the end): it gathers the m rows q_i = q[i*b + j]
+// and out_k = out[k*b + j] (16-byte cp.async, rows padded to MP = 16, 32 or 64 with zeros), and
 // every m x m x D contraction is a handful of MMAs out of swizzled shared memory. The L step is
 // HBM-bound (~10 flop/byte), so the tensor cores only serve to keep the arithmetic off the
 // critical path; outputs are staged in shared memory and written with 16-byte stores.
@@ -242,8 +243,8 @@ __device__ __forceinline__ int64_t head_off(const View& v, int n1, int64_t hb) {
 
 template <typename T, int CH>
 __device__ __forceinline__ void gather(T* dst, const T* src, int64_t W, int c0, int nch, int m, int64_t b, int j,
-                                       int64_t skip, int lane) {
-  for (int c = lane; c < m * nch; c += 32) {
+                                       int64_t skip, int lane, int nthr = 32) {
+  for (int c = lane; c < m * nch; c += nthr) {
     const int i = c / nch, ch = c % nch;
     const int64_t tok = (int64_t)i * b + j;
     const bool ok = tok >= skip;
@@ -251,8 +252,8 @@ __device__ __forceinline__ void gather(T* dst, const T* src, int64_t W, int c0, 
   }
 }
 template <typename T, int CH>
-__device__ __forceinline__ void zero_row(T* dst, int m, int lane) {
-  for (int ch = lane; ch < CH; ch += 32) *reinterpret_cast<uint4*>(dst + m * CH * 8 + ch * 8) = make_uint4(0, 0, 0, 0);
+__device__ __forceinline__ void zero_row(T* dst, int m, int lane, int nthr = 32) {
+  for (int ch = lane; ch < CH; ch += nthr) *reinterpret_cast<uint4*>(dst + m * CH * 8 + ch * 8) = make_uint4(0, 0, 0, 0);
 }
 
 // Per-warp shared memory (bytes) of the L-step kernels: gathered tiles of m + 1 rows (the last one
@@ -268,8 +269,8 @@ __host__ __device__ __forceinline__ size_t lstep_warp_bytes(int m, int D, int OW
 // Writes rows r < m of a swizzled [MP][CH] staging tile to token r*b + j of a [N][W] tensor.
 template <typename T, int CH>
 __device__ __forceinline__ void scatter(T* dst, const T* S, int64_t W, int c0, int nch, int m, int64_t b, int j,
-                                        int64_t skip, int MP, int lane) {
-  for (int c = lane; c < MP * nch; c += 32) {
+                                        int64_t skip, int MP, int lane, int nthr = 32) {
+  for (int c = lane; c < MP * nch; c += nthr) {
     const int r = c / nch, ch = c % nch;
     const int64_t tok = (int64_t)r * b + j;
     if (r < m && tok >= skip)
@@ -614,6 +615,481 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   scatter<T, OCH>(gdo, so, p.doutv.rs, 0, OCH, m, p.b, j, 0, MP, lane);
 }
 
+// ============================================================================ 32 < m <= 64
+// One CTA of four warps per grid column (MP = 64). Warp w owns the logit rows [16 w, 16 w + 16):
+// the row-local products (logits, softmax, z, G or dA, dlog, dq) stay in its registers, as in the
+// one-warp kernels above; the products that sum over rows (column masses, u, dout) go through
+// m x m staging tiles in shared memory, warp w producing their rows [16 w, 16 w + 16). The
+// helpers below are the one-m-tile forms of the ones above.
+constexpr int kMP4 = 64;
+constexpr int kWarps4 = 4;
+constexpr int kNT4 = kMP4 / 8;  // 8-column tiles of an m x m row block
+
+// acc[nt] (rows [r0, r0 + 16), all MP columns k) = sum_d X[r][d] * Y[k][d]
+template <typename T, int D, int XCH, int YCH>
+__device__ __forceinline__ void mm_rows_t(float (&acc)[kNT4][4], const T* X, int xc0, const T* Y, int yc0, int r0,
+                                          int zr, int lane) {
+#pragma unroll
+  for (int kk = 0; kk < D / 16; ++kk) {
+    uint32_t a[4];
+    ldsm_x4(smem_u32(X + swz<XCH>(min(r0 + (lane & 15), zr), xc0 + kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
+#pragma unroll
+    for (int np = 0; np < kMP4 / 16; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4(smem_u32(Y + swz<YCH>(min(np * 16 + (lane & 7) + ((lane >> 4) << 3), zr), yc0 + kk * 2 + ((lane >> 3) & 1))),
+              b0, b1, b2, b3);
+      mma16816<T>(acc[2 * np], a, b0, b1);
+      mma16816<T>(acc[2 * np + 1], a, b2, b3);
+    }
+  }
+}
+
+__device__ __forceinline__ void zero_t(float (&a)[8][4]) {
+#pragma unroll
+  for (int n = 0; n < 8; ++n) a[n][0] = a[n][1] = a[n][2] = a[n][3] = 0.f;
+}
+
+// softmax_rows for the rows [r0, r0 + 16)
+__device__ __forceinline__ void softmax_t(float (&acc)[kNT4][4], const float (&ent)[kNT4][2], float scale, int m, int r0,
+                                          int lane) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float mx = -INFINITY;
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int k = nt * 8 + (lane & 3) * 2 + e;
+        const float x = k < m ? (acc[nt][2 * h + e] * scale + ent[nt][e]) * kLog2e : -INFINITY;
+        acc[nt][2 * h + e] = x;
+        mx = fmaxf(mx, x);
+      }
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+    mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+    float s = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float pv = exp2f(acc[nt][2 * h + e] - mx);
+        acc[nt][2 * h + e] = pv;
+        s += pv;
+      }
+    s += __shfl_xor_sync(0xffffffffu, s, 1);
+    s += __shfl_xor_sync(0xffffffffu, s, 2);
+    const bool row_ok = r0 + (lane >> 2) + h * 8 < m;
+    const float inv = row_ok ? 1.f / s : 0.f;
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) acc[nt][2 * h + e] *= inv;
+  }
+}
+
+// Column sums over this warp's 16 rows: cs[nt][e] is column nt * 8 + 2 (lane & 3) + e (replicated
+// over lane >> 2).
+__device__ __forceinline__ void col_sums_t(const float (&v)[kNT4][4], float (&cs)[kNT4][2]) {
+#pragma unroll
+  for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float s = v[nt][e] + v[nt][2 + e];
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 8);
+      s += __shfl_xor_sync(0xffffffffu, s, 16);
+      cs[nt][e] = s;
+    }
+}
+
+// Rows [r0, r0 + 16) of an m x m matrix into the row-major [MP][SA] staging tile.
+template <typename T>
+__device__ __forceinline__ void stage_mm_t(T* S, const float (&v)[kNT4][4], int r0, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int r = r0 + (lane >> 2) + h * 8, c = nt * 8 + (lane & 3) * 2;
+      *reinterpret_cast<uint32_t*>(S + r * Tile<kMP4>::SA + c) = Elem<T>::pack(v[nt][2 * h], v[nt][2 * h + 1]);
+    }
+}
+
+// out[k][n] for k in [r0, r0 + 16), 64 columns from chunk bc0 of B: sum_i S[i][k] * B[i][n]
+// (the staging tile read transposed, B rows i).
+template <typename T, int BCH>
+__device__ __forceinline__ void mm_tn64_t(float (&acc)[8][4], const T* S, const T* B, int bc0, int r0, int zr, int lane) {
+  const int mi = lane >> 3;
+#pragma unroll
+  for (int kk = 0; kk < kMP4 / 16; ++kk) {
+    uint32_t a[4];
+    ldsm_x4_t(smem_u32(S + (kk * 16 + (lane & 7) + ((mi >> 1) << 3)) * Tile<kMP4>::SA + r0 + ((mi & 1) << 3)), a[0], a[1],
+              a[2], a[3]);
+    const int r = min(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), zr);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(smem_u32(B + swz<BCH>(r, bc0 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
+      mma16816<T>(acc[2 * np], a, b0, b1);
+      mma16816<T>(acc[2 * np + 1], a, b2, b3);
+    }
+  }
+}
+
+// out[i][n] += sum_k A[i][k] * B[k][n] for this warp's 16 rows, A in accumulator layout.
+template <typename T, int BCH>
+__device__ __forceinline__ void mm_rn64_t(float (&acc)[8][4], const float (&A)[kNT4][4], const T* B, int bc0, int zr,
+                                          int lane) {
+#pragma unroll
+  for (int kk = 0; kk < kMP4 / 16; ++kk) {
+    uint32_t a[4];
+    a[0] = Elem<T>::pack(A[2 * kk][0], A[2 * kk][1]);
+    a[1] = Elem<T>::pack(A[2 * kk][2], A[2 * kk][3]);
+    a[2] = Elem<T>::pack(A[2 * kk + 1][0], A[2 * kk + 1][1]);
+    a[3] = Elem<T>::pack(A[2 * kk + 1][2], A[2 * kk + 1][3]);
+    const int r = min(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), zr);
+#pragma unroll
+    for (int np = 0; np < 4; ++np) {
+      uint32_t b0, b1, b2, b3;
+      ldsm_x4_t(smem_u32(B + swz<BCH>(r, bc0 + np * 2 + (lane >> 4))), b0, b1, b2, b3);
+      mma16816<T>(acc[2 * np], a, b0, b1);
+      mma16816<T>(acc[2 * np + 1], a, b2, b3);
+    }
+  }
+}
+
+// stage_rows64 / stage_rows64_dot for the rows [r0, r0 + 16)
+template <typename T, int CH>
+__device__ __forceinline__ void stage_rows64_t(T* S, int c0, const float (&v)[8][4], const float* rowscale, int m, int r0,
+                                               int lane) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = r0 + (lane >> 2) + h * 8;
+    if (r >= m) continue;
+    const float s = rowscale ? rowscale[r] : 1.f;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int col = c0 * 8 + nt * 8 + (lane & 3) * 2;
+      *reinterpret_cast<uint32_t*>(S + swz<CH>(r, col >> 3) + (col & 7)) = Elem<T>::pack(v[nt][2 * h] * s, v[nt][2 * h + 1] * s);
+    }
+  }
+}
+template <typename T, int CH>
+__device__ __forceinline__ void stage_rows64_dot_t(T* S, int c0, const float (&v)[8][4], float (&dot)[2], int m, int r0,
+                                                   int lane) {
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int r = r0 + (lane >> 2) + h * 8;
+    if (r >= m) continue;
+#pragma unroll
+    for (int nt = 0; nt < 8; ++nt) {
+      const int col = c0 * 8 + nt * 8 + (lane & 3) * 2;
+      uint32_t* q = reinterpret_cast<uint32_t*>(S + swz<CH>(r, col >> 3) + (col & 7));
+      const uint32_t w = Elem<T>::pack(v[nt][2 * h], v[nt][2 * h + 1]);
+      const float2 o = Elem<T>::unpack(*q), g = Elem<T>::unpack(w);
+      dot[h] = fmaf(o.x, g.x, fmaf(o.y, g.y, dot[h]));
+      *q = w;
+    }
+  }
+}
+
+// Shared memory (bytes) of one column's CTA: gathered tiles of m + 1 rows, the m x m staging
+// tiles (the forward's a; the backward's dlog and a), then fp32 column partials and scales.
+__host__ __device__ __forceinline__ size_t lstep4_bytes(int m, int D, int OW, bool bwd, int esize) {
+  const size_t rows = (size_t)m + 1;
+  const size_t tiles = bwd ? rows * (2 * D + OW) : rows * (D + OW);
+  const size_t stg = (bwd ? 2 : 1) * (size_t)kMP4 * Tile<kMP4>::SA;
+  const size_t floats = bwd ? (2 * kWarps4 + 2) * (size_t)kMP4 : (kWarps4 + 1) * (size_t)kMP4;
+  return (tiles + stg) * esize + floats * sizeof(float);
+}
+
+template <typename T, int D, bool LAST>
+__global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const LstepParams p) {
+  constexpr int MP = kMP4, DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8, NTH = kWarps4 * 32;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r0 = 16 * warp;
+  const int m = (int)p.m;
+  T* sq = reinterpret_cast<T*>(smem_raw);
+  T* so = sq + (m + 1) * D;
+  T* sa = so + (m + 1) * OW;                                        // a, MP x SA
+  float* part = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);  // [warp][k] column partials
+  float* svec = part + kWarps4 * MP;                               // [k] c_k
+
+  const int64_t bh = blockIdx.x / p.b;  // one CTA per grid column: bh * b CTAs
+  const int j = (int)(blockIdx.x % p.b);
+  const int64_t N = p.m * p.b;
+  const T* gq = static_cast<const T*>(p.q) + head_off(p.qv, p.n1, bh);
+  const T* go = static_cast<const T*>(p.out) + head_off(p.outv, p.n1, bh);
+  gather<T, DCH>(sq, gq, p.qv.rs, 0, DCH, m, p.b, j, 0, tid, NTH);
+  gather<T, OCH>(so, go, p.outv.rs, 0, OCH, m, p.b, j, 0, tid, NTH);
+  cp_async_commit();
+  zero_row<T, DCH>(sq, m, tid, NTH);
+  zero_row<T, OCH>(so, m, tid, NTH);
+  float ent[kNT4][2];
+  load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
+  cp_async_wait<0>();
+  __syncthreads();
+
+  float a[kNT4][4];
+#pragma unroll
+  for (int nt = 0; nt < kNT4; ++nt) a[nt][0] = a[nt][1] = a[nt][2] = a[nt][3] = 0.f;
+  mm_rows_t<T, D, DCH, OCH>(a, sq, 0, so, 0, r0, m, lane);
+  softmax_t(a, ent, p.scale, m, r0, lane);
+
+  if (LAST) {
+    // z_i = sum_k a_ik y_k -> staged in sq once every warp's logits have read it
+    __syncthreads();
+    T* gz = static_cast<T*>(p.z) + head_off(p.zv, p.n1, bh);
+#pragma unroll 1
+    for (int half = 0; half < D / 64; ++half) {
+      float z[8][4];
+      zero_t(z);
+      mm_rn64_t<T, OCH>(z, a, so, DCH + half * 8, m, lane);
+      stage_rows64_t<T, DCH>(sq, half * 8, z, nullptr, m, r0, lane);
+    }
+    __syncthreads();
+    scatter<T, DCH>(gz, sq, p.zv.rs, 0, DCH, m, p.b, j, p.skip_rows, MP, tid, NTH);
+  } else {
+    float cs[kNT4][2];
+    col_sums_t(a, cs);
+    if ((lane >> 2) == 0) {
+#pragma unroll
+      for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) part[warp * MP + nt * 8 + lane * 2 + e] = cs[nt][e];
+    }
+    stage_mm_t<T>(sa, a, r0, lane);
+    __syncthreads();
+    if (tid < MP) {
+      float c = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps4; ++w) c += part[w * MP + tid];
+      svec[tid] = p.scale / fmaxf(c, p.min_col_mass);
+    }
+    __syncthreads();
+    // u_k = c_k sum_i a_ik q_i for k in this warp's rows, staged over out_D (free after the logits)
+    T* gu = static_cast<T*>(p.u) + head_off(p.uv, p.n1, bh);
+#pragma unroll 1
+    for (int half = 0; half < D / 64; ++half) {
+      float u[8][4];
+      zero_t(u);
+      mm_tn64_t<T, DCH>(u, sa, sq, half * 8, r0, m, lane);
+      stage_rows64_t<T, OCH>(so, half * 8, u, svec, m, r0, lane);
+    }
+    __syncthreads();
+    scatter<T, OCH>(gu, so, p.uv.rs, 0, DCH, m, p.b, j, 0, MP, tid, NTH);
+  }
+}
+
+template <typename T, int D, bool LAST>
+__global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const LstepParams p) {
+  constexpr int MP = kMP4, DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8, NTH = kWarps4 * 32;
+  extern __shared__ __align__(128) uint8_t smem_raw[];
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r0 = 16 * warp;
+  const int m = (int)p.m;
+  T* sq = reinterpret_cast<T*>(smem_raw);
+  T* so = sq + (m + 1) * D;          // out rows (kr | y), later the dout staging
+  T* sg = so + (m + 1) * OW;         // du (non-last) or dz (last), element dtype
+  T* sd = sg + (m + 1) * D;          // dlog staging, MP x SA
+  T* sa = sd + MP * Tile<MP>::SA;    // a staging (last), MP x SA
+  float* part = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);  // [2][warp][k]: sums of a, of a G
+  float* svec = part + 2 * kWarps4 * MP;                           // [2][k]: c_k, dcm_k
+
+  const int64_t bh = blockIdx.x / p.b;
+  const int j = (int)(blockIdx.x % p.b);
+  const int64_t N = p.m * p.b;
+  gather<T, DCH>(sq, static_cast<const T*>(p.q) + head_off(p.qv, p.n1, bh), p.qv.rs, 0, DCH, m, p.b, j, 0, tid, NTH);
+  gather<T, OCH>(so, static_cast<const T*>(p.out) + head_off(p.outv, p.n1, bh), p.outv.rs, 0, OCH, m, p.b, j, 0, tid,
+                 NTH);
+  if (LAST)
+    gather<T, DCH>(sg, static_cast<const T*>(p.dz) + head_off(p.dzv, p.n1, bh), p.dzv.rs, 0, DCH, m, p.b, j,
+                   p.skip_rows, tid, NTH);
+  cp_async_commit();
+  zero_row<T, DCH>(sq, m, tid, NTH);
+  zero_row<T, OCH>(so, m, tid, NTH);
+  zero_row<T, DCH>(sg, m, tid, NTH);
+  if (!LAST) {  // du is fp32: convert while the other rows are in flight, four chunks per round trip
+    const float* du = p.du + head_off(p.duv, p.n1, bh);
+    const int kChunks = (m * DCH + NTH - 1) / NTH;
+#pragma unroll 1
+    for (int t0 = 0; t0 < kChunks; t0 += 4) {
+      float4 v[4][2];
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = tid + NTH * (t0 + u), k = c / DCH, ch = c % DCH;
+        if (k < m) {
+          const float4* src = reinterpret_cast<const float4*>(du + ((int64_t)k * p.b + j) * p.duv.rs + ch * 8);
+          v[u][0] = src[0];
+          v[u][1] = src[1];
+        } else {
+          v[u][0] = v[u][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        const int c = tid + NTH * (t0 + u), k = c / DCH, ch = c % DCH;
+        if (k >= m) continue;
+        uint4 w;
+        w.x = Elem<T>::pack(v[u][0].x, v[u][0].y);
+        w.y = Elem<T>::pack(v[u][0].z, v[u][0].w);
+        w.z = Elem<T>::pack(v[u][1].x, v[u][1].y);
+        w.w = Elem<T>::pack(v[u][1].z, v[u][1].w);
+        *reinterpret_cast<uint4*>(sg + swz<DCH>(k, ch)) = w;
+      }
+    }
+  }
+  float ent[kNT4][2];
+  load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
+  cp_async_wait<0>();
+  __syncthreads();
+
+  float a[kNT4][4], g[kNT4][4], ac[kNT4][4];
+#pragma unroll
+  for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+    for (int e = 0; e < 4; ++e) a[nt][e] = g[nt][e] = ac[nt][e] = 0.f;
+  mm_rows_t<T, D, DCH, OCH>(a, sq, 0, so, 0, r0, m, lane);
+  softmax_t(a, ent, p.scale, m, r0, lane);
+  if (LAST) {
+    mm_rows_t<T, D, DCH, OCH>(g, sg, 0, so, DCH, r0, m, lane);  // dA = dz y^T
+  } else {
+    // G = q du^T; column sums of a and of a G over all rows (every warp's partials)
+    mm_rows_t<T, D, DCH, DCH>(g, sq, 0, sg, 0, r0, m, lane);
+    float cs[kNT4][2], dc[kNT4][2];
+    col_sums_t(a, cs);
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) ac[nt][e] = a[nt][e] * g[nt][e];
+    col_sums_t(ac, dc);
+    if ((lane >> 2) == 0) {
+#pragma unroll
+      for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+          part[warp * MP + nt * 8 + lane * 2 + e] = cs[nt][e];
+          part[(kWarps4 + warp) * MP + nt * 8 + lane * 2 + e] = dc[nt][e];
+        }
+    }
+    __syncthreads();
+    if (tid < MP) {
+      float csum = 0.f, dsum = 0.f;
+#pragma unroll
+      for (int w = 0; w < kWarps4; ++w) {
+        csum += part[w * MP + tid];
+        dsum += part[(kWarps4 + w) * MP + tid];
+      }
+      const float cm = fmaxf(csum, p.min_col_mass);
+      const float c = p.scale / cm;
+      svec[tid] = c;
+      svec[MP + tid] = csum > p.min_col_mass ? -dsum * c / cm : 0.f;
+    }
+    __syncthreads();
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const int k = nt * 8 + (lane & 3) * 2 + e;
+        const float c = svec[k], dcm = svec[MP + k];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          g[nt][2 * h + e] = c * g[nt][2 * h + e] + dcm;  // dA
+          ac[nt][2 * h + e] = a[nt][2 * h + e] * c;       // a * c
+        }
+      }
+  }
+  // dlog = a (dA - rowsum(a dA)), in place in g and pre-multiplied by scale
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    float rs = 0.f;
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt) rs += a[nt][2 * h] * g[nt][2 * h] + a[nt][2 * h + 1] * g[nt][2 * h + 1];
+    rs += __shfl_xor_sync(0xffffffffu, rs, 1);
+    rs += __shfl_xor_sync(0xffffffffu, rs, 2);
+#pragma unroll
+    for (int nt = 0; nt < kNT4; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) g[nt][2 * h + e] = a[nt][2 * h + e] * (g[nt][2 * h + e] - rs) * p.scale;
+  }
+
+  // dq_i += sum_k (scale dlog_ik) out_k  [non-last: + sum_k (a_ik c_k) du_k] for this warp's rows
+  float* gdq = p.dq + head_off(p.dqv, p.n1, bh);
+#pragma unroll 1
+  for (int half = 0; half < D / 64; ++half) {
+    float acc[8][4];
+    zero_t(acc);
+    mm_rn64_t<T, OCH>(acc, g, so, half * 8, m, lane);
+    if (!LAST) mm_rn64_t<T, DCH>(acc, ac, sg, half * 8, m, lane);
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int i = r0 + (lane >> 2) + h * 8;
+      if (i >= m) continue;
+      float* dst = gdq + ((int64_t)i * p.b + j) * p.dqv.rs + half * 64 + (lane & 3) * 2;
+      if (p.dq_store) {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+          *reinterpret_cast<float2*>(dst + nt * 8) = make_float2(acc[nt][2 * h], acc[nt][2 * h + 1]);
+      } else {
+#pragma unroll
+        for (int nt = 0; nt < 8; ++nt)
+          asm volatile("red.global.add.v2.f32 [%0], {%1, %2};" ::"l"(dst + nt * 8), "f"(acc[nt][2 * h]),
+                       "f"(acc[nt][2 * h + 1])
+                       : "memory");
+      }
+    }
+  }
+  stage_mm_t<T>(sd, g, r0, lane);
+  if (LAST) stage_mm_t<T>(sa, a, r0, lane);
+  __syncthreads();  // dlog (and a) staged; every warp's dq products are done with the out rows
+
+  // dout_k[:D] = sum_i (scale dlog_ik) q_i ; last: dout_k[D:] = sum_i a_ik dz_i, for k in this
+  // warp's rows, staged over out with delta_k = sum_c out_k[c] dout_k[c] summed on the way
+  T* gdo = static_cast<T*>(p.dout) + head_off(p.doutv, p.n1, bh);
+  float dot[2] = {0.f, 0.f};
+#pragma unroll 1
+  for (int half = 0; half < D / 64; ++half) {
+    float acc[8][4];
+    zero_t(acc);
+    mm_tn64_t<T, DCH>(acc, sd, sq, half * 8, r0, m, lane);
+    stage_rows64_dot_t<T, OCH>(so, half * 8, acc, dot, m, r0, lane);
+  }
+  if (LAST) {
+#pragma unroll 1
+    for (int half = 0; half < D / 64; ++half) {
+      float acc[8][4];
+      zero_t(acc);
+      mm_tn64_t<T, DCH>(acc, sa, sg, half * 8, r0, m, lane);
+      stage_rows64_dot_t<T, OCH>(so, DCH + half * 8, acc, dot, m, r0, lane);
+    }
+  }
+  if (p.delta_out) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      float d = dot[h];
+      d += __shfl_xor_sync(0xffffffffu, d, 1);
+      d += __shfl_xor_sync(0xffffffffu, d, 2);
+      const int r = r0 + (lane >> 2) + h * 8;
+      if ((lane & 3) == 0 && r < m) p.delta_out[bh * N + (int64_t)r * p.b + j] = d;
+    }
+  }
+  __syncthreads();
+  scatter<T, OCH>(gdo, so, p.doutv.rs, 0, OCH, m, p.b, j, 0, MP, tid, NTH);
+}
+
+template <typename T, int D, bool LAST>
+cudaError_t launch4(const LstepParams& p, bool bwd, cudaStream_t st) {
+  constexpr int OW = LAST ? 2 * D : D;
+  const size_t smem = lstep4_bytes((int)p.m, D, OW, bwd, sizeof(T));
+  auto kern = bwd ? lstep_bwd_mma4_kernel<T, D, LAST> : lstep_fwd_mma4_kernel<T, D, LAST>;
+  cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  if (e != cudaSuccess) return e;
+  e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
+  if (e != cudaSuccess) return e;
+  const int64_t blocks = p.bh * p.b;
+  if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
+  if (blocks == 0) return cudaSuccess;
+  kern<<<(unsigned)blocks, kWarps4 * 32, smem, st>>>(p);
+  return cudaGetLastError();
+}
+
 template <typename T, int MP, int D, bool LAST>
 cudaError_t launch(const LstepParams& p, bool bwd, cudaStream_t st) {
   constexpr int OW = LAST ? 2 * D : D;
@@ -635,13 +1111,14 @@ cudaError_t launch(const LstepParams& p, bool bwd, cudaStream_t st) {
 template <typename T, int D>
 cudaError_t dispatch_m(const LstepParams& p, bool last, bool bwd, cudaStream_t st) {
   if (p.m <= 16) return last ? launch<T, 16, D, true>(p, bwd, st) : launch<T, 16, D, false>(p, bwd, st);
-  return last ? launch<T, 32, D, true>(p, bwd, st) : launch<T, 32, D, false>(p, bwd, st);
+  if (p.m <= 32) return last ? launch<T, 32, D, true>(p, bwd, st) : launch<T, 32, D, false>(p, bwd, st);
+  return last ? launch4<T, D, true>(p, bwd, st) : launch4<T, D, false>(p, bwd, st);
 }
 
 }  // namespace
 
 bool lstep_mma_supported(const LstepParams& p, bool last) {
-  return p.m <= 32 && (p.d == 64 || p.d == 128) && p.dw == (last ? 2 * p.d : p.d);
+  return p.m <= kMP4 && (p.d == 64 || p.d == 128) && p.dw == (last ? 2 * p.d : p.d);
 }
 
 cudaError_t lstep_mma_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st) {
