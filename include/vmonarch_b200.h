@@ -223,12 +223,13 @@ int vmb_fea_bwd_noalloc(const vmb_fea_bwd_args* a, void* stream);
  * backward, last == 1: dz [bh][N][dw-d] gradient of z; tokens < skip_rows carry none
  * backward outputs: dq [bh][N][d] fp32 (ADDED into, or OVERWRITTEN when dq_store != 0),
  *   dout [bh][N][dw] gradient of out.
- * m <= 64, d in {16, 32, 64, 128}, dw - d in {16, ..., 256} and a multiple of d when last.
+ * m <= 128 (m <= 64 unless d in {64, 128} with dw = d, or 2d when last), d in {16, 32, 64, 128},
+ * dw - d in {16, ..., 256} and a multiple of d when last.
  */
 /* Strided layout of an L-step call (ABI version 6): each tensor is a [bh][N][cols] view (rows =
  * tokens) whose head hb starts at (hb % n1) * s1 + (hb / n1) * s3 (s2 unused); a token-major
  * (B, N, H, D) tensor is {H * D, D, 0, N * H * D} with n1 = H. ent and delta_out stay dense. The
- * kernels for m <= 64 with d in {64, 128} take any view; other shapes need dense tensors. */
+ * kernels for m <= 128 with d in {64, 128} take any view; other shapes need dense tensors. */
 typedef struct vmb_lstep_layout {
   int64_t n1;
   vmb_view q, out, u, z, du, dz, dq, dout;

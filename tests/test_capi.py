@@ -138,8 +138,11 @@ def test_fea_bwd_workspace_and_validation():
 def test_lstep_validation():
     a = N.LstepArgs()
     a.q = a.out = a.ent = a.u = 256
-    a.bh, a.m, a.b, a.d, a.dw, a.dtype = 1, 65, 4, 64, 64, 0
-    assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # m > 64
+    a.bh, a.m, a.b, a.d, a.dw, a.dtype = 1, 129, 4, 64, 64, 0
+    assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # m > 128
+    a.m, a.d, a.dw = 65, 32, 32
+    assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # m > 64 on the generic kernel (d = 32)
+    assert b"> 64" in N.lib.vmb_last_error()
     a.m = 4
     a.d = a.dw = 256
     assert N.lib.vmb_lstep_fwd(ctypes.byref(a), None) == 2     # d = 256 (D + Dv <= 256 in VMonarch)

@@ -29,10 +29,12 @@ def oracle_lstep(q, out, ent, m, b, D, last, scale, mcm):
 
 # (21, 1560): 780 column groups, more than the persistent tcgen05 forward keeps resident, so its
 # CTAs walk several groups each;
-# m in (32, 64]: the four-warp kernels (one CTA per grid column)
+# m in (32, 128]: the four- and eight-warp kernels (one CTA per grid column)
 @pytest.mark.parametrize("m, b, D, Dv", [(21, 37, 128, 128), (4, 64, 64, 64), (64, 9, 64, 128), (1, 33, 128, 128),
                                          (32, 16, 128, 128), (21, 1560, 128, 128), (33, 17, 128, 128),
-                                         (48, 40, 128, 128), (64, 25, 128, 128), (40, 30, 64, 64)])
+                                         (48, 40, 128, 128), (64, 25, 128, 128), (40, 30, 64, 64),
+                                         (65, 12, 128, 128), (100, 20, 128, 128), (128, 9, 64, 64),
+                                         (128, 17, 128, 128)])
 @pytest.mark.parametrize("last, skip_half", [(False, False), (True, False), (True, True)])
 def test_lstep_forward_and_backward(m, b, D, Dv, last, skip_half):
     # D = 128 forwards without skipped tokens run the tcgen05 kernel, the others mma.sync

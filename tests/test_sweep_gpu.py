@@ -70,7 +70,7 @@ def test_fea_sweep(case):
 
 def vm_draw(seed):
     r = random.Random(10_000 + seed)
-    m = r.randint(2, 64)
+    m = r.randint(2, 128)
     b = r.choice([16, 33, 64, 100, 128, 129, 200, 257])
     N = m * b
     return dict(B=r.choice([1, 2]), H=r.choice([1, 2]), m=m, b=b, iters=r.choice([1, 2, 3]),

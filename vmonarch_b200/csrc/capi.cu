@@ -454,7 +454,7 @@ static int lstep_check(const char* what, const vmb_lstep_args* a, bool bwd) {
   if (!a) return fail(VMB_EINVAL, "%s: null args", what);
   if (a->dtype != VMB_DTYPE_BF16 && a->dtype != VMB_DTYPE_F16) return fail(VMB_EINVAL, "%s: unknown dtype", what);
   if (a->d != 16 && a->d != 32 && a->d != 64 && a->d != 128) return fail(VMB_ENOTSUP, "%s: no kernel for d=%d", what, a->d);
-  if (a->m < 1 || a->m > 64) return fail(VMB_ENOTSUP, "%s: num_blocks m=%lld outside [1, 64]", what, (long long)a->m);
+  if (a->m < 1 || a->m > 128) return fail(VMB_ENOTSUP, "%s: num_blocks m=%lld outside [1, 128]", what, (long long)a->m);
   if (a->b < 1 || a->bh < 0) return fail(VMB_EINVAL, "%s: bad sizes", what);
   if (a->last) {
     const int dv = a->dw - a->d;
@@ -514,6 +514,10 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
     return cuda_status(vmb::lstep_tc_launch(p, a->last != 0, bwd, bf16, st), what);
   if (vmb::lstep_mma_supported(p, a->last != 0))
     return cuda_status(vmb::lstep_mma_launch(p, a->last != 0, bwd, bf16, st), what);
+  // the generic kernel keeps the m rows of every operand in shared memory
+  if (a->m > 64)
+    return fail(VMB_ENOTSUP, "%s: num_blocks m=%lld > 64 needs d in {64, 128} with dw = d (2d when last)", what,
+                (long long)a->m);
   if (L) {
     // the generic kernel takes dense [bh][N][cols] tensors only
     auto dense = [&](const vmb::View& v, int64_t cols, const void* ptr) {
@@ -523,7 +527,7 @@ static int lstep_run(const char* what, const vmb_lstep_args* a, bool bwd, void* 
     if (!dense(p.qv, a->d, a->q) || !dense(p.outv, a->dw, a->out) || !dense(p.uv, a->d, a->u) ||
         !dense(p.zv, dv, a->z) || (bwd && (!dense(p.duv, a->d, a->du) || !dense(p.dzv, dv, a->dz) ||
                                            !dense(p.dqv, a->d, a->dq) || !dense(p.doutv, a->dw, a->dout))))
-      return fail(VMB_ENOTSUP, "%s: strided layouts need m <= 64 and d in {64, 128} (got m=%lld, d=%d)", what, (long long)a->m, a->d);
+      return fail(VMB_ENOTSUP, "%s: strided layouts need m <= 128 and d in {64, 128} (got m=%lld, d=%d)", what, (long long)a->m, a->d);
   }
   cudaError_t e = vmb::lstep_launch(p, a->last != 0, bwd, bf16, st);
   if (e == cudaSuccess && p.delta_out) {

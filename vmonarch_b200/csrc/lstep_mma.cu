@@ -1,10 +1,10 @@
-// Monarch L step on warp-level tensor-core MMA (mma.sync m16n8k16, fp32 accumulate), m <= 64.
+// Monarch L step on warp-level tensor-core MMA (mma.sync m16n8k16, fp32 accumulate), m <= 128.
 //
 // Same mathematics as lstep.cu (reference video_monarch_attention/vmonarch.py:51-63 and its
-// autograd backward); this is the fast path for the shapes VMonarch uses (Dv == D, m <= 64).
-// For m <= 32 one warp owns one grid column j of one (batch, head) (for m <= 64, one CTA of four
-// warps: see the kernels at the end): it gathers the m rows q_i = q[i*b + j]
-// and out_k = out[k*b + j] (16-byte cp.async, rows padded to MP = 16, 32 or 64 with zeros), and
+// autograd backward); this is the fast path for the shapes VMonarch uses (Dv == D, m <= 128).
+// For m <= 32 one warp owns one grid column j of one (batch, head) (for m <= 128, one CTA of four
+// or eight warps: see the kernels at the end): it gathers the m rows q_i = q[i*b + j]
+// and out_k = out[k*b + j] (16-byte cp.async, rows padded to MP = 16, 32, 64 or 128 with zeros), and
 // every m x m x D contraction is a handful of MMAs out of swizzled shared memory. The L step is
 // HBM-bound (~10 flop/byte), so the tensor cores only serve to keep the arithmetic off the
 // critical path; outputs are staged in shared memory and written with 16-byte stores.
@@ -615,26 +615,25 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   scatter<T, OCH>(gdo, so, p.doutv.rs, 0, OCH, m, p.b, j, 0, MP, lane);
 }
 
-// ============================================================================ 32 < m <= 64
-// One CTA of four warps per grid column (MP = 64). Warp w owns the logit rows [16 w, 16 w + 16):
+// ============================================================================ 32 < m <= 128
+// One CTA of NW = 4 (m <= 64) or 8 (m <= 128) warps per grid column, MP = 16 NW. Warp w owns the
+// logit rows [16 w, 16 w + 16):
 // the row-local products (logits, softmax, z, G or dA, dlog, dq) stay in its registers, as in the
 // one-warp kernels above; the products that sum over rows (column masses, u, dout) go through
 // m x m staging tiles in shared memory, warp w producing their rows [16 w, 16 w + 16). The
 // helpers below are the one-m-tile forms of the ones above.
-constexpr int kMP4 = 64;
-constexpr int kWarps4 = 4;
-constexpr int kNT4 = kMP4 / 8;  // 8-column tiles of an m x m row block
+constexpr int kMaxMP = 128;  // the largest grid (m) of the tensor-core L-step kernels
 
 // acc[nt] (rows [r0, r0 + 16), all MP columns k) = sum_d X[r][d] * Y[k][d]
-template <typename T, int D, int XCH, int YCH>
-__device__ __forceinline__ void mm_rows_t(float (&acc)[kNT4][4], const T* X, int xc0, const T* Y, int yc0, int r0,
+template <typename T, int MP, int D, int XCH, int YCH>
+__device__ __forceinline__ void mm_rows_t(float (&acc)[MP / 8][4], const T* X, int xc0, const T* Y, int yc0, int r0,
                                           int zr, int lane) {
 #pragma unroll
   for (int kk = 0; kk < D / 16; ++kk) {
     uint32_t a[4];
     ldsm_x4(smem_u32(X + swz<XCH>(min(r0 + (lane & 15), zr), xc0 + kk * 2 + (lane >> 4))), a[0], a[1], a[2], a[3]);
 #pragma unroll
-    for (int np = 0; np < kMP4 / 16; ++np) {
+    for (int np = 0; np < MP / 16; ++np) {
       uint32_t b0, b1, b2, b3;
       ldsm_x4(smem_u32(Y + swz<YCH>(min(np * 16 + (lane & 7) + ((lane >> 4) << 3), zr), yc0 + kk * 2 + ((lane >> 3) & 1))),
               b0, b1, b2, b3);
@@ -650,13 +649,14 @@ __device__ __forceinline__ void zero_t(float (&a)[8][4]) {
 }
 
 // softmax_rows for the rows [r0, r0 + 16)
-__device__ __forceinline__ void softmax_t(float (&acc)[kNT4][4], const float (&ent)[kNT4][2], float scale, int m, int r0,
+template <int MP>
+__device__ __forceinline__ void softmax_t(float (&acc)[MP / 8][4], const float (&ent)[MP / 8][2], float scale, int m, int r0,
                                           int lane) {
 #pragma unroll
   for (int h = 0; h < 2; ++h) {
     float mx = -INFINITY;
 #pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt)
+    for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int k = nt * 8 + (lane & 3) * 2 + e;
@@ -668,7 +668,7 @@ __device__ __forceinline__ void softmax_t(float (&acc)[kNT4][4], const float (&e
     mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
     float s = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt)
+    for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const float pv = exp2f(acc[nt][2 * h + e] - mx);
@@ -680,7 +680,7 @@ __device__ __forceinline__ void softmax_t(float (&acc)[kNT4][4], const float (&e
     const bool row_ok = r0 + (lane >> 2) + h * 8 < m;
     const float inv = row_ok ? 1.f / s : 0.f;
 #pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt)
+    for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) acc[nt][2 * h + e] *= inv;
   }
@@ -688,9 +688,10 @@ __device__ __forceinline__ void softmax_t(float (&acc)[kNT4][4], const float (&e
 
 // Column sums over this warp's 16 rows: cs[nt][e] is column nt * 8 + 2 (lane & 3) + e (replicated
 // over lane >> 2).
-__device__ __forceinline__ void col_sums_t(const float (&v)[kNT4][4], float (&cs)[kNT4][2]) {
+template <int MP>
+__device__ __forceinline__ void col_sums_t(const float (&v)[MP / 8][4], float (&cs)[MP / 8][2]) {
 #pragma unroll
-  for (int nt = 0; nt < kNT4; ++nt)
+  for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
     for (int e = 0; e < 2; ++e) {
       float s = v[nt][e] + v[nt][2 + e];
@@ -701,27 +702,43 @@ __device__ __forceinline__ void col_sums_t(const float (&v)[kNT4][4], float (&cs
     }
 }
 
-// Rows [r0, r0 + 16) of an m x m matrix into the row-major [MP][SA] staging tile.
-template <typename T>
-__device__ __forceinline__ void stage_mm_t(T* S, const float (&v)[kNT4][4], int r0, int lane) {
+// col_sums_t of the elementwise product u * v
+template <int MP>
+__device__ __forceinline__ void col_sums_prod_t(const float (&u)[MP / 8][4], const float (&v)[MP / 8][4],
+                                                float (&cs)[MP / 8][2]) {
 #pragma unroll
-  for (int nt = 0; nt < kNT4; ++nt)
+  for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+    for (int e = 0; e < 2; ++e) {
+      float s = u[nt][e] * v[nt][e] + u[nt][2 + e] * v[nt][2 + e];
+      s += __shfl_xor_sync(0xffffffffu, s, 4);
+      s += __shfl_xor_sync(0xffffffffu, s, 8);
+      s += __shfl_xor_sync(0xffffffffu, s, 16);
+      cs[nt][e] = s;
+    }
+}
+
+// Rows [r0, r0 + 16) of an m x m matrix into the row-major [MP][SA] staging tile.
+template <typename T, int MP>
+__device__ __forceinline__ void stage_mm_t(T* S, const float (&v)[MP / 8][4], int r0, int lane) {
+#pragma unroll
+  for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int r = r0 + (lane >> 2) + h * 8, c = nt * 8 + (lane & 3) * 2;
-      *reinterpret_cast<uint32_t*>(S + r * Tile<kMP4>::SA + c) = Elem<T>::pack(v[nt][2 * h], v[nt][2 * h + 1]);
+      *reinterpret_cast<uint32_t*>(S + r * Tile<MP>::SA + c) = Elem<T>::pack(v[nt][2 * h], v[nt][2 * h + 1]);
     }
 }
 
 // out[k][n] for k in [r0, r0 + 16), 64 columns from chunk bc0 of B: sum_i S[i][k] * B[i][n]
 // (the staging tile read transposed, B rows i).
-template <typename T, int BCH>
+template <typename T, int BCH, int MP>
 __device__ __forceinline__ void mm_tn64_t(float (&acc)[8][4], const T* S, const T* B, int bc0, int r0, int zr, int lane) {
   const int mi = lane >> 3;
 #pragma unroll
-  for (int kk = 0; kk < kMP4 / 16; ++kk) {
+  for (int kk = 0; kk < MP / 16; ++kk) {
     uint32_t a[4];
-    ldsm_x4_t(smem_u32(S + (kk * 16 + (lane & 7) + ((mi >> 1) << 3)) * Tile<kMP4>::SA + r0 + ((mi & 1) << 3)), a[0], a[1],
+    ldsm_x4_t(smem_u32(S + (kk * 16 + (lane & 7) + ((mi >> 1) << 3)) * Tile<MP>::SA + r0 + ((mi & 1) << 3)), a[0], a[1],
               a[2], a[3]);
     const int r = min(kk * 16 + (lane & 7) + (((lane >> 3) & 1) << 3), zr);
 #pragma unroll
@@ -735,11 +752,11 @@ __device__ __forceinline__ void mm_tn64_t(float (&acc)[8][4], const T* S, const 
 }
 
 // out[i][n] += sum_k A[i][k] * B[k][n] for this warp's 16 rows, A in accumulator layout.
-template <typename T, int BCH>
-__device__ __forceinline__ void mm_rn64_t(float (&acc)[8][4], const float (&A)[kNT4][4], const T* B, int bc0, int zr,
+template <typename T, int BCH, int MP>
+__device__ __forceinline__ void mm_rn64_t(float (&acc)[8][4], const float (&A)[MP / 8][4], const T* B, int bc0, int zr,
                                           int lane) {
 #pragma unroll
-  for (int kk = 0; kk < kMP4 / 16; ++kk) {
+  for (int kk = 0; kk < MP / 16; ++kk) {
     uint32_t a[4];
     a[0] = Elem<T>::pack(A[2 * kk][0], A[2 * kk][1]);
     a[1] = Elem<T>::pack(A[2 * kk][2], A[2 * kk][3]);
@@ -793,17 +810,17 @@ __device__ __forceinline__ void stage_rows64_dot_t(T* S, int c0, const float (&v
 
 // Shared memory (bytes) of one column's CTA: gathered tiles of m + 1 rows, the m x m staging
 // tiles (the forward's a; the backward's dlog and a), then fp32 column partials and scales.
-__host__ __device__ __forceinline__ size_t lstep4_bytes(int m, int D, int OW, bool bwd, int esize) {
-  const size_t rows = (size_t)m + 1;
+__host__ __device__ __forceinline__ size_t lstepw_bytes(int m, int D, int OW, bool bwd, int esize, int NW) {
+  const size_t MP = 16 * (size_t)NW, rows = (size_t)m + 1;
   const size_t tiles = bwd ? rows * (2 * D + OW) : rows * (D + OW);
-  const size_t stg = (bwd ? 2 : 1) * (size_t)kMP4 * Tile<kMP4>::SA;
-  const size_t floats = bwd ? (2 * kWarps4 + 2) * (size_t)kMP4 : (kWarps4 + 1) * (size_t)kMP4;
+  const size_t stg = (bwd ? 2 : 1) * MP * (MP + 8);  // Tile<MP>::SA = MP + 8
+  const size_t floats = bwd ? (2 * NW + 2) * MP : (NW + 1) * MP;
   return (tiles + stg) * esize + floats * sizeof(float);
 }
 
-template <typename T, int D, bool LAST>
-__global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const LstepParams p) {
-  constexpr int MP = kMP4, DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8, NTH = kWarps4 * 32;
+template <typename T, int D, bool LAST, int NW>
+__global__ void __launch_bounds__(NW * 32) lstep_fwd_mmaw_kernel(const LstepParams p) {
+  constexpr int MP = 16 * NW, DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8, NTH = NW * 32;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r0 = 16 * warp;
   const int m = (int)p.m;
@@ -811,7 +828,7 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const Lste
   T* so = sq + (m + 1) * D;
   T* sa = so + (m + 1) * OW;                                        // a, MP x SA
   float* part = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);  // [warp][k] column partials
-  float* svec = part + kWarps4 * MP;                               // [k] c_k
+  float* svec = part + NW * MP;                               // [k] c_k
 
   const int64_t bh = blockIdx.x / p.b;  // one CTA per grid column: bh * b CTAs
   const int j = (int)(blockIdx.x % p.b);
@@ -823,16 +840,16 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const Lste
   cp_async_commit();
   zero_row<T, DCH>(sq, m, tid, NTH);
   zero_row<T, OCH>(so, m, tid, NTH);
-  float ent[kNT4][2];
+  float ent[MP / 8][2];
   load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
   cp_async_wait<0>();
   __syncthreads();
 
-  float a[kNT4][4];
+  float a[MP / 8][4];
 #pragma unroll
-  for (int nt = 0; nt < kNT4; ++nt) a[nt][0] = a[nt][1] = a[nt][2] = a[nt][3] = 0.f;
-  mm_rows_t<T, D, DCH, OCH>(a, sq, 0, so, 0, r0, m, lane);
-  softmax_t(a, ent, p.scale, m, r0, lane);
+  for (int nt = 0; nt < MP / 8; ++nt) a[nt][0] = a[nt][1] = a[nt][2] = a[nt][3] = 0.f;
+  mm_rows_t<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, r0, m, lane);
+  softmax_t<MP>(a, ent, p.scale, m, r0, lane);
 
   if (LAST) {
     // z_i = sum_k a_ik y_k -> staged in sq once every warp's logits have read it
@@ -842,26 +859,26 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const Lste
     for (int half = 0; half < D / 64; ++half) {
       float z[8][4];
       zero_t(z);
-      mm_rn64_t<T, OCH>(z, a, so, DCH + half * 8, m, lane);
+      mm_rn64_t<T, OCH, MP>(z, a, so, DCH + half * 8, m, lane);
       stage_rows64_t<T, DCH>(sq, half * 8, z, nullptr, m, r0, lane);
     }
     __syncthreads();
     scatter<T, DCH>(gz, sq, p.zv.rs, 0, DCH, m, p.b, j, p.skip_rows, MP, tid, NTH);
   } else {
-    float cs[kNT4][2];
-    col_sums_t(a, cs);
+    float cs[MP / 8][2];
+    col_sums_t<MP>(a, cs);
     if ((lane >> 2) == 0) {
 #pragma unroll
-      for (int nt = 0; nt < kNT4; ++nt)
+      for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) part[warp * MP + nt * 8 + lane * 2 + e] = cs[nt][e];
     }
-    stage_mm_t<T>(sa, a, r0, lane);
+    stage_mm_t<T, MP>(sa, a, r0, lane);
     __syncthreads();
     if (tid < MP) {
       float c = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps4; ++w) c += part[w * MP + tid];
+      for (int w = 0; w < NW; ++w) c += part[w * MP + tid];
       svec[tid] = p.scale / fmaxf(c, p.min_col_mass);
     }
     __syncthreads();
@@ -871,7 +888,7 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const Lste
     for (int half = 0; half < D / 64; ++half) {
       float u[8][4];
       zero_t(u);
-      mm_tn64_t<T, DCH>(u, sa, sq, half * 8, r0, m, lane);
+      mm_tn64_t<T, DCH, MP>(u, sa, sq, half * 8, r0, m, lane);
       stage_rows64_t<T, OCH>(so, half * 8, u, svec, m, r0, lane);
     }
     __syncthreads();
@@ -879,9 +896,9 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_fwd_mma4_kernel(const Lste
   }
 }
 
-template <typename T, int D, bool LAST>
-__global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const LstepParams p) {
-  constexpr int MP = kMP4, DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8, NTH = kWarps4 * 32;
+template <typename T, int D, bool LAST, int NW>
+__global__ void __launch_bounds__(NW * 32) lstep_bwd_mmaw_kernel(const LstepParams p) {
+  constexpr int MP = 16 * NW, DCH = D / 8, OW = LAST ? 2 * D : D, OCH = OW / 8, NTH = NW * 32;
   extern __shared__ __align__(128) uint8_t smem_raw[];
   const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, r0 = 16 * warp;
   const int m = (int)p.m;
@@ -891,7 +908,7 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
   T* sd = sg + (m + 1) * D;          // dlog staging, MP x SA
   T* sa = sd + MP * Tile<MP>::SA;    // a staging (last), MP x SA
   float* part = reinterpret_cast<float*>(sa + MP * Tile<MP>::SA);  // [2][warp][k]: sums of a, of a G
-  float* svec = part + 2 * kWarps4 * MP;                           // [2][k]: c_k, dcm_k
+  float* svec = part + 2 * NW * MP;                           // [2][k]: c_k, dcm_k
 
   const int64_t bh = blockIdx.x / p.b;
   const int j = (int)(blockIdx.x % p.b);
@@ -936,46 +953,43 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
       }
     }
   }
-  float ent[kNT4][2];
+  float ent[MP / 8][2];
   load_ent<T, MP>(ent, p.ent + bh * N, p.b, j, m, lane);
   cp_async_wait<0>();
   __syncthreads();
 
-  float a[kNT4][4], g[kNT4][4], ac[kNT4][4];
+  // a, then (non-last, once dlog is formed) a_ik c_k in place: two m x m arrays per thread
+  float a[MP / 8][4], g[MP / 8][4];
 #pragma unroll
-  for (int nt = 0; nt < kNT4; ++nt)
+  for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
-    for (int e = 0; e < 4; ++e) a[nt][e] = g[nt][e] = ac[nt][e] = 0.f;
-  mm_rows_t<T, D, DCH, OCH>(a, sq, 0, so, 0, r0, m, lane);
-  softmax_t(a, ent, p.scale, m, r0, lane);
+    for (int e = 0; e < 4; ++e) a[nt][e] = g[nt][e] = 0.f;
+  mm_rows_t<T, MP, D, DCH, OCH>(a, sq, 0, so, 0, r0, m, lane);
+  softmax_t<MP>(a, ent, p.scale, m, r0, lane);
   if (LAST) {
-    mm_rows_t<T, D, DCH, OCH>(g, sg, 0, so, DCH, r0, m, lane);  // dA = dz y^T
+    mm_rows_t<T, MP, D, DCH, OCH>(g, sg, 0, so, DCH, r0, m, lane);  // dA = dz y^T
   } else {
     // G = q du^T; column sums of a and of a G over all rows (every warp's partials)
-    mm_rows_t<T, D, DCH, DCH>(g, sq, 0, sg, 0, r0, m, lane);
-    float cs[kNT4][2], dc[kNT4][2];
-    col_sums_t(a, cs);
-#pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt)
-#pragma unroll
-      for (int e = 0; e < 4; ++e) ac[nt][e] = a[nt][e] * g[nt][e];
-    col_sums_t(ac, dc);
+    mm_rows_t<T, MP, D, DCH, DCH>(g, sq, 0, sg, 0, r0, m, lane);
+    float cs[MP / 8][2], dc[MP / 8][2];
+    col_sums_t<MP>(a, cs);
+    col_sums_prod_t<MP>(a, g, dc);
     if ((lane >> 2) == 0) {
 #pragma unroll
-      for (int nt = 0; nt < kNT4; ++nt)
+      for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
           part[warp * MP + nt * 8 + lane * 2 + e] = cs[nt][e];
-          part[(kWarps4 + warp) * MP + nt * 8 + lane * 2 + e] = dc[nt][e];
+          part[(NW + warp) * MP + nt * 8 + lane * 2 + e] = dc[nt][e];
         }
     }
     __syncthreads();
     if (tid < MP) {
       float csum = 0.f, dsum = 0.f;
 #pragma unroll
-      for (int w = 0; w < kWarps4; ++w) {
+      for (int w = 0; w < NW; ++w) {
         csum += part[w * MP + tid];
-        dsum += part[(kWarps4 + w) * MP + tid];
+        dsum += part[(NW + w) * MP + tid];
       }
       const float cm = fmaxf(csum, p.min_col_mass);
       const float c = p.scale / cm;
@@ -984,16 +998,13 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
     }
     __syncthreads();
 #pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt)
+    for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) {
         const int k = nt * 8 + (lane & 3) * 2 + e;
         const float c = svec[k], dcm = svec[MP + k];
 #pragma unroll
-        for (int h = 0; h < 2; ++h) {
-          g[nt][2 * h + e] = c * g[nt][2 * h + e] + dcm;  // dA
-          ac[nt][2 * h + e] = a[nt][2 * h + e] * c;       // a * c
-        }
+        for (int h = 0; h < 2; ++h) g[nt][2 * h + e] = c * g[nt][2 * h + e] + dcm;  // dA
       }
   }
   // dlog = a (dA - rowsum(a dA)), in place in g and pre-multiplied by scale
@@ -1001,13 +1012,23 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
   for (int h = 0; h < 2; ++h) {
     float rs = 0.f;
 #pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt) rs += a[nt][2 * h] * g[nt][2 * h] + a[nt][2 * h + 1] * g[nt][2 * h + 1];
+    for (int nt = 0; nt < MP / 8; ++nt) rs += a[nt][2 * h] * g[nt][2 * h] + a[nt][2 * h + 1] * g[nt][2 * h + 1];
     rs += __shfl_xor_sync(0xffffffffu, rs, 1);
     rs += __shfl_xor_sync(0xffffffffu, rs, 2);
 #pragma unroll
-    for (int nt = 0; nt < kNT4; ++nt)
+    for (int nt = 0; nt < MP / 8; ++nt)
 #pragma unroll
       for (int e = 0; e < 2; ++e) g[nt][2 * h + e] = a[nt][2 * h + e] * (g[nt][2 * h + e] - rs) * p.scale;
+  }
+  if (!LAST) {  // a -> a_ik c_k for the dq term
+#pragma unroll
+    for (int nt = 0; nt < MP / 8; ++nt)
+#pragma unroll
+      for (int e = 0; e < 2; ++e) {
+        const float c = svec[nt * 8 + (lane & 3) * 2 + e];
+        a[nt][e] *= c;
+        a[nt][2 + e] *= c;
+      }
   }
 
   // dq_i += sum_k (scale dlog_ik) out_k  [non-last: + sum_k (a_ik c_k) du_k] for this warp's rows
@@ -1016,8 +1037,8 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
   for (int half = 0; half < D / 64; ++half) {
     float acc[8][4];
     zero_t(acc);
-    mm_rn64_t<T, OCH>(acc, g, so, half * 8, m, lane);
-    if (!LAST) mm_rn64_t<T, DCH>(acc, ac, sg, half * 8, m, lane);
+    mm_rn64_t<T, OCH, MP>(acc, g, so, half * 8, m, lane);
+    if (!LAST) mm_rn64_t<T, DCH, MP>(acc, a, sg, half * 8, m, lane);
 #pragma unroll
     for (int h = 0; h < 2; ++h) {
       const int i = r0 + (lane >> 2) + h * 8;
@@ -1036,8 +1057,8 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
       }
     }
   }
-  stage_mm_t<T>(sd, g, r0, lane);
-  if (LAST) stage_mm_t<T>(sa, a, r0, lane);
+  stage_mm_t<T, MP>(sd, g, r0, lane);
+  if (LAST) stage_mm_t<T, MP>(sa, a, r0, lane);
   __syncthreads();  // dlog (and a) staged; every warp's dq products are done with the out rows
 
   // dout_k[:D] = sum_i (scale dlog_ik) q_i ; last: dout_k[D:] = sum_i a_ik dz_i, for k in this
@@ -1048,7 +1069,7 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
   for (int half = 0; half < D / 64; ++half) {
     float acc[8][4];
     zero_t(acc);
-    mm_tn64_t<T, DCH>(acc, sd, sq, half * 8, r0, m, lane);
+    mm_tn64_t<T, DCH, MP>(acc, sd, sq, half * 8, r0, m, lane);
     stage_rows64_dot_t<T, OCH>(so, half * 8, acc, dot, m, r0, lane);
   }
   if (LAST) {
@@ -1056,7 +1077,7 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
     for (int half = 0; half < D / 64; ++half) {
       float acc[8][4];
       zero_t(acc);
-      mm_tn64_t<T, DCH>(acc, sa, sg, half * 8, r0, m, lane);
+      mm_tn64_t<T, DCH, MP>(acc, sa, sg, half * 8, r0, m, lane);
       stage_rows64_dot_t<T, OCH>(so, DCH + half * 8, acc, dot, m, r0, lane);
     }
   }
@@ -1074,11 +1095,11 @@ __global__ void __launch_bounds__(kWarps4 * 32) lstep_bwd_mma4_kernel(const Lste
   scatter<T, OCH>(gdo, so, p.doutv.rs, 0, OCH, m, p.b, j, 0, MP, tid, NTH);
 }
 
-template <typename T, int D, bool LAST>
-cudaError_t launch4(const LstepParams& p, bool bwd, cudaStream_t st) {
+template <typename T, int D, bool LAST, int NW>
+cudaError_t launch_w(const LstepParams& p, bool bwd, cudaStream_t st) {
   constexpr int OW = LAST ? 2 * D : D;
-  const size_t smem = lstep4_bytes((int)p.m, D, OW, bwd, sizeof(T));
-  auto kern = bwd ? lstep_bwd_mma4_kernel<T, D, LAST> : lstep_fwd_mma4_kernel<T, D, LAST>;
+  const size_t smem = lstepw_bytes((int)p.m, D, OW, bwd, sizeof(T), NW);
+  auto kern = bwd ? lstep_bwd_mmaw_kernel<T, D, LAST, NW> : lstep_fwd_mmaw_kernel<T, D, LAST, NW>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   if (e != cudaSuccess) return e;
   e = cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, cudaSharedmemCarveoutMaxShared);
@@ -1086,7 +1107,7 @@ cudaError_t launch4(const LstepParams& p, bool bwd, cudaStream_t st) {
   const int64_t blocks = p.bh * p.b;
   if (blocks > 0x7fffffff) return cudaErrorInvalidConfiguration;
   if (blocks == 0) return cudaSuccess;
-  kern<<<(unsigned)blocks, kWarps4 * 32, smem, st>>>(p);
+  kern<<<(unsigned)blocks, NW * 32, smem, st>>>(p);
   return cudaGetLastError();
 }
 
@@ -1112,13 +1133,14 @@ template <typename T, int D>
 cudaError_t dispatch_m(const LstepParams& p, bool last, bool bwd, cudaStream_t st) {
   if (p.m <= 16) return last ? launch<T, 16, D, true>(p, bwd, st) : launch<T, 16, D, false>(p, bwd, st);
   if (p.m <= 32) return last ? launch<T, 32, D, true>(p, bwd, st) : launch<T, 32, D, false>(p, bwd, st);
-  return last ? launch4<T, D, true>(p, bwd, st) : launch4<T, D, false>(p, bwd, st);
+  if (p.m <= 64) return last ? launch_w<T, D, true, 4>(p, bwd, st) : launch_w<T, D, false, 4>(p, bwd, st);
+  return last ? launch_w<T, D, true, 8>(p, bwd, st) : launch_w<T, D, false, 8>(p, bwd, st);
 }
 
 }  // namespace
 
 bool lstep_mma_supported(const LstepParams& p, bool last) {
-  return p.m <= kMP4 && (p.d == 64 || p.d == 128) && p.dw == (last ? 2 * p.d : p.d);
+  return p.m <= kMaxMP && (p.d == 64 || p.d == 128) && p.dw == (last ? 2 * p.d : p.d);
 }
 
 cudaError_t lstep_mma_launch(const LstepParams& p, bool last, bool bwd, bool bf16, cudaStream_t st) {

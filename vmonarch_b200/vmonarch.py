@@ -48,7 +48,7 @@ def _alloc_like_layout(ref: torch.Tensor, cols: int, dtype) -> torch.Tensor:
 
 def _in_place(t: torch.Tensor, strided: bool) -> torch.Tensor:
     """`t` itself when the kernels can read it through its strides (dense or token-major; the D = 128
-    kernels with m <= 64 take any such layout), else a dense copy."""
+    kernels with m <= 128 take any such layout), else a dense copy."""
     return t if strided and ops.viewable(t) else t.contiguous()
 
 
@@ -63,7 +63,7 @@ class _VMonarchAttention(torch.autograd.Function):
         Dv = v.shape[-1]
         m, b = num_blocks, block_size
         scale = D ** -0.5
-        strided = D == 128 and Dv == 128 and m <= 64
+        strided = D == 128 and Dv == 128 and m <= 128
         qs, ks, vs = (_in_place(t, strided) for t in (q, k, v))
         dev, dt = q.device, q.dtype
         rr = min(max(int(recompute_tokens), 0), N)
