@@ -95,6 +95,22 @@ def check_exact_rows(z, q, k, v, r):
     torch.testing.assert_close(z[:, :, :r], sdpa, rtol=1.6e-2, atol=2e-3)
 
 
+@pytest.mark.parametrize("m, b, D", [(100, 9, 128), (128, 5, 64)])
+def test_vmonarch_many_grid_rows(m, b, D):
+    # grids above 64 rows run the eight-warp L-step kernels
+    gen = torch.Generator().manual_seed(m)
+    q, k, v, dz = (torch.randn(1, 2, m * b, D, generator=gen).bfloat16().float() for _ in range(4))
+    check(run_cuda(q, k, v, dz, m, b, 2, b), run_oracle(q, k, v, dz, m, b, 2, b))
+
+
+@pytest.mark.parametrize("m, D, Dv", [(129, 128, 128), (65, 32, 32), (65, 64, 128)])
+def test_vmonarch_grid_row_limit(m, D, Dv):
+    q, k = (torch.zeros(1, 1, m * 2, D, device="cuda", dtype=torch.bfloat16) for _ in range(2))
+    v = torch.zeros(1, 1, m * 2, Dv, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(NotImplementedError, match="grid rows"):
+        vmonarch_attention(q, k, v, m, 2, 2)
+
+
 def test_recompute_tokens_are_exact():
     torch.manual_seed(0)
     q, k, v = (torch.randn(1, 2, 4 * 128, 64, device="cuda", dtype=torch.bfloat16) for _ in range(3))

@@ -201,6 +201,12 @@ def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_t
     # the last R step attends over [k | v] (vmonarch.py:50): its value width D + Dv must be a
     # multiple of D and a width the reference kernel accepts (kernel.py:260, 324)
     assert (D + Dv) % D == 0 and D + Dv <= 256, f"D + Dv = {D + Dv} is not a valid last-step value width"
+    # the L step keeps a grid column's m rows on chip: up to 128 on the tensor-core kernels (D in
+    # {64, 128} with Dv == D), 64 on the generic kernel
+    max_m = 128 if D in (64, 128) and Dv == D else 64
+    if num_blocks > max_m:
+        raise NotImplementedError(f"num_blocks={num_blocks} > {max_m}: the L step supports at most {max_m} grid rows "
+                                  f"for D={D}, Dv={Dv}")
     return _VMonarchAttention.apply(q, k, v, int(num_blocks), int(block_size), int(num_iters), recompute_tokens,
                                     float(min_col_mass))
 
