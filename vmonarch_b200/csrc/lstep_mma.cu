@@ -616,7 +616,7 @@ __global__ void __launch_bounds__(kWarpsBwd * 32) lstep_bwd_mma_kernel(const Lst
   scatter<T, OCH>(gdo, so, p.doutv.rs, 0, OCH, m, p.b, j, 0, MP, lane);
 }
 
-// ============================================================================ 32 < m <= 128
+// ============================================================================ several warps per column
 // One CTA of NW = 4 (m <= 64) or 8 (m <= 128) warps per grid column, MP = 16 NW; also NW = 2 for
 // the non-last steps with 16 < m <= 32. Warp w owns the logit rows [16 w, 16 w + 16):
 // the row-local products (logits, softmax, z, G or dA, dlog, dq) stay in its registers, as in the
