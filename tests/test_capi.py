@@ -103,6 +103,10 @@ def test_fea_bwd_workspace_and_validation():
     # D = Dv = 64 runs the tcgen05 kernels over 64-column maps: the folded statistics planes only
     a.d, a.dv, a.dv1, a.grad_mode = 64, 64, 64, 0
     assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 3 * ((3 * 128 * 4 + 255) // 256) * 256
+    # D = 64 with Dv = 128 (separate values) takes the same kernels
+    a.dv = a.dv1 = 128
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 3 * ((3 * 128 * 4 + 255) // 256) * 256
+    a.dv = a.dv1 = 64
     # D = 128 runs on the tcgen05 kernels: three folded statistics planes of 3 x round_up(100, 128)
     # rows. Three query tiles cannot fill the GPU, so the dS^T route is not taken: no dS^T buffer.
     a.d, a.dv, a.dv1 = 128, 128, 128

@@ -184,7 +184,7 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   const bool vk = fwd_v_is_k(a) && a->d != 64;
   if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk)) {
     // a split key range adds the merge kernel
-    count(vmb::fea_fwd_sm100_split(a->batch, p.n_q, p.n_kv, a->dv, p.work, p.work_bytes) > 1 ? 2 : 1);
+    count(vmb::fea_fwd_sm100_split(a->batch, p.n_q, p.n_kv, a->d, a->dv, p.work, p.work_bytes) > 1 ? 2 : 1);
     return cuda_status(vmb::fea_fwd_sm100(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, vk, st), "vmb_fea_fwd");
   }
   if (L) {

@@ -1357,8 +1357,9 @@ int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv) {
 }
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {
-  // d = dv = 64 with separate values: the 128-column kernels over 64-column maps (zero second atom)
-  if (d == 64) return !vk && dv == 64 && dv1 == 64;
+  // d = 64 with separate values, dv = 64 or 128: the 128-column kernels over 64-column maps of the
+  // 64-wide tensors (zero second atom)
+  if (d == 64) return !vk && (dv == 64 || dv == 128) && dv1 == dv;
   if (d != 128) return false;
   if (vk) return dv1 == 128 && (dv == 128 || dv == 256);
   return dv == 128 && dv1 == 128;

@@ -1050,8 +1050,8 @@ cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bo
     if (dv == 128) return launch2<T, true, ENT>(p, batch, st);
     if (dv == 256 && dv1 == 128) return launch<T, 2, true, 3, ENT>(p, batch, st);
   } else {
-    // dv = 64 (d = 64): the 128-column kernel over 64-column maps; the second atoms load as zeros
-    // and the second half of O is clipped on store
+    // d = 64: the 128-column kernel over 64-column q / k maps (their second atoms load as zeros);
+    // with dv = 64 the v map loads zeros too and the second half of O is clipped on store
     if (dv == 128 || dv == 64) return launch2<T, false, ENT>(p, batch, st);
     if (dv == 256) return launch<T, 4, false, 2, ENT>(p, batch, st);
   }
@@ -1061,19 +1061,20 @@ cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bo
 }  // namespace
 
 bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk) {
-  if (d == 64) return !vk && dv == 64 && dv1 == 64;  // no key-range split (its merge is 128 wide)
+  // d = 64: 64-column q / k maps (second atoms load as zeros), v and o 64 or 128 wide; no key-range split
+  if (d == 64) return !vk && (dv == 64 || dv == 128) && dv1 == dv;
   if (d != 128) return false;
   if (vk) return dv == 128 || (dv == 256 && dv1 == 128);
   return (dv == 128 || dv == 256) && dv1 == dv;
 }
 
 int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk) {
-  if (!fea_fwd_sm100_supported(d, dv, dv1, vk) || dv != 128) return 0;  // only the two-stream kernel splits (d = 128)
+  if (d != 128 || !fea_fwd_sm100_supported(d, dv, dv1, vk) || dv != 128) return 0;  // only the two-stream kernel splits (d = 128)
   return split_bytes(fwd2_split(batch, n_q, n_kv), batch, n_q);
 }
 
-int fea_fwd_sm100_split(int64_t batch, int n_q, int n_kv, int dv, const void* work, int64_t work_bytes) {
-  if (dv != 128 || !work) return 1;
+int fea_fwd_sm100_split(int64_t batch, int n_q, int n_kv, int d, int dv, const void* work, int64_t work_bytes) {
+  if (d != 128 || dv != 128 || !work) return 1;
   const int ks = fwd2_split(batch, n_q, n_kv);
   return (ks > 1 && work_bytes >= split_bytes(ks, batch, n_q)) ? ks : 1;
 }
@@ -1105,7 +1106,7 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
   p.scale_log2 = fp.scale_log2;
   // key-range split (two-stream kernel, with a large enough workspace)
   const int nkt = (fp.n_kv + 127) / 128;
-  p.kv_split = fea_fwd_sm100_split(batch, fp.n_q, fp.n_kv, dv, fp.work, fp.work_bytes);
+  p.kv_split = fea_fwd_sm100_split(batch, fp.n_q, fp.n_kv, d, dv, fp.work, fp.work_bytes);
   p.kt_per = (nkt + p.kv_split - 1) / p.kv_split;
   p.n_seq = (int)batch;
   p.n_pad = (fp.n_q + 127) / 128 * 128;

@@ -54,7 +54,7 @@ int64_t fea_bwd_min_workspace_bytes(const vmb_fea_bwd_args* a);
 // Workspace bytes that let the tcgen05 forward split long key ranges (0: it would not split).
 int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk);
 // Key-range split the tcgen05 forward will use with this workspace (1 = none).
-int fea_fwd_sm100_split(int64_t batch, int n_q, int n_kv, int dv, const void* work, int64_t work_bytes);
+int fea_fwd_sm100_split(int64_t batch, int n_q, int n_kv, int d, int dv, const void* work, int64_t work_bytes);
 cudaError_t fea_bwd_sm100_status(cudaStream_t st, int* out);
 cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool vk, bool bf16, cudaStream_t st);
 cudaError_t fea_bwd_pre(const void* o, View ov, const void* dout, View dov, int n1, int n2, const float* lse,
