@@ -181,7 +181,9 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   const bool bf16 = a->dtype == VMB_DTYPE_BF16;
   // V aliasing K (the VMonarch R step): the key tile in shared memory doubles as the value tile.
   // At d = 64 the separate-values kernel reads the same tensor twice instead (its only tcgen05 route).
-  const bool vk = fwd_v_is_k(a) && a->d != 64;
+  // d = 64: V aliasing K runs as such only with a second value tensor ([K | V2], dv = 128); V = K
+  // alone takes the separate-values kernel over the same pointer
+  const bool vk = fwd_v_is_k(a) && (a->d != 64 || a->dv == 128);
   if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk)) {
     // a split key range adds the merge kernel
     count(vmb::fea_fwd_sm100_split(a->batch, p.n_q, p.n_kv, a->d, a->dv, p.work, p.work_bytes) > 1 ? 2 : 1);

@@ -54,6 +54,10 @@ struct Sm100FwdParams {
   int n1, n2;                   // batch split of the q / k / v / o maps (fea_params.h View)
   long long wait_limit;         // pipeline wait limit in cycles (0: kWaitCycles); shortened by tests
   int hold_loads;               // test of the timeout path: the producers issue no load
+  // d = 64 with V aliasing K and a second value tensor: the K tile's second atom is loaded from
+  // tm_x (V2) at column 0, so the tile holds [K | V2]; Q's second atom is zero, so S = Q K^T is
+  // unchanged and P V over the tile gives [P K | P V2]
+  int k_hi_x;
   int64_t n_pad;      // n_q rounded up to 128
   float scale_log2;
 };
@@ -592,11 +596,13 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         const uint32_t full = kl ? BAR_KFULL(s) : BAR_VFULL(s);
         const uint32_t slot = (kl ? sK : sV) + s * 2 * kAtom;
         mbar_expect_tx(full, 2 * kAtom);
+        const bool hx = kl && p.k_hi_x;  // second atom of the K tile from V2
+        const CUtensorMap* hi = (kl && !hx) ? &p.tm_k : &p.tm_x;
         tma_load(slot, kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j) * 128, bx, full);
-        tma_load(slot + kAtom, kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j) * 128, bx, full);
+        tma_load(slot + kAtom, hi, hx ? 0 : 64, (kt0 + j) * 128, bx, full);
         if (j + nslot < n_kt) {  // the tile one ring ahead into L2
           tma_prefetch(kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j + nslot) * 128, bx);
-          tma_prefetch(kl ? &p.tm_k : &p.tm_x, 64, (kt0 + j + nslot) * 128, bx);
+          tma_prefetch(hi, hx ? 0 : 64, (kt0 + j + nslot) * 128, bx);
         }
         armed[s] = j / nslot + 1;
       }
@@ -1061,8 +1067,9 @@ cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bo
 }  // namespace
 
 bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk) {
-  // d = 64: 64-column q / k maps (second atoms load as zeros), v and o 64 or 128 wide; no key-range split
-  if (d == 64) return !vk && (dv == 64 || dv == 128) && dv1 == dv;
+  // d = 64: 64-column q / k maps (second atoms load as zeros), v and o 64 or 128 wide; with V
+  // aliasing K, only [K | V2] (dv = 128): the K tile's second atom holds V2. No key-range split.
+  if (d == 64) return vk ? dv == 128 && dv1 == 64 : (dv == 64 || dv == 128) && dv1 == dv;
   if (d != 128) return false;
   if (vk) return dv == 128 || (dv == 256 && dv1 == 128);
   return (dv == 128 || dv == 256) && dv1 == dv;
@@ -1098,6 +1105,7 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
   p.n2 = n2;
   p.wait_limit = fp.wait_limit;
   p.hold_loads = fp.hold_loads;
+  p.k_hi_x = (d == 64 && vk && dv == 128) ? 1 : 0;
   p.lse = fp.lse;
   p.ent = fp.ent;
   p.n_q = fp.n_q;
