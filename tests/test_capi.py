@@ -106,7 +106,14 @@ def test_fea_bwd_workspace_and_validation():
     # D = 64 with Dv = 128 (separate values) takes the same kernels
     a.dv = a.dv1 = 128
     assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 3 * ((3 * 128 * 4 + 255) // 256) * 256
+    # ... and so does D = 64 with V aliasing K and a second value tensor ([K | V2] tiles), except in
+    # the finalize mode, which the warp-level kernels serve (c and g per row)
+    a.dv, a.dv1, a.v_is_k, a.grad_mode = 128, 64, 1, 2
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 3 * ((3 * 128 * 4 + 255) // 256) * 256
+    a.grad_mode = 3
+    assert N.lib.vmb_fea_bwd_workspace_bytes(ctypes.byref(a)) == 2 * 1280
     a.dv = a.dv1 = 64
+    a.v_is_k, a.grad_mode = 0, 0
     # D = 128 runs on the tcgen05 kernels: three folded statistics planes of 3 x round_up(100, 128)
     # rows. Three query tiles cannot fill the GPU, so the dS^T route is not taken: no dS^T buffer.
     a.d, a.dv, a.dv1 = 128, 128, 128

@@ -206,6 +206,8 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
 // partial dQ tiles [split][batch][round_up(n_q, 128)][128]; the mma.sync path keeps c and g
 // [batch][n_q] and, in grad_mode 0, an fp32 dQ accumulator.
 static bool bwd_uses_sm100(const vmb_fea_bwd_args* a) {
+  // d = 64 with [K | V2]: the dK tile's halves are dK and dV2, with no finalize (grad_mode 3) form
+  if (a->d == 64 && a->v_is_k && a->dv == 128 && a->grad_mode == 3) return false;
   return vmb::fea_bwd_sm100_supported(a->d, a->dv, a->dv1, a->v_is_k != 0);
 }
 
@@ -248,7 +250,7 @@ static bool bwd_dq_uniform(const vmb_fea_bwd_args* a) {
 
 // tcgen05 path: dQ formed inside the dK kernel (no dq kernel, no split)
 static bool bwd_fuses_dq(const vmb_fea_bwd_args* a) {
-  return vmb::fea_bwd_fuses_dq((int)a->n_kv, a->dv, a->v_is_k != 0, a->grad_mode,
+  return vmb::fea_bwd_fuses_dq((int)a->n_kv, a->d, a->dv, a->v_is_k != 0, a->grad_mode,
                                a->deterministic != 0 || !bwd_dq_uniform(a));
 }
 

@@ -72,6 +72,11 @@ struct Sm100BwdParams {
   float* dq;     // fused dQ: dense fp32 [batch][n_q][128] with batch stride dq_bs, added into
   int64_t dq_bs;
   CUtensorMap tm_f0, tm_f1;  // acc 3: the fp32 accumulators of tm_g0 / tm_g1 (boxes of 32 x 128)
+  // d = 64 with V aliasing K and a second value tensor: the second atom of every K tile is V2,
+  // loaded from tm_b (dK / dV kernel) or tm_d (dq kernel) at column 0, so the tile is [K | V2];
+  // Q's second atom is zero, so S and dS are unchanged, dP = dO [K | V2]^T, and the dK
+  // accumulator's second half is dV2 (stored through tm_g1)
+  int k_hi_x;
   void* ds;                  // dK/dV kernel: dS^T out [batch][ds_rows][ds_ld] (16-bit), or null
   int64_t ds_ld, ds_bs;      // row stride (queries, padded to 64) and batch stride (elements)
 };
@@ -155,6 +160,24 @@ __device__ __forceinline__ void issue_grad_tile(const CUtensorMap* tm, uint32_t 
     for (int c = 0; c < 4; ++c) tma_store(tm, 32 * c, row0, bi, stage + c * 16384);
   } else {
     for (int a = 0; a < 2; ++a) tma_store(tm, 64 * a, row0, bi, stage + a * 16384);
+  }
+}
+
+// issue_grad_tile for a [lo | hi] tile of two 64-column tensors: columns [0, 64) through `lo`,
+// [64, 128) through `hi` from its column 0 (modes 0, 1, 2).
+__device__ __forceinline__ void issue_grad_tile_split(const CUtensorMap* lo, const CUtensorMap* hi, uint32_t stage,
+                                                      int row0, BIdx bi, int mode) {
+  if (mode == 1 || mode == 2) {
+    for (int c = 0; c < 4; ++c) {
+      const CUtensorMap* tm = c < 2 ? lo : hi;
+      if (mode == 1)
+        tma_reduce_add(tm, 32 * (c & 1), row0, bi, stage + c * 16384);
+      else
+        tma_store(tm, 32 * (c & 1), row0, bi, stage + c * 16384);
+    }
+  } else {
+    tma_store(lo, 0, row0, bi, stage);
+    tma_store(hi, 0, row0, bi, stage + 16384);
   }
 }
 
@@ -299,7 +322,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       prefetch_tmap(&p.tm_d);
       mbar_expect_tx(BAR_KV, C::RES);
       tma_load(sRes, &p.tm_a, 0, k0, bx, BAR_KV);
-      tma_load(sRes + kAtom128, &p.tm_a, 64, k0, bx, BAR_KV);
+      tma_load(sRes + kAtom128, p.k_hi_x ? &p.tm_b : &p.tm_a, p.k_hi_x ? 0 : 64, k0, bx, BAR_KV);
       for (int a = 0; a < XA; ++a) tma_load(sRes + (2 + a) * kAtom128, &p.tm_b, 64 * a, k0, bx, BAR_KV);
     }
     for (int i = 0; i < nq; ++i) {
@@ -586,7 +609,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
     fence_proxy_async_smem();
     ok = named_bar_and(1, 128 * NWG, ok);
     if (warp == 2 && lane == 0 && ok && !*abort) {
-      issue_grad_tile(&p.tm_g0, fin ? sRes : stage0, k0, bx, fin ? 0 : p.acc);
+      if (!C::HAS_DV && p.k_hi_x)  // [dK | dV2] (never with acc 3)
+        issue_grad_tile_split(&p.tm_g0, &p.tm_g1, stage0, k0, bx, p.acc);
+      else
+        issue_grad_tile(&p.tm_g0, fin ? sRes : stage0, k0, bx, fin ? 0 : p.acc);
       if (C::HAS_DV) issue_grad_tile(&p.tm_g1, fin ? sRes + 32768 : stage1, k0, bx, fin ? 0 : p.acc);
       tma_store_commit_and_wait();
     }
@@ -718,11 +744,13 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dq128_kernel(const 
         const int s = j % NK;
         if (j >= NK && !mbar_wait(BAR(B_KEMPTY + s), ((j / NK) - 1) & 1, abort, &g_bwd_err, 16)) break;
         mbar_expect_tx(BAR(B_KFULL + s), C::KSLOT);
+        const CUtensorMap* khi = p.k_hi_x ? &p.tm_d : &p.tm_c;  // [K | V2] tiles (k_hi_x)
+        const int xhi = p.k_hi_x ? 0 : 64;
         tma_load(sK + s * C::KSLOT, &p.tm_c, 0, (kt0 + j) * 128, bx, BAR(B_KFULL + s));
-        tma_load(sK + s * C::KSLOT + kAtom128, &p.tm_c, 64, (kt0 + j) * 128, bx, BAR(B_KFULL + s));
+        tma_load(sK + s * C::KSLOT + kAtom128, khi, xhi, (kt0 + j) * 128, bx, BAR(B_KFULL + s));
         if (j + NK < nk) {  // the K tile NK loads ahead into L2
           tma_prefetch(&p.tm_c, 0, (kt0 + j + NK) * 128, bx);
-          tma_prefetch(&p.tm_c, 64, (kt0 + j + NK) * 128, bx);
+          tma_prefetch(khi, xhi, (kt0 + j + NK) * 128, bx);
         }
         if (p.acc == 3 && j == nk - 1)  // the accumulator tile the epilogue reads, into L2
           for (int c = 0; c < 4; ++c) tma_prefetch(&p.tm_f0, 32 * c, q0, bx);
@@ -1146,7 +1174,12 @@ cudaError_t run(Kern kern, int smem, int64_t blocks, int threads, const Sm100Bwd
 template <typename T>
 cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaStream_t st) {
   const bool bf16 = Elem<T>::is_bf16;
-  const int xa = vk ? (dv - 128) / 64 : dv / 64;  // value atoms beyond K (vk) or V atoms
+  // d = 64 with V aliasing K: the K tiles are [K | V2] (dv = 128, k_hi_x) or [K | 0] (dv = 64), so
+  // the kernels of V aliasing a 128-wide K run with no value atoms of their own
+  const bool vk64 = vk && b.d == 64;
+  const bool k_hi_x = vk64 && dv == 128;
+  if (k_hi_x && (b.acc_kv == 3 || b.acc_q == 3)) return cudaErrorNotSupported;  // no [dK | dV2] finalize
+  const int xa = vk ? (vk64 ? 0 : (dv - 128) / 64) : dv / 64;  // value atoms beyond K (vk) or V atoms
   const void* xsrc = vk ? b.v2 : b.v;
   const View xv = vk ? b.v2v : b.vv;
   const int n1 = b.n1, n2 = b.n2;
@@ -1161,9 +1194,12 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   if (!tma::make_map_view(&pa.tm_a, b.k, bf16, d, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
     if (!tma::make_map_view(&pa.tm_b, xsrc, bf16, 64 * xa, b.n_kv, batch, xv, n1, n2, 128)) return cudaErrorInvalidValue;
+  } else if (k_hi_x) {  // V2: the second atom of the resident K tile
+    if (!tma::make_map_view(&pa.tm_b, b.v2, bf16, 64, b.n_kv, batch, b.v2v, n1, n2, 128)) return cudaErrorInvalidValue;
   } else {
     pa.tm_b = pa.tm_a;
   }
+  pa.k_hi_x = k_hi_x ? 1 : 0;
   if (!tma::make_map_view(&pa.tm_c, b.q, bf16, d, b.n_q, batch, b.qv, n1, n2, qrows)) return cudaErrorInvalidValue;
   if (!tma::make_map_view(&pa.tm_d, b.dout, bf16, dv, b.n_q, batch, b.dov, n1, n2, qrows)) return cudaErrorInvalidValue;
   pa.nl = b.fold;
@@ -1180,6 +1216,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   if (!grad_map(&pa.tm_g0, b.dk, d, b.n_kv, b.dkv, f32_kv)) return cudaErrorInvalidValue;
   if (xa > 0 && !grad_map(&pa.tm_g1, vk ? b.dv2 : b.dv, xcols, b.n_kv, vk ? b.dv2v : b.dvv, f32_kv))
     return cudaErrorInvalidValue;
+  if (k_hi_x && !grad_map(&pa.tm_g1, b.dv2, 64, b.n_kv, b.dv2v, f32_kv)) return cudaErrorInvalidValue;
   if (b.acc_kv == 3) {
     if (!tma::make_map_view_f32(&pa.tm_f0, b.fin_k, d, b.n_kv, batch, b.finkv, n1, n2, 128))
       return cudaErrorInvalidValue;
@@ -1201,7 +1238,7 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   pa.sm_scale = b.sm_scale;
   cudaError_t e;
   const int64_t blocks_a = (int64_t)pa.n_tiles * batch;
-  if (fea_bwd_fuses_dq(b.n_kv, dv, vk, b.acc_q, b.deterministic)) {
+  if (fea_bwd_fuses_dq(b.n_kv, d, dv, vk, b.acc_q, b.deterministic)) {
     // dQ comes from the dK kernel as reductions into fp32: clear it first in the overwrite mode
     if (b.acc_q == 2) {
       e = cudaMemset2DAsync(b.dq, b.dq_bs * 4, 0, (size_t)b.n_q * 128 * 4, batch, st);
@@ -1246,9 +1283,12 @@ cudaError_t launch_all(const BwdParams& b, int64_t batch, int dv, bool vk, cudaS
   if (!tma::make_map_view(&pb.tm_c, b.k, bf16, d, b.n_kv, batch, b.kv, n1, n2, 128)) return cudaErrorInvalidValue;
   if (xa > 0) {
     if (!tma::make_map_view(&pb.tm_d, xsrc, bf16, 64 * xa, b.n_kv, batch, xv, n1, n2, 128)) return cudaErrorInvalidValue;
+  } else if (k_hi_x) {  // V2: the second atom of every K tile
+    if (!tma::make_map_view(&pb.tm_d, b.v2, bf16, 64, b.n_kv, batch, b.v2v, n1, n2, 128)) return cudaErrorInvalidValue;
   } else {
     pb.tm_d = pb.tm_c;
   }
+  pb.k_hi_x = k_hi_x ? 1 : 0;
   pb.dout = b.dout;
   pb.dov = b.dov;
   pb.nl = b.fold;
@@ -1328,10 +1368,11 @@ int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc) {
   return best;
 }
 
-bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic) {
-  // dQ from the dK kernel (no dq kernel) when V aliases K without V2 (free TMEM columns), dQ is
-  // fp32 (reductions) and each dQ element receives at most 32 of them (<= 32 key tiles)
-  return vk && dv == 128 && (acc_q == 1 || acc_q == 2) && !deterministic && (n_kv + 127) / 128 <= 32;
+bool fea_bwd_fuses_dq(int n_kv, int d, int dv, bool vk, int acc_q, bool deterministic) {
+  // dQ from the dK kernel (no dq kernel) when V aliases a 128-wide K without V2 (free TMEM columns;
+  // its reductions address dQ rows of 128), dQ is fp32 (reductions) and each dQ element receives at
+  // most 32 of them (<= 32 key tiles)
+  return vk && d == 128 && dv == 128 && (acc_q == 1 || acc_q == 2) && !deterministic && (n_kv + 127) / 128 <= 32;
 }
 
 bool fea_bwd_ds_gemm(int64_t batch, int n_q, int n_kv, int dv, bool vk, int acc_q) {
@@ -1357,9 +1398,9 @@ int64_t fea_bwd_ds_bytes(int64_t batch, int n_q, int n_kv) {
 }
 
 bool fea_bwd_sm100_supported(int d, int dv, int dv1, bool vk) {
-  // d = 64 with separate values, dv = 64 or 128: the 128-column kernels over 64-column maps of the
-  // 64-wide tensors (zero second atom)
-  if (d == 64) return !vk && (dv == 64 || dv == 128) && dv1 == dv;
+  // d = 64, dv = 64 or 128: the 128-column kernels over 64-column maps of the 64-wide tensors
+  // (zero second atom); with V aliasing K, V2 (dv = 128) is the K tiles' second atom
+  if (d == 64) return vk ? dv1 == 64 && (dv == 64 || dv == 128) : (dv == 64 || dv == 128) && dv1 == dv;
   if (d != 128) return false;
   if (vk) return dv1 == 128 && (dv == 128 || dv == 256);
   return dv == 128 && dv1 == 128;

@@ -42,7 +42,7 @@ cudaError_t fea_bwd_sm100(const BwdParams& p, int64_t batch, int dv, bool vk, bo
 // fp32 of workspace when the result is above 1.
 int fea_bwd_dq_split(int64_t batch, int n_q, int n_kv, bool acc);
 // True when the tcgen05 backward forms dQ inside the dK kernel (fp32 reductions, no dq kernel).
-bool fea_bwd_fuses_dq(int n_kv, int dv, bool vk, int acc_q, bool deterministic);
+bool fea_bwd_fuses_dq(int n_kv, int d, int dv, bool vk, int acc_q, bool deterministic);
 // True when the tcgen05 backward takes dQ from dS: the dK/dV kernel stores dS^T (16-bit) and a
 // GEMM forms dQ = dS K, instead of a dq kernel recomputing S and dP.
 bool fea_bwd_ds_gemm(int64_t batch, int n_q, int n_kv, int dv, bool vk, int acc_q);
