@@ -5,7 +5,7 @@ device memory) or foreign-language bindings (which can only pass the user's tens
 vmb_fea_bwd its scratch workspace; this entry point uses a fixed buffer inside the library instead.
 The test calls it through the C ABI on calls of different shapes in a row, so each call finds the
 previous one's leftover scratch, on three kernel routes: the tcgen05 backward (d = 128), the
-mma.sync backward at d = 64 (whose fp32 dQ accumulator in the scratch must be cleared on every
+mma.sync backward at d = 32 (whose fp32 dQ accumulator in the scratch must be cleared on every
 call) and the last VMonarch R step (V aliasing K with a second value tensor, dv = 256), whose dS^T
 buffer fits the built-in scratch at this size. Each result is checked against vmb_fea_bwd with an
 ordinary caller-provided workspace of the same route, within the tolerances of the
@@ -98,7 +98,7 @@ def _close(x, ref):
 def test_noalloc_backward_matches_workspace_backward():
     torch.cuda.set_device(0)
     cases = [Case(11, 6, 333, 128, 128),               # tcgen05 backward, separate V
-             Case(12, 4, 200, 64, 64),                 # mma.sync backward: dQ accumulator in the scratch
+             Case(12, 4, 200, 32, 32),                 # mma.sync backward: dQ accumulator in the scratch
              Case(13, 8, 1000, 128, 256, v_is_k=True)]  # last R step: dS^T in the scratch
     dst = cases[2]
     a = dst.args(dst.grads_like(0.0))
