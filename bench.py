@@ -80,6 +80,8 @@ def parse_args():
     ap.add_argument("--no-verify", action="store_true", help="skip the gather + single-GPU check after timing")
     ap.add_argument("--no-fea-forward", action="store_true", help="skip the fea32k forward timing (N = 1)")
     ap.add_argument("--fwd-only", action="store_true", help="impl triton: time the forward alone")
+    ap.add_argument("--fp8-r-step", action="store_true",
+                    help="VMonarch R steps on e4m3 operands (opt-in extension; the default line is bf16)")
     ap.add_argument("--cpu-budget-s", type=float, default=150.0, help="wall-clock cap of the CPU reference arm")
     return ap.parse_args()
 
@@ -154,11 +156,14 @@ def restrict_heads(w: Workload, heads: int) -> Workload:
     return replace(w, H=heads, name=f"{w.name}[{heads} heads]")
 
 
-def make_step(w: Workload, api):
-    """Returns step(q, k, v, do, de) -> (out, grads) running forward + backward through `api`."""
+def make_step(w: Workload, api, fp8: bool = False):
+    """Returns step(q, k, v, do, de) -> (out, grads) running forward + backward through `api`
+    (fp8: VMonarch with e4m3 R-step operands, an option of this package only)."""
     if w.kind == "vmonarch":
+        kw = {"fp8_r_step": True} if fp8 else {}
+
         def step(q, k, v, do, de):
-            z = api.vmonarch_attention(q, k, v, w.m, w.b, w.iters, recompute_tokens=w.recompute)
+            z = api.vmonarch_attention(q, k, v, w.m, w.b, w.iters, recompute_tokens=w.recompute, **kw)
             return z, torch.autograd.grad(z, (q, k, v), do)
     else:
         def step(q, k, v, do, de):
@@ -425,6 +430,8 @@ def base_line(args, w, n_gpus, ms, value, impl=None) -> dict:
                        "parallelism": (f"heads split over {n_gpus} GPUs ({per_rank} per GPU), no collective on the "
                                        "hot path" if strong else f"one full layer per GPU x{n_gpus}, no collective"),
                        "l2": l2_note(w), "cuda_graph": bool(args.graph)}}
+    if getattr(args, "fp8_r_step", False):
+        line["config"]["r_step_operands"] = "e4m3 (fp8_r_step)"
     if impl:
         line["impl"] = impl
     return line
@@ -522,7 +529,7 @@ def run_ours(args, info, device):
         de = de[..., :0]  # not an input of the VMonarch step: nothing to copy
     dev = [t.to(device, non_blocking=True) for t in (q, k, v, do, de)]
     dev = [t.requires_grad_() if i < 3 else t for i, t in enumerate(dev)]
-    step = make_step(w, api)
+    step = make_step(w, api, fp8=args.fp8_r_step)
     n_local = len(heads)
     flops_local = scaled_flops(w, n_local)
     flops_job = flops_local * (info.world if args.scaling == "weak" else 1)

@@ -26,7 +26,7 @@
 extern "C" {
 #endif
 
-#define VMB_ABI_VERSION 6
+#define VMB_ABI_VERSION 7
 
 #define VMB_DTYPE_BF16 0
 #define VMB_DTYPE_F16 1
@@ -119,6 +119,13 @@ typedef struct vmb_fea_fwd_args {
   void* workspace;  int64_t workspace_bytes;  /* optional, see above (ABI version 2) */
   const vmb_fea_layout* layout;  /* optional strided layout of q, k, v, v2, o (ABI version 6);
                                     NULL: dense with the *_bs batch strides */
+  int32_t qkv_e4m3;  /* ABI version 7. Nonzero: q, k, v and v2 hold e4m3 (fp8, one byte per
+                        element; see vmb_quant_e4m3) and both products run on the fp8 tensor cores,
+                        with P rounded to e4m3 as well; o, lse and ent are as usual (dtype gives o's
+                        type). Only the VMonarch R-step forms: d = 128, v aliasing k (v == k, dv1 = d),
+                        dv = 128 or dv = 256 with a 128-wide v2. Batch and layout strides are then
+                        multiples of 16 elements (bytes). No reference counterpart: an opt-in
+                        B200 extension of the R step (the reference computes it in bf16). */
 } vmb_fea_fwd_args;
 
 /* Workspace that lets vmb_fea_fwd split long key ranges (0 when it would not split). No
@@ -263,6 +270,14 @@ int vmb_lstep_bwd(const vmb_lstep_args* a, void* stream);
  * Converts the fp32 gradient accumulators of grad_mode 1 to the element dtype. */
 int vmb_cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, int64_t batch, int64_t n,
                  int32_t dtype, void* stream);
+
+/* dst(s, r, c) = e4m3(scale * src(s, r, c)) over [batch][rows][cols] views with batch split (n1, n2)
+ * (ABI version 7): the operands of an e4m3 forward (vmb_fea_fwd_args.qkv_e4m3) from 16-bit tensors
+ * of element type dtype. Rounded to nearest even, saturating at +-448 (the format's largest finite
+ * value); NaN stays NaN. cols a multiple of 16; src rows 16-byte aligned (view strides multiples of
+ * 8 elements), dst rows 16-byte aligned (multiples of 16). */
+int vmb_quant_e4m3(const void* src, const vmb_view* src_view, void* dst, const vmb_view* dst_view, int64_t n1,
+                   int64_t n2, int64_t batch, int64_t rows, int64_t cols, int32_t dtype, float scale, void* stream);
 
 /* dst(s, r, c) = (dtype) src(s, r, c) over [batch][rows][cols] views with batch split (n1, n2)
  * (ABI version 6): the fp32 accumulator of a strided (e.g. token-major) gradient converted into

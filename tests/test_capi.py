@@ -20,7 +20,7 @@ def declared_functions():
 
 def test_library_loads_and_reports_abi():
     assert N.LIB_PATH.exists()
-    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 6
+    assert N.lib.vmb_abi_version() == N.ABI_VERSION == 7
 
 
 def test_every_declared_symbol_is_exported_and_bound():

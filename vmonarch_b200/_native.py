@@ -25,7 +25,7 @@ c_vp = ctypes.c_void_p
 c_fp = ctypes.POINTER(ctypes.c_float)
 
 
-ABI_VERSION = 6  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
+ABI_VERSION = 7  # VMB_ABI_VERSION of include/vmonarch_b200.h that these structures mirror
 
 
 class View(ctypes.Structure):
@@ -56,6 +56,7 @@ class FeaFwdArgs(ctypes.Structure):
         ("sm_scale", ctypes.c_float),
         ("workspace", c_vp), ("workspace_bytes", c_i64),
         ("layout", ctypes.POINTER(FeaLayout)),
+        ("qkv_e4m3", c_i32),
     ]
 
 
@@ -121,6 +122,8 @@ SIGNATURES = {
     "vmb_cast_f32": (ctypes.c_int, [c_vp, c_i64, c_vp, c_i64, c_i64, c_i64, c_i32, c_vp]),
     "vmb_cast_f32_view": (ctypes.c_int, [c_vp, ctypes.POINTER(View), c_vp, ctypes.POINTER(View), c_i64, c_i64, c_i64,
                                          c_i64, c_i64, c_i32, c_vp]),
+    "vmb_quant_e4m3": (ctypes.c_int, [c_vp, ctypes.POINTER(View), c_vp, ctypes.POINTER(View), c_i64, c_i64, c_i64,
+                                      c_i64, c_i64, c_i32, ctypes.c_float, c_vp]),
 }
 
 

@@ -139,7 +139,7 @@ static bool fwd_v_is_k(const vmb_fea_fwd_args* a) {
 
 int64_t vmb_fea_fwd_workspace_bytes(const vmb_fea_fwd_args* a) {
   if (!a || a->batch < 0 || a->n_q < 0 || a->n_kv < 1) return -1;
-  if (a->batch == 0 || a->n_q == 0 || a->n_q > 0x7fffffff || a->n_kv > 0x7fffffff) return 0;
+  if (a->batch == 0 || a->n_q == 0 || a->n_q > 0x7fffffff || a->n_kv > 0x7fffffff || a->qkv_e4m3) return 0;
   return vmb::fea_fwd_sm100_workspace_bytes(a->batch, (int)a->n_q, (int)a->n_kv, a->d, a->dv, a->dv1,
                                             fwd_v_is_k(a));
 }
@@ -154,6 +154,16 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
     return fail(VMB_EINVAL, "vmb_fea_fwd: tensors must be 16-byte aligned");
   if ((a->q_bs | a->k_bs | a->v_bs | a->o_bs | a->v2_bs) & 7)
     return fail(VMB_EINVAL, "vmb_fea_fwd: batch strides must be multiples of 8 elements");
+  const bool e4m3 = a->qkv_e4m3 != 0;
+  if (e4m3) {
+    // fp8 operands: the VMonarch R-step forms only (one-byte elements, 16-byte aligned rows)
+    if (!fwd_v_is_k(a) || !vmb::fea_fwd_sm100_e4m3_supported(a->d, a->dv, a->dv1, true))
+      return fail(VMB_ENOTSUP,
+                  "vmb_fea_fwd: e4m3 operands need d = 128 with v aliasing k and dv = 128, or dv = 256 with a "
+                  "128-wide v2 (got d=%d dv=%d dv1=%d)", a->d, a->dv, a->dv1);
+    if ((a->q_bs | a->k_bs | a->v2_bs) & 15)
+      return fail(VMB_EINVAL, "vmb_fea_fwd: e4m3 batch strides must be multiples of 16 elements");
+  }
   if (a->workspace && (!aligned16(a->workspace) || a->workspace_bytes < 0))
     return fail(VMB_EINVAL, "vmb_fea_fwd: workspace must be 16-byte aligned");
   vmb::FwdParams p{};
@@ -171,6 +181,9 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   if (L && (!view_ok(p.qv, a->d, 8) || !view_ok(p.kv, a->d, 8) || !view_ok(p.vv, a->dv1, 8) ||
             (a->v2 && !view_ok(p.v2v, a->dv - a->dv1, 8)) || !view_ok(p.ov, a->dv, 8)))
     return fail(VMB_EINVAL, "vmb_fea_fwd: layout strides must be multiples of 8 elements with rows >= cols");
+  if (L && e4m3 && (!view_ok(p.qv, a->d, 16) || !view_ok(p.kv, a->d, 16) || (a->v2 && !view_ok(p.v2v, a->dv - a->dv1, 16))))
+    return fail(VMB_EINVAL, "vmb_fea_fwd: e4m3 layout strides must be multiples of 16 elements");
+  p.e4m3 = e4m3;
   p.n_q = (int)a->n_q; p.n_kv = (int)a->n_kv; p.dv1 = a->dv1;
   p.scale_log2 = a->sm_scale * kLog2eHost;
   p.wait_limit = g_test_wait_cycles.load(std::memory_order_relaxed);
@@ -184,6 +197,10 @@ int vmb_fea_fwd(const vmb_fea_fwd_args* a, void* stream) {
   // d = 64: V aliasing K runs as such only with a second value tensor ([K | V2], dv = 128); V = K
   // alone takes the separate-values kernel over the same pointer
   const bool vk = fwd_v_is_k(a) && (a->d != 64 || a->dv == 128);
+  if (e4m3) {
+    count(1);
+    return cuda_status(vmb::fea_fwd_sm100(p, a->batch, a->d, a->dv, a->ent != nullptr, bf16, true, st), "vmb_fea_fwd");
+  }
   if (vmb::fea_fwd_sm100_supported(a->d, a->dv, a->dv1, vk)) {
     // a split key range adds the merge kernel
     count(vmb::fea_fwd_sm100_split(a->batch, p.n_q, p.n_kv, a->d, a->dv, p.work, p.work_bytes) > 1 ? 2 : 1);
@@ -557,6 +574,23 @@ int vmb_cast_f32(const float* src, int64_t src_bs, void* dst, int64_t dst_bs, in
   count(1);
   return cuda_status(vmb::cast_f32(src, src_bs, dst, dst_bs, batch, n, dtype == VMB_DTYPE_BF16, static_cast<cudaStream_t>(stream)),
                      "vmb_cast_f32");
+}
+
+int vmb_quant_e4m3(const void* src, const vmb_view* src_view, void* dst, const vmb_view* dst_view, int64_t n1,
+                   int64_t n2, int64_t batch, int64_t rows, int64_t cols, int32_t dtype, float scale, void* stream) {
+  if (dtype != VMB_DTYPE_BF16 && dtype != VMB_DTYPE_F16) return fail(VMB_EINVAL, "vmb_quant_e4m3: unknown dtype");
+  if (!src_view || !dst_view || batch < 0 || rows < 0 || cols < 0 || cols % 16)
+    return fail(VMB_EINVAL, "vmb_quant_e4m3: bad sizes or views (cols a multiple of 16)");
+  int rc = check_split("vmb_quant_e4m3", n1, n2, batch);
+  if (rc) return rc;
+  if (batch == 0 || rows == 0 || cols == 0) return VMB_OK;
+  const vmb::View sv = to_view(*src_view), dv = to_view(*dst_view);
+  if (!src || !dst || !aligned16(src) || !aligned16(dst) || !view_ok(sv, cols, 8) || !view_ok(dv, cols, 16))
+    return fail(VMB_EINVAL, "vmb_quant_e4m3: bad pointer or view");
+  count(1);
+  return cuda_status(vmb::quant_e4m3(src, sv, dst, dv, (int)n1, (int)n2, batch, rows, cols, dtype == VMB_DTYPE_BF16,
+                                     scale, static_cast<cudaStream_t>(stream)),
+                     "vmb_quant_e4m3");
 }
 
 int vmb_cast_f32_view(const float* src, const vmb_view* src_view, void* dst, const vmb_view* dst_view, int64_t n1,

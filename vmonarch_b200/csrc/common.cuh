@@ -8,6 +8,7 @@
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
 #include <cuda_fp16.h>
+#include <cuda_fp8.h>
 #include <stdint.h>
 
 #if defined(__CUDA_ARCH__) && (__CUDA_ARCH__ < 1000)
@@ -21,6 +22,11 @@ constexpr float kLn2 = 0.6931471805599453f;
 
 // ---------------------------------------------------------------- element types
 template <typename T> struct Elem;
+
+// Two floats -> two e4m3 bytes (lo in the low byte), rounded to nearest, saturating at +-448.
+__device__ __forceinline__ uint32_t pack_e4m3x2(float lo, float hi) {
+  return (uint32_t)__nv_cvt_float2_to_fp8x2(make_float2(lo, hi), __NV_SATFINITE, __NV_E4M3);
+}
 template <> struct Elem<__nv_bfloat16> {
   static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);

@@ -62,16 +62,29 @@ struct Sm100FwdParams {
   float scale_log2;
 };
 
-template <int XA, bool VK, int NSLOT>
+template <int XA, bool VK, int NSLOT, bool F8 = false>
 struct FwdCfg {
   static constexpr int NV = VK ? 128 + 64 * XA : 64 * XA;  // N of the P V MMA = output columns
-  static constexpr int SLOT = (2 + XA) * kAtom;            // bytes per ring slot
-  static constexpr int PV_OFF = VK ? 0 : 2 * kAtom;         // start of the P V operand in a slot
-  static constexpr int Q_BYTES = 2 * kAtom;
+  // swizzle atoms per 128-row tile of q / k (D = 128) and of X (64 XA columns): a 128-byte atom row
+  // holds 64 16-bit or 128 e4m3 elements
+  static constexpr int KA = F8 ? 1 : 2;
+  static constexpr int XAT = F8 ? XA / 2 : XA;
+  static constexpr int SLOT = (KA + XAT) * kAtom;          // bytes per ring slot
+  static constexpr int PV_OFF = VK ? 0 : KA * kAtom;       // start of the P V operand in a slot
+  static constexpr int Q_BYTES = KA * kAtom;
   static constexpr int SMEM = 1024 + Q_BYTES + NSLOT * SLOT;
   static_assert(NV == 128 || NV == 256, "P V width must be 128 or 256");
+  static_assert(!F8 || (VK && XA % 2 == 0), "e4m3: V aliasing K, whole X atoms");
+  static_assert(NSLOT * SLOT >= NV * 256, "the epilogue stages the 16-bit O tile in the ring");
   static_assert(SMEM <= 232448, "shared memory budget");
 };
+
+// P of one 64-key segment into TMEM: 32 columns of 16-bit pairs, or 16 columns of e4m3 quads.
+template <bool F8>
+__device__ __forceinline__ void tmem_st_p(uint32_t taddr, const uint32_t* pk) {
+  if constexpr (F8) tmem_st16(taddr, pk);
+  else tmem_st32(taddr, pk);
+}
 
 // Three-input max (sm_100: one instruction).
 __device__ __forceinline__ float fmax3(float a, float b, float c) {
@@ -99,9 +112,11 @@ __device__ __forceinline__ float row_max_raw(const uint32_t (&sr)[N], int valid)
 // (one instruction per pair) into two chains each. Keys >= valid (MASK) get x - m = -1e30, so
 // p = 0 and p (x - m) = 0 exactly. MAXO (unmasked segments): also returns the segment's max of
 // s * scale (four chains of three-input maxima beside the exponentials), else -1e30.
-template <typename T, int N, bool ENT, bool MASK, bool MAXO = false>
-__device__ __forceinline__ float probs_row(const uint32_t (&sr)[N], uint32_t (&pk)[N / 2], float sc, float m,
-                                           int valid, float& l, float& h) {
+// F8: p packed as e4m3, four keys per 32-bit word (p <= 2^8 under the lazy rescale, inside the
+// format's range); l and h sum the unrounded p.
+template <typename T, int N, bool ENT, bool MASK, bool MAXO = false, bool F8 = false>
+__device__ __forceinline__ float probs_row(const uint32_t (&sr)[N], uint32_t (&pk)[F8 ? N / 4 : N / 2], float sc,
+                                           float m, int valid, float& l, float& h) {
   static_assert(!MASK || !MAXO, "masked segments take a separate max");
   float2 la[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
   float2 ha[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
@@ -118,7 +133,13 @@ __device__ __forceinline__ float probs_row(const uint32_t (&sr)[N], uint32_t (&p
     const float2 pp = make_float2(fast_exp2(d.x), fast_exp2(d.y));
     la[i & 1] = __fadd2_rn(la[i & 1], pp);
     if (ENT) ha[i & 1] = __ffma2_rn(pp, d, ha[i & 1]);
-    pk[i] = Elem<T>::pack(pp.x, pp.y);
+    if constexpr (F8) {
+      const uint32_t b2 = pack_e4m3x2(pp.x, pp.y);
+      if (i & 1) pk[i >> 1] |= b2 << 16;
+      else pk[i >> 1] = b2;
+    } else {
+      pk[i] = Elem<T>::pack(pp.x, pp.y);
+    }
   }
   l += (la[0].x + la[0].y) + (la[1].x + la[1].y);
   if (ENT) h += (ha[0].x + ha[0].y) + (ha[1].x + ha[1].y);
@@ -127,13 +148,19 @@ __device__ __forceinline__ float probs_row(const uint32_t (&sr)[N], uint32_t (&p
 
 
 
-template <typename T, int XA, bool VK, int NSLOT, bool ENT>
+template <typename T, int XA, bool VK, int NSLOT, bool ENT, bool F8 = false>
 __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
-  using C = FwdCfg<XA, VK, NSLOT>;
+  using C = FwdCfg<XA, VK, NSLOT, F8>;
   constexpr bool kBf16 = Elem<T>::is_bf16;
-  constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
-  constexpr uint32_t IDESC_S32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 keys
-  constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, C::NV, false, true);
+  // F8: q, k and X are e4m3 (kind::f8f6f4, K = 32 per MMA) and P is stored as e4m3; o stays T
+  constexpr uint32_t IDESC_S = F8 ? idesc_e4m3(128, 128, false, false) : idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_S32 =  // a last tile of <= 32 keys
+      F8 ? idesc_e4m3(128, 32, false, false) : idesc_f16(kBf16, 128, 32, false, false);
+  constexpr uint32_t IDESC_PV = F8 ? idesc_e4m3(128, C::NV, false, true) : idesc_f16(kBf16, 128, C::NV, false, true);
+  constexpr int SK = F8 ? 4 : 8;              // S MMAs over D = 128 (32 bytes of each row per step)
+  constexpr int PVS = F8 ? 4 : 8;             // P V MMAs over a 128-key tile
+  constexpr int PVB = 128 / PVS * 128;        // bytes of X rows per P V step
+  constexpr int PK = F8 ? 16 : 32;            // 32-bit words of P per 64-key segment
 
   extern __shared__ uint8_t smem_raw[];
   __shared__ __align__(8) uint64_t bars[8 + 3 * NSLOT];
@@ -194,26 +221,25 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       prefetch_tmap(&p.tm_q);
       prefetch_tmap(&p.tm_k);
       if (XA > 0) prefetch_tmap(&p.tm_x);
+      constexpr int AX = F8 ? 128 : 64;  // columns per atom
       mbar_expect_tx(BAR_Q, C::Q_BYTES);
-      tma_load(sQ, &p.tm_q, 0, q0, bx, BAR_Q);
-      tma_load(sQ + kAtom, &p.tm_q, 64, q0, bx, BAR_Q);
+      for (int a = 0; a < C::KA; ++a) tma_load(sQ + a * kAtom, &p.tm_q, AX * a, q0, bx, BAR_Q);
       int armed[NSLOT];
       for (int s = 0; s < NSLOT; ++s) armed[s] = 0;
       for (int j = 0; j < n_kt; ++j) {
         const int s = j % NSLOT;
         if (j >= NSLOT && !mbar_wait(BAR_EMPTY(s), ((j / NSLOT) - 1) & 1, abort, &g_fwd_err, 1, p.wait_limit)) break;
         const uint32_t slot = sRing + s * C::SLOT;
-        mbar_expect_tx(BAR_KFULL(s), 2 * kAtom);
-        tma_load(slot, &p.tm_k, 0, j * 128, bx, BAR_KFULL(s));
-        tma_load(slot + kAtom, &p.tm_k, 64, j * 128, bx, BAR_KFULL(s));
+        mbar_expect_tx(BAR_KFULL(s), C::KA * kAtom);
+        for (int a = 0; a < C::KA; ++a) tma_load(slot + a * kAtom, &p.tm_k, AX * a, j * 128, bx, BAR_KFULL(s));
         if (XA > 0) {
-          mbar_expect_tx(BAR_VFULL(s), XA * kAtom);
-          for (int a = 0; a < XA; ++a) tma_load(slot + (2 + a) * kAtom, &p.tm_x, 64 * a, j * 128, bx, BAR_VFULL(s));
+          mbar_expect_tx(BAR_VFULL(s), C::XAT * kAtom);
+          for (int a = 0; a < C::XAT; ++a)
+            tma_load(slot + (C::KA + a) * kAtom, &p.tm_x, AX * a, j * 128, bx, BAR_VFULL(s));
         }
         if (j + NSLOT < n_kt) {  // the tiles one ring ahead into L2
-          tma_prefetch(&p.tm_k, 0, (j + NSLOT) * 128, bx);
-          tma_prefetch(&p.tm_k, 64, (j + NSLOT) * 128, bx);
-          for (int a = 0; a < XA; ++a) tma_prefetch(&p.tm_x, 64 * a, (j + NSLOT) * 128, bx);
+          for (int a = 0; a < C::KA; ++a) tma_prefetch(&p.tm_k, AX * a, (j + NSLOT) * 128, bx);
+          for (int a = 0; a < C::XAT; ++a) tma_prefetch(&p.tm_x, AX * a, (j + NSLOT) * 128, bx);
         }
         armed[s] = j / NSLOT + 1;
       }
@@ -246,9 +272,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         // a last tile of <= 32 keys: N = 32 (the softmax masks the columns past n_kv by index)
         const uint32_t idesc = p.n_kv - j * 128 <= 32 ? IDESC_S32 : IDESC_S;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < SK; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
+          mmax_ss_if<F8>(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc,
+                         kk > 0);
         }
         mma_commit_if(leader, BAR_SFULL(j & 1));
       }
@@ -264,11 +291,12 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       {
         const uint32_t vb = sRing + s * C::SLOT + C::PV_OFF;
         const uint32_t a_tm = tmem + (uint32_t)((j & 1) * 128);
-        const int ksteps = p.n_kv - j * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
+        const int ksteps = p.n_kv - j * 128 <= 32 ? 32 * PVS / 128 : PVS;  // keys of the tile, 128 / PVS per step
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk)  // P of keys [64 h, 64 h + 64) sits in columns [64 h, 64 h + 32)
-          mma_ts_if(leader & (kk < ksteps ? 1u : 0u), tmem + 256, a_tm + (kk >> 2) * 64 + (kk & 3) * 8,
-                    smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        for (int kk = 0; kk < PVS; ++kk)  // P of keys [64 h, 64 h + 64) sits in the first PK columns from 64 h
+          mmax_ts_if<F8>(leader & (kk < ksteps ? 1u : 0u), tmem + 256,
+                         a_tm + (kk / (PVS / 2)) * 64 + (kk % (PVS / 2)) * 8,
+                         smem_desc_sw128(vb + kk * PVB, kAtom, 1024), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
         mma_commit_if(leader, BAR_EMPTY(s));
         mma_commit_if(leader, BAR_PVD(j & 1));
       }
@@ -319,7 +347,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         tmem_ld32(tS + wg * 64 + 32, sr + 32);
         tmem_wait_ld();
       }
-      uint32_t pk[32];
+      uint32_t pk[PK];
       float lt = 0.f, ht = 0.f;
       // A full tile after the first: the exponentials against the current reference with the
       // half's max beside them, P stored at once. One barrier tells both warpgroups whether any
@@ -331,8 +359,8 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       if (fast) {
         float mh = -1e30f;
         if (good) {
-          mh = probs_row<T, 64, ENT, false, true>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
-          tmem_st32(tS + wg * 64, pk);  // this warpgroup's own half of S (already loaded)
+          mh = probs_row<T, 64, ENT, false, true, F8>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+          tmem_st_p<F8>(tS + wg * 64, pk);  // this warpgroup's own half of S (already loaded)
         }
         redo = named_bar_or(1, 256, !good || mh > m_ref + kRescaleThreshold);
       }
@@ -379,10 +407,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         if (fresh) {
           lt = 0.f;
           ht = 0.f;
-          if (valid < 64) probs_row<T, 64, ENT, true>(sr, pk, p.scale_log2, m_ref, valid, lt, ht);
-          else probs_row<T, 64, ENT, false>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+          if (valid < 64) probs_row<T, 64, ENT, true, false, F8>(sr, pk, p.scale_log2, m_ref, valid, lt, ht);
+          else probs_row<T, 64, ENT, false, false, F8>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
         }
-        if (good) tmem_st32(tS + wg * 64, pk);
+        if (good) tmem_st_p<F8>(tS + wg * 64, pk);
       }
       l += lt;
       h += ht;
@@ -472,28 +500,40 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 // NS = 1 (V aliasing K, short sequences): one stream and one query tile, S [0,128) and O [128,256),
 // so two CTAs share an SM (96 KB of shared memory, 256 TMEM columns each) and one CTA's Q load and
 // epilogue overlap the other's key loop; S goes out in two halves (HS, below).
-template <bool VK, int NS = 2>
+template <bool VK, int NS = 2, bool F8 = false>
 struct Fwd2Cfg {
   static_assert(NS == 2 || (NS == 1 && VK), "one stream only with V aliasing K");
-  static constexpr int NK = NS == 1 ? 2 : (VK ? 5 : 3);  // K ring slots (V aliasing K: also the V operand)
+  static_assert(!F8 || NS == 1, "e4m3: the one-stream instance");
+  // a 128-row tile of q or k (D = 128) is two 128-byte swizzle atoms of 16-bit elements, one of e4m3
+  static constexpr int TILE = (F8 ? 1 : 2) * kAtom;
+  static constexpr int NK = NS == 1 ? (F8 ? 4 : 2) : (VK ? 5 : 3);  // K ring slots (V aliasing K: also the V operand)
   static constexpr int NVS = VK ? 0 : 2;                 // V ring slots
-  static constexpr int Q_BYTES = NS * 2 * kAtom;         // one 128-row query tile per stream
-  static constexpr int SMEM = 1024 + Q_BYTES + (NK + NVS) * 2 * kAtom;
+  static constexpr int Q_BYTES = NS * TILE;              // one 128-row query tile per stream
+  static constexpr int SMEM = 1024 + Q_BYTES + (NK + NVS) * TILE;
+  static_assert((NK + NVS) * TILE >= NS * 2 * kAtom, "the epilogue stages the 16-bit O tiles in the ring");
   static constexpr int THREADS = 64 + 128 * NS;
   static_assert(SMEM <= 232448 - 1024, "shared memory budget");
   static_assert(NS == 2 || 2 * (SMEM + 1024) <= 233472, "two CTAs per SM");
 };
 
-template <typename T, bool VK, bool ENT, int NS = 2>
+template <typename T, bool VK, bool ENT, int NS = 2, bool F8 = false>
 __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(const __grid_constant__ Sm100FwdParams p) {
-  using C = Fwd2Cfg<VK, NS>;
+  using C = Fwd2Cfg<VK, NS, F8>;
   constexpr uint32_t kTmemCols = NS == 2 ? 512 : 256;
   constexpr int NK = C::NK, NVS = C::NVS;
+  constexpr uint32_t TILE = C::TILE;
   constexpr bool kBf16 = Elem<T>::is_bf16;
-  constexpr uint32_t IDESC_S = idesc_f16(kBf16, 128, 128, false, false);
-  constexpr uint32_t IDESC_S32 = idesc_f16(kBf16, 128, 32, false, false);  // a last tile of <= 32 keys
-  constexpr uint32_t IDESC_S64 = idesc_f16(kBf16, 128, 64, false, false);  // one 64-key half of S
-  constexpr uint32_t IDESC_PV = idesc_f16(kBf16, 128, 128, false, true);
+  // F8: q and k are e4m3 (kind::f8f6f4, K = 32 per MMA) and P is stored as e4m3; o stays T
+  constexpr uint32_t IDESC_S = F8 ? idesc_e4m3(128, 128, false, false) : idesc_f16(kBf16, 128, 128, false, false);
+  constexpr uint32_t IDESC_S32 =  // a last tile of <= 32 keys
+      F8 ? idesc_e4m3(128, 32, false, false) : idesc_f16(kBf16, 128, 32, false, false);
+  constexpr uint32_t IDESC_S64 =  // one 64-key half of S
+      F8 ? idesc_e4m3(128, 64, false, false) : idesc_f16(kBf16, 128, 64, false, false);
+  constexpr uint32_t IDESC_PV = F8 ? idesc_e4m3(128, 128, false, true) : idesc_f16(kBf16, 128, 128, false, true);
+  constexpr int SK = F8 ? 4 : 8;        // S MMAs over D = 128 (32 bytes of each row per step)
+  constexpr int PVS = F8 ? 4 : 8;       // P V MMAs over a 128-key tile
+  constexpr int PVB = 128 / PVS * 128;  // bytes of V rows per P V step
+  constexpr int PK = F8 ? 16 : 32;      // 32-bit words of P per 64-key segment
   // HS (the one-stream instance): S in two 64-key halves, S_A = keys [0, 64) -> columns [0, 64) and
   // S_B = keys [64, 128) -> columns [64, 128), with P of each half over the first 32 columns of its
   // own half. S_A(j + NS) is issued right behind P V of the first half of tile j and S_B(j + NS)
@@ -521,7 +561,7 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
   const uint32_t sbase = (smem_u32(smem_raw) + 1023u) & ~1023u;
   const uint32_t sQ = sbase;
   const uint32_t sK = sbase + C::Q_BYTES;
-  const uint32_t sV = sK + NK * 2 * kAtom;
+  const uint32_t sV = sK + NK * TILE;
   const uint32_t bar0 = smem_u32(bars);
   const uint32_t BAR_Q = bar0;
   auto BAR_KFULL = [&](int s) { return bar0 + 8u * (1 + s); };
@@ -581,8 +621,8 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         prefetch_tmap(&p.tm_k);
         mbar_expect_tx(BAR_Q, C::Q_BYTES);
         for (int w = 0; w < NS; ++w) {
-          tma_load(sQ + w * 2 * kAtom, &p.tm_q, 0, q0 + 128 * w, bx, BAR_Q);
-          tma_load(sQ + w * 2 * kAtom + kAtom, &p.tm_q, 64, q0 + 128 * w, bx, BAR_Q);
+          tma_load(sQ + w * TILE, &p.tm_q, 0, q0 + 128 * w, bx, BAR_Q);
+          if (!F8) tma_load(sQ + w * TILE + kAtom, &p.tm_q, 64, q0 + 128 * w, bx, BAR_Q);
         }
       } else {
         prefetch_tmap(&p.tm_x);
@@ -594,15 +634,15 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         const uint32_t empty = kl ? BAR_KEMPTY(s) : BAR_VEMPTY(s);
         if (j >= nslot && !mbar_wait(empty, ((j / nslot) - 1) & 1, abort, &g_fwd_err, 1, p.wait_limit)) break;
         const uint32_t full = kl ? BAR_KFULL(s) : BAR_VFULL(s);
-        const uint32_t slot = (kl ? sK : sV) + s * 2 * kAtom;
-        mbar_expect_tx(full, 2 * kAtom);
+        const uint32_t slot = (kl ? sK : sV) + s * TILE;
+        mbar_expect_tx(full, TILE);
         const bool hx = kl && p.k_hi_x;  // second atom of the K tile from V2
         const CUtensorMap* hi = (kl && !hx) ? &p.tm_k : &p.tm_x;
         tma_load(slot, kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j) * 128, bx, full);
-        tma_load(slot + kAtom, hi, hx ? 0 : 64, (kt0 + j) * 128, bx, full);
+        if (!F8) tma_load(slot + kAtom, hi, hx ? 0 : 64, (kt0 + j) * 128, bx, full);
         if (j + nslot < n_kt) {  // the tile one ring ahead into L2
           tma_prefetch(kl ? &p.tm_k : &p.tm_x, 0, (kt0 + j + nslot) * 128, bx);
-          tma_prefetch(hi, hx ? 0 : 64, (kt0 + j + nslot) * 128, bx);
+          if (!F8) tma_prefetch(hi, hx ? 0 : 64, (kt0 + j + nslot) * 128, bx);
         }
         armed[s] = j / nslot + 1;
       }
@@ -624,14 +664,15 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       if (!wwait(BAR_KFULL(s), (t / NK) & 1, 2)) return false;
       tc_fence_after();
       {
-        const uint32_t kb = sK + s * 2 * kAtom, qb = sQ + w * 2 * kAtom;
+        const uint32_t kb = sK + s * TILE, qb = sQ + w * TILE;
         const uint32_t d = tmem + (uint32_t)(w * 128);
         // a last tile of <= 32 keys: N = 32 (the softmax masks the columns past n_kv by index)
         const uint32_t idesc = p.n_kv - (kt0 + t) * 128 <= 32 ? IDESC_S32 : IDESC_S;
 #pragma unroll
-        for (int kk = 0; kk < 8; ++kk) {
+        for (int kk = 0; kk < SK; ++kk) {
           const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-          mma_ss_if(leader, d, smem_desc_sw128(qb + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
+          mmax_ss_if<F8>(leader, d, smem_desc_sw128(qb + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc,
+                         kk > 0);
         }
         mma_commit_if(leader, BAR_SFULL(w));
       }
@@ -643,26 +684,28 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       const int s = j % NK;
       if (!wwait(BAR_KFULL(s), (j / NK) & 1, 2)) return false;
       tc_fence_after();
-      const uint32_t kb = sK + s * 2 * kAtom;
+      const uint32_t kb = sK + s * TILE;
       const uint32_t d = tmem + (uint32_t)((j % NS) * 128);
       const uint32_t idesc = p.n_kv - (kt0 + j) * 128 <= 32 ? IDESC_S32 : IDESC_S64;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
+      for (int kk = 0; kk < SK; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        mma_ss_if(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc, kk > 0);
+        mmax_ss_if<F8>(leader, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), idesc,
+                       kk > 0);
       }
       mma_commit_if(leader, BAR_SA(j % NS));
       return true;
     };
     auto issue_sb = [&](int j) {  // K(j) has landed (issue_sa)
       const int s = j % NK;
-      const uint32_t kb = sK + s * 2 * kAtom + 64 * 128;  // key rows [64, 128)
+      const uint32_t kb = sK + s * TILE + 64 * 128;  // key rows [64, 128)
       const uint32_t d = tmem + (uint32_t)((j % NS) * 128) + 64;
       const uint32_t on = p.n_kv - (kt0 + j) * 128 > 64 ? leader : 0u;
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
+      for (int kk = 0; kk < SK; ++kk) {
         const uint32_t off = (kk >> 2) * kAtom + (kk & 3) * 32;
-        mma_ss_if(on, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S64, kk > 0);
+        mmax_ss_if<F8>(on, d, smem_desc_sw128(sQ + off, 16, 1024), smem_desc_sw128(kb + off, 16, 1024), IDESC_S64,
+                       kk > 0);
       }
       mma_commit_if(leader, BAR_SFULL(j % NS));
       if (!VK) mma_commit_if(leader, BAR_KEMPTY(s));  // separate V: K(j) is read by S(j) only
@@ -678,25 +721,25 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
     // (BAR_PHALF), so it runs while the softmax computes the second half
     for (int j = 0; ok && j < n_steps; ++j) {
       const int w = j % NS, t = j / NS;
-      const uint32_t vb = VK ? sK + (t % NK) * 2 * kAtom : sV + (t % NVS) * 2 * kAtom;
+      const uint32_t vb = VK ? sK + (t % NK) * TILE : sV + (t % NVS) * TILE;
       const uint32_t a_tm = tmem + (uint32_t)(w * 128);
       const uint32_t o_tm = tmem + NS * 128 + (uint32_t)(w * 128);
-      const int ksteps = p.n_kv - (kt0 + t) * 128 <= 32 ? 2 : 8;  // keys of the tile, 16 per step
+      const int ksteps = p.n_kv - (kt0 + t) * 128 <= 32 ? 32 * PVS / 128 : PVS;  // keys of the tile, 128 / PVS per step
       if (!wwait(BAR_PHALF(w), t & 1, 4)) break;
       if (!VK && !wwait(BAR_VFULL(t % NVS), (t / NVS) & 1, 4)) break;
       tc_fence_after();
 #pragma unroll
-      for (int kk = 0; kk < 4; ++kk)
-        mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8, smem_desc_sw128(vb + kk * 2048, kAtom, 1024),
-                  IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
+      for (int kk = 0; kk < PVS / 2; ++kk)
+        mmax_ts_if<F8>(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + kk * 8,
+                       smem_desc_sw128(vb + kk * PVB, kAtom, 1024), IDESC_PV, (t > 0 || kk > 0) ? 1u : 0u);
       mma_commit_if(leader, BAR_PVH(w));  // a softmax that rescales O mid-tile waits for it
       if (HS && j + NS < n_steps && !(ok = issue_sa(j + NS))) break;
       if (!wwait(BAR_PFULL(w), t & 1, 4)) break;
       tc_fence_after();
 #pragma unroll
-      for (int kk = 4; kk < 8; ++kk)  // HS: P of keys [64, 128) sits in columns [64, 96)
-        mma_ts_if(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + (HS ? 64 + (kk - 4) * 8 : kk * 8),
-                  smem_desc_sw128(vb + kk * 2048, kAtom, 1024), IDESC_PV, 1u);
+      for (int kk = PVS / 2; kk < PVS; ++kk)  // HS: P of keys [64, 128) sits in the first PK columns from 64
+        mmax_ts_if<F8>(leader & (kk < ksteps ? 1u : 0u), o_tm, a_tm + (HS ? 64 + (kk - PVS / 2) * 8 : kk * 8),
+                       smem_desc_sw128(vb + kk * PVB, kAtom, 1024), IDESC_PV, 1u);
       if (HS) {
         mma_commit_if(leader, BAR_PVB(w));
         mma_commit_if(leader, VK ? BAR_KEMPTY(t % NK) : BAR_VEMPTY(t % NVS));  // the slot P V(j) read
@@ -771,9 +814,9 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           tmem_ld32(tS + 0, sa);
           tmem_ld32(tS + 32, sa + 32);
           tmem_wait_ld();
-          uint32_t pk[32];
+          uint32_t pk[PK];
           float lt = 0.f, ht = 0.f;
-          const float mx = probs_row<T, 64, ENT, false, true>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
+          const float mx = probs_row<T, 64, ENT, false, true, F8>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
           if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
             // every earlier P V into O_w has completed (S_w(t) complete; HS: S_A(t) only follows the
             // first half of P V(t - 1), so wait for the second); P V(t) is not issued yet
@@ -782,11 +825,11 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
             rescale(mx);
             lt = 0.f;
             ht = 0.f;
-            probs_row<T, 64, ENT, false>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
+            probs_row<T, 64, ENT, false, false, F8>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
           }
           l += lt;
           h += ht;
-          tmem_st32(tS + 0, pk);
+          tmem_st_p<F8>(tS + 0, pk);
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(BAR_PHALF(w));
@@ -800,9 +843,9 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           tmem_ld32(tS + 64, sb);
           tmem_ld32(tS + 96, sb + 32);
           tmem_wait_ld();
-          uint32_t pk[32];
+          uint32_t pk[PK];
           float lt = 0.f, ht = 0.f;
-          const float mx = probs_row<T, 64, ENT, false, true>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
+          const float mx = probs_row<T, 64, ENT, false, true, F8>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
           if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
             // the first half of P V(t) may still be adding into O_w: wait for its commit
             if (!warp_wait(BAR_PVH(w), t & 1, 16)) { ok = false; break; }
@@ -810,11 +853,11 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
             rescale(mx);
             lt = 0.f;
             ht = 0.f;
-            probs_row<T, 64, ENT, false>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
+            probs_row<T, 64, ENT, false, false, F8>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
           }
           l += lt;
           h += ht;
-          tmem_st32(tS + (HS ? 64 : 32), pk);
+          tmem_st_p<F8>(tS + (HS ? 64 : 32), pk);
         }
       } else {
         // the stream's first tile (sets the reference) and the ragged last tile: the tile max first
@@ -842,10 +885,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
         {  // the second half of S is loaded again from TMEM (its columns are only overwritten by the
            // second half of P), so the first half's scores are the only ones live through the exponentials
           const uint32_t(&sh)[64] = *reinterpret_cast<const uint32_t(*)[64]>(&sr[0]);
-          uint32_t pk[32];
-          if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid, l, h);
-          else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
-          tmem_st32(tS + 0, pk);
+          uint32_t pk[PK];
+          if (valid < 128) probs_row<T, 64, ENT, true, false, F8>(sh, pk, p.scale_log2, m_ref, valid, l, h);
+          else probs_row<T, 64, ENT, false, false, F8>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          tmem_st_p<F8>(tS + 0, pk);
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(BAR_PHALF(w));
@@ -855,10 +898,10 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           tmem_ld32(tS + 64, sh);
           tmem_ld32(tS + 96, sh + 32);
           tmem_wait_ld();
-          uint32_t pk[32];
-          if (valid < 128) probs_row<T, 64, ENT, true>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
-          else probs_row<T, 64, ENT, false>(sh, pk, p.scale_log2, m_ref, 64, l, h);
-          tmem_st32(tS + (HS ? 64 : 32), pk);
+          uint32_t pk[PK];
+          if (valid < 128) probs_row<T, 64, ENT, true, false, F8>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
+          else probs_row<T, 64, ENT, false, false, F8>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          tmem_st_p<F8>(tS + (HS ? 64 : 32), pk);
         }
       }
       tmem_wait_st();
@@ -1020,10 +1063,10 @@ int64_t split_bytes(int split, int64_t batch, int n_q) {
 }
 
 // ---------------------------------------------------------------------------------- host side
-template <typename T, int XA, bool VK, int NSLOT, bool ENT>
+template <typename T, int XA, bool VK, int NSLOT, bool ENT, bool F8 = false>
 cudaError_t launch(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
-  using C = FwdCfg<XA, VK, NSLOT>;
-  auto kern = fea_fwd_sm100_kernel<T, XA, VK, NSLOT, ENT>;
+  using C = FwdCfg<XA, VK, NSLOT, F8>;
+  auto kern = fea_fwd_sm100_kernel<T, XA, VK, NSLOT, ENT, F8>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)p.n_qtiles * batch;
@@ -1032,10 +1075,10 @@ cudaError_t launch(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
   return cudaGetLastError();
 }
 
-template <typename T, bool VK, bool ENT, int NS = 2>
+template <typename T, bool VK, bool ENT, int NS = 2, bool F8 = false>
 cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
-  using C = Fwd2Cfg<VK, NS>;
-  auto kern = fea_fwd2_sm100_kernel<T, VK, ENT, NS>;
+  using C = Fwd2Cfg<VK, NS, F8>;
+  auto kern = fea_fwd2_sm100_kernel<T, VK, ENT, NS, F8>;
   cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM);
   if (e != cudaSuccess) return e;
   const int64_t blocks = (int64_t)((p.n_qtiles + NS - 1) / NS) * p.kv_split * batch;  // NS query tiles per CTA
@@ -1050,7 +1093,13 @@ cudaError_t launch2(const Sm100FwdParams& p, int64_t batch, cudaStream_t st) {
 bool fwd_one_stream(int n_kv, int kv_split) { (void)n_kv; return kv_split == 1; }
 
 template <typename T, bool ENT>
-cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bool vk, cudaStream_t st) {
+cudaError_t dispatch(const Sm100FwdParams& p, int64_t batch, int dv, int dv1, bool vk, bool e4m3, cudaStream_t st) {
+  if (e4m3) {  // the R steps: V aliasing K, without (dv = 128) or with a second value tensor
+    if (!vk || p.kv_split != 1) return cudaErrorNotSupported;
+    if (dv == 128) return launch2<T, true, ENT, 1, true>(p, batch, st);
+    if (dv == 256 && dv1 == 128) return launch<T, 2, true, 4, ENT, true>(p, batch, st);
+    return cudaErrorNotSupported;
+  }
   if (vk) {
     if (dv == 128 && fwd_one_stream(p.n_kv, p.kv_split)) return launch2<T, true, ENT, 1>(p, batch, st);
     if (dv == 128) return launch2<T, true, ENT>(p, batch, st);
@@ -1075,6 +1124,11 @@ bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk) {
   return (dv == 128 || dv == 256) && dv1 == dv;
 }
 
+bool fea_fwd_sm100_e4m3_supported(int d, int dv, int dv1, bool vk) {
+  // e4m3 operands: the VMonarch R-step forms (D = 128, V aliasing K, with or without [K | V2])
+  return d == 128 && vk && (dv == 128 || (dv == 256 && dv1 == 128));
+}
+
 int64_t fea_fwd_sm100_workspace_bytes(int64_t batch, int n_q, int n_kv, int d, int dv, int dv1, bool vk) {
   if (d != 128 || !fea_fwd_sm100_supported(d, dv, dv1, vk) || dv != 128) return 0;  // only the two-stream kernel splits (d = 128)
   return split_bytes(fwd2_split(batch, n_q, n_kv), batch, n_q);
@@ -1091,14 +1145,26 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
   Sm100FwdParams p;
   const int dv1 = fp.dv1;
   const int n1 = fp.n1, n2 = fp.n2;
-  if (!tma::make_map_view(&p.tm_q, fp.q, bf16, d, fp.n_q, batch, fp.qv, n1, n2, 128)) return cudaErrorInvalidValue;
-  if (!tma::make_map_view(&p.tm_k, fp.k, bf16, d, fp.n_kv, batch, fp.kv, n1, n2, 128)) return cudaErrorInvalidValue;
-  if (vk) {
-    if (dv > dv1 && !tma::make_map_view(&p.tm_x, fp.v2, bf16, dv - dv1, fp.n_kv, batch, fp.v2v, n1, n2, 128))
+  if (fp.e4m3) {
+    // e4m3 operands: one 128-byte box per 128-column row segment; only the R-step forms
+    if (d != 128 || !vk || !fea_fwd_sm100_e4m3_supported(d, dv, dv1, vk)) return cudaErrorNotSupported;
+    if (!tma::make_map_view_e4m3(&p.tm_q, fp.q, d, fp.n_q, batch, fp.qv, n1, n2, 128) ||
+        !tma::make_map_view_e4m3(&p.tm_k, fp.k, d, fp.n_kv, batch, fp.kv, n1, n2, 128))
+      return cudaErrorInvalidValue;
+    if (dv > dv1 && !tma::make_map_view_e4m3(&p.tm_x, fp.v2, dv - dv1, fp.n_kv, batch, fp.v2v, n1, n2, 128))
       return cudaErrorInvalidValue;
     if (dv == dv1) p.tm_x = p.tm_k;
   } else {
-    if (!tma::make_map_view(&p.tm_x, fp.v, bf16, dv, fp.n_kv, batch, fp.vv, n1, n2, 128)) return cudaErrorInvalidValue;
+    if (!tma::make_map_view(&p.tm_q, fp.q, bf16, d, fp.n_q, batch, fp.qv, n1, n2, 128) ||
+        !tma::make_map_view(&p.tm_k, fp.k, bf16, d, fp.n_kv, batch, fp.kv, n1, n2, 128))
+      return cudaErrorInvalidValue;
+    if (vk) {
+      if (dv > dv1 && !tma::make_map_view(&p.tm_x, fp.v2, bf16, dv - dv1, fp.n_kv, batch, fp.v2v, n1, n2, 128))
+        return cudaErrorInvalidValue;
+      if (dv == dv1) p.tm_x = p.tm_k;
+    } else if (!tma::make_map_view(&p.tm_x, fp.v, bf16, dv, fp.n_kv, batch, fp.vv, n1, n2, 128)) {
+      return cudaErrorInvalidValue;
+    }
   }
   if (!tma::make_map_view(&p.tm_o, fp.o, bf16, dv, fp.n_q, batch, fp.ov, n1, n2, 128)) return cudaErrorInvalidValue;
   p.n1 = n1;
@@ -1114,7 +1180,7 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
   p.scale_log2 = fp.scale_log2;
   // key-range split (two-stream kernel, with a large enough workspace)
   const int nkt = (fp.n_kv + 127) / 128;
-  p.kv_split = fea_fwd_sm100_split(batch, fp.n_q, fp.n_kv, d, dv, fp.work, fp.work_bytes);
+  p.kv_split = fp.e4m3 ? 1 : fea_fwd_sm100_split(batch, fp.n_q, fp.n_kv, d, dv, fp.work, fp.work_bytes);
   p.kt_per = (nkt + p.kv_split - 1) / p.kv_split;
   p.n_seq = (int)batch;
   p.n_pad = (fp.n_q + 127) / 128 * 128;
@@ -1128,11 +1194,13 @@ cudaError_t fea_fwd_sm100(const FwdParams& fp, int64_t batch, int d, int dv, boo
       return cudaErrorInvalidValue;
   }
   cudaError_t e;
+  const bool f8 = fp.e4m3;
   if (bf16)
-    e = ent ? dispatch<__nv_bfloat16, true>(p, batch, dv, dv1, vk, st)
-            : dispatch<__nv_bfloat16, false>(p, batch, dv, dv1, vk, st);
+    e = ent ? dispatch<__nv_bfloat16, true>(p, batch, dv, dv1, vk, f8, st)
+            : dispatch<__nv_bfloat16, false>(p, batch, dv, dv1, vk, f8, st);
   else
-    e = ent ? dispatch<__half, true>(p, batch, dv, dv1, vk, st) : dispatch<__half, false>(p, batch, dv, dv1, vk, st);
+    e = ent ? dispatch<__half, true>(p, batch, dv, dv1, vk, f8, st)
+            : dispatch<__half, false>(p, batch, dv, dv1, vk, f8, st);
   if (e != cudaSuccess || p.kv_split == 1) return e;
   const int64_t rows = batch * fp.n_q;
   const int64_t blocks = (rows + 7) / 8;

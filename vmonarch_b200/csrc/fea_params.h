@@ -45,6 +45,7 @@ struct FwdParams {
   int64_t work_bytes;
   long long wait_limit;  // tcgen05 kernels' pipeline wait limit in cycles (0: the default ~2 s)
   int hold_loads;        // test of the timeout path: the tcgen05 producers issue no load
+  bool e4m3;             // q, k, v, v2 hold e4m3 bytes (dense, D = 128, V aliasing K); o stays 16-bit
 };
 
 struct BwdParams {

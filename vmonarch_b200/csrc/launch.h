@@ -32,6 +32,7 @@ struct LstepParams {
 
 cudaError_t fea_fwd_mma(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, cudaStream_t st);
 bool fea_fwd_sm100_supported(int d, int dv, int dv1, bool vk);
+bool fea_fwd_sm100_e4m3_supported(int d, int dv, int dv1, bool vk);
 cudaError_t fea_fwd_sm100(const FwdParams& p, int64_t batch, int d, int dv, bool ent, bool bf16, bool vk,
                           cudaStream_t st);
 cudaError_t fea_fwd_sm100_status(cudaStream_t st, int* out);
@@ -60,6 +61,9 @@ cudaError_t fea_bwd_mma(const BwdParams& p, int64_t batch, int d, int dv, bool v
 cudaError_t fea_bwd_pre(const void* o, View ov, const void* dout, View dov, int n1, int n2, const float* lse,
                         const float* ent, const float* dent, float* cc, float* gg, int64_t batch, int n_q, int dv,
                         float* fold, int64_t n_pad, float sm_scale, const float* delta, bool bf16, cudaStream_t st);
+// dst = e4m3(scale * src) over [batch][rows][cols] views (16-bit src); cols % 16 == 0.
+cudaError_t quant_e4m3(const void* src, const View& sv, void* dst, const View& dvw, int n1, int n2, int64_t batch,
+                       int64_t rows, int64_t cols, bool bf16, float scale, cudaStream_t st);
 // dst = (16-bit) src over [batch][rows][cols] views with batch split (n1, n2); cols % 4 == 0.
 cudaError_t cast_f32_view(const float* src, const View& sv, void* dst, const View& dvw, int n1, int n2, int64_t batch,
                           int64_t rows, int64_t cols, bool bf16, cudaStream_t st);

@@ -202,4 +202,63 @@ cudaError_t cast_f32_view(const float* src, const View& sv, void* dst, const Vie
   return cudaGetLastError();
 }
 
+// e4m3 operands of the fp8 R step: dst(s, r, c) = e4m3(scale * src(s, r, c)), rounded to nearest,
+// saturating. Same walk as cast_f32_view: one warp per four rows, lane = 8 columns (one 16-byte load,
+// one 8-byte store), view offsets once per batch entry.
+template <typename T>
+__global__ void __launch_bounds__(256) quant_e4m3_kernel(const T* src, View sv, uint8_t* dst, View dvw, int n1, int n2,
+                                                         int64_t batch, int64_t rows, int c8n, float scale) {
+  const int warps = blockDim.x >> 5, lane = threadIdx.x & 31;
+  for (int64_t bi = blockIdx.y; bi < batch; bi += gridDim.y) {
+    const T* s0 = src + view_offset(sv, n1, n2, bi, 0);
+    uint8_t* d0 = dst + view_offset(dvw, n1, n2, bi, 0);
+    for (int64_t r0 = ((int64_t)blockIdx.x * warps + (threadIdx.x >> 5)) * 4; r0 < rows;
+         r0 += (int64_t)gridDim.x * warps * 4) {
+      const int nr = rows - r0 < 4 ? (int)(rows - r0) : 4;
+      for (int c = lane; c < c8n; c += 32) {
+        uint4 v[4];
+#pragma unroll
+        for (int u = 0; u < 4; ++u)
+          if (u < nr) v[u] = *reinterpret_cast<const uint4*>(s0 + (r0 + u) * sv.rs + 8 * c);
+#pragma unroll
+        for (int u = 0; u < 4; ++u) {
+          if (u < nr) {
+            const uint32_t w4[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+            uint32_t q[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+              const float2 a = Elem<T>::unpack(w4[2 * h]), b = Elem<T>::unpack(w4[2 * h + 1]);
+              q[h] = pack_e4m3x2(a.x * scale, a.y * scale) | (pack_e4m3x2(b.x * scale, b.y * scale) << 16);
+            }
+            *reinterpret_cast<uint2*>(d0 + (r0 + u) * dvw.rs + 8 * c) = make_uint2(q[0], q[1]);
+          }
+        }
+      }
+    }
+  }
+}
+
+cudaError_t quant_e4m3(const void* src, const View& sv, void* dst, const View& dvw, int n1, int n2, int64_t batch,
+                       int64_t rows, int64_t cols, bool bf16, float scale, cudaStream_t st) {
+  if (batch == 0 || rows == 0 || cols == 0) return cudaSuccess;
+  int dev = 0, sms = 148;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  const int64_t gy = batch < 65535 ? batch : 65535;
+  int64_t gx = ((int64_t)sms * 8 + gy - 1) / gy;
+  const int64_t need = (rows + 31) / 32;  // 8 warps x 4 rows per block and pass
+  if (gx > need) gx = need;
+  if (gx < 1) gx = 1;
+  const dim3 grid((unsigned)gx, (unsigned)gy);
+  const int c8n = (int)(cols / 8);
+  uint8_t* d = static_cast<uint8_t*>(dst);
+  if (bf16)
+    quant_e4m3_kernel<__nv_bfloat16><<<grid, 256, 0, st>>>(static_cast<const __nv_bfloat16*>(src), sv, d, dvw, n1, n2,
+                                                           batch, rows, c8n, scale);
+  else
+    quant_e4m3_kernel<__half><<<grid, 256, 0, st>>>(static_cast<const __half*>(src), sv, d, dvw, n1, n2, batch, rows,
+                                                    c8n, scale);
+  return cudaGetLastError();
+}
+
 }  // namespace vmb

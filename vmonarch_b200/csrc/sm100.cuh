@@ -184,6 +184,36 @@ __device__ __forceinline__ void mma_ts_if(uint32_t issue, uint32_t d_tmem, uint3
       "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
       : "memory");
 }
+// The same predicated forms for kind::f8f6f4 (e4m3 A and B, K = 32 per instruction).
+__device__ __forceinline__ void mma8_ss_if(uint32_t issue, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %5, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
+      : "memory");
+}
+__device__ __forceinline__ void mma8_ts_if(uint32_t issue, uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p, e;\n\tsetp.ne.b32 p, %4, 0;\n\tsetp.ne.b32 e, %5, 0;\n\t"
+      "@e tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], [%1], %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate), "r"(issue)
+      : "memory");
+}
+// Element-type dispatch: F8 selects kind::f8f6f4, else kind::f16.
+template <bool F8>
+__device__ __forceinline__ void mmax_ss_if(uint32_t issue, uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  if (F8) mma8_ss_if(issue, d_tmem, a_desc, b_desc, idesc, accumulate);
+  else mma_ss_if(issue, d_tmem, a_desc, b_desc, idesc, accumulate);
+}
+template <bool F8>
+__device__ __forceinline__ void mmax_ts_if(uint32_t issue, uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
+                                           uint32_t idesc, uint32_t accumulate) {
+  if (F8) mma8_ts_if(issue, d_tmem, a_tmem, b_desc, idesc, accumulate);
+  else mma_ts_if(issue, d_tmem, a_tmem, b_desc, idesc, accumulate);
+}
 __device__ __forceinline__ void mma_commit_if(uint32_t issue, uint32_t bar) {
   asm volatile(
       "{\n\t.reg .pred e;\n\tsetp.ne.b32 e, %1, 0;\n\t"
@@ -263,6 +293,13 @@ __host__ __device__ constexpr uint32_t idesc_f16(bool bf16, int M, int N, bool a
          | ((bf16 ? 1u : 0u) << 7) | ((bf16 ? 1u : 0u) << 10)  // A, B = bf16 or f16
          | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16)
          | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// Instruction descriptor of tcgen05.mma kind::f8f6f4 with e4m3 A and B (format code 0) and fp32
+// accumulation; the other fields as in idesc_f16 (MN-major operands are valid for e4m3).
+__host__ __device__ constexpr uint32_t idesc_e4m3(int M, int N, bool a_mn, bool b_mn) {
+  return (1u << 4) | ((a_mn ? 1u : 0u) << 15) | ((b_mn ? 1u : 0u) << 16) | ((uint32_t)(N >> 3) << 17) |
+         ((uint32_t)(M >> 4) << 24);
 }
 
 // One lane of a fully converged warp (elect.sync over all 32 lanes; every lane must execute it).

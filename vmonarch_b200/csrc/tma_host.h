@@ -66,6 +66,12 @@ inline bool make_map_view(CUtensorMap* m, const void* base, bool bf16, int64_t c
                    batch, v, n1, n2, 64, box_rows);
 }
 
+// e4m3 (one-byte) elements, boxes of 128 columns.
+inline bool make_map_view_e4m3(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int64_t batch,
+                               const View& v, int n1, int n2, int box_rows) {
+  return make_map5(m, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, base, cols, rows, batch, v, n1, n2, 128, box_rows);
+}
+
 // fp32 elements, boxes of 32 columns.
 inline bool make_map_view_f32(CUtensorMap* m, const void* base, int64_t cols, int64_t rows, int64_t batch,
                               const View& v, int n1, int n2, int box_rows) {

@@ -91,7 +91,8 @@ def _stats(t, batch: int, rows: int):
 
 # ----------------------------------------------------------------------------------------- forward
 def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
-    """o = softmax(sm_scale q k^T) [v | v2] per batch entry; lse/ent per query row (see header)."""
+    """o = softmax(sm_scale q k^T) [v | v2] per batch entry; lse/ent per query row (see header).
+    q, k, v (and v2) may be float8_e4m3fn (from quant_e4m3) for the R-step forms, o 16-bit."""
     bshape = q.shape[:-2]
     nb = len(bshape)
     for t in (k, v, o, v2):
@@ -111,7 +112,11 @@ def fea_fwd(q, k, v, o, lse, ent, sm_scale: float, v2=None) -> None:
     a.ent = _stats(ent, batch, q.size(-2))
     a.batch, a.n_q, a.n_kv = batch, q.size(-2), k.size(-2)
     a.d, a.dv, a.dv1 = q.size(-1), o.size(-1), v.size(-1)
-    a.dtype = N.dtype_code(q.dtype)
+    a.dtype = N.dtype_code(o.dtype)
+    e4m3 = q.dtype == torch.float8_e4m3fn
+    if any((t.dtype == torch.float8_e4m3fn) != e4m3 for t in (k, v, v2) if t is not None):
+        raise AssertionError("q, k, v and v2 must all be 16-bit or all e4m3")
+    a.qkv_e4m3 = int(e4m3)
     a.sm_scale = float(sm_scale)
     nbytes = N.lib.vmb_fea_fwd_workspace_bytes(ctypes.byref(a))
     ws = None
@@ -302,6 +307,24 @@ def lstep_bwd(q, out, ent, m: int, b: int, scale: float, min_col_mass: float, dq
                          dict(du=du, dz=dz, dq=dq, dout=dout, delta_out=delta_out))
     a.dq_store = int(dq_store)
     _call("vmb_lstep_bwd", N.lib.vmb_lstep_bwd, a, q.device)
+
+
+def quant_e4m3(src: torch.Tensor, scale: float = 1.0) -> torch.Tensor:
+    """e4m3(scale * src) as a new dense float8_e4m3fn tensor of src's shape; src 16-bit, (*batch,
+    rows, cols) with cols a multiple of 16, any strides the kernels can read in place (dense or
+    token-major). Rounded to nearest, saturating at +-448."""
+    bshape = src.shape[:-2]
+    nb = len(bshape)
+    dst = torch.empty(src.shape, dtype=torch.float8_e4m3fn, device=src.device)
+    if src.numel() == 0:
+        return dst
+    src = src if viewable(src) else src.contiguous()
+    n1, n2 = _split(bshape)
+    sv, dv = _view(src, nb), _view(dst, nb)
+    N.check(N.lib.vmb_quant_e4m3(src.data_ptr(), ctypes.byref(sv), dst.data_ptr(), ctypes.byref(dv), n1, n2,
+                                 math.prod(bshape), src.size(-2), src.size(-1), N.dtype_code(src.dtype), float(scale),
+                                 N.stream_ptr(src.device)), "vmb_quant_e4m3")
+    return dst
 
 
 def cast_f32(src: torch.Tensor, dst: torch.Tensor) -> None:

@@ -20,6 +20,10 @@ Execution per iteration (all on the C ABI, no torch math on the hot path):
           rescale of vmonarch.py:51-63.
 Recompute: the first `recompute_tokens` queries run exact attention (vmb_fea_fwd without entropy)
           written straight into rows [0, r) of z, replacing SDPA + torch.cat (vmonarch.py:66-68).
+FP8 R step (opt-in, `fp8_r_step=True`; no reference counterpart): q, k, v and each iteration's u
+          are rounded to e4m3 (vmb_quant_e4m3, saturating at +-448) and the R steps' two products run
+          on the fp8 tensor cores with P in e4m3 too; the L steps, the recompute and the whole
+          backward stay 16-bit (the backward differentiates the 16-bit R step at the same inputs).
 The backward is hand-derived (the reference relies on autograd through the same ops) and
 accumulates dq / dk / dv in fp32 across the recompute and every R and L step.
 """
@@ -58,7 +62,7 @@ class _VMonarchAttention(torch.autograd.Function):
     queries u and the fp32 gradient accumulators are dense internal buffers."""
 
     @staticmethod
-    def forward(ctx, q, k, v, num_blocks, block_size, num_iters, recompute_tokens, min_col_mass):
+    def forward(ctx, q, k, v, num_blocks, block_size, num_iters, recompute_tokens, min_col_mass, fp8_r_step=False):
         B, H, N, D = q.shape
         Dv = v.shape[-1]
         m, b = num_blocks, block_size
@@ -72,6 +76,8 @@ class _VMonarchAttention(torch.autograd.Function):
         steps = []
         u = qs
         z = None
+        if fp8_r_step:  # e4m3 operands of the R steps (dense copies; u is rounded per iteration)
+            k8, v8 = ops.quant_e4m3(ks), ops.quant_e4m3(vs)
         for it in range(num_iters):
             last = it == num_iters - 1
             Dw = D + Dv if last else D
@@ -79,7 +85,11 @@ class _VMonarchAttention(torch.autograd.Function):
             lse = torch.empty((B, H, N), device=dev, dtype=torch.float32)
             ent = torch.empty((B, H, N), device=dev, dtype=torch.float32)
             sm = scale if it == 0 else 1.0
-            ops.fea_fwd(grid(u), grid(ks), grid(ks), grid(out), lse, ent, sm, v2=grid(vs) if last else None)
+            if fp8_r_step:
+                ops.fea_fwd(grid(ops.quant_e4m3(u)), grid(k8), grid(k8), grid(out), lse, ent, sm,
+                            v2=grid(v8) if last else None)
+            else:
+                ops.fea_fwd(grid(u), grid(ks), grid(ks), grid(out), lse, ent, sm, v2=grid(vs) if last else None)
             if last:
                 z = _alloc_like_layout(qs, Dv, dt)
                 # every token of z is produced here (the tensor-core L step writes whole stacked
@@ -176,10 +186,11 @@ class _VMonarchAttention(torch.autograd.Function):
             ops.cast_f32(dq_acc, dq)
             ops.cast_f32(dk_acc, dk)
             ops.cast_f32(dv_acc, dv)
-        return dq, dk, dv, None, None, None, None, None
+        return dq, dk, dv, None, None, None, None, None, None
 
 
-def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_tokens=0, min_col_mass=0.01):
+def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_tokens=0, min_col_mass=0.01,
+                       fp8_r_step=False):
     """
     Args:
         q, k: (B, H, N, D); v: (B, H, N, Dv), with N == num_blocks * block_size.
@@ -188,6 +199,7 @@ def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_t
         num_iters: alternating-minimization steps.
         recompute_tokens: the first `recompute_tokens` queries use exact attention.
         min_col_mass: lower bound of the column mass of L, for stability.
+        fp8_r_step: (B200 extension, default off) R-step attention on e4m3 operands; D = Dv = 128.
     Returns:
         (B, H, N, Dv)
     """
@@ -207,21 +219,24 @@ def vmonarch_attention(q, k, v, num_blocks, block_size, num_iters=2, recompute_t
     if num_blocks > max_m:
         raise NotImplementedError(f"num_blocks={num_blocks} > {max_m}: the L step supports at most {max_m} grid rows "
                                   f"for D={D}, Dv={Dv}")
+    if fp8_r_step and (D != 128 or Dv != 128):
+        raise NotImplementedError(f"fp8_r_step needs D = Dv = 128 (got D={D}, Dv={Dv})")
     return _VMonarchAttention.apply(q, k, v, int(num_blocks), int(block_size), int(num_iters), recompute_tokens,
-                                    float(min_col_mass))
+                                    float(min_col_mass), bool(fp8_r_step))
 
 
 class VMonarchAttention(nn.Module):
-    def __init__(self, num_blocks, block_size, num_iters=2, min_col_mass=0.01):
+    def __init__(self, num_blocks, block_size, num_iters=2, min_col_mass=0.01, fp8_r_step=False):
         super().__init__()
         self.num_blocks = num_blocks
         self.block_size = block_size
         self.num_iters = num_iters
         self.min_col_mass = min_col_mass
+        self.fp8_r_step = fp8_r_step
 
     def forward(self, q, k, v, recompute_tokens=0):
         return vmonarch_attention(q, k, v, self.num_blocks, self.block_size, self.num_iters,
-                                  recompute_tokens, self.min_col_mass)
+                                  recompute_tokens, self.min_col_mass, self.fp8_r_step)
 
     def extra_repr(self):
         return f"num_blocks={self.num_blocks}, block_size={self.block_size}, num_iters={self.num_iters}"
