@@ -20,8 +20,8 @@
   README shape, config 2 and on four heads of the dit14b layer the north-star bounds of the 16-bit
   path hold (z max-abs 2e-2 / mean-abs 2e-3, max-rel 3e-2; gradients 5e-2); on the small ragged
   grids below the e4m3 rounding of P (steps of 6 %) averages over few keys (one iteration, or
-  ~100 keys per grid row) and z is held to mean-abs 4e-3 (the CPU emulation gives max-rel up to
-  0.08 there).
+  ~100 keys per grid row) and z is held to mean-abs 4e-3 and to 1.5 x the emulation's own
+  mean-abs error + 5e-4 (the CPU emulation gives max-rel up to 0.08 there).
 """
 import pytest
 import torch
@@ -166,8 +166,9 @@ def test_vmonarch_fp8_r_step(B, H, m, b, iters, r, token_major, north_star):
         assert (g - g_r).abs().max() <= 5e-2 and max_rel_err(g, g_r) <= 0.1
     if north_star:
         check_vm(got, exact)
-    else:
-        assert (z - exact[0]).abs().mean() <= 4e-3
+    else:  # no further from the exact oracle than the e4m3 arithmetic itself is
+        own = (z8 - exact[0]).abs().mean().item()
+        assert (z - exact[0]).abs().mean() <= min(4e-3, 1.5 * own + 5e-4), own
 
 
 def test_vmonarch_fp8_dit14b_four_heads():

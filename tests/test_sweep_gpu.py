@@ -102,3 +102,39 @@ def test_vmonarch_sweep(case):
     z_r = oracle.vmonarch_attention(*ref_leaves, m, b, c["iters"], recompute_tokens=c["r"])
     g_r = torch.autograd.grad((z_r * dz).sum(), ref_leaves)
     check_vm(got, [z_r.detach(), *(g.detach() for g in g_r)])
+
+
+def fp8_draw(seed):
+    r = random.Random(20_000 + seed)
+    m = r.randint(2, 40)
+    b = r.choice([64, 100, 128, 129, 200, 256, 300])
+    N = m * b
+    return dict(B=r.choice([1, 2]), H=r.choice([1, 2]), m=m, b=b, iters=r.choice([1, 2, 3]),
+                r=r.choice([0, b, r.randint(1, N)]), token_major=r.random() < 0.3)
+
+
+FP8_CASES = [fp8_draw(s) for s in range(12)]
+
+
+@pytest.mark.parametrize("case", FP8_CASES, ids=[f"s{i}-" + "-".join(f"{k}{v}" for k, v in c.items())
+                                                 for i, c in enumerate(FP8_CASES)])
+def test_vmonarch_fp8_sweep(case):
+    """The opt-in e4m3 R step on seeded grids (D = 128, bf16): z against the oracle whose R step
+    emulates the e4m3 kernels, and against the exact oracle no further than that emulation is
+    (its mean-abs error x 1.5 + 5e-4); gradients against the exact oracle (bounds of test_fp8_gpu)."""
+    from test_fp8_gpu import e4m3_oracle_z, run_cuda_fp8
+    from test_vmonarch_gpu import run_oracle
+    c = case
+    B, H, m, b = c["B"], c["H"], c["m"], c["b"]
+    gen = torch.Generator().manual_seed(3000 + m * b)
+    q, k, v = (torch.randn(B, H, m * b, 128, generator=gen).bfloat16().float() for _ in range(3))
+    dz = torch.randn(B, H, m * b, 128, generator=gen)
+    got = run_cuda_fp8(q, k, v, dz, m, b, c["iters"], c["r"], c["token_major"])
+    exact = run_oracle(q, k, v, dz, m, b, c["iters"], c["r"])
+    z8 = e4m3_oracle_z(q, k, v, m, b, c["iters"], c["r"])
+    err = (got[0] - z8).abs()
+    assert err.max() <= 2e-2 and err.mean() <= 2e-3, (err.max().item(), err.mean().item())
+    own = (z8 - exact[0]).abs().mean().item()  # the e4m3 arithmetic's own error at this shape
+    assert (got[0] - exact[0]).abs().mean() <= 1.5 * own + 5e-4, own
+    for g, g_r in zip(got[1:], exact[1:]):
+        assert (g - g_r).abs().max() <= 5e-2
