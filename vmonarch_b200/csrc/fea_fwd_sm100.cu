@@ -21,6 +21,10 @@
 //                  N = 128 + 64*XA operand, so the non-last R steps load K only vmonarch.py:50)
 // Tails: TMA zero-fills rows past n_q / n_kv per sequence (3-D maps [batch][rows][cols]); keys
 // past n_kv are masked to p = 0; the O tile is written with a TMA store, which clips rows >= n_q.
+// e4m3 instances (template flag F8, the opt-in FP8 R step): q, k and X arrive as e4m3 (one 128-byte
+// swizzle atom per 128 columns, so a D = 128 tile is one atom), both products are
+// tcgen05.mma.kind::f8f6f4 (K = 32 per instruction) and P is packed to e4m3 in TMEM, four keys per
+// column; the statistics use the unrounded p and O is written in the 16-bit type as usual.
 //
 // Every mbarrier wait is bounded (sm100.cuh); a CTA that gives up records an error code in
 // g_fwd_err (read by vmb_device_status) and drains its in-flight copies and MMAs before freeing
