@@ -243,7 +243,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   auto pcol = [](int kk) -> uint32_t { return NWG == 4 ? 32 * (kk >> 1) + 8 * (kk & 1) : 8 * kk; };
 
   extern __shared__ uint8_t smem_raw[];
-  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5 + 2 + 1];
+  __shared__ __align__(8) uint64_t bars[1 + 2 * NQS + 5 + 2 + 1 + 2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ int abort_sh;
 
@@ -275,6 +275,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
   // fused dQ: stream b has drained dQ^T of its previous tile and staged dS^T of the current one
   auto BAR_DQFREE = [&](int b) { return bar0 + 8u * (6 + 2 * NQS + b); };
   const uint32_t BAR_FIN = bar0 + 8u * (8 + 2 * NQS);  // acc 3: the fp32 accumulator tiles landed
+  // fused dQ: dQ^T of stream b's latest tile complete (commit behind it). S^T / dP^T of tile i + 2
+  // is issued before dQ^T(i), so its completion no longer implies dQ^T(i)'s: the stream waits here
+  // before overwriting its dS^T staging and before draining dQ^T(i)
+  auto BAR_DQDONE = [&](int b) { return bar0 + 8u * (9 + 2 * NQS + b); };
   volatile int* abort = &abort_sh;
   // Query slot: 64-query tiles of Q (2 atoms of 64 columns) and dO (DW / 64 atoms). With V aliasing
   // K the first two dO atoms interleave with Q's (Q0 dO0 Q1 dO1 [dO2 dO3]), so that Q atom a and
@@ -298,6 +302,7 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       mbar_init(BAR_SPFULL(b), 1);
       mbar_init(BAR_PDSFULL(b), 64 * NWG);
       if (FQ) mbar_init(BAR_DQFREE(b), 64 * NWG);
+      if (FQ) mbar_init(BAR_DQDONE(b), 1);
     }
     mbar_init(BAR_DONE, 1);
     mbar_init(BAR_FIN, 1);
@@ -438,6 +443,10 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
                         smem_desc_sw128(vb + kk * 2048, kAtom64, 1024), IDESC_ACC, (i > 0 || kk > 0) ? 1u : 0u);
           }
           mma_commit_if(leader, BAR_QEMPTY(s));
+          // the next S^T / dP^T of this buffer is issued after the MMAs that read its P^T / dS^T;
+          // with fused dQ also ahead of dQ^T(i), which reads dS^T from shared memory, so the pipe
+          // has that group's work while the stream drains dQ^T(i - 2)
+          if (i + 2 < nq && !(ok = issue_sp(i + 2))) break;
           if (FQ) {
             // dQ^T = K^T dS^T over the 128 keys (A: the resident K read M-major; B: the staged dS^T),
             // once the stream has drained the dQ^T of its previous tile from this buffer
@@ -449,11 +458,9 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
             for (int kk = 0; kk < 8; ++kk)
               mma_ss_if(leader, dqt, smem_desc_sw128(sRes + kk * 2048, kAtom128, 1024),
                         smem_desc_sw128(sds + kk * 2048, kAtom128, 1024), idq, kk > 0);
+            mma_commit_if(leader, BAR_DQDONE(i & 1));
           }
         }
-        // the next S^T / dP^T of this buffer is issued after the MMAs that read its P^T / dS^T
-        // (and, with fused dQ, after dQ^T of this tile: its completion also completes dQ^T)
-        if (i + 2 < nq) ok = issue_sp(i + 2);
       }
       if (elect_one()) {
         mma_commit(BAR_DONE);
@@ -495,6 +502,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
       const int s = i % NQS;
       if (!warp_wait(BAR_SPFULL(stm), (i >> 1) & 1, 8)) { ok = false; break; }
       if (!warp_wait(BAR_QFULL(s), (i / NQS) & 1, 8)) { ok = false; break; }
+      // fused dQ: dQ^T(i - 2) has finished reading this stream's dS^T staging (and may be drained)
+      if (FQ && i >= 2 && !warp_wait(BAR_DQDONE(stm), ((i >> 1) - 1) & 1, 8)) { ok = false; break; }
       tc_fence_after();
       const uint32_t st = slot_stats(s);
       const float2 sc2 = make_float2(p.scale_log2, p.scale_log2), sm2 = make_float2(p.sm_scale, p.sm_scale);
@@ -560,8 +569,8 @@ __global__ void __launch_bounds__(64 + 128 * NWG, 1) fea_bwd_dkdv_kernel(const _
         st_global_v8(dst + 32, ds_hold[1]);
       }
       if (FQ) {
-        // while the MMA warp runs this tile's dK MMAs: drain dQ^T(i - 2), complete since S^T(i) was
-        // issued after it; then its buffer may take dQ^T(i)
+        // while the MMA warp runs this tile's dK MMAs and S^T / dP^T(i + 2): drain dQ^T(i - 2)
+        // (complete: DQDONE was waited for above); then its buffer may take dQ^T(i)
         if (i >= 2) drain_dq(i - 2);
         tc_fence_before();
         mbar_arrive(BAR_DQFREE(stm));
