@@ -11,9 +11,10 @@
 //   warps 2-9 softmax + epilogue, two warpgroups: thread = one query row (TMEM lane) x one half
 //            (64 keys) of each 128-key tile; the half-row maxima are exchanged once per tile.
 // TMEM (512 columns): S0 [0,128), S1 [128,256), O [256, 256 + NV).
-// The max is rescaled lazily: O, l and h keep a stale reference max m_ref until a tile's max
-// exceeds it by more than 8 (p <= 256), the only point where O is read back and rescaled. The
-// entropy identity E = log l - h / l holds for any reference, so this is exact.
+// The max is rescaled lazily: O, l and h keep a stale reference max m_ref until a tile's scores
+// pass it (a 64-key half's sum of p above 2^14 on full tiles, its max above m_ref + 8 on first and
+// ragged tiles and with e4m3 P), the only point where O is read back and rescaled. The entropy
+// identity E = log l - h / l holds for any reference, so this is exact.
 //
 // Shared-memory ring slot = [K tile (2 swizzle atoms of 128 keys x 64 cols)][X tile]:
 //   separate V   : X = V (NV/64 atoms); P V reads the X atoms                 (plain FEA, recompute)
@@ -46,6 +47,13 @@ using namespace sm100;
 constexpr int kThreads = 320;
 constexpr int kAtom = 128 * 128;  // bytes of one swizzle atom column block: 128 rows x 128 B
 constexpr float kRescaleThreshold = 8.0f;
+// Full tiles after a stream's first, 16-bit P: the exponentials go against the current reference
+// and are kept unless a 64-key half's sum of p exceeds this (64 x 2^8). The test costs one compare
+// per half instead of a running max beside every pair of exponentials. Kept halves hold
+// p <= 2^14 (inside bf16 and fp16, and the fp32 accumulators' relative precision does not depend
+// on the scale); a row whose max passed the reference by more than kRescaleThreshold + 6 always
+// fails it. e4m3 P (max 448) keeps the max test against kRescaleThreshold (p <= 2^8).
+constexpr float kSumThreshold = 16384.0f;
 
 struct Sm100FwdParams {
   CUtensorMap tm_q, tm_k, tm_x, tm_o;
@@ -317,7 +325,7 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
     // Two warpgroups split every 128-key tile by columns: warpgroup wg owns keys [64 wg, 64 wg + 64)
     // of each row and O columns [wg NV/2, (wg + 1) NV/2). Both hold the same m_ref and take
     // identical rescale decisions: on full tiles after the first, the exponentials run against
-    // m_ref and one OR barrier (named barrier 1) confirms that no row's max passed it; otherwise
+    // m_ref and one OR barrier (named barrier 1) confirms that no row's sum passed the limit; otherwise
     // they exchange the half-row maxima through TMEM (named barrier 1 again) and compute P against
     // the agreed reference. l and h are per-warpgroup partial sums, added in the epilogue. Every
     // named barrier is reached by all 256 threads and reduces their status, so a failed wait in
@@ -353,9 +361,9 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       }
       uint32_t pk[PK];
       float lt = 0.f, ht = 0.f;
-      // A full tile after the first: the exponentials against the current reference with the
-      // half's max beside them, P stored at once. One barrier tells both warpgroups whether any
-      // row's max passed the reference by more than the threshold (or a wait failed). Otherwise
+      // A full tile after the first: the exponentials against the current reference, P stored at
+      // once. One barrier tells both warpgroups whether any row's half sum passed kSumThreshold
+      // (e4m3: its max passed the reference by more than the threshold) or a wait failed. Otherwise
       // (first tile, ragged tile, or a row past the threshold) the half-row maxima are exchanged
       // as below and P is computed (again) against the agreed reference and stored.
       bool redo = true;
@@ -363,10 +371,10 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
       if (fast) {
         float mh = -1e30f;
         if (good) {
-          mh = probs_row<T, 64, ENT, false, true, F8>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+          mh = probs_row<T, 64, ENT, false, F8, F8>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
           tmem_st_p<F8>(tS + wg * 64, pk);  // this warpgroup's own half of S (already loaded)
         }
-        redo = named_bar_or(1, 256, !good || mh > m_ref + kRescaleThreshold);
+        redo = named_bar_or(1, 256, !good || (F8 ? mh > m_ref + kRescaleThreshold : !(lt <= kSumThreshold)));
       }
       if (redo) {
         float mh = -1e30f;
@@ -489,8 +497,9 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
 // A tile's P goes out in two 64-key halves: BAR_PHALF after the first lets the MMA warp issue
 // P V for those keys while the softmax works on the second (the chain softmax -> own P V -> next S
 // bounds each stream's cycle). Full tiles after a stream's first skip the separate max pass: the
-// exponentials run against the current reference m_ref with each half's max taken beside them,
-// and a half whose max passes m_ref + threshold is redone from its scores (still in registers)
+// exponentials run against the current reference m_ref, and a half whose sum of p passes
+// kSumThreshold (e4m3: whose max, taken beside the exponentials, passes m_ref + threshold) is
+// redone from its scores (still in registers)
 // after the rescale; a redo in the second half first waits for BAR_PVH, the commit behind the
 // first half's P V, which adds into O. The stream's first tile and a ragged last tile take the
 // max first.
@@ -809,10 +818,9 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
       // P in two 64-key halves: keys [64 k, 64 k + 64) -> columns [32 k, 32 k + 32); BAR_PHALF
       // after the first lets P V of those keys start.
       if (t > 0 && valid >= 128) {
-        // A full tile after the stream's first: the exponentials go against the current reference
-        // while the half's max is taken beside them; a half whose max passes the reference by
-        // more than the threshold (rare: the reference only grows) is redone after the rescale,
-        // from the scores still in registers.
+        // A full tile after the stream's first: the exponentials go against the current reference;
+        // a half whose sum passes kSumThreshold (rare: the reference only grows) is redone after
+        // the rescale to its max, from the scores still in registers.
         {
           uint32_t sa[64];
           tmem_ld32(tS + 0, sa);
@@ -820,13 +828,13 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           tmem_wait_ld();
           uint32_t pk[PK];
           float lt = 0.f, ht = 0.f;
-          const float mx = probs_row<T, 64, ENT, false, true, F8>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
-          if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+          const float mx = probs_row<T, 64, ENT, false, F8, F8>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
+          if (__any_sync(0xffffffffu, F8 ? mx > m_ref + kRescaleThreshold : !(lt <= kSumThreshold))) {
             // every earlier P V into O_w has completed (S_w(t) complete; HS: S_A(t) only follows the
             // first half of P V(t - 1), so wait for the second); P V(t) is not issued yet
             if (HS && !warp_wait(BAR_PVB(w), (t - 1) & 1, 16)) { ok = false; break; }
             tc_fence_after();
-            rescale(mx);
+            rescale(F8 ? mx : row_max_raw<64, false>(sa, 64) * p.scale_log2);
             lt = 0.f;
             ht = 0.f;
             probs_row<T, 64, ENT, false, false, F8>(sa, pk, p.scale_log2, m_ref, 64, lt, ht);
@@ -849,12 +857,12 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
           tmem_wait_ld();
           uint32_t pk[PK];
           float lt = 0.f, ht = 0.f;
-          const float mx = probs_row<T, 64, ENT, false, true, F8>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
-          if (__any_sync(0xffffffffu, mx > m_ref + kRescaleThreshold)) {
+          const float mx = probs_row<T, 64, ENT, false, F8, F8>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
+          if (__any_sync(0xffffffffu, F8 ? mx > m_ref + kRescaleThreshold : !(lt <= kSumThreshold))) {
             // the first half of P V(t) may still be adding into O_w: wait for its commit
             if (!warp_wait(BAR_PVH(w), t & 1, 16)) { ok = false; break; }
             tc_fence_after();
-            rescale(mx);
+            rescale(F8 ? mx : row_max_raw<64, false>(sb, 64) * p.scale_log2);
             lt = 0.f;
             ht = 0.f;
             probs_row<T, 64, ENT, false, false, F8>(sb, pk, p.scale_log2, m_ref, 64, lt, ht);
