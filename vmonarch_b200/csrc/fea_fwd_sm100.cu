@@ -419,8 +419,20 @@ __global__ void __launch_bounds__(kThreads, 1) fea_fwd_sm100_kernel(const __grid
         if (fresh) {
           lt = 0.f;
           ht = 0.f;
-          if (valid < 64) probs_row<T, 64, ENT, true, false, F8>(sr, pk, p.scale_log2, m_ref, valid, lt, ht);
-          else probs_row<T, 64, ENT, false, false, F8>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+          if (valid <= 0) {  // no key of this half (a ragged last tile): P = 0 with no exponentials
+#pragma unroll
+            for (int i = 0; i < PK; ++i) pk[i] = 0u;
+          } else if (valid <= 32) {  // keys [0, 32) of the half only
+            const uint32_t(&s32)[32] = *reinterpret_cast<const uint32_t(*)[32]>(&sr[0]);
+            uint32_t(&p32)[PK / 2] = *reinterpret_cast<uint32_t(*)[PK / 2]>(&pk[0]);
+            probs_row<T, 32, ENT, true, false, F8>(s32, p32, p.scale_log2, m_ref, valid, lt, ht);
+#pragma unroll
+            for (int i = PK / 2; i < PK; ++i) pk[i] = 0u;
+          } else if (valid < 64) {
+            probs_row<T, 64, ENT, true, false, F8>(sr, pk, p.scale_log2, m_ref, valid, lt, ht);
+          } else {
+            probs_row<T, 64, ENT, false, false, F8>(sr, pk, p.scale_log2, m_ref, 64, lt, ht);
+          }
         }
         if (good) tmem_st_p<F8>(tS + wg * 64, pk);
       }
@@ -898,21 +910,37 @@ __global__ void __launch_bounds__(64 + 128 * NS, 3 - NS) fea_fwd2_sm100_kernel(c
            // second half of P), so the first half's scores are the only ones live through the exponentials
           const uint32_t(&sh)[64] = *reinterpret_cast<const uint32_t(*)[64]>(&sr[0]);
           uint32_t pk[PK];
-          if (valid < 128) probs_row<T, 64, ENT, true, false, F8>(sh, pk, p.scale_log2, m_ref, valid, l, h);
-          else probs_row<T, 64, ENT, false, false, F8>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          if (valid <= 32) {  // keys [0, 32) only (the S and P V MMAs of such a tile are N / K = 32)
+            const uint32_t(&s32)[32] = *reinterpret_cast<const uint32_t(*)[32]>(&sr[0]);
+            uint32_t(&p32)[PK / 2] = *reinterpret_cast<uint32_t(*)[PK / 2]>(&pk[0]);
+            probs_row<T, 32, ENT, true, false, F8>(s32, p32, p.scale_log2, m_ref, valid, l, h);
+#pragma unroll
+            for (int i = PK / 2; i < PK; ++i) pk[i] = 0u;
+          } else if (valid < 128) {
+            probs_row<T, 64, ENT, true, false, F8>(sh, pk, p.scale_log2, m_ref, valid, l, h);
+          } else {
+            probs_row<T, 64, ENT, false, false, F8>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          }
           tmem_st_p<F8>(tS + 0, pk);
           tmem_wait_st();
           tc_fence_before();
           mbar_arrive(BAR_PHALF(w));
         }
         {
-          uint32_t sh[64];
-          tmem_ld32(tS + 64, sh);
-          tmem_ld32(tS + 96, sh + 32);
-          tmem_wait_ld();
           uint32_t pk[PK];
-          if (valid < 128) probs_row<T, 64, ENT, true, false, F8>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
-          else probs_row<T, 64, ENT, false, false, F8>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          if (valid > 64) {
+            uint32_t sh[64];
+            tmem_ld32(tS + 64, sh);
+            tmem_ld32(tS + 96, sh + 32);
+            tmem_wait_ld();
+            if (valid < 128) probs_row<T, 64, ENT, true, false, F8>(sh, pk, p.scale_log2, m_ref, valid - 64, l, h);
+            else probs_row<T, 64, ENT, false, false, F8>(sh, pk, p.scale_log2, m_ref, 64, l, h);
+          } else {
+            // no key of the tile in [64, 128) (the R-step tails at b = 1560 hold 24): P = 0 with no
+            // exponentials; P V reads these columns when the tile has more than 32 keys
+#pragma unroll
+            for (int i = 0; i < PK; ++i) pk[i] = 0u;
+          }
           tmem_st_p<F8>(tS + (HS ? 64 : 32), pk);
         }
       }
