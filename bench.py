@@ -36,6 +36,7 @@ import statistics
 import subprocess
 import sys
 import tempfile
+import threading
 import time
 from pathlib import Path
 
@@ -88,22 +89,123 @@ def parse_args():
 
 # ----------------------------------------------------------------------------------------- clocks
 class ClockSampler:
-    """Samples nvidia-smi clocks / throttle reasons every 200 ms while the timed region runs."""
+    """SM clock, power and clock-event (throttle) reasons of this GPU while the timed region runs.
 
+    A host thread reads them through NVML (the library nvidia-smi reports from) every 5 ms, each
+    sample stamped with the host time; `begin()` / `end()` (called by `time_steps` at the
+    synchronisations that bracket the timed region) restrict the summary to that span and
+    snapshot NVML's cumulative per-reason throttle timers, so `throttle_ms` is the time the GPU
+    spent in each reason over the timed region. The begin snapshot is taken by the sampling thread
+    (an NVML field read can take tens of ms, which must not delay the timed launches, nor leave
+    the GPU idle before them); the end snapshot is read after the region's final synchronisation.
+    NVML refreshes clock and power readings only every ~100 ms, so on a region of a few steps the
+    timers are the exact record and the sampled median clock is coarse. Without NVML it falls back
+    to `nvidia-smi -lms 200` over the whole `with` block. Reading clocks changes no GPU setting."""
+
+    PERIOD_S = 0.005
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
+    REASON_BITS = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+                   "sw_power_cap": 0x4}
 
-    def __init__(self, device: torch.device):
+    def __init__(self, device: torch.device, nvml=None):
         self.uuid = None
         try:
             self.uuid = "GPU-" + str(torch.cuda.get_device_properties(device).uuid)
         except Exception:
             pass
+        self.nvml = nvml  # a stand-in module for tests; None: pynvml if importable
+        self.handle = None
+        self.samples = []  # (host time, sm MHz, reason bits, power W)
+        self.max_mhz = None
+        self.span = None
+        self.t0 = None
+        self.timers0 = None
+        self.want_timers = threading.Event()
+        self.throttle_ms = None
+        self.timer_lag_ms = None
+        self.stop = None
+        self.thread = None
         self.proc = None
         self.tmp = None
 
+    def window(self, t0: float, t1: float) -> None:
+        self.span = (t0, t1)
+
+    # NVML field ids of the cumulative throttle timers (ns), by reason
+    def _timer_fields(self):
+        nv = self.nvml
+        names = (("sw_power_cap", "NVML_FI_DEV_CLOCKS_EVENT_REASON_SW_POWER_CAP"),
+                 ("hw_power_brake_slowdown", "NVML_FI_DEV_CLOCKS_EVENT_REASON_HW_POWER_BRAKE_SLOWDOWN"),
+                 ("hw_thermal_slowdown", "NVML_FI_DEV_CLOCKS_EVENT_REASON_HW_THERM_SLOWDOWN"),
+                 ("sw_thermal_slowdown", "NVML_FI_DEV_CLOCKS_EVENT_REASON_SW_THERM_SLOWDOWN"))
+        return [(n, getattr(nv, f)) for n, f in names if hasattr(nv, f)]
+
+    def _timers(self):
+        if self.handle is None or not hasattr(self.nvml, "nvmlDeviceGetFieldValues"):
+            return None
+        try:
+            fields = self._timer_fields()
+            vals = self.nvml.nvmlDeviceGetFieldValues(self.handle, [f for _, f in fields])
+            return {n: v.value.ullVal for (n, _), v in zip(fields, vals) if v.nvmlReturn == 0}
+        except Exception:
+            return None
+
+    def begin(self) -> None:
+        self.t0 = time.monotonic()
+        self.timers0 = None
+        if self.thread is not None:
+            self.want_timers.set()  # the sampling thread snapshots the timers; the caller goes on
+
+    def end(self) -> None:
+        t1 = time.monotonic()
+        timers1 = self._timers()
+        if self.t0 is not None:
+            self.window(self.t0, t1)
+        if self.timers0 is not None and timers1 is not None:
+            self.throttle_ms = {n: round((timers1[n] - self.timers0[n]) / 1e6, 2)
+                                for n in timers1 if n in self.timers0}
+
+    def _open_nvml(self) -> bool:
+        try:
+            if self.nvml is None:
+                import pynvml
+                self.nvml = pynvml
+            nv = self.nvml
+            nv.nvmlInit()
+            if self.uuid:
+                self.handle = nv.nvmlDeviceGetHandleByUUID(self.uuid)
+            else:  # no CUDA device properties: the first GPU (NVML numbering)
+                self.handle = nv.nvmlDeviceGetHandleByIndex(0)
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(self.handle, nv.NVML_CLOCK_SM))
+            return True
+        except Exception:
+            self.handle = None
+            return False
+
+    def _poll(self) -> None:
+        nv, h = self.nvml, self.handle
+        reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
+            nv.nvmlDeviceGetCurrentClocksThrottleReasons
+        while not self.stop.is_set():
+            if self.want_timers.is_set():
+                self.want_timers.clear()
+                self.timers0 = self._timers()
+                self.timer_lag_ms = round((time.monotonic() - self.t0) * 1e3, 2)
+            try:
+                self.samples.append((time.monotonic(), float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
+                                     int(reasons(h)), nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
+            except Exception:
+                pass
+            self.stop.wait(self.PERIOD_S)
+
     def __enter__(self):
+        if self._open_nvml():
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
         try:
             self.tmp = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
             self.proc = subprocess.Popen(["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -113,6 +215,13 @@ class ClockSampler:
         return self
 
     def __exit__(self, *exc):
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join(timeout=5)
+            try:
+                self.nvml.nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -121,6 +230,27 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
+        if self.thread is not None:
+            rows = self.samples
+            if self.span is not None:
+                inside = [r for r in rows if self.span[0] <= r[0] <= self.span[1]]
+                rows = inside or rows
+            if not rows:
+                return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["no samples"]}
+            reasons = {n for n, b in self.REASON_BITS.items() if any(r[2] & b for r in rows)}
+            out = {"sm_mhz": statistics.median(r[1] for r in rows), "sm_mhz_min": min(r[1] for r in rows),
+                   "sm_max_mhz": self.max_mhz, "samples": len(rows),
+                   "power_w_max": round(max(r[3] for r in rows), 1),
+                   "source": "NVML every 5 ms inside the timed region" if self.span else "NVML every 5 ms"}
+            if self.throttle_ms is not None:
+                out["throttle_ms"] = self.throttle_ms
+                out["region_ms"] = round((self.span[1] - self.span[0]) * 1e3, 2)
+                out["throttle_timers_from_ms"] = self.timer_lag_ms  # begin snapshot, after the region's start
+                # a power-brake slowdown is one of the hardware slowdowns nvidia-smi reports as hw_slowdown
+                reasons |= {"hw_slowdown" if n == "hw_power_brake_slowdown" else n
+                            for n, v in self.throttle_ms.items() if v > 0}
+            out["reasons"] = sorted(reasons)
+            return out
         if self.proc is None or self.tmp is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
         rows = []
@@ -137,7 +267,7 @@ class ClockSampler:
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({names[i] for r in rows for i in range(4) if r[4 + i].lower().startswith("active")})
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": float(rows[0][2]),
-                "samples": len(rows), "reasons": reasons}
+                "samples": len(rows), "reasons": reasons, "source": "nvidia-smi every 200 ms"}
 
 
 # ----------------------------------------------------------------------------------------- steps
@@ -177,10 +307,11 @@ def scaled_flops(w: Workload, n_heads: int) -> float:
     return (f["fwd"] + f["bwd"]) * n_heads / w.H
 
 
-def time_steps(step, args_dev, steps: int, warmup: int, device, launches=None) -> float:
+def time_steps(step, args_dev, steps: int, warmup: int, device, launches=None, clock=None) -> float:
     """ms per step: W warm-up steps, then K steps bracketed by barrier + synchronize, CUDA events.
     `launches`, when given, is a list that receives this library's kernel launches issued by the
-    K timed steps (warm-up excluded)."""
+    K timed steps (warm-up excluded); `clock` (a ClockSampler) is given the timed region's host
+    time span."""
     count = lambda: 0  # noqa: E731  (other arms load nothing of this library)
     if launches is not None:
         from vmonarch_b200 import ops
@@ -192,12 +323,16 @@ def time_steps(step, args_dev, steps: int, warmup: int, device, launches=None) -
     torch.cuda.synchronize(device)
     start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     n0 = count()
+    if clock is not None:
+        clock.begin()
     start.record()
     for _ in range(steps):
         step(*args_dev)
     end.record()
     n1 = count()
     torch.cuda.synchronize(device)
+    if clock is not None:
+        clock.end()
     shard.barrier()
     if launches is not None:
         launches.append(n1 - n0)
@@ -539,13 +674,13 @@ def run_ours(args, info, device):
     if args.graph:
         graph, graph_outs, per_replay = capture_step(step, dev, args.warmup, device)
         with ClockSampler(device) as clk:
-            ms = time_steps(lambda *_: graph.replay(), dev, args.steps, args.warmup, device)
+            ms = time_steps(lambda *_: graph.replay(), dev, args.steps, args.warmup, device, clock=clk)
         launches = per_replay * args.steps
         del graph, graph_outs
     else:
         counted = []
         with ClockSampler(device) as clk:
-            ms = time_steps(step, dev, args.steps, args.warmup, device, launches=counted)
+            ms = time_steps(step, dev, args.steps, args.warmup, device, launches=counted, clock=clk)
         launches = counted[0]
     ms_max = shard.max_over_ranks(ms, device)
     value = flops_job / (ms_max * 1e-3) / 1e12
@@ -659,7 +794,7 @@ def run_triton(args, info, device):
                 with torch.no_grad():
                     return ref.flash_entropy_attention(q, k, v)
     with ClockSampler(device) as clk:
-        ms = time_steps(step, dev, args.steps, args.warmup, device)
+        ms = time_steps(step, dev, args.steps, args.warmup, device, clock=clk)
     ms_max = shard.max_over_ranks(ms, device)
     f = w.flops()
     per_head = (f["fwd"] + (f["bwd"] if mode == "forward+backward" else 0.0)) / w.H

@@ -51,3 +51,47 @@ def test_both_arms_report_the_same_config():
 def test_reference_arm_other_ranks_print_nothing():
     out = _run({"RANK": "1", "WORLD_SIZE": "2", "LOCAL_RANK": "1"})
     assert not [x for x in out.splitlines() if x.startswith("{")]
+
+
+def test_clock_sampler_keeps_the_timed_window():
+    # A stand-in for NVML: the SM clock drops and the power-cap reason comes on after the first
+    # samples. The summary keeps only samples inside the window the timed region reports.
+    import importlib.util
+    import time
+    import types
+    spec = importlib.util.spec_from_file_location("_bench_clock_test", os.path.join(ROOT, "bench.py"))
+    bench = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(bench)
+    calls = {"n": 0}
+
+    def clock(h, kind):
+        calls["n"] += 1
+        return 1965 if calls["n"] <= 3 else 1700
+
+    timer = {"ns": 0}
+
+    def fields(h, ids):  # cumulative power-cap timer: +3 ms per read, the other reasons stay 0
+        timer["ns"] += 3_000_000
+        return [types.SimpleNamespace(nvmlReturn=0, value=types.SimpleNamespace(ullVal=timer["ns"] if i == 11 else 0))
+                for i in ids]
+
+    fake = types.SimpleNamespace(
+        NVML_CLOCK_SM=1, nvmlInit=lambda: None, nvmlShutdown=lambda: None, nvmlDeviceGetFieldValues=fields,
+        NVML_FI_DEV_CLOCKS_EVENT_REASON_SW_POWER_CAP=11, NVML_FI_DEV_CLOCKS_EVENT_REASON_HW_POWER_BRAKE_SLOWDOWN=12,
+        NVML_FI_DEV_CLOCKS_EVENT_REASON_HW_THERM_SLOWDOWN=13, NVML_FI_DEV_CLOCKS_EVENT_REASON_SW_THERM_SLOWDOWN=14,
+        nvmlDeviceGetHandleByUUID=lambda u: "h", nvmlDeviceGetHandleByIndex=lambda i: "h",
+        nvmlDeviceGetMaxClockInfo=lambda h, kind: 1965, nvmlDeviceGetClockInfo=clock,
+        nvmlDeviceGetCurrentClocksEventReasons=lambda h: 0x4 if calls["n"] > 3 else 0x1,
+        nvmlDeviceGetPowerUsage=lambda h: 990000)
+    with bench.ClockSampler("cpu", nvml=fake) as clk:
+        time.sleep(0.1)
+        clk.begin()
+        time.sleep(0.1)
+        clk.end()
+    s = clk.summary()
+    assert s["sm_mhz"] == 1700 and s["sm_max_mhz"] == 1965 and s["samples"] >= 5
+    assert s["reasons"] == ["sw_power_cap"] and s["power_w_max"] == 990.0
+    assert "inside the timed region" in s["source"]
+    assert s["throttle_ms"] == {"sw_power_cap": 3.0, "hw_power_brake_slowdown": 0.0, "hw_thermal_slowdown": 0.0,
+                                "sw_thermal_slowdown": 0.0}
+    assert 90 <= s["region_ms"] <= 1000
