@@ -95,14 +95,20 @@ class ClockSampler:
     sample stamped with the host time; `begin()` / `end()` (called by `time_steps` at the
     synchronisations that bracket the timed region) restrict the summary to that span and
     snapshot NVML's cumulative per-reason throttle timers, so `throttle_ms` is the time the GPU
-    spent in each reason over the timed region. The begin snapshot is taken by the sampling thread
-    (an NVML field read can take tens of ms, which must not delay the timed launches, nor leave
-    the GPU idle before them); the end snapshot is read after the region's final synchronisation.
-    NVML refreshes clock and power readings only every ~100 ms, so on a region of a few steps the
-    timers are the exact record and the sampled median clock is coarse. Without NVML it falls back
+    spent in each reason over the timed region. The sampling thread snapshots the timers
+    continuously (an NVML field read can take tens of ms, which must not delay the timed launches,
+    nor leave the GPU idle before them); the begin reference is the last snapshot completed before
+    the region started, so the timed span (`throttle_span_ms`, up to one read longer than the
+    region, into the warm-up) covers the whole region and may over-count, never under-count; the
+    end snapshot is read after the region's final synchronisation.
+    NVML refreshes its readings (clocks, power, reasons and these timers) only every ~100 ms, so
+    `end()` keeps the record open TRAIL_S past the region (the GPU is idle then; the timed region
+    is over): every state NVML held during the region is seen, and a reason that starts just after
+    it is counted too (the record may over-count, never under-count). Without NVML it falls back
     to `nvidia-smi -lms 200` over the whole `with` block. Reading clocks changes no GPU setting."""
 
     PERIOD_S = 0.005
+    TRAIL_S = 0.12
     FIELDS = ("uuid,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.hw_slowdown,"
               "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
               "clocks_event_reasons.sw_power_cap")
@@ -121,10 +127,10 @@ class ClockSampler:
         self.max_mhz = None
         self.span = None
         self.t0 = None
-        self.timers0 = None
-        self.want_timers = threading.Event()
+        self.snaps = []  # (host time the read started, host time it returned, timers)
         self.throttle_ms = None
-        self.timer_lag_ms = None
+        self.throttle_span_ms = None
+        self.region_ms = None
         self.stop = None
         self.thread = None
         self.proc = None
@@ -154,18 +160,22 @@ class ClockSampler:
 
     def begin(self) -> None:
         self.t0 = time.monotonic()
-        self.timers0 = None
-        if self.thread is not None:
-            self.want_timers.set()  # the sampling thread snapshots the timers; the caller goes on
 
     def end(self) -> None:
         t1 = time.monotonic()
+        if self.thread is not None:
+            time.sleep(self.TRAIL_S)  # past NVML's refresh period: the region's state is published
         timers1 = self._timers()
-        if self.t0 is not None:
-            self.window(self.t0, t1)
-        if self.timers0 is not None and timers1 is not None:
-            self.throttle_ms = {n: round((timers1[n] - self.timers0[n]) / 1e6, 2)
-                                for n in timers1 if n in self.timers0}
+        if self.t0 is None:
+            return
+        self.region_ms = round((t1 - self.t0) * 1e3, 2)
+        t1 = time.monotonic()
+        self.window(self.t0, t1)
+        before = [sn for sn in list(self.snaps) if sn[1] <= self.t0 and sn[2]]
+        if before and timers1 is not None:
+            ts, _, timers0 = before[-1]
+            self.throttle_ms = {n: round((timers1[n] - timers0[n]) / 1e6, 2) for n in timers1 if n in timers0}
+            self.throttle_span_ms = round((t1 - ts) * 1e3, 2)
 
     def _open_nvml(self) -> bool:
         try:
@@ -189,10 +199,10 @@ class ClockSampler:
         reasons = getattr(nv, "nvmlDeviceGetCurrentClocksEventReasons", None) or \
             nv.nvmlDeviceGetCurrentClocksThrottleReasons
         while not self.stop.is_set():
-            if self.want_timers.is_set():
-                self.want_timers.clear()
-                self.timers0 = self._timers()
-                self.timer_lag_ms = round((time.monotonic() - self.t0) * 1e3, 2)
+            ts = time.monotonic()
+            timers = self._timers()
+            if timers:
+                self.snaps.append((ts, time.monotonic(), timers))
             try:
                 self.samples.append((time.monotonic(), float(nv.nvmlDeviceGetClockInfo(h, nv.NVML_CLOCK_SM)),
                                      int(reasons(h)), nv.nvmlDeviceGetPowerUsage(h) / 1000.0))
@@ -241,11 +251,12 @@ class ClockSampler:
             out = {"sm_mhz": statistics.median(r[1] for r in rows), "sm_mhz_min": min(r[1] for r in rows),
                    "sm_max_mhz": self.max_mhz, "samples": len(rows),
                    "power_w_max": round(max(r[3] for r in rows), 1),
-                   "source": "NVML every 5 ms inside the timed region" if self.span else "NVML every 5 ms"}
+                   "source": (f"NVML every 5 ms from the timed region's start to {int(self.TRAIL_S * 1e3)} ms past "
+                              "its end (NVML refreshes every ~100 ms)") if self.span else "NVML every 5 ms"}
             if self.throttle_ms is not None:
                 out["throttle_ms"] = self.throttle_ms
-                out["region_ms"] = round((self.span[1] - self.span[0]) * 1e3, 2)
-                out["throttle_timers_from_ms"] = self.timer_lag_ms  # begin snapshot, after the region's start
+                out["region_ms"] = self.region_ms
+                out["throttle_span_ms"] = self.throttle_span_ms  # covers the region, from just before it
                 # a power-brake slowdown is one of the hardware slowdowns nvidia-smi reports as hw_slowdown
                 reasons |= {"hw_slowdown" if n == "hw_power_brake_slowdown" else n
                             for n, v in self.throttle_ms.items() if v > 0}
