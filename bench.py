@@ -212,6 +212,12 @@ class ClockSampler:
 
     def __enter__(self):
         if self._open_nvml():
+            # one snapshot before the warm-up (the GPU is idle here), so a region whose warm-up is
+            # shorter than an NVML read still has a reference taken before it
+            t = time.monotonic()
+            timers = self._timers()
+            if timers:
+                self.snaps.append((t, time.monotonic(), timers))
             self.stop = threading.Event()
             self.thread = threading.Thread(target=self._poll, daemon=True)
             self.thread.start()
