@@ -91,8 +91,8 @@ def parse_args():
 class ClockSampler:
     """SM clock, power and clock-event (throttle) reasons of this GPU while the timed region runs.
 
-    A host thread reads them through NVML (the library nvidia-smi reports from) every 5 ms, each
-    sample stamped with the host time; `begin()` / `end()` (called by `time_steps` at the
+    A host thread reads them through NVML (the library nvidia-smi reports from) continuously (a
+    pass every 5-10 ms, a timer read included), each sample stamped with the host time; `begin()` / `end()` (called by `time_steps` at the
     synchronisations that bracket the timed region) restrict the summary to that span and
     snapshot NVML's cumulative per-reason throttle timers, so `throttle_ms` is the time the GPU
     spent in each reason over the timed region. The sampling thread snapshots the timers
@@ -257,8 +257,8 @@ class ClockSampler:
             out = {"sm_mhz": statistics.median(r[1] for r in rows), "sm_mhz_min": min(r[1] for r in rows),
                    "sm_max_mhz": self.max_mhz, "samples": len(rows),
                    "power_w_max": round(max(r[3] for r in rows), 1),
-                   "source": (f"NVML every 5 ms from the timed region's start to {int(self.TRAIL_S * 1e3)} ms past "
-                              "its end (NVML refreshes every ~100 ms)") if self.span else "NVML every 5 ms"}
+                   "source": (f"NVML sampled continuously from the timed region's start to {int(self.TRAIL_S * 1e3)} "
+                              "ms past its end (NVML refreshes every ~100 ms)") if self.span else "NVML"}
             if self.throttle_ms is not None:
                 out["throttle_ms"] = self.throttle_ms
                 out["region_ms"] = self.region_ms
